@@ -1,0 +1,550 @@
+// DFlash objective (KL or CE against verifier logits, slot decay), forward and
+// backward, for sm_100a.
+//
+// Reference behaviour (harvestingmoon/cuda-spec-decode):
+//   models/dflash/loss.py:31-126   dflash_loss_fwd  (two passes: maxima, then A, B, C, D sums)
+//   models/dflash/loss.py:128-166  dflash_loss_bwd  (s * (softmax(draft) - softmax(target) | onehot))
+//   models/dflash/tests/test_loss.py:21-49  speculators oracle whose numbers this file reproduces
+//     (decay index j % block_size as in test_loss.py:62; raw float mask in the
+//      numerator and the denominator as in test_loss.py:46-49)
+//
+// Forward, one launch, ONE read of each row pair. With xl = draft logits,
+// xt = verifier logits, p = softmax(xt), q = softmax(xl):
+//   KL(p || q) = sum_v p_v (xt_v - xl_v) - logZp + logZq
+// Each piece keeps, in base 2 and relative to running maxima,
+//   sq = sum 2^(xl*log2e - m2q),  sp = sum 2^(xt*log2e - m2p),
+//   t  = sum 2^(xt*log2e - m2p) * (xt - xl),
+// (t rescales with the verifier max only), or for CE the first-index argmax
+// of xt with the draft logit at that index. The CTA landing last on a row
+// merges the pieces in slot order and writes the row's loss, scale and
+// log-normalisers; a global counter elects the CTA that sums the row losses
+// in index order into the scalar loss. Rows whose weight mask*decay is 0 are
+// never read.
+#include "specdec_common.cuh"
+#include "specdec_internal.h"
+
+#include <climits>
+
+namespace specdec {
+
+namespace {
+
+struct DfState {
+  float m2q, sq;      // draft log-sum-exp state
+  float m2p, sp, t;   // verifier log-sum-exp state and the p-weighted (xt - xl) sum (KL)
+  float bx, bl;       // CE: best verifier logit, draft logit at that index
+  int bi;             // CE: index of the best verifier logit (first occurrence)
+};
+
+__device__ __forceinline__ void df_init(DfState& st) {
+  st.m2q = kNegSeed;
+  st.sq = 0.f;
+  st.m2p = kNegSeed;
+  st.sp = 0.f;
+  st.t = 0.f;
+  st.bx = -INFINITY;
+  st.bl = 0.f;
+  st.bi = INT_MAX;
+}
+
+template <int KIND>
+__device__ __forceinline__ void df_merge(DfState& x, const DfState& o) {
+  lse2_merge(x.m2q, x.sq, o.m2q, o.sq);
+  if (KIND == kKindKL) {
+    const float M = fmaxf(x.m2p, o.m2p);
+    const float fa = exp2_approx(x.m2p - M), fb = exp2_approx(o.m2p - M);
+    x.sp = x.sp * fa + o.sp * fb;
+    x.t = x.t * fa + o.t * fb;
+    x.m2p = M;
+  } else {
+    if (o.bx > x.bx || (o.bx == x.bx && o.bi < x.bi)) {
+      x.bx = o.bx;
+      x.bi = o.bi;
+      x.bl = o.bl;
+    }
+  }
+}
+
+template <int KIND>
+__device__ __forceinline__ DfState df_shfl(const DfState& s, int o) {
+  DfState r;
+  r.m2q = __shfl_xor_sync(kFullMask, s.m2q, o);
+  r.sq = __shfl_xor_sync(kFullMask, s.sq, o);
+  if (KIND == kKindKL) {
+    r.m2p = __shfl_xor_sync(kFullMask, s.m2p, o);
+    r.sp = __shfl_xor_sync(kFullMask, s.sp, o);
+    r.t = __shfl_xor_sync(kFullMask, s.t, o);
+  } else {
+    r.bx = __shfl_xor_sync(kFullMask, s.bx, o);
+    r.bl = __shfl_xor_sync(kFullMask, s.bl, o);
+    r.bi = __shfl_xor_sync(kFullMask, s.bi, o);
+  }
+  return r;
+}
+
+template <int KIND>
+__device__ __forceinline__ void df_warp_merge(DfState& s) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const DfState other = df_shfl<KIND>(s, o);
+    df_merge<KIND>(s, other);
+  }
+}
+
+// One element (scalar path); idx is the index within the row.
+template <int KIND>
+__device__ __forceinline__ void df_push(DfState& s, float a, float b, int idx) {
+  lse2_push(s.m2q, s.sq, a);
+  if (KIND == kKindKL) {
+    const float b2 = b * kLog2e;
+    if (b2 > s.m2p) {
+      const float f = exp2_approx(s.m2p - b2);
+      s.sp *= f;
+      s.t *= f;
+      s.m2p = b2;
+    }
+    const float e = exp2_approx(fmaf(b, kLog2e, -s.m2p));
+    s.sp += e;
+    s.t = fmaf(e, b - a, s.t);
+  } else {
+    if (b > s.bx || (b == s.bx && idx < s.bi)) {
+      s.bx = b;
+      s.bi = idx;
+      s.bl = a;
+    }
+  }
+}
+
+template <int KIND, int U>
+__device__ __forceinline__ void df_group(DfState& s, const float4 (&a)[U], const float4 (&b)[U],
+                                         int base_idx, int stride_idx) {
+  float cma = max4(a[0]);
+#pragma unroll
+  for (int u = 1; u < U; ++u) cma = fmaxf(cma, max4(a[u]));
+  const float cma2 = cma * kLog2e;
+  if (cma2 > s.m2q) {
+    s.sq *= exp2_approx(s.m2q - cma2);
+    s.m2q = cma2;
+  }
+  const float nq = -s.m2q;
+  float accq = 0.f;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    accq += exp2_approx(fmaf(a[u].x, kLog2e, nq)) + exp2_approx(fmaf(a[u].y, kLog2e, nq)) +
+            exp2_approx(fmaf(a[u].z, kLog2e, nq)) + exp2_approx(fmaf(a[u].w, kLog2e, nq));
+  }
+  s.sq += accq;
+  float cmb = max4(b[0]);
+#pragma unroll
+  for (int u = 1; u < U; ++u) cmb = fmaxf(cmb, max4(b[u]));
+  if (KIND == kKindKL) {
+    const float cmb2 = cmb * kLog2e;
+    if (cmb2 > s.m2p) {
+      const float f = exp2_approx(s.m2p - cmb2);
+      s.sp *= f;
+      s.t *= f;
+      s.m2p = cmb2;
+    }
+    const float np = -s.m2p;
+    float accp = 0.f, acct = 0.f;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const float ex = exp2_approx(fmaf(b[u].x, kLog2e, np));
+      const float ey = exp2_approx(fmaf(b[u].y, kLog2e, np));
+      const float ez = exp2_approx(fmaf(b[u].z, kLog2e, np));
+      const float ew = exp2_approx(fmaf(b[u].w, kLog2e, np));
+      accp += (ex + ey) + (ez + ew);
+      acct = fmaf(ex, b[u].x - a[u].x, acct);
+      acct = fmaf(ey, b[u].y - a[u].y, acct);
+      acct = fmaf(ez, b[u].z - a[u].z, acct);
+      acct = fmaf(ew, b[u].w - a[u].w, acct);
+    }
+    s.sp += accp;
+    s.t += acct;
+  } else {
+    if (cmb > s.bx) {
+      // first element of the group equal to its max, in index order
+#pragma unroll
+      for (int u = U - 1; u >= 0; --u) {
+        const int k = base_idx + u * stride_idx;
+        if (b[u].w == cmb) { s.bi = k + 3; s.bl = a[u].w; }
+        if (b[u].z == cmb) { s.bi = k + 2; s.bl = a[u].z; }
+        if (b[u].y == cmb) { s.bi = k + 1; s.bl = a[u].y; }
+        if (b[u].x == cmb) { s.bi = k + 0; s.bl = a[u].x; }
+      }
+      s.bx = cmb;
+    }
+  }
+}
+
+// Streams one piece [lo, hi) of a row pair. `vec` selects 128-bit loads (both
+// rows share the same 16-byte phase).
+template <int KIND, int NT, int U>
+__device__ __forceinline__ void df_stream(DfState& s, const float* __restrict__ xl,
+                                          const float* __restrict__ xt, int64_t lo, int64_t hi) {
+  const int tid = threadIdx.x;
+  const float* pl = xl + lo;
+  const float* pt = xt + lo;
+  const int64_t n = hi - lo;
+  const bool vec = ((reinterpret_cast<uintptr_t>(pl) ^ reinterpret_cast<uintptr_t>(pt)) & 15) == 0;
+  int64_t head = vec ? (((16 - (reinterpret_cast<uintptr_t>(pl) & 15)) & 15) >> 2) : n;
+  if (head > n) head = n;
+  const int64_t body = (n - head) >> 2;
+  const int64_t tail0 = head + (body << 2);
+  // index order per thread: head, body, tail (the CE argmax keeps the first max)
+  for (int64_t i = tid; i < head; i += NT) df_push<KIND>(s, pl[i], pt[i], (int)(lo + i));
+  const float4* ql = reinterpret_cast<const float4*>(pl + head);
+  const float4* qt = reinterpret_cast<const float4*>(pt + head);
+  const int base = (int)(lo + head);
+  int64_t i = tid;
+  for (; i + (U - 1) * NT < body; i += U * NT) {
+    float4 a[U], b[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      a[u] = ld_stream(ql + i + u * NT);
+      b[u] = ld_stream(qt + i + u * NT);
+    }
+    df_group<KIND, U>(s, a, b, base + 4 * (int)i, 4 * NT);
+  }
+  for (; i < body; i += NT) {
+    float4 a[1], b[1];
+    a[0] = ld_stream(ql + i);
+    b[0] = ld_stream(qt + i);
+    df_group<KIND, 1>(s, a, b, base + 4 * (int)i, 0);
+  }
+  for (int64_t i2 = tail0 + tid; i2 < n; i2 += NT) df_push<KIND>(s, pl[i2], pt[i2], (int)(lo + i2));
+}
+
+// Row weight w = mask * decay(pos) / (sum_j mask + 1e-5), pos = j % block_size.
+// Follows models/dflash/tests/test_loss.py:23-27,43-49 (raw float mask).
+__device__ __forceinline__ float df_decay(const DflashFwdArgs& a, int j) {
+  const int pos = j % a.block_size;
+  if (a.sfa) return expf(__fdiv_rn(-(float)pos, a.gamma));
+  if (pos == 0) return 0.f;
+  return expf(__fdiv_rn(-(float)(pos - 1), a.gamma));
+}
+
+__device__ __forceinline__ float df_mask(const DflashFwdArgs& a, int64_t r) {
+  return a.mask ? a.mask[r] : 1.f;
+}
+
+// Numerator of the weight only (mask * decay): zero exactly when the row's
+// weight is zero, so the row can be skipped.
+__device__ __forceinline__ float df_numer(const DflashFwdArgs& a, int64_t r) {
+  return __fmul_rn(df_mask(a, r), df_decay(a, (int)(r % a.B)));
+}
+
+template <int KIND>
+__device__ void df_finalize_row(const DflashFwdArgs& a, int64_t r, int* sh_last) {
+  const int lane = threadIdx.x & 31;
+  __threadfence();
+  const int64_t n = r / a.B;
+  // denominator: sum of the sequence's raw mask values + 1e-5
+  float m = 0.f;
+  for (int i = lane; i < a.B; i += 32) m += df_mask(a, n * a.B + i);
+  const float denom = warp_sum(m) + 1e-5f;
+  const float numer = df_numer(a, r);
+  const float w = __fdiv_rn(numer, denom);
+  float el = 0.f, lzq = 0.f, lzp = 0.f;
+  int64_t tgt = 0;
+  if (numer != 0.f) {
+    DfState s;
+    df_init(s);
+    const int k = a.pt.pieces(r);
+    const DfPiece* part = a.part + r * a.pt.pmax;
+    for (int q = lane; q < k; q += 32) {
+      DfState o;
+      const float4 lo4 = __ldcg(reinterpret_cast<const float4*>(part + q));
+      const float4 hi4 = __ldcg(reinterpret_cast<const float4*>(part + q) + 1);
+      o.m2q = lo4.x; o.sq = lo4.y; o.m2p = lo4.z; o.sp = lo4.w;
+      o.t = hi4.x; o.bx = hi4.y; o.bl = hi4.z; o.bi = __float_as_int(hi4.w);
+      df_merge<KIND>(s, o);
+    }
+    df_warp_merge<KIND>(s);
+    lzq = (s.m2q + log2f(s.sq)) * kLn2;
+    if (KIND == kKindKL) {
+      lzp = (s.m2p + log2f(s.sp)) * kLn2;
+      // KL = sum p (xt - xl) - logZp + logZq, the normaliser difference taken in base 2
+      el = s.t / s.sp + ((s.m2q - s.m2p) + log2f(s.sq / s.sp)) * kLn2;
+    } else {
+      int bi = s.bi;
+      float bl = s.bl;
+      if (bi == INT_MAX) {  // no finite maximum (all -inf): argmax is index 0
+        bi = 0;
+        bl = a.logits[r * a.V];
+      }
+      tgt = bi;
+      el = lzq - bl;
+    }
+  }
+  if (lane == 0) {
+    const float lr = numer != 0.f ? __fmul_rn(w, el) : 0.f;
+    if (a.loss_rows) a.loss_rows[r] = lr;
+    a.row_loss[r] = lr;
+    a.scale[r] = __fdiv_rn(w, (float)a.n_global);
+    a.logzq[r] = lzq;
+    a.logzp[r] = lzp;
+    if (a.target_id) a.target_id[r] = tgt;
+    a.row_cnt[r] = 0u;
+    __threadfence();
+    const unsigned prev = atomicAdd(a.done_cnt, 1u);
+    *sh_last = (prev + 1 == (unsigned)(a.N * a.B));
+  }
+  __syncwarp();
+}
+
+template <int KIND, int NT, int U>
+__global__ void __launch_bounds__(NT) dflash_fwd_kernel(const __grid_constant__ DflashFwdArgs a) {
+  constexpr int NW = NT / 32;
+  __shared__ __align__(16) DfState sh_red[NW];
+  __shared__ int sh_flag, sh_last;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int64_t c = blockIdx.x;
+  const Partition& pt = a.pt;
+  const int64_t e_begin = c * pt.chunk;
+  const int64_t e_end = min(e_begin + pt.chunk, pt.E);
+  int64_t r = e_begin / pt.V;
+  for (int64_t e = e_begin; e < e_end; ++r) {
+    const int64_t row0 = r * pt.V;
+    const int64_t lo = e - row0;
+    const int64_t hi = min(e_end, row0 + pt.V) - row0;
+    e = row0 + hi;
+    const bool live = df_numer(a, r) != 0.f;
+    if (live) {
+      DfState s;
+      df_init(s);
+      df_stream<KIND, NT, U>(s, a.logits + row0, a.target_logits + row0, lo, hi);
+      df_warp_merge<KIND>(s);
+      if (lane == 0) sh_red[w] = s;
+      __syncthreads();
+      if (w == 0) {
+        if (lane < NW) s = sh_red[lane];
+        else df_init(s);
+        df_warp_merge<KIND>(s);
+        if (lane == 0) {
+          float4* dst = reinterpret_cast<float4*>(a.part + r * pt.pmax + (c - pt.first_cta(r)));
+          dst[0] = make_float4(s.m2q, s.sq, s.m2p, s.sp);
+          dst[1] = make_float4(s.t, s.bx, s.bl, __int_as_float(s.bi));
+        }
+      }
+    }
+    if (tid == 0) {
+      int last = 1;
+      if (pt.pieces(r) > 1) {
+        __threadfence();
+        const unsigned prev = atomicAdd(a.row_cnt + r, 1u);
+        last = (prev + 1 == (unsigned)pt.pieces(r));
+      }
+      sh_flag = last;
+    }
+    __syncthreads();
+    if (sh_flag && w == 0) df_finalize_row<KIND>(a, r, &sh_last);
+    __syncthreads();
+    if (sh_flag && sh_last && w == 0) {
+      __threadfence();
+      const float total = warp_sum_l2(a.row_loss, a.N * a.B);
+      if (lane == 0) {
+        a.loss[0] = total / (float)a.n_global;
+        *a.done_cnt = 0u;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+template <int KIND, int NT, int U>
+__global__ void __launch_bounds__(NT) dflash_bwd_kernel(const __grid_constant__ DflashBwdArgs a) {
+  const int tid = threadIdx.x;
+  const int64_t c = blockIdx.x;
+  const Partition& pt = a.pt;
+  const int64_t e_begin = c * pt.chunk;
+  const int64_t e_end = min(e_begin + pt.chunk, pt.E);
+  const float g = a.dloss ? __ldg(a.dloss) : 1.f;
+  const uint64_t pol = policy_evict_first();
+  int64_t r = e_begin / pt.V;
+  for (int64_t e = e_begin; e < e_end; ++r) {
+    const int64_t row0 = r * pt.V;
+    const int64_t lo = e - row0;
+    const int64_t hi = min(e_end, row0 + pt.V) - row0;
+    e = row0 + hi;
+    const int64_t n = hi - lo;
+    const float sc = __fmul_rn(a.scale[r], g);
+    const float* pl = a.logits + row0 + lo;
+    const float* px = a.target_logits + row0 + lo;
+    float* dst = a.dlogits + row0 + lo;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(pl), ad = reinterpret_cast<uintptr_t>(dst);
+    const uintptr_t ax = KIND == kKindKL ? reinterpret_cast<uintptr_t>(px) : al;
+    const bool vec = (((al ^ ad) | (al ^ ax)) & 15) == 0;
+    int64_t head = vec ? (((16 - (al & 15)) & 15) >> 2) : n;
+    if (head > n) head = n;
+    const int64_t body = (n - head) >> 2;
+    const int64_t tail0 = head + (body << 2);
+    if (sc == 0.f) {
+      for (int64_t i = tid; i < head; i += NT) dst[i] = 0.f;
+      for (int64_t i = tail0 + tid; i < n; i += NT) dst[i] = 0.f;
+      float4* q = reinterpret_cast<float4*>(dst + head);
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int64_t i = tid; i < body; i += NT) st_stream(q + i, z);
+      continue;
+    }
+    const float nq = -(a.logzq[r] * kLog2e);
+    const float np = -(a.logzp[r] * kLog2e);
+    const int64_t t = (KIND == kKindCE ? a.target_id[r] : -1) - lo;
+    auto elem = [&](float xl, float xt, int64_t i) -> float {
+      const float q = exp2_approx(fmaf(xl, kLog2e, nq));
+      const float p = KIND == kKindKL ? exp2_approx(fmaf(xt, kLog2e, np)) : (i == t ? 1.f : 0.f);
+      return sc * (q - p);
+    };
+    for (int64_t i = tid; i < head; i += NT) dst[i] = elem(pl[i], KIND == kKindKL ? px[i] : 0.f, i);
+    for (int64_t i = tail0 + tid; i < n; i += NT)
+      dst[i] = elem(pl[i], KIND == kKindKL ? px[i] : 0.f, i);
+    const float4* ql = reinterpret_cast<const float4*>(pl + head);
+    const float4* qx = reinterpret_cast<const float4*>(px + head);
+    float4* qd = reinterpret_cast<float4*>(dst + head);
+    const int64_t tb = t - head;
+    int64_t i = tid;
+    for (; i + (U - 1) * NT < body; i += U * NT) {
+      float4 va[U], vb[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        va[u] = ld_last(ql + i + u * NT, pol);
+        if (KIND == kKindKL) vb[u] = ld_last(qx + i + u * NT, pol);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t k = i + u * NT;
+        float4 y;
+        y.x = exp2_approx(fmaf(va[u].x, kLog2e, nq));
+        y.y = exp2_approx(fmaf(va[u].y, kLog2e, nq));
+        y.z = exp2_approx(fmaf(va[u].z, kLog2e, nq));
+        y.w = exp2_approx(fmaf(va[u].w, kLog2e, nq));
+        if (KIND == kKindKL) {
+          y.x -= exp2_approx(fmaf(vb[u].x, kLog2e, np));
+          y.y -= exp2_approx(fmaf(vb[u].y, kLog2e, np));
+          y.z -= exp2_approx(fmaf(vb[u].z, kLog2e, np));
+          y.w -= exp2_approx(fmaf(vb[u].w, kLog2e, np));
+        } else {
+          const uint64_t d = (uint64_t)(tb - 4 * k);
+          if (d < 4) {
+            if (d == 0) y.x -= 1.f;
+            else if (d == 1) y.y -= 1.f;
+            else if (d == 2) y.z -= 1.f;
+            else y.w -= 1.f;
+          }
+        }
+        y.x *= sc;
+        y.y *= sc;
+        y.z *= sc;
+        y.w *= sc;
+        st_stream(qd + k, y);
+      }
+    }
+    for (; i < body; i += NT) {
+      const float4 va = ld_last(ql + i, pol);
+      float4 y;
+      y.x = exp2_approx(fmaf(va.x, kLog2e, nq));
+      y.y = exp2_approx(fmaf(va.y, kLog2e, nq));
+      y.z = exp2_approx(fmaf(va.z, kLog2e, nq));
+      y.w = exp2_approx(fmaf(va.w, kLog2e, nq));
+      if (KIND == kKindKL) {
+        const float4 vb = ld_last(qx + i, pol);
+        y.x -= exp2_approx(fmaf(vb.x, kLog2e, np));
+        y.y -= exp2_approx(fmaf(vb.y, kLog2e, np));
+        y.z -= exp2_approx(fmaf(vb.z, kLog2e, np));
+        y.w -= exp2_approx(fmaf(vb.w, kLog2e, np));
+      } else {
+        const uint64_t d = (uint64_t)(tb - 4 * i);
+        if (d < 4) {
+          if (d == 0) y.x -= 1.f;
+          else if (d == 1) y.y -= 1.f;
+          else if (d == 2) y.z -= 1.f;
+          else y.w -= 1.f;
+        }
+      }
+      y.x *= sc;
+      y.y *= sc;
+      y.z *= sc;
+      y.w *= sc;
+      st_stream(qd + i, y);
+    }
+  }
+}
+
+template <class K>
+int occupancy_ctas(K kernel, int nt, int device, int cap_per_sm) {
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, nt, 0) != cudaSuccess) return 0;
+  if (cap_per_sm > 0 && per_sm > cap_per_sm) per_sm = cap_per_sm;
+  if (per_sm < 1) per_sm = 1;
+  return sms * per_sm;
+}
+
+template <int KIND, int NT, int U>
+struct DflashVariant {
+  static int fwd_ctas(int device, int cap) {
+    return occupancy_ctas(dflash_fwd_kernel<KIND, NT, U>, NT, device, cap);
+  }
+  static int bwd_ctas(int device, int cap) {
+    return occupancy_ctas(dflash_bwd_kernel<KIND, NT, U>, NT, device, cap);
+  }
+  static cudaError_t fwd(const DflashFwdArgs& a, cudaStream_t st) {
+    dflash_fwd_kernel<KIND, NT, U><<<(unsigned)a.pt.grid, NT, 0, st>>>(a);
+    return cudaGetLastError();
+  }
+  static cudaError_t bwd(const DflashBwdArgs& a, cudaStream_t st) {
+    dflash_bwd_kernel<KIND, NT, U><<<(unsigned)a.pt.grid, NT, 0, st>>>(a);
+    return cudaGetLastError();
+  }
+};
+
+template <int KIND>
+int fwd_ctas_k(int shape, int device, int cap) {
+  switch (shape) {
+    case 1: return DflashVariant<KIND, 256, 4>::fwd_ctas(device, cap);
+    case 4: return DflashVariant<KIND, 512, 2>::fwd_ctas(device, cap);
+    default: return DflashVariant<KIND, 256, 2>::fwd_ctas(device, cap);
+  }
+}
+template <int KIND>
+int bwd_ctas_k(int shape, int device, int cap) {
+  switch (shape) {
+    case 1: return DflashVariant<KIND, 256, 4>::bwd_ctas(device, cap);
+    case 4: return DflashVariant<KIND, 512, 2>::bwd_ctas(device, cap);
+    default: return DflashVariant<KIND, 512, 4>::bwd_ctas(device, cap);
+  }
+}
+template <int KIND>
+cudaError_t fwd_launch_k(int shape, const DflashFwdArgs& a, cudaStream_t st) {
+  switch (shape) {
+    case 1: return DflashVariant<KIND, 256, 4>::fwd(a, st);
+    case 4: return DflashVariant<KIND, 512, 2>::fwd(a, st);
+    default: return DflashVariant<KIND, 256, 2>::fwd(a, st);
+  }
+}
+template <int KIND>
+cudaError_t bwd_launch_k(int shape, const DflashBwdArgs& a, cudaStream_t st) {
+  switch (shape) {
+    case 1: return DflashVariant<KIND, 256, 4>::bwd(a, st);
+    case 4: return DflashVariant<KIND, 512, 2>::bwd(a, st);
+    default: return DflashVariant<KIND, 512, 4>::bwd(a, st);
+  }
+}
+
+}  // namespace
+
+int dflash_fwd_ctas(int kind, int shape, int device, int cap) {
+  return kind == kKindKL ? fwd_ctas_k<kKindKL>(shape, device, cap) : fwd_ctas_k<kKindCE>(shape, device, cap);
+}
+int dflash_bwd_ctas(int kind, int shape, int device, int cap) {
+  return kind == kKindKL ? bwd_ctas_k<kKindKL>(shape, device, cap) : bwd_ctas_k<kKindCE>(shape, device, cap);
+}
+cudaError_t dflash_fwd_launch(int shape, const DflashFwdArgs& a, cudaStream_t st) {
+  return a.kind == kKindKL ? fwd_launch_k<kKindKL>(shape, a, st) : fwd_launch_k<kKindCE>(shape, a, st);
+}
+cudaError_t dflash_bwd_launch(int shape, const DflashBwdArgs& a, cudaStream_t st) {
+  return a.kind == kKindKL ? bwd_launch_k<kKindKL>(shape, a, st) : bwd_launch_k<kKindCE>(shape, a, st);
+}
+
+}  // namespace specdec

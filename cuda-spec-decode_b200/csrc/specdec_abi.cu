@@ -1,0 +1,389 @@
+// extern "C" entry points of libspecdec.so (declared in include/specdec.h):
+// argument checks, workspace layout, launch-shape selection and error codes.
+// Nothing here allocates device memory or synchronises the stream.
+#include "specdec.h"
+#include "specdec_internal.h"
+
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <map>
+#include <mutex>
+#include <string>
+
+using namespace specdec;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int ok() {
+  g_last_error.clear();
+  return SPECDEC_OK;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(SPECDEC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// Smallest CTA chunk in elements: below this, per-piece bookkeeping dominates.
+constexpr int64_t kMinChunk = 1024;
+
+std::atomic<int> g_shape[4] = {0, 0, 0, 0};
+std::atomic<int> g_cap[4] = {0, 0, 0, 0};
+
+int current_device() {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess) return -1;
+  return d;
+}
+
+// Occupancy-derived CTA counts, cached per (kernel, kind, shape, cap, device).
+int kernel_ctas(int kernel, int kind, int device) {
+  static std::mutex mu;
+  static std::map<uint64_t, int> cache;
+  const int shape = g_shape[kernel].load(), cap = g_cap[kernel].load();
+  const uint64_t key = (uint64_t(kernel) << 56) | (uint64_t(kind & 0xff) << 48) |
+                       (uint64_t(shape & 0xff) << 40) | (uint64_t(cap & 0xffff) << 24) |
+                       uint64_t(device & 0xffffff);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  int ctas = 0;
+  switch (kernel) {
+    case SPECDEC_KERNEL_DPACE_FWD: ctas = dpace_fwd_ctas(shape, device, cap); break;
+    case SPECDEC_KERNEL_DPACE_BWD: ctas = dpace_bwd_ctas(shape, device, cap); break;
+    case SPECDEC_KERNEL_DFLASH_FWD: ctas = dflash_fwd_ctas(kind, shape, device, cap); break;
+    case SPECDEC_KERNEL_DFLASH_BWD: ctas = dflash_bwd_ctas(kind, shape, device, cap); break;
+    default: ctas = 0;
+  }
+  if (ctas > 0) {
+    std::lock_guard<std::mutex> lk(mu);
+    cache[key] = ctas;
+  }
+  return ctas;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// ---- D-PACE workspace layout ----------------------------------------------
+// counters: [done u32][flag i32][pad to 16 B][seq_cnt u32 x N]
+// scratch:  [part float2 x R*pmax][xtgt f32 x R][seq_loss f32 x N]
+struct DpaceLayout {
+  size_t part = 0, xtgt = 0, seq_loss = 0, scratch = 0, counters = 0;
+};
+
+DpaceLayout dpace_layout(int64_t N, int64_t B, const Partition& pt) {
+  DpaceLayout L;
+  const size_t R = size_t(N) * size_t(B);
+  L.part = 0;
+  L.xtgt = align256(L.part + R * size_t(pt.pmax) * sizeof(float2));
+  L.seq_loss = align256(L.xtgt + R * sizeof(float));
+  L.scratch = align256(L.seq_loss + size_t(N) * sizeof(float));
+  L.counters = align256(16 + size_t(N) * sizeof(unsigned));
+  return L;
+}
+
+// ---- DFlash workspace layout -----------------------------------------------
+// counters: [done u32][pad to 16 B][row_cnt u32 x R]
+// scratch:  [part DfPiece x R*pmax][row_loss f32 x R]
+struct DflashLayout {
+  size_t part = 0, row_loss = 0, scratch = 0, counters = 0;
+};
+
+DflashLayout dflash_layout(int64_t N, int64_t B, const Partition& pt) {
+  DflashLayout L;
+  const size_t R = size_t(N) * size_t(B);
+  L.part = 0;
+  L.row_loss = align256(L.part + R * size_t(pt.pmax) * sizeof(DfPiece));
+  L.scratch = align256(L.row_loss + R * sizeof(float));
+  L.counters = align256(16 + R * sizeof(unsigned));
+  return L;
+}
+
+Partition dpace_fwd_partition(int64_t N, int32_t B, int64_t V, int device) {
+  const int ctas = kernel_ctas(SPECDEC_KERNEL_DPACE_FWD, 0, device);
+  return make_partition(N * B, V, ctas, kMinChunk);
+}
+
+Partition dflash_fwd_partition(int64_t N, int32_t B, int64_t V, int kind, int device) {
+  const int ctas = kernel_ctas(SPECDEC_KERNEL_DFLASH_FWD, kind, device);
+  return make_partition(N * B, V, ctas, kMinChunk);
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+int specdec_version(void) { return 100; }
+
+const char* specdec_last_error(void) { return g_last_error.c_str(); }
+
+const char* specdec_status_string(int code) {
+  switch (code) {
+    case SPECDEC_OK: return "ok";
+    case SPECDEC_ERR_ARGUMENT: return "invalid argument";
+    case SPECDEC_ERR_VALUE: return "value out of domain";
+    case SPECDEC_ERR_TARGET_RANGE: return "target id out of range";
+    case SPECDEC_ERR_WORKSPACE: return "workspace too small";
+    case SPECDEC_ERR_CUDA: return "CUDA error";
+    default: return "unknown status";
+  }
+}
+
+int specdec_set_launch_shape(int32_t kernel, int32_t shape, int32_t ctas_per_sm) {
+  if (kernel < 0 || kernel > 3) return fail(SPECDEC_ERR_ARGUMENT, "unknown kernel id %d", kernel);
+  if (shape < 0 || shape > 4) return fail(SPECDEC_ERR_ARGUMENT, "unknown launch shape %d", shape);
+  if (ctas_per_sm < 0 || ctas_per_sm > 32)
+    return fail(SPECDEC_ERR_ARGUMENT, "ctas_per_sm must be in [0, 32], got %d", ctas_per_sm);
+  g_shape[kernel].store(shape);
+  g_cap[kernel].store(ctas_per_sm);
+  return ok();
+}
+
+int64_t specdec_launch_ctas(int32_t kernel, int64_t rows, int64_t V, int device) {
+  if (kernel < 0 || kernel > 3 || rows <= 0 || V <= 0) return 0;
+  const int ctas = kernel_ctas(kernel, 0, device);
+  return make_partition(rows, V, ctas, kMinChunk).grid;
+}
+
+// ---------------------------------------------------------------------------
+// D-PACE
+// ---------------------------------------------------------------------------
+
+size_t specdec_dpace_scratch_bytes(int64_t N, int32_t B, int64_t V, int device) {
+  if (N <= 0 || B <= 0 || V <= 0) return 256;
+  return dpace_layout(N, B, dpace_fwd_partition(N, B, V, device)).scratch;
+}
+
+size_t specdec_dpace_counter_bytes(int64_t N, int32_t B) {
+  (void)B;
+  return align256(16 + size_t(N > 0 ? N : 0) * sizeof(unsigned));
+}
+
+int specdec_dpace_forward(const float* logits, const int64_t* targets, const float* mask,
+                          int64_t N, int32_t B, int64_t V, float alpha, int32_t loss_type,
+                          int64_t n_global, float* loss, float* loss_n, float* lse, float* scale,
+                          int32_t* status, void* scratch, size_t scratch_bytes, void* counters,
+                          size_t counter_bytes, void* stream) {
+  // Mirrors losses/dpace.py:157-173 (_check) order of failures.
+  if (B < 1 || B > 32) return fail(SPECDEC_ERR_ARGUMENT, "kernel configured for block_size <= 32 (B=%d)", B);
+  if (N < 0 || V < 0) return fail(SPECDEC_ERR_ARGUMENT, "negative shape N=%lld V=%lld", (long long)N, (long long)V);
+  if (!(alpha >= 0.f && alpha <= 1.f))
+    return fail(SPECDEC_ERR_VALUE, "dpace_alpha must be in [0, 1], got %g", (double)alpha);
+  if (loss_type < 0 || loss_type > 2) return fail(SPECDEC_ERR_VALUE, "unknown loss_type %d", loss_type);
+  if (n_global < N || n_global < 1) {
+    if (N > 0) return fail(SPECDEC_ERR_ARGUMENT, "n_global (%lld) must be >= N (%lld)", (long long)n_global, (long long)N);
+  }
+  if (!loss) return fail(SPECDEC_ERR_ARGUMENT, "loss output is null");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (N == 0) {
+    // mean over an empty batch: NaN, as torch's mean of an empty tensor
+    cudaError_t e = cudaMemsetAsync(loss, 0xff, sizeof(float), st);
+    if (e == cudaSuccess && status) e = cudaMemsetAsync(status, 0, sizeof(int32_t), st);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "cudaMemsetAsync");
+  }
+  if (V == 0) return fail(SPECDEC_ERR_TARGET_RANGE, "targets out of range [0, 0)");
+  if (!logits || !targets || !lse || !scale || !scratch || !counters)
+    return fail(SPECDEC_ERR_ARGUMENT, "null input, output or workspace pointer");
+  if (!aligned(logits, 4) || !aligned(targets, 8) || !aligned(lse, 4) || !aligned(scale, 4) ||
+      !aligned(scratch, 256) || !aligned(counters, 16))
+    return fail(SPECDEC_ERR_ARGUMENT, "misaligned pointer (scratch needs 256 B, counters 16 B)");
+  const int dev = current_device();
+  if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
+  const Partition pt = dpace_fwd_partition(N, B, V, dev);
+  if (pt.grid <= 0) return fail(SPECDEC_ERR_CUDA, "occupancy query failed");
+  const DpaceLayout L = dpace_layout(N, B, pt);
+  if (scratch_bytes < L.scratch)
+    return fail(SPECDEC_ERR_WORKSPACE, "scratch needs %zu bytes, got %zu", L.scratch, scratch_bytes);
+  if (counter_bytes < L.counters)
+    return fail(SPECDEC_ERR_WORKSPACE, "counters need %zu bytes, got %zu", L.counters, counter_bytes);
+
+  char* ws = static_cast<char*>(scratch);
+  unsigned* cnt = static_cast<unsigned*>(counters);
+  DpaceFwdArgs a;
+  a.logits = logits;
+  a.targets = targets;
+  a.mask = mask;
+  a.N = N;
+  a.B = B;
+  a.V = V;
+  a.alpha = alpha;
+  a.one_minus_alpha = (float)(1.0 - (double)alpha);
+  a.loss_type = loss_type;
+  a.n_global = n_global;
+  a.inv_n = (float)(1.0 / (double)n_global);
+  a.loss = loss;
+  a.loss_n = loss_n;
+  a.lse = lse;
+  a.scale = scale;
+  a.status = status;
+  a.part = reinterpret_cast<float2*>(ws + L.part);
+  a.xtgt = reinterpret_cast<float*>(ws + L.xtgt);
+  a.seq_loss = reinterpret_cast<float*>(ws + L.seq_loss);
+  a.done_cnt = cnt;
+  a.flag = reinterpret_cast<int*>(cnt + 1);
+  a.seq_cnt = cnt + 4;
+  a.pt = pt;
+  const cudaError_t e = dpace_fwd_launch(g_shape[SPECDEC_KERNEL_DPACE_FWD].load(), a, st);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "dpace forward launch");
+}
+
+int specdec_dpace_backward(const float* logits, const int64_t* targets, const float* lse,
+                           const float* scale, const float* dloss, float* dlogits, int64_t N,
+                           int32_t B, int64_t V, void* stream) {
+  if (B < 1 || B > 32) return fail(SPECDEC_ERR_ARGUMENT, "kernel configured for block_size <= 32 (B=%d)", B);
+  if (N < 0 || V < 0) return fail(SPECDEC_ERR_ARGUMENT, "negative shape");
+  if (N == 0 || V == 0) return ok();
+  if (!logits || !targets || !lse || !scale || !dlogits)
+    return fail(SPECDEC_ERR_ARGUMENT, "null input or output pointer");
+  if (logits == dlogits) return fail(SPECDEC_ERR_ARGUMENT, "dlogits must not alias logits");
+  const int dev = current_device();
+  if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
+  const int ctas = kernel_ctas(SPECDEC_KERNEL_DPACE_BWD, 0, dev);
+  if (ctas <= 0) return fail(SPECDEC_ERR_CUDA, "occupancy query failed");
+  DpaceBwdArgs a;
+  a.logits = logits;
+  a.targets = targets;
+  a.lse = lse;
+  a.scale = scale;
+  a.dloss = dloss;
+  a.dlogits = dlogits;
+  a.pt = make_partition(N * B, V, ctas, kMinChunk);
+  const cudaError_t e =
+      dpace_bwd_launch(g_shape[SPECDEC_KERNEL_DPACE_BWD].load(), a, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "dpace backward launch");
+}
+
+// ---------------------------------------------------------------------------
+// DFlash
+// ---------------------------------------------------------------------------
+
+size_t specdec_dflash_scratch_bytes(int64_t N, int32_t B, int64_t V, int device) {
+  if (N <= 0 || B <= 0 || V <= 0) return 256;
+  // both kinds share one partition rule; take the larger of the two
+  const DflashLayout a = dflash_layout(N, B, dflash_fwd_partition(N, B, V, kKindKL, device));
+  const DflashLayout b = dflash_layout(N, B, dflash_fwd_partition(N, B, V, kKindCE, device));
+  return a.scratch > b.scratch ? a.scratch : b.scratch;
+}
+
+size_t specdec_dflash_counter_bytes(int64_t N, int32_t B) {
+  const int64_t R = (N > 0 && B > 0) ? N * B : 0;
+  return align256(16 + size_t(R) * sizeof(unsigned));
+}
+
+int specdec_dflash_forward(const float* logits, const float* target_logits, const float* mask,
+                           int64_t N, int32_t B, int64_t V, int32_t block_size, float gamma,
+                           int32_t sample_from_anchor, int32_t kind, int64_t n_global, float* loss,
+                           float* loss_rows, float* scale, float* logzq, float* logzp,
+                           int64_t* target_id, void* scratch, size_t scratch_bytes, void* counters,
+                           size_t counter_bytes, void* stream) {
+  // Mirrors models/dflash/loss.py:178-191 (_check) order of failures.
+  if (N < 0 || B < 0 || V < 0) return fail(SPECDEC_ERR_ARGUMENT, "negative shape");
+  if (V > INT32_MAX) return fail(SPECDEC_ERR_ARGUMENT, "V must be < 2^31");
+  if (B > 0 && (block_size < 1 || block_size > B))
+    return fail(SPECDEC_ERR_ARGUMENT, "block_size must be in [1, B] (block_size=%d, B=%d)", block_size, B);
+  if (!(gamma > 0.f)) return fail(SPECDEC_ERR_VALUE, "gamma must be > 0, got %g", (double)gamma);
+  if (kind != SPECDEC_DFLASH_KL && kind != SPECDEC_DFLASH_CE)
+    return fail(SPECDEC_ERR_VALUE, "unknown loss kind %d, expected 0 (kl) or 1 (ce)", kind);
+  if (N > 0 && (n_global < N)) return fail(SPECDEC_ERR_ARGUMENT, "n_global must be >= N");
+  if (!loss) return fail(SPECDEC_ERR_ARGUMENT, "loss output is null");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (N == 0 || B == 0 || V == 0) {
+    // sum over no rows / N: NaN for N == 0 (0/0), 0 otherwise
+    const cudaError_t e = cudaMemsetAsync(loss, N == 0 ? 0xff : 0, sizeof(float), st);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "cudaMemsetAsync");
+  }
+  if (!logits || !target_logits || !scale || !logzq || !logzp || !scratch || !counters)
+    return fail(SPECDEC_ERR_ARGUMENT, "null input, output or workspace pointer");
+  if (kind == SPECDEC_DFLASH_CE && !target_id) return fail(SPECDEC_ERR_ARGUMENT, "CE needs target_id output");
+  if (!aligned(scratch, 256) || !aligned(counters, 16))
+    return fail(SPECDEC_ERR_ARGUMENT, "misaligned workspace (scratch 256 B, counters 16 B)");
+  const int dev = current_device();
+  if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
+  const Partition pt = dflash_fwd_partition(N, B, V, kind, dev);
+  if (pt.grid <= 0) return fail(SPECDEC_ERR_CUDA, "occupancy query failed");
+  const DflashLayout L = dflash_layout(N, B, pt);
+  if (scratch_bytes < L.scratch)
+    return fail(SPECDEC_ERR_WORKSPACE, "scratch needs %zu bytes, got %zu", L.scratch, scratch_bytes);
+  if (counter_bytes < L.counters)
+    return fail(SPECDEC_ERR_WORKSPACE, "counters need %zu bytes, got %zu", L.counters, counter_bytes);
+  char* ws = static_cast<char*>(scratch);
+  unsigned* cnt = static_cast<unsigned*>(counters);
+  DflashFwdArgs a;
+  a.logits = logits;
+  a.target_logits = target_logits;
+  a.mask = mask;
+  a.N = N;
+  a.B = B;
+  a.V = V;
+  a.block_size = block_size;
+  a.gamma = gamma;
+  a.sfa = sample_from_anchor ? 1 : 0;
+  a.kind = kind;
+  a.n_global = n_global;
+  a.loss = loss;
+  a.loss_rows = loss_rows;
+  a.scale = scale;
+  a.logzq = logzq;
+  a.logzp = logzp;
+  a.target_id = target_id;
+  a.part = reinterpret_cast<DfPiece*>(ws + L.part);
+  a.row_loss = reinterpret_cast<float*>(ws + L.row_loss);
+  a.done_cnt = cnt;
+  a.row_cnt = cnt + 4;
+  a.pt = pt;
+  const cudaError_t e = dflash_fwd_launch(g_shape[SPECDEC_KERNEL_DFLASH_FWD].load(), a, st);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "dflash forward launch");
+}
+
+int specdec_dflash_backward(const float* logits, const float* target_logits, const float* scale,
+                            const float* logzq, const float* logzp, const int64_t* target_id,
+                            const float* dloss, float* dlogits, int64_t N, int32_t B, int64_t V,
+                            int32_t kind, void* stream) {
+  if (N < 0 || B < 0 || V < 0) return fail(SPECDEC_ERR_ARGUMENT, "negative shape");
+  if (kind != SPECDEC_DFLASH_KL && kind != SPECDEC_DFLASH_CE)
+    return fail(SPECDEC_ERR_VALUE, "unknown loss kind %d", kind);
+  if (N == 0 || B == 0 || V == 0) return ok();
+  if (!logits || !scale || !logzq || !logzp || !dlogits)
+    return fail(SPECDEC_ERR_ARGUMENT, "null input or output pointer");
+  if (kind == SPECDEC_DFLASH_KL && !target_logits) return fail(SPECDEC_ERR_ARGUMENT, "KL needs target_logits");
+  if (kind == SPECDEC_DFLASH_CE && !target_id) return fail(SPECDEC_ERR_ARGUMENT, "CE needs target_id");
+  if (logits == dlogits || target_logits == dlogits)
+    return fail(SPECDEC_ERR_ARGUMENT, "dlogits must not alias an input");
+  const int dev = current_device();
+  if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
+  const int ctas = kernel_ctas(SPECDEC_KERNEL_DFLASH_BWD, kind, dev);
+  if (ctas <= 0) return fail(SPECDEC_ERR_CUDA, "occupancy query failed");
+  DflashBwdArgs a;
+  a.logits = logits;
+  a.target_logits = target_logits;
+  a.scale = scale;
+  a.logzq = logzq;
+  a.logzp = logzp;
+  a.target_id = target_id;
+  a.dloss = dloss;
+  a.dlogits = dlogits;
+  a.kind = kind;
+  a.pt = make_partition(N * B, V, ctas, kMinChunk);
+  const cudaError_t e =
+      dflash_bwd_launch(g_shape[SPECDEC_KERNEL_DFLASH_BWD].load(), a, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "dflash backward launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,164 @@
+// Device helpers shared by the drafter-loss kernels (sm_100a).
+//
+// Every kernel in this library streams rows of fp32 logits [rows, V] from HBM.
+// The work is split the same way everywhere: the flattened element range
+// [0, rows*V) is cut into `grid` equal contiguous chunks, one per CTA, and the
+// grid is exactly (SM count x resident CTAs per SM), so one wave covers the
+// whole problem with no tail. A chunk may start or end inside a row; the part
+// of a row that one CTA sees is a "piece". Per-row reductions are produced per
+// piece and combined later in a fixed order, so results are bitwise
+// repeatable (no float atomics anywhere).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace specdec {
+
+constexpr float kLog2e = 1.44269504088896340736f;
+constexpr float kLn2 = 0.69314718055994530942f;
+// Running-max seed. Finite on purpose: exp2(x - seed) of a -inf logit is 0, not NaN.
+constexpr float kNegSeed = -1e30f;
+constexpr unsigned kFullMask = 0xffffffffu;
+
+// 2^x with the hardware MUFU.EX2 unit (PTX ex2.approx.ftz.f32).
+__device__ __forceinline__ float exp2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Read-only 128-bit load that does not allocate in L1 (the data is touched once
+// per pass); L2 keeps normal priority so a following pass may still hit.
+__device__ __forceinline__ float4 ld_stream(const float4* p) {
+  float4 v;
+  asm("ld.global.nc.L1::no_allocate.v4.f32 {%0, %1, %2, %3}, [%4];"
+      : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+      : "l"(p));
+  return v;
+}
+
+// L2 cache-policy descriptor that marks lines evict-first.
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t pol;
+  asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// Last-use 128-bit load under an L2 policy (the backward pass never re-reads).
+__device__ __forceinline__ float4 ld_last(const float4* p, uint64_t pol) {
+  float4 v;
+  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+      : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+      : "l"(p), "l"(pol));
+  return v;
+}
+
+// Streaming 128-bit store (cache-streaming, evict-first).
+__device__ __forceinline__ void st_stream(float4* p, float4 v) {
+  asm volatile("st.global.cs.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ float max4(const float4& v) {
+  return fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+}
+
+// ---------------------------------------------------------------------------
+// Online log-sum-exp in base 2: the state (m2, s) stands for s * 2^m2, where
+// m2 = fl(max_x * log2 e). Each element contributes 2^(x*log2e - m2) computed
+// with one FMA + one EX2; the max is refreshed once per loaded group, not per
+// element. log-sum-exp(x) = (m2 + log2 s) * ln 2.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void lse2_merge(float& m2, float& s, float om2, float os) {
+  const float M = fmaxf(m2, om2);
+  s = s * exp2_approx(m2 - M) + os * exp2_approx(om2 - M);
+  m2 = M;
+}
+
+__device__ __forceinline__ void lse2_push(float& m2, float& s, float x) {
+  const float x2 = x * kLog2e;
+  if (x2 > m2) {
+    s *= exp2_approx(m2 - x2);
+    m2 = x2;
+  }
+  s += exp2_approx(fmaf(x, kLog2e, -m2));
+}
+
+__device__ __forceinline__ void warp_lse2(float& m2, float& s) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om2 = __shfl_xor_sync(kFullMask, m2, o);
+    const float os = __shfl_xor_sync(kFullMask, s, o);
+    lse2_merge(m2, s, om2, os);
+  }
+}
+
+// Block-wide (m2, s) merge in a fixed butterfly order. `sh` holds 2*NT/32
+// floats. The result is valid in every lane of warp 0. Ends with a barrier.
+template <int NT>
+__device__ __forceinline__ void block_lse2(float& m2, float& s, float* sh) {
+  constexpr int NW = NT / 32;
+  warp_lse2(m2, s);
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (lane == 0) {
+    sh[w] = m2;
+    sh[NW + w] = s;
+  }
+  __syncthreads();
+  if (w == 0) {
+    m2 = lane < NW ? sh[lane] : kNegSeed;
+    s = lane < NW ? sh[NW + lane] : 0.f;
+    warp_lse2(m2, s);
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFullMask, v, o);
+  return v;
+}
+
+// Fixed-order sum of x[0..n) by one warp: lane-strided partials, then a
+// butterfly. Reads through L2 (the values were written by other CTAs).
+__device__ __forceinline__ float warp_sum_l2(const float* x, int64_t n) {
+  const int lane = threadIdx.x & 31;
+  float acc = 0.f;
+  for (int64_t i = lane; i < n; i += 32) acc += __ldcg(x + i);
+  return warp_sum(acc);
+}
+
+// ---------------------------------------------------------------------------
+// Flattened, balanced split of [0, rows*V) into equal CTA chunks.
+// ---------------------------------------------------------------------------
+struct Partition {
+  int64_t V = 0;      // row length in elements
+  int64_t E = 0;      // rows * V
+  int64_t chunk = 0;  // elements per CTA, a multiple of 4
+  int64_t grid = 0;   // number of CTAs
+  int pmax = 0;       // upper bound on the number of CTAs that touch one row
+
+  __host__ __device__ __forceinline__ int64_t first_cta(int64_t r) const { return (r * V) / chunk; }
+  __host__ __device__ __forceinline__ int pieces(int64_t r) const {
+    return int(((r + 1) * V - 1) / chunk - (r * V) / chunk + 1);
+  }
+};
+
+inline Partition make_partition(int64_t rows, int64_t V, int64_t ctas, int64_t min_chunk) {
+  Partition p;
+  p.V = V;
+  p.E = rows * V;
+  if (p.E <= 0) return p;
+  if (ctas < 1) ctas = 1;
+  int64_t c = (p.E + ctas - 1) / ctas;
+  c = (c + 3) & ~int64_t(3);
+  if (c < min_chunk) c = min_chunk;
+  p.chunk = c;
+  p.grid = (p.E + c - 1) / c;
+  p.pmax = int((V - 1) / c + 2);
+  return p;
+}
+
+}  // namespace specdec

@@ -1,0 +1,111 @@
+// Internal launch interface between the C-ABI layer (specdec_abi.cu) and the
+// kernels (dpace_kernels.cu, dflash_kernels.cu). Not part of the public ABI.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "specdec_common.cuh"
+
+namespace specdec {
+
+constexpr int kStatusOk = 0;
+constexpr int kStatusTargetRange = 3;  // equals SPECDEC_ERR_TARGET_RANGE in include/specdec.h
+
+constexpr int kKindKL = 0;
+constexpr int kKindCE = 1;
+
+// Per-piece partial of the DFlash forward (32 bytes, two float4 stores).
+struct alignas(16) DfPiece {
+  float m2q, sq, m2p, sp, t, bx, bl;
+  int bi;
+};
+
+struct DpaceFwdArgs {
+  const float* logits;     // [N, B, V]
+  const int64_t* targets;  // [N, B]
+  const float* mask;       // [N, B] or null (all positions scored); scored iff > 0
+  int64_t N;               // sequences in this launch
+  int B;                   // positions per sequence, 1..32
+  int64_t V;
+  float alpha, one_minus_alpha;
+  int loss_type;           // 0 = S (dpace), 1 = P (cumulative confidence), 2 = S/P (continuation value)
+  int64_t n_global;        // divisor: sequences across all shards
+  float inv_n;             // 1 / n_global
+  float* loss;             // [1]  sum_n loss_n / n_global
+  float* loss_n;           // [N]  sum_j w_j * ce_j, or null
+  float* lse;              // [N, B]
+  float* scale;            // [N, B]  w_j / n_global
+  int* status;             // [1]  device status word, or null
+  // workspace
+  float2* part;            // [N*B, pt.pmax] (m2, s) per row piece
+  float* xtgt;             // [N*B] logit at the target id
+  float* seq_loss;         // [N]
+  unsigned* seq_cnt;       // [N]  zero on entry, zero on exit
+  unsigned* done_cnt;      // [1]  zero on entry, zero on exit
+  int* flag;               // [1]  zero on entry, zero on exit
+  Partition pt;
+};
+
+struct DpaceBwdArgs {
+  const float* logits;
+  const int64_t* targets;
+  const float* lse;
+  const float* scale;
+  const float* dloss;      // [1] upstream gradient, or null for 1
+  float* dlogits;
+  Partition pt;
+};
+
+struct DflashFwdArgs {
+  const float* logits;         // draft [N, B, V]
+  const float* target_logits;  // verifier [N, B, V]
+  const float* mask;           // [N, B] raw float mask, or null for all ones
+  int64_t N;
+  int B;
+  int64_t V;
+  int block_size;              // decay position = j % block_size
+  float gamma;
+  int sfa;                     // sample_from_anchor
+  int kind;                    // kKindKL or kKindCE
+  int64_t n_global;
+  float* loss;                 // [1]
+  float* loss_rows;            // [N*B] or null
+  float* scale;                // [N*B]
+  float* logzq;                // [N*B]
+  float* logzp;                // [N*B]
+  int64_t* target_id;          // [N*B] argmax(verifier) for CE, or null
+  // workspace
+  DfPiece* part;               // [N*B, pt.pmax]
+  float* row_loss;             // [N*B]
+  unsigned* row_cnt;           // [N*B] zero on entry, zero on exit
+  unsigned* done_cnt;          // [1]   zero on entry, zero on exit
+  Partition pt;
+};
+
+struct DflashBwdArgs {
+  const float* logits;
+  const float* target_logits;  // read for KL only
+  const float* scale;
+  const float* logzq;
+  const float* logzp;
+  const int64_t* target_id;    // read for CE only
+  const float* dloss;
+  float* dlogits;
+  int kind;
+  Partition pt;
+};
+
+// Launch shapes: 0 = default; others select alternative (threads, unroll)
+// instantiations (see the switch tables in the kernel files).
+int dpace_fwd_ctas(int shape, int device, int cap_per_sm);
+int dpace_bwd_ctas(int shape, int device, int cap_per_sm);
+cudaError_t dpace_fwd_launch(int shape, const DpaceFwdArgs& a, cudaStream_t st);
+cudaError_t dpace_bwd_launch(int shape, const DpaceBwdArgs& a, cudaStream_t st);
+
+int dflash_fwd_ctas(int kind, int shape, int device, int cap_per_sm);
+int dflash_bwd_ctas(int kind, int shape, int device, int cap_per_sm);
+cudaError_t dflash_fwd_launch(int shape, const DflashFwdArgs& a, cudaStream_t st);
+cudaError_t dflash_bwd_launch(int shape, const DflashBwdArgs& a, cudaStream_t st);
+
+}  // namespace specdec

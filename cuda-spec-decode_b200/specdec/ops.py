@@ -1,0 +1,119 @@
+"""Tensor-level wrappers over the C ABI: allocate outputs with torch, pass raw
+pointers and the current CUDA stream, map status codes to exceptions.
+
+Shape/dtype validation that mirrors the reference's host checks lives in the
+reference-facing modules (losses.dpace, models.dflash.loss); these wrappers
+assume validated, contiguous CUDA inputs.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+DPACE_LOSS_TYPES = {
+    "dpace": 0,
+    "dpace-cumulative-confidence-only": 1,
+    "dpace-continuation-value-only": 2,
+}
+DFLASH_KINDS = {"kl": 0, "ce": 1}
+
+# When True (default, the reference's behaviour) the D-PACE forward raises
+# ValueError for target ids outside [0, V), which costs one 4-byte
+# device-to-host read per call. The kernel never reads out of bounds either
+# way; with validation off an out-of-range id contributes ce = 0.
+VALIDATE_TARGETS = True
+
+
+def set_target_validation(enabled: bool) -> None:
+    global VALIDATE_TARGETS
+    VALIDATE_TARGETS = bool(enabled)
+
+
+def dpace_forward(logits: torch.Tensor, targets: torch.Tensor, mask: torch.Tensor | None,
+                  alpha: float, loss_type: int, n_global: int | None = None,
+                  want_loss_n: bool = False, validate: bool | None = None):
+    """Returns (loss 0-d, lse [N,B], scale [N,B], loss_n [N] or None)."""
+    lib = _lib.load()
+    N, B, V = logits.shape
+    dev = logits.device
+    n_global = N if n_global is None else int(n_global)
+    loss = torch.empty((), dtype=torch.float32, device=dev)
+    lse = torch.empty((N, B), dtype=torch.float32, device=dev)
+    scale = torch.empty((N, B), dtype=torch.float32, device=dev)
+    loss_n = torch.empty((N,), dtype=torch.float32, device=dev) if want_loss_n else None
+    status = torch.empty((1,), dtype=torch.int32, device=dev)
+    ws = _lib.workspace("dpace", dev)
+    sb = lib.specdec_dpace_scratch_bytes(N, B, V, dev.index)
+    cb = lib.specdec_dpace_counter_bytes(N, B)
+    scratch, counters = ws.ensure(dev, sb, cb)
+    code = lib.specdec_dpace_forward(
+        logits.data_ptr(), targets.data_ptr(), _lib.ptr(mask), N, B, V, float(alpha),
+        int(loss_type), n_global, loss.data_ptr(), _lib.ptr(loss_n), lse.data_ptr(),
+        scale.data_ptr(), status.data_ptr(), scratch.data_ptr(), scratch.numel(),
+        counters.data_ptr(), counters.numel(), _lib.stream_handle(dev))
+    _lib.check(code, "specdec_dpace_forward")
+    if (VALIDATE_TARGETS if validate is None else validate) and N * B > 0:
+        if int(status.item()) == _lib.ERR_TARGET_RANGE:
+            raise ValueError(f"targets out of range [0, {V})")
+    return loss, lse, scale, loss_n
+
+
+def dpace_backward(logits: torch.Tensor, targets: torch.Tensor, lse: torch.Tensor,
+                   scale: torch.Tensor, dloss: torch.Tensor | None,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    lib = _lib.load()
+    N, B, V = logits.shape
+    dlogits = torch.empty_like(logits) if out is None else out
+    if dloss is not None:
+        dloss = dloss.detach().to(device=logits.device, dtype=torch.float32).contiguous()
+    code = lib.specdec_dpace_backward(
+        logits.data_ptr(), targets.data_ptr(), lse.data_ptr(), scale.data_ptr(),
+        _lib.ptr(dloss), dlogits.data_ptr(), N, B, V, _lib.stream_handle(logits.device))
+    _lib.check(code, "specdec_dpace_backward")
+    return dlogits
+
+
+def dflash_forward(logits: torch.Tensor, target_logits: torch.Tensor, mask: torch.Tensor | None,
+                   gamma: float, sample_from_anchor: bool, kind: int, block_size: int,
+                   n_global: int | None = None):
+    """Returns (loss 0-d, loss_rows [N,B], scale [N,B], logzq [N,B], logzp [N,B], tgt [N,B] or None)."""
+    lib = _lib.load()
+    N, B, V = logits.shape
+    dev = logits.device
+    n_global = N if n_global is None else int(n_global)
+    loss = torch.empty((), dtype=torch.float32, device=dev)
+    loss_rows = torch.empty((N, B), dtype=torch.float32, device=dev)
+    scale = torch.empty((N, B), dtype=torch.float32, device=dev)
+    logzq = torch.empty((N, B), dtype=torch.float32, device=dev)
+    logzp = torch.empty((N, B), dtype=torch.float32, device=dev)
+    tgt = torch.empty((N, B), dtype=torch.int64, device=dev) if kind == 1 else None
+    ws = _lib.workspace("dflash", dev)
+    sb = lib.specdec_dflash_scratch_bytes(N, B, V, dev.index)
+    cb = lib.specdec_dflash_counter_bytes(N, B)
+    scratch, counters = ws.ensure(dev, sb, cb)
+    code = lib.specdec_dflash_forward(
+        logits.data_ptr(), target_logits.data_ptr(), _lib.ptr(mask), N, B, V, int(block_size),
+        float(gamma), int(bool(sample_from_anchor)), int(kind), n_global, loss.data_ptr(),
+        loss_rows.data_ptr(), scale.data_ptr(), logzq.data_ptr(), logzp.data_ptr(),
+        _lib.ptr(tgt), scratch.data_ptr(), scratch.numel(), counters.data_ptr(),
+        counters.numel(), _lib.stream_handle(dev))
+    _lib.check(code, "specdec_dflash_forward")
+    return loss, loss_rows, scale, logzq, logzp, tgt
+
+
+def dflash_backward(logits: torch.Tensor, target_logits: torch.Tensor | None, scale: torch.Tensor,
+                    logzq: torch.Tensor, logzp: torch.Tensor, tgt: torch.Tensor | None,
+                    dloss: torch.Tensor | None, kind: int,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    lib = _lib.load()
+    N, B, V = logits.shape
+    dlogits = torch.empty_like(logits) if out is None else out
+    if dloss is not None:
+        dloss = dloss.detach().to(device=logits.device, dtype=torch.float32).contiguous()
+    code = lib.specdec_dflash_backward(
+        logits.data_ptr(), _lib.ptr(target_logits), scale.data_ptr(), logzq.data_ptr(),
+        logzp.data_ptr(), _lib.ptr(tgt), _lib.ptr(dloss), dlogits.data_ptr(), N, B, V, int(kind),
+        _lib.stream_handle(logits.device))
+    _lib.check(code, "specdec_dflash_backward")
+    return dlogits

@@ -1,0 +1,177 @@
+/*
+ * specdec.h -- C ABI of the B200 drafter-loss library (libspecdec.so).
+ *
+ * Fused training losses for speculative-decoding drafters over fp32 logits
+ * [N, B, V] (N sequences, B <= 32 draft positions, V vocabulary):
+ *   - D-PACE: cross entropy weighted by the detached, alpha-smoothed
+ *     acceptance prefix/suffix scan of each sequence;
+ *   - DFlash: KL(softmax(verifier) || softmax(draft)) or CE against
+ *     argmax(verifier), weighted by an exponential slot decay.
+ *
+ * Conventions (all entry points):
+ *   - every pointer is a device pointer unless stated otherwise; tensors are
+ *     C-contiguous; no entry point allocates device memory or synchronises;
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream); all work is
+ *     enqueued on it;
+ *   - return value: SPECDEC_OK or an error code; specdec_last_error() gives a
+ *     message for the calling thread;
+ *   - `scratch` is device memory of at least the queried size with no
+ *     initialisation requirement; `counters` is device memory of at least the
+ *     queried size that must be all-zero before the first call and is left
+ *     all-zero by every call that completes on the GPU (zero it once, e.g.
+ *     cudaMemset at allocation, then reuse). Calls that may run concurrently
+ *     on the GPU must not share scratch or counters.
+ *   - results are bitwise repeatable: all reductions run in a fixed order.
+ *
+ * Each entry point cites the reference interface it replaces
+ * (harvestingmoon/cuda-spec-decode, path:line).
+ */
+#ifndef SPECDEC_H_
+#define SPECDEC_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define SPECDEC_OK 0
+#define SPECDEC_ERR_ARGUMENT 1     /* shape, pointer or size contract broken (reference: AssertionError) */
+#define SPECDEC_ERR_VALUE 2        /* alpha, loss_type, gamma or kind out of domain (reference: ValueError) */
+#define SPECDEC_ERR_TARGET_RANGE 3 /* a target id outside [0, V); reported through *status on the device */
+#define SPECDEC_ERR_WORKSPACE 4    /* scratch or counters smaller than the queried size */
+#define SPECDEC_ERR_CUDA 5         /* CUDA runtime or launch failure */
+
+/* D-PACE loss_type values (reference: losses/dpace.py:148 _LOSS_TYPES). */
+#define SPECDEC_DPACE 0                      /* "dpace": w = S_j */
+#define SPECDEC_DPACE_CUMULATIVE_CONFIDENCE 1 /* "dpace-cumulative-confidence-only": w = P_j */
+#define SPECDEC_DPACE_CONTINUATION_VALUE 2   /* "dpace-continuation-value-only": w = S_j / P_j */
+
+/* DFlash kind values (reference: models/dflash/loss.py:169 _KINDS). */
+#define SPECDEC_DFLASH_KL 0
+#define SPECDEC_DFLASH_CE 1
+
+/* Library version, major * 10000 + minor * 100 + patch. */
+int specdec_version(void);
+
+/* Message for the last error on the calling thread ("" when none). */
+const char* specdec_last_error(void);
+
+/* Static name of a status code. */
+const char* specdec_status_string(int code);
+
+/* ------------------------------------------------------------------------- */
+/* D-PACE                                                                     */
+/* ------------------------------------------------------------------------- */
+
+/* Workspace sizes for specdec_dpace_forward on `device` (CUDA ordinal). */
+size_t specdec_dpace_scratch_bytes(int64_t N, int32_t B, int64_t V, int device);
+size_t specdec_dpace_counter_bytes(int64_t N, int32_t B);
+
+/*
+ * D-PACE forward. Replaces the launch of dpace_megakernel in
+ * losses/dpace.py:176-187 (_forward) and its host check losses/dpace.py:157-173
+ * (_check), returning what losses/dpace.py:215 returns (the mean over N).
+ *
+ *   logits    [N, B, V] fp32           targets [N, B] int64
+ *   mask      [N, B] fp32 or NULL      (NULL = every position scored; a
+ *                                       position is scored iff mask > 0)
+ *   n_global  divisor of the loss (N for one shard; the total sequence count
+ *             when N is one shard of a larger batch)
+ * Outputs (device):
+ *   loss      [1]     sum_n sum_j w_j * ce_j / n_global
+ *   loss_n    [N]     sum_j w_j * ce_j per sequence, or NULL
+ *   lse       [N, B]  row log-sum-exp (0 for unscored rows)
+ *   scale     [N, B]  w_j / n_global (dLoss/dce_j), 0 for unscored rows
+ *   status    [1]     int32: SPECDEC_OK, or SPECDEC_ERR_TARGET_RANGE when a
+ *                     target id lies outside [0, V) (the reference raises
+ *                     ValueError, losses/dpace.py:172-173); may be NULL
+ * Host-side errors: SPECDEC_ERR_ARGUMENT for B outside [1, 32], N < 0,
+ * V < 1, null required pointers; SPECDEC_ERR_VALUE for alpha outside [0, 1]
+ * or an unknown loss_type.
+ */
+int specdec_dpace_forward(const float* logits, const int64_t* targets, const float* mask,
+                          int64_t N, int32_t B, int64_t V, float alpha, int32_t loss_type,
+                          int64_t n_global, float* loss, float* loss_n, float* lse, float* scale,
+                          int32_t* status, void* scratch, size_t scratch_bytes, void* counters,
+                          size_t counter_bytes, void* stream);
+
+/*
+ * D-PACE backward. Replaces the launch of dpace_backward in
+ * losses/dpace.py:217-226 (DPACELoss.backward):
+ *   dlogits = scale[n, j] * dloss[0] * (softmax(logits[n, j]) - onehot(targets[n, j]))
+ * dloss may be NULL (treated as 1). dlogits must not alias logits.
+ */
+int specdec_dpace_backward(const float* logits, const int64_t* targets, const float* lse,
+                           const float* scale, const float* dloss, float* dlogits, int64_t N,
+                           int32_t B, int64_t V, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* DFlash objective                                                           */
+/* ------------------------------------------------------------------------- */
+
+size_t specdec_dflash_scratch_bytes(int64_t N, int32_t B, int64_t V, int device);
+size_t specdec_dflash_counter_bytes(int64_t N, int32_t B);
+
+/*
+ * DFlash forward. Replaces the launch of dflash_loss_fwd in
+ * models/dflash/loss.py:194-212 (_forward, including the denominator of
+ * loss.py:200) and its host check models/dflash/loss.py:178-191 (_check),
+ * returning what models/dflash/loss.py:257 returns (sum over rows / N).
+ *
+ *   logits, target_logits  [N, B, V] fp32 (draft, verifier)
+ *   mask        [N, B] fp32 or NULL (all ones); used as a raw weight
+ *   block_size  decay position of slot j is j % block_size, 1 <= block_size <= B
+ *   gamma > 0; sample_from_anchor 0/1; kind SPECDEC_DFLASH_KL or _CE
+ * Outputs: loss [1] (= sum_rows w * elementwise / n_global), loss_rows [N, B]
+ * or NULL, scale [N, B] (= w / n_global), logzq / logzp [N, B] (log-normalisers
+ * of draft / verifier; logzp is 0 for CE), target_id [N, B] int64 argmax of
+ * the verifier row (CE only; may be NULL for KL). Rows with weight 0 have
+ * zeros in every per-row output.
+ */
+int specdec_dflash_forward(const float* logits, const float* target_logits, const float* mask,
+                           int64_t N, int32_t B, int64_t V, int32_t block_size, float gamma,
+                           int32_t sample_from_anchor, int32_t kind, int64_t n_global, float* loss,
+                           float* loss_rows, float* scale, float* logzq, float* logzp,
+                           int64_t* target_id, void* scratch, size_t scratch_bytes, void* counters,
+                           size_t counter_bytes, void* stream);
+
+/*
+ * DFlash backward. Replaces the launch of dflash_loss_bwd in
+ * models/dflash/loss.py:259-269 (DFlashLoss.backward):
+ *   KL: dlogits = scale * dloss * (softmax(logits) - softmax(target_logits))
+ *   CE: dlogits = scale * dloss * (softmax(logits) - onehot(target_id))
+ * target_logits is read for KL only (may be NULL for CE); target_id for CE only.
+ */
+int specdec_dflash_backward(const float* logits, const float* target_logits, const float* scale,
+                            const float* logzq, const float* logzp, const int64_t* target_id,
+                            const float* dloss, float* dlogits, int64_t N, int32_t B, int64_t V,
+                            int32_t kind, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* Launch tuning                                                              */
+/* ------------------------------------------------------------------------- */
+
+/* Kernel ids for specdec_set_launch_shape. */
+#define SPECDEC_KERNEL_DPACE_FWD 0
+#define SPECDEC_KERNEL_DPACE_BWD 1
+#define SPECDEC_KERNEL_DFLASH_FWD 2
+#define SPECDEC_KERNEL_DFLASH_BWD 3
+
+/*
+ * Selects the (threads, unroll) instantiation `shape` (0 = default) and caps
+ * resident CTAs per SM (0 = occupancy limit) for one kernel, process-wide.
+ * Workspace sizes depend on it: query sizes after changing it.
+ */
+int specdec_set_launch_shape(int32_t kernel, int32_t shape, int32_t ctas_per_sm);
+
+/* Number of CTAs the kernel would launch for a problem of rows x V on device. */
+int64_t specdec_launch_ctas(int32_t kernel, int64_t rows, int64_t V, int device);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPECDEC_H_ */
