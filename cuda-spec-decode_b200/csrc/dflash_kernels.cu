@@ -11,9 +11,8 @@
 // Forward, one launch, ONE read of each row pair. With xl = draft logits,
 // xt = verifier logits, p = softmax(xt), q = softmax(xl):
 //   KL(p || q) = sum_v p_v (xt_v - xl_v) - logZp + logZq
-// Each piece keeps, in base 2 and relative to running maxima,
-//   sq = sum 2^(xl*log2e - m2q),  sp = sum 2^(xt*log2e - m2p),
-//   t  = sum 2^(xt*log2e - m2p) * (xt - xl),
+// Each piece keeps, relative to the running maxima mq (draft) and mp (verifier),
+//   sq = sum e^(xl - mq),  sp = sum e^(xt - mp),  t = sum e^(xt - mp) * (xt - xl),
 // (t rescales with the verifier max only), or for CE the first-index argmax
 // of xt with the draft logit at that index. The CTA landing last on a row
 // merges the pieces in slot order and writes the row's loss, scale and
@@ -30,16 +29,16 @@ namespace specdec {
 namespace {
 
 struct DfState {
-  float m2q, sq;      // draft log-sum-exp state
-  float m2p, sp, t;   // verifier log-sum-exp state and the p-weighted (xt - xl) sum (KL)
+  float mq, sq;      // draft log-sum-exp state (running max, sum of e^(x - max))
+  float mp, sp, t;   // verifier log-sum-exp state and the p-weighted (xt - xl) sum (KL)
   float bx, bl;       // CE: best verifier logit, draft logit at that index
   int bi;             // CE: index of the best verifier logit (first occurrence)
 };
 
 __device__ __forceinline__ void df_init(DfState& st) {
-  st.m2q = kNegSeed;
+  st.mq = kNegSeed;
   st.sq = 0.f;
-  st.m2p = kNegSeed;
+  st.mp = kNegSeed;
   st.sp = 0.f;
   st.t = 0.f;
   st.bx = -INFINITY;
@@ -49,13 +48,13 @@ __device__ __forceinline__ void df_init(DfState& st) {
 
 template <int KIND>
 __device__ __forceinline__ void df_merge(DfState& x, const DfState& o) {
-  lse2_merge(x.m2q, x.sq, o.m2q, o.sq);
+  lse_merge(x.mq, x.sq, o.mq, o.sq);
   if (KIND == kKindKL) {
-    const float M = fmaxf(x.m2p, o.m2p);
-    const float fa = exp2_approx(x.m2p - M), fb = exp2_approx(o.m2p - M);
+    const float M = fmaxf(x.mp, o.mp);
+    const float fa = exp_shift(x.mp, M), fb = exp_shift(o.mp, M);
     x.sp = x.sp * fa + o.sp * fb;
     x.t = x.t * fa + o.t * fb;
-    x.m2p = M;
+    x.mp = M;
   } else {
     if (o.bx > x.bx || (o.bx == x.bx && o.bi < x.bi)) {
       x.bx = o.bx;
@@ -68,10 +67,10 @@ __device__ __forceinline__ void df_merge(DfState& x, const DfState& o) {
 template <int KIND>
 __device__ __forceinline__ DfState df_shfl(const DfState& s, int o) {
   DfState r;
-  r.m2q = __shfl_xor_sync(kFullMask, s.m2q, o);
+  r.mq = __shfl_xor_sync(kFullMask, s.mq, o);
   r.sq = __shfl_xor_sync(kFullMask, s.sq, o);
   if (KIND == kKindKL) {
-    r.m2p = __shfl_xor_sync(kFullMask, s.m2p, o);
+    r.mp = __shfl_xor_sync(kFullMask, s.mp, o);
     r.sp = __shfl_xor_sync(kFullMask, s.sp, o);
     r.t = __shfl_xor_sync(kFullMask, s.t, o);
   } else {
@@ -94,16 +93,15 @@ __device__ __forceinline__ void df_warp_merge(DfState& s) {
 // One element (scalar path); idx is the index within the row.
 template <int KIND>
 __device__ __forceinline__ void df_push(DfState& s, float a, float b, int idx) {
-  lse2_push(s.m2q, s.sq, a);
+  lse_push(s.mq, s.sq, a);
   if (KIND == kKindKL) {
-    const float b2 = b * kLog2e;
-    if (b2 > s.m2p) {
-      const float f = exp2_approx(s.m2p - b2);
+    if (b > s.mp) {
+      const float f = exp_shift(s.mp, b);
       s.sp *= f;
       s.t *= f;
-      s.m2p = b2;
+      s.mp = b;
     }
-    const float e = exp2_approx(fmaf(b, kLog2e, -s.m2p));
+    const float e = exp_shift(b, s.mp);
     s.sp += e;
     s.t = fmaf(e, b - a, s.t);
   } else {
@@ -121,38 +119,36 @@ __device__ __forceinline__ void df_group(DfState& s, const float4 (&a)[U], const
   float cma = max4(a[0]);
 #pragma unroll
   for (int u = 1; u < U; ++u) cma = fmaxf(cma, max4(a[u]));
-  const float cma2 = cma * kLog2e;
-  if (cma2 > s.m2q) {
-    s.sq *= exp2_approx(s.m2q - cma2);
-    s.m2q = cma2;
+  if (cma > s.mq) {
+    s.sq *= exp_shift(s.mq, cma);
+    s.mq = cma;
   }
-  const float nq = -s.m2q;
+  const float mq = s.mq;
   float accq = 0.f;
 #pragma unroll
   for (int u = 0; u < U; ++u) {
-    accq += exp2_approx(fmaf(a[u].x, kLog2e, nq)) + exp2_approx(fmaf(a[u].y, kLog2e, nq)) +
-            exp2_approx(fmaf(a[u].z, kLog2e, nq)) + exp2_approx(fmaf(a[u].w, kLog2e, nq));
+    accq += exp_shift(a[u].x, mq) + exp_shift(a[u].y, mq) + exp_shift(a[u].z, mq) +
+            exp_shift(a[u].w, mq);
   }
   s.sq += accq;
   float cmb = max4(b[0]);
 #pragma unroll
   for (int u = 1; u < U; ++u) cmb = fmaxf(cmb, max4(b[u]));
   if (KIND == kKindKL) {
-    const float cmb2 = cmb * kLog2e;
-    if (cmb2 > s.m2p) {
-      const float f = exp2_approx(s.m2p - cmb2);
+    if (cmb > s.mp) {
+      const float f = exp_shift(s.mp, cmb);
       s.sp *= f;
       s.t *= f;
-      s.m2p = cmb2;
+      s.mp = cmb;
     }
-    const float np = -s.m2p;
+    const float mp = s.mp;
     float accp = 0.f, acct = 0.f;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const float ex = exp2_approx(fmaf(b[u].x, kLog2e, np));
-      const float ey = exp2_approx(fmaf(b[u].y, kLog2e, np));
-      const float ez = exp2_approx(fmaf(b[u].z, kLog2e, np));
-      const float ew = exp2_approx(fmaf(b[u].w, kLog2e, np));
+      const float ex = exp_shift(b[u].x, mp);
+      const float ey = exp_shift(b[u].y, mp);
+      const float ez = exp_shift(b[u].z, mp);
+      const float ew = exp_shift(b[u].w, mp);
       accp += (ex + ey) + (ez + ew);
       acct = fmaf(ex, b[u].x - a[u].x, acct);
       acct = fmaf(ey, b[u].y - a[u].y, acct);
@@ -256,16 +252,18 @@ __device__ void df_finalize_row(const DflashFwdArgs& a, int64_t r, int* sh_last)
       DfState o;
       const float4 lo4 = __ldcg(reinterpret_cast<const float4*>(part + q));
       const float4 hi4 = __ldcg(reinterpret_cast<const float4*>(part + q) + 1);
-      o.m2q = lo4.x; o.sq = lo4.y; o.m2p = lo4.z; o.sp = lo4.w;
+      o.mq = lo4.x; o.sq = lo4.y; o.mp = lo4.z; o.sp = lo4.w;
       o.t = hi4.x; o.bx = hi4.y; o.bl = hi4.z; o.bi = __float_as_int(hi4.w);
       df_merge<KIND>(s, o);
     }
     df_warp_merge<KIND>(s);
-    lzq = (s.m2q + log2f(s.sq)) * kLn2;
+    lzq = s.mq + logf(s.sq);
     if (KIND == kKindKL) {
-      lzp = (s.m2p + log2f(s.sp)) * kLn2;
-      // KL = sum p (xt - xl) - logZp + logZq, the normaliser difference taken in base 2
-      el = s.t / s.sp + ((s.m2q - s.m2p) + log2f(s.sq / s.sp)) * kLn2;
+      lzp = s.mp + logf(s.sp);
+      // KL = sum p (xt - xl) - logZp + logZq; the normaliser difference is
+      // (mq - mp) + log(sq / sp): one log of a ratio, no cancellation of two
+      // large log-normalisers
+      el = s.t / s.sp + ((s.mq - s.mp) + logf(s.sq / s.sp));
     } else {
       int bi = s.bi;
       float bl = s.bl;
@@ -323,7 +321,7 @@ __global__ void __launch_bounds__(NT) dflash_fwd_kernel(const __grid_constant__ 
         df_warp_merge<KIND>(s);
         if (lane == 0) {
           float4* dst = reinterpret_cast<float4*>(a.part + r * pt.pmax + (c - pt.first_cta(r)));
-          dst[0] = make_float4(s.m2q, s.sq, s.m2p, s.sp);
+          dst[0] = make_float4(s.mq, s.sq, s.mp, s.sp);
           dst[1] = make_float4(s.t, s.bx, s.bl, __int_as_float(s.bi));
         }
       }
@@ -387,12 +385,12 @@ __global__ void __launch_bounds__(NT) dflash_bwd_kernel(const __grid_constant__ 
       for (int64_t i = tid; i < body; i += NT) st_stream(q + i, z);
       continue;
     }
-    const float nq = -(a.logzq[r] * kLog2e);
-    const float np = -(a.logzp[r] * kLog2e);
+    const float lq = a.logzq[r];
+    const float lp = a.logzp[r];
     const int64_t t = (KIND == kKindCE ? a.target_id[r] : -1) - lo;
     auto elem = [&](float xl, float xt, int64_t i) -> float {
-      const float q = exp2_approx(fmaf(xl, kLog2e, nq));
-      const float p = KIND == kKindKL ? exp2_approx(fmaf(xt, kLog2e, np)) : (i == t ? 1.f : 0.f);
+      const float q = exp_shift(xl, lq);
+      const float p = KIND == kKindKL ? exp_shift(xt, lp) : (i == t ? 1.f : 0.f);
       return sc * (q - p);
     };
     for (int64_t i = tid; i < head; i += NT) dst[i] = elem(pl[i], KIND == kKindKL ? px[i] : 0.f, i);
@@ -414,15 +412,15 @@ __global__ void __launch_bounds__(NT) dflash_bwd_kernel(const __grid_constant__ 
       for (int u = 0; u < U; ++u) {
         const int64_t k = i + u * NT;
         float4 y;
-        y.x = exp2_approx(fmaf(va[u].x, kLog2e, nq));
-        y.y = exp2_approx(fmaf(va[u].y, kLog2e, nq));
-        y.z = exp2_approx(fmaf(va[u].z, kLog2e, nq));
-        y.w = exp2_approx(fmaf(va[u].w, kLog2e, nq));
+        y.x = exp_shift(va[u].x, lq);
+        y.y = exp_shift(va[u].y, lq);
+        y.z = exp_shift(va[u].z, lq);
+        y.w = exp_shift(va[u].w, lq);
         if (KIND == kKindKL) {
-          y.x -= exp2_approx(fmaf(vb[u].x, kLog2e, np));
-          y.y -= exp2_approx(fmaf(vb[u].y, kLog2e, np));
-          y.z -= exp2_approx(fmaf(vb[u].z, kLog2e, np));
-          y.w -= exp2_approx(fmaf(vb[u].w, kLog2e, np));
+          y.x -= exp_shift(vb[u].x, lp);
+          y.y -= exp_shift(vb[u].y, lp);
+          y.z -= exp_shift(vb[u].z, lp);
+          y.w -= exp_shift(vb[u].w, lp);
         } else {
           const uint64_t d = (uint64_t)(tb - 4 * k);
           if (d < 4) {
@@ -442,16 +440,16 @@ __global__ void __launch_bounds__(NT) dflash_bwd_kernel(const __grid_constant__ 
     for (; i < body; i += NT) {
       const float4 va = ld_last(ql + i, pol);
       float4 y;
-      y.x = exp2_approx(fmaf(va.x, kLog2e, nq));
-      y.y = exp2_approx(fmaf(va.y, kLog2e, nq));
-      y.z = exp2_approx(fmaf(va.z, kLog2e, nq));
-      y.w = exp2_approx(fmaf(va.w, kLog2e, nq));
+      y.x = exp_shift(va.x, lq);
+      y.y = exp_shift(va.y, lq);
+      y.z = exp_shift(va.z, lq);
+      y.w = exp_shift(va.w, lq);
       if (KIND == kKindKL) {
         const float4 vb = ld_last(qx + i, pol);
-        y.x -= exp2_approx(fmaf(vb.x, kLog2e, np));
-        y.y -= exp2_approx(fmaf(vb.y, kLog2e, np));
-        y.z -= exp2_approx(fmaf(vb.z, kLog2e, np));
-        y.w -= exp2_approx(fmaf(vb.w, kLog2e, np));
+        y.x -= exp_shift(vb.x, lp);
+        y.y -= exp_shift(vb.y, lp);
+        y.z -= exp_shift(vb.z, lp);
+        y.w -= exp_shift(vb.w, lp);
       } else {
         const uint64_t d = (uint64_t)(tb - 4 * i);
         if (d < 4) {

@@ -7,7 +7,7 @@
 //
 // Forward, one launch:
 //   1. every CTA streams its chunk of the flattened logits once, keeping an
-//      online base-2 log-sum-exp per row piece, and writes (m2, s) per piece to
+//      online log-sum-exp per row piece, and writes (max, sum) per piece to
 //      the workspace; the CTA whose piece holds the target id also stores
 //      x[target];
 //   2. a per-sequence arrival counter elects the CTA that lands last on
@@ -20,8 +20,7 @@
 // Rows whose position mask is 0 are never read: their weight is exactly 0,
 // so neither the loss nor the gradient depends on their logits.
 //
-// Backward, one launch: dlogits = scale * dloss * (2^(x*log2e - lse*log2e) -
-// onehot), one read and one write per element; rows with scale 0 are written
+// Backward, one launch: dlogits = scale * dloss * (exp(x - lse) - onehot), one read and one write per element; rows with scale 0 are written
 // as zeros without being read.
 #include "specdec_common.cuh"
 #include "specdec_internal.h"
@@ -41,15 +40,15 @@ __device__ __forceinline__ unsigned seq_piece_count(const Partition& pt, int64_t
 }
 
 template <int NT, int U>
-__device__ __forceinline__ void stream_lse2(const float* __restrict__ p, int64_t n, float& m2,
-                                            float& s) {
+__device__ __forceinline__ void stream_lse(const float* __restrict__ p, int64_t n, float& m,
+                                           float& s) {
   const int tid = threadIdx.x;
   int64_t head = ((16 - (reinterpret_cast<uintptr_t>(p) & 15)) & 15) >> 2;
   if (head > n) head = n;
   const int64_t body = (n - head) >> 2;
   const int64_t tail0 = head + (body << 2);
-  if (tid < head) lse2_push(m2, s, p[tid]);
-  if (tail0 + tid < n) lse2_push(m2, s, p[tail0 + tid]);
+  if (tid < head) lse_push(m, s, p[tid]);
+  if (tail0 + tid < n) lse_push(m, s, p[tail0 + tid]);
   const float4* q = reinterpret_cast<const float4*>(p + head);
   int64_t i = tid;
   for (; i + (U - 1) * NT < body; i += U * NT) {
@@ -59,30 +58,26 @@ __device__ __forceinline__ void stream_lse2(const float* __restrict__ p, int64_t
     float cm = max4(v[0]);
 #pragma unroll
     for (int u = 1; u < U; ++u) cm = fmaxf(cm, max4(v[u]));
-    const float cm2 = cm * kLog2e;
-    if (cm2 > m2) {
-      s *= exp2_approx(m2 - cm2);
-      m2 = cm2;
+    if (cm > m) {
+      s *= exp_shift(m, cm);
+      m = cm;
     }
-    const float nm = -m2;
     float acc = 0.f;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      acc += exp2_approx(fmaf(v[u].x, kLog2e, nm)) + exp2_approx(fmaf(v[u].y, kLog2e, nm)) +
-             exp2_approx(fmaf(v[u].z, kLog2e, nm)) + exp2_approx(fmaf(v[u].w, kLog2e, nm));
+      acc += exp_shift(v[u].x, m) + exp_shift(v[u].y, m) + exp_shift(v[u].z, m) +
+             exp_shift(v[u].w, m);
     }
     s += acc;
   }
   for (; i < body; i += NT) {
     const float4 v = ld_stream(q + i);
-    const float cm2 = max4(v) * kLog2e;
-    if (cm2 > m2) {
-      s *= exp2_approx(m2 - cm2);
-      m2 = cm2;
+    const float cm = max4(v);
+    if (cm > m) {
+      s *= exp_shift(m, cm);
+      m = cm;
     }
-    const float nm = -m2;
-    s += (exp2_approx(fmaf(v.x, kLog2e, nm)) + exp2_approx(fmaf(v.y, kLog2e, nm))) +
-         (exp2_approx(fmaf(v.z, kLog2e, nm)) + exp2_approx(fmaf(v.w, kLog2e, nm)));
+    s += (exp_shift(v.x, m) + exp_shift(v.y, m)) + (exp_shift(v.z, m) + exp_shift(v.w, m));
   }
 }
 
@@ -99,17 +94,17 @@ __device__ void dpace_finalize_sequence(const DpaceFwdArgs& a, int64_t n, float*
   for (int j = w; j < B; j += NW) {
     const int64_t r = n * B + j;
     const bool live = a.mask == nullptr || a.mask[r] > 0.f;
-    float m2 = kNegSeed, s = 0.f;
+    float m = kNegSeed, s = 0.f;
     if (live) {
       const int k = a.pt.pieces(r);
       const float2* part = a.part + r * a.pt.pmax;
       for (int q = lane; q < k; q += 32) {
         const float2 v = __ldcg(part + q);
-        lse2_merge(m2, s, v.x, v.y);
+        lse_merge(m, s, v.x, v.y);
       }
-      warp_lse2(m2, s);
+      warp_lse(m, s);
     }
-    if (lane == 0) sh_lse[j] = live ? (m2 + log2f(s)) * kLn2 : 0.f;
+    if (lane == 0) sh_lse[j] = live ? m + logf(s) : 0.f;
   }
   __syncthreads();
   // Phase B: the B-scan (B <= 32) in warp 0. The prefix product and the
@@ -202,11 +197,11 @@ __global__ void __launch_bounds__(NT) dpace_fwd_kernel(const __grid_constant__ D
     const bool live = a.mask == nullptr || a.mask[r] > 0.f;
     if (live) {
       const float* row = a.logits + row0;
-      float m2 = kNegSeed, s = 0.f;
-      stream_lse2<NT, U>(row + lo, hi - lo, m2, s);
-      block_lse2<NT>(m2, s, sh_red);
+      float m = kNegSeed, s = 0.f;
+      stream_lse<NT, U>(row + lo, hi - lo, m, s);
+      block_lse<NT>(m, s, sh_red);
       if (tid == 0) {
-        a.part[r * pt.pmax + (c - pt.first_cta(r))] = make_float2(m2, s);
+        a.part[r * pt.pmax + (c - pt.first_cta(r))] = make_float2(m, s);
         const int64_t t = a.targets[r];
         if (t >= lo && t < hi) a.xtgt[r] = row[t];
       }
@@ -242,7 +237,7 @@ __global__ void __launch_bounds__(NT) dpace_bwd_kernel(const __grid_constant__ D
     const float* src = a.logits + row0 + lo;
     float* dst = a.dlogits + row0 + lo;
     const int64_t t = a.targets[r] - lo;  // target position relative to the piece
-    const float nl2 = -(a.lse[r] * kLog2e);
+    const float l = a.lse[r];
     // Vector path when source and destination share 16-byte phase.
     const bool vec = ((reinterpret_cast<uintptr_t>(src) ^ reinterpret_cast<uintptr_t>(dst)) & 15) == 0;
     int64_t head = vec ? (((16 - (reinterpret_cast<uintptr_t>(src) & 15)) & 15) >> 2) : n;
@@ -258,9 +253,9 @@ __global__ void __launch_bounds__(NT) dpace_bwd_kernel(const __grid_constant__ D
       continue;
     }
     for (int64_t i = tid; i < head; i += NT)
-      dst[i] = sc * (exp2_approx(fmaf(src[i], kLog2e, nl2)) - (i == t ? 1.f : 0.f));
+      dst[i] = sc * (exp_shift(src[i], l) - (i == t ? 1.f : 0.f));
     for (int64_t i = tail0 + tid; i < n; i += NT)
-      dst[i] = sc * (exp2_approx(fmaf(src[i], kLog2e, nl2)) - (i == t ? 1.f : 0.f));
+      dst[i] = sc * (exp_shift(src[i], l) - (i == t ? 1.f : 0.f));
     const float4* qs = reinterpret_cast<const float4*>(src + head);
     float4* qd = reinterpret_cast<float4*>(dst + head);
     const int64_t tb = t - head;  // target relative to the vector body
@@ -273,10 +268,10 @@ __global__ void __launch_bounds__(NT) dpace_bwd_kernel(const __grid_constant__ D
       for (int u = 0; u < U; ++u) {
         const int64_t k = i + u * NT;
         float4 y;
-        y.x = exp2_approx(fmaf(v[u].x, kLog2e, nl2));
-        y.y = exp2_approx(fmaf(v[u].y, kLog2e, nl2));
-        y.z = exp2_approx(fmaf(v[u].z, kLog2e, nl2));
-        y.w = exp2_approx(fmaf(v[u].w, kLog2e, nl2));
+        y.x = exp_shift(v[u].x, l);
+        y.y = exp_shift(v[u].y, l);
+        y.z = exp_shift(v[u].z, l);
+        y.w = exp_shift(v[u].w, l);
         const uint64_t d = (uint64_t)(tb - 4 * k);
         if (d < 4) {
           if (d == 0) y.x -= 1.f;
@@ -294,10 +289,10 @@ __global__ void __launch_bounds__(NT) dpace_bwd_kernel(const __grid_constant__ D
     for (; i < body; i += NT) {
       const float4 v = ld_last(qs + i, pol);
       float4 y;
-      y.x = exp2_approx(fmaf(v.x, kLog2e, nl2));
-      y.y = exp2_approx(fmaf(v.y, kLog2e, nl2));
-      y.z = exp2_approx(fmaf(v.z, kLog2e, nl2));
-      y.w = exp2_approx(fmaf(v.w, kLog2e, nl2));
+      y.x = exp_shift(v.x, l);
+      y.y = exp_shift(v.y, l);
+      y.z = exp_shift(v.z, l);
+      y.w = exp_shift(v.w, l);
       const uint64_t d = (uint64_t)(tb - 4 * i);
       if (d < 4) {
         if (d == 0) y.x -= 1.f;

@@ -66,51 +66,53 @@ __device__ __forceinline__ float max4(const float4& v) {
 }
 
 // ---------------------------------------------------------------------------
-// Online log-sum-exp in base 2: the state (m2, s) stands for s * 2^m2, where
-// m2 = fl(max_x * log2 e). Each element contributes 2^(x*log2e - m2) computed
-// with one FMA + one EX2; the max is refreshed once per loaded group, not per
-// element. log-sum-exp(x) = (m2 + log2 s) * ln 2.
+// Online log-sum-exp: the state (m, s) stands for s * e^m with m the running
+// max; each element contributes e^(x - m) = 2^((x - m) * log2 e) (FADD, FMUL,
+// MUFU.EX2). The max element contributes exactly 1, as in torch's
+// log_softmax, and the max is refreshed once per loaded group, not per
+// element. log-sum-exp(x) = m + log(s).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void lse2_merge(float& m2, float& s, float om2, float os) {
-  const float M = fmaxf(m2, om2);
-  s = s * exp2_approx(m2 - M) + os * exp2_approx(om2 - M);
-  m2 = M;
+__device__ __forceinline__ float exp_shift(float x, float m) { return exp2_approx((x - m) * kLog2e); }
+
+__device__ __forceinline__ void lse_merge(float& m, float& s, float om, float os) {
+  const float M = fmaxf(m, om);
+  s = s * exp_shift(m, M) + os * exp_shift(om, M);
+  m = M;
 }
 
-__device__ __forceinline__ void lse2_push(float& m2, float& s, float x) {
-  const float x2 = x * kLog2e;
-  if (x2 > m2) {
-    s *= exp2_approx(m2 - x2);
-    m2 = x2;
+__device__ __forceinline__ void lse_push(float& m, float& s, float x) {
+  if (x > m) {
+    s *= exp_shift(m, x);
+    m = x;
   }
-  s += exp2_approx(fmaf(x, kLog2e, -m2));
+  s += exp_shift(x, m);
 }
 
-__device__ __forceinline__ void warp_lse2(float& m2, float& s) {
+__device__ __forceinline__ void warp_lse(float& m, float& s) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
-    const float om2 = __shfl_xor_sync(kFullMask, m2, o);
+    const float om = __shfl_xor_sync(kFullMask, m, o);
     const float os = __shfl_xor_sync(kFullMask, s, o);
-    lse2_merge(m2, s, om2, os);
+    lse_merge(m, s, om, os);
   }
 }
 
-// Block-wide (m2, s) merge in a fixed butterfly order. `sh` holds 2*NT/32
+// Block-wide (m, s) merge in a fixed butterfly order. `sh` holds 2*NT/32
 // floats. The result is valid in every lane of warp 0. Ends with a barrier.
 template <int NT>
-__device__ __forceinline__ void block_lse2(float& m2, float& s, float* sh) {
+__device__ __forceinline__ void block_lse(float& m, float& s, float* sh) {
   constexpr int NW = NT / 32;
-  warp_lse2(m2, s);
+  warp_lse(m, s);
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   if (lane == 0) {
-    sh[w] = m2;
+    sh[w] = m;
     sh[NW + w] = s;
   }
   __syncthreads();
   if (w == 0) {
-    m2 = lane < NW ? sh[lane] : kNegSeed;
+    m = lane < NW ? sh[lane] : kNegSeed;
     s = lane < NW ? sh[NW + lane] : 0.f;
-    warp_lse2(m2, s);
+    warp_lse(m, s);
   }
   __syncthreads();
 }

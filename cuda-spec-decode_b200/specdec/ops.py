@@ -30,7 +30,7 @@ def set_target_validation(enabled: bool) -> None:
     VALIDATE_TARGETS = bool(enabled)
 
 
-def dpace_forward(logits: torch.Tensor, targets: torch.Tensor, mask: torch.Tensor | None,
+def _dpace_forward(logits: torch.Tensor, targets: torch.Tensor, mask: torch.Tensor | None,
                   alpha: float, loss_type: int, n_global: int | None = None,
                   want_loss_n: bool = False, validate: bool | None = None):
     """Returns (loss 0-d, lse [N,B], scale [N,B], loss_n [N] or None)."""
@@ -59,7 +59,7 @@ def dpace_forward(logits: torch.Tensor, targets: torch.Tensor, mask: torch.Tenso
     return loss, lse, scale, loss_n
 
 
-def dpace_backward(logits: torch.Tensor, targets: torch.Tensor, lse: torch.Tensor,
+def _dpace_backward(logits: torch.Tensor, targets: torch.Tensor, lse: torch.Tensor,
                    scale: torch.Tensor, dloss: torch.Tensor | None,
                    out: torch.Tensor | None = None) -> torch.Tensor:
     lib = _lib.load()
@@ -74,7 +74,7 @@ def dpace_backward(logits: torch.Tensor, targets: torch.Tensor, lse: torch.Tenso
     return dlogits
 
 
-def dflash_forward(logits: torch.Tensor, target_logits: torch.Tensor, mask: torch.Tensor | None,
+def _dflash_forward(logits: torch.Tensor, target_logits: torch.Tensor, mask: torch.Tensor | None,
                    gamma: float, sample_from_anchor: bool, kind: int, block_size: int,
                    n_global: int | None = None):
     """Returns (loss 0-d, loss_rows [N,B], scale [N,B], logzq [N,B], logzp [N,B], tgt [N,B] or None)."""
@@ -102,7 +102,7 @@ def dflash_forward(logits: torch.Tensor, target_logits: torch.Tensor, mask: torc
     return loss, loss_rows, scale, logzq, logzp, tgt
 
 
-def dflash_backward(logits: torch.Tensor, target_logits: torch.Tensor | None, scale: torch.Tensor,
+def _dflash_backward(logits: torch.Tensor, target_logits: torch.Tensor | None, scale: torch.Tensor,
                     logzq: torch.Tensor, logzp: torch.Tensor, tgt: torch.Tensor | None,
                     dloss: torch.Tensor | None, kind: int,
                     out: torch.Tensor | None = None) -> torch.Tensor:
@@ -117,3 +117,20 @@ def dflash_backward(logits: torch.Tensor, target_logits: torch.Tensor | None, sc
         _lib.stream_handle(logits.device))
     _lib.check(code, "specdec_dflash_backward")
     return dlogits
+
+
+def _on_device(fn):
+    def wrapped(logits, *args, **kwargs):
+        with torch.cuda.device(logits.device):
+            return fn(logits, *args, **kwargs)
+    wrapped.__name__ = fn.__name__.lstrip("_")
+    wrapped.__doc__ = fn.__doc__
+    return wrapped
+
+
+# Launches go to the tensors' device (and that device's current stream),
+# whatever the caller's current device is.
+dpace_forward = _on_device(_dpace_forward)
+dpace_backward = _on_device(_dpace_backward)
+dflash_forward = _on_device(_dflash_forward)
+dflash_backward = _on_device(_dflash_backward)
