@@ -1,0 +1,463 @@
+// D-PACE forward and backward on the warp-specialized CTA ring (ring.cuh).
+//
+// Same arithmetic and outputs as dpace_kernels.cu (the 128-bit-load kernels,
+// kept for inputs whose base address is not 16-byte aligned).
+//
+// Forward = two launches on the stream:
+//   1. dpace_fwd_ring_kernel streams the logits once. Each consumer warp keeps
+//      an online (max, sum of e^(x - max)) for the row it is in and, whenever
+//      a (row, block) piece ends, stores it to
+//      part[((r * pmax + block_in_row) * NC) + warp]. Plain stores only, no
+//      counters, no global loads in the consumers.
+//   2. dpace_finalize_kernel (chained with programmatic dependent launch): one
+//      CTA per sequence, warp j <-> row j merges the row's partials in slot
+//      order -> lse_j, reads x[target_j], ce_j = lse_j - x[target_j]; warp 0 runs the B-scan
+//      (q, smoothing, prefix product, suffix sum, weights), writes scale and
+//      loss_n; the last CTA (done counter) sums loss_n in index order.
+// Backward = one launch: dpace_bwd_ring_kernel streams logits through the ring
+// and writes (w_j / N) * dloss * (softmax - onehot) with streaming stores.
+// Rows with position mask 0 are never copied (forward); rows with scale 0 are
+// never copied and written as zeros (backward).
+//
+// Reference behaviour: losses/dpace.py:15-118 (forward), :120-145 (backward);
+// numbers follow losses/dpace_ref.py:8-51.
+#include <cfloat>
+
+#include "ring.cuh"
+#include "specdec_common.cuh"
+#include "specdec_internal.h"
+
+namespace specdec {
+
+namespace {
+
+template <int NC, int S, int SE, int BS>
+__global__ void __launch_bounds__((NC + 1) * 32, 1) dpace_fwd_ring_kernel(const __grid_constant__ DpaceFwdArgs a) {
+  constexpr int kSub = SE / NC;
+  constexpr int64_t BL = (int64_t)BS * SE;
+  constexpr int kLogBL = __builtin_ctzll(BL);
+  static_assert(kSub % 128 == 0, "sub-range must be whole float4 rounds of a warp");
+  static_assert((BL & (BL - 1)) == 0, "block length must be a power of two");
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  auto& sm = *reinterpret_cast<RingSmem<1, S, SE>*>(smem_raw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t E = a.pt.E, V = a.pt.V, R = E / V;
+  const int pmax = a.pt.pmax;
+
+  ring_init(sm, NC);
+  const RowBits rb = build_row_bits(sm.bits, R, NC + 1, [&](int64_t r) {
+    return a.mask == nullptr || a.mask[r] > 0.f;
+  });
+  __syncthreads();
+
+  BlockQueue q;
+  q.ctr = a.q_ctr;
+  q.retired = a.q_retired;
+  q.nblocks = (unsigned)((E + BL - 1) / BL);
+  q.dynamic = a.q_dynamic;
+
+  if (warp == NC) {  // producer
+    if (lane == 0) {
+      const float* src[1] = {a.logits};
+      if (!ring_produce<1, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow)) {
+        atomicOr(a.flag, 2);
+        if (a.status) a.status[0] = kStatusTimeout;
+      }
+    }
+    pdl_trigger();
+    return;
+  }
+
+  // consumer warp `warp`
+  float m = kNegSeed, s = 0.f;
+  int64_t r = 0, blk = -1;
+  bool live = false;
+  auto enter_row = [&](int64_t row) {
+    live = row < R && (rb.valid ? rb.live(row) : (a.mask == nullptr || a.mask[row] > 0.f));
+  };
+  auto close_piece = [&]() {  // the (r, blk) piece of this warp is complete
+    if (live) {
+      warp_lse(m, s);
+      if (lane == 0) {
+        const int64_t slot = blk - (r * V) / BL;
+        a.part[(r * pmax + slot) * NC + warp] = make_float2(m, s);
+      }
+    }
+    m = kNegSeed;
+    s = 0.f;
+  };
+  for (int64_t it = 0;; ++it) {
+    const int slot = (int)(it % S);
+    if (!__all_sync(kFullMask, mbar_wait(sm.full + slot, (uint32_t)((it / S) & 1)))) {
+      if (lane == 0) {
+        atomicOr(a.flag, 2);
+        if (a.status) a.status[0] = kStatusTimeout;
+      }
+      ring_drain<S>(sm.full, it + 1);
+      break;
+    }
+    const int64_t f0 = sm.sf0[slot];
+    if (f0 < 0) break;
+    const int64_t b = f0 >> kLogBL;
+    const int64_t blk_end = min((b + 1) * BL, E);
+    const int64_t f1 = min(f0 + SE, blk_end);
+    if (b != blk) {  // first stage of a new block
+      blk = b;
+      r = sm.srow[slot];
+      enter_row(r);
+    }
+    const float* sb = sm.ring + (size_t)slot * SE;
+    if (f1 - f0 == SE && (r + 1) * V >= f1) {
+      // fast path: a full stage inside one row
+      if (live) warp_lse_full<kSub>(sb + warp * kSub, m, s);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sm.empty + slot);
+      if ((r + 1) * V == f1) {
+        close_piece();
+        ++r;
+        enter_row(r);
+      } else if (f1 == blk_end) {
+        close_piece();  // the block ends inside row r
+      }
+      continue;
+    }
+    const int64_t fv = f0 + ((((f1 - f0) * 4) & ~int64_t(15)) >> 2);  // end of the copied part
+    const int64_t w0 = f0 + (int64_t)warp * kSub, w1 = min(w0 + kSub, f1);
+    int64_t f = f0;
+    while (f < f1) {
+      const int64_t rend = (r + 1) * V;
+      const int64_t g = min(f1, rend);
+      if (live) {
+        const int64_t lo = max(f, w0), hi = min(g, w1);
+        const int64_t hv = min(hi, fv);
+        if (hv > lo) warp_lse_smem(sb, (int)(lo - f0), (int)(hv - f0), m, s);
+        for (int64_t x = max(lo, fv) + lane; x < hi; x += 32) lse_push(m, s, __ldg(a.logits + x));
+      }
+      f = g;
+      if (g == rend) {
+        close_piece();
+        ++r;
+        enter_row(r);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(sm.empty + slot);
+    if (f1 == blk_end && r * V < blk_end) close_piece();  // the block ends inside row r
+  }
+  pdl_trigger();
+}
+
+// One CTA per sequence n, warp j <-> row j (B <= 32 warps).
+__global__ void __launch_bounds__(1024) dpace_finalize_kernel(const __grid_constant__ DpaceFwdArgs a) {
+  __shared__ float sh_ce[32];
+  pdl_wait();  // the streaming grid has completed and its stores are visible
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int B = a.B;
+  const int64_t n = blockIdx.x, V = a.pt.V, BL = a.pt.chunk;
+  const int NC = a.nc;
+  {
+    const int64_t r = n * B + warp;
+    // independent loads first: mask, target id, the row's partials
+    const float mk = a.mask ? a.mask[r] : 1.f;
+    const int64_t t = a.targets[r];
+    const int k = blocks_in_row(r, V, BL) * NC;
+    const float2* part = a.part + r * a.pt.pmax * NC;
+    float2 pv[2];
+    pv[0] = lane < k ? part[lane] : make_float2(kNegSeed, 0.f);
+    pv[1] = lane + 32 < k ? part[lane + 32] : make_float2(kNegSeed, 0.f);
+    const bool tvalid = t >= 0 && t < V;
+    const float xt = tvalid ? __ldg(a.logits + r * V + t) : 0.f;  // x[target], read once per row
+    const bool live = mk > 0.f;
+    float lse = 0.f, ce = 0.f;
+    if (live) {
+      float m = pv[0].x, s = pv[0].y;  // slot-major, warp-minor, then a fixed butterfly
+      lse_merge(m, s, pv[1].x, pv[1].y);
+      for (int qd = lane + 64; qd < k; qd += 32) {
+        const float2 v = part[qd];
+        lse_merge(m, s, v.x, v.y);
+      }
+      warp_lse(m, s);
+      lse = m + logf(s);
+      if (tvalid) ce = lse - xt;
+    }
+    if (!tvalid && lane == 0) atomicOr(a.flag, 1);
+    if (lane == 0) {
+      a.lse[r] = lse;
+      sh_ce[warp] = ce;
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int j = lane;
+    const bool in = j < B;
+    const int64_t r = n * B + (in ? j : 0);
+    const bool live = in && (a.mask == nullptr || a.mask[r] > 0.f);
+    const float ce = in ? sh_ce[j] : 0.f;
+    const float mk = live ? 1.f : 0.f;
+    const float sm = live ? __fadd_rn(__fmul_rn(a.one_minus_alpha, expf(-ce)), a.alpha) : 1.f;
+    // prefix product and suffix sum in double, in sequence order (torch CPU
+    // cumprod / cumsum accumulate in double); every lane runs the serial scan
+    double run = 1.0;
+    float P = 1.f;
+    for (int i = 0; i < B; ++i) {
+      run *= (double)__shfl_sync(kFullMask, sm, i);
+      if (i == j) P = (float)run;
+    }
+    const float pm = __fmul_rn(P, mk);
+    double acc = 0.0;
+    float S = 0.f;
+    for (int i = B - 1; i >= 0; --i) {
+      acc += (double)__shfl_sync(kFullMask, pm, i);
+      if (i == j) S = (float)acc;
+    }
+    float w = a.loss_type == 1 ? P : (a.loss_type == 2 ? __fdiv_rn(S, fmaxf(P, FLT_MIN)) : S);
+    w = __fmul_rn(w, mk);
+    const float contrib = live ? __fmul_rn(ce, w) : 0.f;
+    if (in) a.scale[r] = __fmul_rn(w, a.inv_n);
+    const float loss_n = warp_sum(contrib);
+    unsigned last = 0;
+    if (lane == 0) {
+      if (a.loss_n) a.loss_n[n] = loss_n;
+      a.seq_loss[n] = loss_n;
+      __threadfence();
+      last = (atomicAdd(a.done_cnt, 1u) + 1 == (unsigned)a.N);
+    }
+    last = __shfl_sync(kFullMask, last, 0);
+    if (last) {
+      __threadfence();
+      const float total = warp_sum_l2(a.seq_loss, a.N);
+      if (lane == 0) {
+        a.loss[0] = total / (float)a.n_global;
+        const int f = atomicExch(a.flag, 0);
+        if (a.status) a.status[0] = (f & 2) ? kStatusTimeout : ((f & 1) ? kStatusTargetRange : kStatusOk);
+        *a.done_cnt = 0u;
+      }
+    }
+  }
+}
+
+template <int NC, int S, int SE, int BS>
+__global__ void __launch_bounds__((NC + 1) * 32, 1) dpace_bwd_ring_kernel(const __grid_constant__ DpaceBwdArgs a) {
+  constexpr int kSub = SE / NC;
+  constexpr int64_t BL = (int64_t)BS * SE;
+  static_assert(kSub % 4 == 0, "sub-range must be whole float4s");
+  static_assert((BL & (BL - 1)) == 0, "block length must be a power of two");
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  auto& sm = *reinterpret_cast<RingSmem<1, S, SE>*>(smem_raw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t E = a.pt.E, V = a.pt.V, R = E / V;
+  const float g = a.dloss ? __ldg(a.dloss) : 1.f;
+
+  ring_init(sm, NC);
+  const RowBits rb = build_row_bits(sm.bits, R, NC + 1, [&](int64_t r) {
+    return __fmul_rn(a.scale[r], g) != 0.f;
+  });
+  __syncthreads();
+
+  BlockQueue q;
+  q.ctr = a.q_ctr;
+  q.retired = a.q_retired;
+  q.nblocks = (unsigned)((E + BL - 1) / BL);
+  q.dynamic = a.q_dynamic;
+
+  if (warp == NC) {
+    if (lane == 0) {
+      const float* src[1] = {a.logits};
+      if (!ring_produce<1, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow) && a.flag)
+        atomicOr(a.flag, 2);
+    }
+    return;
+  }
+
+  int64_t r = 0, blk = -1, tf = -1;
+  float sc = 0.f, l = 0.f;
+  auto load_row = [&](int64_t row) {
+    sc = __fmul_rn(a.scale[row], g);
+    l = a.lse[row];
+    tf = row * V + a.targets[row];
+  };
+  for (int64_t it = 0;; ++it) {
+    const int slot = (int)(it % S);
+    if (!__all_sync(kFullMask, mbar_wait(sm.full + slot, (uint32_t)((it / S) & 1)))) {
+      if (lane == 0 && a.flag) atomicOr(a.flag, 2);
+      ring_drain<S>(sm.full, it + 1);
+      return;
+    }
+    const int64_t f0 = sm.sf0[slot];
+    if (f0 < 0) return;
+    const int64_t b = f0 / BL;
+    const int64_t blk_end = min((b + 1) * BL, E);
+    const int64_t f1 = min(f0 + SE, blk_end);
+    if (b != blk) {
+      blk = b;
+      r = sm.srow[slot];
+      load_row(r);
+    }
+    const int64_t fv = f0 + ((((f1 - f0) * 4) & ~int64_t(15)) >> 2);
+    const int64_t w0 = f0 + (int64_t)warp * kSub, w1 = min(w0 + kSub, f1);
+    const float* sb = sm.ring + (size_t)slot * SE;
+    int64_t f = f0;
+    while (f < f1) {
+      const int64_t rend = (r + 1) * V;
+      const int64_t ge = min(f1, rend);
+      const int64_t lo = max(f, w0), hi = min(ge, w1);
+      if (lo < hi) {
+        const bool zero = sc == 0.f || !rb.live(r);
+        // [lo, hi): scalar head to a 4-element boundary, float4 body, scalar tail
+        const int64_t lo4 = (lo + 3) & ~int64_t(3), hi4 = min(hi, fv) & ~int64_t(3);
+        float* dst = a.dlogits;
+        auto scalar = [&](int64_t x) {
+          if (zero) {
+            dst[x] = 0.f;
+          } else {
+            const float v = x < fv ? sb[x - f0] : __ldg(a.logits + x);
+            dst[x] = sc * (exp_shift(v, l) - (x == tf ? 1.f : 0.f));
+          }
+        };
+        if (lo4 < hi4) {
+          for (int64_t x = lo + lane; x < lo4; x += 32) scalar(x);
+          for (int64_t x = hi4 + lane; x < hi; x += 32) scalar(x);
+          float4* d4 = reinterpret_cast<float4*>(dst + lo4);
+          const float4* s4 = reinterpret_cast<const float4*>(sb + (lo4 - f0));
+          const int n4 = (int)((hi4 - lo4) >> 2);
+          if (zero) {
+            const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int k = lane; k < n4; k += 32) st_stream(d4 + k, z);
+          } else {
+            const int64_t tq = tf - lo4;
+            for (int k = lane; k < n4; k += 32) {
+              const float4 v = s4[k];
+              float4 y;
+              y.x = exp_shift(v.x, l);
+              y.y = exp_shift(v.y, l);
+              y.z = exp_shift(v.z, l);
+              y.w = exp_shift(v.w, l);
+              const uint64_t d = (uint64_t)(tq - 4 * (int64_t)k);
+              if (d < 4) {
+                if (d == 0) y.x -= 1.f;
+                else if (d == 1) y.y -= 1.f;
+                else if (d == 2) y.z -= 1.f;
+                else y.w -= 1.f;
+              }
+              y.x *= sc;
+              y.y *= sc;
+              y.z *= sc;
+              y.w *= sc;
+              st_stream(d4 + k, y);
+            }
+          }
+        } else {
+          for (int64_t x = lo + lane; x < hi; x += 32) scalar(x);
+        }
+      }
+      f = ge;
+      if (ge == rend && ge < E) {
+        ++r;
+        load_row(r);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(sm.empty + slot);
+  }
+}
+
+template <int NC, int S, int SE, int BS>
+struct RingVariant {
+  static constexpr size_t smem() { return sizeof(RingSmem<1, S, SE>); }
+  static int fwd_ctas(int device, int cap) {
+    return ring_occupancy_ctas(dpace_fwd_ring_kernel<NC, S, SE, BS>, (NC + 1) * 32, smem(), device, cap);
+  }
+  static int bwd_ctas(int device, int cap) {
+    return ring_occupancy_ctas(dpace_bwd_ring_kernel<NC, S, SE, BS>, (NC + 1) * 32, smem(), device, cap);
+  }
+  static cudaError_t fwd(DpaceFwdArgs a, int ctas, cudaStream_t st) {
+    // the attribute must be set on the launching device before the launch
+    cudaFuncSetAttribute(dpace_fwd_ring_kernel<NC, S, SE, BS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem());
+    a.nc = NC;
+    dpace_fwd_ring_kernel<NC, S, SE, BS><<<ctas, (NC + 1) * 32, smem(), st>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    return launch_pdl(dpace_finalize_kernel, dim3((unsigned)a.N), dim3(32 * a.B), st, a);
+  }
+  static cudaError_t bwd(const DpaceBwdArgs& a, int ctas, cudaStream_t st) {
+    cudaFuncSetAttribute(dpace_bwd_ring_kernel<NC, S, SE, BS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem());
+    dpace_bwd_ring_kernel<NC, S, SE, BS><<<ctas, (NC + 1) * 32, smem(), st>>>(a);
+    return cudaGetLastError();
+  }
+};
+
+// Ring shapes (consumer warps x stages x stage floats x stages per block):
+// 0 = 4 x 4 x 4096 x 4 (64 KB ring, 64 KB blocks, 3 CTAs/SM: the fastest
+// measured on the [64, 16, 128256] workload); 1 = 8 x 4 x 8192 x 2 (128 KB
+// ring, 1 CTA/SM); 2 = 4 x 6 x 4096 x 4 (96 KB ring, 2 CTAs/SM); 3 = 4 x 8 x
+// 4096 x 8 (128 KB ring, 128 KB blocks); 4 = 2 x 6 x 2048 x 8 (48 KB ring,
+// 4 CTAs/SM).
+using R0 = RingVariant<4, 4, 4096, 4>;
+using R1 = RingVariant<8, 4, 8192, 2>;
+using R2 = RingVariant<4, 6, 4096, 4>;
+using R3 = RingVariant<4, 8, 4096, 8>;
+using R4 = RingVariant<2, 6, 2048, 8>;
+
+}  // namespace
+
+int dpace_ring_block_elems(int shape) {
+  switch (shape) {
+    case 1: return 8192 * 2;
+    case 2: return 4096 * 4;
+    case 3: return 4096 * 8;
+    case 4: return 2048 * 8;
+    default: return 4096 * 4;
+  }
+}
+
+int dpace_ring_consumers(int shape) {
+  switch (shape) {
+    case 1: return 8;
+    case 4: return 2;
+    default: return 4;
+  }
+}
+
+int dpace_fwd_ring_ctas(int shape, int device, int cap) {
+  switch (shape) {
+    case 1: return R1::fwd_ctas(device, cap);
+    case 2: return R2::fwd_ctas(device, cap);
+    case 3: return R3::fwd_ctas(device, cap);
+    case 4: return R4::fwd_ctas(device, cap);
+    default: return R0::fwd_ctas(device, cap);
+  }
+}
+
+int dpace_bwd_ring_ctas(int shape, int device, int cap) {
+  switch (shape) {
+    case 1: return R1::bwd_ctas(device, cap);
+    case 2: return R2::bwd_ctas(device, cap);
+    case 3: return R3::bwd_ctas(device, cap);
+    case 4: return R4::bwd_ctas(device, cap);
+    default: return R0::bwd_ctas(device, cap);
+  }
+}
+
+cudaError_t dpace_fwd_ring_launch(int shape, const DpaceFwdArgs& a, int ctas, cudaStream_t st) {
+  switch (shape) {
+    case 1: return R1::fwd(a, ctas, st);
+    case 2: return R2::fwd(a, ctas, st);
+    case 3: return R3::fwd(a, ctas, st);
+    case 4: return R4::fwd(a, ctas, st);
+    default: return R0::fwd(a, ctas, st);
+  }
+}
+
+cudaError_t dpace_bwd_ring_launch(int shape, const DpaceBwdArgs& a, int ctas, cudaStream_t st) {
+  switch (shape) {
+    case 1: return R1::bwd(a, ctas, st);
+    case 2: return R2::bwd(a, ctas, st);
+    case 3: return R3::bwd(a, ctas, st);
+    case 4: return R4::bwd(a, ctas, st);
+    default: return R0::bwd(a, ctas, st);
+  }
+}
+
+}  // namespace specdec

@@ -1,0 +1,276 @@
+// Warp-specialized CTA streaming ring for sm_100a (shared by the ring kernels).
+//
+// A persistent CTA has two roles:
+//   - producer warp (lane 0): takes BLOCKS of BS * SE flattened elements from
+//     a global atomic queue (or a static interleave) and keeps S shared-memory
+//     stages in flight with cp.async.bulk; per stage it posts the stage's
+//     flattened start in `sf0` and completes `full[slot]` (byte count);
+//   - NC consumer warps: wait on `full[slot]`, each reduces / transforms its
+//     own contiguous SE/NC sub-range of the stage from shared memory, then
+//     arrives on `empty[slot]` so the producer can refill it.
+// Forward kernels only stream: each consumer warp stores the partial of every
+// (row, block) piece it saw with a plain store, at a slot fixed by (block
+// index within the row, warp), so the result does not depend on which CTA
+// took which block. A small finalize kernel, chained with programmatic
+// dependent launch (PDL), merges the partials once the streaming grid is done.
+// Dynamic blocks keep every SM busy to the end: equal bytes do not take equal
+// time on a loaded memory system. Every wait is bounded (kWaitLimitNs).
+#pragma once
+
+#include "bulk_copy.cuh"
+#include "specdec_common.cuh"
+
+namespace specdec {
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Global block queue: `ctr` hands out block indices; each CTA's producer stops
+// after its first index >= nblocks and then retires; the last CTA to retire
+// resets both words, leaving the counters zeroed for the next launch.
+struct BlockQueue {
+  unsigned* ctr;
+  unsigned* retired;
+  unsigned nblocks;
+  int dynamic;  // 0: block = blockIdx.x + k * gridDim.x (static interleave)
+
+  __device__ __forceinline__ unsigned first() const { return dynamic ? atomicAdd(ctr, 1u) : blockIdx.x; }
+  __device__ __forceinline__ unsigned next(unsigned cur) const {
+    return dynamic ? atomicAdd(ctr, 1u) : cur + gridDim.x;
+  }
+  __device__ __forceinline__ void retire() const {
+    if (!dynamic) return;
+    __threadfence();
+    if (atomicAdd(retired, 1u) + 1 == gridDim.x) {
+      *ctr = 0u;
+      *retired = 0u;
+    }
+  }
+};
+
+// Number of blocks of length BL that overlap row r (= slots of its partials).
+__device__ __forceinline__ int blocks_in_row(int64_t r, int64_t V, int64_t BL) {
+  return (int)(((r + 1) * V - 1) / BL - (r * V) / BL + 1);
+}
+
+// Programmatic dependent launch: a CTA that is done signals that the
+// dependent (finalize) grid may start launching; the dependent waits for the
+// whole primary grid to complete and flush before reading its results.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Row-liveness bitmask in shared memory (bit r = row r is read at all).
+struct RowBits {
+  const unsigned* words;
+  bool valid;  // false: too many rows for the table, treat every row as live
+  __device__ __forceinline__ bool live(int64_t r) const {
+    return !valid || ((words[r >> 5] >> (r & 31)) & 1u);
+  }
+};
+
+constexpr int kMaxRowWords = 1024;  // liveness bitmask capacity: 32768 rows
+
+// Builds the liveness bitmask (all threads of the CTA, before the role split).
+template <class LiveFn>
+__device__ __forceinline__ RowBits build_row_bits(unsigned* words, int64_t R, int nwarps, LiveFn live) {
+  RowBits rb;
+  rb.words = words;
+  rb.valid = R <= (int64_t)kMaxRowWords * 32;
+  if (rb.valid) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int64_t wd = warp; wd * 32 < R; wd += nwarps) {
+      const int64_t r = wd * 32 + lane;
+      const unsigned bits = __ballot_sync(0xffffffffu, r < R && live(r));
+      if (lane == 0) words[wd] = bits;
+    }
+  }
+  return rb;
+}
+
+// Producer loop, lane 0 of the producer warp. NIN input streams share the
+// flattened index space (ring k holds stream k's stages at ring + k*S*SE).
+// A stage whose rows are all dead is posted without a copy. Returns false on
+// a wait timeout.
+template <int NIN, int S, int SE, int BS>
+__device__ bool ring_produce(const float* const* src, int64_t E, int64_t V, const RowBits& rb,
+                             const BlockQueue& q, float* ring, uint64_t* full, uint64_t* empty,
+                             int64_t* sf0, int64_t* srow) {
+  constexpr int64_t BL = (int64_t)BS * SE;
+  unsigned b = q.first();
+  unsigned nb = b < q.nblocks ? q.next(b) : q.nblocks;
+  int64_t blk_end = 0, r_issue = 0;
+  int k = 0;
+  if (b < q.nblocks) {
+    blk_end = min((int64_t)(b + 1) * BL, E);
+    r_issue = ((int64_t)b * BL) / V;
+  }
+  bool ok = true;
+  for (int64_t it = 0;; ++it) {
+    const int slot = (int)(it % S);
+    if (!mbar_wait(empty + slot, (uint32_t)(((it / S) & 1) ^ 1))) {
+      ok = false;
+      break;
+    }
+    if (b >= q.nblocks) {
+      sf0[slot] = -1;
+      mbar_arrive(full + slot);
+      break;
+    }
+    const int64_t f0 = (int64_t)b * BL + (int64_t)k * SE;
+    const int64_t f1 = min(f0 + SE, blk_end);
+    sf0[slot] = f0;
+    while ((r_issue + 1) * V <= f0) ++r_issue;
+    srow[slot] = r_issue;
+    bool live = !rb.valid;
+    for (int64_t r = r_issue; !live && r * V < f1; ++r) live = rb.live(r);
+    const uint32_t vbytes = (uint32_t)(((f1 - f0) * 4) & ~int64_t(15));
+    if (live && vbytes) {
+      mbar_arrive_expect_tx(full + slot, vbytes * NIN);
+#pragma unroll
+      for (int i = 0; i < NIN; ++i)
+        bulk_g2s(ring + (size_t)i * S * SE + (size_t)slot * SE, src[i] + f0, vbytes, full + slot);
+    } else {
+      mbar_arrive(full + slot);
+    }
+    if (f1 == blk_end) {
+      b = nb;
+      k = 0;
+      if (b < q.nblocks) {
+        nb = q.next(b);
+        blk_end = min((int64_t)(b + 1) * BL, E);
+        r_issue = ((int64_t)b * BL) / V;
+      }
+    } else {
+      ++k;
+    }
+  }
+  q.retire();
+  return ok;
+}
+
+// After a timeout a consumer waits (bounded) for the next S stages so that no
+// copy into this CTA's shared memory is left in flight when it exits.
+template <int S>
+__device__ __forceinline__ void ring_drain(uint64_t* full, int64_t it) {
+  for (int64_t j = it; j < it + S; ++j) mbar_wait(full + (j % S), (uint32_t)((j / S) & 1));
+}
+
+// Shared-memory layout of a ring: NIN streams x S stages x SE floats, then the
+// stage barriers, the posted stage starts and the liveness bitmask.
+template <int NIN, int S, int SE>
+struct RingSmem {
+  float ring[NIN * S * SE];
+  uint64_t full[S], empty[S];
+  int64_t sf0[S];   // flattened start of the stage (-1: end of work)
+  int64_t srow[S];  // row containing the stage's first element
+  unsigned bits[kMaxRowWords];
+};
+
+template <int NIN, int S, int SE>
+__device__ __forceinline__ void ring_init(RingSmem<NIN, S, SE>& sm, int consumers) {
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(sm.full + i, 1);
+      mbar_init(sm.empty + i, consumers);
+    }
+    fence_mbar_init();
+  }
+}
+
+// Accumulates smem elements [a, b) of a stage into the lane's (m, s).
+__device__ __forceinline__ void warp_lse_smem(const float* sb, int a, int b, float& m, float& s) {
+  const int lane = threadIdx.x & 31;
+  const int a4 = (a + 3) & ~3, b4 = b & ~3;
+  if (a4 >= b4) {
+    for (int k = a + lane; k < b; k += 32) lse_push(m, s, sb[k]);
+    return;
+  }
+  if (lane < a4 - a) lse_push(m, s, sb[a + lane]);
+  if (lane < b - b4) lse_push(m, s, sb[b4 + lane]);
+  const float4* q = reinterpret_cast<const float4*>(sb);
+  int k = (a4 >> 2) + lane;
+  const int kend = b4 >> 2;
+  for (; k + 96 < kend; k += 128) {
+    const float4 v0 = q[k], v1 = q[k + 32], v2 = q[k + 64], v3 = q[k + 96];
+    const float cm = fmaxf(fmaxf(max4(v0), max4(v1)), fmaxf(max4(v2), max4(v3)));
+    if (cm > m) {
+      s *= exp_shift(m, cm);
+      m = cm;
+    }
+    s += ((exp_shift(v0.x, m) + exp_shift(v0.y, m)) + (exp_shift(v0.z, m) + exp_shift(v0.w, m))) +
+         ((exp_shift(v1.x, m) + exp_shift(v1.y, m)) + (exp_shift(v1.z, m) + exp_shift(v1.w, m))) +
+         ((exp_shift(v2.x, m) + exp_shift(v2.y, m)) + (exp_shift(v2.z, m) + exp_shift(v2.w, m))) +
+         ((exp_shift(v3.x, m) + exp_shift(v3.y, m)) + (exp_shift(v3.z, m) + exp_shift(v3.w, m)));
+  }
+  for (; k < kend; k += 32) {
+    const float4 v = q[k];
+    const float cm = max4(v);
+    if (cm > m) {
+      s *= exp_shift(m, cm);
+      m = cm;
+    }
+    s += (exp_shift(v.x, m) + exp_shift(v.y, m)) + (exp_shift(v.z, m) + exp_shift(v.w, m));
+  }
+}
+
+// Accumulates a full sub-range of KSUB floats (KSUB / 128 float4 per lane):
+// all loads first, one max, one rescale, then the exponentials.
+template <int KSUB>
+__device__ __forceinline__ void warp_lse_full(const float* sb, float& m, float& s) {
+  constexpr int U = KSUB / 128;
+  static_assert(KSUB % 128 == 0, "sub-range must be a multiple of 128 floats");
+  const int lane = threadIdx.x & 31;
+  const float4* q = reinterpret_cast<const float4*>(sb) + lane;
+  float4 v[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) v[u] = q[32 * u];
+  float cm = max4(v[0]);
+#pragma unroll
+  for (int u = 1; u < U; ++u) cm = fmaxf(cm, max4(v[u]));
+  if (cm > m) {
+    s *= exp_shift(m, cm);
+    m = cm;
+  }
+  float acc[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u)
+    acc[u] = (exp_shift(v[u].x, m) + exp_shift(v[u].y, m)) + (exp_shift(v[u].z, m) + exp_shift(v[u].w, m));
+#pragma unroll
+  for (int w = 1; w < U; w <<= 1)
+#pragma unroll
+    for (int u = 0; u + w < U; u += 2 * w) acc[u] += acc[u + w];
+  s += acc[0];
+}
+
+// Launches a finalize kernel chained to the previous kernel on the stream with
+// programmatic dependent launch (it starts launching while the streaming grid
+// drains and waits for it inside, with griddepcontrol.wait).
+template <class Kernel, class Args>
+inline cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, cudaStream_t st, const Args& args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args);
+}
+
+template <class K>
+inline int ring_occupancy_ctas(K kernel, int threads, size_t smem, int device, int cap) {
+  int sms = 0, per_sm = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess) return 0;
+  if (cap > 0 && per_sm > cap) per_sm = cap;
+  if (per_sm < 1) return 0;
+  return sms * per_sm;
+}
+
+}  // namespace specdec

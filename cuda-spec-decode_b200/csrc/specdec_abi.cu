@@ -3,6 +3,7 @@
 // Nothing here allocates device memory or synchronises the stream.
 #include "specdec.h"
 #include "specdec_internal.h"
+#include "bulk_copy.cuh"
 
 #include <atomic>
 #include <cmath>
@@ -42,6 +43,7 @@ constexpr int64_t kMinChunk = 1024;
 
 std::atomic<int> g_shape[4] = {0, 0, 0, 0};
 std::atomic<int> g_cap[4] = {0, 0, 0, 0};
+std::atomic<int> g_static_queue{0};  // 1: ring kernels use a static block interleave
 
 int current_device() {
   int d = 0;
@@ -49,12 +51,37 @@ int current_device() {
   return d;
 }
 
-// Occupancy-derived CTA counts, cached per (kernel, kind, shape, cap, device).
-int kernel_ctas(int kernel, int kind, int device) {
+// Launch shapes 0..9 select a per-warp bulk-copy ring variant (used when the
+// pointers are 16-byte aligned, else the 128-bit-load kernels run with their
+// default shape); shapes 10..14 force the 128-bit-load kernels, variant
+// shape - 10.
+constexpr int kLdgShapeBase = 10;
+
+bool has_ring_path(int kernel) {
+  return kernel == SPECDEC_KERNEL_DPACE_FWD || kernel == SPECDEC_KERNEL_DPACE_BWD;
+}
+
+// Variant id inside the chosen kernel family.
+int kernel_shape(int kernel, bool tma) {
+  const int raw = g_shape[kernel].load();
+  if (tma) return raw;
+  if (!has_ring_path(kernel)) return raw % kLdgShapeBase;
+  return raw >= kLdgShapeBase ? raw - kLdgShapeBase : 0;
+}
+
+bool use_tma(int kernel, bool ptrs_aligned) {
+  return g_shape[kernel].load() < kLdgShapeBase && ptrs_aligned &&
+         (kernel == SPECDEC_KERNEL_DPACE_FWD || kernel == SPECDEC_KERNEL_DPACE_BWD);
+}
+
+// Occupancy-derived work units (CTAs for the 128-bit-load kernels, warps for
+// the ring kernels), cached per (kernel, kind, path, shape, cap, device).
+int kernel_units(int kernel, int kind, bool tma, int device) {
   static std::mutex mu;
   static std::map<uint64_t, int> cache;
-  const int shape = g_shape[kernel].load(), cap = g_cap[kernel].load();
-  const uint64_t key = (uint64_t(kernel) << 56) | (uint64_t(kind & 0xff) << 48) |
+  const int cap = g_cap[kernel].load();
+  const int shape = kernel_shape(kernel, tma);
+  const uint64_t key = (uint64_t(kernel) << 56) | (uint64_t(kind & 0x7f) << 49) | (uint64_t(tma) << 48) |
                        (uint64_t(shape & 0xff) << 40) | (uint64_t(cap & 0xffff) << 24) |
                        uint64_t(device & 0xffffff);
   {
@@ -64,8 +91,12 @@ int kernel_ctas(int kernel, int kind, int device) {
   }
   int ctas = 0;
   switch (kernel) {
-    case SPECDEC_KERNEL_DPACE_FWD: ctas = dpace_fwd_ctas(shape, device, cap); break;
-    case SPECDEC_KERNEL_DPACE_BWD: ctas = dpace_bwd_ctas(shape, device, cap); break;
+    case SPECDEC_KERNEL_DPACE_FWD:
+      ctas = tma ? dpace_fwd_ring_ctas(shape, device, cap) : dpace_fwd_ctas(shape, device, cap);
+      break;
+    case SPECDEC_KERNEL_DPACE_BWD:
+      ctas = tma ? dpace_bwd_ring_ctas(shape, device, cap) : dpace_bwd_ctas(shape, device, cap);
+      break;
     case SPECDEC_KERNEL_DFLASH_FWD: ctas = dflash_fwd_ctas(kind, shape, device, cap); break;
     case SPECDEC_KERNEL_DFLASH_BWD: ctas = dflash_bwd_ctas(kind, shape, device, cap); break;
     default: ctas = 0;
@@ -80,21 +111,37 @@ int kernel_ctas(int kernel, int kind, int device) {
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // ---- D-PACE workspace layout ----------------------------------------------
-// counters: [done u32][flag i32][pad to 16 B][seq_cnt u32 x N]
-// scratch:  [part float2 x R*pmax][xtgt f32 x R][seq_loss f32 x N]
+// counters: [done][flag][queue ctr][queue retired] [seq_cnt u32 x N]
+// scratch:  [part float2 x R*pmax*nc][xtgt f32 x R][seq_loss f32 x N]
 struct DpaceLayout {
   size_t part = 0, xtgt = 0, seq_loss = 0, scratch = 0, counters = 0;
 };
 
-DpaceLayout dpace_layout(int64_t N, int64_t B, const Partition& pt) {
+size_t dpace_counter_bytes(int64_t N, int64_t B) {
+  (void)B;
+  return align256(16 + size_t(N) * sizeof(unsigned));
+}
+
+DpaceLayout dpace_layout(int64_t N, int64_t B, const Partition& pt, int nc) {
   DpaceLayout L;
   const size_t R = size_t(N) * size_t(B);
   L.part = 0;
-  L.xtgt = align256(L.part + R * size_t(pt.pmax) * sizeof(float2));
+  L.xtgt = align256(L.part + R * size_t(pt.pmax) * size_t(nc) * sizeof(float2));
   L.seq_loss = align256(L.xtgt + R * sizeof(float));
   L.scratch = align256(L.seq_loss + size_t(N) * sizeof(float));
-  L.counters = align256(16 + size_t(N) * sizeof(unsigned));
+  L.counters = dpace_counter_bytes(N, B);
   return L;
+}
+
+// Ring kernels: the unit of the partial table is a block of BL elements.
+Partition ring_partition(int64_t rows, int64_t V, int64_t block_elems, int ctas) {
+  Partition p;
+  p.V = V;
+  p.E = rows * V;
+  p.chunk = block_elems;
+  p.grid = ctas;
+  p.pmax = int((V - 1) / block_elems + 2);
+  return p;
 }
 
 // ---- DFlash workspace layout -----------------------------------------------
@@ -114,13 +161,15 @@ DflashLayout dflash_layout(int64_t N, int64_t B, const Partition& pt) {
   return L;
 }
 
-Partition dpace_fwd_partition(int64_t N, int32_t B, int64_t V, int device) {
-  const int ctas = kernel_ctas(SPECDEC_KERNEL_DPACE_FWD, 0, device);
-  return make_partition(N * B, V, ctas, kMinChunk);
+Partition dpace_fwd_partition(int64_t N, int32_t B, int64_t V, bool tma, int device) {
+  const int units = kernel_units(SPECDEC_KERNEL_DPACE_FWD, 0, tma, device);
+  if (tma)
+    return ring_partition(N * B, V, dpace_ring_block_elems(kernel_shape(SPECDEC_KERNEL_DPACE_FWD, true)), units);
+  return make_partition(N * B, V, units, kMinChunk);
 }
 
 Partition dflash_fwd_partition(int64_t N, int32_t B, int64_t V, int kind, int device) {
-  const int ctas = kernel_ctas(SPECDEC_KERNEL_DFLASH_FWD, kind, device);
+  const int ctas = kernel_units(SPECDEC_KERNEL_DFLASH_FWD, kind, false, device);
   return make_partition(N * B, V, ctas, kMinChunk);
 }
 
@@ -148,7 +197,8 @@ const char* specdec_status_string(int code) {
 
 int specdec_set_launch_shape(int32_t kernel, int32_t shape, int32_t ctas_per_sm) {
   if (kernel < 0 || kernel > 3) return fail(SPECDEC_ERR_ARGUMENT, "unknown kernel id %d", kernel);
-  if (shape < 0 || shape > 4) return fail(SPECDEC_ERR_ARGUMENT, "unknown launch shape %d", shape);
+  if (shape < 0 || (shape > 4 && shape < kLdgShapeBase) || shape > kLdgShapeBase + 4)
+    return fail(SPECDEC_ERR_ARGUMENT, "unknown launch shape %d", shape);
   if (ctas_per_sm < 0 || ctas_per_sm > 32)
     return fail(SPECDEC_ERR_ARGUMENT, "ctas_per_sm must be in [0, 32], got %d", ctas_per_sm);
   g_shape[kernel].store(shape);
@@ -156,10 +206,17 @@ int specdec_set_launch_shape(int32_t kernel, int32_t shape, int32_t ctas_per_sm)
   return ok();
 }
 
+int specdec_set_block_queue(int32_t dynamic) {
+  g_static_queue.store(dynamic ? 0 : 1);
+  return ok();
+}
+
 int64_t specdec_launch_ctas(int32_t kernel, int64_t rows, int64_t V, int device) {
   if (kernel < 0 || kernel > 3 || rows <= 0 || V <= 0) return 0;
-  const int ctas = kernel_ctas(kernel, 0, device);
-  return make_partition(rows, V, ctas, kMinChunk).grid;
+  const bool tma = use_tma(kernel, true);
+  const int units = kernel_units(kernel, 0, tma, device);
+  if (tma) return units;  // persistent ring CTAs
+  return make_partition(rows, V, units, kMinChunk).grid;
 }
 
 // ---------------------------------------------------------------------------
@@ -168,13 +225,19 @@ int64_t specdec_launch_ctas(int32_t kernel, int64_t rows, int64_t V, int device)
 
 size_t specdec_dpace_scratch_bytes(int64_t N, int32_t B, int64_t V, int device) {
   if (N <= 0 || B <= 0 || V <= 0) return 256;
-  return dpace_layout(N, B, dpace_fwd_partition(N, B, V, device)).scratch;
+  // large enough for either kernel family (the call picks by pointer alignment)
+  const size_t a = dpace_layout(N, B, dpace_fwd_partition(N, B, V, false, device), 1).scratch;
+  if (!use_tma(SPECDEC_KERNEL_DPACE_FWD, true)) return a;
+  const int nc = dpace_ring_consumers(kernel_shape(SPECDEC_KERNEL_DPACE_FWD, true));
+  const size_t b = dpace_layout(N, B, dpace_fwd_partition(N, B, V, true, device), nc).scratch;
+  return a > b ? a : b;
 }
 
 size_t specdec_dpace_counter_bytes(int64_t N, int32_t B) {
-  (void)B;
-  return align256(16 + size_t(N > 0 ? N : 0) * sizeof(unsigned));
+  return dpace_counter_bytes(N > 0 ? N : 0, B > 0 ? B : 0);
 }
+
+size_t specdec_dpace_backward_counter_bytes(void) { return 256; }
 
 int specdec_dpace_forward(const float* logits, const int64_t* targets, const float* mask,
                           int64_t N, int32_t B, int64_t V, float alpha, int32_t loss_type,
@@ -206,9 +269,11 @@ int specdec_dpace_forward(const float* logits, const int64_t* targets, const flo
     return fail(SPECDEC_ERR_ARGUMENT, "misaligned pointer (scratch needs 256 B, counters 16 B)");
   const int dev = current_device();
   if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
-  const Partition pt = dpace_fwd_partition(N, B, V, dev);
+  const bool tma = use_tma(SPECDEC_KERNEL_DPACE_FWD, aligned(logits, 16));
+  const Partition pt = dpace_fwd_partition(N, B, V, tma, dev);
   if (pt.grid <= 0) return fail(SPECDEC_ERR_CUDA, "occupancy query failed");
-  const DpaceLayout L = dpace_layout(N, B, pt);
+  const int nc = tma ? dpace_ring_consumers(kernel_shape(SPECDEC_KERNEL_DPACE_FWD, true)) : 1;
+  const DpaceLayout L = dpace_layout(N, B, pt, nc);
   if (scratch_bytes < L.scratch)
     return fail(SPECDEC_ERR_WORKSPACE, "scratch needs %zu bytes, got %zu", L.scratch, scratch_bytes);
   if (counter_bytes < L.counters)
@@ -236,17 +301,24 @@ int specdec_dpace_forward(const float* logits, const int64_t* targets, const flo
   a.part = reinterpret_cast<float2*>(ws + L.part);
   a.xtgt = reinterpret_cast<float*>(ws + L.xtgt);
   a.seq_loss = reinterpret_cast<float*>(ws + L.seq_loss);
+  a.nc = nc;
   a.done_cnt = cnt;
   a.flag = reinterpret_cast<int*>(cnt + 1);
+  a.q_ctr = cnt + 2;
+  a.q_retired = cnt + 3;
+  a.q_dynamic = g_static_queue.load() ? 0 : 1;
   a.seq_cnt = cnt + 4;
   a.pt = pt;
-  const cudaError_t e = dpace_fwd_launch(g_shape[SPECDEC_KERNEL_DPACE_FWD].load(), a, st);
+  const int shape = kernel_shape(SPECDEC_KERNEL_DPACE_FWD, tma);
+  const cudaError_t e =
+      tma ? dpace_fwd_ring_launch(shape, a, (int)pt.grid, st) : dpace_fwd_launch(shape, a, st);
   return e == cudaSuccess ? ok() : cuda_fail(e, "dpace forward launch");
 }
 
 int specdec_dpace_backward(const float* logits, const int64_t* targets, const float* lse,
                            const float* scale, const float* dloss, float* dlogits, int64_t N,
-                           int32_t B, int64_t V, void* stream) {
+                           int32_t B, int64_t V, void* counters, size_t counter_bytes,
+                           void* stream) {
   if (B < 1 || B > 32) return fail(SPECDEC_ERR_ARGUMENT, "kernel configured for block_size <= 32 (B=%d)", B);
   if (N < 0 || V < 0) return fail(SPECDEC_ERR_ARGUMENT, "negative shape");
   if (N == 0 || V == 0) return ok();
@@ -255,8 +327,9 @@ int specdec_dpace_backward(const float* logits, const int64_t* targets, const fl
   if (logits == dlogits) return fail(SPECDEC_ERR_ARGUMENT, "dlogits must not alias logits");
   const int dev = current_device();
   if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
-  const int ctas = kernel_ctas(SPECDEC_KERNEL_DPACE_BWD, 0, dev);
-  if (ctas <= 0) return fail(SPECDEC_ERR_CUDA, "occupancy query failed");
+  const bool tma = use_tma(SPECDEC_KERNEL_DPACE_BWD, aligned(logits, 16) && aligned(dlogits, 16));
+  const int units = kernel_units(SPECDEC_KERNEL_DPACE_BWD, 0, tma, dev);
+  if (units <= 0) return fail(SPECDEC_ERR_CUDA, "occupancy query failed");
   DpaceBwdArgs a;
   a.logits = logits;
   a.targets = targets;
@@ -264,9 +337,18 @@ int specdec_dpace_backward(const float* logits, const int64_t* targets, const fl
   a.scale = scale;
   a.dloss = dloss;
   a.dlogits = dlogits;
-  a.pt = make_partition(N * B, V, ctas, kMinChunk);
-  const cudaError_t e =
-      dpace_bwd_launch(g_shape[SPECDEC_KERNEL_DPACE_BWD].load(), a, static_cast<cudaStream_t>(stream));
+  a.flag = nullptr;
+  const bool queue = counters != nullptr && counter_bytes >= 16 && aligned(counters, 16) &&
+                     !g_static_queue.load();
+  unsigned* cnt = static_cast<unsigned*>(counters);
+  a.q_ctr = queue ? cnt : nullptr;
+  a.q_retired = queue ? cnt + 1 : nullptr;
+  a.q_dynamic = queue ? 1 : 0;
+  const int shape = kernel_shape(SPECDEC_KERNEL_DPACE_BWD, tma);
+  a.pt = tma ? ring_partition(N * B, V, dpace_ring_block_elems(shape), units)
+             : make_partition(N * B, V, units, kMinChunk);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const cudaError_t e = tma ? dpace_bwd_ring_launch(shape, a, units, st) : dpace_bwd_launch(shape, a, st);
   return e == cudaSuccess ? ok() : cuda_fail(e, "dpace backward launch");
 }
 
@@ -348,7 +430,7 @@ int specdec_dflash_forward(const float* logits, const float* target_logits, cons
   a.done_cnt = cnt;
   a.row_cnt = cnt + 4;
   a.pt = pt;
-  const cudaError_t e = dflash_fwd_launch(g_shape[SPECDEC_KERNEL_DFLASH_FWD].load(), a, st);
+  const cudaError_t e = dflash_fwd_launch(kernel_shape(SPECDEC_KERNEL_DFLASH_FWD, false), a, st);
   return e == cudaSuccess ? ok() : cuda_fail(e, "dflash forward launch");
 }
 
@@ -368,7 +450,7 @@ int specdec_dflash_backward(const float* logits, const float* target_logits, con
     return fail(SPECDEC_ERR_ARGUMENT, "dlogits must not alias an input");
   const int dev = current_device();
   if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
-  const int ctas = kernel_ctas(SPECDEC_KERNEL_DFLASH_BWD, kind, dev);
+  const int ctas = kernel_units(SPECDEC_KERNEL_DFLASH_BWD, kind, false, dev);
   if (ctas <= 0) return fail(SPECDEC_ERR_CUDA, "occupancy query failed");
   DflashBwdArgs a;
   a.logits = logits;
@@ -382,7 +464,7 @@ int specdec_dflash_backward(const float* logits, const float* target_logits, con
   a.kind = kind;
   a.pt = make_partition(N * B, V, ctas, kMinChunk);
   const cudaError_t e =
-      dflash_bwd_launch(g_shape[SPECDEC_KERNEL_DFLASH_BWD].load(), a, static_cast<cudaStream_t>(stream));
+      dflash_bwd_launch(kernel_shape(SPECDEC_KERNEL_DFLASH_BWD, false), a, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? ok() : cuda_fail(e, "dflash backward launch");
 }
 

@@ -11,6 +11,7 @@ namespace specdec {
 
 constexpr int kStatusOk = 0;
 constexpr int kStatusTargetRange = 3;  // equals SPECDEC_ERR_TARGET_RANGE in include/specdec.h
+// kStatusTimeout (= SPECDEC_ERR_CUDA) is defined in bulk_copy.cuh
 
 constexpr int kKindKL = 0;
 constexpr int kKindCE = 1;
@@ -38,13 +39,17 @@ struct DpaceFwdArgs {
   float* scale;            // [N, B]  w_j / n_global
   int* status;             // [1]  device status word, or null
   // workspace
-  float2* part;            // [N*B, pt.pmax] (m2, s) per row piece
+  float2* part;            // [N*B, pt.pmax, nc] (max, sum) per row piece (and consumer warp)
   float* xtgt;             // [N*B] logit at the target id
   float* seq_loss;         // [N]
-  unsigned* seq_cnt;       // [N]  zero on entry, zero on exit
+  unsigned* seq_cnt;       // [N]  128-bit-load kernel: CTA pieces per sequence; zero on entry/exit
   unsigned* done_cnt;      // [1]  zero on entry, zero on exit
   int* flag;               // [1]  zero on entry, zero on exit
-  Partition pt;
+  unsigned* q_ctr;         // [1]  ring kernel block queue; zero on entry/exit
+  unsigned* q_retired;     // [1]
+  int q_dynamic;           // 1: atomic block queue, 0: static interleave
+  int nc;                  // partials per (row, slot): consumer warps (ring) or 1
+  Partition pt;            // ring kernel: chunk = block length, pmax from it
 };
 
 struct DpaceBwdArgs {
@@ -54,6 +59,10 @@ struct DpaceBwdArgs {
   const float* scale;
   const float* dloss;      // [1] upstream gradient, or null for 1
   float* dlogits;
+  int* flag;               // [1] or null: bit 2 set if a copy wait timed out
+  unsigned* q_ctr;         // ring kernel block queue (null: static interleave)
+  unsigned* q_retired;
+  int q_dynamic;
   Partition pt;
 };
 
@@ -102,6 +111,14 @@ int dpace_fwd_ctas(int shape, int device, int cap_per_sm);
 int dpace_bwd_ctas(int shape, int device, int cap_per_sm);
 cudaError_t dpace_fwd_launch(int shape, const DpaceFwdArgs& a, cudaStream_t st);
 cudaError_t dpace_bwd_launch(int shape, const DpaceBwdArgs& a, cudaStream_t st);
+
+// Warp-specialized ring kernels (dpace_ring.cu); sizes in CTAs.
+int dpace_ring_block_elems(int shape);
+int dpace_ring_consumers(int shape);
+int dpace_fwd_ring_ctas(int shape, int device, int cap_per_sm);
+int dpace_bwd_ring_ctas(int shape, int device, int cap_per_sm);
+cudaError_t dpace_fwd_ring_launch(int shape, const DpaceFwdArgs& a, int ctas, cudaStream_t st);
+cudaError_t dpace_bwd_ring_launch(int shape, const DpaceBwdArgs& a, int ctas, cudaStream_t st);
 
 int dflash_fwd_ctas(int kind, int shape, int device, int cap_per_sm);
 int dflash_bwd_ctas(int kind, int shape, int device, int cap_per_sm);

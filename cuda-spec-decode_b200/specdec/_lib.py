@@ -46,8 +46,9 @@ _SIGNATURES = {
     "specdec_dpace_forward": (ctypes.c_int, [
         _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_f32, _c_i32, _c_i64,
         _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_sz, _c_p, _c_sz, _c_p]),
+    "specdec_dpace_backward_counter_bytes": (_c_sz, []),
     "specdec_dpace_backward": (ctypes.c_int, [
-        _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_p]),
+        _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_p, _c_sz, _c_p]),
     "specdec_dflash_scratch_bytes": (_c_sz, [_c_i64, _c_i32, _c_i64, ctypes.c_int]),
     "specdec_dflash_counter_bytes": (_c_sz, [_c_i64, _c_i32]),
     "specdec_dflash_forward": (ctypes.c_int, [
@@ -57,6 +58,7 @@ _SIGNATURES = {
         _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_i32, _c_p]),
     "specdec_set_launch_shape": (ctypes.c_int, [_c_i32, _c_i32, _c_i32]),
     "specdec_launch_ctas": (_c_i64, [_c_i32, _c_i64, _c_i64, ctypes.c_int]),
+    "specdec_set_block_queue": (ctypes.c_int, [_c_i32]),
 }
 
 _lib = None
@@ -114,6 +116,11 @@ def stream_handle(device: torch.device) -> int:
 def set_launch_shape(kernel: int, shape: int, ctas_per_sm: int = 0) -> None:
     check(load().specdec_set_launch_shape(kernel, shape, ctas_per_sm), "set_launch_shape")
     _workspaces.clear()
+
+
+def set_block_queue(dynamic: bool) -> None:
+    """Ring kernels: atomic block queue (True, default) or static interleave."""
+    check(load().specdec_set_block_queue(1 if dynamic else 0), "set_block_queue")
 
 
 class Workspace:

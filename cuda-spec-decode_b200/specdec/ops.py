@@ -54,8 +54,12 @@ def _dpace_forward(logits: torch.Tensor, targets: torch.Tensor, mask: torch.Tens
         counters.data_ptr(), counters.numel(), _lib.stream_handle(dev))
     _lib.check(code, "specdec_dpace_forward")
     if (VALIDATE_TARGETS if validate is None else validate) and N * B > 0:
-        if int(status.item()) == _lib.ERR_TARGET_RANGE:
+        st = int(status.item())
+        if st == _lib.ERR_TARGET_RANGE:
             raise ValueError(f"targets out of range [0, {V})")
+        if st == _lib.ERR_CUDA:  # a bounded copy wait expired: counters are in an unknown state
+            ws.reset_counters()
+            raise RuntimeError("specdec_dpace_forward: a bulk-copy wait timed out")
     return loss, lse, scale, loss_n
 
 
@@ -64,12 +68,16 @@ def _dpace_backward(logits: torch.Tensor, targets: torch.Tensor, lse: torch.Tens
                    out: torch.Tensor | None = None) -> torch.Tensor:
     lib = _lib.load()
     N, B, V = logits.shape
+    dev = logits.device
     dlogits = torch.empty_like(logits) if out is None else out
     if dloss is not None:
-        dloss = dloss.detach().to(device=logits.device, dtype=torch.float32).contiguous()
+        dloss = dloss.detach().to(device=dev, dtype=torch.float32).contiguous()
+    cb = lib.specdec_dpace_backward_counter_bytes()
+    _, counters = _lib.workspace("dpace_bwd", dev).ensure(dev, 256, cb)
     code = lib.specdec_dpace_backward(
         logits.data_ptr(), targets.data_ptr(), lse.data_ptr(), scale.data_ptr(),
-        _lib.ptr(dloss), dlogits.data_ptr(), N, B, V, _lib.stream_handle(logits.device))
+        _lib.ptr(dloss), dlogits.data_ptr(), N, B, V, counters.data_ptr(), counters.numel(),
+        _lib.stream_handle(dev))
     _lib.check(code, "specdec_dpace_backward")
     return dlogits
 

@@ -98,15 +98,21 @@ int specdec_dpace_forward(const float* logits, const int64_t* targets, const flo
                           int32_t* status, void* scratch, size_t scratch_bytes, void* counters,
                           size_t counter_bytes, void* stream);
 
+/* Counter bytes for specdec_dpace_backward's optional block queue. */
+size_t specdec_dpace_backward_counter_bytes(void);
+
 /*
  * D-PACE backward. Replaces the launch of dpace_backward in
  * losses/dpace.py:217-226 (DPACELoss.backward):
  *   dlogits = scale[n, j] * dloss[0] * (softmax(logits[n, j]) - onehot(targets[n, j]))
  * dloss may be NULL (treated as 1). dlogits must not alias logits.
+ * counters (zeroed once, left zeroed; specdec_dpace_backward_counter_bytes())
+ * enable the dynamic block queue; NULL selects a static block interleave.
  */
 int specdec_dpace_backward(const float* logits, const int64_t* targets, const float* lse,
                            const float* scale, const float* dloss, float* dlogits, int64_t N,
-                           int32_t B, int64_t V, void* stream);
+                           int32_t B, int64_t V, void* counters, size_t counter_bytes,
+                           void* stream);
 
 /* ------------------------------------------------------------------------- */
 /* DFlash objective                                                           */
@@ -161,14 +167,23 @@ int specdec_dflash_backward(const float* logits, const float* target_logits, con
 #define SPECDEC_KERNEL_DFLASH_BWD 3
 
 /*
- * Selects the (threads, unroll) instantiation `shape` (0 = default) and caps
- * resident CTAs per SM (0 = occupancy limit) for one kernel, process-wide.
- * Workspace sizes depend on it: query sizes after changing it.
+ * Selects a kernel variant and caps resident CTAs per SM (0 = occupancy
+ * limit) for one kernel, process-wide. For the D-PACE kernels shapes 0..4 are
+ * warp-specialized bulk-copy ring variants (used when logits and dlogits are
+ * 16-byte aligned) and 10..14 force the 128-bit-load kernels; for DFlash,
+ * 0..4 are (threads, unroll) variants. Workspace sizes depend on it: query
+ * sizes after changing it.
  */
 int specdec_set_launch_shape(int32_t kernel, int32_t shape, int32_t ctas_per_sm);
 
 /* Number of CTAs the kernel would launch for a problem of rows x V on device. */
 int64_t specdec_launch_ctas(int32_t kernel, int64_t rows, int64_t V, int device);
+
+/*
+ * Ring kernels hand out blocks through a global atomic queue (dynamic = 1,
+ * default) or a static interleave (dynamic = 0), process-wide.
+ */
+int specdec_set_block_queue(int32_t dynamic);
 
 #ifdef __cplusplus
 }

@@ -275,3 +275,68 @@ def test_large_batch_shard_properties(cuda):
     dead = (m == 0)
     if bool(dead.any()):
         assert float(g[dead].abs().max()) == 0.0
+
+
+SHAPE_CASES = [c for c in cases.DPACE_CASES if c["name"] in (
+    "bern.5_N8_B8_V1024", "B32_N8_V1024", "V7_N6_B8", "V1000_N6_B8", "shift-20_N8_B4_V1024",
+    "type_SP_N4_B8_V1024", "seq0masked_N4_B8_V512", "ws2_N4_B16_V128256_sd2_prefix4")]
+
+
+@pytest.mark.parametrize("shape", [0, 1, 2, 3, 4, 10, 11, 12, 13, 14])
+def test_every_launch_shape_matches_golden(cuda, gd, shape):
+    """Shapes 0-4: per-warp bulk-copy ring variants; 10-14: 128-bit-load kernels."""
+    from specdec import _lib
+
+    try:
+        _lib.set_launch_shape(_lib.KERNEL_DPACE_FWD, shape)
+        _lib.set_launch_shape(_lib.KERNEL_DPACE_BWD, shape)
+        for case in SHAPE_CASES:
+            x, t, m = cases.dpace_inputs(case)
+            key = case["name"]
+            loss, grad = _run(x, t, m, case["alpha"], case["loss_type"])
+            _close_loss(loss, float(gd[f"{key}/loss"]))
+            if f"{key}/grad" in gd.files:
+                np.testing.assert_allclose(grad, gd[f"{key}/grad"], rtol=0, atol=GRAD_ATOL)
+            else:
+                idx = gd[f"{key}/probe_idx"]
+                np.testing.assert_allclose(grad.reshape(-1)[idx], gd[f"{key}/probe_val"], rtol=0,
+                                           atol=GRAD_ATOL)
+    finally:
+        _lib.set_launch_shape(_lib.KERNEL_DPACE_FWD, 0)
+        _lib.set_launch_shape(_lib.KERNEL_DPACE_BWD, 0)
+
+
+def test_static_block_interleave_matches_golden(cuda, gd):
+    """The ring kernels with the atomic block queue off (static interleave)."""
+    from specdec import _lib
+
+    try:
+        _lib.set_block_queue(False)
+        for case in SHAPE_CASES:
+            x, t, m = cases.dpace_inputs(case)
+            loss, grad = _run(x, t, m, case["alpha"], case["loss_type"])
+            _close_loss(loss, float(gd[f"{case['name']}/loss"]))
+            _, g_or = odp.dpace_fwd_bwd_torch(torch.from_numpy(x), torch.from_numpy(t), case["alpha"],
+                                              None if m is None else torch.from_numpy(m),
+                                              case["loss_type"])
+            np.testing.assert_allclose(grad, g_or.numpy(), rtol=0, atol=GRAD_ATOL)
+    finally:
+        _lib.set_block_queue(True)
+
+
+def test_ring_results_are_schedule_independent(cuda):
+    """Partials are slotted by block index, so the dynamic queue's schedule does
+    not change a single bit of the loss or the gradient."""
+    from specdec import _lib, ops
+
+    x, t, m = _workload(16, 16, 128256, 2.0, 4, 3)
+    ref = None
+    for dynamic in (True, False, True):
+        _lib.set_block_queue(dynamic)
+        loss, lse, scale, _ = ops.dpace_forward(x, t, m, 0.5, 0)
+        g = ops.dpace_backward(x, t, lse, scale, None)
+        if ref is None:
+            ref = (loss.clone(), lse.clone(), g.clone())
+        else:
+            assert torch.equal(loss, ref[0]) and torch.equal(lse, ref[1]) and torch.equal(g, ref[2])
+    _lib.set_block_queue(True)
