@@ -177,6 +177,10 @@ bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) %
 
 }  // namespace
 
+namespace specdec {
+void set_last_error(const char* msg) { g_last_error = msg; }
+}  // namespace specdec
+
 extern "C" {
 
 int specdec_version(void) { return 100; }

@@ -120,6 +120,9 @@ int dpace_bwd_ring_ctas(int shape, int device, int cap_per_sm);
 cudaError_t dpace_fwd_ring_launch(int shape, const DpaceFwdArgs& a, int ctas, cudaStream_t st);
 cudaError_t dpace_bwd_ring_launch(int shape, const DpaceBwdArgs& a, int ctas, cudaStream_t st);
 
+// Sets the calling thread's specdec_last_error() text.
+void set_last_error(const char* msg);
+
 int dflash_fwd_ctas(int kind, int shape, int device, int cap_per_sm);
 int dflash_bwd_ctas(int kind, int shape, int device, int cap_per_sm);
 cudaError_t dflash_fwd_launch(int shape, const DflashFwdArgs& a, cudaStream_t st);

@@ -46,6 +46,9 @@ _SIGNATURES = {
     "specdec_dpace_forward": (ctypes.c_int, [
         _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_f32, _c_i32, _c_i64,
         _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_sz, _c_p, _c_sz, _c_p]),
+    "specdec_dpace_forward_noalloc": (ctypes.c_int, [
+        _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_f32, _c_i32, _c_i64,
+        _c_p, _c_p, _c_p, _c_p, _c_p, _c_p]),
     "specdec_dpace_backward_counter_bytes": (_c_sz, []),
     "specdec_dpace_backward": (ctypes.c_int, [
         _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_p, _c_sz, _c_p]),

@@ -114,6 +114,27 @@ int specdec_dpace_backward(const float* logits, const int64_t* targets, const fl
                            int32_t B, int64_t V, void* counters, size_t counter_bytes,
                            void* stream);
 
+/*
+ * D-PACE forward without any caller-provided workspace. No counterpart in the
+ * reference: it serves callers that cannot allocate device memory -- plugin
+ * hosts that pass only input and output buffers, and processes whose device
+ * memory is all reserved by their own pool -- so it calls no cudaMalloc,
+ * cudaFree or other allocating routine. Same arguments, kernels and results
+ * as specdec_dpace_forward minus scratch/counters: its scratch is a 4 MiB
+ * array built into the library (held on every GPU that loads the library
+ * until exit): 64 KiB of counters (N <= 16380) and 4 MiB - 64 KiB of scratch,
+ * about N*B*(32*((V-1)/16384 + 2) + 4) bytes -- e.g. up to ~14000 rows of
+ * N*B at V = 128256. Larger problems return SPECDEC_ERR_WORKSPACE before any
+ * launch. The first call on a device looks up the array's address
+ * with that device current; make it before any stream capture. All calls on a
+ * device share the array: its counters are cleared on `stream` before each
+ * launch, and calls that overlap on the GPU race.
+ */
+int specdec_dpace_forward_noalloc(const float* logits, const int64_t* targets, const float* mask,
+                                  int64_t N, int32_t B, int64_t V, float alpha, int32_t loss_type,
+                                  int64_t n_global, float* loss, float* loss_n, float* lse,
+                                  float* scale, int32_t* status, void* stream);
+
 /* ------------------------------------------------------------------------- */
 /* DFlash objective                                                           */
 /* ------------------------------------------------------------------------- */
