@@ -1,0 +1,165 @@
+// DFlash per-row streaming state and its merges (shared by the ring kernels
+// and the 128-bit-load kernels).
+//
+// For a row pair (xl = draft logits, xt = verifier logits) the state keeps,
+// relative to the running maxima mq (draft) and mp (verifier):
+//   sq = sum e^(xl - mq),  sp = sum e^(xt - mp),  t = sum e^(xt - mp) (xt - xl)
+// (KL), or for CE the first-index argmax of xt (bx, bi) and the draft logit
+// at that index (bl). Merges are exact rescalings, applied in a fixed order.
+#pragma once
+
+#include <climits>
+#include <cstdint>
+
+#include "specdec_common.cuh"
+#include "specdec_internal.h"
+
+namespace specdec {
+
+struct DfState {
+  float mq, sq;      // draft log-sum-exp state (running max, sum of e^(x - max))
+  float mp, sp, t;   // verifier log-sum-exp state and the p-weighted (xt - xl) sum (KL)
+  float bx, bl;       // CE: best verifier logit, draft logit at that index
+  int bi;             // CE: index of the best verifier logit (first occurrence)
+};
+
+__device__ __forceinline__ void df_init(DfState& st) {
+  st.mq = kNegSeed;
+  st.sq = 0.f;
+  st.mp = kNegSeed;
+  st.sp = 0.f;
+  st.t = 0.f;
+  st.bx = -INFINITY;
+  st.bl = 0.f;
+  st.bi = INT_MAX;
+}
+
+template <int KIND>
+__device__ __forceinline__ void df_merge(DfState& x, const DfState& o) {
+  lse_merge(x.mq, x.sq, o.mq, o.sq);
+  if (KIND == kKindKL) {
+    const float M = fmaxf(x.mp, o.mp);
+    const float fa = exp_shift(x.mp, M), fb = exp_shift(o.mp, M);
+    x.sp = x.sp * fa + o.sp * fb;
+    x.t = x.t * fa + o.t * fb;
+    x.mp = M;
+  } else {
+    if (o.bx > x.bx || (o.bx == x.bx && o.bi < x.bi)) {
+      x.bx = o.bx;
+      x.bi = o.bi;
+      x.bl = o.bl;
+    }
+  }
+}
+
+template <int KIND>
+__device__ __forceinline__ DfState df_shfl(const DfState& s, int o) {
+  DfState r;
+  r.mq = __shfl_xor_sync(kFullMask, s.mq, o);
+  r.sq = __shfl_xor_sync(kFullMask, s.sq, o);
+  if (KIND == kKindKL) {
+    r.mp = __shfl_xor_sync(kFullMask, s.mp, o);
+    r.sp = __shfl_xor_sync(kFullMask, s.sp, o);
+    r.t = __shfl_xor_sync(kFullMask, s.t, o);
+  } else {
+    r.bx = __shfl_xor_sync(kFullMask, s.bx, o);
+    r.bl = __shfl_xor_sync(kFullMask, s.bl, o);
+    r.bi = __shfl_xor_sync(kFullMask, s.bi, o);
+  }
+  return r;
+}
+
+template <int KIND>
+__device__ __forceinline__ void df_warp_merge(DfState& s) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const DfState other = df_shfl<KIND>(s, o);
+    df_merge<KIND>(s, other);
+  }
+}
+
+// One element (scalar path); idx is the index within the row.
+template <int KIND>
+__device__ __forceinline__ void df_push(DfState& s, float a, float b, int idx) {
+  lse_push(s.mq, s.sq, a);
+  if (KIND == kKindKL) {
+    if (b > s.mp) {
+      const float f = exp_shift(s.mp, b);
+      s.sp *= f;
+      s.t *= f;
+      s.mp = b;
+    }
+    const float e = exp_shift(b, s.mp);
+    s.sp += e;
+    s.t = fmaf(e, b - a, s.t);
+  } else {
+    if (b > s.bx || (b == s.bx && idx < s.bi)) {
+      s.bx = b;
+      s.bi = idx;
+      s.bl = a;
+    }
+  }
+}
+
+template <int KIND, int U>
+__device__ __forceinline__ void df_group(DfState& s, const float4 (&a)[U], const float4 (&b)[U],
+                                         int base_idx, int stride_idx) {
+  float cma = max4(a[0]);
+#pragma unroll
+  for (int u = 1; u < U; ++u) cma = fmaxf(cma, max4(a[u]));
+  if (cma > s.mq) {
+    s.sq *= exp_shift(s.mq, cma);
+    s.mq = cma;
+  }
+  const float mq = s.mq;
+  float accq = 0.f;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    accq += exp_shift(a[u].x, mq) + exp_shift(a[u].y, mq) + exp_shift(a[u].z, mq) +
+            exp_shift(a[u].w, mq);
+  }
+  s.sq += accq;
+  float cmb = max4(b[0]);
+#pragma unroll
+  for (int u = 1; u < U; ++u) cmb = fmaxf(cmb, max4(b[u]));
+  if (KIND == kKindKL) {
+    if (cmb > s.mp) {
+      const float f = exp_shift(s.mp, cmb);
+      s.sp *= f;
+      s.t *= f;
+      s.mp = cmb;
+    }
+    const float mp = s.mp;
+    float accp = 0.f, acct = 0.f;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const float ex = exp_shift(b[u].x, mp);
+      const float ey = exp_shift(b[u].y, mp);
+      const float ez = exp_shift(b[u].z, mp);
+      const float ew = exp_shift(b[u].w, mp);
+      accp += (ex + ey) + (ez + ew);
+      acct = fmaf(ex, b[u].x - a[u].x, acct);
+      acct = fmaf(ey, b[u].y - a[u].y, acct);
+      acct = fmaf(ez, b[u].z - a[u].z, acct);
+      acct = fmaf(ew, b[u].w - a[u].w, acct);
+    }
+    s.sp += accp;
+    s.t += acct;
+  } else {
+    if (cmb > s.bx) {
+      // first element of the group equal to its max, in index order
+#pragma unroll
+      for (int u = U - 1; u >= 0; --u) {
+        const int k = base_idx + u * stride_idx;
+        if (b[u].w == cmb) { s.bi = k + 3; s.bl = a[u].w; }
+        if (b[u].z == cmb) { s.bi = k + 2; s.bl = a[u].z; }
+        if (b[u].y == cmb) { s.bi = k + 1; s.bl = a[u].y; }
+        if (b[u].x == cmb) { s.bi = k + 0; s.bl = a[u].x; }
+      }
+      s.bx = cmb;
+    }
+  }
+}
+
+
+}  // namespace specdec

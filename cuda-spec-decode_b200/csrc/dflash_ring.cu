@@ -1,0 +1,512 @@
+// DFlash objective, forward and backward, on the warp-specialized CTA ring
+// (ring.cuh), two input streams (draft and verifier logits) per stage.
+//
+// Same arithmetic and outputs as dflash_kernels.cu (the 128-bit-load kernels,
+// kept for inputs whose base addresses are not 16-byte aligned).
+//
+// Forward = two launches on the stream:
+//   1. dflash_fwd_ring_kernel streams each (draft, verifier) row pair once:
+//      every consumer warp keeps the DfState of the row it is in (KL: draft
+//      and verifier log-sum-exp plus t = sum e^(xt - mp) (xt - xl); CE: draft
+//      log-sum-exp plus the first-index argmax of xt and the draft logit
+//      there) and stores it per (row, block) piece at
+//      part[(r * pmax + block_in_row) * NC + warp]. Plain stores only.
+//   2. dflash_finalize_kernel (programmatic dependent launch): one CTA per
+//      sequence, warp j <-> row j merges the row's pieces in slot order,
+//      forms KL = t/sp + (mq - mp) + log(sq/sp) or CE = logZq - xl[argmax],
+//      the weight mask * decay(j % block_size) / (sum mask + 1e-5), writes the
+//      per-row outputs; the last CTA (done counter) sums the per-sequence
+//      losses in index order.
+// Backward = one launch: dflash_bwd_ring_kernel streams the draft (and for KL
+// the verifier) and writes s * (softmax(draft) - softmax(verifier) | onehot).
+// Rows whose weight mask * decay is 0 are never copied.
+//
+// Reference behaviour: models/dflash/loss.py:31-126 (forward), :128-166
+// (backward); numbers follow models/dflash/tests/test_loss.py:21-49.
+#include <climits>
+
+#include "dflash_common.cuh"
+#include "ring.cuh"
+#include "specdec_common.cuh"
+#include "specdec_internal.h"
+
+namespace specdec {
+
+namespace {
+
+// Weight numerator mask * decay(pos), pos = j % block_size (test_loss.py:23-27).
+__device__ __forceinline__ float dr_numer(const DflashFwdArgs& a, int64_t r) {
+  const int pos = (int)(r % a.B) % a.block_size;
+  float decay;
+  if (a.sfa) decay = expf(__fdiv_rn(-(float)pos, a.gamma));
+  else decay = pos == 0 ? 0.f : expf(__fdiv_rn(-(float)(pos - 1), a.gamma));
+  return __fmul_rn(a.mask ? a.mask[r] : 1.f, decay);
+}
+
+template <int KIND, int NC, int S, int SE, int BS>
+__global__ void __launch_bounds__((NC + 1) * 32, 1) dflash_fwd_ring_kernel(const __grid_constant__ DflashFwdArgs a) {
+  constexpr int kSub = SE / NC;
+  constexpr int U = kSub / 128;  // float4 per lane per stream in a full sub-range
+  constexpr int64_t BL = (int64_t)BS * SE;
+  constexpr int kLogBL = __builtin_ctzll(BL);
+  static_assert(kSub % 128 == 0, "sub-range must be whole float4 rounds of a warp");
+  static_assert((BL & (BL - 1)) == 0, "block length must be a power of two");
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  auto& sm = *reinterpret_cast<RingSmem<2, S, SE>*>(smem_raw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t E = a.pt.E, V = a.pt.V, R = E / V;
+  const int pmax = a.pt.pmax;
+
+  ring_init(sm, NC);
+  const RowBits rb = build_row_bits(sm.bits, R, NC + 1, [&](int64_t r) { return dr_numer(a, r) != 0.f; });
+  __syncthreads();
+
+  BlockQueue q;
+  q.ctr = a.q_ctr;
+  q.retired = a.q_retired;
+  q.nblocks = (unsigned)((E + BL - 1) / BL);
+  q.dynamic = a.q_dynamic;
+
+  if (warp == NC) {  // producer
+    if (lane == 0) {
+      const float* src[2] = {a.logits, a.target_logits};
+      if (!ring_produce<2, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow))
+        atomicOr(a.flag, 2);
+    }
+    pdl_trigger();
+    return;
+  }
+
+  const float* ringl = sm.ring;
+  const float* ringt = sm.ring + (size_t)S * SE;
+  DfState st;
+  df_init(st);
+  int64_t r = 0, blk = -1;
+  bool live = false;
+  auto enter_row = [&](int64_t row) {
+    live = row < R && (rb.valid ? rb.live(row) : dr_numer(a, row) != 0.f);
+  };
+  auto close_piece = [&]() {
+    if (live) {
+      df_warp_merge<KIND>(st);
+      if (lane == 0) {
+        const int64_t slot = blk - (r * V) / BL;
+        float4* dst = reinterpret_cast<float4*>(a.part + (r * pmax + slot) * NC + warp);
+        dst[0] = make_float4(st.mq, st.sq, st.mp, st.sp);
+        dst[1] = make_float4(st.t, st.bx, st.bl, __int_as_float(st.bi));
+      }
+    }
+    df_init(st);
+  };
+  for (int64_t it = 0;; ++it) {
+    const int slot = (int)(it % S);
+    if (!__all_sync(kFullMask, mbar_wait(sm.full + slot, (uint32_t)((it / S) & 1)))) {
+      if (lane == 0) atomicOr(a.flag, 2);
+      ring_drain<S>(sm.full, it + 1);
+      break;
+    }
+    const int64_t f0 = sm.sf0[slot];
+    if (f0 < 0) break;
+    const int64_t b = f0 >> kLogBL;
+    const int64_t blk_end = min((b + 1) * BL, E);
+    const int64_t f1 = min(f0 + SE, blk_end);
+    if (b != blk) {
+      blk = b;
+      r = sm.srow[slot];
+      enter_row(r);
+    }
+    const float* sl = ringl + (size_t)slot * SE;
+    const float* sx = ringt + (size_t)slot * SE;
+    if (f1 - f0 == SE && (r + 1) * V >= f1) {
+      // fast path: a full stage inside one row
+      if (live) {
+        const float4* ql = reinterpret_cast<const float4*>(sl + warp * kSub) + lane;
+        const float4* qx = reinterpret_cast<const float4*>(sx + warp * kSub) + lane;
+        float4 va[U], vb[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          va[u] = ql[32 * u];
+          vb[u] = qx[32 * u];
+        }
+        const int base = (int)(f0 - r * V) + warp * kSub + 4 * lane;
+        df_group<KIND, U>(st, va, vb, base, 128);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sm.empty + slot);
+      if ((r + 1) * V == f1) {
+        close_piece();
+        ++r;
+        enter_row(r);
+      } else if (f1 == blk_end) {
+        close_piece();
+      }
+      continue;
+    }
+    const int64_t fv = f0 + ((((f1 - f0) * 4) & ~int64_t(15)) >> 2);  // end of the copied part
+    const int64_t w0 = f0 + (int64_t)warp * kSub, w1 = min(w0 + kSub, f1);
+    int64_t f = f0;
+    while (f < f1) {
+      const int64_t rend = (r + 1) * V;
+      const int64_t g = min(f1, rend);
+      if (live) {
+        const int64_t lo = max(f, w0), hi = min(g, w1);
+        for (int64_t x = lo + lane; x < hi; x += 32) {
+          const float xl = x < fv ? sl[x - f0] : __ldg(a.logits + x);
+          const float xt = x < fv ? sx[x - f0] : __ldg(a.target_logits + x);
+          df_push<KIND>(st, xl, xt, (int)(x - r * V));
+        }
+      }
+      f = g;
+      if (g == rend) {
+        close_piece();
+        ++r;
+        enter_row(r);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(sm.empty + slot);
+    if (f1 == blk_end && r * V < blk_end) close_piece();
+  }
+  pdl_trigger();
+}
+
+// One CTA per sequence n, warp j <-> row j.
+template <int KIND>
+__global__ void __launch_bounds__(1024) dflash_finalize_kernel(const __grid_constant__ DflashFwdArgs a) {
+  __shared__ float sh_loss[32];
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int B = a.B;
+  const int64_t n = blockIdx.x, V = a.pt.V, BL = a.pt.chunk;
+  const int NC = a.nc;
+  const int64_t r = n * B + warp;
+  // denominator: sum of the sequence's raw mask values + 1e-5
+  float mv = 0.f;
+  for (int i = lane; i < B; i += 32) mv += a.mask ? a.mask[n * B + i] : 1.f;
+  const float denom = warp_sum(mv) + 1e-5f;
+  const float numer = dr_numer(a, r);
+  const float w = __fdiv_rn(numer, denom);
+  float el = 0.f, lzq = 0.f, lzp = 0.f;
+  int64_t tgt = 0;
+  if (numer != 0.f) {
+    const int k = blocks_in_row(r, V, BL) * NC;
+    const DfPiece* part = a.part + r * a.pt.pmax * NC;
+    DfState s;
+    df_init(s);
+    for (int qd = lane; qd < k; qd += 32) {  // slot-major, warp-minor: fixed order
+      const float4 lo4 = reinterpret_cast<const float4*>(part + qd)[0];
+      const float4 hi4 = reinterpret_cast<const float4*>(part + qd)[1];
+      DfState o;
+      o.mq = lo4.x; o.sq = lo4.y; o.mp = lo4.z; o.sp = lo4.w;
+      o.t = hi4.x; o.bx = hi4.y; o.bl = hi4.z; o.bi = __float_as_int(hi4.w);
+      df_merge<KIND>(s, o);
+    }
+    df_warp_merge<KIND>(s);
+    lzq = s.mq + logf(s.sq);
+    if (KIND == kKindKL) {
+      lzp = s.mp + logf(s.sp);
+      // KL = sum p (xt - xl) - logZp + logZq, the normaliser difference as one log of a ratio
+      el = s.t / s.sp + ((s.mq - s.mp) + logf(s.sq / s.sp));
+    } else {
+      int bi = s.bi;
+      float bl = s.bl;
+      if (bi == INT_MAX) {  // no finite maximum (all -inf): argmax is index 0
+        bi = 0;
+        bl = a.logits[r * V];
+      }
+      tgt = bi;
+      el = lzq - bl;
+    }
+  }
+  const float lr = numer != 0.f ? __fmul_rn(w, el) : 0.f;
+  if (lane == 0) {
+    if (a.loss_rows) a.loss_rows[r] = lr;
+    a.scale[r] = __fdiv_rn(w, (float)a.n_global);
+    a.logzq[r] = lzq;
+    a.logzp[r] = lzp;
+    if (a.target_id) a.target_id[r] = tgt;
+    sh_loss[warp] = lr;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const float seq = warp_sum(lane < B ? sh_loss[lane] : 0.f);
+    unsigned last = 0;
+    if (lane == 0) {
+      a.seq_loss[n] = seq;
+      __threadfence();
+      last = (atomicAdd(a.done_cnt, 1u) + 1 == (unsigned)a.N);
+    }
+    last = __shfl_sync(kFullMask, last, 0);
+    if (last) {
+      __threadfence();
+      const float total = warp_sum_l2(a.seq_loss, a.N);
+      if (lane == 0) {
+        a.loss[0] = total / (float)a.n_global;
+        *a.done_cnt = 0u;
+      }
+    }
+  }
+}
+
+template <int KIND, int NC, int S, int SE, int BS>
+__global__ void __launch_bounds__((NC + 1) * 32, 1) dflash_bwd_ring_kernel(const __grid_constant__ DflashBwdArgs a) {
+  constexpr int NIN = KIND == kKindKL ? 2 : 1;
+  constexpr int kSub = SE / NC;
+  constexpr int64_t BL = (int64_t)BS * SE;
+  constexpr int kLogBL = __builtin_ctzll(BL);
+  static_assert(kSub % 4 == 0, "sub-range must be whole float4s");
+  static_assert((BL & (BL - 1)) == 0, "block length must be a power of two");
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  auto& sm = *reinterpret_cast<RingSmem<NIN, S, SE>*>(smem_raw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t E = a.pt.E, V = a.pt.V, R = E / V;
+  const float g = a.dloss ? __ldg(a.dloss) : 1.f;
+
+  ring_init(sm, NC);
+  const RowBits rb = build_row_bits(sm.bits, R, NC + 1, [&](int64_t r) { return __fmul_rn(a.scale[r], g) != 0.f; });
+  __syncthreads();
+
+  BlockQueue q;
+  q.ctr = a.q_ctr;
+  q.retired = a.q_retired;
+  q.nblocks = (unsigned)((E + BL - 1) / BL);
+  q.dynamic = a.q_dynamic;
+
+  if (warp == NC) {
+    if (lane == 0) {
+      const float* src[2] = {a.logits, a.target_logits};
+      if (!ring_produce<NIN, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow) &&
+          a.flag)
+        atomicOr(a.flag, 2);
+    }
+    return;
+  }
+
+  const float* ringl = sm.ring;
+  const float* ringt = sm.ring + (size_t)S * SE;  // KL only
+  int64_t r = 0, blk = -1, tf = -1;
+  float sc = 0.f, lq = 0.f, lp = 0.f;
+  auto load_row = [&](int64_t row) {
+    sc = __fmul_rn(a.scale[row], g);
+    lq = a.logzq[row];
+    lp = a.logzp[row];
+    tf = KIND == kKindCE ? row * V + a.target_id[row] : -1;
+  };
+  for (int64_t it = 0;; ++it) {
+    const int slot = (int)(it % S);
+    if (!__all_sync(kFullMask, mbar_wait(sm.full + slot, (uint32_t)((it / S) & 1)))) {
+      if (lane == 0 && a.flag) atomicOr(a.flag, 2);
+      ring_drain<S>(sm.full, it + 1);
+      return;
+    }
+    const int64_t f0 = sm.sf0[slot];
+    if (f0 < 0) return;
+    const int64_t b = f0 >> kLogBL;
+    const int64_t blk_end = min((b + 1) * BL, E);
+    const int64_t f1 = min(f0 + SE, blk_end);
+    if (b != blk) {
+      blk = b;
+      r = sm.srow[slot];
+      load_row(r);
+    }
+    const int64_t fv = f0 + ((((f1 - f0) * 4) & ~int64_t(15)) >> 2);
+    const int64_t w0 = f0 + (int64_t)warp * kSub, w1 = min(w0 + kSub, f1);
+    const float* sl = ringl + (size_t)slot * SE;
+    const float* sx = ringt + (size_t)slot * SE;
+    int64_t f = f0;
+    while (f < f1) {
+      const int64_t rend = (r + 1) * V;
+      const int64_t ge = min(f1, rend);
+      const int64_t lo = max(f, w0), hi = min(ge, w1);
+      if (lo < hi) {
+        const bool zero = sc == 0.f || !rb.live(r);
+        const int64_t lo4 = (lo + 3) & ~int64_t(3), hi4 = min(hi, fv) & ~int64_t(3);
+        float* dst = a.dlogits;
+        auto scalar = [&](int64_t x) {
+          if (zero) {
+            dst[x] = 0.f;
+          } else {
+            const float vl = x < fv ? sl[x - f0] : __ldg(a.logits + x);
+            const float qv = exp_shift(vl, lq);
+            float pv;
+            if (KIND == kKindKL) pv = exp_shift(x < fv ? sx[x - f0] : __ldg(a.target_logits + x), lp);
+            else pv = x == tf ? 1.f : 0.f;
+            dst[x] = sc * (qv - pv);
+          }
+        };
+        if (lo4 < hi4) {
+          for (int64_t x = lo + lane; x < lo4; x += 32) scalar(x);
+          for (int64_t x = hi4 + lane; x < hi; x += 32) scalar(x);
+          float4* d4 = reinterpret_cast<float4*>(dst + lo4);
+          const float4* s4 = reinterpret_cast<const float4*>(sl + (lo4 - f0));
+          const float4* t4 = reinterpret_cast<const float4*>(sx + (lo4 - f0));
+          const int n4 = (int)((hi4 - lo4) >> 2);
+          if (zero) {
+            const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int k = lane; k < n4; k += 32) st_stream(d4 + k, z);
+          } else {
+            const int64_t tq = tf - lo4;
+            for (int k = lane; k < n4; k += 32) {
+              const float4 v = s4[k];
+              float4 y;
+              y.x = exp_shift(v.x, lq);
+              y.y = exp_shift(v.y, lq);
+              y.z = exp_shift(v.z, lq);
+              y.w = exp_shift(v.w, lq);
+              if (KIND == kKindKL) {
+                const float4 u = t4[k];
+                y.x -= exp_shift(u.x, lp);
+                y.y -= exp_shift(u.y, lp);
+                y.z -= exp_shift(u.z, lp);
+                y.w -= exp_shift(u.w, lp);
+              } else {
+                const uint64_t d = (uint64_t)(tq - 4 * (int64_t)k);
+                if (d < 4) {
+                  if (d == 0) y.x -= 1.f;
+                  else if (d == 1) y.y -= 1.f;
+                  else if (d == 2) y.z -= 1.f;
+                  else y.w -= 1.f;
+                }
+              }
+              y.x *= sc;
+              y.y *= sc;
+              y.z *= sc;
+              y.w *= sc;
+              st_stream(d4 + k, y);
+            }
+          }
+        } else {
+          for (int64_t x = lo + lane; x < hi; x += 32) scalar(x);
+        }
+      }
+      f = ge;
+      if (ge == rend && ge < E) {
+        ++r;
+        load_row(r);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(sm.empty + slot);
+  }
+}
+
+template <int NC, int S, int SE, int BS>
+struct DfRing {
+  template <int KIND>
+  static constexpr size_t fsmem() { return sizeof(RingSmem<2, S, SE>); }
+  template <int KIND>
+  static constexpr size_t bsmem() { return sizeof(RingSmem<KIND == kKindKL ? 2 : 1, S, SE>); }
+  template <int KIND>
+  static int fwd_ctas(int device, int cap) {
+    return ring_occupancy_ctas(dflash_fwd_ring_kernel<KIND, NC, S, SE, BS>, (NC + 1) * 32, fsmem<KIND>(), device,
+                               cap);
+  }
+  template <int KIND>
+  static int bwd_ctas(int device, int cap) {
+    return ring_occupancy_ctas(dflash_bwd_ring_kernel<KIND, NC, S, SE, BS>, (NC + 1) * 32, bsmem<KIND>(), device,
+                               cap);
+  }
+  template <int KIND>
+  static cudaError_t fwd(DflashFwdArgs a, int ctas, cudaStream_t st) {
+    cudaFuncSetAttribute(dflash_fwd_ring_kernel<KIND, NC, S, SE, BS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)fsmem<KIND>());
+    a.nc = NC;
+    dflash_fwd_ring_kernel<KIND, NC, S, SE, BS><<<ctas, (NC + 1) * 32, fsmem<KIND>(), st>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    return launch_pdl(dflash_finalize_kernel<KIND>, dim3((unsigned)a.N), dim3(32 * a.B), st, a);
+  }
+  template <int KIND>
+  static cudaError_t bwd(const DflashBwdArgs& a, int ctas, cudaStream_t st) {
+    cudaFuncSetAttribute(dflash_bwd_ring_kernel<KIND, NC, S, SE, BS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)bsmem<KIND>());
+    dflash_bwd_ring_kernel<KIND, NC, S, SE, BS><<<ctas, (NC + 1) * 32, bsmem<KIND>(), st>>>(a);
+    return cudaGetLastError();
+  }
+};
+
+// Ring shapes (consumer warps x stages x stage floats per stream x stages per
+// block); the forward ring holds both streams:
+// 0 = 4 x 4 x 2048 x 8 (64 KB ring, 64 KB blocks per stream, 3 CTAs/SM);
+// 1 = 4 x 4 x 4096 x 4 (128 KB ring, 1 CTA/SM); 2 = 4 x 6 x 2048 x 8 (96 KB
+// ring, 2 CTAs/SM); 3 = 2 x 4 x 2048 x 8 (64 KB ring, 3 CTAs/SM);
+// 4 = 8 x 3 x 4096 x 4 (96 KB ring, 2 CTAs/SM).
+using D0 = DfRing<4, 4, 2048, 8>;
+using D1 = DfRing<4, 4, 4096, 4>;
+using D2 = DfRing<4, 6, 2048, 8>;
+using D3 = DfRing<2, 4, 2048, 8>;
+using D4 = DfRing<8, 3, 4096, 4>;
+
+template <int KIND>
+int fwd_ctas_k(int shape, int device, int cap) {
+  switch (shape) {
+    case 1: return D1::fwd_ctas<KIND>(device, cap);
+    case 2: return D2::fwd_ctas<KIND>(device, cap);
+    case 3: return D3::fwd_ctas<KIND>(device, cap);
+    case 4: return D4::fwd_ctas<KIND>(device, cap);
+    default: return D0::fwd_ctas<KIND>(device, cap);
+  }
+}
+template <int KIND>
+int bwd_ctas_k(int shape, int device, int cap) {
+  switch (shape) {
+    case 1: return D1::bwd_ctas<KIND>(device, cap);
+    case 2: return D2::bwd_ctas<KIND>(device, cap);
+    case 3: return D3::bwd_ctas<KIND>(device, cap);
+    case 4: return D4::bwd_ctas<KIND>(device, cap);
+    default: return D0::bwd_ctas<KIND>(device, cap);
+  }
+}
+template <int KIND>
+cudaError_t fwd_launch_k(int shape, const DflashFwdArgs& a, int ctas, cudaStream_t st) {
+  switch (shape) {
+    case 1: return D1::fwd<KIND>(a, ctas, st);
+    case 2: return D2::fwd<KIND>(a, ctas, st);
+    case 3: return D3::fwd<KIND>(a, ctas, st);
+    case 4: return D4::fwd<KIND>(a, ctas, st);
+    default: return D0::fwd<KIND>(a, ctas, st);
+  }
+}
+template <int KIND>
+cudaError_t bwd_launch_k(int shape, const DflashBwdArgs& a, int ctas, cudaStream_t st) {
+  switch (shape) {
+    case 1: return D1::bwd<KIND>(a, ctas, st);
+    case 2: return D2::bwd<KIND>(a, ctas, st);
+    case 3: return D3::bwd<KIND>(a, ctas, st);
+    case 4: return D4::bwd<KIND>(a, ctas, st);
+    default: return D0::bwd<KIND>(a, ctas, st);
+  }
+}
+
+}  // namespace
+
+int dflash_ring_block_elems(int shape) {
+  switch (shape) {
+    case 1: return 4096 * 4;
+    case 4: return 4096 * 4;
+    default: return 2048 * 8;
+  }
+}
+
+int dflash_ring_consumers(int shape) {
+  switch (shape) {
+    case 3: return 2;
+    case 4: return 8;
+    default: return 4;
+  }
+}
+
+int dflash_fwd_ring_ctas(int kind, int shape, int device, int cap) {
+  return kind == kKindKL ? fwd_ctas_k<kKindKL>(shape, device, cap) : fwd_ctas_k<kKindCE>(shape, device, cap);
+}
+int dflash_bwd_ring_ctas(int kind, int shape, int device, int cap) {
+  return kind == kKindKL ? bwd_ctas_k<kKindKL>(shape, device, cap) : bwd_ctas_k<kKindCE>(shape, device, cap);
+}
+cudaError_t dflash_fwd_ring_launch(int shape, const DflashFwdArgs& a, int ctas, cudaStream_t st) {
+  return a.kind == kKindKL ? fwd_launch_k<kKindKL>(shape, a, ctas, st) : fwd_launch_k<kKindCE>(shape, a, ctas, st);
+}
+cudaError_t dflash_bwd_ring_launch(int shape, const DflashBwdArgs& a, int ctas, cudaStream_t st) {
+  return a.kind == kKindKL ? bwd_launch_k<kKindKL>(shape, a, ctas, st) : bwd_launch_k<kKindCE>(shape, a, ctas, st);
+}
+
+}  // namespace specdec

@@ -57,9 +57,7 @@ int current_device() {
 // shape - 10.
 constexpr int kLdgShapeBase = 10;
 
-bool has_ring_path(int kernel) {
-  return kernel == SPECDEC_KERNEL_DPACE_FWD || kernel == SPECDEC_KERNEL_DPACE_BWD;
-}
+bool has_ring_path(int kernel) { return kernel >= 0 && kernel <= 3; }
 
 // Variant id inside the chosen kernel family.
 int kernel_shape(int kernel, bool tma) {
@@ -70,8 +68,7 @@ int kernel_shape(int kernel, bool tma) {
 }
 
 bool use_tma(int kernel, bool ptrs_aligned) {
-  return g_shape[kernel].load() < kLdgShapeBase && ptrs_aligned &&
-         (kernel == SPECDEC_KERNEL_DPACE_FWD || kernel == SPECDEC_KERNEL_DPACE_BWD);
+  return g_shape[kernel].load() < kLdgShapeBase && ptrs_aligned && has_ring_path(kernel);
 }
 
 // Occupancy-derived work units (CTAs for the 128-bit-load kernels, warps for
@@ -97,8 +94,12 @@ int kernel_units(int kernel, int kind, bool tma, int device) {
     case SPECDEC_KERNEL_DPACE_BWD:
       ctas = tma ? dpace_bwd_ring_ctas(shape, device, cap) : dpace_bwd_ctas(shape, device, cap);
       break;
-    case SPECDEC_KERNEL_DFLASH_FWD: ctas = dflash_fwd_ctas(kind, shape, device, cap); break;
-    case SPECDEC_KERNEL_DFLASH_BWD: ctas = dflash_bwd_ctas(kind, shape, device, cap); break;
+    case SPECDEC_KERNEL_DFLASH_FWD:
+      ctas = tma ? dflash_fwd_ring_ctas(kind, shape, device, cap) : dflash_fwd_ctas(kind, shape, device, cap);
+      break;
+    case SPECDEC_KERNEL_DFLASH_BWD:
+      ctas = tma ? dflash_bwd_ring_ctas(kind, shape, device, cap) : dflash_bwd_ctas(kind, shape, device, cap);
+      break;
     default: ctas = 0;
   }
   if (ctas > 0) {
@@ -145,18 +146,19 @@ Partition ring_partition(int64_t rows, int64_t V, int64_t block_elems, int ctas)
 }
 
 // ---- DFlash workspace layout -----------------------------------------------
-// counters: [done u32][pad to 16 B][row_cnt u32 x R]
-// scratch:  [part DfPiece x R*pmax][row_loss f32 x R]
+// counters: [done][flag][queue ctr][queue retired][row_cnt u32 x R]
+// scratch:  [part DfPiece x R*pmax*nc][row_loss f32 x R][seq_loss f32 x N]
 struct DflashLayout {
-  size_t part = 0, row_loss = 0, scratch = 0, counters = 0;
+  size_t part = 0, row_loss = 0, seq_loss = 0, scratch = 0, counters = 0;
 };
 
-DflashLayout dflash_layout(int64_t N, int64_t B, const Partition& pt) {
+DflashLayout dflash_layout(int64_t N, int64_t B, const Partition& pt, int nc) {
   DflashLayout L;
   const size_t R = size_t(N) * size_t(B);
   L.part = 0;
-  L.row_loss = align256(L.part + R * size_t(pt.pmax) * sizeof(DfPiece));
-  L.scratch = align256(L.row_loss + R * sizeof(float));
+  L.row_loss = align256(L.part + R * size_t(pt.pmax) * size_t(nc) * sizeof(DfPiece));
+  L.seq_loss = align256(L.row_loss + R * sizeof(float));
+  L.scratch = align256(L.seq_loss + size_t(N) * sizeof(float));
   L.counters = align256(16 + R * sizeof(unsigned));
   return L;
 }
@@ -168,9 +170,11 @@ Partition dpace_fwd_partition(int64_t N, int32_t B, int64_t V, bool tma, int dev
   return make_partition(N * B, V, units, kMinChunk);
 }
 
-Partition dflash_fwd_partition(int64_t N, int32_t B, int64_t V, int kind, int device) {
-  const int ctas = kernel_units(SPECDEC_KERNEL_DFLASH_FWD, kind, false, device);
-  return make_partition(N * B, V, ctas, kMinChunk);
+Partition dflash_fwd_partition(int64_t N, int32_t B, int64_t V, int kind, bool tma, int device) {
+  const int units = kernel_units(SPECDEC_KERNEL_DFLASH_FWD, kind, tma, device);
+  if (tma)
+    return ring_partition(N * B, V, dflash_ring_block_elems(kernel_shape(SPECDEC_KERNEL_DFLASH_FWD, true)), units);
+  return make_partition(N * B, V, units, kMinChunk);
 }
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -241,7 +245,7 @@ size_t specdec_dpace_counter_bytes(int64_t N, int32_t B) {
   return dpace_counter_bytes(N > 0 ? N : 0, B > 0 ? B : 0);
 }
 
-size_t specdec_dpace_backward_counter_bytes(void) { return 256; }
+size_t specdec_backward_counter_bytes(void) { return 256; }
 
 int specdec_dpace_forward(const float* logits, const int64_t* targets, const float* mask,
                           int64_t N, int32_t B, int64_t V, float alpha, int32_t loss_type,
@@ -362,10 +366,18 @@ int specdec_dpace_backward(const float* logits, const int64_t* targets, const fl
 
 size_t specdec_dflash_scratch_bytes(int64_t N, int32_t B, int64_t V, int device) {
   if (N <= 0 || B <= 0 || V <= 0) return 256;
-  // both kinds share one partition rule; take the larger of the two
-  const DflashLayout a = dflash_layout(N, B, dflash_fwd_partition(N, B, V, kKindKL, device));
-  const DflashLayout b = dflash_layout(N, B, dflash_fwd_partition(N, B, V, kKindCE, device));
-  return a.scratch > b.scratch ? a.scratch : b.scratch;
+  // large enough for either kind and either kernel family
+  size_t best = 0;
+  for (int kind = 0; kind < 2; ++kind) {
+    const size_t a = dflash_layout(N, B, dflash_fwd_partition(N, B, V, kind, false, device), 1).scratch;
+    best = a > best ? a : best;
+    if (use_tma(SPECDEC_KERNEL_DFLASH_FWD, true) && B <= 32) {
+      const int nc = dflash_ring_consumers(kernel_shape(SPECDEC_KERNEL_DFLASH_FWD, true));
+      const size_t b = dflash_layout(N, B, dflash_fwd_partition(N, B, V, kind, true, device), nc).scratch;
+      best = b > best ? b : best;
+    }
+  }
+  return best;
 }
 
 size_t specdec_dflash_counter_bytes(int64_t N, int32_t B) {
@@ -402,9 +414,12 @@ int specdec_dflash_forward(const float* logits, const float* target_logits, cons
     return fail(SPECDEC_ERR_ARGUMENT, "misaligned workspace (scratch 256 B, counters 16 B)");
   const int dev = current_device();
   if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
-  const Partition pt = dflash_fwd_partition(N, B, V, kind, dev);
+  const bool tma =
+      use_tma(SPECDEC_KERNEL_DFLASH_FWD, aligned(logits, 16) && aligned(target_logits, 16)) && B <= 32;
+  const Partition pt = dflash_fwd_partition(N, B, V, kind, tma, dev);
   if (pt.grid <= 0) return fail(SPECDEC_ERR_CUDA, "occupancy query failed");
-  const DflashLayout L = dflash_layout(N, B, pt);
+  const int nc = tma ? dflash_ring_consumers(kernel_shape(SPECDEC_KERNEL_DFLASH_FWD, true)) : 1;
+  const DflashLayout L = dflash_layout(N, B, pt, nc);
   if (scratch_bytes < L.scratch)
     return fail(SPECDEC_ERR_WORKSPACE, "scratch needs %zu bytes, got %zu", L.scratch, scratch_bytes);
   if (counter_bytes < L.counters)
@@ -431,17 +446,25 @@ int specdec_dflash_forward(const float* logits, const float* target_logits, cons
   a.target_id = target_id;
   a.part = reinterpret_cast<DfPiece*>(ws + L.part);
   a.row_loss = reinterpret_cast<float*>(ws + L.row_loss);
+  a.seq_loss = reinterpret_cast<float*>(ws + L.seq_loss);
   a.done_cnt = cnt;
+  a.flag = reinterpret_cast<int*>(cnt + 1);
+  a.q_ctr = cnt + 2;
+  a.q_retired = cnt + 3;
+  a.q_dynamic = g_static_queue.load() ? 0 : 1;
   a.row_cnt = cnt + 4;
+  a.nc = nc;
   a.pt = pt;
-  const cudaError_t e = dflash_fwd_launch(kernel_shape(SPECDEC_KERNEL_DFLASH_FWD, false), a, st);
+  const int shape = kernel_shape(SPECDEC_KERNEL_DFLASH_FWD, tma);
+  const cudaError_t e =
+      tma ? dflash_fwd_ring_launch(shape, a, (int)pt.grid, st) : dflash_fwd_launch(shape, a, st);
   return e == cudaSuccess ? ok() : cuda_fail(e, "dflash forward launch");
 }
 
 int specdec_dflash_backward(const float* logits, const float* target_logits, const float* scale,
                             const float* logzq, const float* logzp, const int64_t* target_id,
                             const float* dloss, float* dlogits, int64_t N, int32_t B, int64_t V,
-                            int32_t kind, void* stream) {
+                            int32_t kind, void* counters, size_t counter_bytes, void* stream) {
   if (N < 0 || B < 0 || V < 0) return fail(SPECDEC_ERR_ARGUMENT, "negative shape");
   if (kind != SPECDEC_DFLASH_KL && kind != SPECDEC_DFLASH_CE)
     return fail(SPECDEC_ERR_VALUE, "unknown loss kind %d", kind);
@@ -454,7 +477,10 @@ int specdec_dflash_backward(const float* logits, const float* target_logits, con
     return fail(SPECDEC_ERR_ARGUMENT, "dlogits must not alias an input");
   const int dev = current_device();
   if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
-  const int ctas = kernel_units(SPECDEC_KERNEL_DFLASH_BWD, kind, false, dev);
+  const bool tma = use_tma(SPECDEC_KERNEL_DFLASH_BWD,
+                           aligned(logits, 16) && aligned(dlogits, 16) &&
+                               (kind == SPECDEC_DFLASH_CE || aligned(target_logits, 16)));
+  const int ctas = kernel_units(SPECDEC_KERNEL_DFLASH_BWD, kind, tma, dev);
   if (ctas <= 0) return fail(SPECDEC_ERR_CUDA, "occupancy query failed");
   DflashBwdArgs a;
   a.logits = logits;
@@ -466,9 +492,18 @@ int specdec_dflash_backward(const float* logits, const float* target_logits, con
   a.dloss = dloss;
   a.dlogits = dlogits;
   a.kind = kind;
-  a.pt = make_partition(N * B, V, ctas, kMinChunk);
-  const cudaError_t e =
-      dflash_bwd_launch(kernel_shape(SPECDEC_KERNEL_DFLASH_BWD, false), a, static_cast<cudaStream_t>(stream));
+  a.flag = nullptr;
+  const bool queue = counters != nullptr && counter_bytes >= 16 && aligned(counters, 16) &&
+                     !g_static_queue.load();
+  unsigned* cnt = static_cast<unsigned*>(counters);
+  a.q_ctr = queue ? cnt : nullptr;
+  a.q_retired = queue ? cnt + 1 : nullptr;
+  a.q_dynamic = queue ? 1 : 0;
+  const int shape = kernel_shape(SPECDEC_KERNEL_DFLASH_BWD, tma);
+  a.pt = tma ? ring_partition(N * B, V, dflash_ring_block_elems(shape), ctas)
+             : make_partition(N * B, V, ctas, kMinChunk);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const cudaError_t e = tma ? dflash_bwd_ring_launch(shape, a, ctas, st) : dflash_bwd_launch(shape, a, st);
   return e == cudaSuccess ? ok() : cuda_fail(e, "dflash backward launch");
 }
 

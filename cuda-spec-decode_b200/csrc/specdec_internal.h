@@ -85,11 +85,17 @@ struct DflashFwdArgs {
   float* logzp;                // [N*B]
   int64_t* target_id;          // [N*B] argmax(verifier) for CE, or null
   // workspace
-  DfPiece* part;               // [N*B, pt.pmax]
-  float* row_loss;             // [N*B]
-  unsigned* row_cnt;           // [N*B] zero on entry, zero on exit
+  DfPiece* part;               // [N*B, pt.pmax, nc]
+  float* row_loss;             // [N*B] 128-bit-load kernel
+  float* seq_loss;             // [N]   ring kernel
+  unsigned* row_cnt;           // [N*B] 128-bit-load kernel; zero on entry, zero on exit
   unsigned* done_cnt;          // [1]   zero on entry, zero on exit
-  Partition pt;
+  int* flag;                   // [1]   bit 2: a copy wait timed out
+  unsigned* q_ctr;             // ring kernel block queue; zero on entry/exit
+  unsigned* q_retired;
+  int q_dynamic;
+  int nc;                      // partials per (row, slot)
+  Partition pt;                // ring kernel: chunk = block length
 };
 
 struct DflashBwdArgs {
@@ -102,6 +108,10 @@ struct DflashBwdArgs {
   const float* dloss;
   float* dlogits;
   int kind;
+  int* flag;                   // [1] or null
+  unsigned* q_ctr;             // ring kernel block queue (null: static interleave)
+  unsigned* q_retired;
+  int q_dynamic;
   Partition pt;
 };
 
@@ -119,6 +129,14 @@ int dpace_fwd_ring_ctas(int shape, int device, int cap_per_sm);
 int dpace_bwd_ring_ctas(int shape, int device, int cap_per_sm);
 cudaError_t dpace_fwd_ring_launch(int shape, const DpaceFwdArgs& a, int ctas, cudaStream_t st);
 cudaError_t dpace_bwd_ring_launch(int shape, const DpaceBwdArgs& a, int ctas, cudaStream_t st);
+
+// Warp-specialized ring kernels (dflash_ring.cu); sizes in CTAs.
+int dflash_ring_block_elems(int shape);
+int dflash_ring_consumers(int shape);
+int dflash_fwd_ring_ctas(int kind, int shape, int device, int cap_per_sm);
+int dflash_bwd_ring_ctas(int kind, int shape, int device, int cap_per_sm);
+cudaError_t dflash_fwd_ring_launch(int shape, const DflashFwdArgs& a, int ctas, cudaStream_t st);
+cudaError_t dflash_bwd_ring_launch(int shape, const DflashBwdArgs& a, int ctas, cudaStream_t st);
 
 // Sets the calling thread's specdec_last_error() text.
 void set_last_error(const char* msg);

@@ -49,7 +49,7 @@ _SIGNATURES = {
     "specdec_dpace_forward_noalloc": (ctypes.c_int, [
         _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_f32, _c_i32, _c_i64,
         _c_p, _c_p, _c_p, _c_p, _c_p, _c_p]),
-    "specdec_dpace_backward_counter_bytes": (_c_sz, []),
+    "specdec_backward_counter_bytes": (_c_sz, []),
     "specdec_dpace_backward": (ctypes.c_int, [
         _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_p, _c_sz, _c_p]),
     "specdec_dflash_scratch_bytes": (_c_sz, [_c_i64, _c_i32, _c_i64, ctypes.c_int]),
@@ -58,7 +58,8 @@ _SIGNATURES = {
         _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_i32, _c_f32, _c_i32, _c_i32, _c_i64,
         _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_sz, _c_p, _c_sz, _c_p]),
     "specdec_dflash_backward": (ctypes.c_int, [
-        _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_i32, _c_p]),
+        _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_i32, _c_p, _c_sz,
+        _c_p]),
     "specdec_set_launch_shape": (ctypes.c_int, [_c_i32, _c_i32, _c_i32]),
     "specdec_launch_ctas": (_c_i64, [_c_i32, _c_i64, _c_i64, ctypes.c_int]),
     "specdec_set_block_queue": (ctypes.c_int, [_c_i32]),

@@ -72,7 +72,7 @@ def _dpace_backward(logits: torch.Tensor, targets: torch.Tensor, lse: torch.Tens
     dlogits = torch.empty_like(logits) if out is None else out
     if dloss is not None:
         dloss = dloss.detach().to(device=dev, dtype=torch.float32).contiguous()
-    cb = lib.specdec_dpace_backward_counter_bytes()
+    cb = lib.specdec_backward_counter_bytes()
     _, counters = _lib.workspace("dpace_bwd", dev).ensure(dev, 256, cb)
     code = lib.specdec_dpace_backward(
         logits.data_ptr(), targets.data_ptr(), lse.data_ptr(), scale.data_ptr(),
@@ -116,13 +116,16 @@ def _dflash_backward(logits: torch.Tensor, target_logits: torch.Tensor | None, s
                     out: torch.Tensor | None = None) -> torch.Tensor:
     lib = _lib.load()
     N, B, V = logits.shape
+    dev = logits.device
     dlogits = torch.empty_like(logits) if out is None else out
     if dloss is not None:
-        dloss = dloss.detach().to(device=logits.device, dtype=torch.float32).contiguous()
+        dloss = dloss.detach().to(device=dev, dtype=torch.float32).contiguous()
+    cb = lib.specdec_backward_counter_bytes()
+    _, counters = _lib.workspace("dflash_bwd", dev).ensure(dev, 256, cb)
     code = lib.specdec_dflash_backward(
         logits.data_ptr(), _lib.ptr(target_logits), scale.data_ptr(), logzq.data_ptr(),
         logzp.data_ptr(), _lib.ptr(tgt), _lib.ptr(dloss), dlogits.data_ptr(), N, B, V, int(kind),
-        _lib.stream_handle(logits.device))
+        counters.data_ptr(), counters.numel(), _lib.stream_handle(dev))
     _lib.check(code, "specdec_dflash_backward")
     return dlogits
 

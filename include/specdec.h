@@ -98,15 +98,15 @@ int specdec_dpace_forward(const float* logits, const int64_t* targets, const flo
                           int32_t* status, void* scratch, size_t scratch_bytes, void* counters,
                           size_t counter_bytes, void* stream);
 
-/* Counter bytes for specdec_dpace_backward's optional block queue. */
-size_t specdec_dpace_backward_counter_bytes(void);
+/* Counter bytes for the optional block queue of both backward entry points. */
+size_t specdec_backward_counter_bytes(void);
 
 /*
  * D-PACE backward. Replaces the launch of dpace_backward in
  * losses/dpace.py:217-226 (DPACELoss.backward):
  *   dlogits = scale[n, j] * dloss[0] * (softmax(logits[n, j]) - onehot(targets[n, j]))
  * dloss may be NULL (treated as 1). dlogits must not alias logits.
- * counters (zeroed once, left zeroed; specdec_dpace_backward_counter_bytes())
+ * counters (zeroed once, left zeroed; specdec_backward_counter_bytes())
  * enable the dynamic block queue; NULL selects a static block interleave.
  */
 int specdec_dpace_backward(const float* logits, const int64_t* targets, const float* lse,
@@ -171,11 +171,12 @@ int specdec_dflash_forward(const float* logits, const float* target_logits, cons
  *   KL: dlogits = scale * dloss * (softmax(logits) - softmax(target_logits))
  *   CE: dlogits = scale * dloss * (softmax(logits) - onehot(target_id))
  * target_logits is read for KL only (may be NULL for CE); target_id for CE only.
+ * counters: as for specdec_dpace_backward (NULL = static block interleave).
  */
 int specdec_dflash_backward(const float* logits, const float* target_logits, const float* scale,
                             const float* logzq, const float* logzp, const int64_t* target_id,
                             const float* dloss, float* dlogits, int64_t N, int32_t B, int64_t V,
-                            int32_t kind, void* stream);
+                            int32_t kind, void* counters, size_t counter_bytes, void* stream);
 
 /* ------------------------------------------------------------------------- */
 /* Launch tuning                                                              */
@@ -189,11 +190,11 @@ int specdec_dflash_backward(const float* logits, const float* target_logits, con
 
 /*
  * Selects a kernel variant and caps resident CTAs per SM (0 = occupancy
- * limit) for one kernel, process-wide. For the D-PACE kernels shapes 0..4 are
- * warp-specialized bulk-copy ring variants (used when logits and dlogits are
- * 16-byte aligned) and 10..14 force the 128-bit-load kernels; for DFlash,
- * 0..4 are (threads, unroll) variants. Workspace sizes depend on it: query
- * sizes after changing it.
+ * limit) for one kernel, process-wide. Shapes 0..4 are warp-specialized
+ * bulk-copy ring variants (used when the streamed pointers are 16-byte
+ * aligned, and for DFlash when B <= 32; otherwise the 128-bit-load kernels run
+ * with their default shape); 10..14 force the 128-bit-load kernels, variant
+ * shape - 10. Workspace sizes depend on it: query sizes after changing it.
  */
 int specdec_set_launch_shape(int32_t kernel, int32_t shape, int32_t ctas_per_sm);
 

@@ -40,7 +40,7 @@ def test_version_and_status_strings():
 def test_counter_bytes_are_host_only():
     lib = _lib.load()
     assert lib.specdec_dpace_counter_bytes(64, 16) >= 16 + 64 * 4
-    assert lib.specdec_dpace_backward_counter_bytes() >= 16
+    assert lib.specdec_backward_counter_bytes() >= 16
     assert lib.specdec_dflash_counter_bytes(64, 16) >= 16 + 64 * 16 * 4
     assert lib.specdec_dpace_counter_bytes(64, 16) % 256 == 0
 

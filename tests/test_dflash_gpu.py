@@ -192,3 +192,71 @@ def test_full_size_correlated_verifier(cuda, kind):
     _close_loss(float(loss.detach()), float(want))
     diff = (xg.grad.cpu() - gr).abs().max().item()
     assert diff <= GRAD_ATOL, diff
+
+
+SHAPE_CASES = [c for c in cases.DFLASH_CASES if c["name"] in (
+    "kl_bern.5_N8_B8_V1024", "ce_bern.5_N8_B8_V1024", "kl_V7_N6_B8", "kl_V1000_N6_B8",
+    "kl_sfa_N4_B8_V1024", "ce_bs4_N4_B16_V1024", "kl_bs3_N3_B8_V256_ragged", "ce_ties_N4_B8_V64",
+    "ws3_kl_N4_B16_V128256_sd2_corr", "ws3_ce_N2_B16_V128256_sd2_corr")]
+
+
+@pytest.mark.parametrize("shape", [0, 1, 2, 3, 4, 10, 11, 12, 13, 14])
+def test_every_launch_shape_matches_golden(cuda, gf, shape):
+    """Shapes 0-4: warp-specialized bulk-copy ring variants; 10-14: 128-bit-load kernels."""
+    from specdec import _lib
+
+    try:
+        _lib.set_launch_shape(_lib.KERNEL_DFLASH_FWD, shape)
+        _lib.set_launch_shape(_lib.KERNEL_DFLASH_BWD, shape)
+        for case in SHAPE_CASES:
+            x, y, m = cases.dflash_inputs(case)
+            key = case["name"]
+            loss, grad = _run(x, y, m, case["gamma"], case["sfa"], case["kind"], case["block_size"])
+            _close_loss(loss, float(gf[f"{key}/loss"]))
+            if f"{key}/grad" in gf.files:
+                np.testing.assert_allclose(grad, gf[f"{key}/grad"], rtol=0, atol=GRAD_ATOL)
+            else:
+                idx = gf[f"{key}/probe_idx"]
+                np.testing.assert_allclose(grad.reshape(-1)[idx], gf[f"{key}/probe_val"], rtol=0,
+                                           atol=GRAD_ATOL)
+    finally:
+        _lib.set_launch_shape(_lib.KERNEL_DFLASH_FWD, 0)
+        _lib.set_launch_shape(_lib.KERNEL_DFLASH_BWD, 0)
+
+
+def test_static_interleave_and_schedule_independence(cuda):
+    """Ring kernels with the static block interleave give the same bits as the
+    dynamic queue (partials are slotted by block index)."""
+    from specdec import _lib, ops
+
+    g = torch.Generator(device="cuda").manual_seed(9)
+    x = torch.randn(16, 16, 128256, device="cuda", generator=g) * 2.0
+    y = x + torch.randn(16, 16, 128256, device="cuda", generator=g)
+    for kind in (0, 1):
+        ref = None
+        for dynamic in (True, False, True):
+            _lib.set_block_queue(dynamic)
+            loss, rows, scale, lzq, lzp, tgt = ops.dflash_forward(x, y, None, 4.0, False, kind, 16)
+            gr = ops.dflash_backward(x, y if kind == 0 else None, scale, lzq, lzp, tgt, None, kind)
+            if ref is None:
+                ref = (loss.clone(), rows.clone(), gr.clone())
+            else:
+                assert torch.equal(loss, ref[0]) and torch.equal(rows, ref[1]) and torch.equal(gr, ref[2])
+    _lib.set_block_queue(True)
+
+
+def test_large_block_size_falls_back(cuda):
+    """B > 32 positions per sequence (allowed by the reference) runs on the
+    128-bit-load kernels; results match the oracle."""
+    from models.dflash import dflash_loss
+
+    rng = np.random.default_rng(40)
+    N, B, V = 2, 40, 3000
+    x = rng.normal(size=(N, B, V)).astype(np.float32)
+    y = rng.normal(size=(N, B, V)).astype(np.float32)
+    xt = torch.from_numpy(x).cuda().requires_grad_(True)
+    loss = dflash_loss(xt, torch.from_numpy(y).cuda(), None, 4.0, False, "kl", 8)
+    loss.backward()
+    want, g = odf.dflash_fwd_bwd_torch(torch.from_numpy(x), torch.from_numpy(y), None, 4.0, False, "kl", 8)
+    _close_loss(float(loss.detach()), float(want))
+    np.testing.assert_allclose(xt.grad.cpu().numpy(), g.numpy(), rtol=0, atol=GRAD_ATOL)
