@@ -212,6 +212,74 @@ def run_reference(args):
 
 # ----------------------------------------------------------------------------- our arm
 
+def time_dflash(args, dev, stream, world, n_global, max_over_ranks, barrier):
+    """DFlash objective (KL), draft [64, 16, 128256] ~ N(0, 2^2), verifier =
+    draft + N(0, 1), gamma 4, anchor slot unscored, every slot masked in.
+    Bytes model 20 * N*B*V per step (forward reads both, backward reads both
+    and writes the gradient); required bytes skip the zero-weight anchor rows."""
+    from specdec import ops
+
+    N, B, V = args.n, 16, 128256
+    E = N * B * V
+    sets = [dflash_inputs(N, B, V, 2000 * s + int(os.environ.get("RANK", "0")), dev) for s in range(2)]
+    grad = torch.empty(N, B, V, device=dev)
+
+    def step(i, ev=None):
+        x, y = sets[i & 1]
+        if ev is not None:
+            ev[0].record(stream)
+        loss, _, scale, lzq, lzp, _ = ops.dflash_forward(x, y, None, 4.0, False, 0, B, n_global)
+        if ev is not None:
+            ev[1].record(stream)
+        if world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(loss)
+        if ev is not None:
+            ev[2].record(stream)
+        ops.dflash_backward(x, y, scale, lzq, lzp, None, None, 0, out=grad)
+        if ev is not None:
+            ev[3].record(stream)
+
+    for i in range(args.warmup):
+        step(i)
+    K = args.dflash_steps
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(dev)
+    a.record(stream)
+    for k in range(K):
+        step(k, evs[k])
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    ms = max_over_ranks(a.elapsed_time(b)) / K
+    fwd = max_over_ranks(statistics.mean(e[0].elapsed_time(e[1]) for e in evs))
+    bwd = max_over_ranks(statistics.mean(e[2].elapsed_time(e[3]) for e in evs))
+    live = 15.0 / 16.0
+    peak, _ = hbm_peak()
+    bwd_bytes = 8.0 * E * live + 4.0 * E
+    fwd_bytes = 8.0 * E * live
+    wl = f"{N}x{B}x{V}"
+    value = 20.0 * E * world / (ms * 1e-3) / 1e9
+    return {"metric": "DFlash-KL fwd+bwd logits GB/s (20*N*B*V bytes per GPU-step)",
+            "value": round(value, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
+            "rows_per_s": round(N * B * world / (ms * 1e-3), 1),
+            "pct_of_hbm_peak": round(100.0 * value / world / peak, 2),
+            "fwd_ms": round(fwd, 4), "bwd_ms": round(bwd, 4), "steps": K,
+            "config": {"workload": "dflash_kl_fwd_bwd_llama3_vocab", "N_per_gpu": N, "B": B, "V": V,
+                       "draft": "N(0, 2^2)", "verifier": "draft + N(0, 1)", "gamma": 4.0,
+                       "sample_from_anchor": False, "mask": "all ones"},
+            "roofline": {"kernel": "dflash_bwd_ring_kernel<KL>", "bound": "hbm",
+                         "achieved": round(bwd_bytes / (bwd * 1e-3) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(bwd_bytes / (bwd * 1e-3) / 1e9 / peak, 4),
+                         "traffic": profiled_traffic("dflash_bwd_kl", wl), "bytes_per_launch": bwd_bytes},
+            "fwd_roofline": {"kernel": "dflash_fwd_ring_kernel<KL> + finalize",
+                             "achieved": round(fwd_bytes / (fwd * 1e-3) / 1e9, 1),
+                             "frac": round(fwd_bytes / (fwd * 1e-3) / 1e9 / peak, 4),
+                             "traffic": profiled_traffic("dflash_fwd_kl", wl), "bytes_per_launch": fwd_bytes}}
+
+
 def run_ours(args):
     import torch.distributed as dist
     from datetime import timedelta
@@ -245,6 +313,8 @@ def run_ours(args):
     live = [float(m.sum()) / (N * B) for (_, _, m) in sets]
     grad = torch.empty(N, B, V, device=dev)
     stream = torch.cuda.current_stream(dev)
+    # ring kernels (16-byte-aligned inputs): forward = streaming + finalize, backward = 1
+    launches_per_step = 3 if all(x.data_ptr() % 16 == 0 for x, _, _ in sets) else 2
 
     def step(i, ev=None):
         x, t, m = sets[i & 1]
@@ -291,6 +361,9 @@ def run_ours(args):
     bwd_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in evs)
     ms = max_over_ranks(ms_local)
     fwd_ms_max, bwd_ms_max = max_over_ranks(fwd_ms), max_over_ranks(bwd_ms)
+    dflash = None
+    if args.dflash_steps > 0:
+        dflash = time_dflash(args, dev, stream, world, n_global, max_over_ranks, barrier)
     ms_step = ms / args.steps
     total_bytes = 12.0 * E * world
     value = total_bytes / (ms_step * 1e-3) / 1e9
@@ -368,10 +441,13 @@ def run_ours(args):
             "pct_of_hbm_peak": round(100.0 * value / world / peak, 2),
             "roofline": roof_bwd,
             "kernels": {"dpace_fwd_ms": round(fwd_ms_max, 4), "dpace_bwd_ms": round(bwd_ms_max, 4),
-                        "fwd": roof_fwd},
+                        "fwd": roof_fwd,
+                        "launches_per_step": launches_per_step,
+                        "fwd_note": "forward = streaming kernel + PDL-chained finalize kernel"},
+            "dflash_kl": dflash,
             "live_row_fraction": round(live_frac, 4),
             "cpu_baseline": cpu_base, "e2e": e2e,
-            "gpu_launches": 2 * args.steps, "gpu_launches_scope": "per rank",
+            "gpu_launches": launches_per_step * args.steps, "gpu_launches_scope": "per rank",
             "clocks": clocks}
     print(json.dumps(line), flush=True)
     return 0
@@ -386,6 +462,8 @@ def main(argv=None):
     p.add_argument("--n", type=int, default=64, help="sequences per GPU")
     p.add_argument("--soak", type=float, default=1.0, help="seconds of untimed load before timing")
     p.add_argument("--e2e-steps", type=int, default=20)
+    p.add_argument("--dflash-steps", type=int, default=100,
+                   help="timed steps of the DFlash-KL workload (0 = skip)")
     p.add_argument("--cpu-budget", type=float, default=10.0,
                    help="seconds of CPU-oracle timing on rank 0 at N=1 (0 = skip)")
     args = p.parse_args(argv)
