@@ -37,6 +37,8 @@ sys.path.insert(0, REPO)
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
+from specdec.dist import LossReducer  # noqa: E402
+
 METRIC = "fwd+bwd logits GB/s (% of B200 HBM peak) at V=128256; rows/s at 1/2/4/8 GPU"
 UNIT = "GB/s"
 FALLBACK_HBM_GBS = 6650.0
@@ -212,72 +214,263 @@ def run_reference(args):
 
 # ----------------------------------------------------------------------------- our arm
 
-def time_dflash(args, dev, stream, world, n_global, max_over_ranks, barrier):
+def time_pair(args, stream, world, max_over_ranks, barrier, fwd, bwd, steps):
+    """Times `steps` steps of fwd(i) (+ the loss all_reduce when world > 1) +
+    bwd(i, state) on alternating input sets after args.warmup untimed steps.
+    Returns (ms per step, mean forward ms, mean backward ms), max over ranks."""
+
+    reducer = LossReducer(stream.device) if world > 1 else None
+
+    def step(i, ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        loss, state = fwd(i)
+        if ev is not None:
+            ev[1].record(stream)
+        if reducer is not None:
+            reducer.start(loss)
+        if ev is not None:
+            ev[2].record(stream)
+        bwd(i, state)
+        if ev is not None:
+            ev[3].record(stream)
+        if reducer is not None:
+            reducer.wait()
+
+    for i in range(args.warmup):
+        step(i)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    a.record(stream)
+    for k in range(steps):
+        step(k, evs[k])
+    b.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(a.elapsed_time(b)) / steps
+    f = max_over_ranks(statistics.mean(e[0].elapsed_time(e[1]) for e in evs))
+    g = max_over_ranks(statistics.mean(e[2].elapsed_time(e[3]) for e in evs))
+    return ms, f, g
+
+
+def time_dflash(args, dev, stream, world, n_global, max_over_ranks, barrier, dtype=torch.float32, steps=None):
     """DFlash objective (KL), draft [64, 16, 128256] ~ N(0, 2^2), verifier =
     draft + N(0, 1), gamma 4, anchor slot unscored, every slot masked in.
-    Bytes model 20 * N*B*V per step (forward reads both, backward reads both
-    and writes the gradient); required bytes skip the zero-weight anchor rows."""
+    Bytes model 20 * N*B*V per step for fp32 (forward reads both, backward
+    reads both and writes the gradient), 10 * N*B*V for bf16; required bytes
+    skip the zero-weight anchor rows."""
     from specdec import ops
 
     N, B, V = args.n, 16, 128256
     E = N * B * V
-    sets = [dflash_inputs(N, B, V, 2000 * s + int(os.environ.get("RANK", "0")), dev) for s in range(2)]
-    grad = torch.empty(N, B, V, device=dev)
+    esz = 2 if dtype == torch.bfloat16 else 4
+    sets = []
+    for s_ in range(2):
+        x, y = dflash_inputs(N, B, V, 2000 * s_ + int(os.environ.get("RANK", "0")), dev)
+        sets.append((x.to(dtype), y.to(dtype)))
+        del x, y
+    grad = torch.empty(N, B, V, device=dev, dtype=dtype)
 
-    def step(i, ev=None):
+    def fwd(i):
         x, y = sets[i & 1]
-        if ev is not None:
-            ev[0].record(stream)
         loss, _, scale, lzq, lzp, _ = ops.dflash_forward(x, y, None, 4.0, False, 0, B, n_global)
-        if ev is not None:
-            ev[1].record(stream)
-        if world > 1:
-            import torch.distributed as dist
-            dist.all_reduce(loss)
-        if ev is not None:
-            ev[2].record(stream)
-        ops.dflash_backward(x, y, scale, lzq, lzp, None, None, 0, out=grad)
-        if ev is not None:
-            ev[3].record(stream)
+        return loss, (scale, lzq, lzp)
 
-    for i in range(args.warmup):
-        step(i)
-    K = args.dflash_steps
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize(dev)
-    a.record(stream)
-    for k in range(K):
-        step(k, evs[k])
-    b.record(stream)
-    torch.cuda.synchronize(dev)
-    barrier()
-    ms = max_over_ranks(a.elapsed_time(b)) / K
-    fwd = max_over_ranks(statistics.mean(e[0].elapsed_time(e[1]) for e in evs))
-    bwd = max_over_ranks(statistics.mean(e[2].elapsed_time(e[3]) for e in evs))
+    def bwd(i, st):
+        x, y = sets[i & 1]
+        ops.dflash_backward(x, y, st[0], st[1], st[2], None, None, 0, out=grad)
+
+    K = args.dflash_steps if steps is None else steps
+    ms, f, g = time_pair(args, stream, world, max_over_ranks, barrier, fwd, bwd, K)
     live = 15.0 / 16.0
     peak, _ = hbm_peak()
-    bwd_bytes = 8.0 * E * live + 4.0 * E
-    fwd_bytes = 8.0 * E * live
+    bwd_bytes = 2.0 * esz * E * live + esz * E
+    fwd_bytes = 2.0 * esz * E * live
+    model = 5 * esz
     wl = f"{N}x{B}x{V}"
-    value = 20.0 * E * world / (ms * 1e-3) / 1e9
-    return {"metric": "DFlash-KL fwd+bwd logits GB/s (20*N*B*V bytes per GPU-step)",
+    tag = "_bf16" if esz == 2 else ""
+    value = model * E * world / (ms * 1e-3) / 1e9
+    del sets, grad
+    return {"metric": f"DFlash-KL fwd+bwd logits GB/s ({model}*N*B*V bytes per GPU-step)",
             "value": round(value, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
             "rows_per_s": round(N * B * world / (ms * 1e-3), 1),
             "pct_of_hbm_peak": round(100.0 * value / world / peak, 2),
-            "fwd_ms": round(fwd, 4), "bwd_ms": round(bwd, 4), "steps": K,
-            "config": {"workload": "dflash_kl_fwd_bwd_llama3_vocab", "N_per_gpu": N, "B": B, "V": V,
+            "fwd_ms": round(f, 4), "bwd_ms": round(g, 4), "steps": K,
+            "dtype": "bf16" if esz == 2 else "f32",
+            "config": {"workload": f"dflash_kl_fwd_bwd_llama3_vocab{tag}", "N_per_gpu": N, "B": B, "V": V,
                        "draft": "N(0, 2^2)", "verifier": "draft + N(0, 1)", "gamma": 4.0,
-                       "sample_from_anchor": False, "mask": "all ones"},
-            "roofline": {"kernel": "dflash_bwd_ring_kernel<KL>", "bound": "hbm",
-                         "achieved": round(bwd_bytes / (bwd * 1e-3) / 1e9, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(bwd_bytes / (bwd * 1e-3) / 1e9 / peak, 4),
-                         "traffic": profiled_traffic("dflash_bwd_kl", wl), "bytes_per_launch": bwd_bytes},
-            "fwd_roofline": {"kernel": "dflash_fwd_ring_kernel<KL> + finalize",
-                             "achieved": round(fwd_bytes / (fwd * 1e-3) / 1e9, 1),
-                             "frac": round(fwd_bytes / (fwd * 1e-3) / 1e9 / peak, 4),
-                             "traffic": profiled_traffic("dflash_fwd_kl", wl), "bytes_per_launch": fwd_bytes}}
+                       "sample_from_anchor": False, "mask": "all ones",
+                       "logits": "bf16 (fp32 arithmetic)" if esz == 2 else "fp32"},
+            "roofline": {"kernel": f"dflash_bwd_ring_kernel<{'bf16' if esz == 2 else 'f32'}, KL>", "bound": "hbm",
+                         "achieved": round(bwd_bytes / (g * 1e-3) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(bwd_bytes / (g * 1e-3) / 1e9 / peak, 4),
+                         "traffic": profiled_traffic(f"dflash_bwd_kl{tag}", wl), "bytes_per_launch": bwd_bytes},
+            "fwd_roofline": {"kernel": f"dflash_fwd_ring_kernel<{'bf16' if esz == 2 else 'f32'}, KL> + finalize",
+                             "achieved": round(fwd_bytes / (f * 1e-3) / 1e9, 1),
+                             "frac": round(fwd_bytes / (f * 1e-3) / 1e9 / peak, 4),
+                             "traffic": profiled_traffic(f"dflash_fwd_kl{tag}", wl), "bytes_per_launch": fwd_bytes}}
+
+
+def time_dpace_bf16(args, dev, stream, world, n_global, max_over_ranks, barrier):
+    """D-PACE on bf16 logits, the headline workload otherwise: [64, 16, 128256]
+    ~ N(0, 2^2) rounded to bf16, prefix mask k ~ U{0..4}, alpha 0.5. Bytes model
+    6 * N*B*V per step (2-byte elements: forward read, backward read + write);
+    required bytes skip the unscored rows."""
+    from specdec import ops
+
+    N, B, V = args.n, 16, 128256
+    E = N * B * V
+    sets = []
+    for s_ in range(2):
+        x, t, m = dpace_inputs(N, B, V, 2.0, 4, 1000 * s_ + int(os.environ.get("RANK", "0")), dev)
+        sets.append((x.to(torch.bfloat16), t, m))
+        del x
+    live = statistics.mean(float(m.mean()) for _, _, m in sets)
+    grad = torch.empty(N, B, V, device=dev, dtype=torch.bfloat16)
+
+    def fwd(i):
+        x, t, m = sets[i & 1]
+        loss, lse, scale, _ = ops.dpace_forward(x, t, m, 0.5, 0, n_global=n_global, validate=False)
+        return loss, (lse, scale)
+
+    def bwd(i, st):
+        x, t, _ = sets[i & 1]
+        ops.dpace_backward(x, t, st[0], st[1], None, out=grad)
+
+    K = args.bf16_steps
+    ms, f, g = time_pair(args, stream, world, max_over_ranks, barrier, fwd, bwd, K)
+    peak, _ = hbm_peak()
+    bwd_bytes = 2.0 * E * live + 2.0 * E
+    fwd_bytes = 2.0 * E * live
+    wl = f"{N}x{B}x{V}"
+    value = 6.0 * E * world / (ms * 1e-3) / 1e9
+    del sets, grad
+    return {"metric": "D-PACE fwd+bwd bf16 logits GB/s (6*N*B*V bytes per GPU-step)",
+            "value": round(value, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
+            "rows_per_s": round(N * B * world / (ms * 1e-3), 1),
+            "pct_of_hbm_peak": round(100.0 * value / world / peak, 2),
+            "fwd_ms": round(f, 4), "bwd_ms": round(g, 4), "steps": K, "dtype": "bf16",
+            "config": {"workload": "dpace_fwd_bwd_llama3_vocab_bf16", "N_per_gpu": N, "B": B, "V": V,
+                       "sigma": 2.0, "mask": "prefix k~U{0..4}", "alpha": 0.5, "loss_type": "dpace",
+                       "logits": "bf16 (fp32 arithmetic)"},
+            "roofline": {"kernel": "dpace_bwd_ring_kernel<bf16>", "bound": "hbm",
+                         "achieved": round(bwd_bytes / (g * 1e-3) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(bwd_bytes / (g * 1e-3) / 1e9 / peak, 4),
+                         "traffic": profiled_traffic("dpace_bwd_bf16", wl), "bytes_per_launch": bwd_bytes},
+            "fwd_roofline": {"kernel": "dpace_fwd_ring_kernel<bf16> + finalize",
+                             "achieved": round(fwd_bytes / (f * 1e-3) / 1e9, 1),
+                             "frac": round(fwd_bytes / (f * 1e-3) / 1e9 / peak, 4),
+                             "traffic": profiled_traffic("dpace_fwd_bf16", wl), "bytes_per_launch": fwd_bytes}}
+
+
+def torch_ops_dpace_loss(logits, targets, alpha, mask):
+    """D-PACE written with plain torch ops on the GPU (cross_entropy, exp,
+    cumprod, reversed cumsum), the unfused way a user without this library
+    would run the objective; used only as the end-to-end comparison."""
+    N, B, V = logits.shape
+    ce = torch.nn.functional.cross_entropy(logits.reshape(-1, V).float(), targets.reshape(-1),
+                                           reduction="none").view(N, B)
+    with torch.no_grad():
+        live = (mask > 0).float()
+        sm = torch.where(live > 0, (1 - alpha) * torch.exp(-ce) + alpha, torch.ones_like(ce))
+        P = torch.cumprod(sm, dim=1)
+        w = torch.flip(torch.cumsum(torch.flip(P * live, [1]), 1), [1]) * live
+    return (ce * w).sum() / N
+
+
+def time_drafter_step(args, dev, world, max_over_ranks, barrier):
+    """End-to-end drafter training step around the loss hook: the DFlash
+    drafter (d_target 4096, d_model 256, 3 layers, 4 heads, block 16) over
+    target features [32, 512, 4096] with a frozen random lm_head [128256, 4096],
+    D-PACE alpha 0.5 with the anchor slot masked out, AdamW + grad-norm clip
+    as the reference pipeline's step; DDP across ranks when world > 1.
+    Variants: the fused loss on fp32 logits, the same objective in plain torch
+    ops on fp32 logits, and a bf16 lm_head feeding the fused bf16-logits loss.
+    GEMMs run on cuBLAS (TF32 for fp32 operands)."""
+    import torch.nn as nn
+
+    from losses import dpace_loss
+    from models.dflash.model import DFlashSpeculator
+
+    Nb, S, D, V, blk = 32, 512, 4096, 128256, 16
+    prev_tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    torch.manual_seed(1234)
+    head = nn.Linear(D, V, bias=False).to(dev)
+    head_bf16 = nn.Linear(D, V, bias=False, dtype=torch.bfloat16).to(dev)
+    with torch.no_grad():
+        head_bf16.weight.copy_(head.weight)
+    g = torch.Generator(device=dev).manual_seed(99 + int(os.environ.get("RANK", "0")))
+    feats = torch.randn(Nb, S, D, device=dev, generator=g, dtype=torch.bfloat16).float()
+    tokens = torch.randint(0, V, (Nb, blk), device=dev, generator=g)
+    mask = torch.ones(Nb, blk, device=dev)
+    mask[:, 0] = 0.0
+
+    def build(lm_head):
+        m = DFlashSpeculator(d_target=D, d_model=256, target_vocab_size=V, block_size=blk, num_layers=3,
+                             num_heads=4, target_lm_head=lm_head).to(dev)
+        if lm_head.weight.dtype == torch.bfloat16:
+            # the drafter body stays fp32; its output feature enters the bf16 head in bf16
+            m.final_norm.register_forward_hook(lambda _m, _i, out: out.to(torch.bfloat16))
+        if world > 1:
+            m = nn.parallel.DistributedDataParallel(m, device_ids=[dev.index])
+        return m
+
+    def loss_fused(logits, tok):
+        return dpace_loss(logits, tok, 0.5, position_mask=mask)
+
+    def loss_torch(logits, tok):
+        return torch_ops_dpace_loss(logits, tok, 0.5, mask)
+
+    variants = [("fused_loss_fp32_logits", head, loss_fused), ("torch_ops_loss_fp32_logits", head, loss_torch),
+                ("fused_loss_bf16_logits", head_bf16, loss_fused)]
+    out = {}
+    stream = torch.cuda.current_stream(dev)
+    for name, lm_head, lfn in variants:
+        model = build(lm_head)
+        core = model.module if world > 1 else model
+        params = [p for p in model.parameters() if p.requires_grad]
+        opt = torch.optim.AdamW(params, lr=1e-3)
+
+        def step():
+            opt.zero_grad(set_to_none=True)
+            loss = core.compute_loss(feats, tokens, loss_fn=lfn) if world == 1 else \
+                lfn(model(feats), tokens)
+            loss.backward()
+            torch.nn.utils.clip_grad_norm_(params, 1.0)
+            opt.step()
+            return loss
+
+        for _ in range(3):
+            step()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize(dev)
+        a.record(stream)
+        for _ in range(args.drafter_steps):
+            loss = step()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        ms = max_over_ranks(a.elapsed_time(b)) / args.drafter_steps
+        out[name] = {"ms_per_step": round(ms, 3), "rows_per_s": round(Nb * blk * world / (ms * 1e-3), 1),
+                     "loss": round(float(loss.detach()), 6)}
+        del model, core, opt, params
+    torch.backends.cuda.matmul.allow_tf32 = prev_tf32
+    del head, head_bf16, feats
+    torch.cuda.empty_cache()
+    base = out["torch_ops_loss_fp32_logits"]["ms_per_step"]
+    for v in out.values():
+        v["speedup_vs_torch_ops_loss"] = round(base / v["ms_per_step"], 3)
+    return {"metric": "drafter training step (fwd + loss + bwd + AdamW) rows/s",
+            "steps": args.drafter_steps,
+            "config": {"workload": "dflash_drafter_step", "features": [Nb, S, D], "d_model": 256, "layers": 3,
+                       "heads": 4, "block_size": blk, "V": V, "lm_head": "frozen, random",
+                       "objective": "dpace alpha 0.5, anchor slot masked", "optimizer": "AdamW lr 1e-3, clip 1.0",
+                       "gemms": "cuBLAS, TF32 for fp32", "parallelism": f"ddp{world}"},
+            "variants": out}
 
 
 def run_ours(args):
@@ -292,8 +485,12 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     if world > 1:
+        # high-priority NCCL stream: the loss all_reduce is dispatched ahead of
+        # the backward's CTAs and overlaps it
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.is_high_priority_stream = True
         dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
-                                timeout=timedelta(seconds=120))
+                                timeout=timedelta(seconds=120), pg_options=opts)
 
     def barrier():
         if world > 1:
@@ -316,6 +513,8 @@ def run_ours(args):
     # ring kernels (16-byte-aligned inputs): forward = streaming + finalize, backward = 1
     launches_per_step = 3 if all(x.data_ptr() % 16 == 0 for x, _, _ in sets) else 2
 
+    reducer = LossReducer(dev) if world > 1 else None
+
     def step(i, ev=None):
         x, t, m = sets[i & 1]
         if ev is not None:
@@ -323,13 +522,15 @@ def run_ours(args):
         loss, lse, scale, _ = ops.dpace_forward(x, t, m, 0.5, 0, n_global=n_global, validate=False)
         if ev is not None:
             ev[1].record(stream)
-        if world > 1:
-            dist.all_reduce(loss)
+        if reducer is not None:
+            loss = reducer.start(loss)  # global loss, reduced beside the backward
         if ev is not None:
             ev[2].record(stream)
         ops.dpace_backward(x, t, lse, scale, None, out=grad)
         if ev is not None:
             ev[3].record(stream)
+        if reducer is not None:
+            reducer.wait()
         return loss
 
     for i in range(args.warmup):
@@ -364,6 +565,14 @@ def run_ours(args):
     dflash = None
     if args.dflash_steps > 0:
         dflash = time_dflash(args, dev, stream, world, n_global, max_over_ranks, barrier)
+    drafter = None
+    if args.drafter_steps > 0:
+        drafter = time_drafter_step(args, dev, world, max_over_ranks, barrier)
+    bf16 = None
+    if args.bf16_steps > 0:
+        bf16 = {"dpace": time_dpace_bf16(args, dev, stream, world, n_global, max_over_ranks, barrier),
+                "dflash_kl": time_dflash(args, dev, stream, world, n_global, max_over_ranks, barrier,
+                                         dtype=torch.bfloat16, steps=args.bf16_steps)}
     ms_step = ms / args.steps
     total_bytes = 12.0 * E * world
     value = total_bytes / (ms_step * 1e-3) / 1e9
@@ -445,6 +654,8 @@ def run_ours(args):
                         "launches_per_step": launches_per_step,
                         "fwd_note": "forward = streaming kernel + PDL-chained finalize kernel"},
             "dflash_kl": dflash,
+            "bf16": bf16,
+            "drafter_step": drafter,
             "live_row_fraction": round(live_frac, 4),
             "cpu_baseline": cpu_base, "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps, "gpu_launches_scope": "per rank",
@@ -464,6 +675,10 @@ def main(argv=None):
     p.add_argument("--e2e-steps", type=int, default=20)
     p.add_argument("--dflash-steps", type=int, default=100,
                    help="timed steps of the DFlash-KL workload (0 = skip)")
+    p.add_argument("--bf16-steps", type=int, default=100,
+                   help="timed steps of each bf16-logits workload (0 = skip)")
+    p.add_argument("--drafter-steps", type=int, default=10,
+                   help="timed end-to-end drafter training steps per variant (0 = skip)")
     p.add_argument("--cpu-budget", type=float, default=10.0,
                    help="seconds of CPU-oracle timing on rank 0 at N=1 (0 = skip)")
     args = p.parse_args(argv)

@@ -161,5 +161,76 @@ __device__ __forceinline__ void df_group(DfState& s, const float4 (&a)[U], const
   }
 }
 
+// bf16 vectors: lane element k of vector u is row index base_idx +
+// u * stride_idx + k (k = 0..7, the low half of word k/2 first). Maxima are
+// taken on the packed words; each element is widened once.
+template <int KIND, int U>
+__device__ __forceinline__ void df_group(DfState& s, const uint4 (&a)[U], const uint4 (&b)[U], int base_idx,
+                                         int stride_idx) {
+  uint32_t pa = bmax8(a[0]);
+#pragma unroll
+  for (int u = 1; u < U; ++u) pa = bmax2(pa, bmax8(a[u]));
+  const float cma = fmaxf(bf16_lo(pa), bf16_hi(pa));
+  if (cma > s.mq) {
+    s.sq *= exp_shift(s.mq, cma);
+    s.mq = cma;
+  }
+  const float mq = s.mq;
+  float accq = 0.f;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    accq += ((exp_shift(bf16_lo(a[u].x), mq) + exp_shift(bf16_hi(a[u].x), mq)) +
+             (exp_shift(bf16_lo(a[u].y), mq) + exp_shift(bf16_hi(a[u].y), mq))) +
+            ((exp_shift(bf16_lo(a[u].z), mq) + exp_shift(bf16_hi(a[u].z), mq)) +
+             (exp_shift(bf16_lo(a[u].w), mq) + exp_shift(bf16_hi(a[u].w), mq)));
+  }
+  s.sq += accq;
+  uint32_t pb = bmax8(b[0]);
+#pragma unroll
+  for (int u = 1; u < U; ++u) pb = bmax2(pb, bmax8(b[u]));
+  const float cmb = fmaxf(bf16_lo(pb), bf16_hi(pb));
+  if (KIND == kKindKL) {
+    if (cmb > s.mp) {
+      const float f = exp_shift(s.mp, cmb);
+      s.sp *= f;
+      s.t *= f;
+      s.mp = cmb;
+    }
+    const float mp = s.mp;
+    float accp = 0.f, acct = 0.f;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t wa[4] = {a[u].x, a[u].y, a[u].z, a[u].w};
+      const uint32_t wb[4] = {b[u].x, b[u].y, b[u].z, b[u].w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float xl0 = bf16_lo(wa[h]), xl1 = bf16_hi(wa[h]);
+        const float xt0 = bf16_lo(wb[h]), xt1 = bf16_hi(wb[h]);
+        const float e0 = exp_shift(xt0, mp), e1 = exp_shift(xt1, mp);
+        accp += e0 + e1;
+        acct = fmaf(e0, xt0 - xl0, acct);
+        acct = fmaf(e1, xt1 - xl1, acct);
+      }
+    }
+    s.sp += accp;
+    s.t += acct;
+  } else {
+    if (cmb > s.bx) {
+      // first element of the group equal to its max, in index order
+#pragma unroll
+      for (int u = U - 1; u >= 0; --u) {
+        const int k = base_idx + u * stride_idx;
+        const uint32_t wa[4] = {a[u].x, a[u].y, a[u].z, a[u].w};
+        const uint32_t wb[4] = {b[u].x, b[u].y, b[u].z, b[u].w};
+#pragma unroll
+        for (int h = 3; h >= 0; --h) {
+          if (bf16_hi(wb[h]) == cmb) { s.bi = k + 2 * h + 1; s.bl = bf16_hi(wa[h]); }
+          if (bf16_lo(wb[h]) == cmb) { s.bi = k + 2 * h; s.bl = bf16_lo(wa[h]); }
+        }
+      }
+      s.bx = cmb;
+    }
+  }
+}
 
 }  // namespace specdec

@@ -125,7 +125,7 @@ __device__ void df_finalize_row(const DflashFwdArgs& a, int64_t r, int* sh_last)
       float bl = s.bl;
       if (bi == INT_MAX) {  // no finite maximum (all -inf): argmax is index 0
         bi = 0;
-        bl = a.logits[r * a.V];
+        bl = static_cast<const float*>(a.logits)[r * a.V];
       }
       tgt = bi;
       el = lzq - bl;
@@ -167,7 +167,8 @@ __global__ void __launch_bounds__(NT) dflash_fwd_kernel(const __grid_constant__ 
     if (live) {
       DfState s;
       df_init(s);
-      df_stream<KIND, NT, U>(s, a.logits + row0, a.target_logits + row0, lo, hi);
+      df_stream<KIND, NT, U>(s, static_cast<const float*>(a.logits) + row0,
+                             static_cast<const float*>(a.target_logits) + row0, lo, hi);
       df_warp_merge<KIND>(s);
       if (lane == 0) sh_red[w] = s;
       __syncthreads();
@@ -223,9 +224,9 @@ __global__ void __launch_bounds__(NT) dflash_bwd_kernel(const __grid_constant__ 
     e = row0 + hi;
     const int64_t n = hi - lo;
     const float sc = __fmul_rn(a.scale[r], g);
-    const float* pl = a.logits + row0 + lo;
-    const float* px = a.target_logits + row0 + lo;
-    float* dst = a.dlogits + row0 + lo;
+    const float* pl = static_cast<const float*>(a.logits) + row0 + lo;
+    const float* px = static_cast<const float*>(a.target_logits) + row0 + lo;
+    float* dst = static_cast<float*>(a.dlogits) + row0 + lo;
     const uintptr_t al = reinterpret_cast<uintptr_t>(pl), ad = reinterpret_cast<uintptr_t>(dst);
     const uintptr_t ax = KIND == kKindKL ? reinterpret_cast<uintptr_t>(px) : al;
     const bool vec = (((al ^ ad) | (al ^ ax)) & 15) == 0;

@@ -21,9 +21,14 @@
 // the verifier) and writes s * (softmax(draft) - softmax(verifier) | onehot).
 // Rows whose weight mask * decay is 0 are never copied.
 //
+// Element type T: float, or bf16_t (bfloat16 bit patterns) for both streams
+// and the gradient; elements are widened exactly to float, the bf16 gradient
+// is rounded to nearest even.
+//
 // Reference behaviour: models/dflash/loss.py:31-126 (forward), :128-166
 // (backward); numbers follow models/dflash/tests/test_loss.py:21-49.
 #include <climits>
+#include <type_traits>
 
 #include "dflash_common.cuh"
 #include "ring.cuh"
@@ -43,16 +48,19 @@ __device__ __forceinline__ float dr_numer(const DflashFwdArgs& a, int64_t r) {
   return __fmul_rn(a.mask ? a.mask[r] : 1.f, decay);
 }
 
-template <int KIND, int NC, int S, int SE, int BS>
-__global__ void __launch_bounds__((NC + 1) * 32, 1) dflash_fwd_ring_kernel(const __grid_constant__ DflashFwdArgs a) {
+template <class T, int KIND, int NC, int S, int SE, int BS>
+__global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<2, S, SE, T>())) dflash_fwd_ring_kernel(const __grid_constant__ DflashFwdArgs a) {
+  constexpr int kVec = 16 / sizeof(T);  // elements per 16-byte vector
   constexpr int kSub = SE / NC;
-  constexpr int U = kSub / 128;  // float4 per lane per stream in a full sub-range
+  constexpr int U = kSub / (32 * kVec);  // 16-byte vectors per lane per stream in a full sub-range
   constexpr int64_t BL = (int64_t)BS * SE;
   constexpr int kLogBL = __builtin_ctzll(BL);
-  static_assert(kSub % 128 == 0, "sub-range must be whole float4 rounds of a warp");
+  static_assert(kSub % (32 * kVec) == 0, "sub-range must be whole 16-byte rounds of a warp");
   static_assert((BL & (BL - 1)) == 0, "block length must be a power of two");
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  auto& sm = *reinterpret_cast<RingSmem<2, S, SE>*>(smem_raw);
+  auto& sm = *reinterpret_cast<RingSmem<2, S, SE, T>*>(smem_raw);
+  const T* XL = static_cast<const T*>(a.logits);
+  const T* XT = static_cast<const T*>(a.target_logits);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t E = a.pt.E, V = a.pt.V, R = E / V;
   const int pmax = a.pt.pmax;
@@ -69,7 +77,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dflash_fwd_ring_kernel(const
 
   if (warp == NC) {  // producer
     if (lane == 0) {
-      const float* src[2] = {a.logits, a.target_logits};
+      const T* src[2] = {XL, XT};
       if (!ring_produce<2, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow))
         atomicOr(a.flag, 2);
     }
@@ -77,8 +85,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dflash_fwd_ring_kernel(const
     return;
   }
 
-  const float* ringl = sm.ring;
-  const float* ringt = sm.ring + (size_t)S * SE;
+  const T* ringl = sm.ring;
+  const T* ringt = sm.ring + (size_t)S * SE;
   DfState st;
   df_init(st);
   int64_t r = 0, blk = -1;
@@ -115,21 +123,22 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dflash_fwd_ring_kernel(const
       r = sm.srow[slot];
       enter_row(r);
     }
-    const float* sl = ringl + (size_t)slot * SE;
-    const float* sx = ringt + (size_t)slot * SE;
+    const T* sl = ringl + (size_t)slot * SE;
+    const T* sx = ringt + (size_t)slot * SE;
     if (f1 - f0 == SE && (r + 1) * V >= f1) {
       // fast path: a full stage inside one row
       if (live) {
-        const float4* ql = reinterpret_cast<const float4*>(sl + warp * kSub) + lane;
-        const float4* qx = reinterpret_cast<const float4*>(sx + warp * kSub) + lane;
-        float4 va[U], vb[U];
+        using Vec = typename std::conditional<sizeof(T) == 4, float4, uint4>::type;
+        const Vec* ql = reinterpret_cast<const Vec*>(sl + warp * kSub) + lane;
+        const Vec* qx = reinterpret_cast<const Vec*>(sx + warp * kSub) + lane;
+        Vec va[U], vb[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
           va[u] = ql[32 * u];
           vb[u] = qx[32 * u];
         }
-        const int base = (int)(f0 - r * V) + warp * kSub + 4 * lane;
-        df_group<KIND, U>(st, va, vb, base, 128);
+        const int base = (int)(f0 - r * V) + warp * kSub + kVec * lane;
+        df_group<KIND, U>(st, va, vb, base, 32 * kVec);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(sm.empty + slot);
@@ -142,7 +151,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dflash_fwd_ring_kernel(const
       }
       continue;
     }
-    const int64_t fv = f0 + ((((f1 - f0) * 4) & ~int64_t(15)) >> 2);  // end of the copied part
+    const int64_t fv = copied_end<T>(f0, f1);  // end of the copied part
     const int64_t w0 = f0 + (int64_t)warp * kSub, w1 = min(w0 + kSub, f1);
     int64_t f = f0;
     while (f < f1) {
@@ -151,8 +160,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dflash_fwd_ring_kernel(const
       if (live) {
         const int64_t lo = max(f, w0), hi = min(g, w1);
         for (int64_t x = lo + lane; x < hi; x += 32) {
-          const float xl = x < fv ? sl[x - f0] : __ldg(a.logits + x);
-          const float xt = x < fv ? sx[x - f0] : __ldg(a.target_logits + x);
+          const float xl = x < fv ? to_f32(sl[x - f0]) : ldg_f32(XL + x);
+          const float xt = x < fv ? to_f32(sx[x - f0]) : ldg_f32(XT + x);
           df_push<KIND>(st, xl, xt, (int)(x - r * V));
         }
       }
@@ -170,66 +179,71 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dflash_fwd_ring_kernel(const
   pdl_trigger();
 }
 
-// One CTA per sequence n, warp j <-> row j.
-template <int KIND>
+// One CTA per sequence n with min(B, 32) warps; warp w finalizes rows
+// j = w, w + 32, ... of the sequence (for B <= 32: warp j <-> row j).
+template <class T, int KIND>
 __global__ void __launch_bounds__(1024) dflash_finalize_kernel(const __grid_constant__ DflashFwdArgs a) {
   __shared__ float sh_loss[32];
   pdl_wait();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   const int B = a.B;
   const int64_t n = blockIdx.x, V = a.pt.V, BL = a.pt.chunk;
   const int NC = a.nc;
-  const int64_t r = n * B + warp;
   // denominator: sum of the sequence's raw mask values + 1e-5
   float mv = 0.f;
   for (int i = lane; i < B; i += 32) mv += a.mask ? a.mask[n * B + i] : 1.f;
   const float denom = warp_sum(mv) + 1e-5f;
-  const float numer = dr_numer(a, r);
-  const float w = __fdiv_rn(numer, denom);
-  float el = 0.f, lzq = 0.f, lzp = 0.f;
-  int64_t tgt = 0;
-  if (numer != 0.f) {
-    const int k = blocks_in_row(r, V, BL) * NC;
-    const DfPiece* part = a.part + r * a.pt.pmax * NC;
-    DfState s;
-    df_init(s);
-    for (int qd = lane; qd < k; qd += 32) {  // slot-major, warp-minor: fixed order
-      const float4 lo4 = reinterpret_cast<const float4*>(part + qd)[0];
-      const float4 hi4 = reinterpret_cast<const float4*>(part + qd)[1];
-      DfState o;
-      o.mq = lo4.x; o.sq = lo4.y; o.mp = lo4.z; o.sp = lo4.w;
-      o.t = hi4.x; o.bx = hi4.y; o.bl = hi4.z; o.bi = __float_as_int(hi4.w);
-      df_merge<KIND>(s, o);
-    }
-    df_warp_merge<KIND>(s);
-    lzq = s.mq + logf(s.sq);
-    if (KIND == kKindKL) {
-      lzp = s.mp + logf(s.sp);
-      // KL = sum p (xt - xl) - logZp + logZq, the normaliser difference as one log of a ratio
-      el = s.t / s.sp + ((s.mq - s.mp) + logf(s.sq / s.sp));
-    } else {
-      int bi = s.bi;
-      float bl = s.bl;
-      if (bi == INT_MAX) {  // no finite maximum (all -inf): argmax is index 0
-        bi = 0;
-        bl = a.logits[r * V];
+  float acc = 0.f;  // this warp's rows, in row order
+  for (int j = warp; j < B; j += nwarps) {
+    const int64_t r = n * B + j;
+    const float numer = dr_numer(a, r);
+    const float w = __fdiv_rn(numer, denom);
+    float el = 0.f, lzq = 0.f, lzp = 0.f;
+    int64_t tgt = 0;
+    if (numer != 0.f) {
+      const int k = blocks_in_row(r, V, BL) * NC;
+      const DfPiece* part = a.part + r * a.pt.pmax * NC;
+      DfState s;
+      df_init(s);
+      for (int qd = lane; qd < k; qd += 32) {  // slot-major, warp-minor: fixed order
+        const float4 lo4 = reinterpret_cast<const float4*>(part + qd)[0];
+        const float4 hi4 = reinterpret_cast<const float4*>(part + qd)[1];
+        DfState o;
+        o.mq = lo4.x; o.sq = lo4.y; o.mp = lo4.z; o.sp = lo4.w;
+        o.t = hi4.x; o.bx = hi4.y; o.bl = hi4.z; o.bi = __float_as_int(hi4.w);
+        df_merge<KIND>(s, o);
       }
-      tgt = bi;
-      el = lzq - bl;
+      df_warp_merge<KIND>(s);
+      lzq = s.mq + logf(s.sq);
+      if (KIND == kKindKL) {
+        lzp = s.mp + logf(s.sp);
+        // KL = sum p (xt - xl) - logZp + logZq, the normaliser difference as one log of a ratio
+        el = s.t / s.sp + ((s.mq - s.mp) + logf(s.sq / s.sp));
+      } else {
+        int bi = s.bi;
+        float bl = s.bl;
+        if (bi == INT_MAX) {  // no finite maximum (all -inf): argmax is index 0
+          bi = 0;
+          bl = to_f32(static_cast<const T*>(a.logits)[r * V]);
+        }
+        tgt = bi;
+        el = lzq - bl;
+      }
     }
+    const float lr = numer != 0.f ? __fmul_rn(w, el) : 0.f;
+    if (lane == 0) {
+      if (a.loss_rows) a.loss_rows[r] = lr;
+      a.scale[r] = __fdiv_rn(w, (float)a.n_global);
+      a.logzq[r] = lzq;
+      a.logzp[r] = lzp;
+      if (a.target_id) a.target_id[r] = tgt;
+    }
+    acc += lr;
   }
-  const float lr = numer != 0.f ? __fmul_rn(w, el) : 0.f;
-  if (lane == 0) {
-    if (a.loss_rows) a.loss_rows[r] = lr;
-    a.scale[r] = __fdiv_rn(w, (float)a.n_global);
-    a.logzq[r] = lzq;
-    a.logzp[r] = lzp;
-    if (a.target_id) a.target_id[r] = tgt;
-    sh_loss[warp] = lr;
-  }
+  if (lane == 0) sh_loss[warp] = acc;
   __syncthreads();
   if (warp == 0) {
-    const float seq = warp_sum(lane < B ? sh_loss[lane] : 0.f);
+    const float seq = warp_sum(lane < nwarps ? sh_loss[lane] : 0.f);
     unsigned last = 0;
     if (lane == 0) {
       a.seq_loss[n] = seq;
@@ -248,16 +262,20 @@ __global__ void __launch_bounds__(1024) dflash_finalize_kernel(const __grid_cons
   }
 }
 
-template <int KIND, int NC, int S, int SE, int BS>
-__global__ void __launch_bounds__((NC + 1) * 32, 1) dflash_bwd_ring_kernel(const __grid_constant__ DflashBwdArgs a) {
+template <class T, int KIND, int NC, int S, int SE, int BS>
+__global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<(KIND == kKindKL ? 2 : 1), S, SE, T>())) dflash_bwd_ring_kernel(const __grid_constant__ DflashBwdArgs a) {
   constexpr int NIN = KIND == kKindKL ? 2 : 1;
+  constexpr int kVec = 16 / sizeof(T);
   constexpr int kSub = SE / NC;
   constexpr int64_t BL = (int64_t)BS * SE;
   constexpr int kLogBL = __builtin_ctzll(BL);
-  static_assert(kSub % 4 == 0, "sub-range must be whole float4s");
+  static_assert(kSub % kVec == 0, "sub-range must be whole 16-byte vectors");
   static_assert((BL & (BL - 1)) == 0, "block length must be a power of two");
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  auto& sm = *reinterpret_cast<RingSmem<NIN, S, SE>*>(smem_raw);
+  auto& sm = *reinterpret_cast<RingSmem<NIN, S, SE, T>*>(smem_raw);
+  const T* XL = static_cast<const T*>(a.logits);
+  const T* XT = static_cast<const T*>(a.target_logits);
+  T* dst = static_cast<T*>(a.dlogits);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t E = a.pt.E, V = a.pt.V, R = E / V;
   const float g = a.dloss ? __ldg(a.dloss) : 1.f;
@@ -274,7 +292,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dflash_bwd_ring_kernel(const
 
   if (warp == NC) {
     if (lane == 0) {
-      const float* src[2] = {a.logits, a.target_logits};
+      const T* src[2] = {XL, XT};
       if (!ring_produce<NIN, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow) &&
           a.flag)
         atomicOr(a.flag, 2);
@@ -282,8 +300,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dflash_bwd_ring_kernel(const
     return;
   }
 
-  const float* ringl = sm.ring;
-  const float* ringt = sm.ring + (size_t)S * SE;  // KL only
+  const T* ringl = sm.ring;
+  const T* ringt = sm.ring + (size_t)S * SE;  // KL only
   int64_t r = 0, blk = -1, tf = -1;
   float sc = 0.f, lq = 0.f, lp = 0.f;
   auto load_row = [&](int64_t row) {
@@ -309,10 +327,10 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dflash_bwd_ring_kernel(const
       r = sm.srow[slot];
       load_row(r);
     }
-    const int64_t fv = f0 + ((((f1 - f0) * 4) & ~int64_t(15)) >> 2);
+    const int64_t fv = copied_end<T>(f0, f1);
     const int64_t w0 = f0 + (int64_t)warp * kSub, w1 = min(w0 + kSub, f1);
-    const float* sl = ringl + (size_t)slot * SE;
-    const float* sx = ringt + (size_t)slot * SE;
+    const T* sl = ringl + (size_t)slot * SE;
+    const T* sx = ringt + (size_t)slot * SE;
     int64_t f = f0;
     while (f < f1) {
       const int64_t rend = (r + 1) * V;
@@ -320,33 +338,33 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dflash_bwd_ring_kernel(const
       const int64_t lo = max(f, w0), hi = min(ge, w1);
       if (lo < hi) {
         const bool zero = sc == 0.f || !rb.live(r);
-        const int64_t lo4 = (lo + 3) & ~int64_t(3), hi4 = min(hi, fv) & ~int64_t(3);
-        float* dst = a.dlogits;
+        const int64_t lov = (lo + kVec - 1) & ~int64_t(kVec - 1), hiv = min(hi, fv) & ~int64_t(kVec - 1);
         auto scalar = [&](int64_t x) {
           if (zero) {
-            dst[x] = 0.f;
+            store_elem(dst + x, 0.f);
           } else {
-            const float vl = x < fv ? sl[x - f0] : __ldg(a.logits + x);
+            const float vl = x < fv ? to_f32(sl[x - f0]) : ldg_f32(XL + x);
             const float qv = exp_shift(vl, lq);
             float pv;
-            if (KIND == kKindKL) pv = exp_shift(x < fv ? sx[x - f0] : __ldg(a.target_logits + x), lp);
+            if (KIND == kKindKL) pv = exp_shift(x < fv ? to_f32(sx[x - f0]) : ldg_f32(XT + x), lp);
             else pv = x == tf ? 1.f : 0.f;
-            dst[x] = sc * (qv - pv);
+            store_elem(dst + x, sc * (qv - pv));
           }
         };
-        if (lo4 < hi4) {
-          for (int64_t x = lo + lane; x < lo4; x += 32) scalar(x);
-          for (int64_t x = hi4 + lane; x < hi; x += 32) scalar(x);
-          float4* d4 = reinterpret_cast<float4*>(dst + lo4);
-          const float4* s4 = reinterpret_cast<const float4*>(sl + (lo4 - f0));
-          const float4* t4 = reinterpret_cast<const float4*>(sx + (lo4 - f0));
-          const int n4 = (int)((hi4 - lo4) >> 2);
+        if (lov < hiv) {
+          for (int64_t x = lo + lane; x < lov; x += 32) scalar(x);
+          for (int64_t x = hiv + lane; x < hi; x += 32) scalar(x);
+          const int nv = (int)((hiv - lov) / kVec);
           if (zero) {
-            const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int k = lane; k < n4; k += 32) st_stream(d4 + k, z);
-          } else {
-            const int64_t tq = tf - lo4;
-            for (int k = lane; k < n4; k += 32) {
+            const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+            uint4* d4 = reinterpret_cast<uint4*>(dst + lov);
+            for (int k = lane; k < nv; k += 32) st_stream_u4(d4 + k, z);
+          } else if constexpr (sizeof(T) == 4) {
+            float4* d4 = reinterpret_cast<float4*>(dst + lov);
+            const float4* s4 = reinterpret_cast<const float4*>(sl + (lov - f0));
+            const float4* t4 = reinterpret_cast<const float4*>(sx + (lov - f0));
+            const int64_t tq = tf - lov;
+            for (int k = lane; k < nv; k += 32) {
               const float4 v = s4[k];
               float4 y;
               y.x = exp_shift(v.x, lq);
@@ -374,6 +392,36 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dflash_bwd_ring_kernel(const
               y.w *= sc;
               st_stream(d4 + k, y);
             }
+          } else {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + lov);
+            const uint4* s4 = reinterpret_cast<const uint4*>(sl + (lov - f0));
+            const uint4* t4 = reinterpret_cast<const uint4*>(sx + (lov - f0));
+            const int64_t tq = tf - lov;
+            for (int k = lane; k < nv; k += 32) {
+              const uint4 v = s4[k];
+              const uint32_t wl[4] = {v.x, v.y, v.z, v.w};
+              float y[8];
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                y[2 * h] = exp_shift(bf16_lo(wl[h]), lq);
+                y[2 * h + 1] = exp_shift(bf16_hi(wl[h]), lq);
+              }
+              if (KIND == kKindKL) {
+                const uint4 u = t4[k];
+                const uint32_t wt[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                  y[2 * h] -= exp_shift(bf16_lo(wt[h]), lp);
+                  y[2 * h + 1] -= exp_shift(bf16_hi(wt[h]), lp);
+                }
+              } else {
+                const uint64_t d = (uint64_t)(tq - 8 * (int64_t)k);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) y[e] -= d == (uint64_t)e ? 1.f : 0.f;
+              }
+              st_stream_u4(d4 + k, make_uint4(pack_bf16x2(sc * y[0], sc * y[1]), pack_bf16x2(sc * y[2], sc * y[3]),
+                                              pack_bf16x2(sc * y[4], sc * y[5]), pack_bf16x2(sc * y[6], sc * y[7])));
+            }
           }
         } else {
           for (int64_t x = lo + lane; x < hi; x += 32) scalar(x);
@@ -390,102 +438,123 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dflash_bwd_ring_kernel(const
   }
 }
 
-template <int NC, int S, int SE, int BS>
+template <class T, int NC, int S, int SE, int BS>
 struct DfRing {
   template <int KIND>
-  static constexpr size_t fsmem() { return sizeof(RingSmem<2, S, SE>); }
+  static constexpr size_t fsmem() { return sizeof(RingSmem<2, S, SE, T>); }
   template <int KIND>
-  static constexpr size_t bsmem() { return sizeof(RingSmem<KIND == kKindKL ? 2 : 1, S, SE>); }
+  static constexpr size_t bsmem() { return sizeof(RingSmem<KIND == kKindKL ? 2 : 1, S, SE, T>); }
   template <int KIND>
   static int fwd_ctas(int device, int cap) {
-    return ring_occupancy_ctas(dflash_fwd_ring_kernel<KIND, NC, S, SE, BS>, (NC + 1) * 32, fsmem<KIND>(), device,
-                               cap);
+    return ring_occupancy_ctas(dflash_fwd_ring_kernel<T, KIND, NC, S, SE, BS>, (NC + 1) * 32, fsmem<KIND>(),
+                               device, cap);
   }
   template <int KIND>
   static int bwd_ctas(int device, int cap) {
-    return ring_occupancy_ctas(dflash_bwd_ring_kernel<KIND, NC, S, SE, BS>, (NC + 1) * 32, bsmem<KIND>(), device,
-                               cap);
+    return ring_occupancy_ctas(dflash_bwd_ring_kernel<T, KIND, NC, S, SE, BS>, (NC + 1) * 32, bsmem<KIND>(),
+                               device, cap);
   }
   template <int KIND>
   static cudaError_t fwd(DflashFwdArgs a, int ctas, cudaStream_t st) {
-    cudaFuncSetAttribute(dflash_fwd_ring_kernel<KIND, NC, S, SE, BS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)fsmem<KIND>());
+    cudaFuncSetAttribute(dflash_fwd_ring_kernel<T, KIND, NC, S, SE, BS>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsmem<KIND>());
     a.nc = NC;
-    dflash_fwd_ring_kernel<KIND, NC, S, SE, BS><<<ctas, (NC + 1) * 32, fsmem<KIND>(), st>>>(a);
+    dflash_fwd_ring_kernel<T, KIND, NC, S, SE, BS><<<ctas, (NC + 1) * 32, fsmem<KIND>(), st>>>(a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    return launch_pdl(dflash_finalize_kernel<KIND>, dim3((unsigned)a.N), dim3(32 * a.B), st, a);
+    return launch_pdl(dflash_finalize_kernel<T, KIND>, dim3((unsigned)a.N), dim3(32 * (a.B < 32 ? a.B : 32)), st,
+                      a);
   }
   template <int KIND>
   static cudaError_t bwd(const DflashBwdArgs& a, int ctas, cudaStream_t st) {
-    cudaFuncSetAttribute(dflash_bwd_ring_kernel<KIND, NC, S, SE, BS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)bsmem<KIND>());
-    dflash_bwd_ring_kernel<KIND, NC, S, SE, BS><<<ctas, (NC + 1) * 32, bsmem<KIND>(), st>>>(a);
+    cudaFuncSetAttribute(dflash_bwd_ring_kernel<T, KIND, NC, S, SE, BS>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bsmem<KIND>());
+    dflash_bwd_ring_kernel<T, KIND, NC, S, SE, BS><<<ctas, (NC + 1) * 32, bsmem<KIND>(), st>>>(a);
     return cudaGetLastError();
   }
 };
 
-// Ring shapes (consumer warps x stages x stage floats per stream x stages per
-// block); the forward ring holds both streams:
+// Ring shapes (consumer warps x stages x stage elements per stream x stages
+// per block), float elements; the forward ring holds both streams:
 // 0 = 4 x 4 x 2048 x 8 (64 KB ring, 64 KB blocks per stream, 3 CTAs/SM);
 // 1 = 4 x 4 x 4096 x 4 (128 KB ring, 1 CTA/SM); 2 = 4 x 6 x 2048 x 8 (96 KB
 // ring, 2 CTAs/SM); 3 = 2 x 4 x 2048 x 8 (64 KB ring, 3 CTAs/SM);
-// 4 = 8 x 3 x 4096 x 4 (96 KB ring, 2 CTAs/SM).
-using D0 = DfRing<4, 4, 2048, 8>;
-using D1 = DfRing<4, 4, 4096, 4>;
-using D2 = DfRing<4, 6, 2048, 8>;
-using D3 = DfRing<2, 4, 2048, 8>;
-using D4 = DfRing<8, 3, 4096, 4>;
+// 4 = 8 x 3 x 4096 x 4 (96 KB ring, 2 CTAs/SM). bf16 shapes have the same
+// bytes (twice the elements).
+template <class T>
+struct DfShapes {
+  static constexpr int k = 4 / sizeof(T);
+  using D0 = DfRing<T, 4, 4, 2048 * k, 8>;
+  using D1 = DfRing<T, 4, 4, 4096 * k, 4>;
+  using D2 = DfRing<T, 4, 6, 2048 * k, 8>;
+  using D3 = DfRing<T, 2, 4, 2048 * k, 8>;
+  using D4 = DfRing<T, 8, 3, 4096 * k, 4>;
 
-template <int KIND>
-int fwd_ctas_k(int shape, int device, int cap) {
-  switch (shape) {
-    case 1: return D1::fwd_ctas<KIND>(device, cap);
-    case 2: return D2::fwd_ctas<KIND>(device, cap);
-    case 3: return D3::fwd_ctas<KIND>(device, cap);
-    case 4: return D4::fwd_ctas<KIND>(device, cap);
-    default: return D0::fwd_ctas<KIND>(device, cap);
+  static int block_elems(int shape) {
+    switch (shape) {
+      case 1: return 4096 * 4 * k;
+      case 4: return 4096 * 4 * k;
+      default: return 2048 * 8 * k;
+    }
   }
-}
-template <int KIND>
-int bwd_ctas_k(int shape, int device, int cap) {
-  switch (shape) {
-    case 1: return D1::bwd_ctas<KIND>(device, cap);
-    case 2: return D2::bwd_ctas<KIND>(device, cap);
-    case 3: return D3::bwd_ctas<KIND>(device, cap);
-    case 4: return D4::bwd_ctas<KIND>(device, cap);
-    default: return D0::bwd_ctas<KIND>(device, cap);
+  template <int KIND>
+  static int fwd_ctas(int shape, int device, int cap) {
+    switch (shape) {
+      case 1: return D1::template fwd_ctas<KIND>(device, cap);
+      case 2: return D2::template fwd_ctas<KIND>(device, cap);
+      case 3: return D3::template fwd_ctas<KIND>(device, cap);
+      case 4: return D4::template fwd_ctas<KIND>(device, cap);
+      default: return D0::template fwd_ctas<KIND>(device, cap);
+    }
   }
-}
-template <int KIND>
-cudaError_t fwd_launch_k(int shape, const DflashFwdArgs& a, int ctas, cudaStream_t st) {
-  switch (shape) {
-    case 1: return D1::fwd<KIND>(a, ctas, st);
-    case 2: return D2::fwd<KIND>(a, ctas, st);
-    case 3: return D3::fwd<KIND>(a, ctas, st);
-    case 4: return D4::fwd<KIND>(a, ctas, st);
-    default: return D0::fwd<KIND>(a, ctas, st);
+  template <int KIND>
+  static int bwd_ctas(int shape, int device, int cap) {
+    switch (shape) {
+      case 1: return D1::template bwd_ctas<KIND>(device, cap);
+      case 2: return D2::template bwd_ctas<KIND>(device, cap);
+      case 3: return D3::template bwd_ctas<KIND>(device, cap);
+      case 4: return D4::template bwd_ctas<KIND>(device, cap);
+      default: return D0::template bwd_ctas<KIND>(device, cap);
+    }
   }
-}
-template <int KIND>
-cudaError_t bwd_launch_k(int shape, const DflashBwdArgs& a, int ctas, cudaStream_t st) {
-  switch (shape) {
-    case 1: return D1::bwd<KIND>(a, ctas, st);
-    case 2: return D2::bwd<KIND>(a, ctas, st);
-    case 3: return D3::bwd<KIND>(a, ctas, st);
-    case 4: return D4::bwd<KIND>(a, ctas, st);
-    default: return D0::bwd<KIND>(a, ctas, st);
+  template <int KIND>
+  static cudaError_t fwd(int shape, const DflashFwdArgs& a, int ctas, cudaStream_t st) {
+    switch (shape) {
+      case 1: return D1::template fwd<KIND>(a, ctas, st);
+      case 2: return D2::template fwd<KIND>(a, ctas, st);
+      case 3: return D3::template fwd<KIND>(a, ctas, st);
+      case 4: return D4::template fwd<KIND>(a, ctas, st);
+      default: return D0::template fwd<KIND>(a, ctas, st);
+    }
   }
-}
+  template <int KIND>
+  static cudaError_t bwd(int shape, const DflashBwdArgs& a, int ctas, cudaStream_t st) {
+    switch (shape) {
+      case 1: return D1::template bwd<KIND>(a, ctas, st);
+      case 2: return D2::template bwd<KIND>(a, ctas, st);
+      case 3: return D3::template bwd<KIND>(a, ctas, st);
+      case 4: return D4::template bwd<KIND>(a, ctas, st);
+      default: return D0::template bwd<KIND>(a, ctas, st);
+    }
+  }
+  static int fwd_ctas_kind(int kind, int shape, int device, int cap) {
+    return kind == kKindKL ? fwd_ctas<kKindKL>(shape, device, cap) : fwd_ctas<kKindCE>(shape, device, cap);
+  }
+  static int bwd_ctas_kind(int kind, int shape, int device, int cap) {
+    return kind == kKindKL ? bwd_ctas<kKindKL>(shape, device, cap) : bwd_ctas<kKindCE>(shape, device, cap);
+  }
+  static cudaError_t fwd_kind(int shape, const DflashFwdArgs& a, int ctas, cudaStream_t st) {
+    return a.kind == kKindKL ? fwd<kKindKL>(shape, a, ctas, st) : fwd<kKindCE>(shape, a, ctas, st);
+  }
+  static cudaError_t bwd_kind(int shape, const DflashBwdArgs& a, int ctas, cudaStream_t st) {
+    return a.kind == kKindKL ? bwd<kKindKL>(shape, a, ctas, st) : bwd<kKindCE>(shape, a, ctas, st);
+  }
+};
 
 }  // namespace
 
-int dflash_ring_block_elems(int shape) {
-  switch (shape) {
-    case 1: return 4096 * 4;
-    case 4: return 4096 * 4;
-    default: return 2048 * 8;
-  }
+int dflash_ring_block_elems(int dtype, int shape) {
+  return dtype == kDtypeBF16 ? DfShapes<bf16_t>::block_elems(shape) : DfShapes<float>::block_elems(shape);
 }
 
 int dflash_ring_consumers(int shape) {
@@ -496,17 +565,21 @@ int dflash_ring_consumers(int shape) {
   }
 }
 
-int dflash_fwd_ring_ctas(int kind, int shape, int device, int cap) {
-  return kind == kKindKL ? fwd_ctas_k<kKindKL>(shape, device, cap) : fwd_ctas_k<kKindCE>(shape, device, cap);
+int dflash_fwd_ring_ctas(int dtype, int kind, int shape, int device, int cap) {
+  return dtype == kDtypeBF16 ? DfShapes<bf16_t>::fwd_ctas_kind(kind, shape, device, cap)
+                             : DfShapes<float>::fwd_ctas_kind(kind, shape, device, cap);
 }
-int dflash_bwd_ring_ctas(int kind, int shape, int device, int cap) {
-  return kind == kKindKL ? bwd_ctas_k<kKindKL>(shape, device, cap) : bwd_ctas_k<kKindCE>(shape, device, cap);
+int dflash_bwd_ring_ctas(int dtype, int kind, int shape, int device, int cap) {
+  return dtype == kDtypeBF16 ? DfShapes<bf16_t>::bwd_ctas_kind(kind, shape, device, cap)
+                             : DfShapes<float>::bwd_ctas_kind(kind, shape, device, cap);
 }
-cudaError_t dflash_fwd_ring_launch(int shape, const DflashFwdArgs& a, int ctas, cudaStream_t st) {
-  return a.kind == kKindKL ? fwd_launch_k<kKindKL>(shape, a, ctas, st) : fwd_launch_k<kKindCE>(shape, a, ctas, st);
+cudaError_t dflash_fwd_ring_launch(int dtype, int shape, const DflashFwdArgs& a, int ctas, cudaStream_t st) {
+  return dtype == kDtypeBF16 ? DfShapes<bf16_t>::fwd_kind(shape, a, ctas, st)
+                             : DfShapes<float>::fwd_kind(shape, a, ctas, st);
 }
-cudaError_t dflash_bwd_ring_launch(int shape, const DflashBwdArgs& a, int ctas, cudaStream_t st) {
-  return a.kind == kKindKL ? bwd_launch_k<kKindKL>(shape, a, ctas, st) : bwd_launch_k<kKindCE>(shape, a, ctas, st);
+cudaError_t dflash_bwd_ring_launch(int dtype, int shape, const DflashBwdArgs& a, int ctas, cudaStream_t st) {
+  return dtype == kDtypeBF16 ? DfShapes<bf16_t>::bwd_kind(shape, a, ctas, st)
+                             : DfShapes<float>::bwd_kind(shape, a, ctas, st);
 }
 
 }  // namespace specdec

@@ -196,7 +196,7 @@ __global__ void __launch_bounds__(NT) dpace_fwd_kernel(const __grid_constant__ D
     const int64_t n = r / a.B;
     const bool live = a.mask == nullptr || a.mask[r] > 0.f;
     if (live) {
-      const float* row = a.logits + row0;
+      const float* row = static_cast<const float*>(a.logits) + row0;
       float m = kNegSeed, s = 0.f;
       stream_lse<NT, U>(row + lo, hi - lo, m, s);
       block_lse<NT>(m, s, sh_red);
@@ -234,8 +234,8 @@ __global__ void __launch_bounds__(NT) dpace_bwd_kernel(const __grid_constant__ D
     e = row0 + hi;
     const int64_t n = hi - lo;
     const float sc = __fmul_rn(a.scale[r], g);
-    const float* src = a.logits + row0 + lo;
-    float* dst = a.dlogits + row0 + lo;
+    const float* src = static_cast<const float*>(a.logits) + row0 + lo;
+    float* dst = static_cast<float*>(a.dlogits) + row0 + lo;
     const int64_t t = a.targets[r] - lo;  // target position relative to the piece
     const float l = a.lse[r];
     // Vector path when source and destination share 16-byte phase.

@@ -19,6 +19,11 @@
 // Rows with position mask 0 are never copied (forward); rows with scale 0 are
 // never copied and written as zeros (backward).
 //
+// Element type T: float, or bf16_t (bfloat16 bit patterns). bf16 stages hold
+// twice the elements in the same bytes; every element is widened exactly to
+// float and all arithmetic is float; the bf16 backward rounds each gradient
+// element to nearest even.
+//
 // Reference behaviour: losses/dpace.py:15-118 (forward), :120-145 (backward);
 // numbers follow losses/dpace_ref.py:8-51.
 #include <cfloat>
@@ -31,15 +36,16 @@ namespace specdec {
 
 namespace {
 
-template <int NC, int S, int SE, int BS>
-__global__ void __launch_bounds__((NC + 1) * 32, 1) dpace_fwd_ring_kernel(const __grid_constant__ DpaceFwdArgs a) {
+template <class T, int NC, int S, int SE, int BS>
+__global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<1, S, SE, T>())) dpace_fwd_ring_kernel(const __grid_constant__ DpaceFwdArgs a) {
   constexpr int kSub = SE / NC;
   constexpr int64_t BL = (int64_t)BS * SE;
   constexpr int kLogBL = __builtin_ctzll(BL);
-  static_assert(kSub % 128 == 0, "sub-range must be whole float4 rounds of a warp");
+  static_assert(kSub % (32 * (16 / sizeof(T))) == 0, "sub-range must be whole 16-byte rounds of a warp");
   static_assert((BL & (BL - 1)) == 0, "block length must be a power of two");
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  auto& sm = *reinterpret_cast<RingSmem<1, S, SE>*>(smem_raw);
+  auto& sm = *reinterpret_cast<RingSmem<1, S, SE, T>*>(smem_raw);
+  const T* X = static_cast<const T*>(a.logits);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t E = a.pt.E, V = a.pt.V, R = E / V;
   const int pmax = a.pt.pmax;
@@ -58,8 +64,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dpace_fwd_ring_kernel(const 
 
   if (warp == NC) {  // producer
     if (lane == 0) {
-      const float* src[1] = {a.logits};
-      if (!ring_produce<1, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow)) {
+      const T* src[1] = {X};
+      if (!ring_produce<1, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow,
+                                      a.withhold_stage && blockIdx.x == 0)) {
         atomicOr(a.flag, 2);
         if (a.status) a.status[0] = kStatusTimeout;
       }
@@ -106,7 +113,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dpace_fwd_ring_kernel(const 
       r = sm.srow[slot];
       enter_row(r);
     }
-    const float* sb = sm.ring + (size_t)slot * SE;
+    const T* sb = sm.ring + (size_t)slot * SE;
     if (f1 - f0 == SE && (r + 1) * V >= f1) {
       // fast path: a full stage inside one row
       if (live) warp_lse_full<kSub>(sb + warp * kSub, m, s);
@@ -121,7 +128,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dpace_fwd_ring_kernel(const 
       }
       continue;
     }
-    const int64_t fv = f0 + ((((f1 - f0) * 4) & ~int64_t(15)) >> 2);  // end of the copied part
+    const int64_t fv = copied_end<T>(f0, f1);  // end of the copied part
     const int64_t w0 = f0 + (int64_t)warp * kSub, w1 = min(w0 + kSub, f1);
     int64_t f = f0;
     while (f < f1) {
@@ -131,7 +138,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dpace_fwd_ring_kernel(const 
         const int64_t lo = max(f, w0), hi = min(g, w1);
         const int64_t hv = min(hi, fv);
         if (hv > lo) warp_lse_smem(sb, (int)(lo - f0), (int)(hv - f0), m, s);
-        for (int64_t x = max(lo, fv) + lane; x < hi; x += 32) lse_push(m, s, __ldg(a.logits + x));
+        for (int64_t x = max(lo, fv) + lane; x < hi; x += 32) lse_push(m, s, ldg_f32(X + x));
       }
       f = g;
       if (g == rend) {
@@ -148,6 +155,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dpace_fwd_ring_kernel(const 
 }
 
 // One CTA per sequence n, warp j <-> row j (B <= 32 warps).
+template <class T>
 __global__ void __launch_bounds__(1024) dpace_finalize_kernel(const __grid_constant__ DpaceFwdArgs a) {
   __shared__ float sh_ce[32];
   pdl_wait();  // the streaming grid has completed and its stores are visible
@@ -166,7 +174,7 @@ __global__ void __launch_bounds__(1024) dpace_finalize_kernel(const __grid_const
     pv[0] = lane < k ? part[lane] : make_float2(kNegSeed, 0.f);
     pv[1] = lane + 32 < k ? part[lane + 32] : make_float2(kNegSeed, 0.f);
     const bool tvalid = t >= 0 && t < V;
-    const float xt = tvalid ? __ldg(a.logits + r * V + t) : 0.f;  // x[target], read once per row
+    const float xt = tvalid ? ldg_f32(static_cast<const T*>(a.logits) + r * V + t) : 0.f;  // x[target]
     const bool live = mk > 0.f;
     float lse = 0.f, ce = 0.f;
     if (live) {
@@ -236,14 +244,17 @@ __global__ void __launch_bounds__(1024) dpace_finalize_kernel(const __grid_const
   }
 }
 
-template <int NC, int S, int SE, int BS>
-__global__ void __launch_bounds__((NC + 1) * 32, 1) dpace_bwd_ring_kernel(const __grid_constant__ DpaceBwdArgs a) {
+template <class T, int NC, int S, int SE, int BS>
+__global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<1, S, SE, T>())) dpace_bwd_ring_kernel(const __grid_constant__ DpaceBwdArgs a) {
+  constexpr int kVec = 16 / sizeof(T);  // elements per 16-byte vector
   constexpr int kSub = SE / NC;
   constexpr int64_t BL = (int64_t)BS * SE;
-  static_assert(kSub % 4 == 0, "sub-range must be whole float4s");
+  static_assert(kSub % kVec == 0, "sub-range must be whole 16-byte vectors");
   static_assert((BL & (BL - 1)) == 0, "block length must be a power of two");
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  auto& sm = *reinterpret_cast<RingSmem<1, S, SE>*>(smem_raw);
+  auto& sm = *reinterpret_cast<RingSmem<1, S, SE, T>*>(smem_raw);
+  const T* X = static_cast<const T*>(a.logits);
+  T* dst = static_cast<T*>(a.dlogits);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t E = a.pt.E, V = a.pt.V, R = E / V;
   const float g = a.dloss ? __ldg(a.dloss) : 1.f;
@@ -262,7 +273,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dpace_bwd_ring_kernel(const 
 
   if (warp == NC) {
     if (lane == 0) {
-      const float* src[1] = {a.logits};
+      const T* src[1] = {X};
       if (!ring_produce<1, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow) && a.flag)
         atomicOr(a.flag, 2);
     }
@@ -293,9 +304,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dpace_bwd_ring_kernel(const 
       r = sm.srow[slot];
       load_row(r);
     }
-    const int64_t fv = f0 + ((((f1 - f0) * 4) & ~int64_t(15)) >> 2);
+    const int64_t fv = copied_end<T>(f0, f1);
     const int64_t w0 = f0 + (int64_t)warp * kSub, w1 = min(w0 + kSub, f1);
-    const float* sb = sm.ring + (size_t)slot * SE;
+    const T* sb = sm.ring + (size_t)slot * SE;
     int64_t f = f0;
     while (f < f1) {
       const int64_t rend = (r + 1) * V;
@@ -303,29 +314,29 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dpace_bwd_ring_kernel(const 
       const int64_t lo = max(f, w0), hi = min(ge, w1);
       if (lo < hi) {
         const bool zero = sc == 0.f || !rb.live(r);
-        // [lo, hi): scalar head to a 4-element boundary, float4 body, scalar tail
-        const int64_t lo4 = (lo + 3) & ~int64_t(3), hi4 = min(hi, fv) & ~int64_t(3);
-        float* dst = a.dlogits;
+        // [lo, hi): scalar head to a vector boundary, 16-byte body, scalar tail
+        const int64_t lov = (lo + kVec - 1) & ~int64_t(kVec - 1), hiv = min(hi, fv) & ~int64_t(kVec - 1);
         auto scalar = [&](int64_t x) {
           if (zero) {
-            dst[x] = 0.f;
+            store_elem(dst + x, 0.f);
           } else {
-            const float v = x < fv ? sb[x - f0] : __ldg(a.logits + x);
-            dst[x] = sc * (exp_shift(v, l) - (x == tf ? 1.f : 0.f));
+            const float v = x < fv ? to_f32(sb[x - f0]) : ldg_f32(X + x);
+            store_elem(dst + x, sc * (exp_shift(v, l) - (x == tf ? 1.f : 0.f)));
           }
         };
-        if (lo4 < hi4) {
-          for (int64_t x = lo + lane; x < lo4; x += 32) scalar(x);
-          for (int64_t x = hi4 + lane; x < hi; x += 32) scalar(x);
-          float4* d4 = reinterpret_cast<float4*>(dst + lo4);
-          const float4* s4 = reinterpret_cast<const float4*>(sb + (lo4 - f0));
-          const int n4 = (int)((hi4 - lo4) >> 2);
+        if (lov < hiv) {
+          for (int64_t x = lo + lane; x < lov; x += 32) scalar(x);
+          for (int64_t x = hiv + lane; x < hi; x += 32) scalar(x);
+          const int nv = (int)((hiv - lov) / kVec);
           if (zero) {
-            const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int k = lane; k < n4; k += 32) st_stream(d4 + k, z);
-          } else {
-            const int64_t tq = tf - lo4;
-            for (int k = lane; k < n4; k += 32) {
+            const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+            uint4* d4 = reinterpret_cast<uint4*>(dst + lov);
+            for (int k = lane; k < nv; k += 32) st_stream_u4(d4 + k, z);
+          } else if constexpr (sizeof(T) == 4) {
+            float4* d4 = reinterpret_cast<float4*>(dst + lov);
+            const float4* s4 = reinterpret_cast<const float4*>(sb + (lov - f0));
+            const int64_t tq = tf - lov;
+            for (int k = lane; k < nv; k += 32) {
               const float4 v = s4[k];
               float4 y;
               y.x = exp_shift(v.x, l);
@@ -345,6 +356,22 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dpace_bwd_ring_kernel(const 
               y.w *= sc;
               st_stream(d4 + k, y);
             }
+          } else {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + lov);
+            const uint4* s4 = reinterpret_cast<const uint4*>(sb + (lov - f0));
+            const int64_t tq = tf - lov;
+            for (int k = lane; k < nv; k += 32) {
+              const uint4 v = s4[k];
+              float y[8] = {exp_shift(bf16_lo(v.x), l), exp_shift(bf16_hi(v.x), l),
+                            exp_shift(bf16_lo(v.y), l), exp_shift(bf16_hi(v.y), l),
+                            exp_shift(bf16_lo(v.z), l), exp_shift(bf16_hi(v.z), l),
+                            exp_shift(bf16_lo(v.w), l), exp_shift(bf16_hi(v.w), l)};
+              const uint64_t d = (uint64_t)(tq - 8 * (int64_t)k);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) y[e] = sc * (y[e] - (d == (uint64_t)e ? 1.f : 0.f));
+              st_stream_u4(d4 + k, make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]),
+                                              pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7])));
+            }
           }
         } else {
           for (int64_t x = lo + lane; x < hi; x += 32) scalar(x);
@@ -361,55 +388,99 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) dpace_bwd_ring_kernel(const 
   }
 }
 
-template <int NC, int S, int SE, int BS>
+template <class T, int NC, int S, int SE, int BS>
 struct RingVariant {
-  static constexpr size_t smem() { return sizeof(RingSmem<1, S, SE>); }
+  static constexpr size_t smem() { return sizeof(RingSmem<1, S, SE, T>); }
   static int fwd_ctas(int device, int cap) {
-    return ring_occupancy_ctas(dpace_fwd_ring_kernel<NC, S, SE, BS>, (NC + 1) * 32, smem(), device, cap);
+    return ring_occupancy_ctas(dpace_fwd_ring_kernel<T, NC, S, SE, BS>, (NC + 1) * 32, smem(), device, cap);
   }
   static int bwd_ctas(int device, int cap) {
-    return ring_occupancy_ctas(dpace_bwd_ring_kernel<NC, S, SE, BS>, (NC + 1) * 32, smem(), device, cap);
+    return ring_occupancy_ctas(dpace_bwd_ring_kernel<T, NC, S, SE, BS>, (NC + 1) * 32, smem(), device, cap);
   }
   static cudaError_t fwd(DpaceFwdArgs a, int ctas, cudaStream_t st) {
     // the attribute must be set on the launching device before the launch
-    cudaFuncSetAttribute(dpace_fwd_ring_kernel<NC, S, SE, BS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(dpace_fwd_ring_kernel<T, NC, S, SE, BS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem());
     a.nc = NC;
-    dpace_fwd_ring_kernel<NC, S, SE, BS><<<ctas, (NC + 1) * 32, smem(), st>>>(a);
+    dpace_fwd_ring_kernel<T, NC, S, SE, BS><<<ctas, (NC + 1) * 32, smem(), st>>>(a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    return launch_pdl(dpace_finalize_kernel, dim3((unsigned)a.N), dim3(32 * a.B), st, a);
+    return launch_pdl(dpace_finalize_kernel<T>, dim3((unsigned)a.N), dim3(32 * a.B), st, a);
   }
   static cudaError_t bwd(const DpaceBwdArgs& a, int ctas, cudaStream_t st) {
-    cudaFuncSetAttribute(dpace_bwd_ring_kernel<NC, S, SE, BS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(dpace_bwd_ring_kernel<T, NC, S, SE, BS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem());
-    dpace_bwd_ring_kernel<NC, S, SE, BS><<<ctas, (NC + 1) * 32, smem(), st>>>(a);
+    dpace_bwd_ring_kernel<T, NC, S, SE, BS><<<ctas, (NC + 1) * 32, smem(), st>>>(a);
     return cudaGetLastError();
   }
 };
 
-// Ring shapes (consumer warps x stages x stage floats x stages per block):
-// 0 = 4 x 4 x 4096 x 4 (64 KB ring, 64 KB blocks, 3 CTAs/SM: the fastest
-// measured on the [64, 16, 128256] workload); 1 = 8 x 4 x 8192 x 2 (128 KB
-// ring, 1 CTA/SM); 2 = 4 x 6 x 4096 x 4 (96 KB ring, 2 CTAs/SM); 3 = 4 x 8 x
-// 4096 x 8 (128 KB ring, 128 KB blocks); 4 = 2 x 6 x 2048 x 8 (48 KB ring,
-// 4 CTAs/SM).
-using R0 = RingVariant<4, 4, 4096, 4>;
-using R1 = RingVariant<8, 4, 8192, 2>;
-using R2 = RingVariant<4, 6, 4096, 4>;
-using R3 = RingVariant<4, 8, 4096, 8>;
-using R4 = RingVariant<2, 6, 2048, 8>;
+// Ring shapes (consumer warps x stages x stage elements x stages per block),
+// float elements: 0 = 4 x 4 x 4096 x 4 (64 KB ring, 64 KB blocks, 3 CTAs/SM:
+// the fastest measured on the [64, 16, 128256] workload); 1 = 8 x 4 x 8192 x 2
+// (128 KB ring, 1 CTA/SM); 2 = 4 x 6 x 4096 x 4 (96 KB ring, 2 CTAs/SM); 3 =
+// 4 x 8 x 4096 x 8 (128 KB ring, 128 KB blocks); 4 = 2 x 6 x 2048 x 8 (48 KB
+// ring, 4 CTAs/SM). bf16 shapes have the same bytes (twice the elements).
+template <class T>
+struct Shapes {
+  static constexpr int k = 4 / sizeof(T);  // elements per float's bytes
+  using R0 = RingVariant<T, 4, 4, 4096 * k, 4>;
+  using R1 = RingVariant<T, 8, 4, 8192 * k, 2>;
+  using R2 = RingVariant<T, 4, 6, 4096 * k, 4>;
+  using R3 = RingVariant<T, 4, 8, 4096 * k, 8>;
+  using R4 = RingVariant<T, 2, 6, 2048 * k, 8>;
+
+  static int block_elems(int shape) {
+    switch (shape) {
+      case 1: return 8192 * 2 * k;
+      case 2: return 4096 * 4 * k;
+      case 3: return 4096 * 8 * k;
+      case 4: return 2048 * 8 * k;
+      default: return 4096 * 4 * k;
+    }
+  }
+  static int fwd_ctas(int shape, int device, int cap) {
+    switch (shape) {
+      case 1: return R1::fwd_ctas(device, cap);
+      case 2: return R2::fwd_ctas(device, cap);
+      case 3: return R3::fwd_ctas(device, cap);
+      case 4: return R4::fwd_ctas(device, cap);
+      default: return R0::fwd_ctas(device, cap);
+    }
+  }
+  static int bwd_ctas(int shape, int device, int cap) {
+    switch (shape) {
+      case 1: return R1::bwd_ctas(device, cap);
+      case 2: return R2::bwd_ctas(device, cap);
+      case 3: return R3::bwd_ctas(device, cap);
+      case 4: return R4::bwd_ctas(device, cap);
+      default: return R0::bwd_ctas(device, cap);
+    }
+  }
+  static cudaError_t fwd(int shape, const DpaceFwdArgs& a, int ctas, cudaStream_t st) {
+    switch (shape) {
+      case 1: return R1::fwd(a, ctas, st);
+      case 2: return R2::fwd(a, ctas, st);
+      case 3: return R3::fwd(a, ctas, st);
+      case 4: return R4::fwd(a, ctas, st);
+      default: return R0::fwd(a, ctas, st);
+    }
+  }
+  static cudaError_t bwd(int shape, const DpaceBwdArgs& a, int ctas, cudaStream_t st) {
+    switch (shape) {
+      case 1: return R1::bwd(a, ctas, st);
+      case 2: return R2::bwd(a, ctas, st);
+      case 3: return R3::bwd(a, ctas, st);
+      case 4: return R4::bwd(a, ctas, st);
+      default: return R0::bwd(a, ctas, st);
+    }
+  }
+};
 
 }  // namespace
 
-int dpace_ring_block_elems(int shape) {
-  switch (shape) {
-    case 1: return 8192 * 2;
-    case 2: return 4096 * 4;
-    case 3: return 4096 * 8;
-    case 4: return 2048 * 8;
-    default: return 4096 * 4;
-  }
+int dpace_ring_block_elems(int dtype, int shape) {
+  return dtype == kDtypeBF16 ? Shapes<bf16_t>::block_elems(shape) : Shapes<float>::block_elems(shape);
 }
 
 int dpace_ring_consumers(int shape) {
@@ -420,44 +491,22 @@ int dpace_ring_consumers(int shape) {
   }
 }
 
-int dpace_fwd_ring_ctas(int shape, int device, int cap) {
-  switch (shape) {
-    case 1: return R1::fwd_ctas(device, cap);
-    case 2: return R2::fwd_ctas(device, cap);
-    case 3: return R3::fwd_ctas(device, cap);
-    case 4: return R4::fwd_ctas(device, cap);
-    default: return R0::fwd_ctas(device, cap);
-  }
+int dpace_fwd_ring_ctas(int dtype, int shape, int device, int cap) {
+  return dtype == kDtypeBF16 ? Shapes<bf16_t>::fwd_ctas(shape, device, cap)
+                             : Shapes<float>::fwd_ctas(shape, device, cap);
 }
 
-int dpace_bwd_ring_ctas(int shape, int device, int cap) {
-  switch (shape) {
-    case 1: return R1::bwd_ctas(device, cap);
-    case 2: return R2::bwd_ctas(device, cap);
-    case 3: return R3::bwd_ctas(device, cap);
-    case 4: return R4::bwd_ctas(device, cap);
-    default: return R0::bwd_ctas(device, cap);
-  }
+int dpace_bwd_ring_ctas(int dtype, int shape, int device, int cap) {
+  return dtype == kDtypeBF16 ? Shapes<bf16_t>::bwd_ctas(shape, device, cap)
+                             : Shapes<float>::bwd_ctas(shape, device, cap);
 }
 
-cudaError_t dpace_fwd_ring_launch(int shape, const DpaceFwdArgs& a, int ctas, cudaStream_t st) {
-  switch (shape) {
-    case 1: return R1::fwd(a, ctas, st);
-    case 2: return R2::fwd(a, ctas, st);
-    case 3: return R3::fwd(a, ctas, st);
-    case 4: return R4::fwd(a, ctas, st);
-    default: return R0::fwd(a, ctas, st);
-  }
+cudaError_t dpace_fwd_ring_launch(int dtype, int shape, const DpaceFwdArgs& a, int ctas, cudaStream_t st) {
+  return dtype == kDtypeBF16 ? Shapes<bf16_t>::fwd(shape, a, ctas, st) : Shapes<float>::fwd(shape, a, ctas, st);
 }
 
-cudaError_t dpace_bwd_ring_launch(int shape, const DpaceBwdArgs& a, int ctas, cudaStream_t st) {
-  switch (shape) {
-    case 1: return R1::bwd(a, ctas, st);
-    case 2: return R2::bwd(a, ctas, st);
-    case 3: return R3::bwd(a, ctas, st);
-    case 4: return R4::bwd(a, ctas, st);
-    default: return R0::bwd(a, ctas, st);
-  }
+cudaError_t dpace_bwd_ring_launch(int dtype, int shape, const DpaceBwdArgs& a, int ctas, cudaStream_t st) {
+  return dtype == kDtypeBF16 ? Shapes<bf16_t>::bwd(shape, a, ctas, st) : Shapes<float>::bwd(shape, a, ctas, st);
 }
 
 }  // namespace specdec

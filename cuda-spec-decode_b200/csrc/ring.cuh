@@ -88,14 +88,25 @@ __device__ __forceinline__ RowBits build_row_bits(unsigned* words, int64_t R, in
   return rb;
 }
 
-// Producer loop, lane 0 of the producer warp. NIN input streams share the
-// flattened index space (ring k holds stream k's stages at ring + k*S*SE).
-// A stage whose rows are all dead is posted without a copy. Returns false on
-// a wait timeout.
-template <int NIN, int S, int SE, int BS>
-__device__ bool ring_produce(const float* const* src, int64_t E, int64_t V, const RowBits& rb,
-                             const BlockQueue& q, float* ring, uint64_t* full, uint64_t* empty,
-                             int64_t* sf0, int64_t* srow) {
+// Elements of a stage that the bulk copy brought in: [f0, f0 + copied) with
+// copied * sizeof(T) the stage's byte count rounded down to 16 bytes; the
+// rest (at most 15 bytes, only at the very end of the data) is read from
+// global memory.
+template <class T>
+__device__ __forceinline__ int64_t copied_end(int64_t f0, int64_t f1) {
+  return f0 + ((((f1 - f0) * (int64_t)sizeof(T)) & ~int64_t(15)) / (int64_t)sizeof(T));
+}
+
+// Producer loop, lane 0 of the producer warp. NIN input streams of element
+// type T share the flattened index space (ring k holds stream k's stages at
+// ring + k*S*SE). A stage whose rows are all dead is posted without a copy.
+// Returns false on a wait timeout. `withhold_first` (failure-detection tests
+// only) never posts the first stage: this CTA's consumers then see their
+// bounded wait expire, which is the path under test.
+template <int NIN, int S, int SE, int BS, class T>
+__device__ bool ring_produce(const T* const* src, int64_t E, int64_t V, const RowBits& rb,
+                             const BlockQueue& q, T* ring, uint64_t* full, uint64_t* empty,
+                             int64_t* sf0, int64_t* srow, bool withhold_first = false) {
   constexpr int64_t BL = (int64_t)BS * SE;
   unsigned b = q.first();
   unsigned nb = b < q.nblocks ? q.next(b) : q.nblocks;
@@ -112,6 +123,7 @@ __device__ bool ring_produce(const float* const* src, int64_t E, int64_t V, cons
       ok = false;
       break;
     }
+    if (withhold_first && it == 0) continue;  // neither copy nor arrive: full[0] stays incomplete
     if (b >= q.nblocks) {
       sf0[slot] = -1;
       mbar_arrive(full + slot);
@@ -124,7 +136,7 @@ __device__ bool ring_produce(const float* const* src, int64_t E, int64_t V, cons
     srow[slot] = r_issue;
     bool live = !rb.valid;
     for (int64_t r = r_issue; !live && r * V < f1; ++r) live = rb.live(r);
-    const uint32_t vbytes = (uint32_t)(((f1 - f0) * 4) & ~int64_t(15));
+    const uint32_t vbytes = (uint32_t)(((f1 - f0) * (int64_t)sizeof(T)) & ~int64_t(15));
     if (live && vbytes) {
       mbar_arrive_expect_tx(full + slot, vbytes * NIN);
 #pragma unroll
@@ -156,19 +168,27 @@ __device__ __forceinline__ void ring_drain(uint64_t* full, int64_t it) {
   for (int64_t j = it; j < it + S; ++j) mbar_wait(full + (j % S), (uint32_t)((j / S) & 1));
 }
 
-// Shared-memory layout of a ring: NIN streams x S stages x SE floats, then the
-// stage barriers, the posted stage starts and the liveness bitmask.
-template <int NIN, int S, int SE>
+// Shared-memory layout of a ring: NIN streams x S stages x SE elements, then
+// the stage barriers, the posted stage starts and the liveness bitmask.
+template <int NIN, int S, int SE, class T = float>
 struct RingSmem {
-  float ring[NIN * S * SE];
+  T ring[NIN * S * SE];  // first member: 128-byte aligned with the dynamic shared memory
   uint64_t full[S], empty[S];
   int64_t sf0[S];   // flattened start of the stage (-1: end of work)
   int64_t srow[S];  // row containing the stage's first element
   unsigned bits[kMaxRowWords];
 };
 
-template <int NIN, int S, int SE>
-__device__ __forceinline__ void ring_init(RingSmem<NIN, S, SE>& sm, int consumers) {
+// Minimum CTAs per SM a bf16 ring kernel is compiled for: 3 where three rings
+// fit in shared memory (the register budget then allows 3 resident CTAs of
+// 160 threads), else 1. Float kernels are compiled without a minimum.
+template <int NIN, int S, int SE, class T>
+constexpr int ring_min_ctas() {
+  return (sizeof(T) == 2 && 3 * sizeof(RingSmem<NIN, S, SE, T>) <= 227 * 1024) ? 3 : 1;
+}
+
+template <int NIN, int S, int SE, class T>
+__device__ __forceinline__ void ring_init(RingSmem<NIN, S, SE, T>& sm, int consumers) {
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(sm.full + i, 1);
@@ -236,6 +256,46 @@ __device__ __forceinline__ void warp_lse_full(const float* sb, float& m, float& 
 #pragma unroll
   for (int u = 0; u < U; ++u)
     acc[u] = (exp_shift(v[u].x, m) + exp_shift(v[u].y, m)) + (exp_shift(v[u].z, m) + exp_shift(v[u].w, m));
+#pragma unroll
+  for (int w = 1; w < U; w <<= 1)
+#pragma unroll
+    for (int u = 0; u + w < U; u += 2 * w) acc[u] += acc[u + w];
+  s += acc[0];
+}
+
+// bf16 stage, elements [a, b): one element per lane per round (row edges).
+__device__ __forceinline__ void warp_lse_smem(const bf16_t* sb, int a, int b, float& m, float& s) {
+  const int lane = threadIdx.x & 31;
+  for (int k = a + lane; k < b; k += 32) lse_push(m, s, to_f32(sb[k]));
+}
+
+// bf16 full sub-range of KSUB elements (KSUB / 256 16-byte vectors per lane):
+// the max is taken on the packed words, each element is widened once for its
+// exponential.
+template <int KSUB>
+__device__ __forceinline__ void warp_lse_full(const bf16_t* sb, float& m, float& s) {
+  constexpr int U = KSUB / 256;
+  static_assert(KSUB % 256 == 0, "sub-range must be a multiple of 256 bf16");
+  const int lane = threadIdx.x & 31;
+  const uint4* q = reinterpret_cast<const uint4*>(sb) + lane;
+  uint4 v[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) v[u] = q[32 * u];
+  uint32_t mx = bmax8(v[0]);
+#pragma unroll
+  for (int u = 1; u < U; ++u) mx = bmax2(mx, bmax8(v[u]));
+  const float cm = fmaxf(bf16_lo(mx), bf16_hi(mx));
+  if (cm > m) {
+    s *= exp_shift(m, cm);
+    m = cm;
+  }
+  float acc[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u)
+    acc[u] = ((exp_shift(bf16_lo(v[u].x), m) + exp_shift(bf16_hi(v[u].x), m)) +
+              (exp_shift(bf16_lo(v[u].y), m) + exp_shift(bf16_hi(v[u].y), m))) +
+             ((exp_shift(bf16_lo(v[u].z), m) + exp_shift(bf16_hi(v[u].z), m)) +
+              (exp_shift(bf16_lo(v[u].w), m) + exp_shift(bf16_hi(v[u].w), m)));
 #pragma unroll
   for (int w = 1; w < U; w <<= 1)
 #pragma unroll

@@ -44,6 +44,7 @@ constexpr int64_t kMinChunk = 1024;
 std::atomic<int> g_shape[4] = {0, 0, 0, 0};
 std::atomic<int> g_cap[4] = {0, 0, 0, 0};
 std::atomic<int> g_static_queue{0};  // 1: ring kernels use a static block interleave
+std::atomic<int> g_withhold_stage{0};  // failure-detection tests: launches left to withhold a stage
 
 int current_device() {
   int d = 0;
@@ -71,15 +72,27 @@ bool use_tma(int kernel, bool ptrs_aligned) {
   return g_shape[kernel].load() < kLdgShapeBase && ptrs_aligned && has_ring_path(kernel);
 }
 
-// Occupancy-derived work units (CTAs for the 128-bit-load kernels, warps for
-// the ring kernels), cached per (kernel, kind, path, shape, cap, device).
-int kernel_units(int kernel, int kind, bool tma, int device) {
+// bf16 has only the ring kernels: a shape that selects the 128-bit-load
+// kernels falls back to ring shape 0.
+int bf16_shape(int kernel) {
+  const int raw = g_shape[kernel].load();
+  return raw < kLdgShapeBase ? raw : 0;
+}
+
+int ring_shape(int kernel, int dtype) {
+  return dtype == kDtypeBF16 ? bf16_shape(kernel) : kernel_shape(kernel, true);
+}
+
+// Occupancy-derived CTA counts, cached per (kernel, dtype, kind, path,
+// shape, cap, device). bf16 always takes the ring path.
+int kernel_units(int kernel, int kind, bool tma, int device, int dtype = kDtypeF32) {
   static std::mutex mu;
   static std::map<uint64_t, int> cache;
   const int cap = g_cap[kernel].load();
-  const int shape = kernel_shape(kernel, tma);
-  const uint64_t key = (uint64_t(kernel) << 56) | (uint64_t(kind & 0x7f) << 49) | (uint64_t(tma) << 48) |
-                       (uint64_t(shape & 0xff) << 40) | (uint64_t(cap & 0xffff) << 24) |
+  if (dtype == kDtypeBF16) tma = true;
+  const int shape = tma ? ring_shape(kernel, dtype) : kernel_shape(kernel, false);
+  const uint64_t key = (uint64_t(kernel) << 56) | (uint64_t(dtype & 1) << 55) | (uint64_t(kind & 0x3f) << 49) |
+                       (uint64_t(tma) << 48) | (uint64_t(shape & 0xff) << 40) | (uint64_t(cap & 0xffff) << 24) |
                        uint64_t(device & 0xffffff);
   {
     std::lock_guard<std::mutex> lk(mu);
@@ -89,16 +102,16 @@ int kernel_units(int kernel, int kind, bool tma, int device) {
   int ctas = 0;
   switch (kernel) {
     case SPECDEC_KERNEL_DPACE_FWD:
-      ctas = tma ? dpace_fwd_ring_ctas(shape, device, cap) : dpace_fwd_ctas(shape, device, cap);
+      ctas = tma ? dpace_fwd_ring_ctas(dtype, shape, device, cap) : dpace_fwd_ctas(shape, device, cap);
       break;
     case SPECDEC_KERNEL_DPACE_BWD:
-      ctas = tma ? dpace_bwd_ring_ctas(shape, device, cap) : dpace_bwd_ctas(shape, device, cap);
+      ctas = tma ? dpace_bwd_ring_ctas(dtype, shape, device, cap) : dpace_bwd_ctas(shape, device, cap);
       break;
     case SPECDEC_KERNEL_DFLASH_FWD:
-      ctas = tma ? dflash_fwd_ring_ctas(kind, shape, device, cap) : dflash_fwd_ctas(kind, shape, device, cap);
+      ctas = tma ? dflash_fwd_ring_ctas(dtype, kind, shape, device, cap) : dflash_fwd_ctas(kind, shape, device, cap);
       break;
     case SPECDEC_KERNEL_DFLASH_BWD:
-      ctas = tma ? dflash_bwd_ring_ctas(kind, shape, device, cap) : dflash_bwd_ctas(kind, shape, device, cap);
+      ctas = tma ? dflash_bwd_ring_ctas(dtype, kind, shape, device, cap) : dflash_bwd_ctas(kind, shape, device, cap);
       break;
     default: ctas = 0;
   }
@@ -163,17 +176,23 @@ DflashLayout dflash_layout(int64_t N, int64_t B, const Partition& pt, int nc) {
   return L;
 }
 
-Partition dpace_fwd_partition(int64_t N, int32_t B, int64_t V, bool tma, int device) {
-  const int units = kernel_units(SPECDEC_KERNEL_DPACE_FWD, 0, tma, device);
-  if (tma)
-    return ring_partition(N * B, V, dpace_ring_block_elems(kernel_shape(SPECDEC_KERNEL_DPACE_FWD, true)), units);
+// A bf16 block holds twice the elements of the float block of the same shape,
+// so its partition has no more pieces per row: the float workspace sizes
+// bound the bf16 ones.
+Partition dpace_fwd_partition(int64_t N, int32_t B, int64_t V, bool tma, int device, int dtype = kDtypeF32) {
+  const int units = kernel_units(SPECDEC_KERNEL_DPACE_FWD, 0, tma, device, dtype);
+  if (tma || dtype == kDtypeBF16)
+    return ring_partition(N * B, V, dpace_ring_block_elems(dtype, ring_shape(SPECDEC_KERNEL_DPACE_FWD, dtype)),
+                          units);
   return make_partition(N * B, V, units, kMinChunk);
 }
 
-Partition dflash_fwd_partition(int64_t N, int32_t B, int64_t V, int kind, bool tma, int device) {
-  const int units = kernel_units(SPECDEC_KERNEL_DFLASH_FWD, kind, tma, device);
-  if (tma)
-    return ring_partition(N * B, V, dflash_ring_block_elems(kernel_shape(SPECDEC_KERNEL_DFLASH_FWD, true)), units);
+Partition dflash_fwd_partition(int64_t N, int32_t B, int64_t V, int kind, bool tma, int device,
+                               int dtype = kDtypeF32) {
+  const int units = kernel_units(SPECDEC_KERNEL_DFLASH_FWD, kind, tma, device, dtype);
+  if (tma || dtype == kDtypeBF16)
+    return ring_partition(N * B, V, dflash_ring_block_elems(dtype, ring_shape(SPECDEC_KERNEL_DFLASH_FWD, dtype)),
+                          units);
   return make_partition(N * B, V, units, kMinChunk);
 }
 
@@ -219,6 +238,12 @@ int specdec_set_block_queue(int32_t dynamic) {
   return ok();
 }
 
+int specdec_test_withhold_stage(int32_t launches) {
+  if (launches < 0 || launches > 16) return fail(SPECDEC_ERR_ARGUMENT, "launches must be in [0, 16]");
+  g_withhold_stage.store(launches);
+  return ok();
+}
+
 int64_t specdec_launch_ctas(int32_t kernel, int64_t rows, int64_t V, int device) {
   if (kernel < 0 || kernel > 3 || rows <= 0 || V <= 0) return 0;
   const bool tma = use_tma(kernel, true);
@@ -233,12 +258,16 @@ int64_t specdec_launch_ctas(int32_t kernel, int64_t rows, int64_t V, int device)
 
 size_t specdec_dpace_scratch_bytes(int64_t N, int32_t B, int64_t V, int device) {
   if (N <= 0 || B <= 0 || V <= 0) return 256;
-  // large enough for either kernel family (the call picks by pointer alignment)
-  const size_t a = dpace_layout(N, B, dpace_fwd_partition(N, B, V, false, device), 1).scratch;
-  if (!use_tma(SPECDEC_KERNEL_DPACE_FWD, true)) return a;
-  const int nc = dpace_ring_consumers(kernel_shape(SPECDEC_KERNEL_DPACE_FWD, true));
-  const size_t b = dpace_layout(N, B, dpace_fwd_partition(N, B, V, true, device), nc).scratch;
-  return a > b ? a : b;
+  // large enough for either kernel family (the call picks by pointer
+  // alignment) and for either element type
+  size_t best = dpace_layout(N, B, dpace_fwd_partition(N, B, V, false, device), 1).scratch;
+  for (int dtype = kDtypeF32; dtype <= kDtypeBF16; ++dtype) {
+    if (dtype == kDtypeF32 && !use_tma(SPECDEC_KERNEL_DPACE_FWD, true)) continue;
+    const int nc = dpace_ring_consumers(ring_shape(SPECDEC_KERNEL_DPACE_FWD, dtype));
+    const size_t b = dpace_layout(N, B, dpace_fwd_partition(N, B, V, true, device, dtype), nc).scratch;
+    best = b > best ? b : best;
+  }
+  return best;
 }
 
 size_t specdec_dpace_counter_bytes(int64_t N, int32_t B) {
@@ -247,11 +276,14 @@ size_t specdec_dpace_counter_bytes(int64_t N, int32_t B) {
 
 size_t specdec_backward_counter_bytes(void) { return 256; }
 
-int specdec_dpace_forward(const float* logits, const int64_t* targets, const float* mask,
-                          int64_t N, int32_t B, int64_t V, float alpha, int32_t loss_type,
-                          int64_t n_global, float* loss, float* loss_n, float* lse, float* scale,
-                          int32_t* status, void* scratch, size_t scratch_bytes, void* counters,
-                          size_t counter_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+int dpace_forward_impl(int dtype, const void* logits, const int64_t* targets, const float* mask, int64_t N,
+                       int32_t B, int64_t V, float alpha, int32_t loss_type, int64_t n_global, float* loss,
+                       float* loss_n, float* lse, float* scale, int32_t* status, void* scratch,
+                       size_t scratch_bytes, void* counters, size_t counter_bytes, void* stream) {
   // Mirrors losses/dpace.py:157-173 (_check) order of failures.
   if (B < 1 || B > 32) return fail(SPECDEC_ERR_ARGUMENT, "kernel configured for block_size <= 32 (B=%d)", B);
   if (N < 0 || V < 0) return fail(SPECDEC_ERR_ARGUMENT, "negative shape N=%lld V=%lld", (long long)N, (long long)V);
@@ -275,12 +307,15 @@ int specdec_dpace_forward(const float* logits, const int64_t* targets, const flo
   if (!aligned(logits, 4) || !aligned(targets, 8) || !aligned(lse, 4) || !aligned(scale, 4) ||
       !aligned(scratch, 256) || !aligned(counters, 16))
     return fail(SPECDEC_ERR_ARGUMENT, "misaligned pointer (scratch needs 256 B, counters 16 B)");
+  if (dtype == kDtypeBF16 && !aligned(logits, 16))
+    return fail(SPECDEC_ERR_ARGUMENT, "bf16 logits must be 16-byte aligned");
   const int dev = current_device();
   if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
-  const bool tma = use_tma(SPECDEC_KERNEL_DPACE_FWD, aligned(logits, 16));
-  const Partition pt = dpace_fwd_partition(N, B, V, tma, dev);
+  const bool tma = dtype == kDtypeBF16 || use_tma(SPECDEC_KERNEL_DPACE_FWD, aligned(logits, 16));
+  const Partition pt = dpace_fwd_partition(N, B, V, tma, dev, dtype);
   if (pt.grid <= 0) return fail(SPECDEC_ERR_CUDA, "occupancy query failed");
-  const int nc = tma ? dpace_ring_consumers(kernel_shape(SPECDEC_KERNEL_DPACE_FWD, true)) : 1;
+  const int shape = tma ? ring_shape(SPECDEC_KERNEL_DPACE_FWD, dtype) : kernel_shape(SPECDEC_KERNEL_DPACE_FWD, false);
+  const int nc = tma ? dpace_ring_consumers(shape) : 1;
   const DpaceLayout L = dpace_layout(N, B, pt, nc);
   if (scratch_bytes < L.scratch)
     return fail(SPECDEC_ERR_WORKSPACE, "scratch needs %zu bytes, got %zu", L.scratch, scratch_bytes);
@@ -316,27 +351,35 @@ int specdec_dpace_forward(const float* logits, const int64_t* targets, const flo
   a.q_retired = cnt + 3;
   a.q_dynamic = g_static_queue.load() ? 0 : 1;
   a.seq_cnt = cnt + 4;
+  a.withhold_stage = 0;
+  if (tma) {
+    int left = g_withhold_stage.load();
+    while (left > 0 && !g_withhold_stage.compare_exchange_weak(left, left - 1)) {
+    }
+    a.withhold_stage = left > 0 ? 1 : 0;
+  }
   a.pt = pt;
-  const int shape = kernel_shape(SPECDEC_KERNEL_DPACE_FWD, tma);
   const cudaError_t e =
-      tma ? dpace_fwd_ring_launch(shape, a, (int)pt.grid, st) : dpace_fwd_launch(shape, a, st);
+      tma ? dpace_fwd_ring_launch(dtype, shape, a, (int)pt.grid, st) : dpace_fwd_launch(shape, a, st);
   return e == cudaSuccess ? ok() : cuda_fail(e, "dpace forward launch");
 }
 
-int specdec_dpace_backward(const float* logits, const int64_t* targets, const float* lse,
-                           const float* scale, const float* dloss, float* dlogits, int64_t N,
-                           int32_t B, int64_t V, void* counters, size_t counter_bytes,
-                           void* stream) {
+int dpace_backward_impl(int dtype, const void* logits, const int64_t* targets, const float* lse,
+                        const float* scale, const float* dloss, void* dlogits, int64_t N, int32_t B, int64_t V,
+                        void* counters, size_t counter_bytes, void* stream) {
   if (B < 1 || B > 32) return fail(SPECDEC_ERR_ARGUMENT, "kernel configured for block_size <= 32 (B=%d)", B);
   if (N < 0 || V < 0) return fail(SPECDEC_ERR_ARGUMENT, "negative shape");
   if (N == 0 || V == 0) return ok();
   if (!logits || !targets || !lse || !scale || !dlogits)
     return fail(SPECDEC_ERR_ARGUMENT, "null input or output pointer");
   if (logits == dlogits) return fail(SPECDEC_ERR_ARGUMENT, "dlogits must not alias logits");
+  if (dtype == kDtypeBF16 && !(aligned(logits, 16) && aligned(dlogits, 16)))
+    return fail(SPECDEC_ERR_ARGUMENT, "bf16 logits and dlogits must be 16-byte aligned");
   const int dev = current_device();
   if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
-  const bool tma = use_tma(SPECDEC_KERNEL_DPACE_BWD, aligned(logits, 16) && aligned(dlogits, 16));
-  const int units = kernel_units(SPECDEC_KERNEL_DPACE_BWD, 0, tma, dev);
+  const bool tma =
+      dtype == kDtypeBF16 || use_tma(SPECDEC_KERNEL_DPACE_BWD, aligned(logits, 16) && aligned(dlogits, 16));
+  const int units = kernel_units(SPECDEC_KERNEL_DPACE_BWD, 0, tma, dev, dtype);
   if (units <= 0) return fail(SPECDEC_ERR_CUDA, "occupancy query failed");
   DpaceBwdArgs a;
   a.logits = logits;
@@ -352,12 +395,51 @@ int specdec_dpace_backward(const float* logits, const int64_t* targets, const fl
   a.q_ctr = queue ? cnt : nullptr;
   a.q_retired = queue ? cnt + 1 : nullptr;
   a.q_dynamic = queue ? 1 : 0;
-  const int shape = kernel_shape(SPECDEC_KERNEL_DPACE_BWD, tma);
-  a.pt = tma ? ring_partition(N * B, V, dpace_ring_block_elems(shape), units)
+  const int shape = tma ? ring_shape(SPECDEC_KERNEL_DPACE_BWD, dtype) : kernel_shape(SPECDEC_KERNEL_DPACE_BWD, false);
+  a.pt = tma ? ring_partition(N * B, V, dpace_ring_block_elems(dtype, shape), units)
              : make_partition(N * B, V, units, kMinChunk);
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const cudaError_t e = tma ? dpace_bwd_ring_launch(shape, a, units, st) : dpace_bwd_launch(shape, a, st);
+  const cudaError_t e =
+      tma ? dpace_bwd_ring_launch(dtype, shape, a, units, st) : dpace_bwd_launch(shape, a, st);
   return e == cudaSuccess ? ok() : cuda_fail(e, "dpace backward launch");
+}
+
+}  // namespace
+
+extern "C" {
+
+int specdec_dpace_forward(const float* logits, const int64_t* targets, const float* mask,
+                          int64_t N, int32_t B, int64_t V, float alpha, int32_t loss_type,
+                          int64_t n_global, float* loss, float* loss_n, float* lse, float* scale,
+                          int32_t* status, void* scratch, size_t scratch_bytes, void* counters,
+                          size_t counter_bytes, void* stream) {
+  return dpace_forward_impl(kDtypeF32, logits, targets, mask, N, B, V, alpha, loss_type, n_global, loss, loss_n,
+                            lse, scale, status, scratch, scratch_bytes, counters, counter_bytes, stream);
+}
+
+int specdec_dpace_forward_bf16(const uint16_t* logits, const int64_t* targets, const float* mask,
+                               int64_t N, int32_t B, int64_t V, float alpha, int32_t loss_type,
+                               int64_t n_global, float* loss, float* loss_n, float* lse, float* scale,
+                               int32_t* status, void* scratch, size_t scratch_bytes, void* counters,
+                               size_t counter_bytes, void* stream) {
+  return dpace_forward_impl(kDtypeBF16, logits, targets, mask, N, B, V, alpha, loss_type, n_global, loss, loss_n,
+                            lse, scale, status, scratch, scratch_bytes, counters, counter_bytes, stream);
+}
+
+int specdec_dpace_backward(const float* logits, const int64_t* targets, const float* lse,
+                           const float* scale, const float* dloss, float* dlogits, int64_t N,
+                           int32_t B, int64_t V, void* counters, size_t counter_bytes,
+                           void* stream) {
+  return dpace_backward_impl(kDtypeF32, logits, targets, lse, scale, dloss, dlogits, N, B, V, counters,
+                             counter_bytes, stream);
+}
+
+int specdec_dpace_backward_bf16(const uint16_t* logits, const int64_t* targets, const float* lse,
+                                const float* scale, const float* dloss, uint16_t* dlogits, int64_t N,
+                                int32_t B, int64_t V, void* counters, size_t counter_bytes,
+                                void* stream) {
+  return dpace_backward_impl(kDtypeBF16, logits, targets, lse, scale, dloss, dlogits, N, B, V, counters,
+                             counter_bytes, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -366,14 +448,15 @@ int specdec_dpace_backward(const float* logits, const int64_t* targets, const fl
 
 size_t specdec_dflash_scratch_bytes(int64_t N, int32_t B, int64_t V, int device) {
   if (N <= 0 || B <= 0 || V <= 0) return 256;
-  // large enough for either kind and either kernel family
+  // large enough for either kind, either kernel family and either element type
   size_t best = 0;
   for (int kind = 0; kind < 2; ++kind) {
     const size_t a = dflash_layout(N, B, dflash_fwd_partition(N, B, V, kind, false, device), 1).scratch;
     best = a > best ? a : best;
-    if (use_tma(SPECDEC_KERNEL_DFLASH_FWD, true) && B <= 32) {
-      const int nc = dflash_ring_consumers(kernel_shape(SPECDEC_KERNEL_DFLASH_FWD, true));
-      const size_t b = dflash_layout(N, B, dflash_fwd_partition(N, B, V, kind, true, device), nc).scratch;
+    for (int dtype = kDtypeF32; dtype <= kDtypeBF16; ++dtype) {
+      if (dtype == kDtypeF32 && !use_tma(SPECDEC_KERNEL_DFLASH_FWD, true)) continue;
+      const int nc = dflash_ring_consumers(ring_shape(SPECDEC_KERNEL_DFLASH_FWD, dtype));
+      const size_t b = dflash_layout(N, B, dflash_fwd_partition(N, B, V, kind, true, device, dtype), nc).scratch;
       best = b > best ? b : best;
     }
   }
@@ -385,12 +468,15 @@ size_t specdec_dflash_counter_bytes(int64_t N, int32_t B) {
   return align256(16 + size_t(R) * sizeof(unsigned));
 }
 
-int specdec_dflash_forward(const float* logits, const float* target_logits, const float* mask,
-                           int64_t N, int32_t B, int64_t V, int32_t block_size, float gamma,
-                           int32_t sample_from_anchor, int32_t kind, int64_t n_global, float* loss,
-                           float* loss_rows, float* scale, float* logzq, float* logzp,
-                           int64_t* target_id, void* scratch, size_t scratch_bytes, void* counters,
-                           size_t counter_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+int dflash_forward_impl(int dtype, const void* logits, const void* target_logits, const float* mask, int64_t N,
+                        int32_t B, int64_t V, int32_t block_size, float gamma, int32_t sample_from_anchor,
+                        int32_t kind, int64_t n_global, float* loss, float* loss_rows, float* scale, float* logzq,
+                        float* logzp, int64_t* target_id, void* scratch, size_t scratch_bytes, void* counters,
+                        size_t counter_bytes, void* stream) {
   // Mirrors models/dflash/loss.py:178-191 (_check) order of failures.
   if (N < 0 || B < 0 || V < 0) return fail(SPECDEC_ERR_ARGUMENT, "negative shape");
   if (V > INT32_MAX) return fail(SPECDEC_ERR_ARGUMENT, "V must be < 2^31");
@@ -412,13 +498,17 @@ int specdec_dflash_forward(const float* logits, const float* target_logits, cons
   if (kind == SPECDEC_DFLASH_CE && !target_id) return fail(SPECDEC_ERR_ARGUMENT, "CE needs target_id output");
   if (!aligned(scratch, 256) || !aligned(counters, 16))
     return fail(SPECDEC_ERR_ARGUMENT, "misaligned workspace (scratch 256 B, counters 16 B)");
+  if (dtype == kDtypeBF16 && !(aligned(logits, 16) && aligned(target_logits, 16)))
+    return fail(SPECDEC_ERR_ARGUMENT, "bf16 logits and target_logits must be 16-byte aligned");
   const int dev = current_device();
   if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
-  const bool tma =
-      use_tma(SPECDEC_KERNEL_DFLASH_FWD, aligned(logits, 16) && aligned(target_logits, 16)) && B <= 32;
-  const Partition pt = dflash_fwd_partition(N, B, V, kind, tma, dev);
+  const bool tma = dtype == kDtypeBF16 ||
+                   use_tma(SPECDEC_KERNEL_DFLASH_FWD, aligned(logits, 16) && aligned(target_logits, 16));
+  const Partition pt = dflash_fwd_partition(N, B, V, kind, tma, dev, dtype);
   if (pt.grid <= 0) return fail(SPECDEC_ERR_CUDA, "occupancy query failed");
-  const int nc = tma ? dflash_ring_consumers(kernel_shape(SPECDEC_KERNEL_DFLASH_FWD, true)) : 1;
+  const int shape =
+      tma ? ring_shape(SPECDEC_KERNEL_DFLASH_FWD, dtype) : kernel_shape(SPECDEC_KERNEL_DFLASH_FWD, false);
+  const int nc = tma ? dflash_ring_consumers(shape) : 1;
   const DflashLayout L = dflash_layout(N, B, pt, nc);
   if (scratch_bytes < L.scratch)
     return fail(SPECDEC_ERR_WORKSPACE, "scratch needs %zu bytes, got %zu", L.scratch, scratch_bytes);
@@ -455,16 +545,15 @@ int specdec_dflash_forward(const float* logits, const float* target_logits, cons
   a.row_cnt = cnt + 4;
   a.nc = nc;
   a.pt = pt;
-  const int shape = kernel_shape(SPECDEC_KERNEL_DFLASH_FWD, tma);
   const cudaError_t e =
-      tma ? dflash_fwd_ring_launch(shape, a, (int)pt.grid, st) : dflash_fwd_launch(shape, a, st);
+      tma ? dflash_fwd_ring_launch(dtype, shape, a, (int)pt.grid, st) : dflash_fwd_launch(shape, a, st);
   return e == cudaSuccess ? ok() : cuda_fail(e, "dflash forward launch");
 }
 
-int specdec_dflash_backward(const float* logits, const float* target_logits, const float* scale,
-                            const float* logzq, const float* logzp, const int64_t* target_id,
-                            const float* dloss, float* dlogits, int64_t N, int32_t B, int64_t V,
-                            int32_t kind, void* counters, size_t counter_bytes, void* stream) {
+int dflash_backward_impl(int dtype, const void* logits, const void* target_logits, const float* scale,
+                         const float* logzq, const float* logzp, const int64_t* target_id, const float* dloss,
+                         void* dlogits, int64_t N, int32_t B, int64_t V, int32_t kind, void* counters,
+                         size_t counter_bytes, void* stream) {
   if (N < 0 || B < 0 || V < 0) return fail(SPECDEC_ERR_ARGUMENT, "negative shape");
   if (kind != SPECDEC_DFLASH_KL && kind != SPECDEC_DFLASH_CE)
     return fail(SPECDEC_ERR_VALUE, "unknown loss kind %d", kind);
@@ -475,12 +564,14 @@ int specdec_dflash_backward(const float* logits, const float* target_logits, con
   if (kind == SPECDEC_DFLASH_CE && !target_id) return fail(SPECDEC_ERR_ARGUMENT, "CE needs target_id");
   if (logits == dlogits || target_logits == dlogits)
     return fail(SPECDEC_ERR_ARGUMENT, "dlogits must not alias an input");
+  const bool ptrs16 = aligned(logits, 16) && aligned(dlogits, 16) &&
+                      (kind == SPECDEC_DFLASH_CE || aligned(target_logits, 16));
+  if (dtype == kDtypeBF16 && !ptrs16)
+    return fail(SPECDEC_ERR_ARGUMENT, "bf16 logits, target_logits and dlogits must be 16-byte aligned");
   const int dev = current_device();
   if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
-  const bool tma = use_tma(SPECDEC_KERNEL_DFLASH_BWD,
-                           aligned(logits, 16) && aligned(dlogits, 16) &&
-                               (kind == SPECDEC_DFLASH_CE || aligned(target_logits, 16)));
-  const int ctas = kernel_units(SPECDEC_KERNEL_DFLASH_BWD, kind, tma, dev);
+  const bool tma = dtype == kDtypeBF16 || use_tma(SPECDEC_KERNEL_DFLASH_BWD, ptrs16);
+  const int ctas = kernel_units(SPECDEC_KERNEL_DFLASH_BWD, kind, tma, dev, dtype);
   if (ctas <= 0) return fail(SPECDEC_ERR_CUDA, "occupancy query failed");
   DflashBwdArgs a;
   a.logits = logits;
@@ -499,12 +590,56 @@ int specdec_dflash_backward(const float* logits, const float* target_logits, con
   a.q_ctr = queue ? cnt : nullptr;
   a.q_retired = queue ? cnt + 1 : nullptr;
   a.q_dynamic = queue ? 1 : 0;
-  const int shape = kernel_shape(SPECDEC_KERNEL_DFLASH_BWD, tma);
-  a.pt = tma ? ring_partition(N * B, V, dflash_ring_block_elems(shape), ctas)
+  const int shape =
+      tma ? ring_shape(SPECDEC_KERNEL_DFLASH_BWD, dtype) : kernel_shape(SPECDEC_KERNEL_DFLASH_BWD, false);
+  a.pt = tma ? ring_partition(N * B, V, dflash_ring_block_elems(dtype, shape), ctas)
              : make_partition(N * B, V, ctas, kMinChunk);
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const cudaError_t e = tma ? dflash_bwd_ring_launch(shape, a, ctas, st) : dflash_bwd_launch(shape, a, st);
+  const cudaError_t e =
+      tma ? dflash_bwd_ring_launch(dtype, shape, a, ctas, st) : dflash_bwd_launch(shape, a, st);
   return e == cudaSuccess ? ok() : cuda_fail(e, "dflash backward launch");
+}
+
+}  // namespace
+
+extern "C" {
+
+int specdec_dflash_forward(const float* logits, const float* target_logits, const float* mask,
+                           int64_t N, int32_t B, int64_t V, int32_t block_size, float gamma,
+                           int32_t sample_from_anchor, int32_t kind, int64_t n_global, float* loss,
+                           float* loss_rows, float* scale, float* logzq, float* logzp,
+                           int64_t* target_id, void* scratch, size_t scratch_bytes, void* counters,
+                           size_t counter_bytes, void* stream) {
+  return dflash_forward_impl(kDtypeF32, logits, target_logits, mask, N, B, V, block_size, gamma,
+                             sample_from_anchor, kind, n_global, loss, loss_rows, scale, logzq, logzp, target_id,
+                             scratch, scratch_bytes, counters, counter_bytes, stream);
+}
+
+int specdec_dflash_forward_bf16(const uint16_t* logits, const uint16_t* target_logits, const float* mask,
+                                int64_t N, int32_t B, int64_t V, int32_t block_size, float gamma,
+                                int32_t sample_from_anchor, int32_t kind, int64_t n_global, float* loss,
+                                float* loss_rows, float* scale, float* logzq, float* logzp,
+                                int64_t* target_id, void* scratch, size_t scratch_bytes, void* counters,
+                                size_t counter_bytes, void* stream) {
+  return dflash_forward_impl(kDtypeBF16, logits, target_logits, mask, N, B, V, block_size, gamma,
+                             sample_from_anchor, kind, n_global, loss, loss_rows, scale, logzq, logzp, target_id,
+                             scratch, scratch_bytes, counters, counter_bytes, stream);
+}
+
+int specdec_dflash_backward(const float* logits, const float* target_logits, const float* scale,
+                            const float* logzq, const float* logzp, const int64_t* target_id,
+                            const float* dloss, float* dlogits, int64_t N, int32_t B, int64_t V,
+                            int32_t kind, void* counters, size_t counter_bytes, void* stream) {
+  return dflash_backward_impl(kDtypeF32, logits, target_logits, scale, logzq, logzp, target_id, dloss, dlogits,
+                              N, B, V, kind, counters, counter_bytes, stream);
+}
+
+int specdec_dflash_backward_bf16(const uint16_t* logits, const uint16_t* target_logits, const float* scale,
+                                 const float* logzq, const float* logzp, const int64_t* target_id,
+                                 const float* dloss, uint16_t* dlogits, int64_t N, int32_t B, int64_t V,
+                                 int32_t kind, void* counters, size_t counter_bytes, void* stream) {
+  return dflash_backward_impl(kDtypeBF16, logits, target_logits, scale, logzq, logzp, target_id, dloss,
+                              dlogits, N, B, V, kind, counters, counter_bytes, stream);
 }
 
 }  // extern "C"

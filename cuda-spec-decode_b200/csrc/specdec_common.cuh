@@ -66,6 +66,52 @@ __device__ __forceinline__ float max4(const float4& v) {
 }
 
 // ---------------------------------------------------------------------------
+// bfloat16 elements travel as their 16-bit patterns (bf16_t). Widening to
+// float is exact (the pattern is the upper half of the float's); narrowing
+// rounds to nearest even in hardware (cvt.rn.bf16[x2].f32). All arithmetic
+// is float.
+// ---------------------------------------------------------------------------
+using bf16_t = uint16_t;
+
+__device__ __forceinline__ float to_f32(float x) { return x; }
+__device__ __forceinline__ float to_f32(bf16_t x) { return __uint_as_float(uint32_t(x) << 16); }
+// The two elements of a bf16x2 word: the lower address is the low half.
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+__device__ __forceinline__ float ldg_f32(const float* p) { return __ldg(p); }
+__device__ __forceinline__ float ldg_f32(const bf16_t* p) { return to_f32(__ldg(p)); }
+
+// Elementwise max of two bf16x2 words (NaN loses against a number, like fmaxf).
+__device__ __forceinline__ uint32_t bmax2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bmax8(const uint4& v) { return bmax2(bmax2(v.x, v.y), bmax2(v.z, v.w)); }
+
+// Packs round-to-nearest-even bf16(lo) | bf16(hi) << 16.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+__device__ __forceinline__ void store_elem(float* p, float v) { *p = v; }
+__device__ __forceinline__ void store_elem(bf16_t* p, float v) {
+  unsigned short h;
+  asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(h) : "f"(v));
+  *p = h;
+}
+
+// Streaming 128-bit store of raw words (cache-streaming, evict-first).
+__device__ __forceinline__ void st_stream_u4(void* p, uint4 v) {
+  asm volatile("st.global.cs.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
+// ---------------------------------------------------------------------------
 // Online log-sum-exp: the state (m, s) stands for s * e^m with m the running
 // max; each element contributes e^(x - m) = 2^((x - m) * log2 e) (FADD, FMUL,
 // MUFU.EX2). The max element contributes exactly 1, as in torch's

@@ -16,6 +16,10 @@ constexpr int kStatusTargetRange = 3;  // equals SPECDEC_ERR_TARGET_RANGE in inc
 constexpr int kKindKL = 0;
 constexpr int kKindCE = 1;
 
+// Element type of the logits (and of the gradient written for them).
+constexpr int kDtypeF32 = 0;
+constexpr int kDtypeBF16 = 1;
+
 // Per-piece partial of the DFlash forward (32 bytes, two float4 stores).
 struct alignas(16) DfPiece {
   float m2q, sq, m2p, sp, t, bx, bl;
@@ -23,7 +27,7 @@ struct alignas(16) DfPiece {
 };
 
 struct DpaceFwdArgs {
-  const float* logits;     // [N, B, V]
+  const void* logits;      // [N, B, V] float, or bf16 for the bf16 ring kernels
   const int64_t* targets;  // [N, B]
   const float* mask;       // [N, B] or null (all positions scored); scored iff > 0
   int64_t N;               // sequences in this launch
@@ -49,16 +53,17 @@ struct DpaceFwdArgs {
   unsigned* q_retired;     // [1]
   int q_dynamic;           // 1: atomic block queue, 0: static interleave
   int nc;                  // partials per (row, slot): consumer warps (ring) or 1
+  int withhold_stage;      // failure-detection tests: CTA 0 never posts its first stage
   Partition pt;            // ring kernel: chunk = block length, pmax from it
 };
 
 struct DpaceBwdArgs {
-  const float* logits;
+  const void* logits;      // element type as the forward's
   const int64_t* targets;
   const float* lse;
   const float* scale;
   const float* dloss;      // [1] upstream gradient, or null for 1
-  float* dlogits;
+  void* dlogits;           // element type of logits
   int* flag;               // [1] or null: bit 2 set if a copy wait timed out
   unsigned* q_ctr;         // ring kernel block queue (null: static interleave)
   unsigned* q_retired;
@@ -67,8 +72,8 @@ struct DpaceBwdArgs {
 };
 
 struct DflashFwdArgs {
-  const float* logits;         // draft [N, B, V]
-  const float* target_logits;  // verifier [N, B, V]
+  const void* logits;          // draft [N, B, V] (float, or bf16 for the bf16 ring kernels)
+  const void* target_logits;   // verifier [N, B, V], same element type
   const float* mask;           // [N, B] raw float mask, or null for all ones
   int64_t N;
   int B;
@@ -99,14 +104,14 @@ struct DflashFwdArgs {
 };
 
 struct DflashBwdArgs {
-  const float* logits;
-  const float* target_logits;  // read for KL only
+  const void* logits;
+  const void* target_logits;   // read for KL only
   const float* scale;
   const float* logzq;
   const float* logzp;
   const int64_t* target_id;    // read for CE only
   const float* dloss;
-  float* dlogits;
+  void* dlogits;               // element type of logits
   int kind;
   int* flag;                   // [1] or null
   unsigned* q_ctr;             // ring kernel block queue (null: static interleave)
@@ -122,21 +127,23 @@ int dpace_bwd_ctas(int shape, int device, int cap_per_sm);
 cudaError_t dpace_fwd_launch(int shape, const DpaceFwdArgs& a, cudaStream_t st);
 cudaError_t dpace_bwd_launch(int shape, const DpaceBwdArgs& a, cudaStream_t st);
 
-// Warp-specialized ring kernels (dpace_ring.cu); sizes in CTAs.
-int dpace_ring_block_elems(int shape);
+// Warp-specialized ring kernels (dpace_ring.cu); sizes in CTAs. `dtype` is
+// kDtypeF32 or kDtypeBF16; a bf16 shape moves the same bytes per stage as the
+// float shape of the same number (twice the elements).
+int dpace_ring_block_elems(int dtype, int shape);
 int dpace_ring_consumers(int shape);
-int dpace_fwd_ring_ctas(int shape, int device, int cap_per_sm);
-int dpace_bwd_ring_ctas(int shape, int device, int cap_per_sm);
-cudaError_t dpace_fwd_ring_launch(int shape, const DpaceFwdArgs& a, int ctas, cudaStream_t st);
-cudaError_t dpace_bwd_ring_launch(int shape, const DpaceBwdArgs& a, int ctas, cudaStream_t st);
+int dpace_fwd_ring_ctas(int dtype, int shape, int device, int cap_per_sm);
+int dpace_bwd_ring_ctas(int dtype, int shape, int device, int cap_per_sm);
+cudaError_t dpace_fwd_ring_launch(int dtype, int shape, const DpaceFwdArgs& a, int ctas, cudaStream_t st);
+cudaError_t dpace_bwd_ring_launch(int dtype, int shape, const DpaceBwdArgs& a, int ctas, cudaStream_t st);
 
 // Warp-specialized ring kernels (dflash_ring.cu); sizes in CTAs.
-int dflash_ring_block_elems(int shape);
+int dflash_ring_block_elems(int dtype, int shape);
 int dflash_ring_consumers(int shape);
-int dflash_fwd_ring_ctas(int kind, int shape, int device, int cap_per_sm);
-int dflash_bwd_ring_ctas(int kind, int shape, int device, int cap_per_sm);
-cudaError_t dflash_fwd_ring_launch(int shape, const DflashFwdArgs& a, int ctas, cudaStream_t st);
-cudaError_t dflash_bwd_ring_launch(int shape, const DflashBwdArgs& a, int ctas, cudaStream_t st);
+int dflash_fwd_ring_ctas(int dtype, int kind, int shape, int device, int cap_per_sm);
+int dflash_bwd_ring_ctas(int dtype, int kind, int shape, int device, int cap_per_sm);
+cudaError_t dflash_fwd_ring_launch(int dtype, int shape, const DflashFwdArgs& a, int ctas, cudaStream_t st);
+cudaError_t dflash_bwd_ring_launch(int dtype, int shape, const DflashBwdArgs& a, int ctas, cudaStream_t st);
 
 // Sets the calling thread's specdec_last_error() text.
 void set_last_error(const char* msg);

@@ -15,6 +15,11 @@ The math follows the torch oracle losses/dpace_ref.py:8-51:
     loss   = sum_{n,j} w_j ce_j / N
     dL/dx  = (w_j / N) * (softmax(x_j) - onehot(target_j))     (w detached)
 computed by the sm_100a kernels in libspecdec.so; there is no other path.
+
+Beyond the reference (whose kernels take fp32 only, README.md:263): logits may
+also be bfloat16. The kernels widen every element exactly and compute in
+fp32, so the loss is the fp32 loss of the widened logits; the gradient is
+returned in bfloat16 (rounded to nearest even), like the logits.
 """
 from __future__ import annotations
 
@@ -32,7 +37,7 @@ def _check(logits: torch.Tensor, targets: torch.Tensor, mask: torch.Tensor | Non
     The target range check (dpace.py:171-173) runs inside the forward kernel
     and is raised after it as ValueError.
     """
-    assert logits.ndim == 3 and logits.dtype == torch.float32, "logits must be float32 [N, B, V]"
+    assert logits.ndim == 3 and logits.dtype in ops.LOGIT_DTYPES, "logits must be float32 (or bfloat16) [N, B, V]"
     assert targets.shape == logits.shape[:2] and targets.dtype == torch.int64, \
         "targets must be int64 [N, B]"
     assert mask is None or (mask.shape == logits.shape[:2] and mask.dtype == torch.float32), \
@@ -50,7 +55,7 @@ def _check(logits: torch.Tensor, targets: torch.Tensor, mask: torch.Tensor | Non
 
 
 def _prepare(logits, targets, position_mask):
-    assert logits.is_cuda and logits.dtype == torch.float32, "logits must be float32 cuda"
+    assert logits.is_cuda and logits.dtype in ops.LOGIT_DTYPES, "logits must be float32 (or bfloat16) cuda"
     assert targets.dtype == torch.int64, "targets must be int64"
     logits = logits.detach().contiguous()
     targets = targets.detach().contiguous()
@@ -65,7 +70,7 @@ def _forward(logits, targets, mask, alpha, loss_type, n_global=None):
     _check(logits, targets, mask, alpha, loss_type)
     if logits.shape[0] == 0:
         nan = torch.full((), float("nan"), dtype=torch.float32, device=logits.device)
-        empty = logits.new_zeros(logits.shape[:2])
+        empty = torch.zeros(logits.shape[:2], dtype=torch.float32, device=logits.device)
         return nan, empty, empty
     loss, lse, scale, _ = ops.dpace_forward(logits, targets, mask, alpha, _LOSS_TYPES[loss_type],
                                             n_global=n_global)
@@ -74,7 +79,7 @@ def _forward(logits, targets, mask, alpha, loss_type, n_global=None):
 
 def fused_dpace_loss(logits: torch.Tensor, targets: torch.Tensor, alpha: float = 0.5,
                      position_mask=None, loss_type: str = "dpace") -> torch.Tensor:
-    """Forward-only D-PACE loss (eval). logits [N,B,V] float32 CUDA, targets [N,B] int64."""
+    """Forward-only D-PACE loss (eval). logits [N,B,V] float32 (or bfloat16) CUDA, targets [N,B] int64."""
     logits, targets, mask = _prepare(logits, targets, position_mask)
     return _forward(logits, targets, mask, alpha, loss_type)[0]
 
@@ -102,7 +107,7 @@ class DPACELoss(torch.autograd.Function):
 def dpace_loss(logits, targets, alpha: float = 0.5, position_mask=None, loss_type: str = "dpace"):
     """D-PACE loss for torch tensors, with autograd.
 
-    logits [N,B,V] float32 cuda, targets [N,B] int64, position_mask [N,B] bool/float or None.
+    logits [N,B,V] float32 (or bfloat16) cuda, targets [N,B] int64, position_mask [N,B] bool/float or None.
     Returns sum(w*ce)/N as a 0-d float32 tensor.
     """
     return DPACELoss.apply(logits, targets, alpha, position_mask, loss_type)

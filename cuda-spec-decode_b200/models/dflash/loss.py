@@ -18,6 +18,11 @@ models/dflash/tests/test_loss.py:21-49:
 The decay index is j % block_size as in the oracle (test_loss.py:62); the
 reference kernel indexes (n*B + j) % block_size (loss.py:115-116), which
 differs only when B is not a multiple of block_size.
+
+Beyond the reference (fp32 only, README.md:263): logits and target_logits may
+also be bfloat16. The kernels widen every element exactly and compute in fp32;
+the gradient comes back in the logits' dtype (bf16 rounded to nearest even).
+When the two dtypes differ, the bf16 one is widened to fp32 first (exact).
 """
 from __future__ import annotations
 
@@ -30,9 +35,9 @@ _KINDS = ops.DFLASH_KINDS
 
 def _check(logits, target_logits, mask, gamma, kind, block_size) -> None:
     """Host checks in the reference's order (models/dflash/loss.py:178-191)."""
-    assert logits.ndim == 3 and logits.dtype == torch.float32, "logits must be float32 [N, B, V]"
-    assert target_logits.shape == logits.shape and target_logits.dtype == torch.float32, \
-        "target_logits must be float32 [N, B, V]"
+    assert logits.ndim == 3 and logits.dtype in ops.LOGIT_DTYPES, "logits must be float32 (or bfloat16) [N, B, V]"
+    assert target_logits.shape == logits.shape and target_logits.dtype == logits.dtype, \
+        "target_logits must be [N, B, V] of the logits' dtype"
     assert mask is None or (mask.shape == logits.shape[:2] and mask.dtype == torch.float32), \
         "loss_mask must be float32 [N, B]"
     N, B, V = logits.shape
@@ -46,10 +51,15 @@ def _check(logits, target_logits, mask, gamma, kind, block_size) -> None:
 
 
 def _prepare(logits, target_logits, loss_mask):
-    assert logits.is_cuda and logits.dtype == torch.float32, "logits must be float32 cuda"
+    assert logits.is_cuda and logits.dtype in ops.LOGIT_DTYPES, "logits must be float32 (or bfloat16) cuda"
     assert target_logits.shape == logits.shape, "target_logits must match logits' shape"
-    logits = logits.detach().contiguous()
-    target_logits = target_logits.detach().to(logits.device).contiguous()
+    assert target_logits.dtype in ops.LOGIT_DTYPES, "target_logits must be float32 (or bfloat16)"
+    logits = logits.detach()
+    target_logits = target_logits.detach().to(logits.device)
+    if target_logits.dtype != logits.dtype:  # mixed: widen the bf16 one (exact)
+        logits, target_logits = logits.float(), target_logits.float()
+    logits = logits.contiguous()
+    target_logits = target_logits.contiguous()
     mask = None
     if loss_mask is not None:
         mask = loss_mask.detach().to(device=logits.device, dtype=torch.float32).contiguous()
@@ -70,7 +80,7 @@ def _forward(logits, target_logits, mask, gamma, sample_from_anchor, kind, block
 def fused_dflash_loss(logits, target_logits, loss_mask=None, gamma: float = 4.0,
                       sample_from_anchor: bool = False, kind: str = "kl",
                       block_size: int | None = None) -> torch.Tensor:
-    """Forward-only DFlash loss (eval). logits/target_logits [N,B,V] float32 CUDA."""
+    """Forward-only DFlash loss (eval). logits/target_logits [N,B,V] float32 (or bfloat16) CUDA."""
     x, xt, mask = _prepare(logits, target_logits, loss_mask)
     return _forward(x, xt, mask, gamma, sample_from_anchor, kind, block_size)[0]
 
@@ -113,7 +123,7 @@ def dflash_loss(logits, target_logits, loss_mask=None, gamma: float = 4.0,
                 block_size: int | None = None):
     """DFlash loss for torch tensors, with autograd.
 
-    logits / target_logits: [N,B,V] float32 cuda. loss_mask: [N,B] bool/float or None.
+    logits / target_logits: [N,B,V] float32 (or bfloat16) cuda. loss_mask: [N,B] bool/float or None.
     kind="kl" (speculators default) or "ce" (hard argmax(target) labels).
     """
     return DFlashLoss.apply(logits, target_logits, loss_mask, gamma, sample_from_anchor, kind,

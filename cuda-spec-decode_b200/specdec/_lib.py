@@ -63,7 +63,12 @@ _SIGNATURES = {
     "specdec_set_launch_shape": (ctypes.c_int, [_c_i32, _c_i32, _c_i32]),
     "specdec_launch_ctas": (_c_i64, [_c_i32, _c_i64, _c_i64, ctypes.c_int]),
     "specdec_set_block_queue": (ctypes.c_int, [_c_i32]),
+    "specdec_test_withhold_stage": (ctypes.c_int, [_c_i32]),
 }
+# bf16 entry points take the same arguments as their fp32 counterparts
+for _name in ("specdec_dpace_forward", "specdec_dpace_backward", "specdec_dflash_forward",
+              "specdec_dflash_backward"):
+    _SIGNATURES[_name + "_bf16"] = _SIGNATURES[_name]
 
 _lib = None
 _lib_lock = threading.Lock()

@@ -34,6 +34,35 @@ def allreduce_loss(partial: torch.Tensor, group=None) -> torch.Tensor:
     return partial + (total - partial.detach())
 
 
+class LossReducer:
+    """The 4-byte loss all_reduce on a side stream, off the compute stream's
+    critical path.
+
+    The backward needs only this rank's scale (dloss = 1 for the partial), never
+    the global loss, so the collective can run while the backward kernel
+    streams. start(partial) after the forward returns the tensor that will hold
+    the global loss; wait() makes the current stream wait for it (call it
+    before anything reads that tensor, e.g. at the end of the step). Every
+    rank must call start/wait in the same order, like any collective.
+    """
+
+    def __init__(self, device, group=None):
+        self.device = torch.device(device)
+        self.stream = torch.cuda.Stream(device=self.device)
+        self.group = group
+
+    def start(self, partial: torch.Tensor) -> torch.Tensor:
+        total = partial.detach().clone()
+        self.stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(self.stream):
+            dist.all_reduce(total, op=dist.ReduceOp.SUM, group=self.group)
+        total.record_stream(self.stream)
+        return total
+
+    def wait(self) -> None:
+        torch.cuda.current_stream(self.device).wait_stream(self.stream)
+
+
 def sharded_dpace_loss(logits, targets, alpha: float = 0.5, position_mask=None,
                        loss_type: str = "dpace", n_global: int | None = None, group=None):
     """dpace_loss over a batch split by sequence across ranks. `logits` etc. are

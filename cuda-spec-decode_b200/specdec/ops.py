@@ -30,6 +30,23 @@ def set_target_validation(enabled: bool) -> None:
     VALIDATE_TARGETS = bool(enabled)
 
 
+# Element types of the logits the kernels take; the gradient has the logits'
+# type. bf16 calls go to the *_bf16 entry points (fp32 arithmetic inside).
+LOGIT_DTYPES = (torch.float32, torch.bfloat16)
+
+
+def _entry(lib, name: str, t: torch.Tensor):
+    return getattr(lib, name + "_bf16") if t.dtype == torch.bfloat16 else getattr(lib, name)
+
+
+def _aligned(t: torch.Tensor | None) -> torch.Tensor | None:
+    """bf16 tensors must start on a 16-byte boundary (the bulk copies need it);
+    a view that does not is copied once."""
+    if t is None or t.dtype != torch.bfloat16 or t.data_ptr() % 16 == 0:
+        return t
+    return t.clone()
+
+
 def _dpace_forward(logits: torch.Tensor, targets: torch.Tensor, mask: torch.Tensor | None,
                   alpha: float, loss_type: int, n_global: int | None = None,
                   want_loss_n: bool = False, validate: bool | None = None):
@@ -47,7 +64,8 @@ def _dpace_forward(logits: torch.Tensor, targets: torch.Tensor, mask: torch.Tens
     sb = lib.specdec_dpace_scratch_bytes(N, B, V, dev.index)
     cb = lib.specdec_dpace_counter_bytes(N, B)
     scratch, counters = ws.ensure(dev, sb, cb)
-    code = lib.specdec_dpace_forward(
+    logits = _aligned(logits)
+    code = _entry(lib, "specdec_dpace_forward", logits)(
         logits.data_ptr(), targets.data_ptr(), _lib.ptr(mask), N, B, V, float(alpha),
         int(loss_type), n_global, loss.data_ptr(), _lib.ptr(loss_n), lse.data_ptr(),
         scale.data_ptr(), status.data_ptr(), scratch.data_ptr(), scratch.numel(),
@@ -69,12 +87,13 @@ def _dpace_backward(logits: torch.Tensor, targets: torch.Tensor, lse: torch.Tens
     lib = _lib.load()
     N, B, V = logits.shape
     dev = logits.device
+    logits = _aligned(logits)
     dlogits = torch.empty_like(logits) if out is None else out
     if dloss is not None:
         dloss = dloss.detach().to(device=dev, dtype=torch.float32).contiguous()
     cb = lib.specdec_backward_counter_bytes()
     _, counters = _lib.workspace("dpace_bwd", dev).ensure(dev, 256, cb)
-    code = lib.specdec_dpace_backward(
+    code = _entry(lib, "specdec_dpace_backward", logits)(
         logits.data_ptr(), targets.data_ptr(), lse.data_ptr(), scale.data_ptr(),
         _lib.ptr(dloss), dlogits.data_ptr(), N, B, V, counters.data_ptr(), counters.numel(),
         _lib.stream_handle(dev))
@@ -100,7 +119,8 @@ def _dflash_forward(logits: torch.Tensor, target_logits: torch.Tensor, mask: tor
     sb = lib.specdec_dflash_scratch_bytes(N, B, V, dev.index)
     cb = lib.specdec_dflash_counter_bytes(N, B)
     scratch, counters = ws.ensure(dev, sb, cb)
-    code = lib.specdec_dflash_forward(
+    logits, target_logits = _aligned(logits), _aligned(target_logits)
+    code = _entry(lib, "specdec_dflash_forward", logits)(
         logits.data_ptr(), target_logits.data_ptr(), _lib.ptr(mask), N, B, V, int(block_size),
         float(gamma), int(bool(sample_from_anchor)), int(kind), n_global, loss.data_ptr(),
         loss_rows.data_ptr(), scale.data_ptr(), logzq.data_ptr(), logzp.data_ptr(),
@@ -117,12 +137,13 @@ def _dflash_backward(logits: torch.Tensor, target_logits: torch.Tensor | None, s
     lib = _lib.load()
     N, B, V = logits.shape
     dev = logits.device
+    logits, target_logits = _aligned(logits), _aligned(target_logits)
     dlogits = torch.empty_like(logits) if out is None else out
     if dloss is not None:
         dloss = dloss.detach().to(device=dev, dtype=torch.float32).contiguous()
     cb = lib.specdec_backward_counter_bytes()
     _, counters = _lib.workspace("dflash_bwd", dev).ensure(dev, 256, cb)
-    code = lib.specdec_dflash_backward(
+    code = _entry(lib, "specdec_dflash_backward", logits)(
         logits.data_ptr(), _lib.ptr(target_logits), scale.data_ptr(), logzq.data_ptr(),
         logzp.data_ptr(), _lib.ptr(tgt), _lib.ptr(dloss), dlogits.data_ptr(), N, B, V, int(kind),
         counters.data_ptr(), counters.numel(), _lib.stream_handle(dev))

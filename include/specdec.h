@@ -1,8 +1,8 @@
 /*
  * specdec.h -- C ABI of the B200 drafter-loss library (libspecdec.so).
  *
- * Fused training losses for speculative-decoding drafters over fp32 logits
- * [N, B, V] (N sequences, B <= 32 draft positions, V vocabulary):
+ * Fused training losses for speculative-decoding drafters over fp32 (or
+ * bf16) logits [N, B, V] (N sequences, B draft positions, V vocabulary):
  *   - D-PACE: cross entropy weighted by the detached, alpha-smoothed
  *     acceptance prefix/suffix scan of each sequence;
  *   - DFlash: KL(softmax(verifier) || softmax(draft)) or CE against
@@ -179,6 +179,43 @@ int specdec_dflash_backward(const float* logits, const float* target_logits, con
                             int32_t kind, void* counters, size_t counter_bytes, void* stream);
 
 /* ------------------------------------------------------------------------- */
+/* bfloat16 logits                                                            */
+/* ------------------------------------------------------------------------- */
+
+/*
+ * bf16 variants of the four entry points above. No counterpart in the
+ * reference, whose kernels take fp32 only (README.md:263, asserted by
+ * losses/dpace.py:158 and models/dflash/loss.py:179): `logits`,
+ * `target_logits` and `dlogits` hold bfloat16 values as their 16-bit
+ * patterns; everything else (mask, per-row outputs, loss, workspace) is as
+ * in the fp32 entry point of the same name, and the workspace sizes queried
+ * for fp32 cover bf16. Every element is widened exactly to fp32 and all
+ * arithmetic is fp32, so the loss and per-row outputs equal the fp32 entry
+ * point's on the widened logits; the backward writes each gradient element
+ * rounded to nearest even. logits, target_logits and dlogits must be
+ * 16-byte aligned (SPECDEC_ERR_ARGUMENT otherwise).
+ */
+int specdec_dpace_forward_bf16(const uint16_t* logits, const int64_t* targets, const float* mask,
+                               int64_t N, int32_t B, int64_t V, float alpha, int32_t loss_type,
+                               int64_t n_global, float* loss, float* loss_n, float* lse, float* scale,
+                               int32_t* status, void* scratch, size_t scratch_bytes, void* counters,
+                               size_t counter_bytes, void* stream);
+int specdec_dpace_backward_bf16(const uint16_t* logits, const int64_t* targets, const float* lse,
+                                const float* scale, const float* dloss, uint16_t* dlogits, int64_t N,
+                                int32_t B, int64_t V, void* counters, size_t counter_bytes,
+                                void* stream);
+int specdec_dflash_forward_bf16(const uint16_t* logits, const uint16_t* target_logits, const float* mask,
+                                int64_t N, int32_t B, int64_t V, int32_t block_size, float gamma,
+                                int32_t sample_from_anchor, int32_t kind, int64_t n_global, float* loss,
+                                float* loss_rows, float* scale, float* logzq, float* logzp,
+                                int64_t* target_id, void* scratch, size_t scratch_bytes, void* counters,
+                                size_t counter_bytes, void* stream);
+int specdec_dflash_backward_bf16(const uint16_t* logits, const uint16_t* target_logits, const float* scale,
+                                 const float* logzq, const float* logzp, const int64_t* target_id,
+                                 const float* dloss, uint16_t* dlogits, int64_t N, int32_t B, int64_t V,
+                                 int32_t kind, void* counters, size_t counter_bytes, void* stream);
+
+/* ------------------------------------------------------------------------- */
 /* Launch tuning                                                              */
 /* ------------------------------------------------------------------------- */
 
@@ -206,6 +243,17 @@ int64_t specdec_launch_ctas(int32_t kernel, int64_t rows, int64_t V, int device)
  * default) or a static interleave (dynamic = 0), process-wide.
  */
 int specdec_set_block_queue(int32_t dynamic);
+
+/*
+ * Failure-detection test hook (no counterpart in the reference). The next
+ * `launches` D-PACE forward launches on the ring path make CTA 0's producer
+ * withhold its first stage, so that CTA's consumers reach the 1 s limit of
+ * their bounded wait: they record the timeout, wait (bounded) for their own
+ * copies, and return. The launch completes in about 2 s with *status =
+ * SPECDEC_ERR_CUDA and unspecified loss values; the context stays usable and
+ * the next launch is normal. 0 cancels. Not for production use.
+ */
+int specdec_test_withhold_stage(int32_t launches);
 
 #ifdef __cplusplus
 }

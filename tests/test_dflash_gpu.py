@@ -245,9 +245,9 @@ def test_static_interleave_and_schedule_independence(cuda):
     _lib.set_block_queue(True)
 
 
-def test_large_block_size_falls_back(cuda):
-    """B > 32 positions per sequence (allowed by the reference) runs on the
-    128-bit-load kernels; results match the oracle."""
+def test_more_than_32_positions(cuda):
+    """B > 32 positions per sequence (allowed by the reference): the ring
+    finalize loops over rows; results match the oracle."""
     from models.dflash import dflash_loss
 
     rng = np.random.default_rng(40)
