@@ -239,17 +239,23 @@ def time_pair(args, stream, world, max_over_ranks, barrier, fwd, bwd, steps):
 
     for i in range(args.warmup):
         step(i)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+    # the step time comes from an uninstrumented loop (events between kernels
+    # would break the programmatic-dependent-launch chaining of the kernels)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
     a.record(stream)
     for k in range(steps):
-        step(k, evs[k])
+        step(k)
     b.record(stream)
     torch.cuda.synchronize()
     barrier()
     ms = max_over_ranks(a.elapsed_time(b)) / steps
+    # per-kernel split from a second, instrumented pass
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+    for k in range(steps):
+        step(k, evs[k])
+    torch.cuda.synchronize()
     f = max_over_ranks(statistics.mean(e[0].elapsed_time(e[1]) for e in evs))
     g = max_over_ranks(statistics.mean(e[2].elapsed_time(e[3]) for e in evs))
     return ms, f, g
@@ -546,18 +552,24 @@ def run_ours(args):
         if i % 64 == 0:
             torch.cuda.synchronize(dev)
 
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    # timed region: K uninstrumented steps (events between the kernels would
+    # break their programmatic-dependent-launch chaining)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize(dev)
     start.record(stream)
     for k in range(args.steps):
-        step(k, evs[k])
+        step(k)
     stop.record(stream)
     torch.cuda.synchronize(dev)
     barrier()
     clocks = sampler.stop()
     ms_local = start.elapsed_time(stop)
+    # per-kernel split (roofline): a second pass with events around each kernel
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    for k in range(args.steps):
+        step(k, evs[k])
+    torch.cuda.synchronize(dev)
     fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
     bwd_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in evs)
     ms = max_over_ranks(ms_local)

@@ -176,15 +176,10 @@ __device__ __forceinline__ void df_group(DfState& s, const uint4 (&a)[U], const 
     s.mq = cma;
   }
   const float mq = s.mq;
-  float accq = 0.f;
+  float2 accq = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int u = 0; u < U; ++u) {
-    accq += ((exp_shift(bf16_lo(a[u].x), mq) + exp_shift(bf16_hi(a[u].x), mq)) +
-             (exp_shift(bf16_lo(a[u].y), mq) + exp_shift(bf16_hi(a[u].y), mq))) +
-            ((exp_shift(bf16_lo(a[u].z), mq) + exp_shift(bf16_hi(a[u].z), mq)) +
-             (exp_shift(bf16_lo(a[u].w), mq) + exp_shift(bf16_hi(a[u].w), mq)));
-  }
-  s.sq += accq;
+  for (int u = 0; u < U; ++u) accq = fadd2(accq, vec8_expsum2(a[u], mq));
+  s.sq += accq.x + accq.y;
   uint32_t pb = bmax8(b[0]);
 #pragma unroll
   for (int u = 1; u < U; ++u) pb = bmax2(pb, bmax8(b[u]));
@@ -197,23 +192,21 @@ __device__ __forceinline__ void df_group(DfState& s, const uint4 (&a)[U], const 
       s.mp = cmb;
     }
     const float mp = s.mp;
-    float accp = 0.f, acct = 0.f;
+    float2 accp = make_float2(0.f, 0.f), acct = make_float2(0.f, 0.f);
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const uint32_t wa[4] = {a[u].x, a[u].y, a[u].z, a[u].w};
       const uint32_t wb[4] = {b[u].x, b[u].y, b[u].z, b[u].w};
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
-        const float xl0 = bf16_lo(wa[h]), xl1 = bf16_hi(wa[h]);
-        const float xt0 = bf16_lo(wb[h]), xt1 = bf16_hi(wb[h]);
-        const float e0 = exp_shift(xt0, mp), e1 = exp_shift(xt1, mp);
-        accp += e0 + e1;
-        acct = fmaf(e0, xt0 - xl0, acct);
-        acct = fmaf(e1, xt1 - xl1, acct);
+        const float2 xl = bf16x2_f32(wa[h]), xt = bf16x2_f32(wb[h]);
+        const float2 e = exp_shift2(xt, mp);
+        accp = fadd2(accp, e);
+        acct = ffma2(e, fsub2(xt, xl), acct);
       }
     }
-    s.sp += accp;
-    s.t += acct;
+    s.sp += accp.x + accp.y;
+    s.t += acct.x + acct.y;
   } else {
     if (cmb > s.bx) {
       // first element of the group equal to its max, in index order

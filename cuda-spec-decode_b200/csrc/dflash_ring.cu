@@ -66,6 +66,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<2, S, SE, T>()))
   const int pmax = a.pt.pmax;
 
   ring_init(sm, NC);
+  pdl_wait();  // no global memory access before the previous kernel has completed
   const RowBits rb = build_row_bits(sm.bits, R, NC + 1, [&](int64_t r) { return dr_numer(a, r) != 0.f; });
   __syncthreads();
 
@@ -184,15 +185,17 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<2, S, SE, T>()))
 template <class T, int KIND>
 __global__ void __launch_bounds__(1024) dflash_finalize_kernel(const __grid_constant__ DflashFwdArgs a) {
   __shared__ float sh_loss[32];
-  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   const int B = a.B;
   const int64_t n = blockIdx.x, V = a.pt.V, BL = a.pt.chunk;
   const int NC = a.nc;
-  // denominator: sum of the sequence's raw mask values + 1e-5
+  pdl_trigger();  // the backward may become resident now (it waits for this grid)
+  // denominator: sum of the sequence's raw mask values + 1e-5 (the mask is
+  // not written by the streaming grid: read it while that grid drains)
   float mv = 0.f;
   for (int i = lane; i < B; i += 32) mv += a.mask ? a.mask[n * B + i] : 1.f;
   const float denom = warp_sum(mv) + 1e-5f;
+  pdl_wait();  // the streaming grid has completed and its stores are visible
   float acc = 0.f;  // this warp's rows, in row order
   for (int j = warp; j < B; j += nwarps) {
     const int64_t r = n * B + j;
@@ -278,9 +281,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<(KIND == kKindKL
   T* dst = static_cast<T*>(a.dlogits);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t E = a.pt.E, V = a.pt.V, R = E / V;
-  const float g = a.dloss ? __ldg(a.dloss) : 1.f;
-
   ring_init(sm, NC);
+  pdl_wait();  // no global memory access before the previous kernel has completed
+  const float g = a.dloss ? __ldg(a.dloss) : 1.f;
   const RowBits rb = build_row_bits(sm.bits, R, NC + 1, [&](int64_t r) { return __fmul_rn(a.scale[r], g) != 0.f; });
   __syncthreads();
 
@@ -397,30 +400,32 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<(KIND == kKindKL
             const uint4* s4 = reinterpret_cast<const uint4*>(sl + (lov - f0));
             const uint4* t4 = reinterpret_cast<const uint4*>(sx + (lov - f0));
             const int64_t tq = tf - lov;
+            const float2 sc2 = make_float2(sc, sc);
             for (int k = lane; k < nv; k += 32) {
               const uint4 v = s4[k];
               const uint32_t wl[4] = {v.x, v.y, v.z, v.w};
-              float y[8];
+              float2 q[4], y[4];
 #pragma unroll
-              for (int h = 0; h < 4; ++h) {
-                y[2 * h] = exp_shift(bf16_lo(wl[h]), lq);
-                y[2 * h + 1] = exp_shift(bf16_hi(wl[h]), lq);
-              }
+              for (int h = 0; h < 4; ++h) q[h] = exp_shift2(bf16x2_f32(wl[h]), lq);
               if (KIND == kKindKL) {
                 const uint4 u = t4[k];
                 const uint32_t wt[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                  y[2 * h] -= exp_shift(bf16_lo(wt[h]), lp);
-                  y[2 * h + 1] -= exp_shift(bf16_hi(wt[h]), lp);
-                }
+                for (int h = 0; h < 4; ++h) y[h] = fmul2(fsub2(q[h], exp_shift2(bf16x2_f32(wt[h]), lp)), sc2);
               } else {
-                const uint64_t d = (uint64_t)(tq - 8 * (int64_t)k);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) y[e] -= d == (uint64_t)e ? 1.f : 0.f;
+                for (int h = 0; h < 4; ++h) y[h] = fmul2(q[h], sc2);
+                const uint64_t d = (uint64_t)(tq - 8 * (int64_t)k);
+                if (d < 8) {  // the argmax target: sc * (q - 1), as the float kernel
+#pragma unroll
+                  for (int h = 0; h < 4; ++h) {
+                    if (d == (uint64_t)(2 * h)) y[h].x = sc * (q[h].x - 1.f);
+                    if (d == (uint64_t)(2 * h + 1)) y[h].y = sc * (q[h].y - 1.f);
+                  }
+                }
               }
-              st_stream_u4(d4 + k, make_uint4(pack_bf16x2(sc * y[0], sc * y[1]), pack_bf16x2(sc * y[2], sc * y[3]),
-                                              pack_bf16x2(sc * y[4], sc * y[5]), pack_bf16x2(sc * y[6], sc * y[7])));
+              st_stream_u4(d4 + k, make_uint4(pack_bf16x2(y[0].x, y[0].y), pack_bf16x2(y[1].x, y[1].y),
+                                              pack_bf16x2(y[2].x, y[2].y), pack_bf16x2(y[3].x, y[3].y)));
             }
           }
         } else {
@@ -459,18 +464,18 @@ struct DfRing {
     cudaFuncSetAttribute(dflash_fwd_ring_kernel<T, KIND, NC, S, SE, BS>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsmem<KIND>());
     a.nc = NC;
-    dflash_fwd_ring_kernel<T, KIND, NC, S, SE, BS><<<ctas, (NC + 1) * 32, fsmem<KIND>(), st>>>(a);
-    cudaError_t e = cudaGetLastError();
+    const cudaError_t e = launch_pdl(dflash_fwd_ring_kernel<T, KIND, NC, S, SE, BS>, dim3(ctas),
+                                     dim3((NC + 1) * 32), fsmem<KIND>(), st, a);
     if (e != cudaSuccess) return e;
-    return launch_pdl(dflash_finalize_kernel<T, KIND>, dim3((unsigned)a.N), dim3(32 * (a.B < 32 ? a.B : 32)), st,
-                      a);
+    return launch_pdl(dflash_finalize_kernel<T, KIND>, dim3((unsigned)a.N), dim3(32 * (a.B < 32 ? a.B : 32)), 0,
+                      st, a);
   }
   template <int KIND>
   static cudaError_t bwd(const DflashBwdArgs& a, int ctas, cudaStream_t st) {
     cudaFuncSetAttribute(dflash_bwd_ring_kernel<T, KIND, NC, S, SE, BS>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bsmem<KIND>());
-    dflash_bwd_ring_kernel<T, KIND, NC, S, SE, BS><<<ctas, (NC + 1) * 32, bsmem<KIND>(), st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(dflash_bwd_ring_kernel<T, KIND, NC, S, SE, BS>, dim3(ctas), dim3((NC + 1) * 32),
+                      bsmem<KIND>(), st, a);
   }
 };
 

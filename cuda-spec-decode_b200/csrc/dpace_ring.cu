@@ -51,6 +51,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<1, S, SE, T>()))
   const int pmax = a.pt.pmax;
 
   ring_init(sm, NC);
+  pdl_wait();  // no global memory access before the previous kernel has completed
   const RowBits rb = build_row_bits(sm.bits, R, NC + 1, [&](int64_t r) {
     return a.mask == nullptr || a.mask[r] > 0.f;
   });
@@ -158,23 +159,24 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<1, S, SE, T>()))
 template <class T>
 __global__ void __launch_bounds__(1024) dpace_finalize_kernel(const __grid_constant__ DpaceFwdArgs a) {
   __shared__ float sh_ce[32];
-  pdl_wait();  // the streaming grid has completed and its stores are visible
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int B = a.B;
   const int64_t n = blockIdx.x, V = a.pt.V, BL = a.pt.chunk;
   const int NC = a.nc;
   {
     const int64_t r = n * B + warp;
-    // independent loads first: mask, target id, the row's partials
+    pdl_trigger();  // the backward may become resident now (it waits for this grid)
+    // inputs the streaming grid does not write: read them while it drains
     const float mk = a.mask ? a.mask[r] : 1.f;
     const int64_t t = a.targets[r];
+    const bool tvalid = t >= 0 && t < V;
+    const float xt = tvalid ? ldg_f32(static_cast<const T*>(a.logits) + r * V + t) : 0.f;  // x[target]
+    pdl_wait();  // the streaming grid has completed and its stores are visible
     const int k = blocks_in_row(r, V, BL) * NC;
     const float2* part = a.part + r * a.pt.pmax * NC;
     float2 pv[2];
     pv[0] = lane < k ? part[lane] : make_float2(kNegSeed, 0.f);
     pv[1] = lane + 32 < k ? part[lane + 32] : make_float2(kNegSeed, 0.f);
-    const bool tvalid = t >= 0 && t < V;
-    const float xt = tvalid ? ldg_f32(static_cast<const T*>(a.logits) + r * V + t) : 0.f;  // x[target]
     const bool live = mk > 0.f;
     float lse = 0.f, ce = 0.f;
     if (live) {
@@ -257,9 +259,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<1, S, SE, T>()))
   T* dst = static_cast<T*>(a.dlogits);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t E = a.pt.E, V = a.pt.V, R = E / V;
-  const float g = a.dloss ? __ldg(a.dloss) : 1.f;
-
   ring_init(sm, NC);
+  pdl_wait();  // no global memory access before the previous kernel has completed
+  const float g = a.dloss ? __ldg(a.dloss) : 1.f;
   const RowBits rb = build_row_bits(sm.bits, R, NC + 1, [&](int64_t r) {
     return __fmul_rn(a.scale[r], g) != 0.f;
   });
@@ -360,17 +362,26 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<1, S, SE, T>()))
             uint4* d4 = reinterpret_cast<uint4*>(dst + lov);
             const uint4* s4 = reinterpret_cast<const uint4*>(sb + (lov - f0));
             const int64_t tq = tf - lov;
+            const float2 sc2 = make_float2(sc, sc);
             for (int k = lane; k < nv; k += 32) {
               const uint4 v = s4[k];
-              float y[8] = {exp_shift(bf16_lo(v.x), l), exp_shift(bf16_hi(v.x), l),
-                            exp_shift(bf16_lo(v.y), l), exp_shift(bf16_hi(v.y), l),
-                            exp_shift(bf16_lo(v.z), l), exp_shift(bf16_hi(v.z), l),
-                            exp_shift(bf16_lo(v.w), l), exp_shift(bf16_hi(v.w), l)};
-              const uint64_t d = (uint64_t)(tq - 8 * (int64_t)k);
+              const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+              float2 e[4], y[4];
 #pragma unroll
-              for (int e = 0; e < 8; ++e) y[e] = sc * (y[e] - (d == (uint64_t)e ? 1.f : 0.f));
-              st_stream_u4(d4 + k, make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]),
-                                              pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7])));
+              for (int h = 0; h < 4; ++h) {
+                e[h] = exp_shift2(bf16x2_f32(w[h]), l);
+                y[h] = fmul2(e[h], sc2);
+              }
+              const uint64_t d = (uint64_t)(tq - 8 * (int64_t)k);
+              if (d < 8) {  // the target: sc * (p - 1), as the float kernel
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                  if (d == (uint64_t)(2 * h)) y[h].x = sc * (e[h].x - 1.f);
+                  if (d == (uint64_t)(2 * h + 1)) y[h].y = sc * (e[h].y - 1.f);
+                }
+              }
+              st_stream_u4(d4 + k, make_uint4(pack_bf16x2(y[0].x, y[0].y), pack_bf16x2(y[1].x, y[1].y),
+                                              pack_bf16x2(y[2].x, y[2].y), pack_bf16x2(y[3].x, y[3].y)));
             }
           }
         } else {
@@ -402,16 +413,15 @@ struct RingVariant {
     cudaFuncSetAttribute(dpace_fwd_ring_kernel<T, NC, S, SE, BS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem());
     a.nc = NC;
-    dpace_fwd_ring_kernel<T, NC, S, SE, BS><<<ctas, (NC + 1) * 32, smem(), st>>>(a);
-    cudaError_t e = cudaGetLastError();
+    const cudaError_t e =
+        launch_pdl(dpace_fwd_ring_kernel<T, NC, S, SE, BS>, dim3(ctas), dim3((NC + 1) * 32), smem(), st, a);
     if (e != cudaSuccess) return e;
-    return launch_pdl(dpace_finalize_kernel<T>, dim3((unsigned)a.N), dim3(32 * a.B), st, a);
+    return launch_pdl(dpace_finalize_kernel<T>, dim3((unsigned)a.N), dim3(32 * a.B), 0, st, a);
   }
   static cudaError_t bwd(const DpaceBwdArgs& a, int ctas, cudaStream_t st) {
     cudaFuncSetAttribute(dpace_bwd_ring_kernel<T, NC, S, SE, BS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem());
-    dpace_bwd_ring_kernel<T, NC, S, SE, BS><<<ctas, (NC + 1) * 32, smem(), st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(dpace_bwd_ring_kernel<T, NC, S, SE, BS>, dim3(ctas), dim3((NC + 1) * 32), smem(), st, a);
   }
 };
 

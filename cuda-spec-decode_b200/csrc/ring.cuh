@@ -270,8 +270,8 @@ __device__ __forceinline__ void warp_lse_smem(const bf16_t* sb, int a, int b, fl
 }
 
 // bf16 full sub-range of KSUB elements (KSUB / 256 16-byte vectors per lane):
-// the max is taken on the packed words, each element is widened once for its
-// exponential.
+// the max is taken on the packed words, each element is widened once, and the
+// arithmetic runs on fp32 pairs.
 template <int KSUB>
 __device__ __forceinline__ void warp_lse_full(const bf16_t* sb, float& m, float& s) {
   constexpr int U = KSUB / 256;
@@ -289,29 +289,28 @@ __device__ __forceinline__ void warp_lse_full(const bf16_t* sb, float& m, float&
     s *= exp_shift(m, cm);
     m = cm;
   }
-  float acc[U];
+  float2 acc[U];
 #pragma unroll
-  for (int u = 0; u < U; ++u)
-    acc[u] = ((exp_shift(bf16_lo(v[u].x), m) + exp_shift(bf16_hi(v[u].x), m)) +
-              (exp_shift(bf16_lo(v[u].y), m) + exp_shift(bf16_hi(v[u].y), m))) +
-             ((exp_shift(bf16_lo(v[u].z), m) + exp_shift(bf16_hi(v[u].z), m)) +
-              (exp_shift(bf16_lo(v[u].w), m) + exp_shift(bf16_hi(v[u].w), m)));
+  for (int u = 0; u < U; ++u) acc[u] = vec8_expsum2(v[u], m);
 #pragma unroll
   for (int w = 1; w < U; w <<= 1)
 #pragma unroll
-    for (int u = 0; u + w < U; u += 2 * w) acc[u] += acc[u + w];
-  s += acc[0];
+    for (int u = 0; u + w < U; u += 2 * w) acc[u] = fadd2(acc[u], acc[u + w]);
+  s += acc[0].x + acc[0].y;
 }
 
-// Launches a finalize kernel chained to the previous kernel on the stream with
-// programmatic dependent launch (it starts launching while the streaming grid
-// drains and waits for it inside, with griddepcontrol.wait).
+// Launches a kernel chained to the previous kernel on the stream with
+// programmatic dependent launch: it may become resident while that kernel
+// drains, and waits for it inside with griddepcontrol.wait. Every kernel
+// launched this way touches no global memory before its pdl_wait(), so the
+// chaining is safe whatever the previous kernel reads or writes.
 template <class Kernel, class Args>
-inline cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, cudaStream_t st, const Args& args) {
+inline cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              const Args& args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -112,6 +112,38 @@ __device__ __forceinline__ void st_stream_u4(void* p, uint4 v) {
 }
 
 // ---------------------------------------------------------------------------
+// Packed fp32 pairs (sm_100 add/sub/mul/fma.f32x2): two IEEE round-to-nearest
+// operations per issued instruction, bitwise equal to the scalar forms. The
+// bf16 kernels move two elements per byte of fp32 data, so their instruction
+// issue rate, not MUFU or HBM, is what the pairing relieves.
+// ---------------------------------------------------------------------------
+#define SPECDEC_F32X2_OP(name, op)                                                              \
+  __device__ __forceinline__ float2 name(float2 a, float2 b) {                                  \
+    float2 r;                                                                                   \
+    asm("{\n\t.reg .b64 A, B, D;\n\tmov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\t" op \
+        " D, A, B;\n\tmov.b64 {%0, %1}, D;\n\t}"                                              \
+        : "=f"(r.x), "=f"(r.y)                                                                  \
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));                                              \
+    return r;                                                                                   \
+  }
+SPECDEC_F32X2_OP(fadd2, "add.rn.f32x2")
+SPECDEC_F32X2_OP(fsub2, "sub.rn.f32x2")
+SPECDEC_F32X2_OP(fmul2, "mul.rn.f32x2")
+#undef SPECDEC_F32X2_OP
+
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 r;
+  asm("{\n\t.reg .b64 A, B, C, D;\n\tmov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\t"
+      "mov.b64 C, {%6, %7};\n\tfma.rn.f32x2 D, A, B, C;\n\tmov.b64 {%0, %1}, D;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return r;
+}
+
+// The two elements of a bf16x2 word as an fp32 pair (low half first).
+__device__ __forceinline__ float2 bf16x2_f32(uint32_t w) { return make_float2(bf16_lo(w), bf16_hi(w)); }
+
+// ---------------------------------------------------------------------------
 // Online log-sum-exp: the state (m, s) stands for s * e^m with m the running
 // max; each element contributes e^(x - m) = 2^((x - m) * log2 e) (FADD, FMUL,
 // MUFU.EX2). The max element contributes exactly 1, as in torch's
@@ -119,6 +151,20 @@ __device__ __forceinline__ void st_stream_u4(void* p, uint4 v) {
 // element. log-sum-exp(x) = m + log(s).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float exp_shift(float x, float m) { return exp2_approx((x - m) * kLog2e); }
+
+// exp_shift of a pair: (x - m) * log2 e in one packed subtract and multiply,
+// bitwise equal to two exp_shift calls.
+__device__ __forceinline__ float2 exp_shift2(float2 x, float m) {
+  const float2 t = fmul2(fsub2(x, make_float2(m, m)), make_float2(kLog2e, kLog2e));
+  return make_float2(exp2_approx(t.x), exp2_approx(t.y));
+}
+
+// Sum over the 8 elements of a bf16 vector of e^(x - m), as a pair.
+__device__ __forceinline__ float2 vec8_expsum2(const uint4& v, float m) {
+  const float2 e0 = exp_shift2(bf16x2_f32(v.x), m), e1 = exp_shift2(bf16x2_f32(v.y), m);
+  const float2 e2 = exp_shift2(bf16x2_f32(v.z), m), e3 = exp_shift2(bf16x2_f32(v.w), m);
+  return fadd2(fadd2(e0, e1), fadd2(e2, e3));
+}
 
 __device__ __forceinline__ void lse_merge(float& m, float& s, float om, float os) {
   const float M = fmaxf(m, om);
