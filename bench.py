@@ -219,7 +219,7 @@ def time_pair(args, stream, world, max_over_ranks, barrier, fwd, bwd, steps):
     bwd(i, state) on alternating input sets after args.warmup untimed steps.
     Returns (ms per step, mean forward ms, mean backward ms), max over ranks."""
 
-    reducer = LossReducer(stream.device) if world > 1 else None
+    reducer = LossReducer(stream.device) if world > 1 and args.loss_reduce == "overlap" else None
 
     def step(i, ev=None):
         if ev is not None:
@@ -229,6 +229,9 @@ def time_pair(args, stream, world, max_over_ranks, barrier, fwd, bwd, steps):
             ev[1].record(stream)
         if reducer is not None:
             reducer.start(loss)
+        elif world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(loss)
         if ev is not None:
             ev[2].record(stream)
         bwd(i, state)
@@ -519,7 +522,7 @@ def run_ours(args):
     # ring kernels (16-byte-aligned inputs): forward = streaming + finalize, backward = 1
     launches_per_step = 3 if all(x.data_ptr() % 16 == 0 for x, _, _ in sets) else 2
 
-    reducer = LossReducer(dev) if world > 1 else None
+    reducer = LossReducer(dev) if world > 1 and args.loss_reduce == "overlap" else None
 
     def step(i, ev=None):
         x, t, m = sets[i & 1]
@@ -530,6 +533,8 @@ def run_ours(args):
             ev[1].record(stream)
         if reducer is not None:
             loss = reducer.start(loss)  # global loss, reduced beside the backward
+        elif world > 1:
+            dist.all_reduce(loss)
         if ev is not None:
             ev[2].record(stream)
         ops.dpace_backward(x, t, lse, scale, None, out=grad)
@@ -655,7 +660,7 @@ def run_ours(args):
             "data": "synthetic",
             "config": {"workload": "dpace_fwd_bwd_llama3_vocab", "N_per_gpu": N, "B": B, "V": V,
                        "global_N": n_global, "sigma": 2.0, "mask": "prefix k~U{0..4}",
-                       "alpha": 0.5, "loss_type": "dpace", "parallelism": f"dp{world} (N-sharded)",
+                       "alpha": 0.5, "loss_type": "dpace", "parallelism": f"dp{world} (N-sharded)", "loss_all_reduce": args.loss_reduce if world > 1 else None,
                        "l2": "two alternating input sets, each 525 MB > 126 MB L2",
                        "bytes_model": "12*N*B*V per GPU-step"},
             "rows_per_s": round(rows_s, 1),
@@ -691,6 +696,9 @@ def main(argv=None):
                    help="timed steps of each bf16-logits workload (0 = skip)")
     p.add_argument("--drafter-steps", type=int, default=10,
                    help="timed end-to-end drafter training steps per variant (0 = skip)")
+    p.add_argument("--loss-reduce", choices=("overlap", "serial"), default="overlap",
+                   help="N > 1: loss all_reduce on a side stream beside the backward, or between "
+                        "forward and backward on the compute stream")
     p.add_argument("--cpu-budget", type=float, default=10.0,
                    help="seconds of CPU-oracle timing on rank 0 at N=1 (0 = skip)")
     args = p.parse_args(argv)

@@ -66,7 +66,6 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<2, S, SE, T>()))
   const int pmax = a.pt.pmax;
 
   ring_init(sm, NC);
-  pdl_wait();  // no global memory access before the previous kernel has completed
   const RowBits rb = build_row_bits(sm.bits, R, NC + 1, [&](int64_t r) { return dr_numer(a, r) != 0.f; });
   __syncthreads();
 
@@ -189,7 +188,6 @@ __global__ void __launch_bounds__(1024) dflash_finalize_kernel(const __grid_cons
   const int B = a.B;
   const int64_t n = blockIdx.x, V = a.pt.V, BL = a.pt.chunk;
   const int NC = a.nc;
-  pdl_trigger();  // the backward may become resident now (it waits for this grid)
   // denominator: sum of the sequence's raw mask values + 1e-5 (the mask is
   // not written by the streaming grid: read it while that grid drains)
   float mv = 0.f;
@@ -281,9 +279,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<(KIND == kKindKL
   T* dst = static_cast<T*>(a.dlogits);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t E = a.pt.E, V = a.pt.V, R = E / V;
-  ring_init(sm, NC);
-  pdl_wait();  // no global memory access before the previous kernel has completed
   const float g = a.dloss ? __ldg(a.dloss) : 1.f;
+  ring_init(sm, NC);
   const RowBits rb = build_row_bits(sm.bits, R, NC + 1, [&](int64_t r) { return __fmul_rn(a.scale[r], g) != 0.f; });
   __syncthreads();
 
@@ -464,8 +461,10 @@ struct DfRing {
     cudaFuncSetAttribute(dflash_fwd_ring_kernel<T, KIND, NC, S, SE, BS>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsmem<KIND>());
     a.nc = NC;
-    const cudaError_t e = launch_pdl(dflash_fwd_ring_kernel<T, KIND, NC, S, SE, BS>, dim3(ctas),
-                                     dim3((NC + 1) * 32), fsmem<KIND>(), st, a);
+    // plain launch for the streaming kernel (its predecessor is the caller's),
+    // PDL only for the finalize that always follows it
+    dflash_fwd_ring_kernel<T, KIND, NC, S, SE, BS><<<ctas, (NC + 1) * 32, fsmem<KIND>(), st>>>(a);
+    const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     return launch_pdl(dflash_finalize_kernel<T, KIND>, dim3((unsigned)a.N), dim3(32 * (a.B < 32 ? a.B : 32)), 0,
                       st, a);
@@ -474,8 +473,8 @@ struct DfRing {
   static cudaError_t bwd(const DflashBwdArgs& a, int ctas, cudaStream_t st) {
     cudaFuncSetAttribute(dflash_bwd_ring_kernel<T, KIND, NC, S, SE, BS>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bsmem<KIND>());
-    return launch_pdl(dflash_bwd_ring_kernel<T, KIND, NC, S, SE, BS>, dim3(ctas), dim3((NC + 1) * 32),
-                      bsmem<KIND>(), st, a);
+    dflash_bwd_ring_kernel<T, KIND, NC, S, SE, BS><<<ctas, (NC + 1) * 32, bsmem<KIND>(), st>>>(a);
+    return cudaGetLastError();
   }
 };
 

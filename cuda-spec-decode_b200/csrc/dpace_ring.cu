@@ -51,7 +51,6 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<1, S, SE, T>()))
   const int pmax = a.pt.pmax;
 
   ring_init(sm, NC);
-  pdl_wait();  // no global memory access before the previous kernel has completed
   const RowBits rb = build_row_bits(sm.bits, R, NC + 1, [&](int64_t r) {
     return a.mask == nullptr || a.mask[r] > 0.f;
   });
@@ -165,7 +164,6 @@ __global__ void __launch_bounds__(1024) dpace_finalize_kernel(const __grid_const
   const int NC = a.nc;
   {
     const int64_t r = n * B + warp;
-    pdl_trigger();  // the backward may become resident now (it waits for this grid)
     // inputs the streaming grid does not write: read them while it drains
     const float mk = a.mask ? a.mask[r] : 1.f;
     const int64_t t = a.targets[r];
@@ -259,9 +257,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<1, S, SE, T>()))
   T* dst = static_cast<T*>(a.dlogits);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t E = a.pt.E, V = a.pt.V, R = E / V;
-  ring_init(sm, NC);
-  pdl_wait();  // no global memory access before the previous kernel has completed
   const float g = a.dloss ? __ldg(a.dloss) : 1.f;
+  ring_init(sm, NC);
   const RowBits rb = build_row_bits(sm.bits, R, NC + 1, [&](int64_t r) {
     return __fmul_rn(a.scale[r], g) != 0.f;
   });
@@ -413,15 +410,19 @@ struct RingVariant {
     cudaFuncSetAttribute(dpace_fwd_ring_kernel<T, NC, S, SE, BS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem());
     a.nc = NC;
-    const cudaError_t e =
-        launch_pdl(dpace_fwd_ring_kernel<T, NC, S, SE, BS>, dim3(ctas), dim3((NC + 1) * 32), smem(), st, a);
+    // the streaming kernel follows whatever the caller enqueued (possibly a
+    // wait on another stream): a plain launch. Only the finalize, whose
+    // predecessor is always this streaming kernel, is chained with PDL.
+    dpace_fwd_ring_kernel<T, NC, S, SE, BS><<<ctas, (NC + 1) * 32, smem(), st>>>(a);
+    const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     return launch_pdl(dpace_finalize_kernel<T>, dim3((unsigned)a.N), dim3(32 * a.B), 0, st, a);
   }
   static cudaError_t bwd(const DpaceBwdArgs& a, int ctas, cudaStream_t st) {
     cudaFuncSetAttribute(dpace_bwd_ring_kernel<T, NC, S, SE, BS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem());
-    return launch_pdl(dpace_bwd_ring_kernel<T, NC, S, SE, BS>, dim3(ctas), dim3((NC + 1) * 32), smem(), st, a);
+    dpace_bwd_ring_kernel<T, NC, S, SE, BS><<<ctas, (NC + 1) * 32, smem(), st>>>(a);
+    return cudaGetLastError();
   }
 };
 

@@ -301,9 +301,12 @@ __device__ __forceinline__ void warp_lse_full(const bf16_t* sb, float& m, float&
 
 // Launches a kernel chained to the previous kernel on the stream with
 // programmatic dependent launch: it may become resident while that kernel
-// drains, and waits for it inside with griddepcontrol.wait. Every kernel
-// launched this way touches no global memory before its pdl_wait(), so the
-// chaining is safe whatever the previous kernel reads or writes.
+// drains, and waits for it inside with griddepcontrol.wait. Used only where
+// the previous kernel is known: the finalize right after its own streaming
+// kernel, enqueued by the same call. A chained grid that became resident
+// early and waited on work ordered behind another stream (an event wait on a
+// collective, say) could hold every SM that work needs, so kernels whose
+// predecessor is the caller's are launched plainly.
 template <class Kernel, class Args>
 inline cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                               const Args& args) {
