@@ -10,6 +10,7 @@
 
 #include <climits>
 #include <cstdint>
+#include <type_traits>
 
 #include "specdec_common.cuh"
 #include "specdec_internal.h"
@@ -223,6 +224,37 @@ __device__ __forceinline__ void df_group(DfState& s, const uint4 (&a)[U], const 
       }
       s.bx = cmb;
     }
+  }
+}
+
+// A stage range [a, b) of both streams (a stage cut by a row edge):
+// element k of the stage is row index row_off + k. Scalar head and tail to
+// 16-byte boundaries, then 16-byte vectors, four per lane per round.
+template <int KIND, class T>
+__device__ __forceinline__ void df_range(DfState& st, const T* sl, const T* sx, int a, int b, int row_off) {
+  using Vec = typename std::conditional<sizeof(T) == 4, float4, uint4>::type;
+  constexpr int kVec = 16 / sizeof(T);
+  const int lane = threadIdx.x & 31;
+  const int av = (a + kVec - 1) & ~(kVec - 1), bv = b & ~(kVec - 1);
+  if (av >= bv) {
+    for (int k = a + lane; k < b; k += 32) df_push<KIND>(st, to_f32(sl[k]), to_f32(sx[k]), row_off + k);
+    return;
+  }
+  if (lane < av - a) df_push<KIND>(st, to_f32(sl[a + lane]), to_f32(sx[a + lane]), row_off + a + lane);
+  if (lane < b - bv) df_push<KIND>(st, to_f32(sl[bv + lane]), to_f32(sx[bv + lane]), row_off + bv + lane);
+  const Vec* ql = reinterpret_cast<const Vec*>(sl);
+  const Vec* qx = reinterpret_cast<const Vec*>(sx);
+  int k = av / kVec + lane;
+  const int kend = bv / kVec;
+  for (; k + 96 < kend; k += 128) {
+    const Vec va[4] = {ql[k], ql[k + 32], ql[k + 64], ql[k + 96]};
+    const Vec vb[4] = {qx[k], qx[k + 32], qx[k + 64], qx[k + 96]};
+    df_group<KIND, 4>(st, va, vb, row_off + k * kVec, 32 * kVec);
+  }
+  for (; k < kend; k += 32) {
+    const Vec va[1] = {ql[k]};
+    const Vec vb[1] = {qx[k]};
+    df_group<KIND, 1>(st, va, vb, row_off + k * kVec, 32 * kVec);
   }
 }
 

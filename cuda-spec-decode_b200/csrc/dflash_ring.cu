@@ -49,7 +49,7 @@ __device__ __forceinline__ float dr_numer(const DflashFwdArgs& a, int64_t r) {
 }
 
 template <class T, int KIND, int NC, int S, int SE, int BS>
-__global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<2, S, SE, T>())) dflash_fwd_ring_kernel(const __grid_constant__ DflashFwdArgs a) {
+__global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 2, S, SE, T>())) dflash_fwd_ring_kernel(const __grid_constant__ DflashFwdArgs a) {
   constexpr int kVec = 16 / sizeof(T);  // elements per 16-byte vector
   constexpr int kSub = SE / NC;
   constexpr int U = kSub / (32 * kVec);  // 16-byte vectors per lane per stream in a full sub-range
@@ -159,11 +159,10 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<2, S, SE, T>()))
       const int64_t g = min(f1, rend);
       if (live) {
         const int64_t lo = max(f, w0), hi = min(g, w1);
-        for (int64_t x = lo + lane; x < hi; x += 32) {
-          const float xl = x < fv ? to_f32(sl[x - f0]) : ldg_f32(XL + x);
-          const float xt = x < fv ? to_f32(sx[x - f0]) : ldg_f32(XT + x);
-          df_push<KIND>(st, xl, xt, (int)(x - r * V));
-        }
+        const int64_t hv = min(hi, fv);
+        if (hv > lo) df_range<KIND>(st, sl, sx, (int)(lo - f0), (int)(hv - f0), (int)(f0 - r * V));
+        for (int64_t x = max(lo, fv) + lane; x < hi; x += 32)  // past the copied part: global memory
+          df_push<KIND>(st, ldg_f32(XL + x), ldg_f32(XT + x), (int)(x - r * V));
       }
       f = g;
       if (g == rend) {
@@ -264,7 +263,7 @@ __global__ void __launch_bounds__(1024) dflash_finalize_kernel(const __grid_cons
 }
 
 template <class T, int KIND, int NC, int S, int SE, int BS>
-__global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<(KIND == kKindKL ? 2 : 1), S, SE, T>())) dflash_bwd_ring_kernel(const __grid_constant__ DflashBwdArgs a) {
+__global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, (KIND == kKindKL ? 2 : 1), S, SE, T>())) dflash_bwd_ring_kernel(const __grid_constant__ DflashBwdArgs a) {
   constexpr int NIN = KIND == kKindKL ? 2 : 1;
   constexpr int kVec = 16 / sizeof(T);
   constexpr int kSub = SE / NC;
@@ -483,8 +482,9 @@ struct DfRing {
 // 0 = 4 x 4 x 2048 x 8 (64 KB ring, 64 KB blocks per stream, 3 CTAs/SM);
 // 1 = 4 x 4 x 4096 x 4 (128 KB ring, 1 CTA/SM); 2 = 4 x 6 x 2048 x 8 (96 KB
 // ring, 2 CTAs/SM); 3 = 2 x 4 x 2048 x 8 (64 KB ring, 3 CTAs/SM);
-// 4 = 8 x 3 x 4096 x 4 (96 KB ring, 2 CTAs/SM). bf16 shapes have the same
-// bytes (twice the elements).
+// 4 = 8 x 3 x 4096 x 4 (96 KB ring, 2 CTAs/SM); 5 = 8 x 4 x 2048 x 8 (64 KB
+// ring, 8 consumer warps). bf16 shapes have the same bytes (twice the
+// elements).
 template <class T>
 struct DfShapes {
   static constexpr int k = 4 / sizeof(T);
@@ -493,6 +493,7 @@ struct DfShapes {
   using D2 = DfRing<T, 4, 6, 2048 * k, 8>;
   using D3 = DfRing<T, 2, 4, 2048 * k, 8>;
   using D4 = DfRing<T, 8, 3, 4096 * k, 4>;
+  using D5 = DfRing<T, 8, 4, 2048 * k, 8>;
 
   static int block_elems(int shape) {
     switch (shape) {
@@ -508,6 +509,7 @@ struct DfShapes {
       case 2: return D2::template fwd_ctas<KIND>(device, cap);
       case 3: return D3::template fwd_ctas<KIND>(device, cap);
       case 4: return D4::template fwd_ctas<KIND>(device, cap);
+      case 5: return D5::template fwd_ctas<KIND>(device, cap);
       default: return D0::template fwd_ctas<KIND>(device, cap);
     }
   }
@@ -518,6 +520,7 @@ struct DfShapes {
       case 2: return D2::template bwd_ctas<KIND>(device, cap);
       case 3: return D3::template bwd_ctas<KIND>(device, cap);
       case 4: return D4::template bwd_ctas<KIND>(device, cap);
+      case 5: return D5::template bwd_ctas<KIND>(device, cap);
       default: return D0::template bwd_ctas<KIND>(device, cap);
     }
   }
@@ -528,6 +531,7 @@ struct DfShapes {
       case 2: return D2::template fwd<KIND>(a, ctas, st);
       case 3: return D3::template fwd<KIND>(a, ctas, st);
       case 4: return D4::template fwd<KIND>(a, ctas, st);
+      case 5: return D5::template fwd<KIND>(a, ctas, st);
       default: return D0::template fwd<KIND>(a, ctas, st);
     }
   }
@@ -538,6 +542,7 @@ struct DfShapes {
       case 2: return D2::template bwd<KIND>(a, ctas, st);
       case 3: return D3::template bwd<KIND>(a, ctas, st);
       case 4: return D4::template bwd<KIND>(a, ctas, st);
+      case 5: return D5::template bwd<KIND>(a, ctas, st);
       default: return D0::template bwd<KIND>(a, ctas, st);
     }
   }
@@ -565,6 +570,7 @@ int dflash_ring_consumers(int shape) {
   switch (shape) {
     case 3: return 2;
     case 4: return 8;
+    case 5: return 8;
     default: return 4;
   }
 }

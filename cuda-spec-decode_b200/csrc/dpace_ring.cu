@@ -37,7 +37,7 @@ namespace specdec {
 namespace {
 
 template <class T, int NC, int S, int SE, int BS>
-__global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<1, S, SE, T>())) dpace_fwd_ring_kernel(const __grid_constant__ DpaceFwdArgs a) {
+__global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>())) dpace_fwd_ring_kernel(const __grid_constant__ DpaceFwdArgs a) {
   constexpr int kSub = SE / NC;
   constexpr int64_t BL = (int64_t)BS * SE;
   constexpr int kLogBL = __builtin_ctzll(BL);
@@ -245,7 +245,7 @@ __global__ void __launch_bounds__(1024) dpace_finalize_kernel(const __grid_const
 }
 
 template <class T, int NC, int S, int SE, int BS>
-__global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<1, S, SE, T>())) dpace_bwd_ring_kernel(const __grid_constant__ DpaceBwdArgs a) {
+__global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>())) dpace_bwd_ring_kernel(const __grid_constant__ DpaceBwdArgs a) {
   constexpr int kVec = 16 / sizeof(T);  // elements per 16-byte vector
   constexpr int kSub = SE / NC;
   constexpr int64_t BL = (int64_t)BS * SE;
@@ -431,7 +431,8 @@ struct RingVariant {
 // the fastest measured on the [64, 16, 128256] workload); 1 = 8 x 4 x 8192 x 2
 // (128 KB ring, 1 CTA/SM); 2 = 4 x 6 x 4096 x 4 (96 KB ring, 2 CTAs/SM); 3 =
 // 4 x 8 x 4096 x 8 (128 KB ring, 128 KB blocks); 4 = 2 x 6 x 2048 x 8 (48 KB
-// ring, 4 CTAs/SM). bf16 shapes have the same bytes (twice the elements).
+// ring, 4 CTAs/SM); 5 = 8 x 4 x 4096 x 4 (64 KB ring, 8 consumer warps). bf16
+// shapes have the same bytes (twice the elements).
 template <class T>
 struct Shapes {
   static constexpr int k = 4 / sizeof(T);  // elements per float's bytes
@@ -440,6 +441,7 @@ struct Shapes {
   using R2 = RingVariant<T, 4, 6, 4096 * k, 4>;
   using R3 = RingVariant<T, 4, 8, 4096 * k, 8>;
   using R4 = RingVariant<T, 2, 6, 2048 * k, 8>;
+  using R5 = RingVariant<T, 8, 4, 4096 * k, 4>;
 
   static int block_elems(int shape) {
     switch (shape) {
@@ -447,6 +449,7 @@ struct Shapes {
       case 2: return 4096 * 4 * k;
       case 3: return 4096 * 8 * k;
       case 4: return 2048 * 8 * k;
+      case 5: return 4096 * 4 * k;
       default: return 4096 * 4 * k;
     }
   }
@@ -456,6 +459,7 @@ struct Shapes {
       case 2: return R2::fwd_ctas(device, cap);
       case 3: return R3::fwd_ctas(device, cap);
       case 4: return R4::fwd_ctas(device, cap);
+      case 5: return R5::fwd_ctas(device, cap);
       default: return R0::fwd_ctas(device, cap);
     }
   }
@@ -465,6 +469,7 @@ struct Shapes {
       case 2: return R2::bwd_ctas(device, cap);
       case 3: return R3::bwd_ctas(device, cap);
       case 4: return R4::bwd_ctas(device, cap);
+      case 5: return R5::bwd_ctas(device, cap);
       default: return R0::bwd_ctas(device, cap);
     }
   }
@@ -474,6 +479,7 @@ struct Shapes {
       case 2: return R2::fwd(a, ctas, st);
       case 3: return R3::fwd(a, ctas, st);
       case 4: return R4::fwd(a, ctas, st);
+      case 5: return R5::fwd(a, ctas, st);
       default: return R0::fwd(a, ctas, st);
     }
   }
@@ -483,6 +489,7 @@ struct Shapes {
       case 2: return R2::bwd(a, ctas, st);
       case 3: return R3::bwd(a, ctas, st);
       case 4: return R4::bwd(a, ctas, st);
+      case 5: return R5::bwd(a, ctas, st);
       default: return R0::bwd(a, ctas, st);
     }
   }
@@ -498,6 +505,7 @@ int dpace_ring_consumers(int shape) {
   switch (shape) {
     case 1: return 8;
     case 4: return 2;
+    case 5: return 8;
     default: return 4;
   }
 }

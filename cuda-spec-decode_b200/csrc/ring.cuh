@@ -179,12 +179,15 @@ struct RingSmem {
   unsigned bits[kMaxRowWords];
 };
 
-// Minimum CTAs per SM a bf16 ring kernel is compiled for: 3 where three rings
-// fit in shared memory (the register budget then allows 3 resident CTAs of
-// 160 threads), else 1. Float kernels are compiled without a minimum.
-template <int NIN, int S, int SE, class T>
+// Minimum CTAs per SM a bf16 ring kernel is compiled for (it caps the
+// registers per thread): as many rings as fit in shared memory, at most 3 for
+// 160-thread CTAs and 2 for larger ones. Float kernels are compiled without a
+// minimum.
+template <int NC, int NIN, int S, int SE, class T>
 constexpr int ring_min_ctas() {
-  return (sizeof(T) == 2 && 3 * sizeof(RingSmem<NIN, S, SE, T>) <= 227 * 1024) ? 3 : 1;
+  constexpr int by_smem = int((227 * 1024) / sizeof(RingSmem<NIN, S, SE, T>));
+  constexpr int by_threads = (NC + 1) * 32 <= 160 ? 3 : 2;
+  return sizeof(T) == 2 ? (by_smem < by_threads ? (by_smem < 1 ? 1 : by_smem) : by_threads) : 1;
 }
 
 template <int NIN, int S, int SE, class T>
@@ -263,10 +266,43 @@ __device__ __forceinline__ void warp_lse_full(const float* sb, float& m, float& 
   s += acc[0];
 }
 
-// bf16 stage, elements [a, b): one element per lane per round (row edges).
+// bf16 stage, elements [a, b) (a stage cut by a row edge): scalar head and
+// tail to 16-byte boundaries, then 16-byte vectors, four per lane per round.
 __device__ __forceinline__ void warp_lse_smem(const bf16_t* sb, int a, int b, float& m, float& s) {
   const int lane = threadIdx.x & 31;
-  for (int k = a + lane; k < b; k += 32) lse_push(m, s, to_f32(sb[k]));
+  const int a8 = (a + 7) & ~7, b8 = b & ~7;
+  if (a8 >= b8) {
+    for (int k = a + lane; k < b; k += 32) lse_push(m, s, to_f32(sb[k]));
+    return;
+  }
+  if (lane < a8 - a) lse_push(m, s, to_f32(sb[a + lane]));
+  if (lane < b - b8) lse_push(m, s, to_f32(sb[b8 + lane]));
+  const uint4* q = reinterpret_cast<const uint4*>(sb);
+  int k = (a8 >> 3) + lane;
+  const int kend = b8 >> 3;
+  for (; k + 96 < kend; k += 128) {
+    const uint4 v0 = q[k], v1 = q[k + 32], v2 = q[k + 64], v3 = q[k + 96];
+    const uint32_t mx = bmax2(bmax2(bmax8(v0), bmax8(v1)), bmax2(bmax8(v2), bmax8(v3)));
+    const float cm = fmaxf(bf16_lo(mx), bf16_hi(mx));
+    if (cm > m) {
+      s *= exp_shift(m, cm);
+      m = cm;
+    }
+    const float2 acc = fadd2(fadd2(vec8_expsum2(v0, m), vec8_expsum2(v1, m)),
+                             fadd2(vec8_expsum2(v2, m), vec8_expsum2(v3, m)));
+    s += acc.x + acc.y;
+  }
+  for (; k < kend; k += 32) {
+    const uint4 v = q[k];
+    const uint32_t mx = bmax8(v);
+    const float cm = fmaxf(bf16_lo(mx), bf16_hi(mx));
+    if (cm > m) {
+      s *= exp_shift(m, cm);
+      m = cm;
+    }
+    const float2 acc = vec8_expsum2(v, m);
+    s += acc.x + acc.y;
+  }
 }
 
 // bf16 full sub-range of KSUB elements (KSUB / 256 16-byte vectors per lane):

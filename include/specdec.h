@@ -227,11 +227,12 @@ int specdec_dflash_backward_bf16(const uint16_t* logits, const uint16_t* target_
 
 /*
  * Selects a kernel variant and caps resident CTAs per SM (0 = occupancy
- * limit) for one kernel, process-wide. Shapes 0..4 are warp-specialized
+ * limit) for one kernel, process-wide. Shapes 0..5 are warp-specialized
  * bulk-copy ring variants (used when the streamed pointers are 16-byte
- * aligned, and for DFlash when B <= 32; otherwise the 128-bit-load kernels run
- * with their default shape); 10..14 force the 128-bit-load kernels, variant
- * shape - 10. Workspace sizes depend on it: query sizes after changing it.
+ * aligned; otherwise the 128-bit-load kernels run with their default shape);
+ * 10..14 force the 128-bit-load kernels, variant shape - 10 (bf16 entry
+ * points, which have only the ring kernels, then use ring shape 0). Workspace
+ * sizes depend on it: query sizes after changing it.
  */
 int specdec_set_launch_shape(int32_t kernel, int32_t shape, int32_t ctas_per_sm);
 

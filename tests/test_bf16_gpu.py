@@ -177,7 +177,7 @@ def test_dflash_mixed_dtypes_widen_the_bf16_side(cuda):
     assert float((xg.grad.cpu() - g_ref).abs().max()) <= 1e-6
 
 
-@pytest.mark.parametrize("shape", [0, 1, 2, 3, 4, 10])
+@pytest.mark.parametrize("shape", [0, 1, 2, 3, 4, 5, 10])
 def test_bf16_every_launch_shape(cuda, shape):
     """Every bf16 ring shape (10 selects the fp32 128-bit-load kernels, for
     which bf16 uses ring shape 0) gives the oracle's results."""
