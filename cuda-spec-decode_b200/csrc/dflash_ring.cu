@@ -457,21 +457,21 @@ struct DfRing {
   }
   template <int KIND>
   static cudaError_t fwd(DflashFwdArgs a, int ctas, cudaStream_t st) {
-    cudaFuncSetAttribute(dflash_fwd_ring_kernel<T, KIND, NC, S, SE, BS>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsmem<KIND>());
+    cudaError_t e = ensure_smem_limit<dflash_fwd_ring_kernel<T, KIND, NC, S, SE, BS>>(fsmem<KIND>());
+    if (e != cudaSuccess) return e;
     a.nc = NC;
     // plain launch for the streaming kernel (its predecessor is the caller's),
     // PDL only for the finalize that always follows it
     dflash_fwd_ring_kernel<T, KIND, NC, S, SE, BS><<<ctas, (NC + 1) * 32, fsmem<KIND>(), st>>>(a);
-    const cudaError_t e = cudaGetLastError();
+    e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     return launch_pdl(dflash_finalize_kernel<T, KIND>, dim3((unsigned)a.N), dim3(32 * (a.B < 32 ? a.B : 32)), 0,
                       st, a);
   }
   template <int KIND>
   static cudaError_t bwd(const DflashBwdArgs& a, int ctas, cudaStream_t st) {
-    cudaFuncSetAttribute(dflash_bwd_ring_kernel<T, KIND, NC, S, SE, BS>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bsmem<KIND>());
+    const cudaError_t e = ensure_smem_limit<dflash_bwd_ring_kernel<T, KIND, NC, S, SE, BS>>(bsmem<KIND>());
+    if (e != cudaSuccess) return e;
     dflash_bwd_ring_kernel<T, KIND, NC, S, SE, BS><<<ctas, (NC + 1) * 32, bsmem<KIND>(), st>>>(a);
     return cudaGetLastError();
   }

@@ -407,20 +407,20 @@ struct RingVariant {
   }
   static cudaError_t fwd(DpaceFwdArgs a, int ctas, cudaStream_t st) {
     // the attribute must be set on the launching device before the launch
-    cudaFuncSetAttribute(dpace_fwd_ring_kernel<T, NC, S, SE, BS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem());
+    cudaError_t e = ensure_smem_limit<dpace_fwd_ring_kernel<T, NC, S, SE, BS>>(smem());
+    if (e != cudaSuccess) return e;
     a.nc = NC;
     // the streaming kernel follows whatever the caller enqueued (possibly a
     // wait on another stream): a plain launch. Only the finalize, whose
     // predecessor is always this streaming kernel, is chained with PDL.
     dpace_fwd_ring_kernel<T, NC, S, SE, BS><<<ctas, (NC + 1) * 32, smem(), st>>>(a);
-    const cudaError_t e = cudaGetLastError();
+    e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     return launch_pdl(dpace_finalize_kernel<T>, dim3((unsigned)a.N), dim3(32 * a.B), 0, st, a);
   }
   static cudaError_t bwd(const DpaceBwdArgs& a, int ctas, cudaStream_t st) {
-    cudaFuncSetAttribute(dpace_bwd_ring_kernel<T, NC, S, SE, BS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem());
+    const cudaError_t e = ensure_smem_limit<dpace_bwd_ring_kernel<T, NC, S, SE, BS>>(smem());
+    if (e != cudaSuccess) return e;
     dpace_bwd_ring_kernel<T, NC, S, SE, BS><<<ctas, (NC + 1) * 32, smem(), st>>>(a);
     return cudaGetLastError();
   }

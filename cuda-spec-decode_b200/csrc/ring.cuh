@@ -17,6 +17,8 @@
 // time on a loaded memory system. Every wait is bounded (kWaitLimitNs).
 #pragma once
 
+#include <atomic>
+
 #include "bulk_copy.cuh"
 #include "specdec_common.cuh"
 
@@ -357,6 +359,22 @@ inline cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, size_t smem,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, args);
+}
+
+// Raises `Kernel`'s dynamic shared-memory limit to `smem` once per device
+// (the attribute is per device and per function); later launches, including
+// ones under stream capture, skip the call.
+template <auto Kernel>
+inline cudaError_t ensure_smem_limit(size_t smem) {
+  static std::atomic<unsigned long long> done{0};  // bit d: set on device d
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
 }
 
 template <class K>
