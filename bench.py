@@ -396,8 +396,10 @@ def time_drafter_step(args, dev, world, max_over_ranks, barrier):
     D-PACE alpha 0.5 with the anchor slot masked out, AdamW + grad-norm clip
     as the reference pipeline's step; DDP across ranks when world > 1.
     Variants: the fused loss on fp32 logits, the same objective in plain torch
-    ops on fp32 logits, and a bf16 lm_head feeding the fused bf16-logits loss.
-    GEMMs run on cuBLAS (TF32 for fp32 operands)."""
+    ops on fp32 logits, a bf16 lm_head feeding the fused bf16-logits loss, and
+    the whole drafter under bf16 autocast (fused SDPA kernels, bf16 GEMMs)
+    feeding the fused bf16-logits loss. GEMMs run on cuBLAS (TF32 for fp32
+    operands)."""
     import torch.nn as nn
 
     from losses import dpace_loss
@@ -433,11 +435,13 @@ def time_drafter_step(args, dev, world, max_over_ranks, barrier):
     def loss_torch(logits, tok):
         return torch_ops_dpace_loss(logits, tok, 0.5, mask)
 
-    variants = [("fused_loss_fp32_logits", head, loss_fused), ("torch_ops_loss_fp32_logits", head, loss_torch),
-                ("fused_loss_bf16_logits", head_bf16, loss_fused)]
+    variants = [("fused_loss_fp32_logits", head, loss_fused, False),
+                ("torch_ops_loss_fp32_logits", head, loss_torch, False),
+                ("fused_loss_bf16_logits", head_bf16, loss_fused, False),
+                ("bf16_autocast_drafter_fused_loss", head_bf16, loss_fused, True)]
     out = {}
     stream = torch.cuda.current_stream(dev)
-    for name, lm_head, lfn in variants:
+    for name, lm_head, lfn, autocast in variants:
         model = build(lm_head)
         core = model.module if world > 1 else model
         params = [p for p in model.parameters() if p.requires_grad]
@@ -445,8 +449,9 @@ def time_drafter_step(args, dev, world, max_over_ranks, barrier):
 
         def step():
             opt.zero_grad(set_to_none=True)
-            loss = core.compute_loss(feats, tokens, loss_fn=lfn) if world == 1 else \
-                lfn(model(feats), tokens)
+            with torch.autocast("cuda", dtype=torch.bfloat16, enabled=autocast):
+                loss = core.compute_loss(feats, tokens, loss_fn=lfn) if world == 1 else \
+                    lfn(model(feats), tokens)
             loss.backward()
             torch.nn.utils.clip_grad_norm_(params, 1.0)
             opt.step()

@@ -12,8 +12,10 @@ Architecture (model.py:76-150): target features -> proj_in -> append
 a mask where context tokens are causal and block tokens see every token ->
 RMSNorm -> proj_out -> optional RMSNorm -> frozen verifier lm_head ->
 [batch, block_size, V] logits. Attention runs through
-F.scaled_dot_product_attention; everything here is plain torch (the loss is
-the hot path, not the drafter).
+F.scaled_dot_product_attention; the mask is applied by its structure (a
+causal attention over the context plus an unmasked one for the block
+queries), so the fused SDPA kernels run without a [T, T] mask. Everything
+here is plain torch (the loss is the hot path, not the drafter).
 """
 from __future__ import annotations
 
@@ -41,11 +43,24 @@ class DFlashAttention(nn.Module):
         b, s, _ = t.shape
         return t.view(b, s, self.num_heads, self.head_dim).transpose(1, 2)
 
-    def forward(self, x: torch.Tensor, attn_mask: torch.Tensor | None = None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, attn_mask: torch.Tensor | None = None,
+                n_ctx: int | None = None) -> torch.Tensor:
+        """attn_mask: additive [.., T, T] mask (the reference's form). n_ctx
+        instead states the DFlash mask by its structure -- the first n_ctx
+        tokens causal among themselves and blind to the rest, the others
+        seeing every token -- and runs it as two mask-free attentions (causal
+        over the context; the block queries over all keys), which the fused
+        SDPA kernels handle without reading a [T, T] mask."""
         b, s, _ = x.shape
         q, k, v = self._heads(self.q_proj(x)), self._heads(self.k_proj(x)), self._heads(self.v_proj(x))
-        mask = None if attn_mask is None else attn_mask.to(q.dtype)
-        y = F.scaled_dot_product_attention(q, k, v, attn_mask=mask)
+        if n_ctx is not None and attn_mask is None:
+            y_ctx = F.scaled_dot_product_attention(q[:, :, :n_ctx], k[:, :, :n_ctx], v[:, :, :n_ctx],
+                                                   is_causal=True)
+            y_blk = F.scaled_dot_product_attention(q[:, :, n_ctx:], k, v)
+            y = torch.cat([y_ctx, y_blk], dim=2)
+        else:
+            mask = None if attn_mask is None else attn_mask.to(q.dtype)
+            y = F.scaled_dot_product_attention(q, k, v, attn_mask=mask)
         return self.out_proj(y.transpose(1, 2).reshape(b, s, self.d_model))
 
 
@@ -60,8 +75,9 @@ class DFlashTransformerLayer(nn.Module):
         self.mlp = nn.Sequential(nn.Linear(d_model, d_ffn, bias=False), nn.SiLU(),
                                  nn.Linear(d_ffn, d_model, bias=False))
 
-    def forward(self, x: torch.Tensor, attn_mask: torch.Tensor | None = None) -> torch.Tensor:
-        x = x + self.attn(self.norm1(x), attn_mask=attn_mask)
+    def forward(self, x: torch.Tensor, attn_mask: torch.Tensor | None = None,
+                n_ctx: int | None = None) -> torch.Tensor:
+        x = x + self.attn(self.norm1(x), attn_mask=attn_mask, n_ctx=n_ctx)
         return x + self.mlp(self.norm2(x))
 
 
@@ -105,9 +121,9 @@ class DFlashSpeculator(nn.Module):
         b, s_ctx, _ = target_features.shape
         h = torch.cat([self.proj_in(target_features),
                        self.slot_queries.expand(b, -1, -1).to(target_features.dtype)], dim=1)
-        mask = self._build_dflash_mask(s_ctx, self.block_size, target_features.device)
+        # the _build_dflash_mask rule, applied by structure (no [T, T] mask tensor)
         for layer in self.layers:
-            h = layer(h, attn_mask=mask)
+            h = layer(h, n_ctx=s_ctx)
         feat = self.proj_out(self.norm_out(h)[:, s_ctx:, :])
         if self.final_norm is not None:
             feat = self.final_norm(feat)

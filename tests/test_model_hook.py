@@ -56,6 +56,30 @@ def test_mask_rules():
     assert bool((m[0, 0, :4, :4][il[0], il[1]] == 0.0).all())
 
 
+def test_structured_mask_equals_explicit_mask():
+    """forward() applies the _build_dflash_mask rule by structure (a causal
+    attention over the context, an unmasked one for the block queries); the
+    result and every parameter gradient equal the explicit-mask form."""
+    model, _ = _model(7)
+    feats = torch.randn(B, S_CTX, D_TARGET)
+
+    def explicit(m, x):
+        b, s_ctx, _ = x.shape
+        h = torch.cat([m.proj_in(x), m.slot_queries.expand(b, -1, -1)], dim=1)
+        mask = m._build_dflash_mask(s_ctx, m.block_size, x.device)
+        for layer in m.layers:
+            h = layer(h, attn_mask=mask)
+        return m.lm_head(m.final_norm(m.proj_out(m.norm_out(h)[:, s_ctx:, :])))
+
+    a = model(feats)
+    b = explicit(model, feats)
+    assert (a - b).abs().max().item() < 1e-5
+    ga = torch.autograd.grad(a.square().sum(), [p for p in model.parameters() if p.requires_grad])
+    gb = torch.autograd.grad(b.square().sum(), [p for p in model.parameters() if p.requires_grad])
+    for x, y in zip(ga, gb):
+        assert (x - y).abs().max().item() <= 1e-5 * (1 + y.abs().max().item())
+
+
 def test_batch_invariance():
     model, _ = _model()
     feats = torch.randn(B, S_CTX, D_TARGET)
