@@ -552,14 +552,19 @@ def run_ours(args):
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize(dev)
+    # untimed soak of about args.soak seconds: every step holds a collective
+    # when world > 1, so all ranks run the same, agreed number of steps
+    probe = time.perf_counter()
+    for i in range(4):
+        step(i)
+    torch.cuda.synchronize(dev)
+    per_step = max((time.perf_counter() - probe) / 4, 1e-5)
+    soak_steps = int(max_over_ranks(float(int(args.soak / per_step)))) if args.soak > 0 else 0
     sampler = ClockSampler(dev)
     sampler.start()
-    t_soak = time.perf_counter() + args.soak
-    i = 0
-    while time.perf_counter() < t_soak:
+    for i in range(soak_steps):
         step(i)
-        i += 1
-        if i % 64 == 0:
+        if (i + 1) % 64 == 0:
             torch.cuda.synchronize(dev)
 
     # timed region: K uninstrumented steps (events between the kernels would
@@ -624,11 +629,16 @@ def run_ours(args):
         hm = [s[2].cpu().pin_memory() for s in sets]
         hloss = torch.empty((), dtype=torch.float32).pin_memory()
 
+        from specdec.dist import sharded_dpace_loss
+
         def e2e_step(i):
             x = hx[i & 1].to(dev, non_blocking=True).requires_grad_(True)
             t = ht[i & 1].to(dev, non_blocking=True)
             m = hm[i & 1].to(dev, non_blocking=True)
-            loss = dpace_loss(x, t, 0.5, m)
+            if world > 1:  # the multi-GPU entry point: this rank's shard, global loss
+                loss = sharded_dpace_loss(x, t, 0.5, m, n_global=n_global)
+            else:
+                loss = dpace_loss(x, t, 0.5, m)
             loss.backward()
             hloss.copy_(loss.detach(), non_blocking=True)
             return x
@@ -648,8 +658,9 @@ def run_ours(args):
         e2e = {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": UNIT,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4 + 4,
                "ms_per_step": round(e2e_ms, 3), "steps": args.e2e_steps,
-               "path": "losses.dpace.dpace_loss(...).backward() from pinned host buffers; "
-                       "includes the target-range check (4-byte read-back)"}
+               "path": ("specdec.dist.sharded_dpace_loss" if world > 1 else "losses.dpace.dpace_loss")
+                       + "(...).backward() from pinned host buffers; includes the target-range check "
+                         "(4-byte read-back)"}
 
     cpu_base = None
     if rank == 0 and world == 1 and args.cpu_budget > 0:
