@@ -78,7 +78,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 2, S, SE, T>
   if (warp == NC) {  // producer
     if (lane == 0) {
       const T* src[2] = {XL, XT};
-      if (!ring_produce<2, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow))
+      if (!ring_produce<2, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow,
+                                      a.withhold_stage && blockIdx.x == 0))
         atomicOr(a.flag, 2);
     }
     pdl_trigger();
@@ -255,7 +256,9 @@ __global__ void __launch_bounds__(1024) dflash_finalize_kernel(const __grid_cons
       __threadfence();
       const float total = warp_sum_l2(a.seq_loss, a.N);
       if (lane == 0) {
-        a.loss[0] = total / (float)a.n_global;
+        const int f = atomicExch(a.flag, 0);
+        // a timed-out copy wait left partials unwritten: the loss is NaN, not a wrong number
+        a.loss[0] = (f & 2) ? __int_as_float(0x7fc00000) : total / (float)a.n_global;
         *a.done_cnt = 0u;
       }
     }

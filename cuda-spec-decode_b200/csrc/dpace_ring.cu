@@ -235,8 +235,9 @@ __global__ void __launch_bounds__(1024) dpace_finalize_kernel(const __grid_const
       __threadfence();
       const float total = warp_sum_l2(a.seq_loss, a.N);
       if (lane == 0) {
-        a.loss[0] = total / (float)a.n_global;
         const int f = atomicExch(a.flag, 0);
+        // a timed-out copy wait left partials unwritten: the loss is NaN, not a wrong number
+        a.loss[0] = (f & 2) ? __int_as_float(0x7fc00000) : total / (float)a.n_global;
         if (a.status) a.status[0] = (f & 2) ? kStatusTimeout : ((f & 1) ? kStatusTargetRange : kStatusOk);
         *a.done_cnt = 0u;
       }

@@ -198,6 +198,15 @@ Partition dflash_fwd_partition(int64_t N, int32_t B, int64_t V, int kind, bool t
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Failure-detection test hook: 1 if this ring forward launch should withhold a
+// stage (consumes one of the launches armed by specdec_test_withhold_stage).
+int take_withhold_stage() {
+  int left = g_withhold_stage.load();
+  while (left > 0 && !g_withhold_stage.compare_exchange_weak(left, left - 1)) {
+  }
+  return left > 0 ? 1 : 0;
+}
+
 }  // namespace
 
 namespace specdec {
@@ -351,13 +360,7 @@ int dpace_forward_impl(int dtype, const void* logits, const int64_t* targets, co
   a.q_retired = cnt + 3;
   a.q_dynamic = g_static_queue.load() ? 0 : 1;
   a.seq_cnt = cnt + 4;
-  a.withhold_stage = 0;
-  if (tma) {
-    int left = g_withhold_stage.load();
-    while (left > 0 && !g_withhold_stage.compare_exchange_weak(left, left - 1)) {
-    }
-    a.withhold_stage = left > 0 ? 1 : 0;
-  }
+  a.withhold_stage = tma ? take_withhold_stage() : 0;
   a.pt = pt;
   const cudaError_t e =
       tma ? dpace_fwd_ring_launch(dtype, shape, a, (int)pt.grid, st) : dpace_fwd_launch(shape, a, st);
@@ -544,6 +547,7 @@ int dflash_forward_impl(int dtype, const void* logits, const void* target_logits
   a.q_dynamic = g_static_queue.load() ? 0 : 1;
   a.row_cnt = cnt + 4;
   a.nc = nc;
+  a.withhold_stage = tma ? take_withhold_stage() : 0;
   a.pt = pt;
   const cudaError_t e =
       tma ? dflash_fwd_ring_launch(dtype, shape, a, (int)pt.grid, st) : dflash_fwd_launch(shape, a, st);

@@ -100,6 +100,7 @@ struct DflashFwdArgs {
   unsigned* q_retired;
   int q_dynamic;
   int nc;                      // partials per (row, slot)
+  int withhold_stage;          // failure-detection tests: CTA 0 never posts its first stage
   Partition pt;                // ring kernel: chunk = block length
 };
 

@@ -247,12 +247,14 @@ int specdec_set_block_queue(int32_t dynamic);
 
 /*
  * Failure-detection test hook (no counterpart in the reference). The next
- * `launches` D-PACE forward launches on the ring path make CTA 0's producer
- * withhold its first stage, so that CTA's consumers reach the 1 s limit of
- * their bounded wait: they record the timeout, wait (bounded) for their own
- * copies, and return. The launch completes in about 2 s with *status =
- * SPECDEC_ERR_CUDA and unspecified loss values; the context stays usable and
- * the next launch is normal. 0 cancels. Not for production use.
+ * `launches` D-PACE or DFlash forward launches on the ring path make CTA 0's
+ * producer withhold its first stage, so that CTA's consumers reach the 1 s
+ * limit of their bounded wait: they record the timeout, wait (bounded) for
+ * their own copies, and return. The launch completes in about 2 s with a NaN
+ * loss (and, for D-PACE, *status = SPECDEC_ERR_CUDA); per-row outputs are
+ * unspecified; the context stays usable and the next launch is normal. 0
+ * cancels. Not for production use. The same NaN loss / status report any
+ * wait that expires for a real reason.
  */
 int specdec_test_withhold_stage(int32_t launches);
 

@@ -1,12 +1,13 @@
 """Failure detection on the GPU without a fault: a bounded wait that runs out.
 
-specdec_test_withhold_stage(1) makes CTA 0 of the next D-PACE forward never
-post its first stage. Its consumer warps wait on that stage's mbarrier, give up
+specdec_test_withhold_stage(1) makes CTA 0 of the next D-PACE or DFlash
+forward never post its first stage. Its consumer warps wait on that stage's mbarrier, give up
 after the 1 s limit, record the timeout in the status word, wait (bounded) for
 the copies they may still have in flight and return; the launch completes.
-The host must see the error (RuntimeError through the drop-in API, status 5
-through the C ABI) and the next call must be normal: context usable, counters
-zero, results equal to the oracle's."""
+The host must see the error (D-PACE: RuntimeError through the drop-in API,
+status 5 and a NaN loss through the C ABI; DFlash: a NaN loss) and the next
+call must be normal: context usable, counters zero, results equal to the
+oracle's."""
 import pytest
 import torch
 
@@ -71,6 +72,7 @@ def test_expired_wait_status_through_the_c_abi(cuda):
         assert call() == _lib.OK  # the launch itself succeeds
         torch.cuda.synchronize()
         assert int(status.item()) == _lib.ERR_CUDA
+        assert bool(torch.isnan(loss))  # never a plausible wrong number
     finally:
         lib.specdec_test_withhold_stage(0)
     counters.zero_()  # after a timeout the caller clears its counters
@@ -79,3 +81,25 @@ def test_expired_wait_status_through_the_c_abi(cuda):
     assert int(status.item()) == _lib.OK
     want, _ = odp.dpace_fwd_bwd_torch(x.cpu(), t.cpu())
     assert abs(float(loss) - float(want)) <= 1e-5 * abs(float(want))
+
+
+def test_dflash_expired_wait_gives_nan_loss_and_the_next_call_is_normal(cuda):
+    """The DFlash forward has no status word (its reference interface has no
+    device-side check): an expired wait shows as a NaN loss."""
+    from models.dflash import fused_dflash_loss
+    from oracle import dflash as odf
+    from specdec import _lib
+
+    x, _ = _inputs()
+    y = 0.5 * x  # a different distribution: KL well away from 0
+    lib = _lib.load()
+    try:
+        _lib.check(lib.specdec_test_withhold_stage(1), "specdec_test_withhold_stage")
+        loss = fused_dflash_loss(x, y)
+        torch.cuda.synchronize()
+        assert bool(torch.isnan(loss))
+    finally:
+        lib.specdec_test_withhold_stage(0)
+    want, _ = odf.dflash_fwd_bwd_torch(x.cpu(), y.cpu())
+    loss = float(fused_dflash_loss(x, y))
+    assert abs(loss - float(want)) <= 1e-5 * abs(float(want))
