@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(1024) dpace_finalize_kernel(const __grid_const
         lse_merge(m, s, v.x, v.y);
       }
       warp_lse(m, s);
-      lse = m + logf(s);
+      lse = __fadd_rn(m, logf(s));  // no contraction into logf: the same bits in every kernel
       if (tvalid) ce = lse - xt;
     }
     if (!tvalid && lane == 0) atomicOr(a.flag, 1);

@@ -45,6 +45,7 @@ std::atomic<int> g_shape[4] = {0, 0, 0, 0};
 std::atomic<int> g_cap[4] = {0, 0, 0, 0};
 std::atomic<int> g_static_queue{0};  // 1: ring kernels use a static block interleave
 std::atomic<int> g_withhold_stage{0};  // failure-detection tests: launches left to withhold a stage
+std::atomic<int> g_fused_lag_mib{48};   // forward+backward: L2 window between a block's two reads
 
 int current_device() {
   int d = 0;
@@ -131,9 +132,11 @@ struct DpaceLayout {
   size_t part = 0, xtgt = 0, seq_loss = 0, scratch = 0, counters = 0;
 };
 
+// Forward: [done][flag][queue ctr][queue retired][seq_cnt x N];
+// forward+backward: [finalized][flag][queue ctr][done warps][seq_done x N][ready x N].
 size_t dpace_counter_bytes(int64_t N, int64_t B) {
   (void)B;
-  return align256(16 + size_t(N) * sizeof(unsigned));
+  return align256(16 + 2 * size_t(N) * sizeof(unsigned));
 }
 
 DpaceLayout dpace_layout(int64_t N, int64_t B, const Partition& pt, int nc) {
@@ -247,6 +250,12 @@ int specdec_set_block_queue(int32_t dynamic) {
   return ok();
 }
 
+int specdec_set_fused_lag(int32_t mib) {
+  if (mib < 0 || mib > 4096) return fail(SPECDEC_ERR_ARGUMENT, "lag must be in [0, 4096] MiB");
+  g_fused_lag_mib.store(mib == 0 ? 48 : mib);
+  return ok();
+}
+
 int specdec_test_withhold_stage(int32_t launches) {
   if (launches < 0 || launches > 16) return fail(SPECDEC_ERR_ARGUMENT, "launches must be in [0, 16]");
   g_withhold_stage.store(launches);
@@ -271,10 +280,15 @@ size_t specdec_dpace_scratch_bytes(int64_t N, int32_t B, int64_t V, int device) 
   // alignment) and for either element type
   size_t best = dpace_layout(N, B, dpace_fwd_partition(N, B, V, false, device), 1).scratch;
   for (int dtype = kDtypeF32; dtype <= kDtypeBF16; ++dtype) {
-    if (dtype == kDtypeF32 && !use_tma(SPECDEC_KERNEL_DPACE_FWD, true)) continue;
-    const int nc = dpace_ring_consumers(ring_shape(SPECDEC_KERNEL_DPACE_FWD, dtype));
-    const size_t b = dpace_layout(N, B, dpace_fwd_partition(N, B, V, true, device, dtype), nc).scratch;
-    best = b > best ? b : best;
+    if (!(dtype == kDtypeF32 && !use_tma(SPECDEC_KERNEL_DPACE_FWD, true))) {
+      const int nc = dpace_ring_consumers(ring_shape(SPECDEC_KERNEL_DPACE_FWD, dtype));
+      const size_t b = dpace_layout(N, B, dpace_fwd_partition(N, B, V, true, device, dtype), nc).scratch;
+      best = b > best ? b : best;
+    }
+    // forward+backward kernel
+    const size_t c = dpace_layout(N, B, ring_partition(N * B, V, dpace_fused_block_elems(dtype), 1),
+                                  dpace_fused_consumers()).scratch;
+    best = c > best ? c : best;
   }
   return best;
 }
@@ -407,9 +421,153 @@ int dpace_backward_impl(int dtype, const void* logits, const int64_t* targets, c
   return e == cudaSuccess ? ok() : cuda_fail(e, "dpace backward launch");
 }
 
+int dpace_forward_backward_impl(int dtype, const void* logits, const int64_t* targets, const float* mask,
+                                int64_t N, int32_t B, int64_t V, float alpha, int32_t loss_type, int64_t n_global,
+                                float* loss, float* loss_n, float* lse, float* scale, void* dlogits,
+                                int32_t* status, void* scratch, size_t scratch_bytes, void* counters,
+                                size_t counter_bytes, void* stream) {
+  if (B < 1 || B > 32) return fail(SPECDEC_ERR_ARGUMENT, "kernel configured for block_size <= 32 (B=%d)", B);
+  if (N < 0 || V < 0) return fail(SPECDEC_ERR_ARGUMENT, "negative shape N=%lld V=%lld", (long long)N, (long long)V);
+  if (!(alpha >= 0.f && alpha <= 1.f))
+    return fail(SPECDEC_ERR_VALUE, "dpace_alpha must be in [0, 1], got %g", (double)alpha);
+  if (loss_type < 0 || loss_type > 2) return fail(SPECDEC_ERR_VALUE, "unknown loss_type %d", loss_type);
+  if (N > 0 && (n_global < N || n_global < 1))
+    return fail(SPECDEC_ERR_ARGUMENT, "n_global (%lld) must be >= N (%lld)", (long long)n_global, (long long)N);
+  if (!loss) return fail(SPECDEC_ERR_ARGUMENT, "loss output is null");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (N == 0) {
+    cudaError_t e = cudaMemsetAsync(loss, 0xff, sizeof(float), st);
+    if (e == cudaSuccess && status) e = cudaMemsetAsync(status, 0, sizeof(int32_t), st);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "cudaMemsetAsync");
+  }
+  if (V == 0) return fail(SPECDEC_ERR_TARGET_RANGE, "targets out of range [0, 0)");
+  if (!logits || !targets || !lse || !scale || !dlogits || !scratch || !counters)
+    return fail(SPECDEC_ERR_ARGUMENT, "null input, output or workspace pointer");
+  if (logits == dlogits) return fail(SPECDEC_ERR_ARGUMENT, "dlogits must not alias logits");
+  if (!aligned(targets, 8) || !aligned(lse, 4) || !aligned(scale, 4) || !aligned(scratch, 256) ||
+      !aligned(counters, 16))
+    return fail(SPECDEC_ERR_ARGUMENT, "misaligned pointer (scratch needs 256 B, counters 16 B)");
+  const bool ptrs16 = aligned(logits, 16) && aligned(dlogits, 16);
+  if (dtype == kDtypeBF16 && !ptrs16) return fail(SPECDEC_ERR_ARGUMENT, "bf16 logits and dlogits must be 16-byte aligned");
+  if (!ptrs16 || !use_tma(SPECDEC_KERNEL_DPACE_FWD, true)) {
+    // the 128-bit-load kernels: forward, then backward (no L2 reuse)
+    const int rc = dpace_forward_impl(dtype, logits, targets, mask, N, B, V, alpha, loss_type, n_global, loss,
+                                      loss_n, lse, scale, status, scratch, scratch_bytes, counters, counter_bytes,
+                                      stream);
+    if (rc != SPECDEC_OK) return rc;
+    return dpace_backward_impl(dtype, logits, targets, lse, scale, nullptr, dlogits, N, B, V, nullptr, 0, stream);
+  }
+  const int dev = current_device();
+  if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
+  const int ctas = dpace_fused_ctas(dtype, dev, g_cap[SPECDEC_KERNEL_DPACE_FWD].load());
+  if (ctas <= 0) return fail(SPECDEC_ERR_CUDA, "occupancy query failed");
+  const int64_t BL = dpace_fused_block_elems(dtype);
+  const Partition pt = ring_partition(N * B, V, BL, ctas);
+  const int nc = dpace_fused_consumers();
+  const DpaceLayout L = dpace_layout(N, B, pt, nc);
+  if (scratch_bytes < L.scratch)
+    return fail(SPECDEC_ERR_WORKSPACE, "scratch needs %zu bytes, got %zu", L.scratch, scratch_bytes);
+  if (counter_bytes < L.counters)
+    return fail(SPECDEC_ERR_WORKSPACE, "counters need %zu bytes, got %zu", L.counters, counter_bytes);
+  char* ws = static_cast<char*>(scratch);
+  unsigned* cnt = static_cast<unsigned*>(counters);
+  DpaceFusedArgs a;
+  DpaceFwdArgs& f = a.f;
+  f.logits = logits;
+  f.targets = targets;
+  f.mask = mask;
+  f.N = N;
+  f.B = B;
+  f.V = V;
+  f.alpha = alpha;
+  f.one_minus_alpha = (float)(1.0 - (double)alpha);
+  f.loss_type = loss_type;
+  f.n_global = n_global;
+  f.inv_n = (float)(1.0 / (double)n_global);
+  f.loss = loss;
+  f.loss_n = loss_n;
+  f.lse = lse;
+  f.scale = scale;
+  f.status = status;
+  f.part = reinterpret_cast<float2*>(ws + L.part);
+  f.xtgt = nullptr;
+  f.seq_loss = reinterpret_cast<float*>(ws + L.seq_loss);
+  f.seq_cnt = nullptr;
+  f.done_cnt = cnt;
+  f.flag = reinterpret_cast<int*>(cnt + 1);
+  f.q_ctr = cnt + 2;
+  f.q_retired = nullptr;
+  f.q_dynamic = 1;
+  f.nc = nc;
+  f.withhold_stage = 0;
+  f.pt = pt;
+  a.dlogits = dlogits;
+  a.done_warps = cnt + 3;
+  a.seq_done = cnt + 4;
+  a.ready = cnt + 4 + N;
+  // lag: about g_fused_lag_mib of logits between a block's F and B reads, and
+  // at least one sequence's worth of blocks (every F block a B block needs is
+  // then handed out before it)
+  const int64_t esz = dtype == kDtypeBF16 ? 2 : 4;
+  const int64_t lag_blocks = ((int64_t)g_fused_lag_mib.load() << 20) / (BL * esz);
+  const int64_t seq_blocks = ((int64_t)B * V + BL - 1) / BL + 1;
+  a.lag = lag_blocks > seq_blocks ? lag_blocks : seq_blocks;
+  a.withhold_stage = take_withhold_stage();
+  const cudaError_t e = dpace_fused_launch(dtype, a, ctas, st);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "dpace forward+backward launch");
+}
+
 }  // namespace
 
 extern "C" {
+
+int specdec_dpace_forward_backward(const float* logits, const int64_t* targets, const float* mask, int64_t N,
+                                   int32_t B, int64_t V, float alpha, int32_t loss_type, int64_t n_global,
+                                   float* loss, float* loss_n, float* lse, float* scale, float* dlogits,
+                                   int32_t* status, void* scratch, size_t scratch_bytes, void* counters,
+                                   size_t counter_bytes, void* stream) {
+  return dpace_forward_backward_impl(kDtypeF32, logits, targets, mask, N, B, V, alpha, loss_type, n_global, loss,
+                                     loss_n, lse, scale, dlogits, status, scratch, scratch_bytes, counters,
+                                     counter_bytes, stream);
+}
+
+int specdec_dpace_forward_backward_bf16(const uint16_t* logits, const int64_t* targets, const float* mask,
+                                        int64_t N, int32_t B, int64_t V, float alpha, int32_t loss_type,
+                                        int64_t n_global, float* loss, float* loss_n, float* lse, float* scale,
+                                        uint16_t* dlogits, int32_t* status, void* scratch, size_t scratch_bytes,
+                                        void* counters, size_t counter_bytes, void* stream) {
+  return dpace_forward_backward_impl(kDtypeBF16, logits, targets, mask, N, B, V, alpha, loss_type, n_global,
+                                     loss, loss_n, lse, scale, dlogits, status, scratch, scratch_bytes, counters,
+                                     counter_bytes, stream);
+}
+
+}  // extern "C"
+
+namespace {
+int scale_inplace_impl(int dtype, void* x, int64_t n, const float* factor, void* stream) {
+  if (n < 0) return fail(SPECDEC_ERR_ARGUMENT, "negative length");
+  if (n == 0) return ok();
+  if (!x || !factor) return fail(SPECDEC_ERR_ARGUMENT, "null pointer");
+  if (!aligned(x, 16)) return fail(SPECDEC_ERR_ARGUMENT, "x must be 16-byte aligned");
+  const int dev = current_device();
+  if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return fail(SPECDEC_ERR_CUDA, "device query failed");
+  const cudaError_t e = scale_inplace_launch(dtype, x, n, factor, sms * 4, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "scale launch");
+}
+}  // namespace
+
+extern "C" {
+
+int specdec_scale_inplace(float* x, int64_t n, const float* factor, void* stream) {
+  return scale_inplace_impl(kDtypeF32, x, n, factor, stream);
+}
+
+int specdec_scale_inplace_bf16(uint16_t* x, int64_t n, const float* factor, void* stream) {
+  return scale_inplace_impl(kDtypeBF16, x, n, factor, stream);
+}
 
 int specdec_dpace_forward(const float* logits, const int64_t* targets, const float* mask,
                           int64_t N, int32_t B, int64_t V, float alpha, int32_t loss_type,

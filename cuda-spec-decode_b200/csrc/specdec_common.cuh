@@ -166,9 +166,12 @@ __device__ __forceinline__ float2 vec8_expsum2(const uint4& v, float m) {
   return fadd2(fadd2(e0, e1), fadd2(e2, e3));
 }
 
+// The rounding is spelled out (one product, then one fused multiply-add) so
+// that every kernel that merges the same partials gets the same bits; left
+// to the compiler, either product may be the one contracted.
 __device__ __forceinline__ void lse_merge(float& m, float& s, float om, float os) {
   const float M = fmaxf(m, om);
-  s = s * exp_shift(m, M) + os * exp_shift(om, M);
+  s = __fmaf_rn(s, exp_shift(m, M), __fmul_rn(os, exp_shift(om, M)));
   m = M;
 }
 

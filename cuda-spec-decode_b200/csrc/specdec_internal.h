@@ -71,6 +71,19 @@ struct DpaceBwdArgs {
   Partition pt;
 };
 
+// D-PACE forward and backward in one launch (dpace_fused.cu). `f` carries
+// the forward's arguments and workspace; its done_cnt counts finalized
+// sequences, q_ctr is the work queue.
+struct DpaceFusedArgs {
+  DpaceFwdArgs f;
+  void* dlogits;           // element type of the logits
+  unsigned* seq_done;      // [N] finished F-block shares per sequence; zero on entry/exit
+  unsigned* ready;         // [N] sequence finalized; zero on entry/exit
+  unsigned* done_warps;    // [1] consumer warps that have exited; zero on entry/exit
+  int64_t lag;             // D: B block b is handed out about D blocks after F block b
+  int withhold_stage;      // failure-detection tests: CTA 0 never posts its first stage
+};
+
 struct DflashFwdArgs {
   const void* logits;          // draft [N, B, V] (float, or bf16 for the bf16 ring kernels)
   const void* target_logits;   // verifier [N, B, V], same element type
@@ -145,6 +158,13 @@ int dflash_fwd_ring_ctas(int dtype, int kind, int shape, int device, int cap_per
 int dflash_bwd_ring_ctas(int dtype, int kind, int shape, int device, int cap_per_sm);
 cudaError_t dflash_fwd_ring_launch(int dtype, int shape, const DflashFwdArgs& a, int ctas, cudaStream_t st);
 cudaError_t dflash_bwd_ring_launch(int dtype, int shape, const DflashBwdArgs& a, int ctas, cudaStream_t st);
+
+// Fused D-PACE forward + backward (dpace_fused.cu).
+int dpace_fused_block_elems(int dtype);
+int dpace_fused_consumers();
+int dpace_fused_ctas(int dtype, int device, int cap_per_sm);
+cudaError_t dpace_fused_launch(int dtype, const DpaceFusedArgs& a, int ctas, cudaStream_t st);
+cudaError_t scale_inplace_launch(int dtype, void* x, int64_t n, const float* factor, int ctas, cudaStream_t st);
 
 // Sets the calling thread's specdec_last_error() text.
 void set_last_error(const char* msg);

@@ -86,12 +86,25 @@ def fused_dpace_loss(logits: torch.Tensor, targets: torch.Tensor, alpha: float =
 
 class DPACELoss(torch.autograd.Function):
     """Autograd glue (reference: losses/dpace.py:201-226). The weights are
-    detached, so the backward is one fused pass: (w_j/N)(softmax - onehot)."""
+    detached, so the gradient is one fused expression: (w_j/N)(softmax - onehot).
+
+    When the logits need a gradient, the forward computes it together with the
+    loss in one launch that reads the logits from HBM once
+    (specdec_dpace_forward_backward) and keeps it; the backward then only
+    multiplies by dloss on the device, which is no pass at all when dloss is 1
+    (loss.backward()). A second backward through the same graph
+    (retain_graph) recomputes the gradient with the separate kernel."""
 
     @staticmethod
     def forward(ctx, logits, targets, alpha, position_mask, loss_type, n_global=None):
         x, t, mask = _prepare(logits, targets, position_mask)
-        loss, lse, scale = _forward(x, t, mask, alpha, loss_type, n_global)
+        ctx.grad = None
+        if ops.FUSED_BACKWARD and ctx.needs_input_grad[0] and x.numel():
+            _check(x, t, mask, alpha, loss_type)
+            loss, ctx.grad, lse, scale, _ = ops.dpace_forward_backward(
+                x, t, mask, alpha, _LOSS_TYPES[loss_type], n_global=n_global)
+        else:
+            loss, lse, scale = _forward(x, t, mask, alpha, loss_type, n_global)
         ctx.save_for_backward(x, t, lse, scale)
         return loss
 
@@ -100,7 +113,12 @@ class DPACELoss(torch.autograd.Function):
         x, t, lse, scale = ctx.saved_tensors
         grad = None
         if ctx.needs_input_grad[0]:
-            grad = ops.dpace_backward(x, t, lse, scale, dloss) if x.numel() else torch.zeros_like(x)
+            if ctx.grad is not None:
+                grad, ctx.grad = ctx.grad, None
+                if dloss is not None:
+                    ops.scale_inplace(grad, dloss)
+            else:
+                grad = ops.dpace_backward(x, t, lse, scale, dloss) if x.numel() else torch.zeros_like(x)
         return grad, None, None, None, None, None
 
 

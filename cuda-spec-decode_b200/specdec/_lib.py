@@ -64,10 +64,15 @@ _SIGNATURES = {
     "specdec_launch_ctas": (_c_i64, [_c_i32, _c_i64, _c_i64, ctypes.c_int]),
     "specdec_set_block_queue": (ctypes.c_int, [_c_i32]),
     "specdec_test_withhold_stage": (ctypes.c_int, [_c_i32]),
+    "specdec_set_fused_lag": (ctypes.c_int, [_c_i32]),
+    "specdec_dpace_forward_backward": (ctypes.c_int, [
+        _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_f32, _c_i32, _c_i64,
+        _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_sz, _c_p, _c_sz, _c_p]),
+    "specdec_scale_inplace": (ctypes.c_int, [_c_p, _c_i64, _c_p, _c_p]),
 }
 # bf16 entry points take the same arguments as their fp32 counterparts
 for _name in ("specdec_dpace_forward", "specdec_dpace_backward", "specdec_dflash_forward",
-              "specdec_dflash_backward"):
+              "specdec_dflash_backward", "specdec_dpace_forward_backward", "specdec_scale_inplace"):
     _SIGNATURES[_name + "_bf16"] = _SIGNATURES[_name]
 
 _lib = None

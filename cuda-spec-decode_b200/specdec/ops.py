@@ -30,6 +30,18 @@ def set_target_validation(enabled: bool) -> None:
     VALIDATE_TARGETS = bool(enabled)
 
 
+# When True (default) the autograd path of D-PACE computes the gradient in its
+# forward with specdec_dpace_forward_backward (one HBM read of the logits;
+# the backward then only applies dloss, with no pass at all when dloss is 1).
+# False: separate forward and backward launches, as the reference.
+FUSED_BACKWARD = True
+
+
+def set_fused_backward(enabled: bool) -> None:
+    global FUSED_BACKWARD
+    FUSED_BACKWARD = bool(enabled)
+
+
 # Element types of the logits the kernels take; the gradient has the logits'
 # type. bf16 calls go to the *_bf16 entry points (fp32 arithmetic inside).
 LOGIT_DTYPES = (torch.float32, torch.bfloat16)
@@ -79,6 +91,53 @@ def _dpace_forward(logits: torch.Tensor, targets: torch.Tensor, mask: torch.Tens
             ws.reset_counters()
             raise RuntimeError("specdec_dpace_forward: a bulk-copy wait timed out")
     return loss, lse, scale, loss_n
+
+
+def _dpace_forward_backward(logits: torch.Tensor, targets: torch.Tensor, mask: torch.Tensor | None,
+                            alpha: float, loss_type: int, n_global: int | None = None,
+                            want_loss_n: bool = False, validate: bool | None = None,
+                            out: torch.Tensor | None = None):
+    """Loss and gradient (dloss = 1) in one launch that reads the logits from
+    HBM once. Returns (loss 0-d, dlogits, lse [N,B], scale [N,B], loss_n or None)."""
+    lib = _lib.load()
+    N, B, V = logits.shape
+    dev = logits.device
+    n_global = N if n_global is None else int(n_global)
+    logits = _aligned(logits)
+    loss = torch.empty((), dtype=torch.float32, device=dev)
+    lse = torch.empty((N, B), dtype=torch.float32, device=dev)
+    scale = torch.empty((N, B), dtype=torch.float32, device=dev)
+    loss_n = torch.empty((N,), dtype=torch.float32, device=dev) if want_loss_n else None
+    dlogits = torch.empty_like(logits) if out is None else out
+    status = torch.empty((1,), dtype=torch.int32, device=dev)
+    ws = _lib.workspace("dpace", dev)
+    sb = lib.specdec_dpace_scratch_bytes(N, B, V, dev.index)
+    cb = lib.specdec_dpace_counter_bytes(N, B)
+    scratch, counters = ws.ensure(dev, sb, cb)
+    code = _entry(lib, "specdec_dpace_forward_backward", logits)(
+        logits.data_ptr(), targets.data_ptr(), _lib.ptr(mask), N, B, V, float(alpha),
+        int(loss_type), n_global, loss.data_ptr(), _lib.ptr(loss_n), lse.data_ptr(),
+        scale.data_ptr(), dlogits.data_ptr(), status.data_ptr(), scratch.data_ptr(), scratch.numel(),
+        counters.data_ptr(), counters.numel(), _lib.stream_handle(dev))
+    _lib.check(code, "specdec_dpace_forward_backward")
+    if (VALIDATE_TARGETS if validate is None else validate) and N * B > 0:
+        st = int(status.item())
+        if st == _lib.ERR_TARGET_RANGE:
+            raise ValueError(f"targets out of range [0, {V})")
+        if st == _lib.ERR_CUDA:
+            ws.reset_counters()
+            raise RuntimeError("specdec_dpace_forward_backward: a bulk-copy wait timed out")
+    return loss, dlogits, lse, scale, loss_n
+
+
+def _scale_inplace(x: torch.Tensor, factor: torch.Tensor) -> torch.Tensor:
+    """x *= factor (a 1-element device tensor); no pass over x when factor == 1."""
+    lib = _lib.load()
+    f = factor.detach().to(device=x.device, dtype=torch.float32).reshape(1).contiguous()
+    code = _entry(lib, "specdec_scale_inplace", x)(x.data_ptr(), x.numel(), f.data_ptr(),
+                                                    _lib.stream_handle(x.device))
+    _lib.check(code, "specdec_scale_inplace")
+    return x
 
 
 def _dpace_backward(logits: torch.Tensor, targets: torch.Tensor, lse: torch.Tensor,
@@ -164,5 +223,7 @@ def _on_device(fn):
 # whatever the caller's current device is.
 dpace_forward = _on_device(_dpace_forward)
 dpace_backward = _on_device(_dpace_backward)
+dpace_forward_backward = _on_device(_dpace_forward_backward)
+scale_inplace = _on_device(_scale_inplace)
 dflash_forward = _on_device(_dflash_forward)
 dflash_backward = _on_device(_dflash_backward)

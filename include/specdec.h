@@ -115,6 +115,39 @@ int specdec_dpace_backward(const float* logits, const int64_t* targets, const fl
                            void* stream);
 
 /*
+ * D-PACE forward and backward in one call, for callers that want the loss and
+ * the gradient together (dloss = 1): the loss, lse, scale (and loss_n) of
+ * specdec_dpace_forward and the dlogits of specdec_dpace_backward with a
+ * NULL dloss, bit for bit, in one persistent launch that reads the logits
+ * from HBM once -- the backward half re-reads each 64 KB block from L2 about
+ * specdec_set_fused_lag() MiB after the forward half read it. No single
+ * counterpart in the reference (losses/dpace.py:176-187 + :217-226 as one
+ * launch). Arguments as in specdec_dpace_forward plus `dlogits` [N, B, V]
+ * (same element type as logits, must not alias it); same workspace queries.
+ * logits/dlogits not 16-byte aligned: runs the forward and backward kernels
+ * one after the other instead (fp32; bf16 requires alignment).
+ */
+int specdec_dpace_forward_backward(const float* logits, const int64_t* targets, const float* mask, int64_t N,
+                                   int32_t B, int64_t V, float alpha, int32_t loss_type, int64_t n_global,
+                                   float* loss, float* loss_n, float* lse, float* scale, float* dlogits,
+                                   int32_t* status, void* scratch, size_t scratch_bytes, void* counters,
+                                   size_t counter_bytes, void* stream);
+int specdec_dpace_forward_backward_bf16(const uint16_t* logits, const int64_t* targets, const float* mask,
+                                        int64_t N, int32_t B, int64_t V, float alpha, int32_t loss_type,
+                                        int64_t n_global, float* loss, float* loss_n, float* lse, float* scale,
+                                        uint16_t* dlogits, int32_t* status, void* scratch, size_t scratch_bytes,
+                                        void* counters, size_t counter_bytes, void* stream);
+
+/*
+ * x[i] *= *factor for i < n, on the device (16-byte-aligned x); returns
+ * without touching x when *factor == 1 (checked on the device). Applies an
+ * upstream gradient to a gradient computed with dloss = 1. No counterpart in
+ * the reference.
+ */
+int specdec_scale_inplace(float* x, int64_t n, const float* factor, void* stream);
+int specdec_scale_inplace_bf16(uint16_t* x, int64_t n, const float* factor, void* stream);
+
+/*
  * D-PACE forward without any caller-provided workspace. No counterpart in the
  * reference: it serves callers that cannot allocate device memory -- plugin
  * hosts that pass only input and output buffers, and processes whose device
@@ -244,6 +277,13 @@ int64_t specdec_launch_ctas(int32_t kernel, int64_t rows, int64_t V, int device)
  * default) or a static interleave (dynamic = 0), process-wide.
  */
 int specdec_set_block_queue(int32_t dynamic);
+
+/*
+ * Forward+backward: MiB of logits between a block's forward read and its
+ * backward read (the L2 window); 0 restores the default (48). Values beyond
+ * what L2 holds make the backward half read from HBM again.
+ */
+int specdec_set_fused_lag(int32_t mib);
 
 /*
  * Failure-detection test hook (no counterpart in the reference). The next

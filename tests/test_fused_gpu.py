@@ -1,0 +1,119 @@
+"""D-PACE forward + backward in one launch (specdec_dpace_forward_backward):
+bit-for-bit equal to the separate forward and backward kernels, whatever the
+L2 window (lag); dloss applied by the autograd backward; a second backward
+through a retained graph; expired waits reported; CUDA graph capture."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import dpace as odp
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(N, B, V, seed, dtype=torch.float32, mask_p=0.8, sigma=2.0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = (torch.randn(N, B, V, device="cuda", generator=g) * sigma).to(dtype)
+    t = torch.randint(0, V, (N, B), device="cuda", generator=g)
+    m = (torch.rand(N, B, device="cuda", generator=g) < mask_p).float()
+    return x, t, m
+
+
+def _separate(x, t, m, alpha, lt):
+    from specdec import ops
+
+    loss, lse, scale, _ = ops.dpace_forward(x, t, m, alpha, lt)
+    return loss, ops.dpace_backward(x, t, lse, scale, None), lse, scale
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("N,B,V,lt", [(64, 16, 128256, 0), (8, 32, 50257, 2), (40, 7, 3001, 1),
+                                      (200, 4, 37, 0), (3, 1, 1, 0), (16, 16, 16384, 2)])
+def test_fused_equals_separate_kernels(cuda, dtype, N, B, V, lt):
+    from specdec import ops
+
+    x, t, m = _inputs(N, B, V, N * 7 + V, dtype)
+    loss_s, grad_s, lse_s, scale_s = _separate(x, t, m, 0.5, lt)
+    loss_f, grad_f, lse_f, scale_f, _ = ops.dpace_forward_backward(x, t, m, 0.5, lt)
+    torch.cuda.synchronize()
+    assert float(loss_f) == float(loss_s)
+    assert torch.equal(lse_f, lse_s) and torch.equal(scale_f, scale_s)
+    assert torch.equal(grad_f, grad_s)
+
+
+@pytest.mark.parametrize("lag_mib", [1, 8, 48, 4096])
+def test_lag_does_not_change_results(cuda, lag_mib):
+    from specdec import _lib, ops
+
+    x, t, m = _inputs(32, 16, 128256, 5)
+    loss_s, grad_s, _, _ = _separate(x, t, m, 0.5, 0)
+    try:
+        _lib.check(_lib.load().specdec_set_fused_lag(lag_mib), "specdec_set_fused_lag")
+        loss_f, grad_f, _, _, _ = ops.dpace_forward_backward(x, t, m, 0.5, 0)
+        torch.cuda.synchronize()
+    finally:
+        _lib.load().specdec_set_fused_lag(0)
+    assert float(loss_f) == float(loss_s) and torch.equal(grad_f, grad_s)
+
+
+def test_autograd_uses_dloss_and_matches_oracle(cuda):
+    from losses import dpace_loss
+
+    x, t, m = _inputs(6, 16, 20000, 11)
+    want, g_ref = odp.dpace_fwd_bwd_torch(x.cpu(), t.cpu(), 0.5, m.cpu())
+    for factor in (1.0, 3.0, -0.25):
+        xg = x.clone().requires_grad_(True)
+        loss = dpace_loss(xg, t, 0.5, m)
+        (loss * factor).backward()
+        assert abs(float(loss) - float(want)) <= 1e-5 * abs(float(want))
+        assert float((xg.grad.cpu() - factor * g_ref).abs().max()) <= 1e-6 * max(1.0, abs(factor))
+
+
+def test_retained_graph_second_backward(cuda):
+    from losses import dpace_loss
+
+    x, t, m = _inputs(4, 16, 9000, 12)
+    xg = x.clone().requires_grad_(True)
+    loss = dpace_loss(xg, t, 0.5, m)
+    loss.backward(retain_graph=True)
+    g1 = xg.grad.clone()
+    loss.backward()
+    assert float((xg.grad - 2 * g1).abs().max()) <= 1e-6
+
+
+def test_fused_expired_wait_reported_then_normal(cuda):
+    from specdec import _lib, ops
+
+    x, t, m = _inputs(64, 16, 40000, 13)
+    lib = _lib.load()
+    try:
+        _lib.check(lib.specdec_test_withhold_stage(1), "specdec_test_withhold_stage")
+        with pytest.raises(RuntimeError, match="timed out"):
+            ops.dpace_forward_backward(x, t, m, 0.5, 0)
+    finally:
+        lib.specdec_test_withhold_stage(0)
+    torch.cuda.synchronize()
+    loss_s, grad_s, _, _ = _separate(x, t, m, 0.5, 0)
+    loss_f, grad_f, _, _, _ = ops.dpace_forward_backward(x, t, m, 0.5, 0)
+    torch.cuda.synchronize()
+    assert float(loss_f) == float(loss_s) and torch.equal(grad_f, grad_s)
+
+
+def test_fused_graph_capture(cuda):
+    from specdec import ops
+
+    x, t, m = _inputs(8, 16, 50000, 14)
+    side = torch.cuda.Stream()
+    for _ in range(2):
+        with torch.cuda.stream(side):
+            ops.dpace_forward_backward(x, t, m, 0.5, 0, validate=False)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        loss_g, grad_g, _, _, _ = ops.dpace_forward_backward(x, t, m, 0.5, 0, validate=False)
+    g = torch.Generator(device="cuda").manual_seed(99)
+    x.copy_(torch.randn(x.shape, device="cuda", generator=g) * 2)
+    graph.replay()
+    torch.cuda.synchronize()
+    loss_s, grad_s, _, _ = _separate(x, t, m, 0.5, 0)
+    assert float(loss_g) == float(loss_s) and torch.equal(grad_g, grad_s)
