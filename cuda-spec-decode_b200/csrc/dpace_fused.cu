@@ -3,35 +3,43 @@
 //
 // The separate forward / backward kernels (dpace_ring.cu) read every live
 // logit twice from HBM (forward, then backward) and write the gradient once.
-// Here one grid works through a single queue of 64 KB blocks in which each
-// forward (F) block b is followed, about D blocks later, by the backward (B)
-// block b over the same elements:
+// Here one grid works through two queues of blocks (BL elements, 64 KB):
 //   F: stream the logits (bulk copies with an L2 evict_last policy), keep the
 //      per-piece (max, sum of e^(x - max)) partials as the forward kernel
-//      does. When a CTA finishes an F block it counts it for every sequence
-//      the block overlaps; the CTA that completes a sequence's count
-//      finalizes that sequence in place (merge partials -> lse, ce, the
-//      B-scan, scale, loss_n) and publishes a per-sequence ready flag
-//      (release store).
-//   B: stream the same logits again -- within about D x 64 KB of their F
-//      read, so from L2 (loads marked evict_first, the last use) -- wait
-//      (acquire load, bounded) for the row's sequence to be ready, and write
+//      does. When a warp finishes its share of an F block it counts it for
+//      every sequence the block overlaps; the warp that completes a
+//      sequence's count finalizes that sequence in place (merge partials ->
+//      lse, ce, the B-scan, scale, loss_n) and publishes a per-sequence ready
+//      flag (release store).
+//   B: stream the same logits again, soon after their F read, so from L2
+//      (loads marked evict_first, the last use), and write
 //      scale * (softmax - onehot) with streaming stores.
 // HBM traffic per call: one read of the live logits and one write of the
 // gradient, instead of two reads and one write.
 //
-// Coordination is per warp, with no CTA barrier in the loop (a barrier has
-// no timeout): each consumer warp counts its own share of a finished F block,
-// and the warp whose count completes a sequence finalizes it alone.
-// Deadlock freedom: the grid is exactly the resident capacity (persistent
-// CTAs); F work never waits on other warps; the lag D is at least one
-// sequence's worth of blocks, so every F block a B block depends on is handed
-// out before it, and a CTA processes its blocks in hand-out order -- a wait
-// can never close a cycle. Every wait is still bounded (1 s): an expired one
-// sets the flag and the call reports status 5 with a NaN loss.
+// Scheduling is done by each CTA's producer lane, so consumer warps never
+// wait on another CTA. F blocks come from one grid-wide queue; each CTA keeps
+// the F blocks it read in a FIFO and re-reads them itself (its B pass) --
+// L2 is split between the two dies and a partition caches the lines of its
+// own SMs' accesses, so the re-read must come from the SM that made the
+// first read. The producer issues the oldest B block as soon as the
+// sequences it overlaps are ready (acquire loads); until then it claims and
+// issues F blocks, as long as the F front is less than `ahead` sequences past
+// the number of finalized sequences -- that cap bounds how far the F reads
+// run ahead of their B re-reads (the L2 window).
+// Deadlock freedom: a producer waits only when its oldest B block is not
+// ready and no F block can be claimed. If the cap is closed, every F block
+// before the front has been claimed and issued by a running CTA (F work
+// depends on nothing), so the sequences before the front get finalized and
+// the cap opens. If its FIFO is full, the newest entry lies past the last
+// block of the oldest entry's sequences (the FIFO holds more than a
+// sequence's blocks + 2), so those sequences are claimed in full and get
+// finalized. Every wait is still bounded (1 s): an expired one sets the flag
+// and the call reports status 5 with a NaN loss. Blocks must overlap at most
+// two sequences (B * V >= BL); the host runs the separate kernels otherwise.
 //
 // Results equal the separate kernels' bit for bit (same partial layout and
-// merge order, same finalize arithmetic, same gradient expression).
+// merge tree, same finalize arithmetic, same gradient expression).
 //
 // Reference behaviour: losses/dpace.py:15-145; numbers follow
 // losses/dpace_ref.py:8-51.
@@ -45,49 +53,45 @@ namespace specdec {
 
 namespace {
 
-// Work item w -> (phase, block): F blocks 0..D-1 first, then B block k and
-// F block D+k alternate; when the F blocks run out, the rest are B blocks.
-__device__ __forceinline__ void fused_map(int64_t w, int64_t nb, int64_t D, int& phase, int64_t& b) {
-  if (w < D) {
-    phase = 0;
-    b = w;
-  } else if (w < 2 * nb - D) {
-    const int64_t k = w - D;
-    phase = (k & 1) ? 0 : 1;
-    b = (k & 1) ? D + (k >> 1) : (k >> 1);
-  } else {
-    phase = 1;
-    b = w - nb;
-  }
-}
+// F blocks a CTA has read and not yet re-read (its B queue). The host keeps
+// one sequence's blocks + 2 within it (dpace_fused_max_seq_blocks).
+constexpr int kFifo = 1024;
 
 template <int S, int SE, class T>
 struct FusedSmem {
   RingSmem<1, S, SE, T> ring;
-  int sph[S];  // phase of the stage in each slot
+  int sph[S];         // phase of the stage in each slot
+  int fifo[kFifo];    // producer only
 };
 
-// Bounded wait until the sequence's ready flag is set (every lane loads it
-// with acquire semantics, so each lane's later loads see the finalize's
-// stores). False on timeout.
-__device__ __forceinline__ bool wait_ready(const unsigned* ready) {
-  if (ld_acquire(ready)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  while (!ld_acquire(ready)) {
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
-  }
-  return true;
+__device__ __forceinline__ unsigned ld_relaxed(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
-// Finalize sequence n with one warp (lane j <-> row j, B <= 32): the
-// arithmetic of dpace_finalize_kernel. The partial loads of all rows are
-// issued before any merge.
+// Finalize sequence n with one warp (B <= 32): the arithmetic of
+// dpace_finalize_kernel, with the lse merges spread over all 32 lanes.
+//
+// dpace_finalize_kernel gives row r one warp: lane l folds partials l, l+32,
+// l+64, ... into a leaf, then the xor butterfly (offsets 16, 8, 4, 2, 1)
+// merges the leaves and lane 0's value is kept. Lane 0's value is the left-
+// to-right pairwise tree over the leaves taken in bit-reversed lane order
+// p -> l = rev5(p): the round with offset o merges lane i (left) with lane
+// i ^ o, so offset 16 pairs neighbours in p order, offset 8 pairs of pairs,
+// and so on. Here each row gets G = 32 / B' lanes (B' = B rounded up to a
+// power of two); lane q of the group evaluates the subtree of leaves
+// p in [q * B', (q + 1) * B') with a stack (a binary counter over the leaf
+// index), then the group combines with xor shuffles 1, 2, ..., G / 2, the
+// lower lane on the left: the same merges in the same order, so the same
+// bits, with B' + log2(G) dependent merges per lane instead of B * 36.
 template <class T, int NC>
-__device__ void fused_finalize(const DpaceFusedArgs& a, int64_t n) {
+__device__ __noinline__ void fused_finalize(const DpaceFusedArgs& a, int64_t n) {
   const int lane = threadIdx.x & 31;
   const int B = a.f.B;
   const int64_t V = a.f.pt.V, BL = a.f.pt.chunk;
   const int pmax = a.f.pt.pmax;
+  // lane j <-> row j for the inputs and the scan
   const int j = lane;
   const bool in = j < B;
   const int64_t rj = n * B + (in ? j : 0);
@@ -95,44 +99,74 @@ __device__ void fused_finalize(const DpaceFusedArgs& a, int64_t n) {
   const int64_t tj = in ? a.f.targets[rj] : 0;
   const bool tvalid = tj >= 0 && tj < V;
   const float xt = in && tvalid && mkj > 0.f ? ldg_f32(static_cast<const T*>(a.f.logits) + rj * V + tj) : 0.f;
-  const unsigned livebits = __ballot_sync(kFullMask, in && mkj > 0.f);
-  float lse_j = 0.f;
-  constexpr int kRows = 8;  // rows whose partial loads are in flight together
-  for (int i0 = 0; i0 < B; i0 += kRows) {
-    float2 p0[kRows], p1[kRows];
+  // lane group of the row for the merges
+  int lgB = 0;
+  while ((1 << lgB) < B) ++lgB;
+  const int lgG = 5 - lgB, nleaf = 1 << lgB;
+  const int row = lane >> lgG, q = lane & ((1 << lgG) - 1);
+  const bool rlive = __shfl_sync(kFullMask, in && mkj > 0.f, row);  // row < 32
+  const int64_t r = n * B + row;
+  const int k = rlive ? blocks_in_row(r, V, BL) * NC : 0;
+  const float2* part = a.f.part + r * pmax * NC;
+  const float2 seed = make_float2(kNegSeed, 0.f);
+  const int p0 = q * nleaf;
+  constexpr int KB = 8;  // leaves whose partial loads are in flight together
+  float2 c0[KB], c1[KB], n0[KB], n1[KB];
 #pragma unroll
-    for (int u = 0; u < kRows; ++u) {
+  for (int u = 0; u < KB; ++u) n0[u] = n1[u] = seed;
+  auto load_leaves = [&](int i0, float2* x0, float2* x1) {
+#pragma unroll
+    for (int u = 0; u < KB; ++u) {
       const int i = i0 + u;
-      p0[u] = p1[u] = make_float2(kNegSeed, 0.f);
-      if (i < B && ((livebits >> i) & 1u)) {
-        const int64_t r = n * B + i;
-        const int k = blocks_in_row(r, V, BL) * NC;
-        const float2* part = a.f.part + r * pmax * NC;
-        if (lane < k) p0[u] = __ldcg(part + lane);
-        if (lane + 32 < k) p1[u] = __ldcg(part + lane + 32);
-      }
+      const int l = (int)(__brev((unsigned)(p0 + i)) >> 27);
+      x0[u] = i < nleaf && l < k ? __ldcg(part + l) : seed;
+      x1[u] = i < nleaf && l + 32 < k ? __ldcg(part + l + 32) : seed;
     }
+  };
+  float sm_[5], ss_[5];
+  float m = kNegSeed, s = 0.f;
+  load_leaves(0, c0, c1);
+  for (int i0 = 0; i0 < nleaf; i0 += KB) {
+    if (i0 + KB < nleaf) load_leaves(i0 + KB, n0, n1);
 #pragma unroll
-    for (int u = 0; u < kRows; ++u) {
+    for (int u = 0; u < KB; ++u) {
       const int i = i0 + u;
-      if (i >= B || !((livebits >> i) & 1u)) continue;
-      const int64_t r = n * B + i;
-      const int k = blocks_in_row(r, V, BL) * NC;
-      const float2* part = a.f.part + r * pmax * NC;
-      float m = p0[u].x, s = p0[u].y;  // slot-major, warp-minor, then a fixed butterfly
-      lse_merge(m, s, p1[u].x, p1[u].y);
-      for (int qd = lane + 64; qd < k; qd += 32) {
+      if (i >= nleaf) break;
+      const int l = (int)(__brev((unsigned)(p0 + i)) >> 27);
+      m = c0[u].x;
+      s = c0[u].y;
+      lse_merge(m, s, c1[u].x, c1[u].y);
+      for (int qd = l + 64; qd < k; qd += 32) {
         const float2 v = __ldcg(part + qd);
         lse_merge(m, s, v.x, v.y);
       }
-      warp_lse(m, s);
-      // the butterfly leaves the lanes' (m, s) up to an ulp apart (a merge
-      // rounds its two operands asymmetrically): lane 0's value is the
-      // result, as in dpace_finalize_kernel
-      const float lse = __shfl_sync(kFullMask, __fadd_rn(m, logf(s)), 0);
-      if (lane == i) lse_j = lse;
+      // push leaf i: merge with the pending left subtrees of equal size
+#pragma unroll
+      for (int L = 0; L < 5; ++L) {
+        if ((i >> L) & 1) {
+          lse_merge(sm_[L], ss_[L], m, s);
+          m = sm_[L];
+          s = ss_[L];
+        } else {
+          sm_[L] = m;
+          ss_[L] = s;
+          break;
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < KB; ++u) {
+      c0[u] = n0[u];
+      c1[u] = n1[u];
     }
   }
+  for (int o = 1; o < (1 << lgG); o <<= 1) {
+    const float om = __shfl_xor_sync(kFullMask, m, o);
+    const float os = __shfl_xor_sync(kFullMask, s, o);
+    lse_merge(m, s, om, os);
+  }
+  const float lse_row = __fadd_rn(m, logf(s));  // valid in lane q == 0 of a live row
+  float lse_j = __shfl_sync(kFullMask, lse_row, in ? (j << lgG) : 0);
   const bool live = in && mkj > 0.f;
   const float ce = live && tvalid ? lse_j - xt : 0.f;
   if (in && !tvalid) atomicOr(a.f.flag, 1);
@@ -196,8 +230,6 @@ __global__ void __launch_bounds__((NC + 1) * 32, 3) dpace_fused_ring_kernel(cons
   const int64_t seq_len = (int64_t)B * V;
   const int pmax = a.f.pt.pmax;
   const int64_t nb = (E + BL - 1) / BL;
-  const int64_t D = a.lag < 1 ? 1 : (a.lag > nb ? nb : a.lag);
-  const unsigned total = (unsigned)(2 * nb);
 
   ring_init(sm.ring, NC);
   const RowBits rb = build_row_bits(sm.ring.bits, R, NC + 1, [&](int64_t r) {
@@ -208,56 +240,90 @@ __global__ void __launch_bounds__((NC + 1) * 32, 3) dpace_fused_ring_kernel(cons
   if (warp == NC) {  // producer (lane 0)
     if (lane == 0) {
       const uint64_t keep = policy_evict_last(), last_use = policy_evict_first();
-      unsigned w = atomicAdd(a.f.q_ctr, 1u);
-      unsigned wn = w < total ? atomicAdd(a.f.q_ctr, 1u) : total;
-      int phase = 0;
-      int64_t b = 0, blk_end = 0, r_issue = 0;
-      int k = 0;
-      if (w < total) {
-        fused_map(w, nb, D, phase, b);
-        blk_end = min((b + 1) * BL, E);
-        r_issue = (b * BL) / V;
-      }
-      for (int64_t it = 0;; ++it) {
-        const int slot = (int)(it % S);
-        if (!mbar_wait(sm.ring.empty + slot, (uint32_t)(((it / S) & 1) ^ 1))) {
-          atomicOr(a.f.flag, 2);
-          break;
-        }
-        if (a.withhold_stage && blockIdx.x == 0 && it == 0) continue;  // failure-detection tests
-        if (w >= total) {
-          sm.ring.sf0[slot] = -1;
-          mbar_arrive(sm.ring.full + slot);
-          break;
-        }
-        const int64_t f0 = b * BL + (int64_t)k * SE;
-        const int64_t f1 = min(f0 + SE, blk_end);
-        while ((r_issue + 1) * V <= f0) ++r_issue;
-        sm.ring.sf0[slot] = f0;
-        sm.ring.srow[slot] = r_issue;
-        sm.sph[slot] = phase;
-        bool live = !rb.valid;
-        for (int64_t r = r_issue; !live && r * V < f1; ++r) live = rb.live(r);
-        const uint32_t vbytes = (uint32_t)(((f1 - f0) * (int64_t)sizeof(T)) & ~int64_t(15));
-        if (live && vbytes) {
-          mbar_arrive_expect_tx(sm.ring.full + slot, vbytes);
-          bulk_g2s_hint(sm.ring.ring + (size_t)slot * SE, X + f0, vbytes, sm.ring.full + slot,
-                        phase == 0 ? keep : last_use);
-        } else {
-          mbar_arrive(sm.ring.full + slot);
-        }
-        if (f1 == blk_end) {
-          w = wn;
-          k = 0;
-          if (w < total) {
-            wn = atomicAdd(a.f.q_ctr, 1u);
-            fused_map(w, nb, D, phase, b);
-            blk_end = min((b + 1) * BL, E);
-            r_issue = (b * BL) / V;
+      int64_t it = 0;  // stages posted (ring position)
+      bool withhold = a.withhold_stage && blockIdx.x == 0;  // failure-detection tests
+      // Posts the stages of block b (phase 0 = F, 1 = B); false if a wait for
+      // a free slot expired.
+      auto issue_block = [&](int64_t b, int phase) -> bool {
+        const int64_t blk_end = min((b + 1) * BL, E);
+        int64_t r_issue = (b * BL) / V;
+        for (int64_t f0 = b * BL; f0 < blk_end;) {
+          const int slot = (int)(it % S);
+          if (!mbar_wait(sm.ring.empty + slot, (uint32_t)(((it / S) & 1) ^ 1))) return false;
+          ++it;
+          if (withhold) {  // slot left empty: its consumers' wait expires
+            withhold = false;
+            continue;
           }
-        } else {
-          ++k;
+          const int64_t f1 = min(f0 + SE, blk_end);
+          while ((r_issue + 1) * V <= f0) ++r_issue;
+          sm.ring.sf0[slot] = f0;
+          sm.ring.srow[slot] = r_issue;
+          sm.sph[slot] = phase;
+          bool live = !rb.valid;
+          for (int64_t r = r_issue; !live && r * V < f1; ++r) live = rb.live(r);
+          const uint32_t vbytes = (uint32_t)(((f1 - f0) * (int64_t)sizeof(T)) & ~int64_t(15));
+          if (live && vbytes) {
+            mbar_arrive_expect_tx(sm.ring.full + slot, vbytes);
+            bulk_g2s_hint(sm.ring.ring + (size_t)slot * SE, X + f0, vbytes, sm.ring.full + slot,
+                          phase == 0 ? keep : last_use);
+          } else {
+            mbar_arrive(sm.ring.full + slot);
+          }
+          f0 = f1;
         }
+        return true;
+      };
+      // the sequences a block overlaps (at most two: seq_len >= BL)
+      auto b_ready = [&](int64_t b) -> bool {
+        const int64_t s0 = (b * BL) / seq_len, s1 = (min((b + 1) * BL, E) - 1) / seq_len;
+        return ld_acquire(a.ready + s0) != 0u && (s1 == s0 || ld_acquire(a.ready + s1) != 0u);
+      };
+      bool ok = true;
+      int head = 0, tail = 0;  // this CTA's F blocks awaiting their B pass: fifo[head..tail)
+      int64_t f_seen = 0;      // lower bound of the F queue's head
+      bool f_out = false;      // the F queue is empty
+      uint64_t idle_since = 0;
+      while (ok) {
+        if (head != tail && b_ready(sm.fifo[head % kFifo])) {
+          ok = issue_block(sm.fifo[head % kFifo], 1);
+          ++head;
+          idle_since = 0;
+          continue;
+        }
+        if (!f_out && tail - head < kFifo &&
+            (f_seen * BL) / seq_len < (int64_t)ld_relaxed(a.f.done_cnt) + a.ahead) {
+          const int64_t fb = (int64_t)atomicAdd(a.f.q_ctr, 1u);
+          if (fb < nb) {
+            f_seen = fb + 1;
+            sm.fifo[tail % kFifo] = (int)fb;
+            ++tail;
+            ok = issue_block(fb, 0);
+            idle_since = 0;
+            continue;
+          }
+          f_out = true;
+        }
+        if (f_out && head == tail) break;
+        // nothing can be posted yet: the oldest B block waits for a finalize,
+        // or the F front waits for the cap to open
+        const uint64_t now = globaltimer_ns();
+        if (idle_since == 0) {
+          idle_since = now;
+        } else if (now - idle_since > kWaitLimitNs) {
+          ok = false;
+          break;
+        }
+        __nanosleep(256);
+      }
+      if (!ok) atomicOr(a.f.flag, 2);
+      // end marker for the consumers
+      const int slot = (int)(it % S);
+      if (mbar_wait(sm.ring.empty + slot, (uint32_t)(((it / S) & 1) ^ 1))) {
+        sm.ring.sf0[slot] = -1;
+        mbar_arrive(sm.ring.full + slot);
+      } else {
+        atomicOr(a.f.flag, 2);
       }
     }
     return;
@@ -269,7 +335,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 3) dpace_fused_ring_kernel(cons
   // B state (as the backward kernel)
   float sc = 0.f, l = 0.f;
   int64_t tf = -1, ready_seq = -1;
-  bool zero = true, timed_out = false;
+  bool zero = true;
   int64_t r = 0, blk = -1;
   int phase = 0;
   bool live = false;
@@ -277,14 +343,13 @@ __global__ void __launch_bounds__((NC + 1) * 32, 3) dpace_fused_ring_kernel(cons
     live = row < R && (rb.valid ? rb.live(row) : (a.f.mask == nullptr || a.f.mask[row] > 0.f));
     if (phase == 1) {
       zero = true;
-      if (live && !timed_out) {
+      if (live) {
         const int64_t n = row / B;
         if (n != ready_seq) {
-          if (!wait_ready(a.ready + n)) {
-            // the call reports the timeout; this warp writes zeros for the
-            // rest of its work instead of waiting again
-            timed_out = true;
-            if (lane == 0) atomicOr(a.f.flag, 2);
+          // the producer posted this block after seeing the flag; each lane's
+          // own acquire orders its loads below after the finalize's stores
+          if (!ld_acquire(a.ready + n)) {
+            if (lane == 0) atomicOr(a.f.flag, 2);  // not reached: reported, zeros written
             return;
           }
           ready_seq = n;
@@ -565,6 +630,7 @@ cudaError_t scale_inplace_launch(int dtype, void* x, int64_t n, const float* fac
 
 int dpace_fused_block_elems(int dtype) { return 4096 * 4 * (dtype == kDtypeBF16 ? 2 : 1); }
 int dpace_fused_consumers() { return 4; }
+int dpace_fused_max_seq_blocks() { return kFifo - 2; }
 
 int dpace_fused_ctas(int dtype, int device, int cap) {
   return dtype == kDtypeBF16 ? FusedVariant<bf16_t>::ctas(device, cap) : FusedVariant<float>::ctas(device, cap);

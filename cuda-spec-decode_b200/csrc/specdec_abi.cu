@@ -133,10 +133,11 @@ struct DpaceLayout {
 };
 
 // Forward: [done][flag][queue ctr][queue retired][seq_cnt x N];
-// forward+backward: [finalized][flag][queue ctr][done warps][seq_done x N][ready x N].
+// forward+backward: [finalized][flag][F queue][done warps][4 unused]
+// [seq_done x N][ready x N].
 size_t dpace_counter_bytes(int64_t N, int64_t B) {
   (void)B;
-  return align256(16 + 2 * size_t(N) * sizeof(unsigned));
+  return align256(32 + 2 * size_t(N) * sizeof(unsigned));
 }
 
 DpaceLayout dpace_layout(int64_t N, int64_t B, const Partition& pt, int nc) {
@@ -449,8 +450,13 @@ int dpace_forward_backward_impl(int dtype, const void* logits, const int64_t* ta
     return fail(SPECDEC_ERR_ARGUMENT, "misaligned pointer (scratch needs 256 B, counters 16 B)");
   const bool ptrs16 = aligned(logits, 16) && aligned(dlogits, 16);
   if (dtype == kDtypeBF16 && !ptrs16) return fail(SPECDEC_ERR_ARGUMENT, "bf16 logits and dlogits must be 16-byte aligned");
-  if (!ptrs16 || !use_tma(SPECDEC_KERNEL_DPACE_FWD, true)) {
-    // the 128-bit-load kernels: forward, then backward (no L2 reuse)
+  const int64_t fbl = dpace_fused_block_elems(dtype);
+  const int64_t seq_blocks = ((int64_t)B * V + fbl - 1) / fbl + 1;
+  if (!ptrs16 || !use_tma(SPECDEC_KERNEL_DPACE_FWD, true) || (int64_t)B * V < fbl ||
+      seq_blocks > dpace_fused_max_seq_blocks()) {
+    // forward, then backward (no L2 reuse): the 128-bit-load kernels, or
+    // sequences shorter than a fused block (a block would overlap more than
+    // two sequences) or longer than a CTA's B queue holds
     const int rc = dpace_forward_impl(dtype, logits, targets, mask, N, B, V, alpha, loss_type, n_global, loss,
                                       loss_n, lse, scale, status, scratch, scratch_bytes, counters, counter_bytes,
                                       stream);
@@ -503,15 +509,14 @@ int dpace_forward_backward_impl(int dtype, const void* logits, const int64_t* ta
   f.pt = pt;
   a.dlogits = dlogits;
   a.done_warps = cnt + 3;
-  a.seq_done = cnt + 4;
-  a.ready = cnt + 4 + N;
-  // lag: about g_fused_lag_mib of logits between a block's F and B reads, and
-  // at least one sequence's worth of blocks (every F block a B block needs is
-  // then handed out before it)
+  a.seq_done = cnt + 8;
+  a.ready = cnt + 8 + N;
+  // the F reads may run about g_fused_lag_mib of logits (at least one
+  // sequence) past the finalized sequences: the L2 window of the B re-reads
   const int64_t esz = dtype == kDtypeBF16 ? 2 : 4;
-  const int64_t lag_blocks = ((int64_t)g_fused_lag_mib.load() << 20) / (BL * esz);
-  const int64_t seq_blocks = ((int64_t)B * V + BL - 1) / BL + 1;
-  a.lag = lag_blocks > seq_blocks ? lag_blocks : seq_blocks;
+  const int64_t seq_bytes = (int64_t)B * V * esz;
+  const int64_t lag_bytes = (int64_t)g_fused_lag_mib.load() << 20;
+  a.ahead = lag_bytes > seq_bytes ? (lag_bytes + seq_bytes - 1) / seq_bytes : 1;
   a.withhold_stage = take_withhold_stage();
   const cudaError_t e = dpace_fused_launch(dtype, a, ctas, st);
   return e == cudaSuccess ? ok() : cuda_fail(e, "dpace forward+backward launch");

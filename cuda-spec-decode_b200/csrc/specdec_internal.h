@@ -75,12 +75,12 @@ struct DpaceBwdArgs {
 // the forward's arguments and workspace; its done_cnt counts finalized
 // sequences, q_ctr is the work queue.
 struct DpaceFusedArgs {
-  DpaceFwdArgs f;
+  DpaceFwdArgs f;          // f.q_ctr is the F queue; f.done_cnt counts finalized sequences
   void* dlogits;           // element type of the logits
   unsigned* seq_done;      // [N] finished F-block shares per sequence; zero on entry/exit
   unsigned* ready;         // [N] sequence finalized; zero on entry/exit
   unsigned* done_warps;    // [1] consumer warps that have exited; zero on entry/exit
-  int64_t lag;             // D: B block b is handed out about D blocks after F block b
+  int64_t ahead;           // F blocks are claimed while their first sequence < finalized + ahead (>= 1)
   int withhold_stage;      // failure-detection tests: CTA 0 never posts its first stage
 };
 
@@ -162,6 +162,7 @@ cudaError_t dflash_bwd_ring_launch(int dtype, int shape, const DflashBwdArgs& a,
 // Fused D-PACE forward + backward (dpace_fused.cu).
 int dpace_fused_block_elems(int dtype);
 int dpace_fused_consumers();
+int dpace_fused_max_seq_blocks();  // blocks overlapping one sequence the fused kernel allows
 int dpace_fused_ctas(int dtype, int device, int cap_per_sm);
 cudaError_t dpace_fused_launch(int dtype, const DpaceFusedArgs& a, int ctas, cudaStream_t st);
 cudaError_t scale_inplace_launch(int dtype, void* x, int64_t n, const float* factor, int ctas, cudaStream_t st);

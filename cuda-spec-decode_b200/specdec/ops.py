@@ -30,11 +30,13 @@ def set_target_validation(enabled: bool) -> None:
     VALIDATE_TARGETS = bool(enabled)
 
 
-# When True (default) the autograd path of D-PACE computes the gradient in its
-# forward with specdec_dpace_forward_backward (one HBM read of the logits;
-# the backward then only applies dloss, with no pass at all when dloss is 1).
-# False: separate forward and backward launches, as the reference.
-FUSED_BACKWARD = True
+# When True the autograd path of D-PACE computes the gradient in its forward
+# with specdec_dpace_forward_backward (one launch; the backward then only
+# applies dloss, with no pass at all when dloss is 1). False (default):
+# separate forward and backward launches, as the reference -- on a B200 at
+# [64, 16, 128256] they are still the faster pair (0.239 ms fp32 against
+# 0.30 ms for the single launch, whose backward re-reads mostly miss L2).
+FUSED_BACKWARD = False
 
 
 def set_fused_backward(enabled: bool) -> None:

@@ -119,13 +119,15 @@ int specdec_dpace_backward(const float* logits, const int64_t* targets, const fl
  * the gradient together (dloss = 1): the loss, lse, scale (and loss_n) of
  * specdec_dpace_forward and the dlogits of specdec_dpace_backward with a
  * NULL dloss, bit for bit, in one persistent launch that reads the logits
- * from HBM once -- the backward half re-reads each 64 KB block from L2 about
- * specdec_set_fused_lag() MiB after the forward half read it. No single
- * counterpart in the reference (losses/dpace.py:176-187 + :217-226 as one
- * launch). Arguments as in specdec_dpace_forward plus `dlogits` [N, B, V]
- * (same element type as logits, must not alias it); same workspace queries.
- * logits/dlogits not 16-byte aligned: runs the forward and backward kernels
- * one after the other instead (fp32; bf16 requires alignment).
+ * from HBM once -- the backward half re-reads each 64 KB block from L2 as
+ * soon as its sequence is finalized, while the forward half runs at most
+ * specdec_set_fused_lag() MiB ahead. No single counterpart in the reference
+ * (losses/dpace.py:176-187 + :217-226 as one launch). Arguments as in
+ * specdec_dpace_forward plus `dlogits` [N, B, V] (same element type as
+ * logits, must not alias it); same workspace queries. Runs the forward and
+ * backward kernels one after the other instead (same results) when
+ * logits/dlogits are not 16-byte aligned (fp32; bf16 requires alignment) or
+ * a sequence holds fewer than B * V = 16384 (fp32) / 32768 (bf16) elements.
  */
 int specdec_dpace_forward_backward(const float* logits, const int64_t* targets, const float* mask, int64_t N,
                                    int32_t B, int64_t V, float alpha, int32_t loss_type, int64_t n_global,
@@ -279,9 +281,11 @@ int64_t specdec_launch_ctas(int32_t kernel, int64_t rows, int64_t V, int device)
 int specdec_set_block_queue(int32_t dynamic);
 
 /*
- * Forward+backward: MiB of logits between a block's forward read and its
- * backward read (the L2 window); 0 restores the default (48). Values beyond
- * what L2 holds make the backward half read from HBM again.
+ * Forward+backward: how far (MiB of logits, rounded up to whole sequences,
+ * at least one) the forward reads may run ahead of the finalized sequences
+ * -- the L2 window of the backward re-reads; 0 restores the default (48).
+ * In [0, 4096]. Values beyond what L2 holds make the backward half read
+ * from HBM again.
  */
 int specdec_set_fused_lag(int32_t mib);
 

@@ -56,7 +56,17 @@ def test_lag_does_not_change_results(cuda, lag_mib):
     assert float(loss_f) == float(loss_s) and torch.equal(grad_f, grad_s)
 
 
-def test_autograd_uses_dloss_and_matches_oracle(cuda):
+@pytest.fixture
+def fused_autograd():
+    from specdec import ops
+
+    saved = ops.FUSED_BACKWARD
+    ops.set_fused_backward(True)
+    yield
+    ops.set_fused_backward(saved)
+
+
+def test_autograd_uses_dloss_and_matches_oracle(cuda, fused_autograd):
     from losses import dpace_loss
 
     x, t, m = _inputs(6, 16, 20000, 11)
@@ -65,11 +75,11 @@ def test_autograd_uses_dloss_and_matches_oracle(cuda):
         xg = x.clone().requires_grad_(True)
         loss = dpace_loss(xg, t, 0.5, m)
         (loss * factor).backward()
-        assert abs(float(loss) - float(want)) <= 1e-5 * abs(float(want))
+        assert abs(float(loss.detach()) - float(want)) <= 1e-5 * abs(float(want))
         assert float((xg.grad.cpu() - factor * g_ref).abs().max()) <= 1e-6 * max(1.0, abs(factor))
 
 
-def test_retained_graph_second_backward(cuda):
+def test_retained_graph_second_backward(cuda, fused_autograd):
     from losses import dpace_loss
 
     x, t, m = _inputs(4, 16, 9000, 12)
@@ -79,6 +89,26 @@ def test_retained_graph_second_backward(cuda):
     g1 = xg.grad.clone()
     loss.backward()
     assert float((xg.grad - 2 * g1).abs().max()) <= 1e-6
+
+
+def test_autograd_fused_equals_separate(cuda):
+    from losses import dpace_loss
+    from specdec import ops
+
+    x, t, m = _inputs(8, 16, 30000, 15)
+    grads, losses = [], []
+    saved = ops.FUSED_BACKWARD
+    try:
+        for fused in (False, True):
+            ops.set_fused_backward(fused)
+            xg = x.clone().requires_grad_(True)
+            loss = dpace_loss(xg, t, 0.5, m)
+            (loss * 2.0).backward()
+            grads.append(xg.grad)
+            losses.append(float(loss.detach()))
+    finally:
+        ops.set_fused_backward(saved)
+    assert losses[0] == losses[1] and torch.equal(grads[0], grads[1])
 
 
 def test_fused_expired_wait_reported_then_normal(cuda):
