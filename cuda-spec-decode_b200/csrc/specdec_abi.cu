@@ -45,7 +45,8 @@ std::atomic<int> g_shape[4] = {0, 0, 0, 0};
 std::atomic<int> g_cap[4] = {0, 0, 0, 0};
 std::atomic<int> g_static_queue{0};  // 1: ring kernels use a static block interleave
 std::atomic<int> g_withhold_stage{0};  // failure-detection tests: launches left to withhold a stage
-std::atomic<int> g_fused_lag_mib{48};   // forward+backward: L2 window between a block's two reads
+std::atomic<int> g_pipe_slots{0};       // forward+backward: cap on sequences per CTA (0: as many as fit)
+std::atomic<int> g_pipe_lag{0};         // forward+backward: sequences between F and B (0: default)
 
 int current_device() {
   int d = 0;
@@ -133,8 +134,8 @@ struct DpaceLayout {
 };
 
 // Forward: [done][flag][queue ctr][queue retired][seq_cnt x N];
-// forward+backward: [finalized][flag][F queue][done warps][4 unused]
-// [seq_done x N][ready x N].
+// forward+backward: [finalized][flag][exited CTAs][5 unused][seq_done x N]
+// [ready x N].
 size_t dpace_counter_bytes(int64_t N, int64_t B) {
   (void)B;
   return align256(32 + 2 * size_t(N) * sizeof(unsigned));
@@ -211,6 +212,24 @@ int take_withhold_stage() {
   return left > 0 ? 1 : 0;
 }
 
+// The forward+backward pipeline's plan for this shape on `device`, with the
+// specdec_set_pipe_slots() cap applied; ok = false when the shape does not
+// fit it or a CTA with that shared memory cannot be resident.
+PipePlan pipe_plan(int dtype, int64_t B, int64_t V, int device) {
+  PipePlan p = dpace_pipe_plan(dtype, B, V, device);
+  if (!p.ok) return p;
+  const int cap = g_pipe_slots.load();
+  if (cap >= 3 && cap < p.K) {
+    p.smem = p.smem / (size_t)p.K * (size_t)cap;
+    p.K = cap;
+    p.L = p.K / 2 > 2 ? p.K / 2 : 2;
+  }
+  const int lag = g_pipe_lag.load();
+  if (lag > 0) p.L = lag < p.K ? lag : p.K - 1;
+  if (dpace_pipe_resident(dtype, p.smem) < 1) p.ok = false;
+  return p;
+}
+
 }  // namespace
 
 namespace specdec {
@@ -251,9 +270,21 @@ int specdec_set_block_queue(int32_t dynamic) {
   return ok();
 }
 
-int specdec_set_fused_lag(int32_t mib) {
-  if (mib < 0 || mib > 4096) return fail(SPECDEC_ERR_ARGUMENT, "lag must be in [0, 4096] MiB");
-  g_fused_lag_mib.store(mib == 0 ? 48 : mib);
+int specdec_dpace_pipeline_slots(int32_t B, int64_t V, int32_t bf16, int device) {
+  const PipePlan p = pipe_plan(bf16 ? kDtypeBF16 : kDtypeF32, B, V, device);
+  return p.ok ? p.K : 0;
+}
+
+int specdec_set_pipe_lag(int32_t lag) {
+  if (lag < 0 || lag >= kPipeMaxSlots) return fail(SPECDEC_ERR_ARGUMENT, "lag must be in [0, %d]", kPipeMaxSlots - 1);
+  g_pipe_lag.store(lag);
+  return ok();
+}
+
+int specdec_set_pipe_slots(int32_t slots) {
+  if (slots != 0 && (slots < 3 || slots > kPipeMaxSlots))
+    return fail(SPECDEC_ERR_ARGUMENT, "slots must be 0 or in [3, %d]", kPipeMaxSlots);
+  g_pipe_slots.store(slots);
   return ok();
 }
 
@@ -287,9 +318,13 @@ size_t specdec_dpace_scratch_bytes(int64_t N, int32_t B, int64_t V, int device) 
       best = b > best ? b : best;
     }
     // forward+backward kernel
-    const size_t c = dpace_layout(N, B, ring_partition(N * B, V, dpace_fused_block_elems(dtype), 1),
-                                  dpace_fused_consumers()).scratch;
-    best = c > best ? c : best;
+    const PipePlan plan = pipe_plan(dtype, B, V, device);
+    if (plan.ok) {
+      Partition pt;
+      pt.pmax = plan.PM;
+      const size_t c = dpace_layout(N, B, pt, 1).scratch;
+      best = c > best ? c : best;
+    }
   }
   return best;
 }
@@ -450,34 +485,30 @@ int dpace_forward_backward_impl(int dtype, const void* logits, const int64_t* ta
     return fail(SPECDEC_ERR_ARGUMENT, "misaligned pointer (scratch needs 256 B, counters 16 B)");
   const bool ptrs16 = aligned(logits, 16) && aligned(dlogits, 16);
   if (dtype == kDtypeBF16 && !ptrs16) return fail(SPECDEC_ERR_ARGUMENT, "bf16 logits and dlogits must be 16-byte aligned");
-  const int64_t fbl = dpace_fused_block_elems(dtype);
-  const int64_t seq_blocks = ((int64_t)B * V + fbl - 1) / fbl + 1;
-  if (!ptrs16 || !use_tma(SPECDEC_KERNEL_DPACE_FWD, true) || (int64_t)B * V < fbl ||
-      seq_blocks > dpace_fused_max_seq_blocks()) {
-    // forward, then backward (no L2 reuse): the 128-bit-load kernels, or
-    // sequences shorter than a fused block (a block would overlap more than
-    // two sequences) or longer than a CTA's B queue holds
+  const int dev = current_device();
+  if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
+  const PipePlan plan = pipe_plan(dtype, B, V, dev);
+  if (!ptrs16 || !use_tma(SPECDEC_KERNEL_DPACE_FWD, true) || !plan.ok) {
+    // forward, then backward: the 128-bit-load kernels, or shapes whose
+    // slices do not fit the pipeline (see dpace_pipe_plan)
     const int rc = dpace_forward_impl(dtype, logits, targets, mask, N, B, V, alpha, loss_type, n_global, loss,
                                       loss_n, lse, scale, status, scratch, scratch_bytes, counters, counter_bytes,
                                       stream);
     if (rc != SPECDEC_OK) return rc;
     return dpace_backward_impl(dtype, logits, targets, lse, scale, nullptr, dlogits, N, B, V, nullptr, 0, stream);
   }
-  const int dev = current_device();
-  if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
-  const int ctas = dpace_fused_ctas(dtype, dev, g_cap[SPECDEC_KERNEL_DPACE_FWD].load());
-  if (ctas <= 0) return fail(SPECDEC_ERR_CUDA, "occupancy query failed");
-  const int64_t BL = dpace_fused_block_elems(dtype);
-  const Partition pt = ring_partition(N * B, V, BL, ctas);
-  const int nc = dpace_fused_consumers();
-  const DpaceLayout L = dpace_layout(N, B, pt, nc);
+  Partition pt;
+  pt.V = V;
+  pt.E = N * B * V;
+  pt.pmax = plan.PM;
+  const DpaceLayout L = dpace_layout(N, B, pt, 1);
   if (scratch_bytes < L.scratch)
     return fail(SPECDEC_ERR_WORKSPACE, "scratch needs %zu bytes, got %zu", L.scratch, scratch_bytes);
   if (counter_bytes < L.counters)
     return fail(SPECDEC_ERR_WORKSPACE, "counters need %zu bytes, got %zu", L.counters, counter_bytes);
   char* ws = static_cast<char*>(scratch);
   unsigned* cnt = static_cast<unsigned*>(counters);
-  DpaceFusedArgs a;
+  DpacePipeArgs a;
   DpaceFwdArgs& f = a.f;
   f.logits = logits;
   f.targets = targets;
@@ -496,29 +527,26 @@ int dpace_forward_backward_impl(int dtype, const void* logits, const int64_t* ta
   f.scale = scale;
   f.status = status;
   f.part = reinterpret_cast<float2*>(ws + L.part);
-  f.xtgt = nullptr;
+  f.xtgt = reinterpret_cast<float*>(ws + L.xtgt);
   f.seq_loss = reinterpret_cast<float*>(ws + L.seq_loss);
   f.seq_cnt = nullptr;
   f.done_cnt = cnt;
   f.flag = reinterpret_cast<int*>(cnt + 1);
-  f.q_ctr = cnt + 2;
+  f.q_ctr = nullptr;
   f.q_retired = nullptr;
-  f.q_dynamic = 1;
-  f.nc = nc;
+  f.q_dynamic = 0;
+  f.nc = 1;
   f.withhold_stage = 0;
   f.pt = pt;
   a.dlogits = dlogits;
-  a.done_warps = cnt + 3;
+  a.exit_cnt = cnt + 2;
   a.seq_done = cnt + 8;
-  a.ready = cnt + 8 + N;
-  // the F reads may run about g_fused_lag_mib of logits (at least one
-  // sequence) past the finalized sequences: the L2 window of the B re-reads
-  const int64_t esz = dtype == kDtypeBF16 ? 2 : 4;
-  const int64_t seq_bytes = (int64_t)B * V * esz;
-  const int64_t lag_bytes = (int64_t)g_fused_lag_mib.load() << 20;
-  a.ahead = lag_bytes > seq_bytes ? (lag_bytes + seq_bytes - 1) / seq_bytes : 1;
+  a.SL = plan.SL;
+  a.K = plan.K;
+  a.L = plan.L;
+  a.PM = plan.PM;
   a.withhold_stage = take_withhold_stage();
-  const cudaError_t e = dpace_fused_launch(dtype, a, ctas, st);
+  const cudaError_t e = dpace_pipe_launch(dtype, a, plan.G, plan.smem, st);
   return e == cudaSuccess ? ok() : cuda_fail(e, "dpace forward+backward launch");
 }
 
