@@ -45,8 +45,6 @@ std::atomic<int> g_shape[4] = {0, 0, 0, 0};
 std::atomic<int> g_cap[4] = {0, 0, 0, 0};
 std::atomic<int> g_static_queue{0};  // 1: ring kernels use a static block interleave
 std::atomic<int> g_withhold_stage{0};  // failure-detection tests: launches left to withhold a stage
-std::atomic<int> g_pipe_slots{0};       // forward+backward: cap on sequences per CTA (0: as many as fit)
-std::atomic<int> g_pipe_lag{0};         // forward+backward: sequences between F and B (0: default)
 
 int current_device() {
   int d = 0;
@@ -133,12 +131,10 @@ struct DpaceLayout {
   size_t part = 0, xtgt = 0, seq_loss = 0, scratch = 0, counters = 0;
 };
 
-// Forward: [done][flag][queue ctr][queue retired][seq_cnt x N];
-// forward+backward: [finalized][flag][exited CTAs][5 unused][seq_done x N]
-// [ready x N].
+// [done][flag][queue ctr][queue retired][seq_cnt x N]
 size_t dpace_counter_bytes(int64_t N, int64_t B) {
   (void)B;
-  return align256(32 + 2 * size_t(N) * sizeof(unsigned));
+  return align256(16 + size_t(N) * sizeof(unsigned));
 }
 
 DpaceLayout dpace_layout(int64_t N, int64_t B, const Partition& pt, int nc) {
@@ -212,24 +208,6 @@ int take_withhold_stage() {
   return left > 0 ? 1 : 0;
 }
 
-// The forward+backward pipeline's plan for this shape on `device`, with the
-// specdec_set_pipe_slots() cap applied; ok = false when the shape does not
-// fit it or a CTA with that shared memory cannot be resident.
-PipePlan pipe_plan(int dtype, int64_t B, int64_t V, int device) {
-  PipePlan p = dpace_pipe_plan(dtype, B, V, device);
-  if (!p.ok) return p;
-  const int cap = g_pipe_slots.load();
-  if (cap >= 3 && cap < p.K) {
-    p.smem = p.smem / (size_t)p.K * (size_t)cap;
-    p.K = cap;
-    p.L = p.K / 2 > 2 ? p.K / 2 : 2;
-  }
-  const int lag = g_pipe_lag.load();
-  if (lag > 0) p.L = lag < p.K ? lag : p.K - 1;
-  if (dpace_pipe_resident(dtype, p.smem) < 1) p.ok = false;
-  return p;
-}
-
 }  // namespace
 
 namespace specdec {
@@ -270,23 +248,6 @@ int specdec_set_block_queue(int32_t dynamic) {
   return ok();
 }
 
-int specdec_dpace_pipeline_slots(int32_t B, int64_t V, int32_t bf16, int device) {
-  const PipePlan p = pipe_plan(bf16 ? kDtypeBF16 : kDtypeF32, B, V, device);
-  return p.ok ? p.K : 0;
-}
-
-int specdec_set_pipe_lag(int32_t lag) {
-  if (lag < 0 || lag >= kPipeMaxSlots) return fail(SPECDEC_ERR_ARGUMENT, "lag must be in [0, %d]", kPipeMaxSlots - 1);
-  g_pipe_lag.store(lag);
-  return ok();
-}
-
-int specdec_set_pipe_slots(int32_t slots) {
-  if (slots != 0 && (slots < 3 || slots > kPipeMaxSlots))
-    return fail(SPECDEC_ERR_ARGUMENT, "slots must be 0 or in [3, %d]", kPipeMaxSlots);
-  g_pipe_slots.store(slots);
-  return ok();
-}
 
 int specdec_test_withhold_stage(int32_t launches) {
   if (launches < 0 || launches > 16) return fail(SPECDEC_ERR_ARGUMENT, "launches must be in [0, 16]");
@@ -316,14 +277,6 @@ size_t specdec_dpace_scratch_bytes(int64_t N, int32_t B, int64_t V, int device) 
       const int nc = dpace_ring_consumers(ring_shape(SPECDEC_KERNEL_DPACE_FWD, dtype));
       const size_t b = dpace_layout(N, B, dpace_fwd_partition(N, B, V, true, device, dtype), nc).scratch;
       best = b > best ? b : best;
-    }
-    // forward+backward kernel
-    const PipePlan plan = pipe_plan(dtype, B, V, device);
-    if (plan.ok) {
-      Partition pt;
-      pt.pmax = plan.PM;
-      const size_t c = dpace_layout(N, B, pt, 1).scratch;
-      best = c > best ? c : best;
     }
   }
   return best;
@@ -485,69 +438,10 @@ int dpace_forward_backward_impl(int dtype, const void* logits, const int64_t* ta
     return fail(SPECDEC_ERR_ARGUMENT, "misaligned pointer (scratch needs 256 B, counters 16 B)");
   const bool ptrs16 = aligned(logits, 16) && aligned(dlogits, 16);
   if (dtype == kDtypeBF16 && !ptrs16) return fail(SPECDEC_ERR_ARGUMENT, "bf16 logits and dlogits must be 16-byte aligned");
-  const int dev = current_device();
-  if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
-  const PipePlan plan = pipe_plan(dtype, B, V, dev);
-  if (!ptrs16 || !use_tma(SPECDEC_KERNEL_DPACE_FWD, true) || !plan.ok) {
-    // forward, then backward: the 128-bit-load kernels, or shapes whose
-    // slices do not fit the pipeline (see dpace_pipe_plan)
-    const int rc = dpace_forward_impl(dtype, logits, targets, mask, N, B, V, alpha, loss_type, n_global, loss,
-                                      loss_n, lse, scale, status, scratch, scratch_bytes, counters, counter_bytes,
-                                      stream);
-    if (rc != SPECDEC_OK) return rc;
-    return dpace_backward_impl(dtype, logits, targets, lse, scale, nullptr, dlogits, N, B, V, nullptr, 0, stream);
-  }
-  Partition pt;
-  pt.V = V;
-  pt.E = N * B * V;
-  pt.pmax = plan.PM;
-  const DpaceLayout L = dpace_layout(N, B, pt, 1);
-  if (scratch_bytes < L.scratch)
-    return fail(SPECDEC_ERR_WORKSPACE, "scratch needs %zu bytes, got %zu", L.scratch, scratch_bytes);
-  if (counter_bytes < L.counters)
-    return fail(SPECDEC_ERR_WORKSPACE, "counters need %zu bytes, got %zu", L.counters, counter_bytes);
-  char* ws = static_cast<char*>(scratch);
-  unsigned* cnt = static_cast<unsigned*>(counters);
-  DpacePipeArgs a;
-  DpaceFwdArgs& f = a.f;
-  f.logits = logits;
-  f.targets = targets;
-  f.mask = mask;
-  f.N = N;
-  f.B = B;
-  f.V = V;
-  f.alpha = alpha;
-  f.one_minus_alpha = (float)(1.0 - (double)alpha);
-  f.loss_type = loss_type;
-  f.n_global = n_global;
-  f.inv_n = (float)(1.0 / (double)n_global);
-  f.loss = loss;
-  f.loss_n = loss_n;
-  f.lse = lse;
-  f.scale = scale;
-  f.status = status;
-  f.part = reinterpret_cast<float2*>(ws + L.part);
-  f.xtgt = reinterpret_cast<float*>(ws + L.xtgt);
-  f.seq_loss = reinterpret_cast<float*>(ws + L.seq_loss);
-  f.seq_cnt = nullptr;
-  f.done_cnt = cnt;
-  f.flag = reinterpret_cast<int*>(cnt + 1);
-  f.q_ctr = nullptr;
-  f.q_retired = nullptr;
-  f.q_dynamic = 0;
-  f.nc = 1;
-  f.withhold_stage = 0;
-  f.pt = pt;
-  a.dlogits = dlogits;
-  a.exit_cnt = cnt + 2;
-  a.seq_done = cnt + 8;
-  a.SL = plan.SL;
-  a.K = plan.K;
-  a.L = plan.L;
-  a.PM = plan.PM;
-  a.withhold_stage = take_withhold_stage();
-  const cudaError_t e = dpace_pipe_launch(dtype, a, plan.G, plan.smem, st);
-  return e == cudaSuccess ? ok() : cuda_fail(e, "dpace forward+backward launch");
+  const int rc = dpace_forward_impl(dtype, logits, targets, mask, N, B, V, alpha, loss_type, n_global, loss, loss_n,
+                                    lse, scale, status, scratch, scratch_bytes, counters, counter_bytes, stream);
+  if (rc != SPECDEC_OK) return rc;
+  return dpace_backward_impl(dtype, logits, targets, lse, scale, nullptr, dlogits, N, B, V, nullptr, 0, stream);
 }
 
 }  // namespace

@@ -71,34 +71,6 @@ struct DpaceBwdArgs {
   Partition pt;
 };
 
-// D-PACE forward+backward pipeline (dpace_pipe.cu): one CTA per SM, each
-// holding its slice of K sequences in shared memory.
-constexpr int kPipeMaxSlots = 8;              // sequences a CTA holds
-constexpr int kPipeMaxRows = 4;               // rows a slice may overlap
-constexpr int64_t kPipeSmemBudget = 224 * 1024;  // dynamic shared memory for the slots
-
-struct DpacePipeArgs {
-  DpaceFwdArgs f;          // f.part: [N*B, PM] partial per (row, CTA); f.done_cnt counts finalized sequences
-  void* dlogits;           // element type of the logits
-  unsigned* seq_done;      // [N] CTAs done with a sequence's forward; zero on entry/exit
-  unsigned* exit_cnt;      // [1] CTAs that have exited; zero on entry/exit
-  int64_t SL;              // slice length (elements) of a sequence per CTA
-  int K;                   // slots (sequences held per CTA)
-  int L;                   // the backward runs L (1 <= L < K) sequences behind the forward
-  int PM;                  // partial slots per row
-  int withhold_stage;      // failure-detection tests: CTA 0's first copy comes after the wait limit
-};
-
-struct PipePlan {
-  bool ok = false;
-  int G = 0;       // CTAs (one per SM)
-  int64_t SL = 0;
-  int K = 0;
-  int L = 0;
-  int PM = 0;
-  size_t smem = 0;  // dynamic shared memory per CTA
-};
-
 struct DflashFwdArgs {
   const void* logits;          // draft [N, B, V] (float, or bf16 for the bf16 ring kernels)
   const void* target_logits;   // verifier [N, B, V], same element type
@@ -174,11 +146,7 @@ int dflash_bwd_ring_ctas(int dtype, int kind, int shape, int device, int cap_per
 cudaError_t dflash_fwd_ring_launch(int dtype, int shape, const DflashFwdArgs& a, int ctas, cudaStream_t st);
 cudaError_t dflash_bwd_ring_launch(int dtype, int shape, const DflashBwdArgs& a, int ctas, cudaStream_t st);
 
-// D-PACE forward + backward in one launch, and the in-place dloss scaling
-// (dpace_pipe.cu).
-PipePlan dpace_pipe_plan(int dtype, int64_t B, int64_t V, int device);  // ok = false: shape not supported
-int dpace_pipe_resident(int dtype, size_t smem);                        // CTAs per SM at that shared memory
-cudaError_t dpace_pipe_launch(int dtype, const DpacePipeArgs& a, int G, size_t smem, cudaStream_t st);
+// In-place dloss scaling of a gradient (dpace_scale.cu).
 cudaError_t scale_inplace_launch(int dtype, void* x, int64_t n, const float* factor, int ctas, cudaStream_t st);
 
 // Sets the calling thread's specdec_last_error() text.

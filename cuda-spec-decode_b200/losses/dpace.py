@@ -88,12 +88,13 @@ class DPACELoss(torch.autograd.Function):
     """Autograd glue (reference: losses/dpace.py:201-226). The weights are
     detached, so the gradient is one fused expression: (w_j/N)(softmax - onehot).
 
-    When the logits need a gradient, the forward computes it together with the
-    loss in one launch that reads the logits from HBM once
+    Default (as the reference): the backward kernel runs in the autograd
+    backward with the real dloss. With specdec.ops.set_fused_backward(True)
+    the forward computes the gradient for dloss = 1 in the same call
     (specdec_dpace_forward_backward) and keeps it; the backward then only
     multiplies by dloss on the device, which is no pass at all when dloss is 1
     (loss.backward()). A second backward through the same graph
-    (retain_graph) recomputes the gradient with the separate kernel."""
+    (retain_graph) recomputes the gradient with the backward kernel."""
 
     @staticmethod
     def forward(ctx, logits, targets, alpha, position_mask, loss_type, n_global=None):

@@ -64,9 +64,6 @@ _SIGNATURES = {
     "specdec_launch_ctas": (_c_i64, [_c_i32, _c_i64, _c_i64, ctypes.c_int]),
     "specdec_set_block_queue": (ctypes.c_int, [_c_i32]),
     "specdec_test_withhold_stage": (ctypes.c_int, [_c_i32]),
-    "specdec_set_pipe_slots": (ctypes.c_int, [_c_i32]),
-    "specdec_set_pipe_lag": (ctypes.c_int, [_c_i32]),
-    "specdec_dpace_pipeline_slots": (ctypes.c_int, [_c_i32, _c_i64, _c_i32, ctypes.c_int]),
     "specdec_dpace_forward_backward": (ctypes.c_int, [
         _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_f32, _c_i32, _c_i64,
         _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_sz, _c_p, _c_sz, _c_p]),

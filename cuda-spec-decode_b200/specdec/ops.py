@@ -31,11 +31,10 @@ def set_target_validation(enabled: bool) -> None:
 
 
 # When True the autograd path of D-PACE computes the gradient in its forward
-# with specdec_dpace_forward_backward (one launch; the backward then only
-# applies dloss, with no pass at all when dloss is 1). False (default):
-# separate forward and backward launches, as the reference -- on a B200 at
-# [64, 16, 128256] they are still the faster pair (0.239 ms fp32 against
-# 0.30 ms for the single launch, whose backward re-reads mostly miss L2).
+# with specdec_dpace_forward_backward (the forward and backward kernels in one
+# call, dloss = 1; the backward then only applies dloss, with no pass at all
+# when dloss is 1). False (default): the backward kernel runs in the autograd
+# backward with the real dloss, as in the reference.
 FUSED_BACKWARD = False
 
 
@@ -99,8 +98,9 @@ def _dpace_forward_backward(logits: torch.Tensor, targets: torch.Tensor, mask: t
                             alpha: float, loss_type: int, n_global: int | None = None,
                             want_loss_n: bool = False, validate: bool | None = None,
                             out: torch.Tensor | None = None):
-    """Loss and gradient (dloss = 1) in one launch that reads the logits from
-    HBM once. Returns (loss 0-d, dlogits, lse [N,B], scale [N,B], loss_n or None)."""
+    """Loss and gradient (dloss = 1) in one call: the forward and backward
+    kernels back to back on the current stream. Returns (loss 0-d, dlogits,
+    lse [N,B], scale [N,B], loss_n or None)."""
     lib = _lib.load()
     N, B, V = logits.shape
     dev = logits.device

@@ -118,18 +118,10 @@ int specdec_dpace_backward(const float* logits, const int64_t* targets, const fl
  * D-PACE forward and backward in one call, for callers that want the loss and
  * the gradient together (dloss = 1): the loss, lse, scale (and loss_n) of
  * specdec_dpace_forward and the dlogits of specdec_dpace_backward with a
- * NULL dloss, in one cooperative launch that keeps each sequence's logits in
- * shared memory between the two passes (one CTA per SM, each holding its
- * slice of several sequences), so the logits are read from HBM once. No
- * single counterpart in the reference (losses/dpace.py:176-187 + :217-226
- * as one launch). Results agree with the separate calls to float rounding
- * (the partial sums merge in a different order). Arguments as in
- * specdec_dpace_forward plus `dlogits` [N, B, V] (same element type as
- * logits, must not alias it); same workspace queries. Runs the forward and
- * backward kernels one after the other instead when logits/dlogits are not
- * 16-byte aligned (fp32; bf16 requires alignment), V * sizeof(element) is not
- * a multiple of 16, or a sequence's slices do not fit (B * V larger than
- * about 3 * V * SMs, or too large for 3 slices of shared memory per SM).
+ * NULL dloss -- the same two kernels on `stream`, so the same bits. No single
+ * counterpart in the reference (losses/dpace.py:176-187 + :217-226 in one
+ * call). Arguments as in specdec_dpace_forward plus `dlogits` [N, B, V] (same
+ * element type as logits, must not alias it); same workspace queries.
  */
 int specdec_dpace_forward_backward(const float* logits, const int64_t* targets, const float* mask, int64_t N,
                                    int32_t B, int64_t V, float alpha, int32_t loss_type, int64_t n_global,
@@ -281,28 +273,6 @@ int64_t specdec_launch_ctas(int32_t kernel, int64_t rows, int64_t V, int device)
  * default) or a static interleave (dynamic = 0), process-wide.
  */
 int specdec_set_block_queue(int32_t dynamic);
-
-/*
- * Forward+backward: cap on the sequences each CTA holds in shared memory;
- * 0 (default): as many as fit, at most 8; otherwise 3..8. Results do not
- * depend on it.
- */
-int specdec_set_pipe_slots(int32_t slots);
-
-/*
- * Forward+backward: sequences between a sequence's forward and its backward
- * (the time the finalize has); the other slots prefetch. 0 (default):
- * max(2, slots / 2); otherwise 1..7, capped at slots - 1. Results do not
- * depend on it.
- */
-int specdec_set_pipe_lag(int32_t lag);
-
-/*
- * Sequences per CTA the single-launch forward+backward would hold for this
- * shape on `device` (bf16 != 0: bf16 logits), or 0 when it runs the forward
- * and backward kernels one after the other (pointer alignment aside).
- */
-int specdec_dpace_pipeline_slots(int32_t B, int64_t V, int32_t bf16, int device);
 
 /*
  * Failure-detection test hook (no counterpart in the reference). The next
