@@ -214,6 +214,16 @@ def run_reference(args):
 
 # ----------------------------------------------------------------------------- our arm
 
+def device_barrier_on(world, dev):
+    """A 1-element all_reduce on the current stream: every rank's next event
+    fires when it completes, so a rank whose host left the barrier late does
+    not land its delay inside the other ranks' timed windows."""
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(torch.zeros(1, device=dev))
+
+
 def time_pair(args, stream, world, max_over_ranks, barrier, fwd, bwd, steps):
     """Times `steps` steps of fwd(i) (+ the loss all_reduce when world > 1) +
     bwd(i, state) on alternating input sets after args.warmup untimed steps.
@@ -247,6 +257,7 @@ def time_pair(args, stream, world, max_over_ranks, barrier, fwd, bwd, steps):
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
+    device_barrier_on(world, stream.device)
     a.record(stream)
     for k in range(steps):
         step(k)
@@ -462,6 +473,7 @@ def time_drafter_step(args, dev, world, max_over_ranks, barrier):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
         torch.cuda.synchronize(dev)
+        device_barrier_on(world, dev)
         a.record(stream)
         for _ in range(args.drafter_steps):
             loss = step()
@@ -509,6 +521,9 @@ def run_ours(args):
     def barrier():
         if world > 1:
             dist.barrier()
+
+    def device_barrier():
+        device_barrier_on(world, dev)
 
     def max_over_ranks(v: float) -> float:
         if world == 1:
@@ -572,6 +587,7 @@ def run_ours(args):
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize(dev)
+    device_barrier()
     start.record(stream)
     for k in range(args.steps):
         step(k)
@@ -647,6 +663,7 @@ def run_ours(args):
             e2e_step(i)
         torch.cuda.synchronize(dev)
         barrier()
+        device_barrier()
         s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s0.record(stream)
         for i in range(args.e2e_steps):
