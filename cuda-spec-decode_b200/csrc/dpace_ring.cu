@@ -205,17 +205,25 @@ __global__ void __launch_bounds__(1024) dpace_finalize_kernel(const __grid_const
     const float sm = live ? __fadd_rn(__fmul_rn(a.one_minus_alpha, expf(-ce)), a.alpha) : 1.f;
     // prefix product and suffix sum in double, in sequence order (torch CPU
     // cumprod / cumsum accumulate in double); every lane runs the serial scan
+    // on factors gathered first, so the dependent chain is arithmetic only
+    float f[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) f[i] = __shfl_sync(kFullMask, sm, i);
     double run = 1.0;
     float P = 1.f;
-    for (int i = 0; i < B; ++i) {
-      run *= (double)__shfl_sync(kFullMask, sm, i);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if (i < B) run *= (double)f[i];
       if (i == j) P = (float)run;
     }
     const float pm = __fmul_rn(P, mk);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) f[i] = __shfl_sync(kFullMask, pm, i);
     double acc = 0.0;
     float S = 0.f;
-    for (int i = B - 1; i >= 0; --i) {
-      acc += (double)__shfl_sync(kFullMask, pm, i);
+#pragma unroll
+    for (int i = 31; i >= 0; --i) {
+      if (i < B) acc += (double)f[i];
       if (i == j) S = (float)acc;
     }
     float w = a.loss_type == 1 ? P : (a.loss_type == 2 ? __fdiv_rn(S, fmaxf(P, FLT_MIN)) : S);
