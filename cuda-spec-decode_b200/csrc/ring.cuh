@@ -80,11 +80,24 @@ __device__ __forceinline__ RowBits build_row_bits(unsigned* words, int64_t R, in
   rb.words = words;
   rb.valid = R <= (int64_t)kMaxRowWords * 32;
   if (rb.valid) {
+    // a warp takes kU consecutive words at a time and issues all their loads
+    // before the first ballot: one memory round trip per kU words (the whole
+    // table at the bench size) instead of one per word, ahead of the first copy
+    constexpr int kU = 8;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int64_t wd = warp; wd * 32 < R; wd += nwarps) {
-      const int64_t r = wd * 32 + lane;
-      const unsigned bits = __ballot_sync(0xffffffffu, r < R && live(r));
-      if (lane == 0) words[wd] = bits;
+    const int64_t nwords = (R + 31) / 32;
+    for (int64_t w0 = (int64_t)warp * kU; w0 < nwords; w0 += (int64_t)nwarps * kU) {
+      bool lv[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t r = (w0 + u) * 32 + lane;
+        lv[u] = r < R && live(r);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const unsigned bits = __ballot_sync(0xffffffffu, lv[u]);
+        if (lane == 0 && w0 + u < nwords) words[w0 + u] = bits;
+      }
     }
   }
   return rb;
