@@ -3,17 +3,26 @@
     python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...
 
-Default workload (per GPU): D-PACE forward + backward over fp32 logits
+Headline workload (per GPU): D-PACE forward + backward over fp32 logits
 [N=64, B=16, V=128256] ~ N(0, 2^2), uniform targets, per-sequence prefix mask
 k ~ U{0..4}, alpha 0.5, loss_type "dpace" -- the Llama-3-vocabulary
 configuration the metric is quoted on. With N GPUs every rank holds its own 64
 sequences of a 64*N-sequence batch (weak scaling): the loss divisor is the
 global N and the only collective is one 4-byte NCCL all_reduce of the loss
-per step. A step = forward (+ all_reduce) + backward through the C ABI with
+per step. A step = specdec_dpace_forward_backward through the C ABI (loss and
+gradient in one call; the backward is chained to the forward's finalize) with
 inputs resident in HBM; two input sets alternate, each larger than L2.
 
 Metric: fwd+bwd logits GB/s = 12 * N*B*V bytes (forward read, backward read,
-backward write) / step time, summed over GPUs; rows/s alongside.
+backward write) / step time, summed over GPUs; rows/s alongside. The bytes a
+step actually moves are fewer (unscored rows are never read):
+moved_bytes_per_step and pct_of_hbm_peak use those.
+
+Other legs in the same line: the large-batch workload [512, 32, 151936]
+~ N(0, 3^2), prefix mask k ~ U{0..8}, its 512 sequences split across the N
+GPUs (strong scaling, "c4"); the DFlash objective (KL) at [64, 16, 128256];
+bf16 logits; the end-to-end drafter training step; the same D-PACE metric
+end to end from pinned host memory through the public API ("e2e").
 
 --impl reference times the reference's CPU path (its torch oracle,
 losses/dpace_ref.py, restated in oracle/dpace.py) on the host cores with all
@@ -180,6 +189,38 @@ def time_cpu_baseline(B, V, budget_s=10.0, N_s=4):
             "rows_per_s": round(N_s * B / sec, 1), "ms_per_step": round(sec * 1e3, 2)}
 
 
+def time_cpu_baseline_dflash(B, V, budget_s=10.0, N_s=4):
+    """The reference's DFlash CPU path -- its speculators oracle (loss_function
+    + kl_div_loss, models/dflash/tests/test_loss.py:21-49, restated in
+    oracle/dflash.py) -- fwd+bwd on the host cores over a bounded sample of
+    the DFlash-KL workload; 20*E bytes per step like the GPU leg."""
+    from oracle.dflash import dflash_loss_torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    x, y = dflash_inputs(N_s, B, V, 0, torch.device("cpu"))
+    x.requires_grad_(True)
+
+    def step():
+        x.grad = None
+        loss = dflash_loss_torch(x, y, None, 4.0, False, "kl")
+        loss.backward()
+
+    step()
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    E = N_s * B * V
+    return {"value": round(20 * E / sec / 1e9, 4), "unit": UNIT, "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"DFlash-KL fwd+bwd via the reference's speculators oracle (oracle/dflash.py) on "
+                      f"[{N_s},{B},{V}] of the workload, median of {len(times)} runs",
+            "rows_per_s": round(N_s * B / sec, 1), "ms_per_step": round(sec * 1e3, 2)}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -224,65 +265,109 @@ def device_barrier_on(world, dev):
         dist.all_reduce(torch.zeros(1, device=dev))
 
 
-def time_pair(args, stream, world, max_over_ranks, barrier, fwd, bwd, steps):
-    """Times `steps` steps of fwd(i) (+ the loss all_reduce when world > 1) +
-    bwd(i, state) on alternating input sets after args.warmup untimed steps.
-    Returns (ms per step, mean forward ms, mean backward ms), max over ranks."""
+class Timing:
+    """Per-rank timing context: the compute stream, the world, the max-over-
+    ranks reduction, the host barrier and the loss reducer (NCCL all_reduce
+    of the 4-byte loss on a side stream, or on the compute stream for
+    --loss-reduce serial)."""
 
-    reducer = LossReducer(stream.device) if world > 1 and args.loss_reduce == "overlap" else None
+    def __init__(self, args, dev, world):
+        import torch.distributed as dist
 
-    def step(i, ev=None):
-        if ev is not None:
-            ev[0].record(stream)
-        loss, state = fwd(i)
-        if ev is not None:
-            ev[1].record(stream)
-        if reducer is not None:
-            reducer.start(loss)
-        elif world > 1:
-            import torch.distributed as dist
-            dist.all_reduce(loss)
-        if ev is not None:
-            ev[2].record(stream)
-        bwd(i, state)
-        if ev is not None:
-            ev[3].record(stream)
-        if reducer is not None:
-            reducer.wait()
+        self.args, self.dev, self.world = args, dev, world
+        self.stream = torch.cuda.current_stream(dev)
+        self.reducer = LossReducer(dev) if world > 1 and args.loss_reduce == "overlap" else None
+        self._dist = dist
 
-    for i in range(args.warmup):
-        step(i)
-    # the step time comes from an uninstrumented loop (events between kernels
-    # would break the programmatic-dependent-launch chaining of the kernels)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
-    device_barrier_on(world, stream.device)
-    a.record(stream)
-    for k in range(steps):
-        step(k)
-    b.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    ms = max_over_ranks(a.elapsed_time(b)) / steps
-    # per-kernel split from a second, instrumented pass
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
-    for k in range(steps):
-        step(k, evs[k])
-    torch.cuda.synchronize()
-    f = max_over_ranks(statistics.mean(e[0].elapsed_time(e[1]) for e in evs))
-    g = max_over_ranks(statistics.mean(e[2].elapsed_time(e[3]) for e in evs))
-    return ms, f, g
+    def max(self, v: float) -> float:
+        if self.world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=self.dev)
+        self._dist.all_reduce(t, op=self._dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def barrier(self):
+        if self.world > 1:
+            self._dist.barrier()
+
+    def reduce(self, loss):
+        """Starts the global loss reduction of a step (no-op on one GPU)."""
+        if self.world == 1:
+            return loss
+        if self.reducer is not None:
+            return self.reducer.start(loss)
+        self._dist.all_reduce(loss)
+        return loss
+
+    def settle(self):
+        """The compute stream waits for every loss reduction started so far."""
+        if self.reducer is not None:
+            self.reducer.wait()
+
+    def loop(self, step, steps):
+        """args.warmup untimed steps, then `steps` timed steps of step(i) in one
+        event pair on the compute stream, behind a host and a device barrier.
+        Returns (ms per step max over ranks, this rank's ms per step)."""
+        for i in range(self.args.warmup):
+            step(i)
+        self.settle()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        self.barrier()
+        torch.cuda.synchronize(self.dev)
+        device_barrier_on(self.world, self.dev)
+        a.record(self.stream)
+        for k in range(steps):
+            step(k)
+        self.settle()
+        b.record(self.stream)
+        torch.cuda.synchronize(self.dev)
+        self.barrier()
+        local = a.elapsed_time(b) / steps
+        return self.max(local), local
+
+    def split(self, fwd, bwd, steps):
+        """A second, instrumented pass: events around the forward call and the
+        backward call of each step (separate calls, so no chaining between
+        them). Returns (mean forward ms, mean backward ms), max over ranks."""
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+        for k in range(steps):
+            evs[k][0].record(self.stream)
+            loss, state = fwd(k)
+            evs[k][1].record(self.stream)
+            self.reduce(loss)
+            evs[k][2].record(self.stream)
+            bwd(k, state)
+            evs[k][3].record(self.stream)
+            self.settle()
+        torch.cuda.synchronize(self.dev)
+        f = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+        g = statistics.mean(e[2].elapsed_time(e[3]) for e in evs)
+        return self.max(f), self.max(g)
 
 
-def time_dflash(args, dev, stream, world, n_global, max_over_ranks, barrier, dtype=torch.float32, steps=None):
+def roofline(kernel, nbytes, ms, peak, traffic=None, **extra):
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    d = {"kernel": kernel, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+         "frac": round(achieved / peak, 4), "traffic": traffic, "bytes_per_launch": nbytes}
+    d.update(extra)
+    return d
+
+
+def dpace_moved_bytes(E, live, esz):
+    """Bytes a D-PACE step moves: forward reads the scored rows, backward
+    re-reads them and writes every gradient element."""
+    return esz * E * (2.0 * live + 1.0)
+
+
+def time_dflash(args, T, n_global, dtype=torch.float32, steps=None):
     """DFlash objective (KL), draft [64, 16, 128256] ~ N(0, 2^2), verifier =
     draft + N(0, 1), gamma 4, anchor slot unscored, every slot masked in.
     Bytes model 20 * N*B*V per step for fp32 (forward reads both, backward
-    reads both and writes the gradient), 10 * N*B*V for bf16; required bytes
+    reads both and writes the gradient), 10 * N*B*V for bf16; moved bytes
     skip the zero-weight anchor rows."""
     from specdec import ops
 
+    dev, world = T.dev, T.world
     N, B, V = args.n, 16, 128256
     E = N * B * V
     esz = 2 if dtype == torch.bfloat16 else 4
@@ -302,87 +387,151 @@ def time_dflash(args, dev, stream, world, n_global, max_over_ranks, barrier, dty
         x, y = sets[i & 1]
         ops.dflash_backward(x, y, st[0], st[1], st[2], None, None, 0, out=grad)
 
+    def step(i):
+        loss, st = fwd(i)
+        T.reduce(loss)
+        bwd(i, st)
+        T.settle()
+
     K = args.dflash_steps if steps is None else steps
-    ms, f, g = time_pair(args, stream, world, max_over_ranks, barrier, fwd, bwd, K)
+    ms, ms_local = T.loop(step, K)
+    f, g = T.split(fwd, bwd, K)
     live = 15.0 / 16.0
     peak, _ = hbm_peak()
     bwd_bytes = 2.0 * esz * E * live + esz * E
     fwd_bytes = 2.0 * esz * E * live
+    moved = fwd_bytes + bwd_bytes
     model = 5 * esz
     wl = f"{N}x{B}x{V}"
     tag = "_bf16" if esz == 2 else ""
     value = model * E * world / (ms * 1e-3) / 1e9
     del sets, grad
+    kname = "bf16" if esz == 2 else "f32"
     return {"metric": f"DFlash-KL fwd+bwd logits GB/s ({model}*N*B*V bytes per GPU-step)",
             "value": round(value, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
+            "ms_per_step_this_rank": round(ms_local, 4),
             "rows_per_s": round(N * B * world / (ms * 1e-3), 1),
-            "pct_of_hbm_peak": round(100.0 * value / world / peak, 2),
+            "moved_bytes_per_step": moved,
+            "pct_of_hbm_peak": round(100.0 * moved / (ms * 1e-3) / 1e9 / peak, 2),
+            "pct_basis": "moved bytes (anchor rows are not read) / ms_per_step / measured HBM peak",
             "fwd_ms": round(f, 4), "bwd_ms": round(g, 4), "steps": K,
             "dtype": "bf16" if esz == 2 else "f32",
             "config": {"workload": f"dflash_kl_fwd_bwd_llama3_vocab{tag}", "N_per_gpu": N, "B": B, "V": V,
                        "draft": "N(0, 2^2)", "verifier": "draft + N(0, 1)", "gamma": 4.0,
                        "sample_from_anchor": False, "mask": "all ones",
                        "logits": "bf16 (fp32 arithmetic)" if esz == 2 else "fp32"},
-            "roofline": {"kernel": f"dflash_bwd_ring_kernel<{'bf16' if esz == 2 else 'f32'}, KL>", "bound": "hbm",
-                         "achieved": round(bwd_bytes / (g * 1e-3) / 1e9, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(bwd_bytes / (g * 1e-3) / 1e9 / peak, 4),
-                         "traffic": profiled_traffic(f"dflash_bwd_kl{tag}", wl), "bytes_per_launch": bwd_bytes},
-            "fwd_roofline": {"kernel": f"dflash_fwd_ring_kernel<{'bf16' if esz == 2 else 'f32'}, KL> + finalize",
-                             "achieved": round(fwd_bytes / (f * 1e-3) / 1e9, 1),
-                             "frac": round(fwd_bytes / (f * 1e-3) / 1e9 / peak, 4),
-                             "traffic": profiled_traffic(f"dflash_fwd_kl{tag}", wl), "bytes_per_launch": fwd_bytes}}
+            "roofline": roofline(f"dflash_bwd_ring_kernel<{kname}, KL>", bwd_bytes, g, peak,
+                                 profiled_traffic(f"dflash_bwd_kl{tag}", wl)),
+            "fwd_roofline": roofline(f"dflash_fwd_ring_kernel<{kname}, KL> + finalize", fwd_bytes, f, peak,
+                                     profiled_traffic(f"dflash_fwd_kl{tag}", wl))}
 
 
-def time_dpace_bf16(args, dev, stream, world, n_global, max_over_ranks, barrier):
-    """D-PACE on bf16 logits, the headline workload otherwise: [64, 16, 128256]
-    ~ N(0, 2^2) rounded to bf16, prefix mask k ~ U{0..4}, alpha 0.5. Bytes model
-    6 * N*B*V per step (2-byte elements: forward read, backward read + write);
-    required bytes skip the unscored rows."""
+def dpace_leg(args, T, N, B, V, sigma, kmax, n_global, steps, dtype=torch.float32, sets_n=2, seed0=1000):
+    """Times a D-PACE workload: `steps` steps of specdec_dpace_forward_backward
+    (plus the loss reduction when world > 1), then the instrumented split pass
+    of separate forward / backward calls. Returns a dict of raw figures."""
     from specdec import ops
 
-    N, B, V = args.n, 16, 128256
-    E = N * B * V
+    dev = T.dev
+    rank = int(os.environ.get("RANK", "0"))
     sets = []
-    for s_ in range(2):
-        x, t, m = dpace_inputs(N, B, V, 2.0, 4, 1000 * s_ + int(os.environ.get("RANK", "0")), dev)
-        sets.append((x.to(torch.bfloat16), t, m))
+    for s_ in range(sets_n):
+        x, t, m = dpace_inputs(N, B, V, sigma, kmax, seed0 * s_ + rank, dev)
+        sets.append((x if dtype == torch.float32 else x.to(dtype), t, m))
         del x
     live = statistics.mean(float(m.mean()) for _, _, m in sets)
-    grad = torch.empty(N, B, V, device=dev, dtype=torch.bfloat16)
+    grad = torch.empty(N, B, V, device=dev, dtype=dtype)
+
+    def step(i):
+        x, t, m = sets[i % sets_n]
+        loss, _, _, _, _ = ops.dpace_forward_backward(x, t, m, 0.5, 0, n_global=n_global, validate=False,
+                                                      out=grad)
+        T.reduce(loss)
 
     def fwd(i):
-        x, t, m = sets[i & 1]
+        x, t, m = sets[i % sets_n]
         loss, lse, scale, _ = ops.dpace_forward(x, t, m, 0.5, 0, n_global=n_global, validate=False)
         return loss, (lse, scale)
 
     def bwd(i, st):
-        x, t, _ = sets[i & 1]
+        x, t, _ = sets[i % sets_n]
         ops.dpace_backward(x, t, st[0], st[1], None, out=grad)
 
-    K = args.bf16_steps
-    ms, f, g = time_pair(args, stream, world, max_over_ranks, barrier, fwd, bwd, K)
-    peak, _ = hbm_peak()
-    bwd_bytes = 2.0 * E * live + 2.0 * E
-    fwd_bytes = 2.0 * E * live
-    wl = f"{N}x{B}x{V}"
-    value = 6.0 * E * world / (ms * 1e-3) / 1e9
+    ms, ms_local = T.loop(step, steps)
+    f, g = T.split(fwd, bwd, steps)
+    aligned = all(x.data_ptr() % 16 == 0 for x, _, _ in sets)
+    out = {"ms": ms, "ms_local": ms_local, "fwd_ms": f, "bwd_ms": g, "live": live, "aligned": aligned}
     del sets, grad
-    return {"metric": "D-PACE fwd+bwd bf16 logits GB/s (6*N*B*V bytes per GPU-step)",
-            "value": round(value, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
-            "rows_per_s": round(N * B * world / (ms * 1e-3), 1),
-            "pct_of_hbm_peak": round(100.0 * value / world / peak, 2),
-            "fwd_ms": round(f, 4), "bwd_ms": round(g, 4), "steps": K, "dtype": "bf16",
-            "config": {"workload": "dpace_fwd_bwd_llama3_vocab_bf16", "N_per_gpu": N, "B": B, "V": V,
-                       "sigma": 2.0, "mask": "prefix k~U{0..4}", "alpha": 0.5, "loss_type": "dpace",
-                       "logits": "bf16 (fp32 arithmetic)"},
-            "roofline": {"kernel": "dpace_bwd_ring_kernel<bf16>", "bound": "hbm",
-                         "achieved": round(bwd_bytes / (g * 1e-3) / 1e9, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(bwd_bytes / (g * 1e-3) / 1e9 / peak, 4),
-                         "traffic": profiled_traffic("dpace_bwd_bf16", wl), "bytes_per_launch": bwd_bytes},
-            "fwd_roofline": {"kernel": "dpace_fwd_ring_kernel<bf16> + finalize",
-                             "achieved": round(fwd_bytes / (f * 1e-3) / 1e9, 1),
-                             "frac": round(fwd_bytes / (f * 1e-3) / 1e9 / peak, 4),
-                             "traffic": profiled_traffic("dpace_fwd_bf16", wl), "bytes_per_launch": fwd_bytes}}
+    torch.cuda.empty_cache()
+    return out
+
+
+def dpace_report(r, N, B, V, world, esz, n_total_rows, peak, scaling, wl_tag=""):
+    """Common fields of a D-PACE leg: model bytes 12E (or 6E for bf16) per
+    GPU-step summed over GPUs, moved bytes, fractions of the measured peak,
+    the backward kernel's roofline."""
+    E = N * B * V
+    ms = r["ms"]
+    model_bytes = 3 * esz * E  # per GPU-step: forward read + backward read + write
+    moved = dpace_moved_bytes(E, r["live"], esz)
+    bwd_bytes = esz * E * r["live"] + esz * E
+    fwd_bytes = esz * E * r["live"]
+    kname = "bf16" if esz == 2 else "f32"
+    wl = f"{N}x{B}x{V}"
+    return {"value": round(model_bytes * world / (ms * 1e-3) / 1e9, 2), "ms_per_step": round(ms, 4),
+            "ms_per_step_this_rank": round(r["ms_local"], 4),
+            "rows_per_s": round(n_total_rows / (ms * 1e-3), 1),
+            "moved_bytes_per_step": moved,
+            "pct_of_hbm_peak": round(100.0 * moved / (ms * 1e-3) / 1e9 / peak, 2),
+            "pct_basis": "moved bytes per GPU (unscored rows are not read) / ms_per_step / measured HBM peak",
+            "live_row_fraction": round(r["live"], 4),
+            "roofline": roofline(f"dpace_bwd_ring_kernel<{kname}>", bwd_bytes, r["bwd_ms"], peak,
+                                 profiled_traffic("dpace_bwd" + wl_tag, wl)),
+            "fwd_roofline": roofline(f"dpace_fwd_ring_kernel<{kname}> + dpace_finalize_kernel", fwd_bytes,
+                                     r["fwd_ms"], peak, profiled_traffic("dpace_fwd" + wl_tag, wl)),
+            "split_ms": {"fwd": round(r["fwd_ms"], 4), "bwd": round(r["bwd_ms"], 4),
+                         "note": "separate forward / backward calls with events between them"},
+            "scaling": scaling}
+
+
+def time_dpace_bf16(args, T, n_global):
+    """D-PACE on bf16 logits, the headline workload otherwise: [64, 16, 128256]
+    ~ N(0, 2^2) rounded to bf16, prefix mask k ~ U{0..4}, alpha 0.5. Bytes model
+    6 * N*B*V per step (2-byte elements: forward read, backward read + write)."""
+    N, B, V = args.n, 16, 128256
+    r = dpace_leg(args, T, N, B, V, 2.0, 4, n_global, args.bf16_steps, dtype=torch.bfloat16)
+    peak, _ = hbm_peak()
+    d = {"metric": "D-PACE fwd+bwd bf16 logits GB/s (6*N*B*V bytes per GPU-step)", "unit": "GB/s",
+         "steps": args.bf16_steps, "dtype": "bf16",
+         "config": {"workload": "dpace_fwd_bwd_llama3_vocab_bf16", "N_per_gpu": N, "B": B, "V": V,
+                    "sigma": 2.0, "mask": "prefix k~U{0..4}", "alpha": 0.5, "loss_type": "dpace",
+                    "logits": "bf16 (fp32 arithmetic)", "step": "specdec_dpace_forward_backward_bf16"}}
+    d.update(dpace_report(r, N, B, V, T.world, 2, N * B * T.world, peak, "weak", "_bf16"))
+    return d
+
+
+def time_c4(args, T):
+    """The large-batch workload: [512, 32, 151936] fp32 ~ N(0, 3^2), uniform
+    targets, per-sequence prefix mask k ~ U{0..8}, alpha 0.5, the 512
+    sequences split contiguously across the ranks (strong scaling: 512/N per
+    GPU, loss divisor 512, one 4-byte all_reduce per step). One input set:
+    every shard (>= 1.2 GB at N = 8) is larger than L2."""
+    from specdec.dist import shard_range
+
+    rank = int(os.environ.get("RANK", "0"))
+    NT, B, V = 512, 32, 151936
+    lo, hi = shard_range(NT, rank, T.world)
+    N = hi - lo
+    r = dpace_leg(args, T, N, B, V, 3.0, 8, NT, args.c4_steps, sets_n=1, seed0=4000)
+    peak, _ = hbm_peak()
+    d = {"metric": "D-PACE fwd+bwd logits GB/s, large batch (12*N*B*V bytes per GPU-step, summed)",
+         "unit": "GB/s", "steps": args.c4_steps, "dtype": "f32",
+         "config": {"workload": "dpace_large_batch_strong_scaling", "N_total": NT, "N_per_gpu": N, "B": B,
+                    "V": V, "sigma": 3.0, "mask": "prefix k~U{0..8}", "alpha": 0.5, "loss_type": "dpace",
+                    "shards": f"contiguous, {T.world} ranks", "l2": "one input set, > 126 MB L2 per rank",
+                    "step": "specdec_dpace_forward_backward"}}
+    d.update(dpace_report(r, N, B, V, T.world, 4, NT, peak, "strong"))
+    return d
 
 
 def torch_ops_dpace_loss(logits, targets, alpha, mask):
@@ -503,8 +652,6 @@ def run_ours(args):
     import torch.distributed as dist
     from datetime import timedelta
 
-    from specdec import _lib, ops
-
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -512,204 +659,182 @@ def run_ours(args):
     torch.cuda.set_device(dev)
     if world > 1:
         # high-priority NCCL stream: the loss all_reduce is dispatched ahead of
-        # the backward's CTAs and overlaps it
+        # the next kernel's CTAs and overlaps it
         opts = dist.ProcessGroupNCCL.Options()
         opts.is_high_priority_stream = True
         dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                                 timeout=timedelta(seconds=120), pg_options=opts)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def device_barrier():
-        device_barrier_on(world, dev)
-
-    def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    T = Timing(args, dev, world)
 
     N, B, V = args.n, 16, 128256
     E = N * B * V
     n_global = N * world
-    sets = [dpace_inputs(N, B, V, 2.0, 4, 1000 * s + rank, dev) for s in range(2)]
-    live = [float(m.sum()) / (N * B) for (_, _, m) in sets]
-    grad = torch.empty(N, B, V, device=dev)
-    stream = torch.cuda.current_stream(dev)
-    # ring kernels (16-byte-aligned inputs): forward = streaming + finalize, backward = 1
-    launches_per_step = 3 if all(x.data_ptr() % 16 == 0 for x, _, _ in sets) else 2
+    peak, peak_src = hbm_peak()
 
-    reducer = LossReducer(dev) if world > 1 and args.loss_reduce == "overlap" else None
-
-    def step(i, ev=None):
-        x, t, m = sets[i & 1]
-        if ev is not None:
-            ev[0].record(stream)
-        loss, lse, scale, _ = ops.dpace_forward(x, t, m, 0.5, 0, n_global=n_global, validate=False)
-        if ev is not None:
-            ev[1].record(stream)
-        if reducer is not None:
-            loss = reducer.start(loss)  # global loss, reduced beside the backward
-        elif world > 1:
-            dist.all_reduce(loss)
-        if ev is not None:
-            ev[2].record(stream)
-        ops.dpace_backward(x, t, lse, scale, None, out=grad)
-        if ev is not None:
-            ev[3].record(stream)
-        if reducer is not None:
-            reducer.wait()
-        return loss
-
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize(dev)
-    # untimed soak of about args.soak seconds: every step holds a collective
-    # when world > 1, so all ranks run the same, agreed number of steps
-    probe = time.perf_counter()
-    for i in range(4):
-        step(i)
-    torch.cuda.synchronize(dev)
-    per_step = max((time.perf_counter() - probe) / 4, 1e-5)
-    soak_steps = int(max_over_ranks(float(int(args.soak / per_step)))) if args.soak > 0 else 0
+    # untimed soak of about args.soak seconds on the headline workload, with
+    # the clock sampler running from here through the timed region
     sampler = ClockSampler(dev)
     sampler.start()
-    for i in range(soak_steps):
-        step(i)
-        if (i + 1) % 64 == 0:
-            torch.cuda.synchronize(dev)
+    head = None
+    if args.soak > 0:
+        from specdec import ops
 
-    # timed region: K uninstrumented steps (events between the kernels would
-    # break their programmatic-dependent-launch chaining)
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize(dev)
-    device_barrier()
-    start.record(stream)
-    for k in range(args.steps):
-        step(k)
-    stop.record(stream)
-    torch.cuda.synchronize(dev)
-    barrier()
+        x, t, m = dpace_inputs(N, B, V, 2.0, 4, rank, dev)
+        g = torch.empty_like(x)
+        ops.dpace_forward_backward(x, t, m, 0.5, 0, n_global=n_global, validate=False, out=g)
+        torch.cuda.synchronize(dev)
+        probe = time.perf_counter()
+        for _ in range(4):
+            ops.dpace_forward_backward(x, t, m, 0.5, 0, n_global=n_global, validate=False, out=g)
+        torch.cuda.synchronize(dev)
+        per_step = max((time.perf_counter() - probe) / 4, 1e-5)
+        soak_steps = int(T.max(float(int(args.soak / per_step))))
+        for i in range(soak_steps):
+            ops.dpace_forward_backward(x, t, m, 0.5, 0, n_global=n_global, validate=False, out=g)
+            if (i + 1) % 64 == 0:
+                torch.cuda.synchronize(dev)
+        torch.cuda.synchronize(dev)
+        del x, t, m, g
+    head = dpace_leg(args, T, N, B, V, 2.0, 4, n_global, args.steps)
     clocks = sampler.stop()
-    ms_local = start.elapsed_time(stop)
-    # per-kernel split (roofline): a second pass with events around each kernel
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
-    for k in range(args.steps):
-        step(k, evs[k])
-    torch.cuda.synchronize(dev)
-    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
-    bwd_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in evs)
-    ms = max_over_ranks(ms_local)
-    fwd_ms_max, bwd_ms_max = max_over_ranks(fwd_ms), max_over_ranks(bwd_ms)
-    dflash = None
-    if args.dflash_steps > 0:
-        dflash = time_dflash(args, dev, stream, world, n_global, max_over_ranks, barrier)
-    drafter = None
-    if args.drafter_steps > 0:
-        drafter = time_drafter_step(args, dev, world, max_over_ranks, barrier)
+    launches_per_step = 3 if head["aligned"] else 2  # ring: stream + finalize + backward
+
+    c4 = time_c4(args, T) if args.c4_steps > 0 else None
+    dflash = time_dflash(args, T, n_global) if args.dflash_steps > 0 else None
+    drafter = time_drafter_step(args, dev, world, T.max, T.barrier) if args.drafter_steps > 0 else None
     bf16 = None
     if args.bf16_steps > 0:
-        bf16 = {"dpace": time_dpace_bf16(args, dev, stream, world, n_global, max_over_ranks, barrier),
-                "dflash_kl": time_dflash(args, dev, stream, world, n_global, max_over_ranks, barrier,
-                                         dtype=torch.bfloat16, steps=args.bf16_steps)}
-    ms_step = ms / args.steps
-    total_bytes = 12.0 * E * world
-    value = total_bytes / (ms_step * 1e-3) / 1e9
-    rows_s = N * B * world / (ms_step * 1e-3)
+        bf16 = {"dpace": time_dpace_bf16(args, T, n_global),
+                "dflash_kl": time_dflash(args, T, n_global, dtype=torch.bfloat16, steps=args.bf16_steps)}
 
-    # roofline of the dominant kernel (the backward): bytes it must move per launch
-    peak, peak_src = hbm_peak()
-    live_frac = statistics.mean(live)
-    bwd_bytes = 4.0 * E * live_frac + 4.0 * E
-    fwd_bytes = 4.0 * E * live_frac
-    wl = f"{N}x{B}x{V}"
-    roof_bwd = {"kernel": "dpace_bwd_kernel", "bound": "hbm", "achieved": round(bwd_bytes / (bwd_ms_max * 1e-3) / 1e9, 1),
-                "peak": peak, "unit": "GB/s", "traffic": profiled_traffic("dpace_bwd", wl),
-                "bytes_per_launch": bwd_bytes, "peak_source": peak_src}
-    roof_bwd["frac"] = round(roof_bwd["achieved"] / peak, 4)
-    roof_fwd = {"kernel": "dpace_fwd_kernel", "achieved": round(fwd_bytes / (fwd_ms_max * 1e-3) / 1e9, 1),
-                "bytes_per_launch": fwd_bytes, "traffic": profiled_traffic("dpace_fwd", wl)}
-    roof_fwd["frac"] = round(roof_fwd["achieved"] / peak, 4)
-
-    # end to end through the public API: pinned host inputs -> dpace_loss -> backward -> loss to host
+    # end to end through the public API: pinned host inputs -> dpace_loss ->
+    # backward -> loss to host. The next step's inputs are copied on a copy
+    # stream while this step computes (double-buffered device inputs).
     e2e = None
     if args.e2e_steps > 0:
         from losses import dpace_loss
-
-        hx = [s[0].cpu().pin_memory() for s in sets]
-        ht = [s[1].cpu().pin_memory() for s in sets]
-        hm = [s[2].cpu().pin_memory() for s in sets]
-        hloss = torch.empty((), dtype=torch.float32).pin_memory()
-
+        from specdec import ops
         from specdec.dist import sharded_dpace_loss
 
-        def e2e_step(i):
-            x = hx[i & 1].to(dev, non_blocking=True).requires_grad_(True)
-            t = ht[i & 1].to(dev, non_blocking=True)
-            m = hm[i & 1].to(dev, non_blocking=True)
+        hsets = [dpace_inputs(N, B, V, 2.0, 4, 1000 * s_ + rank, torch.device("cpu")) for s_ in range(2)]
+        hx = [h[0].pin_memory() for h in hsets]
+        ht = [h[1].pin_memory() for h in hsets]
+        hm = [h[2].pin_memory() for h in hsets]
+        del hsets
+        hloss = torch.empty((), dtype=torch.float32).pin_memory()
+        bufs = [(torch.empty(N, B, V, device=dev), torch.empty(N, B, dtype=torch.int64, device=dev),
+                 torch.empty(N, B, device=dev)) for _ in range(2)]
+        copy_stream = torch.cuda.Stream(dev)
+        ready = [torch.cuda.Event() for _ in range(2)]
+        free = [torch.cuda.Event() for _ in range(2)]
+        for ev in free:
+            ev.record(T.stream)
+        saved_fused = ops.FUSED_BACKWARD
+        ops.set_fused_backward(args.e2e_fused)
+
+        def h2d(i):
+            j = i & 1
+            with torch.cuda.stream(copy_stream):
+                copy_stream.wait_event(free[j])
+                for d, h in zip(bufs[j], (hx[j], ht[j], hm[j])):
+                    d.copy_(h, non_blocking=True)
+                ready[j].record(copy_stream)
+
+        def e2e_step(i, steps):
+            j = i & 1
+            if i + 1 < steps:
+                h2d(i + 1)  # prefetch the next step's inputs
+            T.stream.wait_event(ready[j])
+            x = bufs[j][0].detach().requires_grad_(True)
+            t, m = bufs[j][1], bufs[j][2]
             if world > 1:  # the multi-GPU entry point: this rank's shard, global loss
                 loss = sharded_dpace_loss(x, t, 0.5, m, n_global=n_global)
             else:
                 loss = dpace_loss(x, t, 0.5, m)
             loss.backward()
+            free[j].record(T.stream)
             hloss.copy_(loss.detach(), non_blocking=True)
-            return x
 
+        h2d(0)
         for i in range(2):
-            e2e_step(i)
+            e2e_step(i, 2)
         torch.cuda.synchronize(dev)
-        barrier()
-        device_barrier()
+        T.barrier()
+        device_barrier_on(world, dev)
         s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s0.record(stream)
+        s0.record(T.stream)
+        copy_stream.wait_event(s0)  # every one of the K steps' copies runs inside the timed region
+        h2d(0)
         for i in range(args.e2e_steps):
-            e2e_step(i)
-        s1.record(stream)
+            e2e_step(i, args.e2e_steps)
+        s1.record(T.stream)
         torch.cuda.synchronize(dev)
-        e2e_ms = max_over_ranks(s0.elapsed_time(s1)) / args.e2e_steps
-        h2d = hx[0].numel() * 4 + ht[0].numel() * 8 + hm[0].numel() * 4
-        e2e = {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": UNIT,
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4 + 4,
+        ops.set_fused_backward(saved_fused)
+        e2e_ms = T.max(s0.elapsed_time(s1)) / args.e2e_steps
+        h2d_bytes = hx[0].numel() * 4 + ht[0].numel() * 8 + hm[0].numel() * 4
+        e2e = {"value": round(12.0 * E * world / (e2e_ms * 1e-3) / 1e9, 2), "unit": UNIT,
+               "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": 4 + 12,
                "ms_per_step": round(e2e_ms, 3), "steps": args.e2e_steps,
+               "h2d_gbs": round(h2d_bytes / (e2e_ms * 1e-3) / 1e9, 2),
                "path": ("specdec.dist.sharded_dpace_loss" if world > 1 else "losses.dpace.dpace_loss")
-                       + "(...).backward() from pinned host buffers; includes the target-range check "
-                         "(4-byte read-back)"}
+                       + "(...).backward() from pinned host buffers (each step's inputs copied on a copy "
+                         "stream while the previous step computes); includes the target-range check "
+                         "(12-byte status read-back)"
+                       + ("; specdec.ops.set_fused_backward(True)" if args.e2e_fused else "")}
+        del bufs, hx, ht, hm
 
-    cpu_base = None
+    cpu_base = cpu_dflash = None
     if rank == 0 and world == 1 and args.cpu_budget > 0:
         cpu_base = time_cpu_baseline(B, V, args.cpu_budget)
+        cpu_dflash = time_cpu_baseline_dflash(B, V, args.cpu_budget)
+        if dflash is not None:
+            dflash["cpu_baseline"] = cpu_dflash
 
+    # every rank's own figures, for the scaling record
+    mine = {"rank": rank, "ms_per_step": round(head["ms_local"], 4), "clocks": clocks,
+            "c4_ms_per_step": None if c4 is None else c4["ms_per_step_this_rank"],
+            "dflash_ms_per_step": None if dflash is None else dflash["ms_per_step_this_rank"]}
+    per_rank = [None] * world
     if world > 1:
+        dist.all_gather_object(per_rank, mine)
         dist.destroy_process_group()
+    else:
+        per_rank = [mine]
     if rank != 0:
         return 0
-    line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+
+    rep = dpace_report(head, N, B, V, world, 4, N * B * world, peak, "weak")
+    line = {"metric": METRIC, "value": rep["value"], "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": rep["ms_per_step"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
             "config": {"workload": "dpace_fwd_bwd_llama3_vocab", "N_per_gpu": N, "B": B, "V": V,
                        "global_N": n_global, "sigma": 2.0, "mask": "prefix k~U{0..4}",
-                       "alpha": 0.5, "loss_type": "dpace", "parallelism": f"dp{world} (N-sharded)", "loss_all_reduce": args.loss_reduce if world > 1 else None,
+                       "alpha": 0.5, "loss_type": "dpace", "parallelism": f"dp{world} (N-sharded)",
+                       "loss_all_reduce": (args.loss_reduce + ", one per step, started after the step's "
+                                           "call, waited for once before the stop event") if world > 1
+                       else None,
                        "l2": "two alternating input sets, each 525 MB > 126 MB L2",
-                       "bytes_model": "12*N*B*V per GPU-step"},
-            "rows_per_s": round(rows_s, 1),
-            "pct_of_hbm_peak": round(100.0 * value / world / peak, 2),
-            "roofline": roof_bwd,
-            "kernels": {"dpace_fwd_ms": round(fwd_ms_max, 4), "dpace_bwd_ms": round(bwd_ms_max, 4),
-                        "fwd": roof_fwd,
+                       "bytes_model": "12*N*B*V per GPU-step",
+                       "step": "specdec_dpace_forward_backward through the C ABI (library level: the "
+                               "public API's 4-byte status read-back is timed in e2e)"},
+            "rows_per_s": rep["rows_per_s"],
+            "moved_bytes_per_step": rep["moved_bytes_per_step"],
+            "pct_of_hbm_peak": rep["pct_of_hbm_peak"], "pct_basis": rep["pct_basis"],
+            "roofline": dict(rep["roofline"], peak_source=peak_src),
+            "kernels": {"fwd": rep["fwd_roofline"], "split_ms": rep["split_ms"],
                         "launches_per_step": launches_per_step,
-                        "fwd_note": "forward = streaming kernel + PDL-chained finalize kernel"},
+                        "fwd_note": "forward = streaming kernel + PDL-chained finalize kernel; in the "
+                                    "timed step the backward is PDL-chained to the finalize"},
+            "live_row_fraction": rep["live_row_fraction"],
+            "c4": c4,
             "dflash_kl": dflash,
             "bf16": bf16,
             "drafter_step": drafter,
-            "live_row_fraction": round(live_frac, 4),
             "cpu_baseline": cpu_base, "e2e": e2e,
-            "gpu_launches": launches_per_step * args.steps, "gpu_launches_scope": "per rank",
-            "clocks": clocks}
+            "gpu_launches": launches_per_step * args.steps, "gpu_launches_scope": "per rank, headline loop",
+            "clocks": clocks,
+            "per_rank": per_rank}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -733,7 +858,11 @@ def main(argv=None):
                    help="N > 1: loss all_reduce on a side stream beside the backward, or between "
                         "forward and backward on the compute stream")
     p.add_argument("--cpu-budget", type=float, default=10.0,
-                   help="seconds of CPU-oracle timing on rank 0 at N=1 (0 = skip)")
+                   help="seconds of CPU-oracle timing per objective on rank 0 at N=1 (0 = skip)")
+    p.add_argument("--c4-steps", type=int, default=10,
+                   help="timed steps of the large-batch [512,32,151936] workload (0 = skip)")
+    p.add_argument("--e2e-fused", type=int, default=1,
+                   help="e2e: specdec.ops.set_fused_backward (1) or the separate backward kernel (0)")
     args = p.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3

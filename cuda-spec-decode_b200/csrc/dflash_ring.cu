@@ -81,6 +81,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 2, S, SE, T>
       if (!ring_produce<2, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow,
                                       a.withhold_stage && blockIdx.x == 0))
         atomicOr(a.flag, 2);
+      q.retire();
     }
     pdl_trigger();
     return;
@@ -194,6 +195,9 @@ __global__ void __launch_bounds__(1024) dflash_finalize_kernel(const __grid_cons
   for (int i = lane; i < B; i += 32) mv += a.mask ? a.mask[n * B + i] : 1.f;
   const float denom = warp_sum(mv) + 1e-5f;
   pdl_wait();  // the streaming grid has completed and its stores are visible
+  // a wait of the streaming grid expired: pieces may be missing, so every
+  // per-row output is NaN (a backward from them gives a NaN gradient)
+  const bool timed_out = (*reinterpret_cast<volatile int*>(a.flag) & 2) != 0;
   float acc = 0.f;  // this warp's rows, in row order
   for (int j = warp; j < B; j += nwarps) {
     const int64_t r = n * B + j;
@@ -233,10 +237,11 @@ __global__ void __launch_bounds__(1024) dflash_finalize_kernel(const __grid_cons
     }
     const float lr = numer != 0.f ? __fmul_rn(w, el) : 0.f;
     if (lane == 0) {
+      const float nan = __int_as_float(0x7fc00000);
       if (a.loss_rows) a.loss_rows[r] = lr;
-      a.scale[r] = __fdiv_rn(w, (float)a.n_global);
-      a.logzq[r] = lzq;
-      a.logzp[r] = lzp;
+      a.scale[r] = timed_out ? nan : __fdiv_rn(w, (float)a.n_global);
+      a.logzq[r] = timed_out ? nan : lzq;
+      a.logzp[r] = timed_out ? nan : lzp;
       if (a.target_id) a.target_id[r] = tgt;
     }
     acc += lr;
@@ -295,151 +300,155 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, (KIND == kKi
   if (warp == NC) {
     if (lane == 0) {
       const T* src[2] = {XL, XT};
-      if (!ring_produce<NIN, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow) &&
-          a.flag)
-        atomicOr(a.flag, 2);
+      if (!ring_produce<NIN, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow,
+                                        a.withhold_stage && blockIdx.x == 0, &sm.trk))
+        sm.trk.timeout = 1;
     }
-    return;
-  }
-
-  const T* ringl = sm.ring;
-  const T* ringt = sm.ring + (size_t)S * SE;  // KL only
-  int64_t r = 0, blk = -1, tf = -1;
-  float sc = 0.f, lq = 0.f, lp = 0.f;
-  auto load_row = [&](int64_t row) {
-    sc = __fmul_rn(a.scale[row], g);
-    lq = a.logzq[row];
-    lp = a.logzp[row];
-    tf = KIND == kKindCE ? row * V + a.target_id[row] : -1;
-  };
-  for (int64_t it = 0;; ++it) {
-    const int slot = (int)(it % S);
-    if (!__all_sync(kFullMask, mbar_wait(sm.full + slot, (uint32_t)((it / S) & 1)))) {
-      if (lane == 0 && a.flag) atomicOr(a.flag, 2);
-      ring_drain<S>(sm.full, it + 1);
-      return;
-    }
-    const int64_t f0 = sm.sf0[slot];
-    if (f0 < 0) return;
-    const int64_t b = f0 >> kLogBL;
-    const int64_t blk_end = min((b + 1) * BL, E);
-    const int64_t f1 = min(f0 + SE, blk_end);
-    if (b != blk) {
-      blk = b;
-      r = sm.srow[slot];
-      load_row(r);
-    }
-    const int64_t fv = copied_end<T>(f0, f1);
-    const int64_t w0 = f0 + (int64_t)warp * kSub, w1 = min(w0 + kSub, f1);
-    const T* sl = ringl + (size_t)slot * SE;
-    const T* sx = ringt + (size_t)slot * SE;
-    int64_t f = f0;
-    while (f < f1) {
-      const int64_t rend = (r + 1) * V;
-      const int64_t ge = min(f1, rend);
-      const int64_t lo = max(f, w0), hi = min(ge, w1);
-      if (lo < hi) {
-        const bool zero = sc == 0.f || !rb.live(r);
-        const int64_t lov = (lo + kVec - 1) & ~int64_t(kVec - 1), hiv = min(hi, fv) & ~int64_t(kVec - 1);
-        auto scalar = [&](int64_t x) {
-          if (zero) {
-            store_elem(dst + x, 0.f);
-          } else {
-            const float vl = x < fv ? to_f32(sl[x - f0]) : ldg_f32(XL + x);
-            const float qv = exp_shift(vl, lq);
-            float pv;
-            if (KIND == kKindKL) pv = exp_shift(x < fv ? to_f32(sx[x - f0]) : ldg_f32(XT + x), lp);
-            else pv = x == tf ? 1.f : 0.f;
-            store_elem(dst + x, sc * (qv - pv));
-          }
-        };
-        if (lov < hiv) {
-          for (int64_t x = lo + lane; x < lov; x += 32) scalar(x);
-          for (int64_t x = hiv + lane; x < hi; x += 32) scalar(x);
-          const int nv = (int)((hiv - lov) / kVec);
-          if (zero) {
-            const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-            uint4* d4 = reinterpret_cast<uint4*>(dst + lov);
-            for (int k = lane; k < nv; k += 32) st_stream_u4(d4 + k, z);
-          } else if constexpr (sizeof(T) == 4) {
-            float4* d4 = reinterpret_cast<float4*>(dst + lov);
-            const float4* s4 = reinterpret_cast<const float4*>(sl + (lov - f0));
-            const float4* t4 = reinterpret_cast<const float4*>(sx + (lov - f0));
-            const int64_t tq = tf - lov;
-            for (int k = lane; k < nv; k += 32) {
-              const float4 v = s4[k];
-              float4 y;
-              y.x = exp_shift(v.x, lq);
-              y.y = exp_shift(v.y, lq);
-              y.z = exp_shift(v.z, lq);
-              y.w = exp_shift(v.w, lq);
-              if (KIND == kKindKL) {
-                const float4 u = t4[k];
-                y.x -= exp_shift(u.x, lp);
-                y.y -= exp_shift(u.y, lp);
-                y.z -= exp_shift(u.z, lp);
-                y.w -= exp_shift(u.w, lp);
-              } else {
-                const uint64_t d = (uint64_t)(tq - 4 * (int64_t)k);
-                if (d < 4) {
-                  if (d == 0) y.x -= 1.f;
-                  else if (d == 1) y.y -= 1.f;
-                  else if (d == 2) y.z -= 1.f;
-                  else y.w -= 1.f;
-                }
-              }
-              y.x *= sc;
-              y.y *= sc;
-              y.z *= sc;
-              y.w *= sc;
-              st_stream(d4 + k, y);
-            }
-          } else {
-            uint4* d4 = reinterpret_cast<uint4*>(dst + lov);
-            const uint4* s4 = reinterpret_cast<const uint4*>(sl + (lov - f0));
-            const uint4* t4 = reinterpret_cast<const uint4*>(sx + (lov - f0));
-            const int64_t tq = tf - lov;
-            const float2 sc2 = make_float2(sc, sc);
-            for (int k = lane; k < nv; k += 32) {
-              const uint4 v = s4[k];
-              const uint32_t wl[4] = {v.x, v.y, v.z, v.w};
-              float2 q[4], y[4];
-#pragma unroll
-              for (int h = 0; h < 4; ++h) q[h] = exp_shift2(bf16x2_f32(wl[h]), lq);
-              if (KIND == kKindKL) {
-                const uint4 u = t4[k];
-                const uint32_t wt[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-                for (int h = 0; h < 4; ++h) y[h] = fmul2(fsub2(q[h], exp_shift2(bf16x2_f32(wt[h]), lp)), sc2);
-              } else {
-#pragma unroll
-                for (int h = 0; h < 4; ++h) y[h] = fmul2(q[h], sc2);
-                const uint64_t d = (uint64_t)(tq - 8 * (int64_t)k);
-                if (d < 8) {  // the argmax target: sc * (q - 1), as the float kernel
-#pragma unroll
-                  for (int h = 0; h < 4; ++h) {
-                    if (d == (uint64_t)(2 * h)) y[h].x = sc * (q[h].x - 1.f);
-                    if (d == (uint64_t)(2 * h + 1)) y[h].y = sc * (q[h].y - 1.f);
-                  }
-                }
-              }
-              st_stream_u4(d4 + k, make_uint4(pack_bf16x2(y[0].x, y[0].y), pack_bf16x2(y[1].x, y[1].y),
-                                              pack_bf16x2(y[2].x, y[2].y), pack_bf16x2(y[3].x, y[3].y)));
-            }
-          }
-        } else {
-          for (int64_t x = lo + lane; x < hi; x += 32) scalar(x);
-        }
+  } else {
+    const T* ringl = sm.ring;
+    const T* ringt = sm.ring + (size_t)S * SE;  // KL only
+    int64_t r = 0, blk = -1, tf = -1;
+    float sc = 0.f, lq = 0.f, lp = 0.f;
+    auto load_row = [&](int64_t row) {
+      sc = __fmul_rn(a.scale[row], g);
+      lq = a.logzq[row];
+      lp = a.logzp[row];
+      tf = KIND == kKindCE ? row * V + a.target_id[row] : -1;
+    };
+    int64_t it = 0;
+    for (;; ++it) {
+      const int slot = (int)(it % S);
+      if (!__all_sync(kFullMask, mbar_wait(sm.full + slot, (uint32_t)((it / S) & 1)))) {
+        if (lane == 0) sm.trk.timeout = 1;
+        ring_drain<S>(sm.full, it + 1);
+        break;
       }
-      f = ge;
-      if (ge == rend && ge < E) {
-        ++r;
+      const int64_t f0 = sm.sf0[slot];
+      if (f0 < 0) break;
+      const int64_t b = f0 >> kLogBL;
+      const int64_t blk_end = min((b + 1) * BL, E);
+      const int64_t f1 = min(f0 + SE, blk_end);
+      if (b != blk) {
+        blk = b;
+        r = sm.srow[slot];
         load_row(r);
       }
+      const int64_t fv = copied_end<T>(f0, f1);
+      const int64_t w0 = f0 + (int64_t)warp * kSub, w1 = min(w0 + kSub, f1);
+      const T* sl = ringl + (size_t)slot * SE;
+      const T* sx = ringt + (size_t)slot * SE;
+      int64_t f = f0;
+      while (f < f1) {
+        const int64_t rend = (r + 1) * V;
+        const int64_t ge = min(f1, rend);
+        const int64_t lo = max(f, w0), hi = min(ge, w1);
+        if (lo < hi) {
+          const bool zero = sc == 0.f || !rb.live(r);
+          const int64_t lov = (lo + kVec - 1) & ~int64_t(kVec - 1), hiv = min(hi, fv) & ~int64_t(kVec - 1);
+          auto scalar = [&](int64_t x) {
+            if (zero) {
+              store_elem(dst + x, 0.f);
+            } else {
+              const float vl = x < fv ? to_f32(sl[x - f0]) : ldg_f32(XL + x);
+              const float qv = exp_shift(vl, lq);
+              float pv;
+              if (KIND == kKindKL) pv = exp_shift(x < fv ? to_f32(sx[x - f0]) : ldg_f32(XT + x), lp);
+              else pv = x == tf ? 1.f : 0.f;
+              store_elem(dst + x, sc * (qv - pv));
+            }
+          };
+          if (lov < hiv) {
+            for (int64_t x = lo + lane; x < lov; x += 32) scalar(x);
+            for (int64_t x = hiv + lane; x < hi; x += 32) scalar(x);
+            const int nv = (int)((hiv - lov) / kVec);
+            if (zero) {
+              const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+              uint4* d4 = reinterpret_cast<uint4*>(dst + lov);
+              for (int k = lane; k < nv; k += 32) st_stream_u4(d4 + k, z);
+            } else if constexpr (sizeof(T) == 4) {
+              float4* d4 = reinterpret_cast<float4*>(dst + lov);
+              const float4* s4 = reinterpret_cast<const float4*>(sl + (lov - f0));
+              const float4* t4 = reinterpret_cast<const float4*>(sx + (lov - f0));
+              const int64_t tq = tf - lov;
+              for (int k = lane; k < nv; k += 32) {
+                const float4 v = s4[k];
+                float4 y;
+                y.x = exp_shift(v.x, lq);
+                y.y = exp_shift(v.y, lq);
+                y.z = exp_shift(v.z, lq);
+                y.w = exp_shift(v.w, lq);
+                if (KIND == kKindKL) {
+                  const float4 u = t4[k];
+                  y.x -= exp_shift(u.x, lp);
+                  y.y -= exp_shift(u.y, lp);
+                  y.z -= exp_shift(u.z, lp);
+                  y.w -= exp_shift(u.w, lp);
+                } else {
+                  const uint64_t d = (uint64_t)(tq - 4 * (int64_t)k);
+                  if (d < 4) {
+                    if (d == 0) y.x -= 1.f;
+                    else if (d == 1) y.y -= 1.f;
+                    else if (d == 2) y.z -= 1.f;
+                    else y.w -= 1.f;
+                  }
+                }
+                y.x *= sc;
+                y.y *= sc;
+                y.z *= sc;
+                y.w *= sc;
+                st_stream(d4 + k, y);
+              }
+            } else {
+              uint4* d4 = reinterpret_cast<uint4*>(dst + lov);
+              const uint4* s4 = reinterpret_cast<const uint4*>(sl + (lov - f0));
+              const uint4* t4 = reinterpret_cast<const uint4*>(sx + (lov - f0));
+              const int64_t tq = tf - lov;
+              const float2 sc2 = make_float2(sc, sc);
+              for (int k = lane; k < nv; k += 32) {
+                const uint4 v = s4[k];
+                const uint32_t wl[4] = {v.x, v.y, v.z, v.w};
+                float2 q[4], y[4];
+  #pragma unroll
+                for (int h = 0; h < 4; ++h) q[h] = exp_shift2(bf16x2_f32(wl[h]), lq);
+                if (KIND == kKindKL) {
+                  const uint4 u = t4[k];
+                  const uint32_t wt[4] = {u.x, u.y, u.z, u.w};
+  #pragma unroll
+                  for (int h = 0; h < 4; ++h) y[h] = fmul2(fsub2(q[h], exp_shift2(bf16x2_f32(wt[h]), lp)), sc2);
+                } else {
+  #pragma unroll
+                  for (int h = 0; h < 4; ++h) y[h] = fmul2(q[h], sc2);
+                  const uint64_t d = (uint64_t)(tq - 8 * (int64_t)k);
+                  if (d < 8) {  // the argmax target: sc * (q - 1), as the float kernel
+  #pragma unroll
+                    for (int h = 0; h < 4; ++h) {
+                      if (d == (uint64_t)(2 * h)) y[h].x = sc * (q[h].x - 1.f);
+                      if (d == (uint64_t)(2 * h + 1)) y[h].y = sc * (q[h].y - 1.f);
+                    }
+                  }
+                }
+                st_stream_u4(d4 + k, make_uint4(pack_bf16x2(y[0].x, y[0].y), pack_bf16x2(y[1].x, y[1].y),
+                                                pack_bf16x2(y[2].x, y[2].y), pack_bf16x2(y[3].x, y[3].y)));
+              }
+            }
+          } else {
+            for (int64_t x = lo + lane; x < hi; x += 32) scalar(x);
+          }
+        }
+        f = ge;
+        if (ge == rend && ge < E) {
+          ++r;
+          load_row(r);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sm.empty + slot);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(sm.empty + slot);
+    if (lane == 0) sm.trk.done[warp] = it;
   }
+  __syncthreads();
+  if (sm.trk.timeout) ring_poison<T, S>(dst, E, BL, q.nblocks, sm.trk, NC);
+  if (threadIdx.x == 0) bwd_finish(q, a, sm.trk.timeout != 0);
 }
 
 template <class T, int NC, int S, int SE, int BS>

@@ -14,13 +14,16 @@
 //   - nothing here calls cudaMalloc, cudaFree or any allocating routine;
 //   - the first call on a device looks up the array's device address
 //     (cudaGetSymbolAddress, with that device current); make that first call
-//     before any stream capture;
+//     before any stream capture. The address is kept for the life of the
+//     process, so the entry point must not be used on a device after
+//     cudaDeviceReset (or another destruction of its primary context);
 //   - every call on a device shares the one array, which keeps the last
 //     call's contents: the counter region is cleared on the caller's stream
 //     before each launch, and calls that overlap on the GPU (different
 //     streams, no ordering between them) race on the array;
-//   - problems whose scratch does not fit are rejected with
-//     SPECDEC_ERR_WORKSPACE before anything is launched.
+//   - the arguments are checked first, exactly as specdec_dpace_forward
+//     checks them; then problems whose scratch does not fit are rejected
+//     with SPECDEC_ERR_WORKSPACE; nothing is enqueued for either.
 #include "specdec.h"
 #include "specdec_internal.h"
 
@@ -64,9 +67,14 @@ extern "C" int specdec_dpace_forward_noalloc(const float* logits, const int64_t*
                                              float alpha, int32_t loss_type, int64_t n_global,
                                              float* loss, float* loss_n, float* lse, float* scale,
                                              int32_t* status, void* stream) {
-  if (N <= 0 || V <= 0 || B < 1 || B > 32) {
-    // nothing to stream, or an argument error: the allocating entry point
-    // handles these without touching any scratch
+  // argument errors first, in the allocating entry point's order, before
+  // anything touches the shared array
+  const int rc = specdec::dpace_forward_check(specdec::kDtypeF32, logits, targets, N, B, V, alpha, loss_type,
+                                              n_global, loss, lse, scale);
+  if (rc != SPECDEC_OK) return rc;
+  if (N == 0) {
+    // an empty batch: the allocating entry point writes the NaN loss and
+    // touches no scratch
     return specdec_dpace_forward(logits, targets, mask, N, B, V, alpha, loss_type, n_global, loss,
                                  loss_n, lse, scale, status, nullptr, 0, nullptr, 0, stream);
   }

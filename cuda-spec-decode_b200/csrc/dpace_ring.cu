@@ -70,6 +70,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
         atomicOr(a.flag, 2);
         if (a.status) a.status[0] = kStatusTimeout;
       }
+      q.retire();
     }
     pdl_trigger();
     return;
@@ -158,10 +159,14 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
 template <class T>
 __global__ void __launch_bounds__(1024) dpace_finalize_kernel(const __grid_constant__ DpaceFwdArgs a) {
   __shared__ float sh_ce[32];
+  // a backward chained behind this kernel (specdec_dpace_forward_backward)
+  // may become resident now: it streams logits and waits for lse / scale
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int B = a.B;
   const int64_t n = blockIdx.x, V = a.pt.V, BL = a.pt.chunk;
   const int NC = a.nc;
+  bool timed_out;
   {
     const int64_t r = n * B + warp;
     // inputs the streaming grid does not write: read them while it drains
@@ -170,6 +175,9 @@ __global__ void __launch_bounds__(1024) dpace_finalize_kernel(const __grid_const
     const bool tvalid = t >= 0 && t < V;
     const float xt = tvalid ? ldg_f32(static_cast<const T*>(a.logits) + r * V + t) : 0.f;  // x[target]
     pdl_wait();  // the streaming grid has completed and its stores are visible
+    // a wait of the streaming grid expired: partials may be missing, so every
+    // per-row output is NaN (a backward from them gives a NaN gradient)
+    timed_out = (*reinterpret_cast<volatile int*>(a.flag) & 2) != 0;
     const int k = blocks_in_row(r, V, BL) * NC;
     const float2* part = a.part + r * a.pt.pmax * NC;
     float2 pv[2];
@@ -190,7 +198,7 @@ __global__ void __launch_bounds__(1024) dpace_finalize_kernel(const __grid_const
     }
     if (!tvalid && lane == 0) atomicOr(a.flag, 1);
     if (lane == 0) {
-      a.lse[r] = lse;
+      a.lse[r] = timed_out ? __int_as_float(0x7fc00000) : lse;
       sh_ce[warp] = ce;
     }
   }
@@ -229,7 +237,7 @@ __global__ void __launch_bounds__(1024) dpace_finalize_kernel(const __grid_const
     float w = a.loss_type == 1 ? P : (a.loss_type == 2 ? __fdiv_rn(S, fmaxf(P, FLT_MIN)) : S);
     w = __fmul_rn(w, mk);
     const float contrib = live ? __fmul_rn(ce, w) : 0.f;
-    if (in) a.scale[r] = __fmul_rn(w, a.inv_n);
+    if (in) a.scale[r] = timed_out ? __int_as_float(0x7fc00000) : __fmul_rn(w, a.inv_n);
     const float loss_n = warp_sum(contrib);
     unsigned last = 0;
     if (lane == 0) {
@@ -268,8 +276,14 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
   const int64_t E = a.pt.E, V = a.pt.V, R = E / V;
   const float g = a.dloss ? __ldg(a.dloss) : 1.f;
   ring_init(sm, NC);
+  // Rows to read: those with a nonzero scale * dloss -- or, when chained
+  // behind the finalize that writes scale, those with a scored mask, which is
+  // known at once (a row with mask 0 has scale 0; a scored row whose scale is
+  // 0 is read and written as zeros). Everything before the consumers' wait
+  // touches only inputs the finalize does not write.
+  if (!a.mask_liveness) pdl_wait();
   const RowBits rb = build_row_bits(sm.bits, R, NC + 1, [&](int64_t r) {
-    return __fmul_rn(a.scale[r], g) != 0.f;
+    return a.mask_liveness ? (a.live_mask == nullptr || a.live_mask[r] > 0.f) : __fmul_rn(a.scale[r], g) != 0.f;
   });
   __syncthreads();
 
@@ -282,127 +296,133 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
   if (warp == NC) {
     if (lane == 0) {
       const T* src[1] = {X};
-      if (!ring_produce<1, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow) && a.flag)
-        atomicOr(a.flag, 2);
+      if (!ring_produce<1, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow,
+                                      a.withhold_stage && blockIdx.x == 0, &sm.trk))
+        sm.trk.timeout = 1;
     }
-    return;
-  }
-
-  int64_t r = 0, blk = -1, tf = -1;
-  float sc = 0.f, l = 0.f;
-  auto load_row = [&](int64_t row) {
-    sc = __fmul_rn(a.scale[row], g);
-    l = a.lse[row];
-    tf = row * V + a.targets[row];
-  };
-  for (int64_t it = 0;; ++it) {
-    const int slot = (int)(it % S);
-    if (!__all_sync(kFullMask, mbar_wait(sm.full + slot, (uint32_t)((it / S) & 1)))) {
-      if (lane == 0 && a.flag) atomicOr(a.flag, 2);
-      ring_drain<S>(sm.full, it + 1);
-      return;
-    }
-    const int64_t f0 = sm.sf0[slot];
-    if (f0 < 0) return;
-    const int64_t b = f0 / BL;
-    const int64_t blk_end = min((b + 1) * BL, E);
-    const int64_t f1 = min(f0 + SE, blk_end);
-    if (b != blk) {
-      blk = b;
-      r = sm.srow[slot];
-      load_row(r);
-    }
-    const int64_t fv = copied_end<T>(f0, f1);
-    const int64_t w0 = f0 + (int64_t)warp * kSub, w1 = min(w0 + kSub, f1);
-    const T* sb = sm.ring + (size_t)slot * SE;
-    int64_t f = f0;
-    while (f < f1) {
-      const int64_t rend = (r + 1) * V;
-      const int64_t ge = min(f1, rend);
-      const int64_t lo = max(f, w0), hi = min(ge, w1);
-      if (lo < hi) {
-        const bool zero = sc == 0.f || !rb.live(r);
-        // [lo, hi): scalar head to a vector boundary, 16-byte body, scalar tail
-        const int64_t lov = (lo + kVec - 1) & ~int64_t(kVec - 1), hiv = min(hi, fv) & ~int64_t(kVec - 1);
-        auto scalar = [&](int64_t x) {
-          if (zero) {
-            store_elem(dst + x, 0.f);
-          } else {
-            const float v = x < fv ? to_f32(sb[x - f0]) : ldg_f32(X + x);
-            store_elem(dst + x, sc * (exp_shift(v, l) - (x == tf ? 1.f : 0.f)));
-          }
-        };
-        if (lov < hiv) {
-          for (int64_t x = lo + lane; x < lov; x += 32) scalar(x);
-          for (int64_t x = hiv + lane; x < hi; x += 32) scalar(x);
-          const int nv = (int)((hiv - lov) / kVec);
-          if (zero) {
-            const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-            uint4* d4 = reinterpret_cast<uint4*>(dst + lov);
-            for (int k = lane; k < nv; k += 32) st_stream_u4(d4 + k, z);
-          } else if constexpr (sizeof(T) == 4) {
-            float4* d4 = reinterpret_cast<float4*>(dst + lov);
-            const float4* s4 = reinterpret_cast<const float4*>(sb + (lov - f0));
-            const int64_t tq = tf - lov;
-            for (int k = lane; k < nv; k += 32) {
-              const float4 v = s4[k];
-              float4 y;
-              y.x = exp_shift(v.x, l);
-              y.y = exp_shift(v.y, l);
-              y.z = exp_shift(v.z, l);
-              y.w = exp_shift(v.w, l);
-              const uint64_t d = (uint64_t)(tq - 4 * (int64_t)k);
-              if (d < 4) {
-                if (d == 0) y.x -= 1.f;
-                else if (d == 1) y.y -= 1.f;
-                else if (d == 2) y.z -= 1.f;
-                else y.w -= 1.f;
-              }
-              y.x *= sc;
-              y.y *= sc;
-              y.z *= sc;
-              y.w *= sc;
-              st_stream(d4 + k, y);
-            }
-          } else {
-            uint4* d4 = reinterpret_cast<uint4*>(dst + lov);
-            const uint4* s4 = reinterpret_cast<const uint4*>(sb + (lov - f0));
-            const int64_t tq = tf - lov;
-            const float2 sc2 = make_float2(sc, sc);
-            for (int k = lane; k < nv; k += 32) {
-              const uint4 v = s4[k];
-              const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-              float2 e[4], y[4];
-#pragma unroll
-              for (int h = 0; h < 4; ++h) {
-                e[h] = exp_shift2(bf16x2_f32(w[h]), l);
-                y[h] = fmul2(e[h], sc2);
-              }
-              const uint64_t d = (uint64_t)(tq - 8 * (int64_t)k);
-              if (d < 8) {  // the target: sc * (p - 1), as the float kernel
-#pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                  if (d == (uint64_t)(2 * h)) y[h].x = sc * (e[h].x - 1.f);
-                  if (d == (uint64_t)(2 * h + 1)) y[h].y = sc * (e[h].y - 1.f);
-                }
-              }
-              st_stream_u4(d4 + k, make_uint4(pack_bf16x2(y[0].x, y[0].y), pack_bf16x2(y[1].x, y[1].y),
-                                              pack_bf16x2(y[2].x, y[2].y), pack_bf16x2(y[3].x, y[3].y)));
-            }
-          }
-        } else {
-          for (int64_t x = lo + lane; x < hi; x += 32) scalar(x);
-        }
+  } else {
+    pdl_wait();  // lse and scale (chained: written by the finalize)
+    int64_t r = 0, blk = -1, tf = -1;
+    float sc = 0.f, l = 0.f;
+    auto load_row = [&](int64_t row) {
+      sc = __fmul_rn(a.scale[row], g);
+      l = a.lse[row];
+      tf = row * V + a.targets[row];
+    };
+    int64_t it = 0;
+    for (;; ++it) {
+      const int slot = (int)(it % S);
+      if (!__all_sync(kFullMask, mbar_wait(sm.full + slot, (uint32_t)((it / S) & 1)))) {
+        if (lane == 0) sm.trk.timeout = 1;
+        ring_drain<S>(sm.full, it + 1);
+        break;
       }
-      f = ge;
-      if (ge == rend && ge < E) {
-        ++r;
+      const int64_t f0 = sm.sf0[slot];
+      if (f0 < 0) break;
+      const int64_t b = f0 / BL;
+      const int64_t blk_end = min((b + 1) * BL, E);
+      const int64_t f1 = min(f0 + SE, blk_end);
+      if (b != blk) {
+        blk = b;
+        r = sm.srow[slot];
         load_row(r);
       }
+      const int64_t fv = copied_end<T>(f0, f1);
+      const int64_t w0 = f0 + (int64_t)warp * kSub, w1 = min(w0 + kSub, f1);
+      const T* sb = sm.ring + (size_t)slot * SE;
+      int64_t f = f0;
+      while (f < f1) {
+        const int64_t rend = (r + 1) * V;
+        const int64_t ge = min(f1, rend);
+        const int64_t lo = max(f, w0), hi = min(ge, w1);
+        if (lo < hi) {
+          const bool zero = sc == 0.f || !rb.live(r);
+          // [lo, hi): scalar head to a vector boundary, 16-byte body, scalar tail
+          const int64_t lov = (lo + kVec - 1) & ~int64_t(kVec - 1), hiv = min(hi, fv) & ~int64_t(kVec - 1);
+          auto scalar = [&](int64_t x) {
+            if (zero) {
+              store_elem(dst + x, 0.f);
+            } else {
+              const float v = x < fv ? to_f32(sb[x - f0]) : ldg_f32(X + x);
+              store_elem(dst + x, sc * (exp_shift(v, l) - (x == tf ? 1.f : 0.f)));
+            }
+          };
+          if (lov < hiv) {
+            for (int64_t x = lo + lane; x < lov; x += 32) scalar(x);
+            for (int64_t x = hiv + lane; x < hi; x += 32) scalar(x);
+            const int nv = (int)((hiv - lov) / kVec);
+            if (zero) {
+              const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+              uint4* d4 = reinterpret_cast<uint4*>(dst + lov);
+              for (int k = lane; k < nv; k += 32) st_stream_u4(d4 + k, z);
+            } else if constexpr (sizeof(T) == 4) {
+              float4* d4 = reinterpret_cast<float4*>(dst + lov);
+              const float4* s4 = reinterpret_cast<const float4*>(sb + (lov - f0));
+              const int64_t tq = tf - lov;
+              for (int k = lane; k < nv; k += 32) {
+                const float4 v = s4[k];
+                float4 y;
+                y.x = exp_shift(v.x, l);
+                y.y = exp_shift(v.y, l);
+                y.z = exp_shift(v.z, l);
+                y.w = exp_shift(v.w, l);
+                const uint64_t d = (uint64_t)(tq - 4 * (int64_t)k);
+                if (d < 4) {
+                  if (d == 0) y.x -= 1.f;
+                  else if (d == 1) y.y -= 1.f;
+                  else if (d == 2) y.z -= 1.f;
+                  else y.w -= 1.f;
+                }
+                y.x *= sc;
+                y.y *= sc;
+                y.z *= sc;
+                y.w *= sc;
+                st_stream(d4 + k, y);
+              }
+            } else {
+              uint4* d4 = reinterpret_cast<uint4*>(dst + lov);
+              const uint4* s4 = reinterpret_cast<const uint4*>(sb + (lov - f0));
+              const int64_t tq = tf - lov;
+              const float2 sc2 = make_float2(sc, sc);
+              for (int k = lane; k < nv; k += 32) {
+                const uint4 v = s4[k];
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+                float2 e[4], y[4];
+  #pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                  e[h] = exp_shift2(bf16x2_f32(w[h]), l);
+                  y[h] = fmul2(e[h], sc2);
+                }
+                const uint64_t d = (uint64_t)(tq - 8 * (int64_t)k);
+                if (d < 8) {  // the target: sc * (p - 1), as the float kernel
+  #pragma unroll
+                  for (int h = 0; h < 4; ++h) {
+                    if (d == (uint64_t)(2 * h)) y[h].x = sc * (e[h].x - 1.f);
+                    if (d == (uint64_t)(2 * h + 1)) y[h].y = sc * (e[h].y - 1.f);
+                  }
+                }
+                st_stream_u4(d4 + k, make_uint4(pack_bf16x2(y[0].x, y[0].y), pack_bf16x2(y[1].x, y[1].y),
+                                                pack_bf16x2(y[2].x, y[2].y), pack_bf16x2(y[3].x, y[3].y)));
+              }
+            }
+          } else {
+            for (int64_t x = lo + lane; x < hi; x += 32) scalar(x);
+          }
+        }
+        f = ge;
+        if (ge == rend && ge < E) {
+          ++r;
+          load_row(r);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sm.empty + slot);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(sm.empty + slot);
+    if (lane == 0) sm.trk.done[warp] = it;
   }
+  __syncthreads();
+  if (sm.trk.timeout) ring_poison<T, S>(dst, E, BL, q.nblocks, sm.trk, NC);
+  if (threadIdx.x == 0) bwd_finish(q, a, sm.trk.timeout != 0);
 }
 
 template <class T, int NC, int S, int SE, int BS>
@@ -430,6 +450,9 @@ struct RingVariant {
   static cudaError_t bwd(const DpaceBwdArgs& a, int ctas, cudaStream_t st) {
     const cudaError_t e = ensure_smem_limit<dpace_bwd_ring_kernel<T, NC, S, SE, BS>>(smem());
     if (e != cudaSuccess) return e;
+    // chained only behind this library's own finalize (forward_backward)
+    if (a.chained)
+      return launch_pdl(dpace_bwd_ring_kernel<T, NC, S, SE, BS>, dim3(ctas), dim3((NC + 1) * 32), smem(), st, a);
     dpace_bwd_ring_kernel<T, NC, S, SE, BS><<<ctas, (NC + 1) * 32, smem(), st>>>(a);
     return cudaGetLastError();
   }

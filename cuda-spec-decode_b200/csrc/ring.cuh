@@ -29,11 +29,11 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
 }
 
 // Global block queue: `ctr` hands out block indices; each CTA's producer stops
-// after its first index >= nblocks and then retires; the last CTA to retire
-// resets both words, leaving the counters zeroed for the next launch.
+// after its first index >= nblocks. Every CTA then retires once; the last CTA
+// to retire resets both words, leaving the counters zeroed for the next launch.
 struct BlockQueue {
-  unsigned* ctr;
-  unsigned* retired;
+  unsigned* ctr;      // dynamic queue word (unused by the static interleave)
+  unsigned* retired;  // CTAs retired; null: no counters at all (nothing to retire)
   unsigned nblocks;
   int dynamic;  // 0: block = blockIdx.x + k * gridDim.x (static interleave)
 
@@ -41,14 +41,33 @@ struct BlockQueue {
   __device__ __forceinline__ unsigned next(unsigned cur) const {
     return dynamic ? atomicAdd(ctr, 1u) : cur + gridDim.x;
   }
-  __device__ __forceinline__ void retire() const {
-    if (!dynamic) return;
+  // Called once per CTA, after its last dequeue; true for the last CTA, which
+  // has seen every earlier CTA's writes that preceded their retire.
+  __device__ __forceinline__ bool retire() const {
+    if (retired == nullptr) return false;
     __threadfence();
     if (atomicAdd(retired, 1u) + 1 == gridDim.x) {
-      *ctr = 0u;
+      __threadfence();
+      if (dynamic) *ctr = 0u;
       *retired = 0u;
+      return true;
     }
+    return false;
   }
+};
+
+// What a CTA may have left unfinished when one of its waits expired: the
+// producer records the block of every stage it posts, the blocks it had
+// dequeued but not yet fully posted and the stage count; each consumer warp
+// records how many stages it finished. Read only after a timeout (the
+// backward kernels then overwrite those blocks of the gradient with NaN).
+template <int S>
+struct RingTrack {
+  unsigned sblk[S];   // block of the stage last posted in each slot
+  unsigned held[2];   // dequeued, not fully posted (>= nblocks: none)
+  int64_t posted;     // stages posted (or withheld), the end-of-work stage included
+  int64_t done[8];    // per consumer warp: stages finished
+  int timeout;        // a wait in this CTA expired
 };
 
 // Number of blocks of length BL that overlap row r (= slots of its partials).
@@ -117,11 +136,13 @@ __device__ __forceinline__ int64_t copied_end(int64_t f0, int64_t f1) {
 // ring + k*S*SE). A stage whose rows are all dead is posted without a copy.
 // Returns false on a wait timeout. `withhold_first` (failure-detection tests
 // only) never posts the first stage: this CTA's consumers then see their
-// bounded wait expire, which is the path under test.
+// bounded wait expire, which is the path under test. `trk` (or null) receives
+// the progress record. The caller retires the CTA from the queue afterwards.
 template <int NIN, int S, int SE, int BS, class T>
 __device__ bool ring_produce(const T* const* src, int64_t E, int64_t V, const RowBits& rb,
                              const BlockQueue& q, T* ring, uint64_t* full, uint64_t* empty,
-                             int64_t* sf0, int64_t* srow, bool withhold_first = false) {
+                             int64_t* sf0, int64_t* srow, bool withhold_first = false,
+                             RingTrack<S>* trk = nullptr) {
   constexpr int64_t BL = (int64_t)BS * SE;
   unsigned b = q.first();
   unsigned nb = b < q.nblocks ? q.next(b) : q.nblocks;
@@ -132,16 +153,19 @@ __device__ bool ring_produce(const T* const* src, int64_t E, int64_t V, const Ro
     r_issue = ((int64_t)b * BL) / V;
   }
   bool ok = true;
-  for (int64_t it = 0;; ++it) {
+  int64_t it = 0;
+  for (;; ++it) {
     const int slot = (int)(it % S);
     if (!mbar_wait(empty + slot, (uint32_t)(((it / S) & 1) ^ 1))) {
       ok = false;
       break;
     }
+    if (trk) trk->sblk[slot] = b;
     if (withhold_first && it == 0) continue;  // neither copy nor arrive: full[0] stays incomplete
     if (b >= q.nblocks) {
       sf0[slot] = -1;
       mbar_arrive(full + slot);
+      ++it;
       break;
     }
     const int64_t f0 = (int64_t)b * BL + (int64_t)k * SE;
@@ -172,7 +196,11 @@ __device__ bool ring_produce(const T* const* src, int64_t E, int64_t V, const Ro
       ++k;
     }
   }
-  q.retire();
+  if (trk) {
+    trk->held[0] = b;
+    trk->held[1] = nb;
+    trk->posted = it;
+  }
   return ok;
 }
 
@@ -191,6 +219,7 @@ struct RingSmem {
   uint64_t full[S], empty[S];
   int64_t sf0[S];   // flattened start of the stage (-1: end of work)
   int64_t srow[S];  // row containing the stage's first element
+  RingTrack<S> trk;
   unsigned bits[kMaxRowWords];
 };
 
@@ -212,7 +241,34 @@ __device__ __forceinline__ void ring_init(RingSmem<NIN, S, SE, T>& sm, int consu
       mbar_init(sm.full + i, 1);
       mbar_init(sm.empty + i, consumers);
     }
+    sm.trk.timeout = 0;
     fence_mbar_init();
+  }
+}
+
+// After a wait in this CTA expired (all threads, after a CTA-wide barrier):
+// overwrites with NaN every block of dst that this CTA may have left
+// unfinished -- the blocks of the stages some consumer warp had not finished
+// (at most S stages: the producer never runs more than S ahead of the slowest
+// consumer) and the blocks the producer had dequeued but not fully posted.
+// Blocks this CTA finished are left as written, so a gradient is never
+// partly stale: every element is either correct or NaN.
+template <class T, int S>
+__device__ void ring_poison(T* dst, int64_t E, int64_t BL, unsigned nblocks, const RingTrack<S>& trk, int nc) {
+  int64_t lo = trk.done[0];
+  for (int w = 1; w < nc; ++w) lo = min(lo, trk.done[w]);
+  unsigned ids[S + 2];
+  int n = 0;
+  for (int64_t st = max(lo, trk.posted - S); st < trk.posted; ++st) ids[n++] = trk.sblk[st % S];
+  ids[n++] = trk.held[0];
+  ids[n++] = trk.held[1];
+  for (int i = 0; i < n; ++i) {
+    const unsigned b = ids[i];
+    bool seen = b >= nblocks;
+    for (int j = 0; j < i; ++j) seen = seen || ids[j] == b;
+    if (seen) continue;
+    const int64_t f0 = (int64_t)b * BL, f1 = min(f0 + BL, E);
+    for (int64_t x = f0 + threadIdx.x; x < f1; x += blockDim.x) store_elem(dst + x, __int_as_float(0x7fc00000));
   }
 }
 
@@ -348,6 +404,26 @@ __device__ __forceinline__ void warp_lse_full(const bf16_t* sb, float& m, float&
 #pragma unroll
     for (int u = 0; u + w < U; u += 2 * w) acc[u] = fadd2(acc[u], acc[u + w]);
   s += acc[0].x + acc[0].y;
+}
+
+// End of a backward CTA (thread 0, after its poison writes, if any): folds
+// this CTA's timeout into the launch's flag word and retires it; the last CTA
+// to retire turns the flag into the status word (SPECDEC_ERR_CUDA = a wait
+// expired somewhere; otherwise 0 unless `status_merge`, which only ever
+// raises the word) and clears the flag. Without counters (no retire count) a
+// timed-out CTA writes the status itself, over the 0 the entry point stored.
+template <class Args>
+__device__ __forceinline__ void bwd_finish(const BlockQueue& q, const Args& a, bool timeout) {
+  if (timeout && a.flag) atomicOr(a.flag, 2);
+  if (q.retire()) {
+    const int f = a.flag ? atomicExch(a.flag, 0) : 0;
+    if (a.status) {
+      if (f & 2) a.status[0] = kStatusTimeout;
+      else if (!a.status_merge) a.status[0] = 0;
+    }
+  } else if (q.retired == nullptr && timeout && a.status) {
+    a.status[0] = kStatusTimeout;
+  }
 }
 
 // Launches a kernel chained to the previous kernel on the stream with

@@ -125,16 +125,20 @@ int kernel_units(int kernel, int kind, bool tma, int device, int dtype = kDtypeF
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // ---- D-PACE workspace layout ----------------------------------------------
-// counters: [done][flag][queue ctr][queue retired] [seq_cnt u32 x N]
+// counters: [done][flag][queue ctr][queue retired]
+//           [backward queue ctr][backward retired][backward flag][-]  (forward_backward)
+//           [seq_cnt u32 x N]
 // scratch:  [part float2 x R*pmax*nc][xtgt f32 x R][seq_loss f32 x N]
 struct DpaceLayout {
   size_t part = 0, xtgt = 0, seq_loss = 0, scratch = 0, counters = 0;
 };
 
-// [done][flag][queue ctr][queue retired][seq_cnt x N]
+constexpr int kDpaceBwdWords = 4;  // word offset of the backward's three counter words
+constexpr int kDpaceSeqWords = 8;  // word offset of seq_cnt
+
 size_t dpace_counter_bytes(int64_t N, int64_t B) {
   (void)B;
-  return align256(16 + size_t(N) * sizeof(unsigned));
+  return align256(kDpaceSeqWords * sizeof(unsigned) + size_t(N) * sizeof(unsigned));
 }
 
 DpaceLayout dpace_layout(int64_t N, int64_t B, const Partition& pt, int nc) {
@@ -212,6 +216,29 @@ int take_withhold_stage() {
 
 namespace specdec {
 void set_last_error(const char* msg) { g_last_error = msg; }
+
+// The checks of specdec_dpace_forward that need no workspace, in the order of
+// losses/dpace.py:157-173 (_check); SPECDEC_OK with nothing to launch when N == 0.
+int dpace_forward_check(int dtype, const void* logits, const int64_t* targets, int64_t N, int32_t B, int64_t V,
+                        float alpha, int32_t loss_type, int64_t n_global, const float* loss, const float* lse,
+                        const float* scale) {
+  if (B < 1 || B > 32) return fail(SPECDEC_ERR_ARGUMENT, "kernel configured for block_size <= 32 (B=%d)", B);
+  if (N < 0 || V < 0) return fail(SPECDEC_ERR_ARGUMENT, "negative shape N=%lld V=%lld", (long long)N, (long long)V);
+  if (!(alpha >= 0.f && alpha <= 1.f))
+    return fail(SPECDEC_ERR_VALUE, "dpace_alpha must be in [0, 1], got %g", (double)alpha);
+  if (loss_type < 0 || loss_type > 2) return fail(SPECDEC_ERR_VALUE, "unknown loss_type %d", loss_type);
+  if (N > 0 && (n_global < N || n_global < 1))
+    return fail(SPECDEC_ERR_ARGUMENT, "n_global (%lld) must be >= N (%lld)", (long long)n_global, (long long)N);
+  if (!loss) return fail(SPECDEC_ERR_ARGUMENT, "loss output is null");
+  if (N == 0) return ok();
+  if (V == 0) return fail(SPECDEC_ERR_TARGET_RANGE, "targets out of range [0, 0)");
+  if (!logits || !targets || !lse || !scale) return fail(SPECDEC_ERR_ARGUMENT, "null input or output pointer");
+  if (!aligned(logits, 4) || !aligned(targets, 8) || !aligned(lse, 4) || !aligned(scale, 4))
+    return fail(SPECDEC_ERR_ARGUMENT, "misaligned input or output pointer");
+  if (dtype == kDtypeBF16 && !aligned(logits, 16))
+    return fail(SPECDEC_ERR_ARGUMENT, "bf16 logits must be 16-byte aligned");
+  return ok();
+}
 }  // namespace specdec
 
 extern "C" {
@@ -296,16 +323,9 @@ int dpace_forward_impl(int dtype, const void* logits, const int64_t* targets, co
                        int32_t B, int64_t V, float alpha, int32_t loss_type, int64_t n_global, float* loss,
                        float* loss_n, float* lse, float* scale, int32_t* status, void* scratch,
                        size_t scratch_bytes, void* counters, size_t counter_bytes, void* stream) {
-  // Mirrors losses/dpace.py:157-173 (_check) order of failures.
-  if (B < 1 || B > 32) return fail(SPECDEC_ERR_ARGUMENT, "kernel configured for block_size <= 32 (B=%d)", B);
-  if (N < 0 || V < 0) return fail(SPECDEC_ERR_ARGUMENT, "negative shape N=%lld V=%lld", (long long)N, (long long)V);
-  if (!(alpha >= 0.f && alpha <= 1.f))
-    return fail(SPECDEC_ERR_VALUE, "dpace_alpha must be in [0, 1], got %g", (double)alpha);
-  if (loss_type < 0 || loss_type > 2) return fail(SPECDEC_ERR_VALUE, "unknown loss_type %d", loss_type);
-  if (n_global < N || n_global < 1) {
-    if (N > 0) return fail(SPECDEC_ERR_ARGUMENT, "n_global (%lld) must be >= N (%lld)", (long long)n_global, (long long)N);
-  }
-  if (!loss) return fail(SPECDEC_ERR_ARGUMENT, "loss output is null");
+  const int rc = specdec::dpace_forward_check(dtype, logits, targets, N, B, V, alpha, loss_type, n_global, loss,
+                                              lse, scale);
+  if (rc != SPECDEC_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (N == 0) {
     // mean over an empty batch: NaN, as torch's mean of an empty tensor
@@ -313,14 +333,9 @@ int dpace_forward_impl(int dtype, const void* logits, const int64_t* targets, co
     if (e == cudaSuccess && status) e = cudaMemsetAsync(status, 0, sizeof(int32_t), st);
     return e == cudaSuccess ? ok() : cuda_fail(e, "cudaMemsetAsync");
   }
-  if (V == 0) return fail(SPECDEC_ERR_TARGET_RANGE, "targets out of range [0, 0)");
-  if (!logits || !targets || !lse || !scale || !scratch || !counters)
-    return fail(SPECDEC_ERR_ARGUMENT, "null input, output or workspace pointer");
-  if (!aligned(logits, 4) || !aligned(targets, 8) || !aligned(lse, 4) || !aligned(scale, 4) ||
-      !aligned(scratch, 256) || !aligned(counters, 16))
-    return fail(SPECDEC_ERR_ARGUMENT, "misaligned pointer (scratch needs 256 B, counters 16 B)");
-  if (dtype == kDtypeBF16 && !aligned(logits, 16))
-    return fail(SPECDEC_ERR_ARGUMENT, "bf16 logits must be 16-byte aligned");
+  if (!scratch || !counters) return fail(SPECDEC_ERR_ARGUMENT, "null workspace pointer");
+  if (!aligned(scratch, 256) || !aligned(counters, 16))
+    return fail(SPECDEC_ERR_ARGUMENT, "misaligned workspace (scratch needs 256 B, counters 16 B)");
   const int dev = current_device();
   if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
   const bool tma = dtype == kDtypeBF16 || use_tma(SPECDEC_KERNEL_DPACE_FWD, aligned(logits, 16));
@@ -362,7 +377,7 @@ int dpace_forward_impl(int dtype, const void* logits, const int64_t* targets, co
   a.q_ctr = cnt + 2;
   a.q_retired = cnt + 3;
   a.q_dynamic = g_static_queue.load() ? 0 : 1;
-  a.seq_cnt = cnt + 4;
+  a.seq_cnt = cnt + kDpaceSeqWords;
   a.withhold_stage = tma ? take_withhold_stage() : 0;
   a.pt = pt;
   const cudaError_t e =
@@ -370,12 +385,23 @@ int dpace_forward_impl(int dtype, const void* logits, const int64_t* targets, co
   return e == cudaSuccess ? ok() : cuda_fail(e, "dpace forward launch");
 }
 
+// The backward's counter block (specdec_backward_counter_bytes):
+// [queue ctr][retired][flag]. `chained`: launched with programmatic dependent
+// launch behind this library's own finalize, with row liveness from `mask`.
 int dpace_backward_impl(int dtype, const void* logits, const int64_t* targets, const float* lse,
                         const float* scale, const float* dloss, void* dlogits, int64_t N, int32_t B, int64_t V,
-                        void* counters, size_t counter_bytes, void* stream) {
+                        int32_t* status, void* counters, size_t counter_bytes, void* stream,
+                        bool status_merge = false, bool chained = false, const float* mask = nullptr) {
   if (B < 1 || B > 32) return fail(SPECDEC_ERR_ARGUMENT, "kernel configured for block_size <= 32 (B=%d)", B);
   if (N < 0 || V < 0) return fail(SPECDEC_ERR_ARGUMENT, "negative shape");
-  if (N == 0 || V == 0) return ok();
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (N == 0 || V == 0) {
+    if (status && !status_merge) {
+      const cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int32_t), st);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+    }
+    return ok();
+  }
   if (!logits || !targets || !lse || !scale || !dlogits)
     return fail(SPECDEC_ERR_ARGUMENT, "null input or output pointer");
   if (logits == dlogits) return fail(SPECDEC_ERR_ARGUMENT, "dlogits must not alias logits");
@@ -387,6 +413,13 @@ int dpace_backward_impl(int dtype, const void* logits, const int64_t* targets, c
       dtype == kDtypeBF16 || use_tma(SPECDEC_KERNEL_DPACE_BWD, aligned(logits, 16) && aligned(dlogits, 16));
   const int units = kernel_units(SPECDEC_KERNEL_DPACE_BWD, 0, tma, dev, dtype);
   if (units <= 0) return fail(SPECDEC_ERR_CUDA, "occupancy query failed");
+  const bool have_cnt = tma && counters != nullptr && counter_bytes >= 16 && aligned(counters, 16);
+  // the 128-bit-load kernels have no waits; without a retire count the ring
+  // kernel's CTAs only ever raise the word: start it at 0 on the stream
+  if (status && !status_merge && !have_cnt) {
+    const cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int32_t), st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+  }
   DpaceBwdArgs a;
   a.logits = logits;
   a.targets = targets;
@@ -394,17 +427,20 @@ int dpace_backward_impl(int dtype, const void* logits, const int64_t* targets, c
   a.scale = scale;
   a.dloss = dloss;
   a.dlogits = dlogits;
-  a.flag = nullptr;
-  const bool queue = counters != nullptr && counter_bytes >= 16 && aligned(counters, 16) &&
-                     !g_static_queue.load();
   unsigned* cnt = static_cast<unsigned*>(counters);
-  a.q_ctr = queue ? cnt : nullptr;
-  a.q_retired = queue ? cnt + 1 : nullptr;
-  a.q_dynamic = queue ? 1 : 0;
+  a.q_ctr = have_cnt ? cnt : nullptr;
+  a.q_retired = have_cnt ? cnt + 1 : nullptr;
+  a.flag = have_cnt ? reinterpret_cast<int*>(cnt + 2) : nullptr;
+  a.q_dynamic = have_cnt && !g_static_queue.load() ? 1 : 0;
+  a.status = tma ? status : nullptr;
+  a.status_merge = status_merge ? 1 : 0;
+  a.chained = chained && tma ? 1 : 0;
+  a.mask_liveness = a.chained;
+  a.live_mask = mask;
+  a.withhold_stage = tma ? take_withhold_stage() : 0;
   const int shape = tma ? ring_shape(SPECDEC_KERNEL_DPACE_BWD, dtype) : kernel_shape(SPECDEC_KERNEL_DPACE_BWD, false);
   a.pt = tma ? ring_partition(N * B, V, dpace_ring_block_elems(dtype, shape), units)
              : make_partition(N * B, V, units, kMinChunk);
-  const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const cudaError_t e =
       tma ? dpace_bwd_ring_launch(dtype, shape, a, units, st) : dpace_bwd_launch(shape, a, st);
   return e == cudaSuccess ? ok() : cuda_fail(e, "dpace backward launch");
@@ -441,7 +477,15 @@ int dpace_forward_backward_impl(int dtype, const void* logits, const int64_t* ta
   const int rc = dpace_forward_impl(dtype, logits, targets, mask, N, B, V, alpha, loss_type, n_global, loss, loss_n,
                                     lse, scale, status, scratch, scratch_bytes, counters, counter_bytes, stream);
   if (rc != SPECDEC_OK) return rc;
-  return dpace_backward_impl(dtype, logits, targets, lse, scale, nullptr, dlogits, N, B, V, nullptr, 0, stream);
+  // The backward follows the finalize this call just enqueued, so it is
+  // chained to it (programmatic dependent launch): its CTAs become resident
+  // and start streaming logits -- rows chosen by the mask -- while the
+  // finalize runs, and wait for lse / scale before computing. It uses its own
+  // words of the counter block; its status only ever raises the forward's.
+  unsigned* bcnt = static_cast<unsigned*>(counters) + kDpaceBwdWords;
+  return dpace_backward_impl(dtype, logits, targets, lse, scale, nullptr, dlogits, N, B, V, status, bcnt,
+                             counter_bytes - kDpaceBwdWords * sizeof(unsigned), stream, /*status_merge=*/true,
+                             /*chained=*/true, mask);
 }
 
 }  // namespace
@@ -516,17 +560,17 @@ int specdec_dpace_forward_bf16(const uint16_t* logits, const int64_t* targets, c
 
 int specdec_dpace_backward(const float* logits, const int64_t* targets, const float* lse,
                            const float* scale, const float* dloss, float* dlogits, int64_t N,
-                           int32_t B, int64_t V, void* counters, size_t counter_bytes,
+                           int32_t B, int64_t V, int32_t* status, void* counters, size_t counter_bytes,
                            void* stream) {
-  return dpace_backward_impl(kDtypeF32, logits, targets, lse, scale, dloss, dlogits, N, B, V, counters,
+  return dpace_backward_impl(kDtypeF32, logits, targets, lse, scale, dloss, dlogits, N, B, V, status, counters,
                              counter_bytes, stream);
 }
 
 int specdec_dpace_backward_bf16(const uint16_t* logits, const int64_t* targets, const float* lse,
                                 const float* scale, const float* dloss, uint16_t* dlogits, int64_t N,
-                                int32_t B, int64_t V, void* counters, size_t counter_bytes,
+                                int32_t B, int64_t V, int32_t* status, void* counters, size_t counter_bytes,
                                 void* stream) {
-  return dpace_backward_impl(kDtypeBF16, logits, targets, lse, scale, dloss, dlogits, N, B, V, counters,
+  return dpace_backward_impl(kDtypeBF16, logits, targets, lse, scale, dloss, dlogits, N, B, V, status, counters,
                              counter_bytes, stream);
 }
 
@@ -641,12 +685,19 @@ int dflash_forward_impl(int dtype, const void* logits, const void* target_logits
 
 int dflash_backward_impl(int dtype, const void* logits, const void* target_logits, const float* scale,
                          const float* logzq, const float* logzp, const int64_t* target_id, const float* dloss,
-                         void* dlogits, int64_t N, int32_t B, int64_t V, int32_t kind, void* counters,
-                         size_t counter_bytes, void* stream) {
+                         void* dlogits, int64_t N, int32_t B, int64_t V, int32_t kind, int32_t* status,
+                         void* counters, size_t counter_bytes, void* stream) {
   if (N < 0 || B < 0 || V < 0) return fail(SPECDEC_ERR_ARGUMENT, "negative shape");
   if (kind != SPECDEC_DFLASH_KL && kind != SPECDEC_DFLASH_CE)
     return fail(SPECDEC_ERR_VALUE, "unknown loss kind %d", kind);
-  if (N == 0 || B == 0 || V == 0) return ok();
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (N == 0 || B == 0 || V == 0) {
+    if (status) {
+      const cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int32_t), st);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+    }
+    return ok();
+  }
   if (!logits || !scale || !logzq || !logzp || !dlogits)
     return fail(SPECDEC_ERR_ARGUMENT, "null input or output pointer");
   if (kind == SPECDEC_DFLASH_KL && !target_logits) return fail(SPECDEC_ERR_ARGUMENT, "KL needs target_logits");
@@ -662,6 +713,11 @@ int dflash_backward_impl(int dtype, const void* logits, const void* target_logit
   const bool tma = dtype == kDtypeBF16 || use_tma(SPECDEC_KERNEL_DFLASH_BWD, ptrs16);
   const int ctas = kernel_units(SPECDEC_KERNEL_DFLASH_BWD, kind, tma, dev, dtype);
   if (ctas <= 0) return fail(SPECDEC_ERR_CUDA, "occupancy query failed");
+  const bool have_cnt = tma && counters != nullptr && counter_bytes >= 16 && aligned(counters, 16);
+  if (status && !have_cnt) {
+    const cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int32_t), st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+  }
   DflashBwdArgs a;
   a.logits = logits;
   a.target_logits = target_logits;
@@ -672,18 +728,18 @@ int dflash_backward_impl(int dtype, const void* logits, const void* target_logit
   a.dloss = dloss;
   a.dlogits = dlogits;
   a.kind = kind;
-  a.flag = nullptr;
-  const bool queue = counters != nullptr && counter_bytes >= 16 && aligned(counters, 16) &&
-                     !g_static_queue.load();
   unsigned* cnt = static_cast<unsigned*>(counters);
-  a.q_ctr = queue ? cnt : nullptr;
-  a.q_retired = queue ? cnt + 1 : nullptr;
-  a.q_dynamic = queue ? 1 : 0;
+  a.q_ctr = have_cnt ? cnt : nullptr;
+  a.q_retired = have_cnt ? cnt + 1 : nullptr;
+  a.flag = have_cnt ? reinterpret_cast<int*>(cnt + 2) : nullptr;
+  a.q_dynamic = have_cnt && !g_static_queue.load() ? 1 : 0;
+  a.status = tma ? status : nullptr;
+  a.status_merge = 0;
+  a.withhold_stage = tma ? take_withhold_stage() : 0;
   const int shape =
       tma ? ring_shape(SPECDEC_KERNEL_DFLASH_BWD, dtype) : kernel_shape(SPECDEC_KERNEL_DFLASH_BWD, false);
   a.pt = tma ? ring_partition(N * B, V, dflash_ring_block_elems(dtype, shape), ctas)
              : make_partition(N * B, V, ctas, kMinChunk);
-  const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const cudaError_t e =
       tma ? dflash_bwd_ring_launch(dtype, shape, a, ctas, st) : dflash_bwd_launch(shape, a, st);
   return e == cudaSuccess ? ok() : cuda_fail(e, "dflash backward launch");
@@ -718,17 +774,18 @@ int specdec_dflash_forward_bf16(const uint16_t* logits, const uint16_t* target_l
 int specdec_dflash_backward(const float* logits, const float* target_logits, const float* scale,
                             const float* logzq, const float* logzp, const int64_t* target_id,
                             const float* dloss, float* dlogits, int64_t N, int32_t B, int64_t V,
-                            int32_t kind, void* counters, size_t counter_bytes, void* stream) {
+                            int32_t kind, int32_t* status, void* counters, size_t counter_bytes, void* stream) {
   return dflash_backward_impl(kDtypeF32, logits, target_logits, scale, logzq, logzp, target_id, dloss, dlogits,
-                              N, B, V, kind, counters, counter_bytes, stream);
+                              N, B, V, kind, status, counters, counter_bytes, stream);
 }
 
 int specdec_dflash_backward_bf16(const uint16_t* logits, const uint16_t* target_logits, const float* scale,
                                  const float* logzq, const float* logzp, const int64_t* target_id,
                                  const float* dloss, uint16_t* dlogits, int64_t N, int32_t B, int64_t V,
-                                 int32_t kind, void* counters, size_t counter_bytes, void* stream) {
+                                 int32_t kind, int32_t* status, void* counters, size_t counter_bytes,
+                                 void* stream) {
   return dflash_backward_impl(kDtypeBF16, logits, target_logits, scale, logzq, logzp, target_id, dloss,
-                              dlogits, N, B, V, kind, counters, counter_bytes, stream);
+                              dlogits, N, B, V, kind, status, counters, counter_bytes, stream);
 }
 
 }  // extern "C"

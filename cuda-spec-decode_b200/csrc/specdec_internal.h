@@ -64,10 +64,16 @@ struct DpaceBwdArgs {
   const float* scale;
   const float* dloss;      // [1] upstream gradient, or null for 1
   void* dlogits;           // element type of logits
-  int* flag;               // [1] or null: bit 2 set if a copy wait timed out
-  unsigned* q_ctr;         // ring kernel block queue (null: static interleave)
-  unsigned* q_retired;
+  int* status;             // [1] or null: 0, or kStatusTimeout if a wait expired
+  int status_merge;        // 1: only ever raise *status (it holds the forward's word)
+  int* flag;               // [1] or null (no counters): bit 2 set if a copy wait timed out
+  unsigned* q_ctr;         // ring kernel block queue word
+  unsigned* q_retired;     // null: no counters (static interleave, no retire count)
   int q_dynamic;
+  int mask_liveness;       // 1: rows are read iff live_mask > 0 (null: all), known before lse/scale
+  const float* live_mask;  // [N, B] position mask, with mask_liveness
+  int chained;             // 1: launched with programmatic dependent launch after the finalize
+  int withhold_stage;      // failure-detection tests: CTA 0 never posts its first stage
   Partition pt;
 };
 
@@ -114,10 +120,13 @@ struct DflashBwdArgs {
   const float* dloss;
   void* dlogits;               // element type of logits
   int kind;
-  int* flag;                   // [1] or null
-  unsigned* q_ctr;             // ring kernel block queue (null: static interleave)
-  unsigned* q_retired;
+  int* status;                 // [1] or null: 0, or kStatusTimeout if a wait expired
+  int status_merge;            // 1: only ever raise *status
+  int* flag;                   // [1] or null (no counters)
+  unsigned* q_ctr;             // ring kernel block queue word
+  unsigned* q_retired;         // null: no counters (static interleave, no retire count)
   int q_dynamic;
+  int withhold_stage;          // failure-detection tests: CTA 0 never posts its first stage
   Partition pt;
 };
 
@@ -151,6 +160,12 @@ cudaError_t scale_inplace_launch(int dtype, void* x, int64_t n, const float* fac
 
 // Sets the calling thread's specdec_last_error() text.
 void set_last_error(const char* msg);
+
+// specdec_dpace_forward's checks that need no workspace (status code; sets
+// the error text).
+int dpace_forward_check(int dtype, const void* logits, const int64_t* targets, int64_t N, int32_t B, int64_t V,
+                        float alpha, int32_t loss_type, int64_t n_global, const float* loss, const float* lse,
+                        const float* scale);
 
 int dflash_fwd_ctas(int kind, int shape, int device, int cap_per_sm);
 int dflash_bwd_ctas(int kind, int shape, int device, int cap_per_sm);

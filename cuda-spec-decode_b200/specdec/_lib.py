@@ -51,15 +51,15 @@ _SIGNATURES = {
         _c_p, _c_p, _c_p, _c_p, _c_p, _c_p]),
     "specdec_backward_counter_bytes": (_c_sz, []),
     "specdec_dpace_backward": (ctypes.c_int, [
-        _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_p, _c_sz, _c_p]),
+        _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_p, _c_p, _c_sz, _c_p]),
     "specdec_dflash_scratch_bytes": (_c_sz, [_c_i64, _c_i32, _c_i64, ctypes.c_int]),
     "specdec_dflash_counter_bytes": (_c_sz, [_c_i64, _c_i32]),
     "specdec_dflash_forward": (ctypes.c_int, [
         _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_i32, _c_f32, _c_i32, _c_i32, _c_i64,
         _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_sz, _c_p, _c_sz, _c_p]),
     "specdec_dflash_backward": (ctypes.c_int, [
-        _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_i32, _c_p, _c_sz,
-        _c_p]),
+        _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_i32, _c_p, _c_p,
+        _c_sz, _c_p]),
     "specdec_set_launch_shape": (ctypes.c_int, [_c_i32, _c_i32, _c_i32]),
     "specdec_launch_ctas": (_c_i64, [_c_i32, _c_i64, _c_i64, ctypes.c_int]),
     "specdec_set_block_queue": (ctypes.c_int, [_c_i32]),
@@ -170,3 +170,20 @@ def workspace(family: str, device: torch.device) -> Workspace:
     if ws is None:
         ws = _workspaces[key] = Workspace()
     return ws
+
+
+# Device status words per (device, stream), written by the kernels:
+STATUS_DPACE_FWD = 0   # the D-PACE forward (and forward_backward): 0, ERR_TARGET_RANGE or ERR_CUDA
+STATUS_DPACE_BWD = 1   # the last D-PACE backward: 0 or ERR_CUDA
+STATUS_DFLASH_BWD = 2  # the last DFlash backward: 0 or ERR_CUDA
+_status: dict = {}
+
+
+def status_words(device: torch.device) -> torch.Tensor:
+    """int32[4] on `device` for the current stream, zero-initialised once; the
+    entry points write their status word into it on the device."""
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    t = _status.get(key)
+    if t is None:
+        t = _status[key] = torch.zeros(4, dtype=torch.int32, device=device)
+    return t

@@ -60,6 +60,42 @@ def _aligned(t: torch.Tensor | None) -> torch.Tensor | None:
     return t.clone()
 
 
+_BWD_TIMEOUT_MSG = ("an earlier backward launch on this stream had a bounded wait expire; the blocks of "
+                    "its gradient that the failed part left unfinished hold NaN")
+
+
+def _read_status(dev: torch.device, what: str, V: int) -> None:
+    """One device-to-host read of this stream's status words, after a D-PACE
+    forward: raises ValueError for an out-of-range target (the reference's
+    check), RuntimeError for an expired wait in this forward or in an earlier
+    backward on the stream (reported here, at the next synchronising call, so
+    that the autograd backward itself never synchronises)."""
+    words = _lib.status_words(dev)
+    st = words[:3].tolist()
+    if st[_lib.STATUS_DPACE_BWD] or st[_lib.STATUS_DFLASH_BWD]:
+        words[1:3].zero_()
+        raise RuntimeError(_BWD_TIMEOUT_MSG)
+    if st[_lib.STATUS_DPACE_FWD] == _lib.ERR_TARGET_RANGE:
+        raise ValueError(f"targets out of range [0, {V})")
+    if st[_lib.STATUS_DPACE_FWD] == _lib.ERR_CUDA:  # counters are in an unknown state
+        _lib.workspace("dpace", dev).reset_counters()
+        raise RuntimeError(f"{what}: a bulk-copy wait timed out")
+
+
+def check_backward(device: torch.device | int | None = None) -> None:
+    """Synchronise with the current stream of `device` and raise RuntimeError
+    if a D-PACE or DFlash backward launched on it since the last check had a
+    bounded wait expire (its gradient then holds NaN blocks). Every D-PACE
+    forward that validates its targets performs this check as well."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                       (device if isinstance(device, int) else device.index))
+    words = _lib.status_words(dev)
+    st = words[:3].tolist()
+    if st[_lib.STATUS_DPACE_BWD] or st[_lib.STATUS_DFLASH_BWD]:
+        words[1:3].zero_()
+        raise RuntimeError(_BWD_TIMEOUT_MSG)
+
+
 def _dpace_forward(logits: torch.Tensor, targets: torch.Tensor, mask: torch.Tensor | None,
                   alpha: float, loss_type: int, n_global: int | None = None,
                   want_loss_n: bool = False, validate: bool | None = None):
@@ -72,7 +108,7 @@ def _dpace_forward(logits: torch.Tensor, targets: torch.Tensor, mask: torch.Tens
     lse = torch.empty((N, B), dtype=torch.float32, device=dev)
     scale = torch.empty((N, B), dtype=torch.float32, device=dev)
     loss_n = torch.empty((N,), dtype=torch.float32, device=dev) if want_loss_n else None
-    status = torch.empty((1,), dtype=torch.int32, device=dev)
+    status = _lib.status_words(dev)[_lib.STATUS_DPACE_FWD:]
     ws = _lib.workspace("dpace", dev)
     sb = lib.specdec_dpace_scratch_bytes(N, B, V, dev.index)
     cb = lib.specdec_dpace_counter_bytes(N, B)
@@ -85,12 +121,7 @@ def _dpace_forward(logits: torch.Tensor, targets: torch.Tensor, mask: torch.Tens
         counters.data_ptr(), counters.numel(), _lib.stream_handle(dev))
     _lib.check(code, "specdec_dpace_forward")
     if (VALIDATE_TARGETS if validate is None else validate) and N * B > 0:
-        st = int(status.item())
-        if st == _lib.ERR_TARGET_RANGE:
-            raise ValueError(f"targets out of range [0, {V})")
-        if st == _lib.ERR_CUDA:  # a bounded copy wait expired: counters are in an unknown state
-            ws.reset_counters()
-            raise RuntimeError("specdec_dpace_forward: a bulk-copy wait timed out")
+        _read_status(dev, "specdec_dpace_forward", V)
     return loss, lse, scale, loss_n
 
 
@@ -111,7 +142,7 @@ def _dpace_forward_backward(logits: torch.Tensor, targets: torch.Tensor, mask: t
     scale = torch.empty((N, B), dtype=torch.float32, device=dev)
     loss_n = torch.empty((N,), dtype=torch.float32, device=dev) if want_loss_n else None
     dlogits = torch.empty_like(logits) if out is None else out
-    status = torch.empty((1,), dtype=torch.int32, device=dev)
+    status = _lib.status_words(dev)[_lib.STATUS_DPACE_FWD:]
     ws = _lib.workspace("dpace", dev)
     sb = lib.specdec_dpace_scratch_bytes(N, B, V, dev.index)
     cb = lib.specdec_dpace_counter_bytes(N, B)
@@ -123,12 +154,7 @@ def _dpace_forward_backward(logits: torch.Tensor, targets: torch.Tensor, mask: t
         counters.data_ptr(), counters.numel(), _lib.stream_handle(dev))
     _lib.check(code, "specdec_dpace_forward_backward")
     if (VALIDATE_TARGETS if validate is None else validate) and N * B > 0:
-        st = int(status.item())
-        if st == _lib.ERR_TARGET_RANGE:
-            raise ValueError(f"targets out of range [0, {V})")
-        if st == _lib.ERR_CUDA:
-            ws.reset_counters()
-            raise RuntimeError("specdec_dpace_forward_backward: a bulk-copy wait timed out")
+        _read_status(dev, "specdec_dpace_forward_backward", V)
     return loss, dlogits, lse, scale, loss_n
 
 
@@ -154,10 +180,11 @@ def _dpace_backward(logits: torch.Tensor, targets: torch.Tensor, lse: torch.Tens
         dloss = dloss.detach().to(device=dev, dtype=torch.float32).contiguous()
     cb = lib.specdec_backward_counter_bytes()
     _, counters = _lib.workspace("dpace_bwd", dev).ensure(dev, 256, cb)
+    status = _lib.status_words(dev)[_lib.STATUS_DPACE_BWD:]
     code = _entry(lib, "specdec_dpace_backward", logits)(
         logits.data_ptr(), targets.data_ptr(), lse.data_ptr(), scale.data_ptr(),
-        _lib.ptr(dloss), dlogits.data_ptr(), N, B, V, counters.data_ptr(), counters.numel(),
-        _lib.stream_handle(dev))
+        _lib.ptr(dloss), dlogits.data_ptr(), N, B, V, status.data_ptr(), counters.data_ptr(),
+        counters.numel(), _lib.stream_handle(dev))
     _lib.check(code, "specdec_dpace_backward")
     return dlogits
 
@@ -204,10 +231,11 @@ def _dflash_backward(logits: torch.Tensor, target_logits: torch.Tensor | None, s
         dloss = dloss.detach().to(device=dev, dtype=torch.float32).contiguous()
     cb = lib.specdec_backward_counter_bytes()
     _, counters = _lib.workspace("dflash_bwd", dev).ensure(dev, 256, cb)
+    status = _lib.status_words(dev)[_lib.STATUS_DFLASH_BWD:]
     code = _entry(lib, "specdec_dflash_backward", logits)(
         logits.data_ptr(), _lib.ptr(target_logits), scale.data_ptr(), logzq.data_ptr(),
         logzp.data_ptr(), _lib.ptr(tgt), _lib.ptr(dloss), dlogits.data_ptr(), N, B, V, int(kind),
-        counters.data_ptr(), counters.numel(), _lib.stream_handle(dev))
+        status.data_ptr(), counters.data_ptr(), counters.numel(), _lib.stream_handle(dev))
     _lib.check(code, "specdec_dflash_backward")
     return dlogits
 

@@ -98,7 +98,7 @@ int specdec_dpace_forward(const float* logits, const int64_t* targets, const flo
                           int32_t* status, void* scratch, size_t scratch_bytes, void* counters,
                           size_t counter_bytes, void* stream);
 
-/* Counter bytes for the optional block queue of both backward entry points. */
+/* Counter bytes for the block queue and status of both backward entry points. */
 size_t specdec_backward_counter_bytes(void);
 
 /*
@@ -108,20 +108,31 @@ size_t specdec_backward_counter_bytes(void);
  * dloss may be NULL (treated as 1). dlogits must not alias logits.
  * counters (zeroed once, left zeroed; specdec_backward_counter_bytes())
  * enable the dynamic block queue; NULL selects a static block interleave.
+ * status [1] int32 (device, may be NULL): SPECDEC_OK, or SPECDEC_ERR_CUDA when
+ * a bounded wait inside the launch expired. The reference's backward has no
+ * device waits; this failure mode is this design's, so it is reported two
+ * ways: through *status, and in the gradient itself -- every block of
+ * dlogits the failed part of the launch may have left unfinished is
+ * overwritten with NaN, so a gradient is never partly stale. A forward whose
+ * wait expired writes NaN lse/scale, so a backward from it is NaN throughout.
  */
 int specdec_dpace_backward(const float* logits, const int64_t* targets, const float* lse,
                            const float* scale, const float* dloss, float* dlogits, int64_t N,
-                           int32_t B, int64_t V, void* counters, size_t counter_bytes,
+                           int32_t B, int64_t V, int32_t* status, void* counters, size_t counter_bytes,
                            void* stream);
 
 /*
  * D-PACE forward and backward in one call, for callers that want the loss and
  * the gradient together (dloss = 1): the loss, lse, scale (and loss_n) of
  * specdec_dpace_forward and the dlogits of specdec_dpace_backward with a
- * NULL dloss -- the same two kernels on `stream`, so the same bits. No single
- * counterpart in the reference (losses/dpace.py:176-187 + :217-226 in one
- * call). Arguments as in specdec_dpace_forward plus `dlogits` [N, B, V] (same
- * element type as logits, must not alias it); same workspace queries.
+ * NULL dloss -- the same kernels on `stream`, so the same bits. Because the
+ * call owns both launches, the backward is chained to the forward's last
+ * kernel (programmatic dependent launch): it starts streaming the logits of
+ * the scored rows while the forward finishes. No single counterpart in the
+ * reference (losses/dpace.py:176-187 + :217-226 in one call). Arguments as in
+ * specdec_dpace_forward plus `dlogits` [N, B, V] (same element type as
+ * logits, must not alias it); same workspace queries. *status is the
+ * forward's word, raised to SPECDEC_ERR_CUDA if a wait of the backward expired.
  */
 int specdec_dpace_forward_backward(const float* logits, const int64_t* targets, const float* mask, int64_t N,
                                    int32_t B, int64_t V, float alpha, int32_t loss_type, int64_t n_global,
@@ -151,13 +162,18 @@ int specdec_scale_inplace_bf16(uint16_t* x, int64_t n, const float* factor, void
  * cudaFree or other allocating routine. Same arguments, kernels and results
  * as specdec_dpace_forward minus scratch/counters: its scratch is a 4 MiB
  * array built into the library (held on every GPU that loads the library
- * until exit): 64 KiB of counters (N <= 16380) and 4 MiB - 64 KiB of scratch,
- * about N*B*(32*((V-1)/16384 + 2) + 4) bytes -- e.g. up to ~14000 rows of
- * N*B at V = 128256. Larger problems return SPECDEC_ERR_WORKSPACE before any
- * launch. The first call on a device looks up the array's address
- * with that device current; make it before any stream capture. All calls on a
- * device share the array: its counters are cleared on `stream` before each
- * launch, and calls that overlap on the GPU race.
+ * until exit): 64 KiB of counters and 4 MiB - 64 KiB of scratch. A problem
+ * fits when specdec_dpace_counter_bytes(N, B) <= 64 KiB (N <= 16376) and
+ * specdec_dpace_scratch_bytes(N, B, V, device) <= 4 MiB - 64 KiB -- at
+ * V = 128256 about 14000 rows of N*B (292 bytes of scratch per row). Larger problems
+ * return SPECDEC_ERR_WORKSPACE before any launch; invalid arguments return
+ * the same codes as specdec_dpace_forward, checked first. The first call on
+ * a device looks up the array's address with that device current; make it
+ * before any stream capture. The address is kept for the life of the
+ * process: do not call this entry point on a device after cudaDeviceReset
+ * (or any other destruction of its primary context). All calls on a device
+ * share the array: its counters are cleared on `stream` before each launch,
+ * and calls that overlap on the GPU race.
  */
 int specdec_dpace_forward_noalloc(const float* logits, const int64_t* targets, const float* mask,
                                   int64_t N, int32_t B, int64_t V, float alpha, int32_t loss_type,
@@ -200,12 +216,14 @@ int specdec_dflash_forward(const float* logits, const float* target_logits, cons
  *   KL: dlogits = scale * dloss * (softmax(logits) - softmax(target_logits))
  *   CE: dlogits = scale * dloss * (softmax(logits) - onehot(target_id))
  * target_logits is read for KL only (may be NULL for CE); target_id for CE only.
- * counters: as for specdec_dpace_backward (NULL = static block interleave).
+ * counters and status: as for specdec_dpace_backward (NULL counters = static
+ * block interleave; an expired wait gives SPECDEC_ERR_CUDA and NaN blocks).
  */
 int specdec_dflash_backward(const float* logits, const float* target_logits, const float* scale,
                             const float* logzq, const float* logzp, const int64_t* target_id,
                             const float* dloss, float* dlogits, int64_t N, int32_t B, int64_t V,
-                            int32_t kind, void* counters, size_t counter_bytes, void* stream);
+                            int32_t kind, int32_t* status, void* counters, size_t counter_bytes,
+                            void* stream);
 
 /* ------------------------------------------------------------------------- */
 /* bfloat16 logits                                                            */
@@ -231,7 +249,7 @@ int specdec_dpace_forward_bf16(const uint16_t* logits, const int64_t* targets, c
                                size_t counter_bytes, void* stream);
 int specdec_dpace_backward_bf16(const uint16_t* logits, const int64_t* targets, const float* lse,
                                 const float* scale, const float* dloss, uint16_t* dlogits, int64_t N,
-                                int32_t B, int64_t V, void* counters, size_t counter_bytes,
+                                int32_t B, int64_t V, int32_t* status, void* counters, size_t counter_bytes,
                                 void* stream);
 int specdec_dflash_forward_bf16(const uint16_t* logits, const uint16_t* target_logits, const float* mask,
                                 int64_t N, int32_t B, int64_t V, int32_t block_size, float gamma,
@@ -242,7 +260,8 @@ int specdec_dflash_forward_bf16(const uint16_t* logits, const uint16_t* target_l
 int specdec_dflash_backward_bf16(const uint16_t* logits, const uint16_t* target_logits, const float* scale,
                                  const float* logzq, const float* logzp, const int64_t* target_id,
                                  const float* dloss, uint16_t* dlogits, int64_t N, int32_t B, int64_t V,
-                                 int32_t kind, void* counters, size_t counter_bytes, void* stream);
+                                 int32_t kind, int32_t* status, void* counters, size_t counter_bytes,
+                                 void* stream);
 
 /* ------------------------------------------------------------------------- */
 /* Launch tuning                                                              */
@@ -276,14 +295,15 @@ int specdec_set_block_queue(int32_t dynamic);
 
 /*
  * Failure-detection test hook (no counterpart in the reference). The next
- * `launches` D-PACE or DFlash forward launches on the ring path make CTA 0's
- * producer withhold its first stage, so that CTA's consumers reach the 1 s
- * limit of their bounded wait: they record the timeout, wait (bounded) for
- * their own copies, and return. The launch completes in about 2 s with a NaN
- * loss (and, for D-PACE, *status = SPECDEC_ERR_CUDA); per-row outputs are
- * unspecified; the context stays usable and the next launch is normal. 0
- * cancels. Not for production use. The same NaN loss / status report any
- * wait that expires for a real reason.
+ * `launches` D-PACE or DFlash launches on the ring path (forward or backward)
+ * make CTA 0's producer withhold its first stage, so that CTA's consumers
+ * reach the 1 s limit of their bounded wait: they record the timeout, wait
+ * (bounded) for their own copies, and return. The launch completes in about
+ * 2 s. A forward so failed gives a NaN loss and NaN per-row lse/scale/logz
+ * (and, for D-PACE, *status = SPECDEC_ERR_CUDA); a backward gives
+ * *status = SPECDEC_ERR_CUDA and NaN over the blocks CTA 0 held. The context
+ * stays usable and the next launch is normal. 0 cancels. Not for production
+ * use. The same reports follow any wait that expires for a real reason.
  */
 int specdec_test_withhold_stage(int32_t launches);
 

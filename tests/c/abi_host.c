@@ -69,7 +69,8 @@ int main(int argc, char** argv) {
   CUDA(cudaGetDevice(&dev));
   float *x, *y = NULL, *g, *mask = NULL, *loss, *r0, *r1, *r2, *r3;
   int64_t *t = NULL, *tid = NULL;
-  int32_t* status;
+  int32_t* status;  /* forward (D-PACE) */
+  int32_t* bstatus; /* backward */
   CUDA(cudaMalloc((void**)&x, E * 4));
   CUDA(cudaMalloc((void**)&g, E * 4));
   CUDA(cudaMalloc((void**)&loss, 4));
@@ -79,6 +80,7 @@ int main(int argc, char** argv) {
   CUDA(cudaMalloc((void**)&r3, R * 4));
   CUDA(cudaMalloc((void**)&tid, R * 8));
   CUDA(cudaMalloc((void**)&status, 4));
+  CUDA(cudaMalloc((void**)&bstatus, 4));
   CUDA(cudaMemcpy(x, h_x, E * 4, cudaMemcpyHostToDevice));
   const size_t bwd_cb = specdec_backward_counter_bytes();
   void *scratch, *counters, *bwd_counters;
@@ -103,22 +105,24 @@ int main(int argc, char** argv) {
     CUDA(cudaMemcpy(mask, h_m, R * 4, cudaMemcpyHostToDevice));
     ABI(specdec_dpace_forward(x, t, mask, N, B, V, param, code, N, loss, NULL, r0, r1, status, scratch, sb,
                               counters, cb, st));
-    ABI(specdec_dpace_backward(x, t, r0, r1, NULL, g, N, B, V, bwd_counters, bwd_cb, st));
+    ABI(specdec_dpace_backward(x, t, r0, r1, NULL, g, N, B, V, bstatus, bwd_counters, bwd_cb, st));
   } else {
     CUDA(cudaMalloc((void**)&y, E * 4));
     CUDA(cudaMemcpy(y, h_y, E * 4, cudaMemcpyHostToDevice));
     ABI(specdec_dflash_forward(x, y, NULL, N, B, V, B, param, 0, code, N, loss, NULL, r1, r2, r3, tid, scratch,
                                sb, counters, cb, st));
     ABI(specdec_dflash_backward(x, code == SPECDEC_DFLASH_KL ? y : NULL, r1, r2, r3, tid, NULL, g, N, B, V, code,
-                                bwd_counters, bwd_cb, st));
+                                bstatus, bwd_counters, bwd_cb, st));
     CUDA(cudaMemsetAsync(status, 0, 4, st));
   }
   CUDA(cudaStreamSynchronize(st));
-  int32_t h_status;
+  int32_t h_status, h_bstatus;
   float h_loss;
   CUDA(cudaMemcpy(&h_status, status, 4, cudaMemcpyDeviceToHost));
-  if (h_status != SPECDEC_OK) {
-    fprintf(stderr, "device status %d: %s\n", h_status, specdec_status_string(h_status));
+  CUDA(cudaMemcpy(&h_bstatus, bstatus, 4, cudaMemcpyDeviceToHost));
+  if (h_status != SPECDEC_OK || h_bstatus != SPECDEC_OK) {
+    fprintf(stderr, "device status %d / %d: %s\n", h_status, h_bstatus,
+            specdec_status_string(h_status != SPECDEC_OK ? h_status : h_bstatus));
     return 5;
   }
   CUDA(cudaMemcpy(&h_loss, loss, 4, cudaMemcpyDeviceToHost));

@@ -1,7 +1,7 @@
 """Generate the golden vectors in tests/golden/ from the REFERENCE's own oracles.
 
-Runs only where the reference checkout exists (default /root/reference, or
-$SPECDEC_REF). It evaluates, on the CPU and in float32:
+Runs only where a checkout of the reference exists; its path is the required
+argument (or $SPECDEC_REF). It evaluates, on the CPU and in float32:
   - losses/dpace_ref.py::d_pace_loss (loaded by file path: the package
     __init__ imports cupy), with torch autograd for the gradient;
   - the specforge oracle _naive_dpace_weight / oracle_loss and the speculators
@@ -11,7 +11,7 @@ $SPECDEC_REF). It evaluates, on the CPU and in float32:
 on the seeded inputs of tests/golden/cases.py, and writes
 dpace_golden.npz / dflash_golden.npz (+ a readable golden_summary.json).
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <path of the reference checkout>
 """
 from __future__ import annotations
 
@@ -29,7 +29,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 import cases  # noqa: E402
 
-REF = os.environ.get("SPECDEC_REF", "/root/reference")
+REF = None  # the reference checkout: argv[1] or $SPECDEC_REF
 
 
 def load_module_by_path(name: str, path: str):
@@ -125,4 +125,7 @@ def main() -> None:
 
 
 if __name__ == "__main__":
+    REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("SPECDEC_REF")
+    if not REF or not os.path.isdir(REF):
+        sys.exit("usage: make_golden.py <path of the reference checkout> (or set SPECDEC_REF)")
     main()

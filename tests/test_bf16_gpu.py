@@ -158,7 +158,7 @@ def test_bf16_abi_rejects_misaligned_pointers(cuda):
     g = torch.empty_like(x)
     code = lib.specdec_dpace_backward_bf16(
         x.data_ptr(), t.data_ptr(), out[0].data_ptr(), out[1].data_ptr(), None, g.data_ptr() + 8,
-        N, B, V, None, 0, None)
+        N, B, V, None, None, 0, None)
     assert code == _lib.ERR_ARGUMENT
 
 

@@ -1,13 +1,15 @@
 """Failure detection on the GPU without a fault: a bounded wait that runs out.
 
 specdec_test_withhold_stage(1) makes CTA 0 of the next D-PACE or DFlash
-forward never post its first stage. Its consumer warps wait on that stage's mbarrier, give up
-after the 1 s limit, record the timeout in the status word, wait (bounded) for
-the copies they may still have in flight and return; the launch completes.
-The host must see the error (D-PACE: RuntimeError through the drop-in API,
-status 5 and a NaN loss through the C ABI; DFlash: a NaN loss) and the next
-call must be normal: context usable, counters zero, results equal to the
-oracle's."""
+launch on the ring path (forward or backward) never post its first stage. Its
+consumer warps wait on that stage's mbarrier, give up after the 1 s limit,
+record the timeout, wait (bounded) for the copies they may still have in
+flight and return; the launch completes. The host must see the error --
+forward: a NaN loss and NaN per-row outputs (so a backward from them is NaN
+throughout), status 5 for D-PACE, RuntimeError through the drop-in API;
+backward: status 5 and NaN over every block the failed CTA may have left
+unfinished, never a partly stale gradient -- and the next call must be
+normal: context usable, counters zero, results equal to the oracle's."""
 import pytest
 import torch
 
@@ -103,3 +105,137 @@ def test_dflash_expired_wait_gives_nan_loss_and_the_next_call_is_normal(cuda):
     want, _ = odf.dflash_fwd_bwd_torch(x.cpu(), y.cpu())
     loss = float(fused_dflash_loss(x, y))
     assert abs(loss - float(want)) <= 1e-5 * abs(float(want))
+
+
+def _dpace_state(x, t):
+    from specdec import ops
+
+    loss, lse, scale, _ = ops.dpace_forward(x, t, None, 0.5, 0)
+    return lse, scale
+
+
+def _nan_blocks_else_exact(g, g_ref):
+    """Every element is NaN or within 1e-6 of the oracle; returns the NaN count."""
+    nan = torch.isnan(g)
+    ok = (g - g_ref).abs() <= 1e-6
+    assert bool((nan | ok).all())
+    return int(nan.sum())
+
+
+def test_backward_expired_wait_gives_status_and_nan_blocks(cuda):
+    from specdec import _lib, ops
+
+    x, t = _inputs()
+    _, g_ref = odp.dpace_fwd_bwd_torch(x.cpu(), t.cpu())
+    lse, scale = _dpace_state(x, t)
+    lib = _lib.load()
+    try:
+        _lib.check(lib.specdec_test_withhold_stage(1), "specdec_test_withhold_stage")
+        g = ops.dpace_backward(x, t, lse, scale, None)  # asynchronous: no error yet
+        torch.cuda.synchronize()
+    finally:
+        lib.specdec_test_withhold_stage(0)
+    assert int(_lib.status_words(x.device)[_lib.STATUS_DPACE_BWD]) == _lib.ERR_CUDA
+    n = _nan_blocks_else_exact(g.cpu(), g_ref)
+    assert 0 < n <= 2 * 16384  # the (at most two) blocks CTA 0 held
+    with pytest.raises(RuntimeError, match="earlier backward"):
+        ops.check_backward(x.device)
+    ops.check_backward(x.device)  # reported once
+    g = ops.dpace_backward(x, t, lse, scale, None)
+    assert float((g.cpu() - g_ref).abs().max()) <= 1e-6
+    ops.check_backward(x.device)
+
+
+def test_backward_expired_wait_is_raised_by_the_next_forward(cuda):
+    from losses import fused_dpace_loss
+    from specdec import _lib, ops
+
+    x, t = _inputs()
+    lse, scale = _dpace_state(x, t)
+    lib = _lib.load()
+    try:
+        lib.specdec_test_withhold_stage(1)
+        ops.dpace_backward(x, t, lse, scale, None)
+    finally:
+        lib.specdec_test_withhold_stage(0)
+    with pytest.raises(RuntimeError, match="earlier backward"):
+        fused_dpace_loss(x, t)
+    want, _ = odp.dpace_fwd_bwd_torch(x.cpu(), t.cpu())
+    assert abs(float(fused_dpace_loss(x, t)) - float(want)) <= 1e-5 * abs(float(want))
+
+
+def test_backward_expired_wait_status_without_counters(cuda):
+    """Static block interleave (no counter block): the entry point clears the
+    status word on the stream and the failed CTA raises it."""
+    from specdec import _lib
+
+    lib = _lib.load()
+    x, t = _inputs()
+    N, B, V = x.shape
+    _, g_ref = odp.dpace_fwd_bwd_torch(x.cpu(), t.cpu())
+    lse, scale = _dpace_state(x, t)
+    g = torch.empty_like(x)
+    status = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def call():
+        return lib.specdec_dpace_backward(x.data_ptr(), t.data_ptr(), lse.data_ptr(), scale.data_ptr(), None,
+                                          g.data_ptr(), N, B, V, status.data_ptr(), None, 0, stream)
+
+    try:
+        lib.specdec_test_withhold_stage(1)
+        assert call() == _lib.OK
+        torch.cuda.synchronize()
+    finally:
+        lib.specdec_test_withhold_stage(0)
+    assert int(status.item()) == _lib.ERR_CUDA
+    assert 0 < _nan_blocks_else_exact(g.cpu(), g_ref) <= 2 * 16384
+    assert call() == _lib.OK
+    torch.cuda.synchronize()
+    assert int(status.item()) == _lib.OK
+    assert float((g.cpu() - g_ref).abs().max()) <= 1e-6
+
+
+def test_dflash_backward_expired_wait_gives_status_and_nan_blocks(cuda):
+    from oracle import dflash as odf
+    from specdec import _lib, ops
+
+    x, _ = _inputs()
+    y = 0.5 * x
+    _, g_ref = odf.dflash_fwd_bwd_torch(x.cpu(), y.cpu())
+    B = x.shape[1]
+    _, _, scale, lzq, lzp, _ = ops.dflash_forward(x, y, None, 4.0, False, 0, B)
+    lib = _lib.load()
+    try:
+        lib.specdec_test_withhold_stage(1)
+        g = ops.dflash_backward(x, y, scale, lzq, lzp, None, None, 0)
+        torch.cuda.synchronize()
+    finally:
+        lib.specdec_test_withhold_stage(0)
+    assert int(_lib.status_words(x.device)[_lib.STATUS_DFLASH_BWD]) == _lib.ERR_CUDA
+    assert 0 < _nan_blocks_else_exact(g.cpu(), g_ref) <= 2 * 16384
+    with pytest.raises(RuntimeError, match="earlier backward"):
+        ops.check_backward(x.device)
+    g = ops.dflash_backward(x, y, scale, lzq, lzp, None, None, 0)
+    assert float((g.cpu() - g_ref).abs().max()) <= 1e-6
+
+
+def test_dflash_forward_expired_wait_makes_the_whole_gradient_nan(cuda):
+    """A failed forward writes NaN scale / log-normalisers, so autograd's
+    backward from it cannot return a plausible gradient."""
+    from models.dflash import dflash_loss
+    from specdec import _lib
+
+    x, _ = _inputs()
+    y = 0.5 * x
+    xg = x.clone().requires_grad_(True)
+    lib = _lib.load()
+    try:
+        lib.specdec_test_withhold_stage(1)
+        loss = dflash_loss(xg, y)
+    finally:
+        lib.specdec_test_withhold_stage(0)
+    loss.backward()
+    torch.cuda.synchronize()
+    assert bool(torch.isnan(loss.detach()))
+    assert bool(torch.isnan(xg.grad).all())
