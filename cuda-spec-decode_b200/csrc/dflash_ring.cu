@@ -447,7 +447,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, (KIND == kKi
     if (lane == 0) sm.trk.done[warp] = it;
   }
   __syncthreads();
-  if (sm.trk.timeout) ring_poison<T, S>(dst, E, BL, q.nblocks, sm.trk, NC);
+  if (sm.trk.timeout) ring_poison<T, S>(dst, E, BL, q.nblocks, sm.trk, NC, q.dynamic ? 0u : gridDim.x);
   if (threadIdx.x == 0) bwd_finish(q, a, sm.trk.timeout != 0);
 }
 

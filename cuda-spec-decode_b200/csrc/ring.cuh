@@ -251,10 +251,14 @@ __device__ __forceinline__ void ring_init(RingSmem<NIN, S, SE, T>& sm, int consu
 // unfinished -- the blocks of the stages some consumer warp had not finished
 // (at most S stages: the producer never runs more than S ahead of the slowest
 // consumer) and the blocks the producer had dequeued but not fully posted.
-// Blocks this CTA finished are left as written, so a gradient is never
-// partly stale: every element is either correct or NaN.
+// With the static interleave (`stride` = the grid) this CTA also owns every
+// later block of its sequence, held[1] + k * stride, which no other CTA will
+// write: those are overwritten too. Blocks this CTA finished are left as
+// written, so a gradient is never partly stale: every element is either
+// correct or NaN.
 template <class T, int S>
-__device__ void ring_poison(T* dst, int64_t E, int64_t BL, unsigned nblocks, const RingTrack<S>& trk, int nc) {
+__device__ void ring_poison(T* dst, int64_t E, int64_t BL, unsigned nblocks, const RingTrack<S>& trk, int nc,
+                            unsigned stride) {
   int64_t lo = trk.done[0];
   for (int w = 1; w < nc; ++w) lo = min(lo, trk.done[w]);
   unsigned ids[S + 2];
@@ -269,6 +273,12 @@ __device__ void ring_poison(T* dst, int64_t E, int64_t BL, unsigned nblocks, con
     if (seen) continue;
     const int64_t f0 = (int64_t)b * BL, f1 = min(f0 + BL, E);
     for (int64_t x = f0 + threadIdx.x; x < f1; x += blockDim.x) store_elem(dst + x, __int_as_float(0x7fc00000));
+  }
+  if (stride != 0 && trk.held[1] < nblocks) {
+    for (uint64_t b = (uint64_t)trk.held[1] + stride; b < nblocks; b += stride) {
+      const int64_t f0 = (int64_t)b * BL, f1 = min(f0 + BL, E);
+      for (int64_t x = f0 + threadIdx.x; x < f1; x += blockDim.x) store_elem(dst + x, __int_as_float(0x7fc00000));
+    }
   }
 }
 

@@ -88,3 +88,30 @@ def test_golden_edge_values(gd, gf):
     assert float(gf["kl_allmasked_N4_B8_V512/loss"]) == 0.0
     # B=1 without sample_from_anchor: the only slot is the anchor, weight 0
     assert float(gf["kl_B1_N8_V1024/loss"]) == 0.0
+
+
+def test_flat_gradient_bound_is_below_fp32_resolution_for_the_oracle():
+    """Draw 0 of the D-PACE random sweep (tests/test_random_gpu.py, seed 1000:
+    sigma 5, lse ~ 20): the reference's fp32 oracle itself is more than 1e-6
+    from the float64 gradient, and within 1e-6 + ulp_fp32(lse_row) * |g| -- the
+    bound the sweep applies to the kernel."""
+    rng = np.random.default_rng(1000)
+    V = int(np.exp(rng.uniform(0, np.log(70000))))
+    B = int(rng.integers(1, 33))
+    N = int(rng.integers(1, 7))
+    while N * B * V > 2_000_000 and N > 1:
+        N -= 1
+    sigma = float(rng.choice([0.5, 2.0, 5.0]))
+    x = torch.from_numpy(rng.normal(0, sigma, (N, B, V)).astype(np.float32))
+    t = torch.from_numpy(rng.integers(0, V, (N, B)))
+    mode = int(rng.integers(0, 3))
+    m = None if mode == 0 else torch.from_numpy((rng.random((N, B)) < rng.uniform(0.3, 1.0)).astype(np.float32))
+    alpha = float(rng.uniform(0, 1))
+    lt = odp.LOSS_TYPES[int(rng.integers(0, 3))]
+    assert sigma == 5.0
+    _, g_ref = odp.dpace_fwd_bwd_torch(x, t, alpha, m, lt)
+    _, g64, lse64, _ = odp.dpace_f64(x.numpy(), t.numpy(), alpha, None if m is None else m.numpy(), lt)
+    err = np.abs(g_ref.numpy().astype(np.float64) - g64)
+    tol = 1e-6 + np.spacing(np.abs(lse64).astype(np.float32)).astype(np.float64)[..., None] * np.abs(g64)
+    assert float(err.max()) > 1e-6
+    assert bool((err <= tol).all())
