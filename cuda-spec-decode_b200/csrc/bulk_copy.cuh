@@ -73,6 +73,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return true;
 }
 
+// Releases a stage slot as soon as the calling warp's values are in
+// registers, before the arithmetic on them: `dep` is computed from every
+// value the lane loaded from the stage (its maximum), and it is an operand of
+// both the warp barrier and the arrive, so no lane reaches the barrier -- and
+// lane 0 does not arrive -- before its shared-memory loads have returned. The
+// producer then refills the slot while the warp works from registers, which
+// keeps more of the ring's bytes in flight.
+__device__ __forceinline__ void release_stage(uint64_t* empty, float dep) {
+  asm volatile("bar.warp.sync %0;" ::"r"(kFullMask), "f"(dep) : "memory");
+  if ((threadIdx.x & 31) == 0)
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(empty)), "f"(dep) : "memory");
+}
+
 // Bulk copy global -> this CTA's shared memory, completing `bytes` on `bar`.
 // src and dst 16-byte aligned, bytes a multiple of 16. No multicast.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

@@ -12,6 +12,7 @@
 #include <cstdint>
 #include <type_traits>
 
+#include "bulk_copy.cuh"
 #include "specdec_common.cuh"
 #include "specdec_internal.h"
 
@@ -104,10 +105,14 @@ __device__ __forceinline__ void df_push(DfState& s, float a, float b, int idx) {
 
 template <int KIND, int U>
 __device__ __forceinline__ void df_group(DfState& s, const float4 (&a)[U], const float4 (&b)[U],
-                                         int base_idx, int stride_idx) {
+                                         int base_idx, int stride_idx, uint64_t* empty = nullptr) {
   float cma = max4(a[0]);
 #pragma unroll
   for (int u = 1; u < U; ++u) cma = fmaxf(cma, max4(a[u]));
+  float cmb = max4(b[0]);
+#pragma unroll
+  for (int u = 1; u < U; ++u) cmb = fmaxf(cmb, max4(b[u]));
+  if (empty) release_stage(empty, fmaxf(cma, cmb));  // both streams are in registers
   if (cma > s.mq) {
     s.sq *= exp_shift(s.mq, cma);
     s.mq = cma;
@@ -120,9 +125,6 @@ __device__ __forceinline__ void df_group(DfState& s, const float4 (&a)[U], const
             exp_shift(a[u].w, mq);
   }
   s.sq += accq;
-  float cmb = max4(b[0]);
-#pragma unroll
-  for (int u = 1; u < U; ++u) cmb = fmaxf(cmb, max4(b[u]));
   if (KIND == kKindKL) {
     if (cmb > s.mp) {
       const float f = exp_shift(s.mp, cmb);
@@ -167,11 +169,16 @@ __device__ __forceinline__ void df_group(DfState& s, const float4 (&a)[U], const
 // taken on the packed words; each element is widened once.
 template <int KIND, int U>
 __device__ __forceinline__ void df_group(DfState& s, const uint4 (&a)[U], const uint4 (&b)[U], int base_idx,
-                                         int stride_idx) {
+                                         int stride_idx, uint64_t* empty = nullptr) {
   uint32_t pa = bmax8(a[0]);
 #pragma unroll
   for (int u = 1; u < U; ++u) pa = bmax2(pa, bmax8(a[u]));
   const float cma = fmaxf(bf16_lo(pa), bf16_hi(pa));
+  uint32_t pb = bmax8(b[0]);
+#pragma unroll
+  for (int u = 1; u < U; ++u) pb = bmax2(pb, bmax8(b[u]));
+  const float cmb = fmaxf(bf16_lo(pb), bf16_hi(pb));
+  if (empty) release_stage(empty, fmaxf(cma, cmb));  // both streams are in registers
   if (cma > s.mq) {
     s.sq *= exp_shift(s.mq, cma);
     s.mq = cma;
@@ -181,10 +188,6 @@ __device__ __forceinline__ void df_group(DfState& s, const uint4 (&a)[U], const 
 #pragma unroll
   for (int u = 0; u < U; ++u) accq = fadd2(accq, vec8_expsum2(a[u], mq));
   s.sq += accq.x + accq.y;
-  uint32_t pb = bmax8(b[0]);
-#pragma unroll
-  for (int u = 1; u < U; ++u) pb = bmax2(pb, bmax8(b[u]));
-  const float cmb = fmaxf(bf16_lo(pb), bf16_hi(pb));
   if (KIND == kKindKL) {
     if (cmb > s.mp) {
       const float f = exp_shift(s.mp, cmb);

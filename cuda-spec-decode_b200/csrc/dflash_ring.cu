@@ -65,20 +65,22 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 2, S, SE, T>
   const int64_t E = a.pt.E, V = a.pt.V, R = E / V;
   const int pmax = a.pt.pmax;
 
-  ring_init(sm, NC);
-  const RowBits rb = build_row_bits(sm.bits, R, NC + 1, [&](int64_t r) { return dr_numer(a, r) != 0.f; });
-  __syncthreads();
-
   BlockQueue q;
   q.ctr = a.q_ctr;
   q.retired = a.q_retired;
   q.nblocks = (unsigned)((E + BL - 1) / BL);
   q.dynamic = a.q_dynamic;
+  // the producer's first block, dequeued before the prologue so that the
+  // atomic's latency overlaps it
+  const unsigned first = (warp == NC && lane == 0) ? q.first() : 0u;
+  ring_init(sm, NC);
+  const RowBits rb = build_row_bits(sm.bits, R, NC + 1, [&](int64_t r) { return dr_numer(a, r) != 0.f; });
+  __syncthreads();
 
   if (warp == NC) {  // producer
     if (lane == 0) {
       const T* src[2] = {XL, XT};
-      if (!ring_produce<2, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow,
+      if (!ring_produce<2, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow, first,
                                       a.withhold_stage && blockIdx.x == 0))
         atomicOr(a.flag, 2);
       q.retire();
@@ -140,10 +142,12 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 2, S, SE, T>
           vb[u] = qx[32 * u];
         }
         const int base = (int)(f0 - r * V) + warp * kSub + kVec * lane;
-        df_group<KIND, U>(st, va, vb, base, 32 * kVec);
+        // the slot is released inside, once both streams are in registers
+        df_group<KIND, U>(st, va, vb, base, 32 * kVec, sm.empty + slot);
+      } else {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sm.empty + slot);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(sm.empty + slot);
       if ((r + 1) * V == f1) {
         close_piece();
         ++r;
@@ -287,20 +291,22 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, (KIND == kKi
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t E = a.pt.E, V = a.pt.V, R = E / V;
   const float g = a.dloss ? __ldg(a.dloss) : 1.f;
-  ring_init(sm, NC);
-  const RowBits rb = build_row_bits(sm.bits, R, NC + 1, [&](int64_t r) { return __fmul_rn(a.scale[r], g) != 0.f; });
-  __syncthreads();
-
   BlockQueue q;
   q.ctr = a.q_ctr;
   q.retired = a.q_retired;
   q.nblocks = (unsigned)((E + BL - 1) / BL);
   q.dynamic = a.q_dynamic;
+  // the producer's first block, dequeued before the prologue so that the
+  // atomic's latency overlaps it
+  const unsigned first = (warp == NC && lane == 0) ? q.first() : 0u;
+  ring_init(sm, NC);
+  const RowBits rb = build_row_bits(sm.bits, R, NC + 1, [&](int64_t r) { return __fmul_rn(a.scale[r], g) != 0.f; });
+  __syncthreads();
 
   if (warp == NC) {
     if (lane == 0) {
       const T* src[2] = {XL, XT};
-      if (!ring_produce<NIN, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow,
+      if (!ring_produce<NIN, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow, first,
                                         a.withhold_stage && blockIdx.x == 0, &sm.trk))
         sm.trk.timeout = 1;
     }
@@ -451,6 +457,14 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, (KIND == kKi
   if (threadIdx.x == 0) bwd_finish(q, a, sm.trk.timeout != 0);
 }
 
+// Stages per queue block of the backward kernels: small blocks (the backward
+// has no per-block partials), so that no CTA holds more than a little
+// unstarted work when the queue runs dry.
+#ifndef SPECDEC_DFBWD_BLOCK_STAGES
+#define SPECDEC_DFBWD_BLOCK_STAGES 2
+#endif
+constexpr int kDfBwdBlockStages = SPECDEC_DFBWD_BLOCK_STAGES;
+
 template <class T, int NC, int S, int SE, int BS>
 struct DfRing {
   template <int KIND>
@@ -464,7 +478,7 @@ struct DfRing {
   }
   template <int KIND>
   static int bwd_ctas(int device, int cap) {
-    return ring_occupancy_ctas(dflash_bwd_ring_kernel<T, KIND, NC, S, SE, BS>, (NC + 1) * 32, bsmem<KIND>(),
+    return ring_occupancy_ctas(dflash_bwd_ring_kernel<T, KIND, NC, S, SE, kDfBwdBlockStages>, (NC + 1) * 32, bsmem<KIND>(),
                                device, cap);
   }
   template <int KIND>
@@ -482,9 +496,9 @@ struct DfRing {
   }
   template <int KIND>
   static cudaError_t bwd(const DflashBwdArgs& a, int ctas, cudaStream_t st) {
-    const cudaError_t e = ensure_smem_limit<dflash_bwd_ring_kernel<T, KIND, NC, S, SE, BS>>(bsmem<KIND>());
+    const cudaError_t e = ensure_smem_limit<dflash_bwd_ring_kernel<T, KIND, NC, S, SE, kDfBwdBlockStages>>(bsmem<KIND>());
     if (e != cudaSuccess) return e;
-    dflash_bwd_ring_kernel<T, KIND, NC, S, SE, BS><<<ctas, (NC + 1) * 32, bsmem<KIND>(), st>>>(a);
+    dflash_bwd_ring_kernel<T, KIND, NC, S, SE, kDfBwdBlockStages><<<ctas, (NC + 1) * 32, bsmem<KIND>(), st>>>(a);
     return cudaGetLastError();
   }
 };

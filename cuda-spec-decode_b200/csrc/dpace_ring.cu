@@ -50,22 +50,24 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
   const int64_t E = a.pt.E, V = a.pt.V, R = E / V;
   const int pmax = a.pt.pmax;
 
+  BlockQueue q;
+  q.ctr = a.q_ctr;
+  q.retired = a.q_retired;
+  q.nblocks = (unsigned)((E + BL - 1) / BL);
+  q.dynamic = a.q_dynamic;
+  // the producer's first block, dequeued before the prologue so that the
+  // atomic's latency overlaps it
+  const unsigned first = (warp == NC && lane == 0) ? q.first() : 0u;
   ring_init(sm, NC);
   const RowBits rb = build_row_bits(sm.bits, R, NC + 1, [&](int64_t r) {
     return a.mask == nullptr || a.mask[r] > 0.f;
   });
   __syncthreads();
 
-  BlockQueue q;
-  q.ctr = a.q_ctr;
-  q.retired = a.q_retired;
-  q.nblocks = (unsigned)((E + BL - 1) / BL);
-  q.dynamic = a.q_dynamic;
-
   if (warp == NC) {  // producer
     if (lane == 0) {
       const T* src[1] = {X};
-      if (!ring_produce<1, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow,
+      if (!ring_produce<1, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow, first,
                                       a.withhold_stage && blockIdx.x == 0)) {
         atomicOr(a.flag, 2);
         if (a.status) a.status[0] = kStatusTimeout;
@@ -116,10 +118,14 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
     }
     const T* sb = sm.ring + (size_t)slot * SE;
     if (f1 - f0 == SE && (r + 1) * V >= f1) {
-      // fast path: a full stage inside one row
-      if (live) warp_lse_full<kSub>(sb + warp * kSub, m, s);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(sm.empty + slot);
+      // fast path: a full stage inside one row; the slot is released as soon
+      // as the warp's values are in registers
+      if (live) {
+        warp_lse_full<kSub>(sb + warp * kSub, m, s, sm.empty + slot);
+      } else {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sm.empty + slot);
+      }
       if ((r + 1) * V == f1) {
         close_piece();
         ++r;
@@ -275,6 +281,14 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t E = a.pt.E, V = a.pt.V, R = E / V;
   const float g = a.dloss ? __ldg(a.dloss) : 1.f;
+  BlockQueue q;
+  q.ctr = a.q_ctr;
+  q.retired = a.q_retired;
+  q.nblocks = (unsigned)((E + BL - 1) / BL);
+  q.dynamic = a.q_dynamic;
+  // the producer's first block, dequeued before the prologue so that the
+  // atomic's latency overlaps it
+  const unsigned first = (warp == NC && lane == 0) ? q.first() : 0u;
   ring_init(sm, NC);
   // Rows to read: those with a nonzero scale * dloss -- or, when chained
   // behind the finalize that writes scale, those with a scored mask, which is
@@ -287,16 +301,10 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
   });
   __syncthreads();
 
-  BlockQueue q;
-  q.ctr = a.q_ctr;
-  q.retired = a.q_retired;
-  q.nblocks = (unsigned)((E + BL - 1) / BL);
-  q.dynamic = a.q_dynamic;
-
   if (warp == NC) {
     if (lane == 0) {
       const T* src[1] = {X};
-      if (!ring_produce<1, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow,
+      if (!ring_produce<1, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow, first,
                                       a.withhold_stage && blockIdx.x == 0, &sm.trk))
         sm.trk.timeout = 1;
     }
@@ -425,6 +433,15 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
   if (threadIdx.x == 0) bwd_finish(q, a, sm.trk.timeout != 0);
 }
 
+// Stages per queue block of the backward kernels. The backward has no
+// per-block partials (the forward's slot layout depends on its block length),
+// so its blocks can be small: a CTA never holds more than one unstarted
+// stage when the queue runs dry, which keeps the end of the launch tight.
+#ifndef SPECDEC_BWD_BLOCK_STAGES
+#define SPECDEC_BWD_BLOCK_STAGES 1
+#endif
+constexpr int kBwdBlockStages = SPECDEC_BWD_BLOCK_STAGES;
+
 template <class T, int NC, int S, int SE, int BS>
 struct RingVariant {
   static constexpr size_t smem() { return sizeof(RingSmem<1, S, SE, T>); }
@@ -432,7 +449,7 @@ struct RingVariant {
     return ring_occupancy_ctas(dpace_fwd_ring_kernel<T, NC, S, SE, BS>, (NC + 1) * 32, smem(), device, cap);
   }
   static int bwd_ctas(int device, int cap) {
-    return ring_occupancy_ctas(dpace_bwd_ring_kernel<T, NC, S, SE, BS>, (NC + 1) * 32, smem(), device, cap);
+    return ring_occupancy_ctas(dpace_bwd_ring_kernel<T, NC, S, SE, kBwdBlockStages>, (NC + 1) * 32, smem(), device, cap);
   }
   static cudaError_t fwd(DpaceFwdArgs a, int ctas, cudaStream_t st) {
     // the attribute must be set on the launching device before the launch
@@ -448,12 +465,12 @@ struct RingVariant {
     return launch_pdl(dpace_finalize_kernel<T>, dim3((unsigned)a.N), dim3(32 * a.B), 0, st, a);
   }
   static cudaError_t bwd(const DpaceBwdArgs& a, int ctas, cudaStream_t st) {
-    const cudaError_t e = ensure_smem_limit<dpace_bwd_ring_kernel<T, NC, S, SE, BS>>(smem());
+    const cudaError_t e = ensure_smem_limit<dpace_bwd_ring_kernel<T, NC, S, SE, kBwdBlockStages>>(smem());
     if (e != cudaSuccess) return e;
     // chained only behind this library's own finalize (forward_backward)
     if (a.chained)
-      return launch_pdl(dpace_bwd_ring_kernel<T, NC, S, SE, BS>, dim3(ctas), dim3((NC + 1) * 32), smem(), st, a);
-    dpace_bwd_ring_kernel<T, NC, S, SE, BS><<<ctas, (NC + 1) * 32, smem(), st>>>(a);
+      return launch_pdl(dpace_bwd_ring_kernel<T, NC, S, SE, kBwdBlockStages>, dim3(ctas), dim3((NC + 1) * 32), smem(), st, a);
+    dpace_bwd_ring_kernel<T, NC, S, SE, kBwdBlockStages><<<ctas, (NC + 1) * 32, smem(), st>>>(a);
     return cudaGetLastError();
   }
 };
@@ -463,8 +480,9 @@ struct RingVariant {
 // the fastest measured on the [64, 16, 128256] workload); 1 = 8 x 4 x 8192 x 2
 // (128 KB ring, 1 CTA/SM); 2 = 4 x 6 x 4096 x 4 (96 KB ring, 2 CTAs/SM); 3 =
 // 4 x 8 x 4096 x 8 (128 KB ring, 128 KB blocks); 4 = 2 x 6 x 2048 x 8 (48 KB
-// ring, 4 CTAs/SM); 5 = 8 x 4 x 4096 x 4 (64 KB ring, 8 consumer warps). bf16
-// shapes have the same bytes (twice the elements).
+// ring, 4 CTAs/SM); 5 = 8 x 4 x 4096 x 4 (64 KB ring, 8 consumer warps); 6 =
+// 4 x 3 x 4096 x 4 (48 KB ring, 4 CTAs/SM). bf16 shapes have the same bytes
+// (twice the elements).
 template <class T>
 struct Shapes {
   static constexpr int k = 4 / sizeof(T);  // elements per float's bytes
@@ -474,6 +492,7 @@ struct Shapes {
   using R3 = RingVariant<T, 4, 8, 4096 * k, 8>;
   using R4 = RingVariant<T, 2, 6, 2048 * k, 8>;
   using R5 = RingVariant<T, 8, 4, 4096 * k, 4>;
+  using R6 = RingVariant<T, 4, 3, 4096 * k, 4>;
 
   static int block_elems(int shape) {
     switch (shape) {
@@ -482,6 +501,7 @@ struct Shapes {
       case 3: return 4096 * 8 * k;
       case 4: return 2048 * 8 * k;
       case 5: return 4096 * 4 * k;
+      case 6: return 4096 * 4 * k;
       default: return 4096 * 4 * k;
     }
   }
@@ -492,6 +512,7 @@ struct Shapes {
       case 3: return R3::fwd_ctas(device, cap);
       case 4: return R4::fwd_ctas(device, cap);
       case 5: return R5::fwd_ctas(device, cap);
+      case 6: return R6::fwd_ctas(device, cap);
       default: return R0::fwd_ctas(device, cap);
     }
   }
@@ -502,6 +523,7 @@ struct Shapes {
       case 3: return R3::bwd_ctas(device, cap);
       case 4: return R4::bwd_ctas(device, cap);
       case 5: return R5::bwd_ctas(device, cap);
+      case 6: return R6::bwd_ctas(device, cap);
       default: return R0::bwd_ctas(device, cap);
     }
   }
@@ -512,6 +534,7 @@ struct Shapes {
       case 3: return R3::fwd(a, ctas, st);
       case 4: return R4::fwd(a, ctas, st);
       case 5: return R5::fwd(a, ctas, st);
+      case 6: return R6::fwd(a, ctas, st);
       default: return R0::fwd(a, ctas, st);
     }
   }
@@ -522,6 +545,7 @@ struct Shapes {
       case 3: return R3::bwd(a, ctas, st);
       case 4: return R4::bwd(a, ctas, st);
       case 5: return R5::bwd(a, ctas, st);
+      case 6: return R6::bwd(a, ctas, st);
       default: return R0::bwd(a, ctas, st);
     }
   }

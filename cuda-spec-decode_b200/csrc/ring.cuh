@@ -134,24 +134,33 @@ __device__ __forceinline__ int64_t copied_end(int64_t f0, int64_t f1) {
 // Producer loop, lane 0 of the producer warp. NIN input streams of element
 // type T share the flattened index space (ring k holds stream k's stages at
 // ring + k*S*SE). A stage whose rows are all dead is posted without a copy.
-// Returns false on a wait timeout. `withhold_first` (failure-detection tests
-// only) never posts the first stage: this CTA's consumers then see their
-// bounded wait expire, which is the path under test. `trk` (or null) receives
-// the progress record. The caller retires the CTA from the queue afterwards.
+// `first` is the CTA's first block, dequeued by the caller before its
+// prologue so that the atomic's latency overlaps it. The next block is
+// dequeued only when the current block's last stage is posted, and taken up
+// after the next slot wait: the atomic's latency hides behind that wait, and
+// no CTA holds a whole unstarted block when the queue runs dry (which would
+// leave the others idle at the end). Returns false on a wait timeout.
+// `withhold_first` (failure-detection tests only) never posts the first
+// stage: this CTA's consumers then see their bounded wait expire, which is
+// the path under test. `trk` (or null) receives the progress record. The
+// caller retires the CTA from the queue afterwards.
 template <int NIN, int S, int SE, int BS, class T>
 __device__ bool ring_produce(const T* const* src, int64_t E, int64_t V, const RowBits& rb,
                              const BlockQueue& q, T* ring, uint64_t* full, uint64_t* empty,
-                             int64_t* sf0, int64_t* srow, bool withhold_first = false,
+                             int64_t* sf0, int64_t* srow, unsigned first, bool withhold_first = false,
                              RingTrack<S>* trk = nullptr) {
   constexpr int64_t BL = (int64_t)BS * SE;
-  unsigned b = q.first();
-  unsigned nb = b < q.nblocks ? q.next(b) : q.nblocks;
+  unsigned b = first, nb = q.nblocks;
+  bool have_nb = false, switch_pending = false;
   int64_t blk_end = 0, r_issue = 0;
   int k = 0;
-  if (b < q.nblocks) {
-    blk_end = min((int64_t)(b + 1) * BL, E);
-    r_issue = ((int64_t)b * BL) / V;
-  }
+  auto enter_block = [&]() {
+    if (b < q.nblocks) {
+      blk_end = min((int64_t)(b + 1) * BL, E);
+      r_issue = ((int64_t)b * BL) / V;
+    }
+  };
+  enter_block();
   bool ok = true;
   int64_t it = 0;
   for (;; ++it) {
@@ -159,6 +168,13 @@ __device__ bool ring_produce(const T* const* src, int64_t E, int64_t V, const Ro
     if (!mbar_wait(empty + slot, (uint32_t)(((it / S) & 1) ^ 1))) {
       ok = false;
       break;
+    }
+    if (switch_pending) {
+      b = nb;
+      have_nb = false;
+      switch_pending = false;
+      k = 0;
+      enter_block();
     }
     if (trk) trk->sblk[slot] = b;
     if (withhold_first && it == 0) continue;  // neither copy nor arrive: full[0] stays incomplete
@@ -170,6 +186,10 @@ __device__ bool ring_produce(const T* const* src, int64_t E, int64_t V, const Ro
     }
     const int64_t f0 = (int64_t)b * BL + (int64_t)k * SE;
     const int64_t f1 = min(f0 + SE, blk_end);
+    if (f1 == blk_end) {  // the block's last stage: dequeue the next block now
+      nb = q.next(b);
+      have_nb = true;
+    }
     sf0[slot] = f0;
     while ((r_issue + 1) * V <= f0) ++r_issue;
     srow[slot] = r_issue;
@@ -184,21 +204,12 @@ __device__ bool ring_produce(const T* const* src, int64_t E, int64_t V, const Ro
     } else {
       mbar_arrive(full + slot);
     }
-    if (f1 == blk_end) {
-      b = nb;
-      k = 0;
-      if (b < q.nblocks) {
-        nb = q.next(b);
-        blk_end = min((int64_t)(b + 1) * BL, E);
-        r_issue = ((int64_t)b * BL) / V;
-      }
-    } else {
-      ++k;
-    }
+    if (f1 == blk_end) switch_pending = true;
+    else ++k;
   }
   if (trk) {
     trk->held[0] = b;
-    trk->held[1] = nb;
+    trk->held[1] = have_nb ? nb : q.nblocks;
     trk->posted = it;
   }
   return ok;
@@ -223,15 +234,17 @@ struct RingSmem {
   unsigned bits[kMaxRowWords];
 };
 
-// Minimum CTAs per SM a bf16 ring kernel is compiled for (it caps the
-// registers per thread): as many rings as fit in shared memory, at most 3 for
-// 160-thread CTAs and 2 for larger ones. Float kernels are compiled without a
-// minimum.
+// Minimum CTAs per SM a ring kernel is compiled for (it caps the registers
+// per thread): as many rings as fit in shared memory, at most 4 for CTAs of
+// up to 160 threads and 2 for larger ones. Float kernels are compiled without
+// a minimum unless 4 rings fit (their default allocation would otherwise
+// leave room for 3).
 template <int NC, int NIN, int S, int SE, class T>
 constexpr int ring_min_ctas() {
   constexpr int by_smem = int((227 * 1024) / sizeof(RingSmem<NIN, S, SE, T>));
-  constexpr int by_threads = (NC + 1) * 32 <= 160 ? 3 : 2;
-  return sizeof(T) == 2 ? (by_smem < by_threads ? (by_smem < 1 ? 1 : by_smem) : by_threads) : 1;
+  constexpr int by_threads = (NC + 1) * 32 <= 160 ? 4 : 2;
+  constexpr int m = by_smem < by_threads ? (by_smem < 1 ? 1 : by_smem) : by_threads;
+  return (sizeof(T) == 2 || m >= 4) ? m : 1;
 }
 
 template <int NIN, int S, int SE, class T>
@@ -319,9 +332,10 @@ __device__ __forceinline__ void warp_lse_smem(const float* sb, int a, int b, flo
 }
 
 // Accumulates a full sub-range of KSUB floats (KSUB / 128 float4 per lane):
-// all loads first, one max, one rescale, then the exponentials.
+// all loads first, one max, then (the stage released to the producer when
+// `empty` is given) one rescale and the exponentials from registers.
 template <int KSUB>
-__device__ __forceinline__ void warp_lse_full(const float* sb, float& m, float& s) {
+__device__ __forceinline__ void warp_lse_full(const float* sb, float& m, float& s, uint64_t* empty = nullptr) {
   constexpr int U = KSUB / 128;
   static_assert(KSUB % 128 == 0, "sub-range must be a multiple of 128 floats");
   const int lane = threadIdx.x & 31;
@@ -332,6 +346,7 @@ __device__ __forceinline__ void warp_lse_full(const float* sb, float& m, float& 
   float cm = max4(v[0]);
 #pragma unroll
   for (int u = 1; u < U; ++u) cm = fmaxf(cm, max4(v[u]));
+  if (empty) release_stage(empty, cm);
   if (cm > m) {
     s *= exp_shift(m, cm);
     m = cm;
@@ -390,7 +405,7 @@ __device__ __forceinline__ void warp_lse_smem(const bf16_t* sb, int a, int b, fl
 // the max is taken on the packed words, each element is widened once, and the
 // arithmetic runs on fp32 pairs.
 template <int KSUB>
-__device__ __forceinline__ void warp_lse_full(const bf16_t* sb, float& m, float& s) {
+__device__ __forceinline__ void warp_lse_full(const bf16_t* sb, float& m, float& s, uint64_t* empty = nullptr) {
   constexpr int U = KSUB / 256;
   static_assert(KSUB % 256 == 0, "sub-range must be a multiple of 256 bf16");
   const int lane = threadIdx.x & 31;
@@ -402,6 +417,7 @@ __device__ __forceinline__ void warp_lse_full(const bf16_t* sb, float& m, float&
 #pragma unroll
   for (int u = 1; u < U; ++u) mx = bmax2(mx, bmax8(v[u]));
   const float cm = fmaxf(bf16_lo(mx), bf16_hi(mx));
+  if (empty) release_stage(empty, cm);
   if (cm > m) {
     s *= exp_shift(m, cm);
     m = cm;

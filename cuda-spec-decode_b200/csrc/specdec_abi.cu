@@ -57,6 +57,8 @@ int current_device() {
 // default shape); shapes 10..14 force the 128-bit-load kernels, variant
 // shape - 10.
 constexpr int kLdgShapeBase = 10;
+// highest ring shape per kernel id (D-PACE fwd/bwd have shape 6, DFlash up to 5)
+constexpr int kMaxRingShape[4] = {6, 6, 5, 5};
 
 bool has_ring_path(int kernel) { return kernel >= 0 && kernel <= 3; }
 
@@ -261,7 +263,7 @@ const char* specdec_status_string(int code) {
 
 int specdec_set_launch_shape(int32_t kernel, int32_t shape, int32_t ctas_per_sm) {
   if (kernel < 0 || kernel > 3) return fail(SPECDEC_ERR_ARGUMENT, "unknown kernel id %d", kernel);
-  if (shape < 0 || (shape > 5 && shape < kLdgShapeBase) || shape > kLdgShapeBase + 4)
+  if (shape < 0 || (shape > kMaxRingShape[kernel] && shape < kLdgShapeBase) || shape > kLdgShapeBase + 4)
     return fail(SPECDEC_ERR_ARGUMENT, "unknown launch shape %d", shape);
   if (ctas_per_sm < 0 || ctas_per_sm > 32)
     return fail(SPECDEC_ERR_ARGUMENT, "ctas_per_sm must be in [0, 32], got %d", ctas_per_sm);

@@ -112,33 +112,17 @@ __device__ __forceinline__ void st_stream_u4(void* p, uint4 v) {
 }
 
 // ---------------------------------------------------------------------------
-// Packed fp32 pairs (sm_100 add/sub/mul/fma.f32x2): two IEEE round-to-nearest
+// Packed fp32 pairs (sm_100 FADD2 / FMUL2 / FFMA2 through the compiler's
+// __fadd2_rn / __fmul2_rn / __ffma2_rn builtins): two IEEE round-to-nearest
 // operations per issued instruction, bitwise equal to the scalar forms. The
 // bf16 kernels move two elements per byte of fp32 data, so their instruction
 // issue rate, not MUFU or HBM, is what the pairing relieves.
 // ---------------------------------------------------------------------------
-#define SPECDEC_F32X2_OP(name, op)                                                              \
-  __device__ __forceinline__ float2 name(float2 a, float2 b) {                                  \
-    float2 r;                                                                                   \
-    asm("{\n\t.reg .b64 A, B, D;\n\tmov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\t" op \
-        " D, A, B;\n\tmov.b64 {%0, %1}, D;\n\t}"                                              \
-        : "=f"(r.x), "=f"(r.y)                                                                  \
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));                                              \
-    return r;                                                                                   \
-  }
-SPECDEC_F32X2_OP(fadd2, "add.rn.f32x2")
-SPECDEC_F32X2_OP(fsub2, "sub.rn.f32x2")
-SPECDEC_F32X2_OP(fmul2, "mul.rn.f32x2")
-#undef SPECDEC_F32X2_OP
-
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-  float2 r;
-  asm("{\n\t.reg .b64 A, B, C, D;\n\tmov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\t"
-      "mov.b64 C, {%6, %7};\n\tfma.rn.f32x2 D, A, B, C;\n\tmov.b64 {%0, %1}, D;\n\t}"
-      : "=f"(r.x), "=f"(r.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return r;
-}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+// a - b is a + (-b) exactly (IEEE subtraction is defined so)
+__device__ __forceinline__ float2 fsub2(float2 a, float2 b) { return __fadd2_rn(a, make_float2(-b.x, -b.y)); }
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 
 // The two elements of a bf16x2 word as an fp32 pair (low half first).
 __device__ __forceinline__ float2 bf16x2_f32(uint32_t w) { return make_float2(bf16_lo(w), bf16_hi(w)); }

@@ -275,8 +275,9 @@ int specdec_dflash_backward_bf16(const uint16_t* logits, const uint16_t* target_
 
 /*
  * Selects a kernel variant and caps resident CTAs per SM (0 = occupancy
- * limit) for one kernel, process-wide. Shapes 0..5 are warp-specialized
- * bulk-copy ring variants (used when the streamed pointers are 16-byte
+ * limit) for one kernel, process-wide. Shapes 0..5 (0..6 for the D-PACE
+ * kernels) are warp-specialized bulk-copy ring variants (used when the
+ * streamed pointers are 16-byte
  * aligned; otherwise the 128-bit-load kernels run with their default shape);
  * 10..14 force the 128-bit-load kernels, variant shape - 10 (bf16 entry
  * points, which have only the ring kernels, then use ring shape 0). Workspace
