@@ -454,7 +454,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, (KIND == kKi
   }
   __syncthreads();
   if (sm.trk.timeout) ring_poison<T, S>(dst, E, BL, q.nblocks, sm.trk, NC, q.dynamic ? 0u : gridDim.x);
-  if (threadIdx.x == 0) bwd_finish(q, a, sm.trk.timeout != 0);
+  if (warp == 0) bwd_finish(q, a, sm.trk.timeout != 0);
 }
 
 // Stages per queue block of the backward kernels: small blocks (the backward

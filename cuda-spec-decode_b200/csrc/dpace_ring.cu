@@ -249,8 +249,10 @@ __global__ void __launch_bounds__(1024) dpace_finalize_kernel(const __grid_const
     if (lane == 0) {
       if (a.loss_n) a.loss_n[n] = loss_n;
       a.seq_loss[n] = loss_n;
-      __threadfence();
-      last = (atomicAdd(a.done_cnt, 1u) + 1 == (unsigned)a.N);
+      if (!a.defer_loss) {  // deferred: the chained backward sums seq_loss when it retires
+        __threadfence();
+        last = (atomicAdd(a.done_cnt, 1u) + 1 == (unsigned)a.N);
+      }
     }
     last = __shfl_sync(kFullMask, last, 0);
     if (last) {
@@ -430,7 +432,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
   }
   __syncthreads();
   if (sm.trk.timeout) ring_poison<T, S>(dst, E, BL, q.nblocks, sm.trk, NC, q.dynamic ? 0u : gridDim.x);
-  if (threadIdx.x == 0) bwd_finish(q, a, sm.trk.timeout != 0);
+  if (warp == 0) bwd_finish(q, a, sm.trk.timeout != 0);
 }
 
 // Stages per queue block of the backward kernels. The backward has no

@@ -21,6 +21,7 @@
 
 #include "bulk_copy.cuh"
 #include "specdec_common.cuh"
+#include "specdec_internal.h"
 
 namespace specdec {
 
@@ -432,22 +433,41 @@ __device__ __forceinline__ void warp_lse_full(const bf16_t* sb, float& m, float&
   s += acc[0].x + acc[0].y;
 }
 
-// End of a backward CTA (thread 0, after its poison writes, if any): folds
-// this CTA's timeout into the launch's flag word and retires it; the last CTA
-// to retire turns the flag into the status word (SPECDEC_ERR_CUDA = a wait
-// expired somewhere; otherwise 0 unless `status_merge`, which only ever
-// raises the word) and clears the flag. Without counters (no retire count) a
-// timed-out CTA writes the status itself, over the 0 the entry point stored.
+// End of a backward CTA (warp 0, after the CTA's poison writes, if any):
+// folds this CTA's timeout into the launch's flag word and retires it; the
+// last CTA to retire turns the flag into the status word (SPECDEC_ERR_CUDA =
+// a wait expired somewhere; otherwise 0 unless `status_merge`, which only
+// ever raises the word) and clears the flag. Without counters (no retire
+// count) a timed-out CTA writes the status itself, over the 0 the entry point
+// stored. With a loss epilogue (a forward_backward call whose finalize left
+// the sum to this kernel) the last CTA also sums the per-sequence losses in
+// index order -- the finalize's own arithmetic, so the same bits -- and
+// writes the loss and the whole status word of the call.
 template <class Args>
 __device__ __forceinline__ void bwd_finish(const BlockQueue& q, const Args& a, bool timeout) {
-  if (timeout && a.flag) atomicOr(a.flag, 2);
-  if (q.retire()) {
-    const int f = a.flag ? atomicExch(a.flag, 0) : 0;
-    if (a.status) {
-      if (f & 2) a.status[0] = kStatusTimeout;
-      else if (!a.status_merge) a.status[0] = 0;
+  const int lane = threadIdx.x & 31;
+  int last = 0;
+  if (lane == 0) {
+    if (timeout && a.flag) atomicOr(a.flag, 2);
+    last = q.retire() ? 1 : 0;
+  }
+  last = __shfl_sync(kFullMask, last, 0);
+  if (last) {
+    float total = 0.f;
+    if (a.loss) total = warp_sum_l2(a.seq_loss, a.nseq);
+    if (lane == 0) {
+      const int fb = a.flag ? atomicExch(a.flag, 0) : 0;
+      if (a.loss) {
+        const int f = atomicExch(a.fwd_flag, 0);
+        a.loss[0] = (f & 2) ? __int_as_float(0x7fc00000) : total / (float)a.n_global;
+        if (a.status)
+          a.status[0] = ((f | fb) & 2) ? kStatusTimeout : ((f & 1) ? kStatusTargetRange : 0);
+      } else if (a.status) {
+        if (fb & 2) a.status[0] = kStatusTimeout;
+        else if (!a.status_merge) a.status[0] = 0;
+      }
     }
-  } else if (q.retired == nullptr && timeout && a.status) {
+  } else if (lane == 0 && q.retired == nullptr && timeout && a.status) {
     a.status[0] = kStatusTimeout;
   }
 }

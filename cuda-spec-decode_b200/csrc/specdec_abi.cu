@@ -321,10 +321,18 @@ size_t specdec_backward_counter_bytes(void) { return 256; }
 
 namespace {
 
+// Where a forward whose finalize deferred its global loss keeps what the
+// chained backward needs to finish it.
+struct DeferredLoss {
+  const float* seq_loss = nullptr;
+  int* flag = nullptr;
+};
+
 int dpace_forward_impl(int dtype, const void* logits, const int64_t* targets, const float* mask, int64_t N,
                        int32_t B, int64_t V, float alpha, int32_t loss_type, int64_t n_global, float* loss,
                        float* loss_n, float* lse, float* scale, int32_t* status, void* scratch,
-                       size_t scratch_bytes, void* counters, size_t counter_bytes, void* stream) {
+                       size_t scratch_bytes, void* counters, size_t counter_bytes, void* stream,
+                       DeferredLoss* defer = nullptr) {
   const int rc = specdec::dpace_forward_check(dtype, logits, targets, N, B, V, alpha, loss_type, n_global, loss,
                                               lse, scale);
   if (rc != SPECDEC_OK) return rc;
@@ -381,6 +389,11 @@ int dpace_forward_impl(int dtype, const void* logits, const int64_t* targets, co
   a.q_dynamic = g_static_queue.load() ? 0 : 1;
   a.seq_cnt = cnt + kDpaceSeqWords;
   a.withhold_stage = tma ? take_withhold_stage() : 0;
+  a.defer_loss = (defer != nullptr && tma) ? 1 : 0;
+  if (defer) {
+    defer->seq_loss = a.defer_loss ? a.seq_loss : nullptr;
+    defer->flag = a.defer_loss ? a.flag : nullptr;
+  }
   a.pt = pt;
   const cudaError_t e =
       tma ? dpace_fwd_ring_launch(dtype, shape, a, (int)pt.grid, st) : dpace_fwd_launch(shape, a, st);
@@ -393,7 +406,8 @@ int dpace_forward_impl(int dtype, const void* logits, const int64_t* targets, co
 int dpace_backward_impl(int dtype, const void* logits, const int64_t* targets, const float* lse,
                         const float* scale, const float* dloss, void* dlogits, int64_t N, int32_t B, int64_t V,
                         int32_t* status, void* counters, size_t counter_bytes, void* stream,
-                        bool status_merge = false, bool chained = false, const float* mask = nullptr) {
+                        bool status_merge = false, bool chained = false, const float* mask = nullptr,
+                        const DeferredLoss* defer = nullptr, float* loss = nullptr, int64_t n_global = 1) {
   if (B < 1 || B > 32) return fail(SPECDEC_ERR_ARGUMENT, "kernel configured for block_size <= 32 (B=%d)", B);
   if (N < 0 || V < 0) return fail(SPECDEC_ERR_ARGUMENT, "negative shape");
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -440,6 +454,15 @@ int dpace_backward_impl(int dtype, const void* logits, const int64_t* targets, c
   a.mask_liveness = a.chained;
   a.live_mask = mask;
   a.withhold_stage = tma ? take_withhold_stage() : 0;
+  if (defer && defer->seq_loss && !(tma && have_cnt))
+    return fail(SPECDEC_ERR_CUDA, "internal: a deferred loss needs the ring backward with counters");
+  if (defer && defer->seq_loss) {  // finish the forward's loss when retiring
+    a.loss = loss;
+    a.seq_loss = defer->seq_loss;
+    a.nseq = N;
+    a.n_global = n_global;
+    a.fwd_flag = defer->flag;
+  }
   const int shape = tma ? ring_shape(SPECDEC_KERNEL_DPACE_BWD, dtype) : kernel_shape(SPECDEC_KERNEL_DPACE_BWD, false);
   a.pt = tma ? ring_partition(N * B, V, dpace_ring_block_elems(dtype, shape), units)
              : make_partition(N * B, V, units, kMinChunk);
@@ -476,8 +499,14 @@ int dpace_forward_backward_impl(int dtype, const void* logits, const int64_t* ta
     return fail(SPECDEC_ERR_ARGUMENT, "misaligned pointer (scratch needs 256 B, counters 16 B)");
   const bool ptrs16 = aligned(logits, 16) && aligned(dlogits, 16);
   if (dtype == kDtypeBF16 && !ptrs16) return fail(SPECDEC_ERR_ARGUMENT, "bf16 logits and dlogits must be 16-byte aligned");
+  // When both launches take the ring kernels, the finalize leaves the global
+  // loss sum (and the status word) to the backward's last CTA, so the
+  // backward, which waits for the finalize, is released sooner.
+  const bool bwd_ring = dtype == kDtypeBF16 || use_tma(SPECDEC_KERNEL_DPACE_BWD, ptrs16);
+  DeferredLoss defer;
   const int rc = dpace_forward_impl(dtype, logits, targets, mask, N, B, V, alpha, loss_type, n_global, loss, loss_n,
-                                    lse, scale, status, scratch, scratch_bytes, counters, counter_bytes, stream);
+                                    lse, scale, status, scratch, scratch_bytes, counters, counter_bytes, stream,
+                                    bwd_ring ? &defer : nullptr);
   if (rc != SPECDEC_OK) return rc;
   // The backward follows the finalize this call just enqueued, so it is
   // chained to it (programmatic dependent launch): its CTAs become resident
@@ -487,7 +516,7 @@ int dpace_forward_backward_impl(int dtype, const void* logits, const int64_t* ta
   unsigned* bcnt = static_cast<unsigned*>(counters) + kDpaceBwdWords;
   return dpace_backward_impl(dtype, logits, targets, lse, scale, nullptr, dlogits, N, B, V, status, bcnt,
                              counter_bytes - kDpaceBwdWords * sizeof(unsigned), stream, /*status_merge=*/true,
-                             /*chained=*/true, mask);
+                             /*chained=*/true, mask, &defer, loss, n_global);
 }
 
 }  // namespace

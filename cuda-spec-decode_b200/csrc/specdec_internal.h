@@ -54,6 +54,7 @@ struct DpaceFwdArgs {
   int q_dynamic;           // 1: atomic block queue, 0: static interleave
   int nc;                  // partials per (row, slot): consumer warps (ring) or 1
   int withhold_stage;      // failure-detection tests: CTA 0 never posts its first stage
+  int defer_loss = 0;      // 1: the chained backward sums seq_loss into loss and writes status
   Partition pt;            // ring kernel: chunk = block length, pmax from it
 };
 
@@ -64,16 +65,22 @@ struct DpaceBwdArgs {
   const float* scale;
   const float* dloss;      // [1] upstream gradient, or null for 1
   void* dlogits;           // element type of logits
-  int* status;             // [1] or null: 0, or kStatusTimeout if a wait expired
-  int status_merge;        // 1: only ever raise *status (it holds the forward's word)
+  int* status = nullptr;   // [1] or null: 0, or kStatusTimeout if a wait expired
+  int status_merge = 0;    // 1: only ever raise *status (it holds the forward's word)
   int* flag;               // [1] or null (no counters): bit 2 set if a copy wait timed out
   unsigned* q_ctr;         // ring kernel block queue word
   unsigned* q_retired;     // null: no counters (static interleave, no retire count)
   int q_dynamic;
-  int mask_liveness;       // 1: rows are read iff live_mask > 0 (null: all), known before lse/scale
-  const float* live_mask;  // [N, B] position mask, with mask_liveness
-  int chained;             // 1: launched with programmatic dependent launch after the finalize
-  int withhold_stage;      // failure-detection tests: CTA 0 never posts its first stage
+  int mask_liveness = 0;   // 1: rows are read iff live_mask > 0 (null: all), known before lse/scale
+  const float* live_mask = nullptr;  // [N, B] position mask, with mask_liveness
+  int chained = 0;         // 1: launched with programmatic dependent launch after the finalize
+  int withhold_stage = 0;  // failure-detection tests: CTA 0 never posts its first stage
+  // loss epilogue of a forward whose finalize deferred it (null loss: none)
+  float* loss = nullptr;   // [1] sum_n seq_loss[n] / n_global, NaN if the forward timed out
+  const float* seq_loss = nullptr;  // [nseq] the finalize's per-sequence losses
+  int64_t nseq = 0;
+  int64_t n_global = 1;
+  int* fwd_flag = nullptr; // the forward's flag word: bit 1 target out of range, bit 2 timeout
   Partition pt;
 };
 
@@ -120,13 +127,19 @@ struct DflashBwdArgs {
   const float* dloss;
   void* dlogits;               // element type of logits
   int kind;
-  int* status;                 // [1] or null: 0, or kStatusTimeout if a wait expired
-  int status_merge;            // 1: only ever raise *status
+  int* status = nullptr;       // [1] or null: 0, or kStatusTimeout if a wait expired
+  int status_merge = 0;        // 1: only ever raise *status
   int* flag;                   // [1] or null (no counters)
   unsigned* q_ctr;             // ring kernel block queue word
   unsigned* q_retired;         // null: no counters (static interleave, no retire count)
   int q_dynamic;
-  int withhold_stage;          // failure-detection tests: CTA 0 never posts its first stage
+  int withhold_stage = 0;      // failure-detection tests: CTA 0 never posts its first stage
+  // no loss epilogue (the DFlash forward always completes its own loss)
+  float* loss = nullptr;
+  const float* seq_loss = nullptr;
+  int64_t nseq = 0;
+  int64_t n_global = 1;
+  int* fwd_flag = nullptr;
   Partition pt;
 };
 
