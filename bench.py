@@ -40,6 +40,11 @@ import threading
 import time
 
 REPO = os.path.dirname(os.path.abspath(__file__))
+if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+    # communicator set-up lines (rank count per communicator) in the log; set
+    # before torch loads NCCL, which reads them once
+    os.environ.setdefault("NCCL_DEBUG", "INFO")
+    os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
 sys.path.insert(0, os.path.join(REPO, "cuda-spec-decode_b200"))
 sys.path.insert(0, REPO)
 
@@ -325,6 +330,35 @@ class Timing:
         local = a.elapsed_time(b) / steps
         return self.max(local), local
 
+    def graphs(self, call, n_sets):
+        """CUDA graphs of call(s) (the library launches of one step on input
+        set s, returning its loss tensor), one per input set, captured on a
+        side stream after eager warm-up calls there (so the workspace and the
+        status words for that stream exist before capture). Returns
+        step(i) = replay graph i % n_sets, then start the loss reduction
+        (eager: no collective inside a graph)."""
+        cap = torch.cuda.Stream(self.dev)
+        cap.wait_stream(self.stream)
+        with torch.cuda.stream(cap):
+            for i in range(3 * n_sets):
+                call(i % n_sets)
+        self.stream.wait_stream(cap)
+        torch.cuda.synchronize(self.dev)
+        gs, outs = [], []
+        for s_ in range(n_sets):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                outs.append(call(s_))
+            gs.append(g)
+        torch.cuda.synchronize(self.dev)
+
+        def step(i):
+            gs[i % n_sets].replay()
+            self.reduce(outs[i % n_sets])
+
+        step.graphs = gs  # kept alive with the step function
+        return step
+
     def split(self, fwd, bwd, steps):
         """A second, instrumented pass: events around the forward call and the
         backward call of each step (separate calls, so no chaining between
@@ -387,14 +421,13 @@ def time_dflash(args, T, n_global, dtype=torch.float32, steps=None):
         x, y = sets[i & 1]
         ops.dflash_backward(x, y, st[0], st[1], st[2], None, None, 0, out=grad)
 
-    def step(i):
+    def call(i):  # one step's launches: forward then backward (dloss = 1)
         loss, st = fwd(i)
-        T.reduce(loss)
         bwd(i, st)
-        T.settle()
+        return loss
 
     K = args.dflash_steps if steps is None else steps
-    ms, ms_local = T.loop(step, K)
+    ms, ms_local = T.loop(T.graphs(call, 2) if args.graphs else (lambda i: T.reduce(call(i))), K)
     f, g = T.split(fwd, bwd, K)
     live = 15.0 / 16.0
     peak, _ = hbm_peak()
@@ -442,11 +475,13 @@ def dpace_leg(args, T, N, B, V, sigma, kmax, n_global, steps, dtype=torch.float3
     live = statistics.mean(float(m.mean()) for _, _, m in sets)
     grad = torch.empty(N, B, V, device=dev, dtype=dtype)
 
-    def step(i):
+    def call(i):  # one step's launches: specdec_dpace_forward_backward
         x, t, m = sets[i % sets_n]
         loss, _, _, _, _ = ops.dpace_forward_backward(x, t, m, 0.5, 0, n_global=n_global, validate=False,
                                                       out=grad)
-        T.reduce(loss)
+        return loss
+
+    step = T.graphs(call, sets_n) if args.graphs else (lambda i: T.reduce(call(i)))
 
     def fwd(i):
         x, t, m = sets[i % sets_n]
@@ -817,7 +852,9 @@ def run_ours(args):
                        "l2": "two alternating input sets, each 525 MB > 126 MB L2",
                        "bytes_model": "12*N*B*V per GPU-step",
                        "step": "specdec_dpace_forward_backward through the C ABI (library level: the "
-                               "public API's 4-byte status read-back is timed in e2e)"},
+                               "public API's 4-byte status read-back is timed in e2e)",
+                       "launch": "one CUDA graph per step (the step's 3 kernel launches), replayed"
+                                 if args.graphs else "eager launches from Python"},
             "rows_per_s": rep["rows_per_s"],
             "moved_bytes_per_step": rep["moved_bytes_per_step"],
             "pct_of_hbm_peak": rep["pct_of_hbm_peak"], "pct_basis": rep["pct_basis"],
@@ -861,6 +898,8 @@ def main(argv=None):
                    help="seconds of CPU-oracle timing per objective on rank 0 at N=1 (0 = skip)")
     p.add_argument("--c4-steps", type=int, default=10,
                    help="timed steps of the large-batch [512,32,151936] workload (0 = skip)")
+    p.add_argument("--graphs", type=int, default=1,
+                   help="timed loops replay one CUDA graph per step (1) or launch from Python (0)")
     p.add_argument("--e2e-fused", type=int, default=1,
                    help="e2e: specdec.ops.set_fused_backward (1) or the separate backward kernel (0)")
     args = p.parse_args(argv)
