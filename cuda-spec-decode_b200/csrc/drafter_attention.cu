@@ -1,0 +1,339 @@
+// Attention of the DFlash drafter on the sm_100a tensor cores (tcgen05).
+//
+// Reference behaviour: models/dflash/model.py:25-53 (DFlashAttention:
+// softmax(q k^T / sqrt(d) + mask) v per head) under the mask of
+// models/dflash/model.py:123-131 (_build_dflash_mask), applied by its
+// structure instead of a [T, T] tensor: query t < n_ctx sees keys j <= t
+// (causal context), query t >= n_ctx (a block slot) sees every key j < T.
+//
+// Layout: q, k, v, o are bf16 [B, T, H, 64] -- the projections' own layout
+// (row (b, t) holds the H heads' 64-element slices), so no transpose is
+// needed on either side. lse is fp32 [B, H, T]: the natural-log
+// log-sum-exp of each query row's scaled scores, kept for a backward.
+//
+// One CTA per (b, h, 128-query tile), 4 warps; thread i owns query row i of
+// the tile, which is TMEM lane i. Per 128-key tile:
+//   1. all threads copy the K and V tiles from global memory into shared
+//      memory in the canonical 128-byte-swizzled layout (rows of 128 bytes,
+//      16-byte chunk c of row r stored at chunk c ^ (r % 8), 8-row atoms of
+//      1024 bytes), fence them to the async proxy, barrier;
+//   2. thread 0 issues S = Q K^T as four tcgen05.mma (M 128, N 128, K 16,
+//      bf16 in, fp32 accumulate in TMEM columns 0..127) and commits them to
+//      an mbarrier;
+//   3. every thread reads its row of S from TMEM twice (32 columns at a
+//      time): the tile's masked maximum, then p = 2^(s' - m) in bf16, written
+//      to shared memory as the A operand of the next product (same swizzled
+//      layout, two 64-key atoms);
+//   4. thread 0 issues O_tile = P V as eight tcgen05.mma (M 128, N 64, K 16;
+//      V read as an MN-major operand: d contiguous) into TMEM columns
+//      128..191, and commits;
+//   5. every thread reads its row of O_tile and folds it into its register
+//      accumulator with the online-softmax rescaling.
+// The stages run one after another (the tiles are small: T ~ 528 gives at
+// most five key tiles per CTA). Every mbarrier wait is bounded; a wait that
+// expires sets *status and the CTA stops issuing work, waits (bounded) for
+// what it issued and releases its TMEM.
+#include <atomic>
+#include <cstdint>
+
+#include "bulk_copy.cuh"
+#include "specdec_common.cuh"
+#include "specdec_internal.h"
+
+namespace specdec {
+
+namespace {
+
+constexpr int kHD = 64;        // head dimension
+constexpr int kTM = 128;       // query rows per CTA (TMEM lanes)
+constexpr int kTN = 128;       // keys per tile
+constexpr int kThreads = 128;  // 4 warps
+constexpr uint32_t kTmemCols = 256;  // S: columns 0..127, O_tile: 128..191
+constexpr uint32_t kColO = 128;
+
+// Shared memory (offsets from a 1024-byte-aligned base).
+constexpr uint32_t kOffQ = 0;             // 128 rows x 128 B
+constexpr uint32_t kOffK = 16384;
+constexpr uint32_t kOffV = 32768;
+constexpr uint32_t kOffP = 49152;         // two atoms of 128 rows x 128 B
+constexpr uint32_t kOffBar = 81920;       // two mbarriers
+constexpr uint32_t kOffTmem = kOffBar + 16;
+constexpr uint32_t kSmemBytes = kOffTmem + 16 + 1024;  // + alignment slack
+
+// Byte offset of 16-byte chunk c of row r in a 128-byte-swizzled tile.
+__device__ __forceinline__ uint32_t sw128(uint32_t r, uint32_t c) { return r * 128u + (((c ^ (r & 7u)) & 7u) << 4); }
+
+// Shared-memory matrix descriptor, 128-byte swizzle: start address, leading
+// byte offset (between 64-element chunks of the contiguous dimension; used
+// by MN-major operands), stride byte offset (between 8-row atoms), version 1.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;  // descriptor version for tcgen05
+  d |= (uint64_t)2u << 61;  // 128-byte swizzle
+  return d;
+}
+
+// Instruction descriptor, kind::f16: bf16 A and B, fp32 D, M x N, majors.
+constexpr uint32_t instr_desc(int M, int N, int a_mn, int b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void st_shared_u4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// Copies rows [t0, t0 + 128) of one head of a [B, T, H, 64] bf16 tensor into
+// a swizzled shared tile (rows at or past T are zeros).
+__device__ __forceinline__ void load_tile(uint32_t tile, const bf16_t* base, int64_t row_stride, int t0, int T) {
+#pragma unroll
+  for (int j = 0; j < (kTM * 8) / kThreads; ++j) {
+    const int idx = threadIdx.x + j * kThreads;
+    const int r = idx >> 3, c = idx & 7;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (t0 + r < T) v = *reinterpret_cast<const uint4*>(base + (int64_t)(t0 + r) * row_stride + c * 8);
+    st_shared_u4(tile + sw128((uint32_t)r, (uint32_t)c), v);
+  }
+}
+
+// Waits for the phase of `bar` with the given parity; false after the limit.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity) { return mbar_wait(bar, parity); }
+
+__global__ void __launch_bounds__(kThreads, 1) dflash_attn_fwd_kernel(const bf16_t* __restrict__ q,
+                                                                      const bf16_t* __restrict__ k,
+                                                                      const bf16_t* __restrict__ v,
+                                                                      bf16_t* __restrict__ o, float* __restrict__ lse,
+                                                                      int T, int H, int n_ctx, float scale_log2,
+                                                                      int* status) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  unsigned char* gbase = smem_raw + (base - smem_u32(smem_raw));
+  uint64_t* bar_s = reinterpret_cast<uint64_t*>(gbase + kOffBar);
+  uint64_t* bar_o = bar_s + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kOffTmem);
+
+  const int warp = threadIdx.x >> 5;
+  const int bh = blockIdx.y, b = bh / H, h = bh % H;
+  const int q0 = blockIdx.x * kTM;
+  const int64_t rs = (int64_t)H * kHD;  // row stride of [B, T, H, 64]
+  const bf16_t* qb = q + (int64_t)b * T * rs + (int64_t)h * kHD;
+  const bf16_t* kb = k + (int64_t)b * T * rs + (int64_t)h * kHD;
+  const bf16_t* vb = v + (int64_t)b * T * rs + (int64_t)h * kHD;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_s, 1);
+    mbar_init(bar_o, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {  // TMEM: 256 columns for this CTA
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  load_tile(base + kOffQ, qb, rs, q0, T);
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+
+  // key range of this query tile: up to its last context row, or every key
+  // once the tile holds a block slot
+  const int q_last = min(q0 + kTM, T) - 1;
+  const int kv_end = q_last >= n_ctx ? T : q_last + 1;
+  const int row = q0 + threadIdx.x;  // this thread's query row
+  constexpr uint32_t kIdS = instr_desc(kTM, kTN, 0, 0);
+  constexpr uint32_t kIdO = instr_desc(kTM, kHD, 0, 1);
+
+  float acc[kHD];
+#pragma unroll
+  for (int i = 0; i < kHD; ++i) acc[i] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;
+  uint32_t ph = 0;
+  bool ok = true;
+
+  for (int k0 = 0; k0 < kv_end && ok; k0 += kTN) {
+    load_tile(base + kOffK, kb, rs, k0, T);
+    load_tile(base + kOffV, vb, rs, k0, T);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (threadIdx.x == 0) {  // S = Q K^T
+#pragma unroll
+      for (int kk = 0; kk < kHD / 16; ++kk)
+        umma_bf16(tmem, smem_desc(base + kOffQ + kk * 32, 16, 1024), smem_desc(base + kOffK + kk * 32, 16, 1024),
+                  kIdS, kk > 0);
+      umma_commit(bar_s);
+    }
+    if (__syncthreads_or(!wait_bar(bar_s, ph) ? 1 : 0)) {  // CTA-uniform: a wait expired
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    // pass 1: the tile's masked maximum of this row (base-2 scaled scores)
+    float mt = -INFINITY;
+#pragma unroll
+    for (int cc = 0; cc < kTN / 32; ++cc) {
+      float s[32];
+      tmem_ld32(tmem + lane_base + cc * 32, s);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int j = k0 + cc * 32 + i;
+        const bool valid = j < T && (row >= n_ctx || j <= row);
+        if (valid) mt = fmaxf(mt, s[i] * scale_log2);
+      }
+    }
+    const float m_new = fmaxf(m_run, mt);
+    const float alpha = m_run == -INFINITY ? 0.f : exp2f(m_run - m_new);
+    // pass 2: p = 2^(s' - m_new), row sum, P in bf16 to shared memory
+    float lt = 0.f;
+#pragma unroll
+    for (int cc = 0; cc < kTN / 32; ++cc) {
+      float s[32];
+      tmem_ld32(tmem + lane_base + cc * 32, s);
+      uint32_t pk[16];
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const int j = k0 + cc * 32 + i;
+        const bool v0 = j < T && (row >= n_ctx || j <= row);
+        const bool v1 = j + 1 < T && (row >= n_ctx || j + 1 <= row);
+        const float p0 = v0 ? exp2f(s[i] * scale_log2 - m_new) : 0.f;
+        const float p1 = v1 ? exp2f(s[i + 1] * scale_log2 - m_new) : 0.f;
+        lt += p0 + p1;
+        pk[i / 2] = pack_bf16x2(p0, p1);
+      }
+      const uint32_t r = (uint32_t)threadIdx.x;
+      const uint32_t atom = base + kOffP + (uint32_t)(cc >> 1) * 16384u;  // keys 0..63 | 64..127
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        const uint32_t chunk = (uint32_t)((cc & 1) * 4 + c4);  // 16-byte chunk within the 64-key atom row
+        st_shared_u4(atom + sw128(r, chunk), make_uint4(pk[4 * c4], pk[4 * c4 + 1], pk[4 * c4 + 2], pk[4 * c4 + 3]));
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (threadIdx.x == 0) {  // O_tile = P V
+#pragma unroll
+      for (int kk = 0; kk < kTN / 16; ++kk) {
+        const uint64_t ad = smem_desc(base + kOffP + (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u, 16, 1024);
+        const uint64_t bd = smem_desc(base + kOffV + (uint32_t)kk * 2048u, 16384, 1024);
+        umma_bf16(tmem + kColO, ad, bd, kIdO, kk > 0);
+      }
+      umma_commit(bar_o);
+    }
+    if (__syncthreads_or(!wait_bar(bar_o, ph) ? 1 : 0)) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+#pragma unroll
+    for (int cc = 0; cc < kHD / 32; ++cc) {
+      float ot[32];
+      tmem_ld32(tmem + lane_base + kColO + cc * 32, ot);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[cc * 32 + i] = fmaf(acc[cc * 32 + i], alpha, ot[i]);
+    }
+    l_run = fmaf(l_run, alpha, lt);
+    m_run = m_new;
+    ph ^= 1u;
+    // every thread is done with S, P, K and V before the next tile overwrites them
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
+
+  if (!ok) {
+    if (threadIdx.x == 0 && status) atomicExch(status, kStatusTimeout);
+    // wait (bounded) for the products this CTA may still have in flight
+    wait_bar(bar_s, ph);
+    wait_bar(bar_o, ph);
+  } else if (row < T) {
+    const float inv = 1.f / l_run;
+    bf16_t* orow = o + ((int64_t)b * T + row) * rs + (int64_t)h * kHD;
+#pragma unroll
+    for (int c = 0; c < kHD / 8; ++c) {
+      const float* a = acc + 8 * c;
+      *reinterpret_cast<uint4*>(orow + 8 * c) =
+          make_uint4(pack_bf16x2(a[0] * inv, a[1] * inv), pack_bf16x2(a[2] * inv, a[3] * inv),
+                     pack_bf16x2(a[4] * inv, a[5] * inv), pack_bf16x2(a[6] * inv, a[7] * inv));
+    }
+    lse[((int64_t)b * H + h) * T + row] = (m_run + log2f(l_run)) * kLn2;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+}
+
+}  // namespace
+
+// Raises the kernel's dynamic shared-memory limit once per device.
+static cudaError_t ensure_smem_limit_attn(size_t bytes) {
+  static std::atomic<unsigned long long> done{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done.load() & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(dflash_attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess) done.fetch_or(bit);
+  return e;
+}
+
+cudaError_t dflash_attn_fwd_launch(const void* q, const void* k, const void* v, void* o, float* lse, int batch, int T,
+                                   int H, int n_ctx, float scale, int* status, cudaStream_t st) {
+  const cudaError_t e = ensure_smem_limit_attn(kSmemBytes);
+  if (e != cudaSuccess) return e;
+  const dim3 grid((unsigned)((T + kTM - 1) / kTM), (unsigned)(batch * H));
+  dflash_attn_fwd_kernel<<<grid, kThreads, kSmemBytes, st>>>(
+      static_cast<const bf16_t*>(q), static_cast<const bf16_t*>(k), static_cast<const bf16_t*>(v),
+      static_cast<bf16_t*>(o), lse, T, H, n_ctx, scale * kLog2e, status);
+  return cudaGetLastError();
+}
+
+}  // namespace specdec

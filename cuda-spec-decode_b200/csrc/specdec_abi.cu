@@ -820,3 +820,81 @@ int specdec_dflash_backward_bf16(const uint16_t* logits, const uint16_t* target_
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// DFlash drafter layers
+// ---------------------------------------------------------------------------
+
+extern "C" {
+
+int specdec_rmsnorm_forward(const void* x, const float* weight, void* y, float* rstd, int64_t rows, int32_t D,
+                            float eps, int32_t dtype, void* stream) {
+  if (rows < 0 || D < 1) return fail(SPECDEC_ERR_ARGUMENT, "bad shape rows=%lld D=%d", (long long)rows, D);
+  if (dtype != kDtypeF32 && dtype != kDtypeBF16) return fail(SPECDEC_ERR_ARGUMENT, "unknown dtype %d", dtype);
+  if (!(eps >= 0.f)) return fail(SPECDEC_ERR_VALUE, "eps must be >= 0, got %g", (double)eps);
+  if (rows == 0) return ok();
+  if (!x || !weight || !y) return fail(SPECDEC_ERR_ARGUMENT, "null input or output pointer");
+  const int dev = current_device();
+  if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return fail(SPECDEC_ERR_CUDA, "device query failed");
+  const int64_t want = (rows + 7) / 8;  // 8 rows (one per warp) per CTA and round
+  const int ctas = (int)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
+  const cudaError_t e = rmsnorm_fwd_launch(dtype, x, weight, y, rstd, rows, D, eps, ctas,
+                                           static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "rmsnorm forward launch");
+}
+
+size_t specdec_rmsnorm_workspace_bytes(int64_t rows, int32_t D, int device) {
+  if (rows <= 0 || D <= 0) return 256;
+  return align256((size_t)rmsnorm_bwd_ctas(rows, device) * (size_t)D * sizeof(float));
+}
+
+int specdec_rmsnorm_backward(const void* x, const float* weight, const float* rstd, const void* dy, void* dx,
+                             float* dweight, int64_t rows, int32_t D, int32_t dtype, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  if (rows < 0 || D < 1) return fail(SPECDEC_ERR_ARGUMENT, "bad shape rows=%lld D=%d", (long long)rows, D);
+  if (dtype != kDtypeF32 && dtype != kDtypeBF16) return fail(SPECDEC_ERR_ARGUMENT, "unknown dtype %d", dtype);
+  if (rmsnorm_bwd_warps(D) < 1) return fail(SPECDEC_ERR_ARGUMENT, "D=%d too large for the backward", D);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (rows == 0) {
+    if (!dweight) return fail(SPECDEC_ERR_ARGUMENT, "null dweight");
+    const cudaError_t e = cudaMemsetAsync(dweight, 0, (size_t)D * sizeof(float), st);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "cudaMemsetAsync");
+  }
+  if (!x || !weight || !rstd || !dy || !dx || !dweight || !workspace)
+    return fail(SPECDEC_ERR_ARGUMENT, "null input, output or workspace pointer");
+  const int dev = current_device();
+  if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
+  const int ctas = rmsnorm_bwd_ctas(rows, dev);
+  if (ctas <= 0) return fail(SPECDEC_ERR_CUDA, "device query failed");
+  const size_t need = (size_t)ctas * (size_t)D * sizeof(float);
+  if (workspace_bytes < need) return fail(SPECDEC_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
+  const cudaError_t e = rmsnorm_bwd_launch(dtype, x, weight, rstd, dy, dx, dweight, static_cast<float*>(workspace),
+                                           rows, D, ctas, st);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "rmsnorm backward launch");
+}
+
+int specdec_dflash_attention_forward(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* o,
+                                     float* lse, int32_t batch, int32_t T, int32_t heads, int32_t head_dim,
+                                     int32_t n_ctx, float scale, int32_t* status, void* stream) {
+  if (head_dim != 64) return fail(SPECDEC_ERR_ARGUMENT, "head_dim must be 64, got %d", head_dim);
+  if (batch < 0 || T < 0 || heads < 1) return fail(SPECDEC_ERR_ARGUMENT, "bad shape");
+  if (n_ctx < 0 || n_ctx > T) return fail(SPECDEC_ERR_ARGUMENT, "n_ctx must be in [0, T] (n_ctx=%d, T=%d)", n_ctx, T);
+  if ((int64_t)batch * heads > 65535) return fail(SPECDEC_ERR_ARGUMENT, "batch * heads must be <= 65535");
+  if (!(scale > 0.f)) return fail(SPECDEC_ERR_VALUE, "scale must be > 0");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (status) {
+    const cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int32_t), st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+  }
+  if (batch == 0 || T == 0) return ok();
+  if (!q || !k || !v || !o || !lse) return fail(SPECDEC_ERR_ARGUMENT, "null input or output pointer");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(o, 16))
+    return fail(SPECDEC_ERR_ARGUMENT, "q, k, v and o must be 16-byte aligned");
+  const cudaError_t e = dflash_attn_fwd_launch(q, k, v, o, lse, batch, T, heads, n_ctx, scale, status, st);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "attention forward launch");
+}
+
+}  // extern "C"

@@ -171,6 +171,19 @@ cudaError_t dflash_bwd_ring_launch(int dtype, int shape, const DflashBwdArgs& a,
 // In-place dloss scaling of a gradient (dpace_scale.cu).
 cudaError_t scale_inplace_launch(int dtype, void* x, int64_t n, const float* factor, int ctas, cudaStream_t st);
 
+// RMSNorm of the drafter (drafter_norm.cu).
+int rmsnorm_bwd_ctas(int64_t rows, int device);
+int rmsnorm_bwd_warps(int D);
+cudaError_t rmsnorm_fwd_launch(int dtype, const void* x, const float* w, void* y, float* rstd, int64_t rows, int D,
+                               float eps, int ctas, cudaStream_t st);
+cudaError_t rmsnorm_bwd_launch(int dtype, const void* x, const float* w, const float* rstd, const void* dy,
+                               void* dx, float* dw, float* part, int64_t rows, int D, int ctas, cudaStream_t st);
+
+// Attention of the drafter on the tensor cores (drafter_attention.cu):
+// bf16 q/k/v/o [B, T, H, 64], lse fp32 [B, H, T].
+cudaError_t dflash_attn_fwd_launch(const void* q, const void* k, const void* v, void* o, float* lse, int batch, int T,
+                                   int H, int n_ctx, float scale, int* status, cudaStream_t st);
+
 // Sets the calling thread's specdec_last_error() text.
 void set_last_error(const char* msg);
 

@@ -11,17 +11,32 @@ Architecture (model.py:76-150): target features -> proj_in -> append
 ``block_size`` trainable slot queries -> pre-RMSNorm transformer layers under
 a mask where context tokens are causal and block tokens see every token ->
 RMSNorm -> proj_out -> optional RMSNorm -> frozen verifier lm_head ->
-[batch, block_size, V] logits. Attention runs through
-F.scaled_dot_product_attention; the mask is applied by its structure (a
-causal attention over the context plus an unmasked one for the block
-queries), so the fused SDPA kernels run without a [T, T] mask. Everything
-here is plain torch (the loss is the hot path, not the drafter).
+[batch, block_size, V] logits. The mask is applied by its structure (the
+context causal, the block queries over every token), never as a [T, T]
+tensor. Layers on this library's kernels (specdec.drafter): the RMSNorms
+(fp32 or bf16 activations) and, for bf16 q/k/v with 64-dim heads (e.g.
+under bf16 autocast), the attention forward on the tensor cores; otherwise
+attention runs through F.scaled_dot_product_attention (a causal attention
+over the context plus an unmasked one for the block queries). GEMMs are
+cuBLAS (nn.Linear).
 """
 from __future__ import annotations
 
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
+
+from specdec import drafter as _kernels
+
+
+class RMSNorm(nn.RMSNorm):
+    """torch.nn.RMSNorm (same parameters and state-dict keys) whose forward
+    runs the library's RMSNorm kernels on CUDA tensors."""
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if len(self.normalized_shape) == 1 and _kernels.rms_norm_supported(x, self.weight):
+            return _kernels.rms_norm(x, self.weight, self.eps)
+        return super().forward(x)
 
 
 class DFlashAttention(nn.Module):
@@ -52,6 +67,13 @@ class DFlashAttention(nn.Module):
         over the context; the block queries over all keys), which the fused
         SDPA kernels handle without reading a [T, T] mask."""
         b, s, _ = x.shape
+        if n_ctx is not None and attn_mask is None:
+            qs = self.q_proj(x).view(b, s, self.num_heads, self.head_dim)
+            if _kernels.attention_supported(qs):  # [b, s, heads, dim]: the kernels' layout
+                ks = self.k_proj(x).view(b, s, self.num_heads, self.head_dim)
+                vs = self.v_proj(x).view(b, s, self.num_heads, self.head_dim)
+                y = _kernels.dflash_attention(qs, ks.to(qs.dtype), vs.to(qs.dtype), n_ctx)
+                return self.out_proj(y.reshape(b, s, self.d_model))
         q, k, v = self._heads(self.q_proj(x)), self._heads(self.k_proj(x)), self._heads(self.v_proj(x))
         if n_ctx is not None and attn_mask is None:
             y_ctx = F.scaled_dot_product_attention(q[:, :, :n_ctx], k[:, :, :n_ctx], v[:, :, :n_ctx],
@@ -69,9 +91,9 @@ class DFlashTransformerLayer(nn.Module):
 
     def __init__(self, d_model: int, num_heads: int, d_ffn: int):
         super().__init__()
-        self.norm1 = nn.RMSNorm(d_model)
+        self.norm1 = RMSNorm(d_model)
         self.attn = DFlashAttention(d_model=d_model, num_heads=num_heads)
-        self.norm2 = nn.RMSNorm(d_model)
+        self.norm2 = RMSNorm(d_model)
         self.mlp = nn.Sequential(nn.Linear(d_model, d_ffn, bias=False), nn.SiLU(),
                                  nn.Linear(d_ffn, d_model, bias=False))
 
@@ -96,9 +118,9 @@ class DFlashSpeculator(nn.Module):
         self.slot_queries = nn.Parameter(0.02 * torch.randn(1, block_size, d_model))
         self.layers = nn.ModuleList(
             DFlashTransformerLayer(d_model, num_heads, 4 * d_model) for _ in range(num_layers))
-        self.norm_out = nn.RMSNorm(d_model)
+        self.norm_out = RMSNorm(d_model)
         self.proj_out = nn.Linear(d_model, d_target, bias=False)
-        self.final_norm = nn.RMSNorm(d_target) if norm_before_head else None
+        self.final_norm = RMSNorm(d_target) if norm_before_head else None
         if target_lm_head is not None:
             self.lm_head = target_lm_head
             self.lm_head.weight.requires_grad = False  # the verifier head stays frozen

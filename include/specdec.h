@@ -264,6 +264,55 @@ int specdec_dflash_backward_bf16(const uint16_t* logits, const uint16_t* target_
                                  void* stream);
 
 /* ------------------------------------------------------------------------- */
+/* DFlash drafter layers                                                      */
+/* ------------------------------------------------------------------------- */
+
+/* Element types of the drafter-layer entry points. */
+#define SPECDEC_DTYPE_F32 0
+#define SPECDEC_DTYPE_BF16 1
+
+/*
+ * RMSNorm over the last dimension of x [rows, D] (fp32 or bf16, `dtype`),
+ * fp32 weight [D]: y = x / sqrt(mean(x^2) + eps) * weight, in x's dtype, all
+ * arithmetic fp32. Replaces torch.nn.RMSNorm in models/dflash/model.py:60,62
+ * (norm1 / norm2), :111 (norm_out) and :114 (final_norm). rstd [rows] (or
+ * NULL) receives 1 / sqrt(mean(x^2) + eps) for the backward.
+ */
+int specdec_rmsnorm_forward(const void* x, const float* weight, void* y, float* rstd, int64_t rows, int32_t D,
+                            float eps, int32_t dtype, void* stream);
+
+/* Workspace bytes of specdec_rmsnorm_backward (partial weight gradients). */
+size_t specdec_rmsnorm_workspace_bytes(int64_t rows, int32_t D, int device);
+
+/*
+ * RMSNorm backward: dx [rows, D] (x's dtype) and dweight [D] (fp32, summed
+ * over rows in a fixed order: bitwise repeatable) from x, weight, the
+ * forward's rstd and dy (x's dtype). The gradient torch.nn.RMSNorm's
+ * autograd computes for models/dflash/model.py's norms. D <= 51200.
+ */
+int specdec_rmsnorm_backward(const void* x, const float* weight, const float* rstd, const void* dy, void* dx,
+                             float* dweight, int64_t rows, int32_t D, int32_t dtype, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
+/*
+ * DFlash attention forward on the tensor cores, bf16. Replaces the per-head
+ * softmax(q k^T * scale + mask) v of models/dflash/model.py:25-53 under the
+ * mask of models/dflash/model.py:123-131, applied by its structure: query
+ * t < n_ctx sees keys j <= t, query t >= n_ctx sees every key j < T.
+ *   q, k, v, o  [batch, T, heads, head_dim] bfloat16 bit patterns (the
+ *               projections' own layout), 16-byte aligned; head_dim = 64
+ *   lse         [batch, heads, T] fp32: log-sum-exp of each query row's
+ *               scaled scores (natural log), for a backward
+ *   status      [1] int32 or NULL: SPECDEC_ERR_CUDA if a bounded wait of
+ *               the kernel expired (the outputs are then unspecified)
+ * P = softmax is rounded to bf16 before the second product, the
+ * accumulation is fp32. 0 <= n_ctx <= T, batch * heads <= 65535.
+ */
+int specdec_dflash_attention_forward(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* o,
+                                     float* lse, int32_t batch, int32_t T, int32_t heads, int32_t head_dim,
+                                     int32_t n_ctx, float scale, int32_t* status, void* stream);
+
+/* ------------------------------------------------------------------------- */
 /* Launch tuning                                                              */
 /* ------------------------------------------------------------------------- */
 
