@@ -630,13 +630,18 @@ def time_drafter_step(args, dev, world, max_over_ranks, barrier):
     def loss_torch(logits, tok):
         return torch_ops_dpace_loss(logits, tok, 0.5, mask)
 
-    variants = [("fused_loss_fp32_logits", head, loss_fused, False),
-                ("torch_ops_loss_fp32_logits", head, loss_torch, False),
-                ("fused_loss_bf16_logits", head_bf16, loss_fused, False),
-                ("bf16_autocast_drafter_fused_loss", head_bf16, loss_fused, True)]
+    from specdec import drafter as layer_kernels
+
+    # (name, lm_head, objective, autocast, the drafter's norms/attention on the library's kernels)
+    variants = [("fused_loss_fp32_logits", head, loss_fused, False, True),
+                ("torch_ops_loss_fp32_logits", head, loss_torch, False, False),
+                ("fused_loss_bf16_logits", head_bf16, loss_fused, False, True),
+                ("bf16_autocast_drafter_fused_loss", head_bf16, loss_fused, True, True),
+                ("bf16_autocast_drafter_torch_layers_fused_loss", head_bf16, loss_fused, True, False)]
     out = {}
     stream = torch.cuda.current_stream(dev)
-    for name, lm_head, lfn, autocast in variants:
+    for name, lm_head, lfn, autocast, kernels in variants:
+        layer_kernels.set_enabled(kernels)
         model = build(lm_head)
         core = model.module if world > 1 else model
         params = [p for p in model.parameters() if p.requires_grad]
@@ -666,8 +671,9 @@ def time_drafter_step(args, dev, world, max_over_ranks, barrier):
         barrier()
         ms = max_over_ranks(a.elapsed_time(b)) / args.drafter_steps
         out[name] = {"ms_per_step": round(ms, 3), "rows_per_s": round(Nb * blk * world / (ms * 1e-3), 1),
-                     "loss": round(float(loss.detach()), 6)}
+                     "loss": round(float(loss.detach()), 6), "library_layers": kernels}
         del model, core, opt, params
+    layer_kernels.set_enabled(True)
     torch.backends.cuda.matmul.allow_tf32 = prev_tf32
     del head, head_bf16, feats
     torch.cuda.empty_cache()
@@ -679,7 +685,9 @@ def time_drafter_step(args, dev, world, max_over_ranks, barrier):
             "config": {"workload": "dflash_drafter_step", "features": [Nb, S, D], "d_model": 256, "layers": 3,
                        "heads": 4, "block_size": blk, "V": V, "lm_head": "frozen, random",
                        "objective": "dpace alpha 0.5, anchor slot masked", "optimizer": "AdamW lr 1e-3, clip 1.0",
-                       "gemms": "cuBLAS, TF32 for fp32", "parallelism": f"ddp{world}"},
+                       "gemms": "cuBLAS, TF32 for fp32", "parallelism": f"ddp{world}",
+                       "library_layers": "RMSNorm kernels (fp32/bf16) and, for bf16 q/k/v, the tcgen05 "
+                                         "attention forward and backward (specdec.drafter)"},
             "variants": out}
 
 

@@ -310,6 +310,339 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_fwd_kernel(const bf16
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
 }
 
+
+// ---------------------------------------------------------------------------
+// Backward. Two kernels, no atomics (every accumulation runs in a fixed order
+// inside one CTA, so the gradients are bitwise repeatable):
+//   dq kernel, one CTA per (b, h, 128-query tile), thread = query row:
+//     delta = sum_d dO * O for its row (kept for the dkv kernel); per key tile:
+//     S = Q K^T and dP = dO V^T (tcgen05, TMEM columns 0..127 / 128..255),
+//     p = e^(s * scale - lse), dS = p * (dP - delta) * scale to shared memory
+//     in bf16, dQ += dS K (K as an MN-major operand) in TMEM columns 256..319.
+//   dkv kernel, one CTA per (b, h, 128-key tile), thread = key row: per query
+//     tile: S^T = K Q^T and dP^T = V dO^T, p^T and dS^T in bf16 to shared
+//     memory, dV += P^T dO and dK += dS^T Q (dO and Q as MN-major operands)
+//     in TMEM columns 256..319 / 320..383.
+// Each CTA holds all 512 TMEM columns (one CTA per SM).
+// ---------------------------------------------------------------------------
+
+constexpr uint32_t kTmemAll = 512;
+constexpr uint32_t kColS = 0, kColDP = 128, kColAcc0 = 256, kColAcc1 = 320;
+
+// Shared memory of the backward kernels (offsets from a 1024-byte-aligned base).
+constexpr uint32_t kBOffA = 0;        // Q (dq kernel) | K (dkv kernel)
+constexpr uint32_t kBOffB = 16384;    // dO            | V
+constexpr uint32_t kBOffC = 32768;    // K             | Q
+constexpr uint32_t kBOffD = 49152;    // V             | dO
+constexpr uint32_t kBOffP = 65536;    // dS            | P^T   (two atoms)
+constexpr uint32_t kBOffS = 98304;    // -             | dS^T  (two atoms)
+constexpr uint32_t kBOffRow = 131072; // -             | lse, delta of the query tile (2 x 128 floats)
+constexpr uint32_t kBOffBar = 132096;
+constexpr uint32_t kBOffTmem = kBOffBar + 16;
+constexpr uint32_t kBSmemBytes = kBOffTmem + 16 + 1024;
+
+__device__ __forceinline__ bool visible(int qrow, int key, int T, int n_ctx) {
+  return qrow < T && key < T && (qrow >= n_ctx || key <= qrow);
+}
+
+// Writes 32 consecutive bf16 values (16 words) of row r of a two-atom
+// K-major operand at columns [32 cc, 32 cc + 32).
+__device__ __forceinline__ void st_row32(uint32_t tile, uint32_t r, int cc, const uint32_t (&w)[16]) {
+  const uint32_t atom = tile + (uint32_t)(cc >> 1) * 16384u;
+#pragma unroll
+  for (int c4 = 0; c4 < 4; ++c4)
+    st_shared_u4(atom + sw128(r, (uint32_t)((cc & 1) * 4 + c4)),
+                 make_uint4(w[4 * c4], w[4 * c4 + 1], w[4 * c4 + 2], w[4 * c4 + 3]));
+}
+
+__device__ __forceinline__ void tmem_alloc_all(uint32_t* slot) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+               "r"(kTmemAll)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cta_sync_tc() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+}
+
+__global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dq_kernel(
+    const bf16_t* __restrict__ q, const bf16_t* __restrict__ k, const bf16_t* __restrict__ v,
+    const bf16_t* __restrict__ o, const float* __restrict__ lse, const bf16_t* __restrict__ dO,
+    bf16_t* __restrict__ dq, float* __restrict__ delta_out, int T, int H, int n_ctx, float scale, int* status) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  unsigned char* gbase = smem_raw + (base - smem_u32(smem_raw));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(gbase + kBOffBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kBOffTmem);
+  const int warp = threadIdx.x >> 5;
+  const int bh = blockIdx.y, b = bh / H, h = bh % H;
+  const int q0 = blockIdx.x * kTM;
+  const int64_t rs = (int64_t)H * kHD;
+  const int64_t head = (int64_t)b * T * rs + (int64_t)h * kHD;
+  const int row = q0 + threadIdx.x;
+  const float sl2 = scale * kLog2e;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc_all(tmem_slot);
+  load_tile(base + kBOffA, q + head, rs, q0, T);
+  load_tile(base + kBOffB, dO + head, rs, q0, T);
+  // delta = sum_d dO * O of this row, and its lse in base 2
+  float delta = 0.f, lse2 = 0.f;
+  if (row < T) {
+    const bf16_t* orow = o + head + (int64_t)row * rs;
+    const bf16_t* grow = dO + head + (int64_t)row * rs;
+#pragma unroll
+    for (int c = 0; c < kHD / 8; ++c) {
+      const uint4 a = *reinterpret_cast<const uint4*>(orow + 8 * c);
+      const uint4 g = *reinterpret_cast<const uint4*>(grow + 8 * c);
+      const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, gw[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        delta = fmaf(bf16_lo(aw[i]), bf16_lo(gw[i]), delta);
+        delta = fmaf(bf16_hi(aw[i]), bf16_hi(gw[i]), delta);
+      }
+    }
+    delta_out[((int64_t)b * H + h) * T + row] = delta;
+    lse2 = lse[((int64_t)b * H + h) * T + row] * kLog2e;
+  }
+  cta_sync_tc();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const int q_last = min(q0 + kTM, T) - 1;
+  const int kv_end = q_last >= n_ctx ? T : q_last + 1;
+  constexpr uint32_t kIdS = instr_desc(kTM, kTN, 0, 0);
+  constexpr uint32_t kIdQ = instr_desc(kTM, kHD, 0, 1);
+  uint32_t ph = 0;
+  bool ok = true;
+  for (int k0 = 0; k0 < kv_end; k0 += kTN) {
+    load_tile(base + kBOffC, k + head, rs, k0, T);
+    load_tile(base + kBOffD, v + head, rs, k0, T);
+    cta_sync_tc();
+    if (threadIdx.x == 0) {
+#pragma unroll
+      for (int kk = 0; kk < kHD / 16; ++kk) {  // S = Q K^T, dP = dO V^T
+        umma_bf16(tmem + kColS, smem_desc(base + kBOffA + kk * 32, 16, 1024),
+                  smem_desc(base + kBOffC + kk * 32, 16, 1024), kIdS, kk > 0);
+        umma_bf16(tmem + kColDP, smem_desc(base + kBOffB + kk * 32, 16, 1024),
+                  smem_desc(base + kBOffD + kk * 32, 16, 1024), kIdS, kk > 0);
+      }
+      umma_commit(bar);
+    }
+    if (__syncthreads_or(!wait_bar(bar, ph) ? 1 : 0)) {
+      ok = false;
+      break;
+    }
+    ph ^= 1u;
+    tc_fence_after();
+#pragma unroll
+    for (int cc = 0; cc < kTN / 32; ++cc) {
+      float sv[32], dp[32];
+      tmem_ld32(tmem + lane_base + kColS + cc * 32, sv);
+      tmem_ld32(tmem + lane_base + kColDP + cc * 32, dp);
+      uint32_t w[16];
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const int j = k0 + cc * 32 + i;
+        const float p0 = visible(row, j, T, n_ctx) ? exp2f(sv[i] * sl2 - lse2) : 0.f;
+        const float p1 = visible(row, j + 1, T, n_ctx) ? exp2f(sv[i + 1] * sl2 - lse2) : 0.f;
+        w[i / 2] = pack_bf16x2(p0 * (dp[i] - delta) * scale, p1 * (dp[i + 1] - delta) * scale);
+      }
+      st_row32(base + kBOffP, (uint32_t)threadIdx.x, cc, w);
+    }
+    cta_sync_tc();
+    if (threadIdx.x == 0) {  // dQ += dS K
+#pragma unroll
+      for (int kk = 0; kk < kTN / 16; ++kk)
+        umma_bf16(tmem + kColAcc0,
+                  smem_desc(base + kBOffP + (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u, 16, 1024),
+                  smem_desc(base + kBOffC + (uint32_t)kk * 2048u, 16384, 1024), kIdQ, (k0 > 0 || kk > 0) ? 1u : 0u);
+      umma_commit(bar);
+    }
+    if (__syncthreads_or(!wait_bar(bar, ph) ? 1 : 0)) {
+      ok = false;
+      break;
+    }
+    ph ^= 1u;
+    cta_sync_tc();
+  }
+  if (!ok) {
+    if (threadIdx.x == 0 && status) atomicExch(status, kStatusTimeout);
+    wait_bar(bar, ph);
+  } else {
+    tc_fence_after();
+    float acc[kHD];
+#pragma unroll
+    for (int cc = 0; cc < kHD / 32; ++cc) {
+      float t[32];
+      tmem_ld32(tmem + lane_base + kColAcc0 + cc * 32, t);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[cc * 32 + i] = t[i];
+    }
+    if (row < T) {
+      bf16_t* drow = dq + head + (int64_t)row * rs;
+#pragma unroll
+      for (int c = 0; c < kHD / 8; ++c) {
+        const float* a = acc + 8 * c;
+        *reinterpret_cast<uint4*>(drow + 8 * c) = make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]),
+                                                              pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemAll) : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dkv_kernel(
+    const bf16_t* __restrict__ q, const bf16_t* __restrict__ k, const bf16_t* __restrict__ v,
+    const float* __restrict__ lse, const float* __restrict__ delta, const bf16_t* __restrict__ dO,
+    bf16_t* __restrict__ dk, bf16_t* __restrict__ dv, int T, int H, int n_ctx, float scale, int* status) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  unsigned char* gbase = smem_raw + (base - smem_u32(smem_raw));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(gbase + kBOffBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kBOffTmem);
+  float* sh_lse = reinterpret_cast<float*>(gbase + kBOffRow);
+  float* sh_delta = sh_lse + kTM;
+  const int warp = threadIdx.x >> 5;
+  const int bh = blockIdx.y, b = bh / H, h = bh % H;
+  const int k0 = blockIdx.x * kTN;
+  const int64_t rs = (int64_t)H * kHD;
+  const int64_t head = (int64_t)b * T * rs + (int64_t)h * kHD;
+  const int64_t rowv = ((int64_t)b * H + h) * T;
+  const int key = k0 + threadIdx.x;
+  const float sl2 = scale * kLog2e;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc_all(tmem_slot);
+  load_tile(base + kBOffA, k + head, rs, k0, T);
+  load_tile(base + kBOffB, v + head, rs, k0, T);
+  cta_sync_tc();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  // query tiles that see a key of this tile: context queries from the
+  // diagonal on, and every tile holding a block slot
+  const int qt_first = (k0 < n_ctx ? k0 : n_ctx) / kTM;
+  const int qt_end = (T + kTM - 1) / kTM;
+  constexpr uint32_t kIdS = instr_desc(kTN, kTM, 0, 0);
+  constexpr uint32_t kIdKV = instr_desc(kTN, kHD, 0, 1);
+  uint32_t ph = 0;
+  bool ok = true;
+  bool first = true;
+  for (int qt = qt_first; qt < qt_end; ++qt) {
+    const int q0 = qt * kTM;
+    load_tile(base + kBOffC, q + head, rs, q0, T);
+    load_tile(base + kBOffD, dO + head, rs, q0, T);
+    {
+      const int qr = q0 + threadIdx.x;
+      sh_lse[threadIdx.x] = qr < T ? lse[rowv + qr] * kLog2e : 0.f;
+      sh_delta[threadIdx.x] = qr < T ? delta[rowv + qr] : 0.f;
+    }
+    cta_sync_tc();
+    if (threadIdx.x == 0) {
+#pragma unroll
+      for (int kk = 0; kk < kHD / 16; ++kk) {  // S^T = K Q^T, dP^T = V dO^T
+        umma_bf16(tmem + kColS, smem_desc(base + kBOffA + kk * 32, 16, 1024),
+                  smem_desc(base + kBOffC + kk * 32, 16, 1024), kIdS, kk > 0);
+        umma_bf16(tmem + kColDP, smem_desc(base + kBOffB + kk * 32, 16, 1024),
+                  smem_desc(base + kBOffD + kk * 32, 16, 1024), kIdS, kk > 0);
+      }
+      umma_commit(bar);
+    }
+    if (__syncthreads_or(!wait_bar(bar, ph) ? 1 : 0)) {
+      ok = false;
+      break;
+    }
+    ph ^= 1u;
+    tc_fence_after();
+#pragma unroll
+    for (int cc = 0; cc < kTM / 32; ++cc) {
+      float sv[32], dp[32];
+      tmem_ld32(tmem + lane_base + kColS + cc * 32, sv);
+      tmem_ld32(tmem + lane_base + kColDP + cc * 32, dp);
+      uint32_t wp[16], wd[16];
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const int c = cc * 32 + i;
+        const float p0 = visible(q0 + c, key, T, n_ctx) ? exp2f(sv[i] * sl2 - sh_lse[c]) : 0.f;
+        const float p1 = visible(q0 + c + 1, key, T, n_ctx) ? exp2f(sv[i + 1] * sl2 - sh_lse[c + 1]) : 0.f;
+        wp[i / 2] = pack_bf16x2(p0, p1);
+        wd[i / 2] = pack_bf16x2(p0 * (dp[i] - sh_delta[c]) * scale, p1 * (dp[i + 1] - sh_delta[c + 1]) * scale);
+      }
+      st_row32(base + kBOffP, (uint32_t)threadIdx.x, cc, wp);
+      st_row32(base + kBOffS, (uint32_t)threadIdx.x, cc, wd);
+    }
+    cta_sync_tc();
+    if (threadIdx.x == 0) {  // dV += P^T dO, dK += dS^T Q
+#pragma unroll
+      for (int kk = 0; kk < kTM / 16; ++kk) {
+        const uint32_t acc = (!first || kk > 0) ? 1u : 0u;
+        const uint32_t aoff = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
+        umma_bf16(tmem + kColAcc0, smem_desc(base + kBOffP + aoff, 16, 1024),
+                  smem_desc(base + kBOffD + (uint32_t)kk * 2048u, 16384, 1024), kIdKV, acc);
+        umma_bf16(tmem + kColAcc1, smem_desc(base + kBOffS + aoff, 16, 1024),
+                  smem_desc(base + kBOffC + (uint32_t)kk * 2048u, 16384, 1024), kIdKV, acc);
+      }
+      umma_commit(bar);
+    }
+    if (__syncthreads_or(!wait_bar(bar, ph) ? 1 : 0)) {
+      ok = false;
+      break;
+    }
+    ph ^= 1u;
+    first = false;
+    cta_sync_tc();
+  }
+  if (!ok) {
+    if (threadIdx.x == 0 && status) atomicExch(status, kStatusTimeout);
+    wait_bar(bar, ph);
+  } else {
+    tc_fence_after();
+    // keys no query sees (none here: the qt loop covers every visible pair) still get zeros
+    float av[kHD], ak[kHD];
+#pragma unroll
+    for (int cc = 0; cc < kHD / 32; ++cc) {
+      float t[32];
+      tmem_ld32(tmem + lane_base + kColAcc0 + cc * 32, t);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) av[cc * 32 + i] = first ? 0.f : t[i];
+      tmem_ld32(tmem + lane_base + kColAcc1 + cc * 32, t);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) ak[cc * 32 + i] = first ? 0.f : t[i];
+    }
+    if (key < T) {
+      bf16_t* vr = dv + head + (int64_t)key * rs;
+      bf16_t* kr = dk + head + (int64_t)key * rs;
+#pragma unroll
+      for (int c = 0; c < kHD / 8; ++c) {
+        const float* a = av + 8 * c;
+        const float* g = ak + 8 * c;
+        *reinterpret_cast<uint4*>(vr + 8 * c) = make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]),
+                                                            pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
+        *reinterpret_cast<uint4*>(kr + 8 * c) = make_uint4(pack_bf16x2(g[0], g[1]), pack_bf16x2(g[2], g[3]),
+                                                            pack_bf16x2(g[4], g[5]), pack_bf16x2(g[6], g[7]));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemAll) : "memory");
+}
+
 }  // namespace
 
 // Raises the kernel's dynamic shared-memory limit once per device.
@@ -333,6 +666,36 @@ cudaError_t dflash_attn_fwd_launch(const void* q, const void* k, const void* v, 
   dflash_attn_fwd_kernel<<<grid, kThreads, kSmemBytes, st>>>(
       static_cast<const bf16_t*>(q), static_cast<const bf16_t*>(k), static_cast<const bf16_t*>(v),
       static_cast<bf16_t*>(o), lse, T, H, n_ctx, scale * kLog2e, status);
+  return cudaGetLastError();
+}
+
+cudaError_t dflash_attn_bwd_launch(const void* q, const void* k, const void* v, const void* o, const float* lse,
+                                   const void* dO, void* dq, void* dk, void* dv, float* delta, int batch, int T, int H,
+                                   int n_ctx, float scale, int* status, cudaStream_t st) {
+  static std::atomic<unsigned long long> done{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(done.load() & bit)) {
+    e = cudaFuncSetAttribute(dflash_attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBSmemBytes);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(dflash_attn_bwd_dkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)kBSmemBytes);
+    if (e != cudaSuccess) return e;
+    done.fetch_or(bit);
+  }
+  const dim3 grid((unsigned)((T + kTM - 1) / kTM), (unsigned)(batch * H));
+  dflash_attn_bwd_dq_kernel<<<grid, kThreads, kBSmemBytes, st>>>(
+      static_cast<const bf16_t*>(q), static_cast<const bf16_t*>(k), static_cast<const bf16_t*>(v),
+      static_cast<const bf16_t*>(o), lse, static_cast<const bf16_t*>(dO), static_cast<bf16_t*>(dq), delta, T, H,
+      n_ctx, scale, status);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  dflash_attn_bwd_dkv_kernel<<<grid, kThreads, kBSmemBytes, st>>>(
+      static_cast<const bf16_t*>(q), static_cast<const bf16_t*>(k), static_cast<const bf16_t*>(v), lse, delta,
+      static_cast<const bf16_t*>(dO), static_cast<bf16_t*>(dk), static_cast<bf16_t*>(dv), T, H, n_ctx, scale,
+      status);
   return cudaGetLastError();
 }
 

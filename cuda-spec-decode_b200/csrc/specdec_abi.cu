@@ -897,4 +897,37 @@ int specdec_dflash_attention_forward(const uint16_t* q, const uint16_t* k, const
   return e == cudaSuccess ? ok() : cuda_fail(e, "attention forward launch");
 }
 
+size_t specdec_dflash_attention_workspace_bytes(int32_t batch, int32_t T, int32_t heads) {
+  if (batch <= 0 || T <= 0 || heads <= 0) return 256;
+  return align256((size_t)batch * (size_t)heads * (size_t)T * sizeof(float));
+}
+
+int specdec_dflash_attention_backward(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* o,
+                                      const float* lse, const uint16_t* dout, uint16_t* dq, uint16_t* dk,
+                                      uint16_t* dv, int32_t batch, int32_t T, int32_t heads, int32_t head_dim,
+                                      int32_t n_ctx, float scale, int32_t* status, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+  if (head_dim != 64) return fail(SPECDEC_ERR_ARGUMENT, "head_dim must be 64, got %d", head_dim);
+  if (batch < 0 || T < 0 || heads < 1) return fail(SPECDEC_ERR_ARGUMENT, "bad shape");
+  if (n_ctx < 0 || n_ctx > T) return fail(SPECDEC_ERR_ARGUMENT, "n_ctx must be in [0, T] (n_ctx=%d, T=%d)", n_ctx, T);
+  if ((int64_t)batch * heads > 65535) return fail(SPECDEC_ERR_ARGUMENT, "batch * heads must be <= 65535");
+  if (!(scale > 0.f)) return fail(SPECDEC_ERR_VALUE, "scale must be > 0");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (status) {
+    const cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int32_t), st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+  }
+  if (batch == 0 || T == 0) return ok();
+  if (!q || !k || !v || !o || !lse || !dout || !dq || !dk || !dv || !workspace)
+    return fail(SPECDEC_ERR_ARGUMENT, "null input, output or workspace pointer");
+  const void* ptrs[] = {q, k, v, o, dout, dq, dk, dv};
+  for (const void* p : ptrs)
+    if (!aligned(p, 16)) return fail(SPECDEC_ERR_ARGUMENT, "attention tensors must be 16-byte aligned");
+  const size_t need = (size_t)batch * (size_t)heads * (size_t)T * sizeof(float);
+  if (workspace_bytes < need) return fail(SPECDEC_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
+  const cudaError_t e = dflash_attn_bwd_launch(q, k, v, o, lse, dout, dq, dk, dv, static_cast<float*>(workspace), batch,
+                                               T, heads, n_ctx, scale, status, st);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "attention backward launch");
+}
+
 }  // extern "C"

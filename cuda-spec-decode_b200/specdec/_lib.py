@@ -74,6 +74,10 @@ _SIGNATURES = {
         _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i32, _c_p, _c_sz, _c_p]),
     "specdec_dflash_attention_forward": (ctypes.c_int, [
         _c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_f32, _c_p, _c_p]),
+    "specdec_dflash_attention_workspace_bytes": (_c_sz, [_c_i32, _c_i32, _c_i32]),
+    "specdec_dflash_attention_backward": (ctypes.c_int, [
+        _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_f32,
+        _c_p, _c_p, _c_sz, _c_p]),
 }
 # bf16 entry points take the same arguments as their fp32 counterparts
 for _name in ("specdec_dpace_forward", "specdec_dpace_backward", "specdec_dflash_forward",

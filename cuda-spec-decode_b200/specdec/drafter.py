@@ -5,10 +5,10 @@
   weight gradient is reduced in a fixed order (bitwise repeatable).
 - ``dflash_attention(q, k, v, n_ctx, scale)``: multi-head attention under the
   DFlash mask (query t < n_ctx sees keys j <= t, later queries see every key)
-  for bf16 q, k, v of shape [B, T, H, 64] -- the projections' own layout. The
-  forward runs on the tensor cores (tcgen05, S and O in tensor memory); the
-  backward recomputes the probabilities from the forward's log-sum-exp and
-  forms dq, dk, dv with batched products.
+  for bf16 q, k, v of shape [B, T, H, 64] -- the projections' own layout.
+  Forward and backward run on the tensor cores (tcgen05: products in tensor
+  memory); the backward recomputes the probabilities from the forward's
+  log-sum-exp and accumulates dq, dk, dv in a fixed order.
 
 Reference: models/dflash/model.py:25-53 (DFlashAttention), :56-73 (the
 pre-norm layer, torch.nn.RMSNorm), :123-131 (the mask).
@@ -83,13 +83,6 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float | None = None) ->
     return _RMSNorm.apply(x, weight, e)
 
 
-def _mask(T: int, n_ctx: int, device) -> torch.Tensor:
-    """Boolean [T, T] visibility of the DFlash mask (row = query)."""
-    i = torch.arange(T, device=device).view(T, 1)
-    j = torch.arange(T, device=device).view(1, T)
-    return (i >= n_ctx) | (j <= i)
-
-
 class _DFlashAttention(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, n_ctx, scale):
@@ -108,22 +101,19 @@ class _DFlashAttention(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, do):
-        # probabilities recomputed from the forward's log-sum-exp; fp32 products
+        lib = _lib.load()
         q, k, v, o, lse = ctx.saved_tensors
         B, T, H, Dh = q.shape
-        qh, kh, vh = (t.permute(0, 2, 1, 3).float() for t in (q, k, v))
-        oh, doh = o.permute(0, 2, 1, 3).float(), do.permute(0, 2, 1, 3).float()
-        s = torch.matmul(qh, kh.transpose(-1, -2)) * ctx.scale
-        vis = _mask(T, ctx.n_ctx, q.device)
-        p = torch.where(vis, torch.exp(s - lse.unsqueeze(-1)), torch.zeros((), device=q.device))
-        dp = torch.matmul(doh, vh.transpose(-1, -2))
-        delta = (doh * oh).sum(-1, keepdim=True)
-        ds = p * (dp - delta) * ctx.scale
-        dq = torch.matmul(ds, kh)
-        dk = torch.matmul(ds.transpose(-1, -2), qh)
-        dv = torch.matmul(p.transpose(-1, -2), doh)
-        back = lambda t: t.permute(0, 2, 1, 3).to(q.dtype)  # noqa: E731
-        return back(dq), back(dk), back(dv), None, None
+        do = do.to(q.dtype).contiguous()
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        with torch.cuda.device(q.device):
+            ws_bytes = lib.specdec_dflash_attention_workspace_bytes(B, T, H)
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+            _lib.check(lib.specdec_dflash_attention_backward(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), do.data_ptr(),
+                dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, T, H, Dh, ctx.n_ctx, ctx.scale, None,
+                ws.data_ptr(), ws_bytes, _stream(q)), "specdec_dflash_attention_backward")
+        return dq, dk, dv, None, None
 
 
 def attention_supported(q: torch.Tensor) -> bool:

@@ -312,6 +312,25 @@ int specdec_dflash_attention_forward(const uint16_t* q, const uint16_t* k, const
                                      float* lse, int32_t batch, int32_t T, int32_t heads, int32_t head_dim,
                                      int32_t n_ctx, float scale, int32_t* status, void* stream);
 
+/* Workspace bytes of specdec_dflash_attention_backward ([batch, heads, T] fp32). */
+size_t specdec_dflash_attention_workspace_bytes(int32_t batch, int32_t T, int32_t heads);
+
+/*
+ * DFlash attention backward on the tensor cores, bf16: dq, dk, dv
+ * [batch, T, heads, 64] from q, k, v, the forward's o and lse, and dout (the
+ * gradient of o). The gradient autograd computes through
+ * models/dflash/model.py:25-53 under the mask of :123-131. Probabilities
+ * are recomputed from lse; dS = P * (dP - rowsum(dout * o)) * scale;
+ * products in bf16 with fp32 accumulation, every sum in a fixed order (no
+ * atomics: bitwise repeatable). workspace: specdec_dflash_attention_
+ * workspace_bytes() of device memory, no initialisation required.
+ */
+int specdec_dflash_attention_backward(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* o,
+                                      const float* lse, const uint16_t* dout, uint16_t* dq, uint16_t* dk,
+                                      uint16_t* dv, int32_t batch, int32_t T, int32_t heads, int32_t head_dim,
+                                      int32_t n_ctx, float scale, int32_t* status, void* workspace,
+                                      size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------- */
 /* Launch tuning                                                              */
 /* ------------------------------------------------------------------------- */

@@ -110,7 +110,7 @@ def test_attention_forward_matches_reference(cuda, B, T, H, n_ctx):
     assert torch.equal(o, o2)
 
 
-@pytest.mark.parametrize("B,T,H,n_ctx", [(2, 528, 4, 512), (2, 300, 4, 200), (1, 129, 2, 0)])
+@pytest.mark.parametrize("B,T,H,n_ctx", SHAPES)
 def test_attention_backward_matches_reference(cuda, B, T, H, n_ctx):
     from specdec import drafter
 
@@ -125,6 +125,13 @@ def test_attention_backward_matches_reference(cuda, B, T, H, n_ctx):
     for got, want in ((qs.grad, qr.grad), (ks.grad, kr.grad), (vs.grad, vr.grad)):
         err = (got.float() - want).abs()
         assert bool((err <= 2e-2 + 2e-2 * want.abs()).all()), float(err.max())
+    # bitwise repeatable (no atomics)
+    g1 = [t.grad.clone() for t in (qs, ks, vs)]
+    for t in (qs, ks, vs):
+        t.grad = None
+    drafter.dflash_attention(qs, ks, vs, n_ctx).backward(do)
+    for a, t in zip(g1, (qs, ks, vs)):
+        assert torch.equal(a, t.grad)
 
 
 def test_attention_rejects_bad_arguments(cuda):
