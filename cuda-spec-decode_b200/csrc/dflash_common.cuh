@@ -71,12 +71,41 @@ __device__ __forceinline__ DfState df_shfl(const DfState& s, int o) {
   return r;
 }
 
+// Merges the 32 lanes' states into the warp's, valid in every lane: each
+// log-sum-exp state is rescaled to the warp maximum (skipped when every lane
+// already holds it -- a factor of e^0 = 1 exactly, the same bits) and summed
+// over a fixed butterfly; the CE argmax is the largest verifier logit, ties
+// to the smallest index.
 template <int KIND>
 __device__ __forceinline__ void df_warp_merge(DfState& s) {
+  const float Mq = warp_max(s.mq);
+  if (__any_sync(kFullMask, s.mq != Mq)) s.sq *= exp_shift(s.mq, Mq);
+  s.mq = Mq;
+  if (KIND == kKindKL) {
+    const float Mp = warp_max(s.mp);
+    if (__any_sync(kFullMask, s.mp != Mp)) {
+      const float f = exp_shift(s.mp, Mp);
+      s.sp *= f;
+      s.t *= f;
+    }
+    s.mp = Mp;
+  } else {
+    const float Mx = warp_max(s.bx);
+    // first index among the lanes that hold the maximum (INT_MAX: none)
+    const unsigned cand = s.bx == Mx ? (unsigned)s.bi : (unsigned)INT_MAX;
+    const unsigned bi = __reduce_min_sync(kFullMask, cand);
+    const unsigned who = __ballot_sync(kFullMask, s.bx == Mx && (unsigned)s.bi == bi);
+    s.bl = __shfl_sync(kFullMask, s.bl, who ? __ffs(who) - 1 : 0);
+    s.bx = Mx;
+    s.bi = (int)bi;
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
-    const DfState other = df_shfl<KIND>(s, o);
-    df_merge<KIND>(s, other);
+    s.sq += __shfl_xor_sync(kFullMask, s.sq, o);
+    if (KIND == kKindKL) {
+      s.sp += __shfl_xor_sync(kFullMask, s.sp, o);
+      s.t += __shfl_xor_sync(kFullMask, s.t, o);
+    }
   }
 }
 
@@ -112,7 +141,12 @@ __device__ __forceinline__ void df_group(DfState& s, const float4 (&a)[U], const
   float cmb = max4(b[0]);
 #pragma unroll
   for (int u = 1; u < U; ++u) cmb = fmaxf(cmb, max4(b[u]));
-  if (empty) release_stage(empty, fmaxf(cma, cmb));  // both streams are in registers
+  if (empty) {  // a full stage, the whole warp here
+    release_stage(empty, fmaxf(cma, cmb));  // both streams are in registers
+    // one running maximum per stream for the whole warp: the piece's close needs no rescale
+    cma = warp_max(cma);
+    if (KIND == kKindKL) cmb = warp_max(cmb);
+  }
   if (cma > s.mq) {
     s.sq *= exp_shift(s.mq, cma);
     s.mq = cma;
@@ -173,12 +207,16 @@ __device__ __forceinline__ void df_group(DfState& s, const uint4 (&a)[U], const 
   uint32_t pa = bmax8(a[0]);
 #pragma unroll
   for (int u = 1; u < U; ++u) pa = bmax2(pa, bmax8(a[u]));
-  const float cma = fmaxf(bf16_lo(pa), bf16_hi(pa));
+  float cma = fmaxf(bf16_lo(pa), bf16_hi(pa));
   uint32_t pb = bmax8(b[0]);
 #pragma unroll
   for (int u = 1; u < U; ++u) pb = bmax2(pb, bmax8(b[u]));
-  const float cmb = fmaxf(bf16_lo(pb), bf16_hi(pb));
-  if (empty) release_stage(empty, fmaxf(cma, cmb));  // both streams are in registers
+  float cmb = fmaxf(bf16_lo(pb), bf16_hi(pb));
+  if (empty) {  // a full stage, the whole warp here
+    release_stage(empty, fmaxf(cma, cmb));  // both streams are in registers
+    cma = warp_max(cma);
+    if (KIND == kKindKL) cmb = warp_max(cmb);
+  }
   if (cma > s.mq) {
     s.sq *= exp_shift(s.mq, cma);
     s.mq = cma;

@@ -198,6 +198,8 @@ __global__ void __launch_bounds__(1024) dflash_finalize_kernel(const __grid_cons
   float mv = 0.f;
   for (int i = lane; i < B; i += 32) mv += a.mask ? a.mask[n * B + i] : 1.f;
   const float denom = warp_sum(mv) + 1e-5f;
+  // the first row's numerator depends on the mask only: read it before the wait too
+  const float numer0 = warp < B ? dr_numer(a, n * B + warp) : 0.f;
   pdl_wait();  // the streaming grid has completed and its stores are visible
   // a wait of the streaming grid expired: pieces may be missing, so every
   // per-row output is NaN (a backward from them gives a NaN gradient)
@@ -205,7 +207,7 @@ __global__ void __launch_bounds__(1024) dflash_finalize_kernel(const __grid_cons
   float acc = 0.f;  // this warp's rows, in row order
   for (int j = warp; j < B; j += nwarps) {
     const int64_t r = n * B + j;
-    const float numer = dr_numer(a, r);
+    const float numer = j == warp ? numer0 : dr_numer(a, r);
     const float w = __fdiv_rn(numer, denom);
     float el = 0.f, lzq = 0.f, lzp = 0.f;
     int64_t tgt = 0;
@@ -263,9 +265,11 @@ __global__ void __launch_bounds__(1024) dflash_finalize_kernel(const __grid_cons
     last = __shfl_sync(kFullMask, last, 0);
     if (last) {
       __threadfence();
+      // the flag exchange and the loss loads are independent: both in flight at once
+      int f = 0;
+      if (lane == 0) f = atomicExch(a.flag, 0);
       const float total = warp_sum_l2(a.seq_loss, a.N);
       if (lane == 0) {
-        const int f = atomicExch(a.flag, 0);
         // a timed-out copy wait left partials unwritten: the loss is NaN, not a wrong number
         a.loss[0] = (f & 2) ? __int_as_float(0x7fc00000) : total / (float)a.n_global;
         *a.done_cnt = 0u;

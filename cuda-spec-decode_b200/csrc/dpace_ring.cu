@@ -165,6 +165,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
 template <class T>
 __global__ void __launch_bounds__(1024) dpace_finalize_kernel(const __grid_constant__ DpaceFwdArgs a) {
   __shared__ float sh_ce[32];
+  __shared__ int sh_live[32];
   // a backward chained behind this kernel (specdec_dpace_forward_backward)
   // may become resident now: it streams logits and waits for lse / scale
   pdl_trigger();
@@ -206,6 +207,7 @@ __global__ void __launch_bounds__(1024) dpace_finalize_kernel(const __grid_const
     if (lane == 0) {
       a.lse[r] = timed_out ? __int_as_float(0x7fc00000) : lse;
       sh_ce[warp] = ce;
+      sh_live[warp] = live;
     }
   }
   __syncthreads();
@@ -213,7 +215,7 @@ __global__ void __launch_bounds__(1024) dpace_finalize_kernel(const __grid_const
     const int j = lane;
     const bool in = j < B;
     const int64_t r = n * B + (in ? j : 0);
-    const bool live = in && (a.mask == nullptr || a.mask[r] > 0.f);
+    const bool live = in && sh_live[j];
     const float ce = in ? sh_ce[j] : 0.f;
     const float mk = live ? 1.f : 0.f;
     const float sm = live ? __fadd_rn(__fmul_rn(a.one_minus_alpha, expf(-ce)), a.alpha) : 1.f;
@@ -257,9 +259,11 @@ __global__ void __launch_bounds__(1024) dpace_finalize_kernel(const __grid_const
     last = __shfl_sync(kFullMask, last, 0);
     if (last) {
       __threadfence();
+      // the flag exchange and the loss loads are independent: both in flight at once
+      int f = 0;
+      if (lane == 0) f = atomicExch(a.flag, 0);
       const float total = warp_sum_l2(a.seq_loss, a.N);
       if (lane == 0) {
-        const int f = atomicExch(a.flag, 0);
         // a timed-out copy wait left partials unwritten: the loss is NaN, not a wrong number
         a.loss[0] = (f & 2) ? __int_as_float(0x7fc00000) : total / (float)a.n_global;
         if (a.status) a.status[0] = (f & 2) ? kStatusTimeout : ((f & 1) ? kStatusTargetRange : kStatusOk);
@@ -443,6 +447,13 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
 #define SPECDEC_BWD_BLOCK_STAGES 1
 #endif
 constexpr int kBwdBlockStages = SPECDEC_BWD_BLOCK_STAGES;
+// Stages per forward block of the default shape (0). A smaller block shortens
+// the end of the launch (the last blocks finish closer together) at the cost
+// of more partials per row for the finalize to merge.
+#ifndef SPECDEC_FWD_BLOCK_STAGES
+#define SPECDEC_FWD_BLOCK_STAGES 4
+#endif
+constexpr int kFwdBlockStages = SPECDEC_FWD_BLOCK_STAGES;
 
 template <class T, int NC, int S, int SE, int BS>
 struct RingVariant {
@@ -488,7 +499,7 @@ struct RingVariant {
 template <class T>
 struct Shapes {
   static constexpr int k = 4 / sizeof(T);  // elements per float's bytes
-  using R0 = RingVariant<T, 4, 4, 4096 * k, 4>;
+  using R0 = RingVariant<T, 4, 4, 4096 * k, kFwdBlockStages>;
   using R1 = RingVariant<T, 8, 4, 8192 * k, 2>;
   using R2 = RingVariant<T, 4, 6, 4096 * k, 4>;
   using R3 = RingVariant<T, 4, 8, 4096 * k, 8>;
@@ -504,7 +515,7 @@ struct Shapes {
       case 4: return 2048 * 8 * k;
       case 5: return 4096 * 4 * k;
       case 6: return 4096 * 4 * k;
-      default: return 4096 * 4 * k;
+      default: return 4096 * kFwdBlockStages * k;
     }
   }
   static int fwd_ctas(int shape, int device, int cap) {

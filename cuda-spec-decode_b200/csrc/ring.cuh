@@ -348,6 +348,7 @@ __device__ __forceinline__ void warp_lse_full(const float* sb, float& m, float& 
 #pragma unroll
   for (int u = 1; u < U; ++u) cm = fmaxf(cm, max4(v[u]));
   if (empty) release_stage(empty, cm);
+  cm = warp_max(cm);  // one running maximum for the whole warp: the piece's close needs no rescale
   if (cm > m) {
     s *= exp_shift(m, cm);
     m = cm;
@@ -417,8 +418,9 @@ __device__ __forceinline__ void warp_lse_full(const bf16_t* sb, float& m, float&
   uint32_t mx = bmax8(v[0]);
 #pragma unroll
   for (int u = 1; u < U; ++u) mx = bmax2(mx, bmax8(v[u]));
-  const float cm = fmaxf(bf16_lo(mx), bf16_hi(mx));
+  float cm = fmaxf(bf16_lo(mx), bf16_hi(mx));
   if (empty) release_stage(empty, cm);
+  cm = warp_max(cm);  // one running maximum for the whole warp: the piece's close needs no rescale
   if (cm > m) {
     s *= exp_shift(m, cm);
     m = cm;

@@ -178,13 +178,26 @@ __device__ __forceinline__ void lse_push(float& m, float& s, float x) {
   s += exp_shift(x, m);
 }
 
+// Maximum over the warp's 32 lanes (one redux.sync on sm_100a; NaN inputs
+// are ignored, as fmaxf ignores them).
+__device__ __forceinline__ float warp_max(float v) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
+}
+
+// Merges the 32 lanes' (m, s) into the warp's (max, sum of e^(x - max)),
+// valid in every lane: the warp maximum M, each lane's s rescaled by
+// e^(m - M), then a sum over a fixed butterfly. A lane whose m already is M
+// is scaled by e^0 = 1 exactly, so the rescale is skipped when every lane
+// holds M (the streaming kernels keep m warp-uniform on full stages): the
+// bits are the same either way.
 __device__ __forceinline__ void warp_lse(float& m, float& s) {
+  const float M = warp_max(m);
+  if (__any_sync(kFullMask, m != M)) s *= exp_shift(m, M);
+  m = M;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float om = __shfl_xor_sync(kFullMask, m, o);
-    const float os = __shfl_xor_sync(kFullMask, s, o);
-    lse_merge(m, s, om, os);
-  }
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(kFullMask, s, o);
 }
 
 // Block-wide (m, s) merge in a fixed butterfly order. `sh` holds 2*NT/32
