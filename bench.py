@@ -675,29 +675,43 @@ def time_drafter_step(args, dev, world, max_over_ranks, barrier):
     from specdec import drafter as layer_kernels
 
     # (name, lm_head, objective, autocast, the drafter's norms/attention on the library's kernels)
-    variants = [("fused_loss_fp32_logits", head, loss_fused, False, True),
-                ("torch_ops_loss_fp32_logits", head, loss_torch, False, False),
-                ("fused_loss_bf16_logits", head_bf16, loss_fused, False, True),
-                ("bf16_autocast_drafter_fused_loss", head_bf16, loss_fused, True, True),
-                ("bf16_autocast_drafter_torch_layers_fused_loss", head_bf16, loss_fused, True, False)]
+    variants = [("fused_loss_fp32_logits", head, loss_fused, False, True, False),
+                ("torch_ops_loss_fp32_logits", head, loss_torch, False, False, False),
+                ("fused_loss_bf16_logits", head_bf16, loss_fused, False, True, False),
+                ("bf16_autocast_drafter_fused_loss", head_bf16, loss_fused, True, True, False),
+                ("bf16_autocast_drafter_torch_layers_fused_loss", head_bf16, loss_fused, True, False, False)]
+    if world == 1:
+        # the same step captured once as a CUDA graph (specdec.graphs.GraphedStep) and replayed
+        variants.append(("bf16_autocast_drafter_fused_loss_graphed", head_bf16, loss_fused, True, True, True))
     out = {}
     stream = torch.cuda.current_stream(dev)
-    for name, lm_head, lfn, autocast, kernels in variants:
+    for name, lm_head, lfn, autocast, kernels, graphed in variants:
         layer_kernels.set_enabled(kernels)
         model = build(lm_head)
         core = model.module if world > 1 else model
         params = [p for p in model.parameters() if p.requires_grad]
-        opt = torch.optim.AdamW(params, lr=1e-3)
+        opt = torch.optim.AdamW(params, lr=1e-3, capturable=graphed)
 
-        def step():
+        def step_fn(f_in, t_in):
             opt.zero_grad(set_to_none=True)
-            with torch.autocast("cuda", dtype=torch.bfloat16, enabled=autocast):
-                loss = core.compute_loss(feats, tokens, loss_fn=lfn) if world == 1 else \
-                    lfn(model(feats), tokens)
+            with torch.autocast("cuda", dtype=torch.bfloat16, enabled=autocast, cache_enabled=not graphed):
+                loss = core.compute_loss(f_in, t_in, loss_fn=lfn) if world == 1 else \
+                    lfn(model(f_in), t_in)
             loss.backward()
             torch.nn.utils.clip_grad_norm_(params, 1.0)
             opt.step()
             return loss
+
+        if graphed:
+            from specdec.graphs import GraphedStep
+
+            gstep = GraphedStep(step_fn, feats, tokens, optimizers=(opt,))
+            step = gstep
+        else:
+            gstep = None
+
+            def step():
+                return step_fn(feats, tokens)
 
         for _ in range(3):
             step()
@@ -711,10 +725,14 @@ def time_drafter_step(args, dev, world, max_over_ranks, barrier):
         b.record(stream)
         torch.cuda.synchronize(dev)
         barrier()
+        if gstep is not None:
+            gstep.check()
         ms = max_over_ranks(a.elapsed_time(b)) / args.drafter_steps
         out[name] = {"ms_per_step": round(ms, 3), "rows_per_s": round(Nb * blk * world / (ms * 1e-3), 1),
-                     "loss": round(float(loss.detach()), 6), "library_layers": kernels}
-        del model, core, opt, params
+                     "loss": round(float(loss.detach()), 6), "library_layers": kernels,
+                     "cuda_graph": graphed}
+        del model, core, opt, params, gstep, step, step_fn
+        torch.cuda.empty_cache()
     layer_kernels.set_enabled(True)
     torch.backends.cuda.matmul.allow_tf32 = prev_tf32
     del head, head_bf16, feats
@@ -729,7 +747,10 @@ def time_drafter_step(args, dev, world, max_over_ranks, barrier):
                        "objective": "dpace alpha 0.5, anchor slot masked", "optimizer": "AdamW lr 1e-3, clip 1.0",
                        "gemms": "cuBLAS, TF32 for fp32", "parallelism": f"ddp{world}",
                        "library_layers": "RMSNorm kernels (fp32/bf16) and, for bf16 q/k/v, the tcgen05 "
-                                         "attention forward and backward (specdec.drafter)"},
+                                         "attention forward and backward (specdec.drafter)",
+                       "cuda_graph": "the _graphed variant (one GPU) replays the whole step -- forward, "
+                                     "loss, backward, clip, AdamW(capturable) -- as one CUDA graph "
+                                     "(specdec.graphs.GraphedStep); the others launch eagerly"},
             "variants": out}
 
 

@@ -839,16 +839,14 @@ int specdec_rmsnorm_forward(const void* x, const float* weight, void* y, float* 
   int sms = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return fail(SPECDEC_ERR_CUDA, "device query failed");
-  const int64_t want = (rows + 7) / 8;  // 8 rows (one per warp) per CTA and round
-  const int ctas = (int)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
-  const cudaError_t e = rmsnorm_fwd_launch(dtype, x, weight, y, rstd, rows, D, eps, ctas,
+  const cudaError_t e = rmsnorm_fwd_launch(dtype, x, weight, y, rstd, rows, D, eps, sms,
                                            static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? ok() : cuda_fail(e, "rmsnorm forward launch");
 }
 
 size_t specdec_rmsnorm_workspace_bytes(int64_t rows, int32_t D, int device) {
   if (rows <= 0 || D <= 0) return 256;
-  return align256((size_t)rmsnorm_bwd_ctas(rows, device) * (size_t)D * sizeof(float));
+  return align256((size_t)rmsnorm_bwd_ctas(rows, D, device) * (size_t)D * sizeof(float));
 }
 
 int specdec_rmsnorm_backward(const void* x, const float* weight, const float* rstd, const void* dy, void* dx,
@@ -867,7 +865,7 @@ int specdec_rmsnorm_backward(const void* x, const float* weight, const float* rs
     return fail(SPECDEC_ERR_ARGUMENT, "null input, output or workspace pointer");
   const int dev = current_device();
   if (dev < 0) return fail(SPECDEC_ERR_CUDA, "cudaGetDevice failed");
-  const int ctas = rmsnorm_bwd_ctas(rows, dev);
+  const int ctas = rmsnorm_bwd_ctas(rows, D, dev);
   if (ctas <= 0) return fail(SPECDEC_ERR_CUDA, "device query failed");
   const size_t need = (size_t)ctas * (size_t)D * sizeof(float);
   if (workspace_bytes < need) return fail(SPECDEC_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);

@@ -172,10 +172,10 @@ cudaError_t dflash_bwd_ring_launch(int dtype, int shape, const DflashBwdArgs& a,
 cudaError_t scale_inplace_launch(int dtype, void* x, int64_t n, const float* factor, int ctas, cudaStream_t st);
 
 // RMSNorm of the drafter (drafter_norm.cu).
-int rmsnorm_bwd_ctas(int64_t rows, int device);
+int rmsnorm_bwd_ctas(int64_t rows, int D, int device);
 int rmsnorm_bwd_warps(int D);
 cudaError_t rmsnorm_fwd_launch(int dtype, const void* x, const float* w, void* y, float* rstd, int64_t rows, int D,
-                               float eps, int ctas, cudaStream_t st);
+                               float eps, int sms, cudaStream_t st);
 cudaError_t rmsnorm_bwd_launch(int dtype, const void* x, const float* w, const float* rstd, const void* dy,
                                void* dx, float* dw, float* part, int64_t rows, int D, int ctas, cudaStream_t st);
 

@@ -1,0 +1,74 @@
+"""A whole training step -- forward, objective, backward, gradient clipping and
+the optimizer update -- captured once as a CUDA graph and replayed.
+
+The drafter's step (models/dflash/model.py:152-170 through the reference
+pipeline's loop, pipeline.py:85-117) is a few hundred small launches; run
+eagerly from Python, the GPU waits on the host between many of them. Replayed
+as one graph the launches go out back to back.
+
+    step = GraphedStep(fn, feats, tokens)     # fn(feats, tokens) -> loss
+    loss = step()                             # replay on the resident inputs
+    loss = step(new_feats, new_tokens)        # copy new inputs in, then replay
+
+Requirements on ``fn``, as for any CUDA-graph capture:
+- no host synchronisation (the library's D-PACE target-range read-back is
+  skipped while a stream is capturing; ``check()`` reads the captured
+  forward's status word after a replay instead);
+- optimizers built with ``capturable=True``; autocast with
+  ``cache_enabled=False``;
+- gradients are set to None before capture (done here), so the captured
+  backward writes them fresh on every replay.
+Warm-up calls and the capture run on one side stream, so the library's
+per-stream workspace and status words exist before capture starts. Replays of
+one GraphedStep must not overlap (they share that workspace).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+
+class GraphedStep:
+    def __init__(self, fn, *example_inputs: torch.Tensor, warmup: int = 3, optimizers=()):
+        self.fn = fn
+        self.static = [t.detach().clone() for t in example_inputs]
+        dev = self.static[0].device if self.static else torch.device("cuda", torch.cuda.current_device())
+        self.device = dev
+        self.stream = torch.cuda.Stream(dev)
+        self.stream.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(self.stream):
+            for _ in range(warmup):
+                fn(*self.static)
+        torch.cuda.current_stream(dev).wait_stream(self.stream)
+        torch.cuda.synchronize(dev)
+        for opt in optimizers:
+            opt.zero_grad(set_to_none=True)
+        with torch.cuda.stream(self.stream):
+            self.status = _lib.status_words(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            self.out = fn(*self.static)
+        torch.cuda.synchronize(dev)
+
+    def __call__(self, *inputs: torch.Tensor):
+        if inputs:
+            if len(inputs) != len(self.static):
+                raise ValueError(f"expected {len(self.static)} inputs, got {len(inputs)}")
+            for st, x in zip(self.static, inputs):
+                st.copy_(x, non_blocking=True)
+        self.graph.replay()
+        return self.out
+
+    def check(self) -> None:
+        """Synchronises and raises as the eager calls would have: ValueError
+        for a D-PACE target outside [0, V) in the last replay, RuntimeError
+        for an expired bounded wait in any captured kernel."""
+        st = self.status[:3].tolist()
+        if st[_lib.STATUS_DPACE_BWD] or st[_lib.STATUS_DFLASH_BWD]:
+            self.status[1:3].zero_()
+            raise RuntimeError("a backward kernel of the captured step had a bounded wait expire")
+        if st[_lib.STATUS_DPACE_FWD] == _lib.ERR_TARGET_RANGE:
+            raise ValueError("targets out of range")
+        if st[_lib.STATUS_DPACE_FWD] == _lib.ERR_CUDA:
+            raise RuntimeError("a forward kernel of the captured step had a bounded wait expire")

@@ -64,6 +64,13 @@ _BWD_TIMEOUT_MSG = ("an earlier backward launch on this stream had a bounded wai
                     "its gradient that the failed part left unfinished hold NaN")
 
 
+def _capturing() -> bool:
+    """True while the current stream is being captured into a CUDA graph: no
+    read-back then (the status word stays on the device; see
+    specdec.graphs.GraphedStep.check)."""
+    return torch.cuda.is_current_stream_capturing()
+
+
 def _read_status(dev: torch.device, what: str, V: int) -> None:
     """One device-to-host read of this stream's status words, after a D-PACE
     forward: raises ValueError for an out-of-range target (the reference's
@@ -120,7 +127,7 @@ def _dpace_forward(logits: torch.Tensor, targets: torch.Tensor, mask: torch.Tens
         scale.data_ptr(), status.data_ptr(), scratch.data_ptr(), scratch.numel(),
         counters.data_ptr(), counters.numel(), _lib.stream_handle(dev))
     _lib.check(code, "specdec_dpace_forward")
-    if (VALIDATE_TARGETS if validate is None else validate) and N * B > 0:
+    if (VALIDATE_TARGETS if validate is None else validate) and N * B > 0 and not _capturing():
         _read_status(dev, "specdec_dpace_forward", V)
     return loss, lse, scale, loss_n
 
@@ -153,7 +160,7 @@ def _dpace_forward_backward(logits: torch.Tensor, targets: torch.Tensor, mask: t
         scale.data_ptr(), dlogits.data_ptr(), status.data_ptr(), scratch.data_ptr(), scratch.numel(),
         counters.data_ptr(), counters.numel(), _lib.stream_handle(dev))
     _lib.check(code, "specdec_dpace_forward_backward")
-    if (VALIDATE_TARGETS if validate is None else validate) and N * B > 0:
+    if (VALIDATE_TARGETS if validate is None else validate) and N * B > 0 and not _capturing():
         _read_status(dev, "specdec_dpace_forward_backward", V)
     return loss, dlogits, lse, scale, loss_n
 

@@ -24,7 +24,8 @@ def _ref_rms(x, w, eps):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("rows,D", [(1, 256), (100, 256), (16896, 256), (512, 4096), (37, 1000), (5, 257)])
+@pytest.mark.parametrize("rows,D", [(1, 256), (100, 256), (16896, 256), (512, 4096), (37, 1000), (5, 257),
+                                    (64, 2048), (8, 8192), (3, 8200), (300, 64)])
 def test_rmsnorm_forward_backward(cuda, dtype, rows, D):
     from specdec import drafter
 
