@@ -12,11 +12,14 @@
 // log-sum-exp of each query row's scaled scores, kept for a backward.
 //
 // One CTA per (b, h, 128-query tile), 4 warps; thread i owns query row i of
-// the tile, which is TMEM lane i. Per 128-key tile:
-//   1. all threads copy the K and V tiles from global memory into shared
-//      memory in the canonical 128-byte-swizzled layout (rows of 128 bytes,
-//      16-byte chunk c of row r stored at chunk c ^ (r % 8), 8-row atoms of
-//      1024 bytes), fence them to the async proxy, barrier;
+// the tile, which is TMEM lane i. The grid runs the heaviest query tiles
+// (those that see the most keys) first. Per 128-key tile:
+//   1. the K and V tiles are in shared memory in the canonical
+//      128-byte-swizzled layout (rows of 128 bytes, 16-byte chunk c of row r
+//      stored at chunk c ^ (r % 8), 8-row atoms of 1024 bytes), copied by
+//      cp.async ahead of use: the next K tile as soon as this tile's QK^T has
+//      read K, the next V tile as soon as P V has read V, so global-memory
+//      latency overlaps the softmax and the products;
 //   2. thread 0 issues S = Q K^T as four tcgen05.mma (M 128, N 128, K 16,
 //      bf16 in, fp32 accumulate in TMEM columns 0..127) and commits them to
 //      an mbarrier;
@@ -29,8 +32,8 @@
 //      128..191, and commits;
 //   5. every thread reads its row of O_tile and folds it into its register
 //      accumulator with the online-softmax rescaling.
-// The stages run one after another (the tiles are small: T ~ 528 gives at
-// most five key tiles per CTA). Every mbarrier wait is bounded; a wait that
+// Apart from the copies the stages run one after another (the tiles are
+// small: T ~ 528 gives at most five key tiles per CTA). Every mbarrier wait is bounded; a wait that
 // expires sets *status and the CTA stops issuing work, waits (bounded) for
 // what it issued and releases its TMEM.
 #include <atomic>
@@ -122,16 +125,32 @@ __device__ __forceinline__ void st_shared_u4(uint32_t addr, uint4 v) {
                : "memory");
 }
 
-// Copies rows [t0, t0 + 128) of one head of a [B, T, H, 64] bf16 tensor into
-// a swizzled shared tile (rows at or past T are zeros).
-__device__ __forceinline__ void load_tile(uint32_t tile, const bf16_t* base, int64_t row_stride, int t0, int T) {
+// Rows [t0, t0 + 128) of one head of a [B, T, H, 64] bf16 tensor into a
+// swizzled shared tile through cp.async (16 bytes per thread and chunk; rows
+// at or past T are zero-filled): the copies run while the thread goes on, and
+// cp_async_wait<n>() waits for all but the n most recently committed groups.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(valid ? 4 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void load_tile_async(uint32_t tile, const bf16_t* base, int64_t row_stride, int t0,
+                                                int T) {
 #pragma unroll
   for (int j = 0; j < (kTM * 8) / kThreads; ++j) {
     const int idx = threadIdx.x + j * kThreads;
     const int r = idx >> 3, c = idx & 7;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (t0 + r < T) v = *reinterpret_cast<const uint4*>(base + (int64_t)(t0 + r) * row_stride + c * 8);
-    st_shared_u4(tile + sw128((uint32_t)r, (uint32_t)c), v);
+    const bool valid = t0 + r < T;
+    const bf16_t* src = base + (valid ? (int64_t)(t0 + r) * row_stride + c * 8 : 0);
+    cp_async16(tile + sw128((uint32_t)r, (uint32_t)c), src, valid);
   }
 }
 
@@ -152,8 +171,10 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_fwd_kernel(const bf16
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kOffTmem);
 
   const int warp = threadIdx.x >> 5;
-  const int bh = blockIdx.y, b = bh / H, h = bh % H;
-  const int q0 = blockIdx.x * kTM;
+  // heaviest query tiles first (the last tile sees every key): blocks are
+  // dispatched in index order, x fastest
+  const int bh = blockIdx.x, b = bh / H, h = bh % H;
+  const int q0 = (gridDim.y - 1 - blockIdx.y) * kTM;
   const int64_t rs = (int64_t)H * kHD;  // row stride of [B, T, H, 64]
   const bf16_t* qb = q + (int64_t)b * T * rs + (int64_t)h * kHD;
   const bf16_t* kb = k + (int64_t)b * T * rs + (int64_t)h * kHD;
@@ -170,8 +191,12 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_fwd_kernel(const bf16
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  load_tile(base + kOffQ, qb, rs, q0, T);
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  // copies in flight: {Q, K tile 0}, then {V tile 0}
+  load_tile_async(base + kOffQ, qb, rs, q0, T);
+  load_tile_async(base + kOffK, kb, rs, 0, T);
+  cp_async_commit();
+  load_tile_async(base + kOffV, vb, rs, 0, T);
+  cp_async_commit();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -194,8 +219,8 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_fwd_kernel(const bf16
   bool ok = true;
 
   for (int k0 = 0; k0 < kv_end && ok; k0 += kTN) {
-    load_tile(base + kOffK, kb, rs, k0, T);
-    load_tile(base + kOffV, vb, rs, k0, T);
+    const bool more = k0 + kTN < kv_end;
+    cp_async_wait<1>();  // this K tile (and Q) landed; the newest group, this V tile, may be in flight
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
     __syncthreads();
@@ -212,6 +237,9 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_fwd_kernel(const bf16
       break;
     }
     tc_fence_after();
+    // the product has read K: the next K tile streams in during the softmax and P V
+    if (more) load_tile_async(base + kOffK, kb, rs, k0 + kTN, T);
+    cp_async_commit();
     // pass 1: the tile's masked maximum of this row (base-2 scaled scores)
     float mt = -INFINITY;
 #pragma unroll
@@ -252,6 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_fwd_kernel(const bf16
         st_shared_u4(atom + sw128(r, chunk), make_uint4(pk[4 * c4], pk[4 * c4 + 1], pk[4 * c4 + 2], pk[4 * c4 + 3]));
       }
     }
+    cp_async_wait<1>();  // this V tile; the next K tile may be in flight
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
     __syncthreads();
@@ -270,6 +299,8 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_fwd_kernel(const bf16
       break;
     }
     tc_fence_after();
+    if (more) load_tile_async(base + kOffV, vb, rs, k0 + kTN, T);  // the product has read V
+    cp_async_commit();
 #pragma unroll
     for (int cc = 0; cc < kHD / 32; ++cc) {
       float ot[32];
@@ -286,6 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_fwd_kernel(const bf16
     tc_fence_after();
   }
 
+  cp_async_wait<0>();  // no copy outlives the CTA
   if (!ok) {
     if (threadIdx.x == 0 && status) atomicExch(status, kStatusTimeout);
     // wait (bounded) for the products this CTA may still have in flight
@@ -323,7 +355,10 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_fwd_kernel(const bf16
 //     tile: S^T = K Q^T and dP^T = V dO^T, p^T and dS^T in bf16 to shared
 //     memory, dV += P^T dO and dK += dS^T Q (dO and Q as MN-major operands)
 //     in TMEM columns 256..319 / 320..383.
-// Each CTA holds all 512 TMEM columns (one CTA per SM).
+// Each CTA holds all 512 TMEM columns (one CTA per SM). Tiles arrive by
+// cp.async one step ahead: the dq kernel double-buffers K (its dS^T area is
+// spare) and refills V once dP has read it; the dkv kernel double-buffers the
+// query tile's Q, dO, lse and delta.
 // ---------------------------------------------------------------------------
 
 constexpr uint32_t kTmemAll = 512;
@@ -335,11 +370,16 @@ constexpr uint32_t kBOffB = 16384;    // dO            | V
 constexpr uint32_t kBOffC = 32768;    // K             | Q
 constexpr uint32_t kBOffD = 49152;    // V             | dO
 constexpr uint32_t kBOffP = 65536;    // dS            | P^T   (two atoms)
-constexpr uint32_t kBOffS = 98304;    // -             | dS^T  (two atoms)
+constexpr uint32_t kBOffS = 98304;    // K (odd tiles)  | dS^T  (two atoms)
 constexpr uint32_t kBOffRow = 131072; // -             | lse, delta of the query tile (2 x 128 floats)
 constexpr uint32_t kBOffBar = 132096;
 constexpr uint32_t kBOffTmem = kBOffBar + 16;
 constexpr uint32_t kBSmemBytes = kBOffTmem + 16 + 1024;
+// dkv kernel only: the second buffer set of the query tile (Q, dO, lse / delta)
+constexpr uint32_t kBOffC2 = 133120;
+constexpr uint32_t kBOffD2 = kBOffC2 + 16384;
+constexpr uint32_t kBOffRow2 = kBOffD2 + 16384;
+constexpr uint32_t kBSmemBytesKV = kBOffRow2 + 1024 + 1024;
 
 __device__ __forceinline__ bool visible(int qrow, int key, int T, int n_ctx) {
   return qrow < T && key < T && (qrow >= n_ctx || key <= qrow);
@@ -379,8 +419,8 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dq_kernel(
   uint64_t* bar = reinterpret_cast<uint64_t*>(gbase + kBOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kBOffTmem);
   const int warp = threadIdx.x >> 5;
-  const int bh = blockIdx.y, b = bh / H, h = bh % H;
-  const int q0 = blockIdx.x * kTM;
+  const int bh = blockIdx.x, b = bh / H, h = bh % H;
+  const int q0 = (gridDim.y - 1 - blockIdx.y) * kTM;  // heaviest query tiles first
   const int64_t rs = (int64_t)H * kHD;
   const int64_t head = (int64_t)b * T * rs + (int64_t)h * kHD;
   const int row = q0 + threadIdx.x;
@@ -391,8 +431,13 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dq_kernel(
     fence_mbar_init();
   }
   if (warp == 0) tmem_alloc_all(tmem_slot);
-  load_tile(base + kBOffA, q + head, rs, q0, T);
-  load_tile(base + kBOffB, dO + head, rs, q0, T);
+  // one copy group: Q, dO and the first K and V tiles (K double-buffered:
+  // tile j in the K area when j is even, in the spare area when odd)
+  load_tile_async(base + kBOffA, q + head, rs, q0, T);
+  load_tile_async(base + kBOffB, dO + head, rs, q0, T);
+  load_tile_async(base + kBOffC, k + head, rs, 0, T);
+  load_tile_async(base + kBOffD, v + head, rs, 0, T);
+  cp_async_commit();
   // delta = sum_d dO * O of this row, and its lse in base 2
   float delta = 0.f, lse2 = 0.f;
   if (row < T) {
@@ -421,15 +466,19 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dq_kernel(
   constexpr uint32_t kIdQ = instr_desc(kTM, kHD, 0, 1);
   uint32_t ph = 0;
   bool ok = true;
-  for (int k0 = 0; k0 < kv_end; k0 += kTN) {
-    load_tile(base + kBOffC, k + head, rs, k0, T);
-    load_tile(base + kBOffD, v + head, rs, k0, T);
+  for (int k0 = 0, it = 0; k0 < kv_end; k0 += kTN, ++it) {
+    const bool more = k0 + kTN < kv_end;
+    const uint32_t kcur = (it & 1) ? kBOffS : kBOffC, knext = (it & 1) ? kBOffC : kBOffS;
+    cp_async_wait<0>();  // this K and V tile
     cta_sync_tc();
+    // the other K buffer was last read by the previous tile's dQ product: fill it now
+    if (more) load_tile_async(base + knext, k + head, rs, k0 + kTN, T);
+    cp_async_commit();
     if (threadIdx.x == 0) {
 #pragma unroll
       for (int kk = 0; kk < kHD / 16; ++kk) {  // S = Q K^T, dP = dO V^T
         umma_bf16(tmem + kColS, smem_desc(base + kBOffA + kk * 32, 16, 1024),
-                  smem_desc(base + kBOffC + kk * 32, 16, 1024), kIdS, kk > 0);
+                  smem_desc(base + kcur + kk * 32, 16, 1024), kIdS, kk > 0);
         umma_bf16(tmem + kColDP, smem_desc(base + kBOffB + kk * 32, 16, 1024),
                   smem_desc(base + kBOffD + kk * 32, 16, 1024), kIdS, kk > 0);
       }
@@ -441,6 +490,8 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dq_kernel(
     }
     ph ^= 1u;
     tc_fence_after();
+    if (more) load_tile_async(base + kBOffD, v + head, rs, k0 + kTN, T);  // dP has read V
+    cp_async_commit();
 #pragma unroll
     for (int cc = 0; cc < kTN / 32; ++cc) {
       float sv[32], dp[32];
@@ -462,7 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dq_kernel(
       for (int kk = 0; kk < kTN / 16; ++kk)
         umma_bf16(tmem + kColAcc0,
                   smem_desc(base + kBOffP + (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u, 16, 1024),
-                  smem_desc(base + kBOffC + (uint32_t)kk * 2048u, 16384, 1024), kIdQ, (k0 > 0 || kk > 0) ? 1u : 0u);
+                  smem_desc(base + kcur + (uint32_t)kk * 2048u, 16384, 1024), kIdQ, (k0 > 0 || kk > 0) ? 1u : 0u);
       umma_commit(bar);
     }
     if (__syncthreads_or(!wait_bar(bar, ph) ? 1 : 0)) {
@@ -472,6 +523,7 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dq_kernel(
     ph ^= 1u;
     cta_sync_tc();
   }
+  cp_async_wait<0>();  // no copy outlives the CTA
   if (!ok) {
     if (threadIdx.x == 0 && status) atomicExch(status, kStatusTimeout);
     wait_bar(bar, ph);
@@ -511,11 +563,9 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dkv_kernel(
   unsigned char* gbase = smem_raw + (base - smem_u32(smem_raw));
   uint64_t* bar = reinterpret_cast<uint64_t*>(gbase + kBOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kBOffTmem);
-  float* sh_lse = reinterpret_cast<float*>(gbase + kBOffRow);
-  float* sh_delta = sh_lse + kTM;
   const int warp = threadIdx.x >> 5;
-  const int bh = blockIdx.y, b = bh / H, h = bh % H;
-  const int k0 = blockIdx.x * kTN;
+  const int bh = blockIdx.x, b = bh / H, h = bh % H;
+  const int k0 = blockIdx.y * kTN;  // the first key tiles are seen by the most query tiles: heaviest first
   const int64_t rs = (int64_t)H * kHD;
   const int64_t head = (int64_t)b * T * rs + (int64_t)h * kHD;
   const int64_t rowv = ((int64_t)b * H + h) * T;
@@ -527,15 +577,27 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dkv_kernel(
     fence_mbar_init();
   }
   if (warp == 0) tmem_alloc_all(tmem_slot);
-  load_tile(base + kBOffA, k + head, rs, k0, T);
-  load_tile(base + kBOffB, v + head, rs, k0, T);
-  cta_sync_tc();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
   // query tiles that see a key of this tile: context queries from the
   // diagonal on, and every tile holding a block slot
   const int qt_first = (k0 < n_ctx ? k0 : n_ctx) / kTM;
   const int qt_end = (T + kTM - 1) / kTM;
+  // Q, dO and the query rows' lse / delta of query tile qt sit in buffer set
+  // (qt - qt_first) & 1; the next set is filled while this one is used.
+  auto load_query_tile = [&](int qt, int set) {
+    const int qq = qt * kTM, qr = qq + threadIdx.x;
+    load_tile_async(base + (set ? kBOffC2 : kBOffC), q + head, rs, qq, T);
+    load_tile_async(base + (set ? kBOffD2 : kBOffD), dO + head, rs, qq, T);
+    const uint32_t rows = base + (set ? kBOffRow2 : kBOffRow);
+    cp_async4(rows + 4u * threadIdx.x, lse + rowv + (qr < T ? qr : 0), qr < T);
+    cp_async4(rows + 4u * (kTM + threadIdx.x), delta + rowv + (qr < T ? qr : 0), qr < T);
+  };
+  load_tile_async(base + kBOffA, k + head, rs, k0, T);
+  load_tile_async(base + kBOffB, v + head, rs, k0, T);
+  if (qt_first < qt_end) load_query_tile(qt_first, 0);
+  cp_async_commit();
+  cta_sync_tc();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
   constexpr uint32_t kIdS = instr_desc(kTN, kTM, 0, 0);
   constexpr uint32_t kIdKV = instr_desc(kTN, kHD, 0, 1);
   uint32_t ph = 0;
@@ -543,21 +605,22 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dkv_kernel(
   bool first = true;
   for (int qt = qt_first; qt < qt_end; ++qt) {
     const int q0 = qt * kTM;
-    load_tile(base + kBOffC, q + head, rs, q0, T);
-    load_tile(base + kBOffD, dO + head, rs, q0, T);
-    {
-      const int qr = q0 + threadIdx.x;
-      sh_lse[threadIdx.x] = qr < T ? lse[rowv + qr] * kLog2e : 0.f;
-      sh_delta[threadIdx.x] = qr < T ? delta[rowv + qr] : 0.f;
-    }
+    const int set = (qt - qt_first) & 1;
+    const uint32_t offq = set ? kBOffC2 : kBOffC, offg = set ? kBOffD2 : kBOffD;
+    const float* sh_lse = reinterpret_cast<const float*>(gbase + (set ? kBOffRow2 : kBOffRow));
+    const float* sh_delta = sh_lse + kTM;
+    cp_async_wait<0>();  // this query tile's Q, dO, lse and delta
     cta_sync_tc();
+    // the other set was last read by the previous tile's dV / dK products
+    if (qt + 1 < qt_end) load_query_tile(qt + 1, set ^ 1);
+    cp_async_commit();
     if (threadIdx.x == 0) {
 #pragma unroll
       for (int kk = 0; kk < kHD / 16; ++kk) {  // S^T = K Q^T, dP^T = V dO^T
         umma_bf16(tmem + kColS, smem_desc(base + kBOffA + kk * 32, 16, 1024),
-                  smem_desc(base + kBOffC + kk * 32, 16, 1024), kIdS, kk > 0);
+                  smem_desc(base + offq + kk * 32, 16, 1024), kIdS, kk > 0);
         umma_bf16(tmem + kColDP, smem_desc(base + kBOffB + kk * 32, 16, 1024),
-                  smem_desc(base + kBOffD + kk * 32, 16, 1024), kIdS, kk > 0);
+                  smem_desc(base + offg + kk * 32, 16, 1024), kIdS, kk > 0);
       }
       umma_commit(bar);
     }
@@ -576,8 +639,9 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dkv_kernel(
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
         const int c = cc * 32 + i;
-        const float p0 = visible(q0 + c, key, T, n_ctx) ? exp2f(sv[i] * sl2 - sh_lse[c]) : 0.f;
-        const float p1 = visible(q0 + c + 1, key, T, n_ctx) ? exp2f(sv[i + 1] * sl2 - sh_lse[c + 1]) : 0.f;
+        const float p0 = visible(q0 + c, key, T, n_ctx) ? exp2f(sv[i] * sl2 - sh_lse[c] * kLog2e) : 0.f;
+        const float p1 =
+            visible(q0 + c + 1, key, T, n_ctx) ? exp2f(sv[i + 1] * sl2 - sh_lse[c + 1] * kLog2e) : 0.f;
         wp[i / 2] = pack_bf16x2(p0, p1);
         wd[i / 2] = pack_bf16x2(p0 * (dp[i] - sh_delta[c]) * scale, p1 * (dp[i + 1] - sh_delta[c + 1]) * scale);
       }
@@ -591,9 +655,9 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dkv_kernel(
         const uint32_t acc = (!first || kk > 0) ? 1u : 0u;
         const uint32_t aoff = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
         umma_bf16(tmem + kColAcc0, smem_desc(base + kBOffP + aoff, 16, 1024),
-                  smem_desc(base + kBOffD + (uint32_t)kk * 2048u, 16384, 1024), kIdKV, acc);
+                  smem_desc(base + offg + (uint32_t)kk * 2048u, 16384, 1024), kIdKV, acc);
         umma_bf16(tmem + kColAcc1, smem_desc(base + kBOffS + aoff, 16, 1024),
-                  smem_desc(base + kBOffC + (uint32_t)kk * 2048u, 16384, 1024), kIdKV, acc);
+                  smem_desc(base + offq + (uint32_t)kk * 2048u, 16384, 1024), kIdKV, acc);
       }
       umma_commit(bar);
     }
@@ -605,6 +669,7 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dkv_kernel(
     first = false;
     cta_sync_tc();
   }
+  cp_async_wait<0>();  // no copy outlives the CTA
   if (!ok) {
     if (threadIdx.x == 0 && status) atomicExch(status, kStatusTimeout);
     wait_bar(bar, ph);
@@ -662,7 +727,7 @@ cudaError_t dflash_attn_fwd_launch(const void* q, const void* k, const void* v, 
                                    int H, int n_ctx, float scale, int* status, cudaStream_t st) {
   const cudaError_t e = ensure_smem_limit_attn(kSmemBytes);
   if (e != cudaSuccess) return e;
-  const dim3 grid((unsigned)((T + kTM - 1) / kTM), (unsigned)(batch * H));
+  const dim3 grid((unsigned)(batch * H), (unsigned)((T + kTM - 1) / kTM));
   dflash_attn_fwd_kernel<<<grid, kThreads, kSmemBytes, st>>>(
       static_cast<const bf16_t*>(q), static_cast<const bf16_t*>(k), static_cast<const bf16_t*>(v),
       static_cast<bf16_t*>(o), lse, T, H, n_ctx, scale * kLog2e, status);
@@ -681,18 +746,18 @@ cudaError_t dflash_attn_bwd_launch(const void* q, const void* k, const void* v, 
     e = cudaFuncSetAttribute(dflash_attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBSmemBytes);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(dflash_attn_bwd_dkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)kBSmemBytes);
+                               (int)kBSmemBytesKV);
     if (e != cudaSuccess) return e;
     done.fetch_or(bit);
   }
-  const dim3 grid((unsigned)((T + kTM - 1) / kTM), (unsigned)(batch * H));
+  const dim3 grid((unsigned)(batch * H), (unsigned)((T + kTM - 1) / kTM));
   dflash_attn_bwd_dq_kernel<<<grid, kThreads, kBSmemBytes, st>>>(
       static_cast<const bf16_t*>(q), static_cast<const bf16_t*>(k), static_cast<const bf16_t*>(v),
       static_cast<const bf16_t*>(o), lse, static_cast<const bf16_t*>(dO), static_cast<bf16_t*>(dq), delta, T, H,
       n_ctx, scale, status);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  dflash_attn_bwd_dkv_kernel<<<grid, kThreads, kBSmemBytes, st>>>(
+  dflash_attn_bwd_dkv_kernel<<<grid, kThreads, kBSmemBytesKV, st>>>(
       static_cast<const bf16_t*>(q), static_cast<const bf16_t*>(k), static_cast<const bf16_t*>(v), lse, delta,
       static_cast<const bf16_t*>(dO), static_cast<bf16_t*>(dk), static_cast<bf16_t*>(dv), T, H, n_ctx, scale,
       status);

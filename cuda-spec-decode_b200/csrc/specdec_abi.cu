@@ -880,7 +880,8 @@ int specdec_dflash_attention_forward(const uint16_t* q, const uint16_t* k, const
   if (head_dim != 64) return fail(SPECDEC_ERR_ARGUMENT, "head_dim must be 64, got %d", head_dim);
   if (batch < 0 || T < 0 || heads < 1) return fail(SPECDEC_ERR_ARGUMENT, "bad shape");
   if (n_ctx < 0 || n_ctx > T) return fail(SPECDEC_ERR_ARGUMENT, "n_ctx must be in [0, T] (n_ctx=%d, T=%d)", n_ctx, T);
-  if ((int64_t)batch * heads > 65535) return fail(SPECDEC_ERR_ARGUMENT, "batch * heads must be <= 65535");
+  if ((int64_t)batch * heads > INT32_MAX) return fail(SPECDEC_ERR_ARGUMENT, "batch * heads must fit in int32");
+  if ((T + 127) / 128 > 65535) return fail(SPECDEC_ERR_ARGUMENT, "T must be <= 65535 * 128");
   if (!(scale > 0.f)) return fail(SPECDEC_ERR_VALUE, "scale must be > 0");
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (status) {
@@ -908,7 +909,8 @@ int specdec_dflash_attention_backward(const uint16_t* q, const uint16_t* k, cons
   if (head_dim != 64) return fail(SPECDEC_ERR_ARGUMENT, "head_dim must be 64, got %d", head_dim);
   if (batch < 0 || T < 0 || heads < 1) return fail(SPECDEC_ERR_ARGUMENT, "bad shape");
   if (n_ctx < 0 || n_ctx > T) return fail(SPECDEC_ERR_ARGUMENT, "n_ctx must be in [0, T] (n_ctx=%d, T=%d)", n_ctx, T);
-  if ((int64_t)batch * heads > 65535) return fail(SPECDEC_ERR_ARGUMENT, "batch * heads must be <= 65535");
+  if ((int64_t)batch * heads > INT32_MAX) return fail(SPECDEC_ERR_ARGUMENT, "batch * heads must fit in int32");
+  if ((T + 127) / 128 > 65535) return fail(SPECDEC_ERR_ARGUMENT, "T must be <= 65535 * 128");
   if (!(scale > 0.f)) return fail(SPECDEC_ERR_VALUE, "scale must be > 0");
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (status) {

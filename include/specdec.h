@@ -306,7 +306,7 @@ int specdec_rmsnorm_backward(const void* x, const float* weight, const float* rs
  *   status      [1] int32 or NULL: SPECDEC_ERR_CUDA if a bounded wait of
  *               the kernel expired (the outputs are then unspecified)
  * P = softmax is rounded to bf16 before the second product, the
- * accumulation is fp32. 0 <= n_ctx <= T, batch * heads <= 65535.
+ * accumulation is fp32. 0 <= n_ctx <= T <= 65535 * 128.
  */
 int specdec_dflash_attention_forward(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* o,
                                      float* lse, int32_t batch, int32_t T, int32_t heads, int32_t head_dim,
