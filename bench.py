@@ -369,11 +369,15 @@ class Timing:
         them). Returns (mean forward ms, mean backward ms), max over ranks.
 
         With --graphs 1 the forward and the backward of each input set are
-        captured as two CUDA graphs (after eager warm-up calls on the capture
-        stream) and replayed between the events. A ~1 ms device-side spin
-        ahead of the first event lets the host's enqueueing run ahead of the
-        GPU, so each interval is device time, not Python launch latency."""
+        captured as two CUDA graphs of `reps` back-to-back calls each (after
+        eager warm-up calls on the capture stream) and replayed between the
+        events; a figure is the graph's time / reps, so it holds the calls'
+        device time without a graph launch's latency. A ~1 ms device-side
+        spin ahead of the first event lets the host's enqueueing run ahead of
+        the GPU."""
+        reps = 1
         if self.args.graphs:
+            reps = 8
             cap = torch.cuda.Stream(self.dev)
             cap.wait_stream(self.stream)
             with torch.cuda.stream(cap):
@@ -386,9 +390,11 @@ class Timing:
             for s_ in range(n_sets):
                 g1, g2 = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g1, stream=cap):
-                    loss, st = fwd(s_)
+                    for _ in range(reps):
+                        loss, st = fwd(s_)
                 with torch.cuda.graph(g2, stream=cap):
-                    bwd(s_, st)
+                    for _ in range(reps):
+                        bwd(s_, st)
                 gf.append(g1)
                 gb.append(g2)
                 outs.append((loss, st))
@@ -414,8 +420,8 @@ class Timing:
             evs[k][3].record(self.stream)
             self.settle()
         torch.cuda.synchronize(self.dev)
-        f = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
-        g = statistics.mean(e[2].elapsed_time(e[3]) for e in evs)
+        f = statistics.mean(e[0].elapsed_time(e[1]) for e in evs) / reps
+        g = statistics.mean(e[2].elapsed_time(e[3]) for e in evs) / reps
         return self.max(f), self.max(g)
 
 
@@ -651,7 +657,10 @@ def time_drafter_step(args, dev, world, max_over_ranks, barrier):
     with torch.no_grad():
         head_bf16.weight.copy_(head.weight)
     g = torch.Generator(device=dev).manual_seed(99 + int(os.environ.get("RANK", "0")))
-    feats = torch.randn(Nb, S, D, device=dev, generator=g, dtype=torch.bfloat16).float()
+    # the verifier's features are bf16; the fp32-logit variants take them widened to fp32 (the
+    # reference loss is fp32-only), the bf16-autocast variants as they are
+    feats_bf16 = torch.randn(Nb, S, D, device=dev, generator=g, dtype=torch.bfloat16)
+    feats = feats_bf16.float()
     tokens = torch.randint(0, V, (Nb, blk), device=dev, generator=g)
     mask = torch.ones(Nb, blk, device=dev)
     mask[:, 0] = 0.0
@@ -705,13 +714,13 @@ def time_drafter_step(args, dev, world, max_over_ranks, barrier):
         if graphed:
             from specdec.graphs import GraphedStep
 
-            gstep = GraphedStep(step_fn, feats, tokens, optimizers=(opt,))
+            gstep = GraphedStep(step_fn, feats_bf16 if autocast else feats, tokens, optimizers=(opt,))
             step = gstep
         else:
             gstep = None
 
             def step():
-                return step_fn(feats, tokens)
+                return step_fn(feats_bf16 if autocast else feats, tokens)
 
         for _ in range(3):
             step()
@@ -735,14 +744,16 @@ def time_drafter_step(args, dev, world, max_over_ranks, barrier):
         torch.cuda.empty_cache()
     layer_kernels.set_enabled(True)
     torch.backends.cuda.matmul.allow_tf32 = prev_tf32
-    del head, head_bf16, feats
+    del head, head_bf16, feats, feats_bf16
     torch.cuda.empty_cache()
     base = out["torch_ops_loss_fp32_logits"]["ms_per_step"]
     for v in out.values():
         v["speedup_vs_torch_ops_loss"] = round(base / v["ms_per_step"], 3)
     return {"metric": "drafter training step (fwd + loss + bwd + AdamW) rows/s",
             "steps": args.drafter_steps,
-            "config": {"workload": "dflash_drafter_step", "features": [Nb, S, D], "d_model": 256, "layers": 3,
+            "config": {"workload": "dflash_drafter_step", "features": [Nb, S, D],
+                       "features_dtype": "bf16, widened to fp32 for the fp32-logit variants", "d_model": 256,
+                       "layers": 3,
                        "heads": 4, "block_size": blk, "V": V, "lm_head": "frozen, random",
                        "objective": "dpace alpha 0.5, anchor slot masked", "optimizer": "AdamW lr 1e-3, clip 1.0",
                        "gemms": "cuBLAS, TF32 for fp32", "parallelism": f"ddp{world}",
@@ -926,8 +937,9 @@ def run_ours(args):
                                "public API's 4-byte status read-back is timed in e2e)",
                        "launch": "one CUDA graph per step (the step's 3 kernel launches), replayed"
                                  if args.graphs else "eager launches from Python",
-                       "split": "forward and backward each captured as a CUDA graph and replayed "
-                                "between events" if args.graphs else "eager calls between events"},
+                       "split": "forward and backward each captured as a CUDA graph of 8 back-to-back calls, "
+                                "replayed between events (time / 8)" if args.graphs else
+                                "eager calls between events"},
             "rows_per_s": rep["rows_per_s"],
             "moved_bytes_per_step": rep["moved_bytes_per_step"],
             "pct_of_hbm_peak": rep["pct_of_hbm_peak"], "pct_basis": rep["pct_basis"],

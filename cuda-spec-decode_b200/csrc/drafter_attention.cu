@@ -240,23 +240,34 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_fwd_kernel(const bf16
     // the product has read K: the next K tile streams in during the softmax and P V
     if (more) load_tile_async(base + kOffK, kb, rs, k0 + kTN, T);
     cp_async_commit();
-    // pass 1: the tile's masked maximum of this row (base-2 scaled scores)
-    float mt = -INFINITY;
+    // every row of this query tile sees every key of this key tile: no
+    // per-element mask (a context row sees keys up to itself, a block row all
+    // keys; rows past T are never stored)
+    const bool full = k0 + kTN <= T && (q0 >= n_ctx || k0 + kTN - 1 <= q0);
+    // pass 1: the tile's (masked) maximum of this row; the base-2 scale is
+    // positive, so scaling the maximum equals the maximum of scaled scores
+    float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
     for (int cc = 0; cc < kTN / 32; ++cc) {
       float s[32];
       tmem_ld32(tmem + lane_base + cc * 32, s);
+      if (full) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int j = k0 + cc * 32 + i;
-        const bool valid = j < T && (row >= n_ctx || j <= row);
-        if (valid) mt = fmaxf(mt, s[i] * scale_log2);
+        for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], s[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int j = k0 + cc * 32 + i;
+          if (j < T && (row >= n_ctx || j <= row)) mx[i & 3] = fmaxf(mx[i & 3], s[i]);
+        }
       }
     }
+    const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale_log2;
     const float m_new = fmaxf(m_run, mt);
-    const float alpha = m_run == -INFINITY ? 0.f : exp2f(m_run - m_new);
-    // pass 2: p = 2^(s' - m_new), row sum, P in bf16 to shared memory
-    float lt = 0.f;
+    const float alpha = m_run == -INFINITY ? 0.f : exp2_approx(m_run - m_new);
+    const float nm = -m_new;
+    // pass 2: p = 2^(s * scale_log2 - m_new), row sum, P in bf16 to shared memory
+    float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int cc = 0; cc < kTN / 32; ++cc) {
       float s[32];
@@ -264,12 +275,14 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_fwd_kernel(const bf16
       uint32_t pk[16];
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
-        const int j = k0 + cc * 32 + i;
-        const bool v0 = j < T && (row >= n_ctx || j <= row);
-        const bool v1 = j + 1 < T && (row >= n_ctx || j + 1 <= row);
-        const float p0 = v0 ? exp2f(s[i] * scale_log2 - m_new) : 0.f;
-        const float p1 = v1 ? exp2f(s[i + 1] * scale_log2 - m_new) : 0.f;
-        lt += p0 + p1;
+        float p0 = exp2_approx(fmaf(s[i], scale_log2, nm));
+        float p1 = exp2_approx(fmaf(s[i + 1], scale_log2, nm));
+        if (!full) {
+          const int j = k0 + cc * 32 + i;
+          p0 = (j < T && (row >= n_ctx || j <= row)) ? p0 : 0.f;
+          p1 = (j + 1 < T && (row >= n_ctx || j + 1 <= row)) ? p1 : 0.f;
+        }
+        ls[(i >> 1) & 3] += p0 + p1;
         pk[i / 2] = pack_bf16x2(p0, p1);
       }
       const uint32_t r = (uint32_t)threadIdx.x;
@@ -280,6 +293,7 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_fwd_kernel(const bf16
         st_shared_u4(atom + sw128(r, chunk), make_uint4(pk[4 * c4], pk[4 * c4 + 1], pk[4 * c4 + 2], pk[4 * c4 + 3]));
       }
     }
+    const float lt = (ls[0] + ls[1]) + (ls[2] + ls[3]);
     cp_async_wait<1>();  // this V tile; the next K tile may be in flight
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
@@ -492,6 +506,8 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dq_kernel(
     tc_fence_after();
     if (more) load_tile_async(base + kBOffD, v + head, rs, k0 + kTN, T);  // dP has read V
     cp_async_commit();
+    // every row of the query tile sees every key of the key tile: no per-element mask
+    const bool full = k0 + kTN <= T && (q0 >= n_ctx || k0 + kTN - 1 <= q0);
 #pragma unroll
     for (int cc = 0; cc < kTN / 32; ++cc) {
       float sv[32], dp[32];
@@ -500,9 +516,13 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dq_kernel(
       uint32_t w[16];
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
-        const int j = k0 + cc * 32 + i;
-        const float p0 = visible(row, j, T, n_ctx) ? exp2f(sv[i] * sl2 - lse2) : 0.f;
-        const float p1 = visible(row, j + 1, T, n_ctx) ? exp2f(sv[i + 1] * sl2 - lse2) : 0.f;
+        float p0 = exp2_approx(fmaf(sv[i], sl2, -lse2));
+        float p1 = exp2_approx(fmaf(sv[i + 1], sl2, -lse2));
+        if (!full) {
+          const int j = k0 + cc * 32 + i;
+          p0 = visible(row, j, T, n_ctx) ? p0 : 0.f;
+          p1 = visible(row, j + 1, T, n_ctx) ? p1 : 0.f;
+        }
         w[i / 2] = pack_bf16x2(p0 * (dp[i] - delta) * scale, p1 * (dp[i + 1] - delta) * scale);
       }
       st_row32(base + kBOffP, (uint32_t)threadIdx.x, cc, w);
@@ -630,6 +650,8 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dkv_kernel(
     }
     ph ^= 1u;
     tc_fence_after();
+    // every query of the tile sees every key of this CTA's tile: no per-element mask
+    const bool full = k0 + kTN <= T && q0 + kTM <= T && (q0 >= n_ctx || k0 + kTN - 1 <= q0);
 #pragma unroll
     for (int cc = 0; cc < kTM / 32; ++cc) {
       float sv[32], dp[32];
@@ -639,9 +661,12 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dkv_kernel(
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
         const int c = cc * 32 + i;
-        const float p0 = visible(q0 + c, key, T, n_ctx) ? exp2f(sv[i] * sl2 - sh_lse[c] * kLog2e) : 0.f;
-        const float p1 =
-            visible(q0 + c + 1, key, T, n_ctx) ? exp2f(sv[i + 1] * sl2 - sh_lse[c + 1] * kLog2e) : 0.f;
+        float p0 = exp2_approx(fmaf(sv[i], sl2, -sh_lse[c] * kLog2e));
+        float p1 = exp2_approx(fmaf(sv[i + 1], sl2, -sh_lse[c + 1] * kLog2e));
+        if (!full) {
+          p0 = visible(q0 + c, key, T, n_ctx) ? p0 : 0.f;
+          p1 = visible(q0 + c + 1, key, T, n_ctx) ? p1 : 0.f;
+        }
         wp[i / 2] = pack_bf16x2(p0, p1);
         wd[i / 2] = pack_bf16x2(p0 * (dp[i] - sh_delta[c]) * scale, p1 * (dp[i + 1] - sh_delta[c + 1]) * scale);
       }
