@@ -41,7 +41,10 @@ int cuda_fail(cudaError_t e, const char* what) {
 // Smallest CTA chunk in elements: below this, per-piece bookkeeping dominates.
 constexpr int64_t kMinChunk = 1024;
 
-std::atomic<int> g_shape[4] = {0, 0, 0, 0};
+// SPECDEC_SHAPE_DEFAULT (-1): the built-in choice per kernel and dtype (see
+// ring_shape); any other value is the caller's.
+std::atomic<int> g_shape[4] = {SPECDEC_SHAPE_DEFAULT, SPECDEC_SHAPE_DEFAULT, SPECDEC_SHAPE_DEFAULT,
+                               SPECDEC_SHAPE_DEFAULT};
 std::atomic<int> g_cap[4] = {0, 0, 0, 0};
 std::atomic<int> g_static_queue{0};  // 1: ring kernels use a static block interleave
 std::atomic<int> g_withhold_stage{0};  // failure-detection tests: launches left to withhold a stage
@@ -65,6 +68,7 @@ bool has_ring_path(int kernel) { return kernel >= 0 && kernel <= 3; }
 // Variant id inside the chosen kernel family.
 int kernel_shape(int kernel, bool tma) {
   const int raw = g_shape[kernel].load();
+  if (raw < 0) return 0;  // default: fp32 ring shape 0, or the 128-bit-load kernels' shape 0
   if (tma) return raw;
   if (!has_ring_path(kernel)) return raw % kLdgShapeBase;
   return raw >= kLdgShapeBase ? raw - kLdgShapeBase : 0;
@@ -75,9 +79,13 @@ bool use_tma(int kernel, bool ptrs_aligned) {
 }
 
 // bf16 has only the ring kernels: a shape that selects the 128-bit-load
-// kernels falls back to ring shape 0.
+// kernels falls back to ring shape 0. Default: ring shape 0, except the
+// D-PACE forward, ring shape 6 (16 consumer warps per SM: the bf16 forward is
+// bound by its consumers' exponentials, and measured 5% faster there at
+// [64, 16, 128256]; the fp32 forward is not, and keeps shape 0).
 int bf16_shape(int kernel) {
   const int raw = g_shape[kernel].load();
+  if (raw < 0) return kernel == SPECDEC_KERNEL_DPACE_FWD ? 6 : 0;
   return raw < kLdgShapeBase ? raw : 0;
 }
 
@@ -263,7 +271,8 @@ const char* specdec_status_string(int code) {
 
 int specdec_set_launch_shape(int32_t kernel, int32_t shape, int32_t ctas_per_sm) {
   if (kernel < 0 || kernel > 3) return fail(SPECDEC_ERR_ARGUMENT, "unknown kernel id %d", kernel);
-  if (shape < 0 || (shape > kMaxRingShape[kernel] && shape < kLdgShapeBase) || shape > kLdgShapeBase + 4)
+  if (shape < SPECDEC_SHAPE_DEFAULT || (shape > kMaxRingShape[kernel] && shape < kLdgShapeBase) ||
+      shape > kLdgShapeBase + 4)
     return fail(SPECDEC_ERR_ARGUMENT, "unknown launch shape %d", shape);
   if (ctas_per_sm < 0 || ctas_per_sm > 32)
     return fail(SPECDEC_ERR_ARGUMENT, "ctas_per_sm must be in [0, 32], got %d", ctas_per_sm);

@@ -29,6 +29,7 @@ KERNEL_DPACE_FWD = 0
 KERNEL_DPACE_BWD = 1
 KERNEL_DFLASH_FWD = 2
 KERNEL_DFLASH_BWD = 3
+SHAPE_DEFAULT = -1  # set_launch_shape: the built-in choice per kernel and dtype
 
 _c_i32 = ctypes.c_int32
 _c_i64 = ctypes.c_int64

@@ -341,6 +341,10 @@ int specdec_dflash_attention_backward(const uint16_t* q, const uint16_t* k, cons
 #define SPECDEC_KERNEL_DFLASH_FWD 2
 #define SPECDEC_KERNEL_DFLASH_BWD 3
 
+/* specdec_set_launch_shape: the built-in choice (ring shape 0 for every
+ * kernel and dtype, except ring shape 6 for the bf16 D-PACE forward). */
+#define SPECDEC_SHAPE_DEFAULT (-1)
+
 /*
  * Selects a kernel variant and caps resident CTAs per SM (0 = occupancy
  * limit) for one kernel, process-wide. Shapes 0..5 (0..6 for the D-PACE
@@ -348,8 +352,9 @@ int specdec_dflash_attention_backward(const uint16_t* q, const uint16_t* k, cons
  * streamed pointers are 16-byte
  * aligned; otherwise the 128-bit-load kernels run with their default shape);
  * 10..14 force the 128-bit-load kernels, variant shape - 10 (bf16 entry
- * points, which have only the ring kernels, then use ring shape 0). Workspace
- * sizes depend on it: query sizes after changing it.
+ * points, which have only the ring kernels, then use ring shape 0);
+ * SPECDEC_SHAPE_DEFAULT restores the built-in choice. Workspace sizes depend
+ * on it: query sizes after changing it.
  */
 int specdec_set_launch_shape(int32_t kernel, int32_t shape, int32_t ctas_per_sm);
 

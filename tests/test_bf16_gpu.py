@@ -203,7 +203,7 @@ def test_bf16_every_launch_shape(cuda, shape):
             _check_grad(g, g_ref)
     finally:
         for k in range(4):
-            _lib.set_launch_shape(k, 0, 0)
+            _lib.set_launch_shape(k, _lib.SHAPE_DEFAULT, 0)
 
 
 def test_bf16_ring_results_are_schedule_independent(cuda):

@@ -220,8 +220,8 @@ def test_every_launch_shape_matches_golden(cuda, gf, shape):
                 np.testing.assert_allclose(grad.reshape(-1)[idx], gf[f"{key}/probe_val"], rtol=0,
                                            atol=GRAD_ATOL)
     finally:
-        _lib.set_launch_shape(_lib.KERNEL_DFLASH_FWD, 0)
-        _lib.set_launch_shape(_lib.KERNEL_DFLASH_BWD, 0)
+        _lib.set_launch_shape(_lib.KERNEL_DFLASH_FWD, _lib.SHAPE_DEFAULT)
+        _lib.set_launch_shape(_lib.KERNEL_DFLASH_BWD, _lib.SHAPE_DEFAULT)
 
 
 def test_static_interleave_and_schedule_independence(cuda):

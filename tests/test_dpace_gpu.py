@@ -316,8 +316,8 @@ def test_every_launch_shape_matches_golden(cuda, gd, shape):
                 np.testing.assert_allclose(grad.reshape(-1)[idx], gd[f"{key}/probe_val"], rtol=0,
                                            atol=GRAD_ATOL)
     finally:
-        _lib.set_launch_shape(_lib.KERNEL_DPACE_FWD, 0)
-        _lib.set_launch_shape(_lib.KERNEL_DPACE_BWD, 0)
+        _lib.set_launch_shape(_lib.KERNEL_DPACE_FWD, _lib.SHAPE_DEFAULT)
+        _lib.set_launch_shape(_lib.KERNEL_DPACE_BWD, _lib.SHAPE_DEFAULT)
 
 
 def test_static_block_interleave_matches_golden(cuda, gd):
