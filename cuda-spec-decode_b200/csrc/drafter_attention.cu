@@ -142,11 +142,12 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+template <int NT = kThreads>
 __device__ __forceinline__ void load_tile_async(uint32_t tile, const bf16_t* base, int64_t row_stride, int t0,
                                                 int T) {
 #pragma unroll
-  for (int j = 0; j < (kTM * 8) / kThreads; ++j) {
-    const int idx = threadIdx.x + j * kThreads;
+  for (int j = 0; j < (kTM * 8) / NT; ++j) {
+    const int idx = threadIdx.x + j * NT;
     const int r = idx >> 3, c = idx & 7;
     const bool valid = t0 + r < T;
     const bf16_t* src = base + (valid ? (int64_t)(t0 + r) * row_stride + c * 8 : 0);
@@ -376,6 +377,11 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_fwd_kernel(const bf16
 // ---------------------------------------------------------------------------
 
 constexpr uint32_t kTmemAll = 512;
+// Backward CTAs: 8 warps. Warps w and w + 4 share TMEM lanes 32 (w % 4) ..
+// 32 (w % 4) + 31 (one row each, thread t and t + 128), and split a tile's
+// 128 columns into halves: with the row's log-sum-exp known, the halves are
+// independent.
+constexpr int kBThreads = 256;
 constexpr uint32_t kColS = 0, kColDP = 128, kColAcc0 = 256, kColAcc1 = 320;
 
 // Shared memory of the backward kernels (offsets from a 1024-byte-aligned base).
@@ -423,7 +429,7 @@ __device__ __forceinline__ void cta_sync_tc() {
   tc_fence_after();
 }
 
-__global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dq_kernel(
+__global__ void __launch_bounds__(kBThreads, 1) dflash_attn_bwd_dq_kernel(
     const bf16_t* __restrict__ q, const bf16_t* __restrict__ k, const bf16_t* __restrict__ v,
     const bf16_t* __restrict__ o, const float* __restrict__ lse, const bf16_t* __restrict__ dO,
     bf16_t* __restrict__ dq, float* __restrict__ delta_out, int T, int H, int n_ctx, float scale, int* status) {
@@ -437,7 +443,8 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dq_kernel(
   const int q0 = (gridDim.y - 1 - blockIdx.y) * kTM;  // heaviest query tiles first
   const int64_t rs = (int64_t)H * kHD;
   const int64_t head = (int64_t)b * T * rs + (int64_t)h * kHD;
-  const int row = q0 + threadIdx.x;
+  const int r_in = threadIdx.x & (kTM - 1), half = threadIdx.x >> 7;
+  const int row = q0 + r_in;
   const float sl2 = scale * kLog2e;
 
   if (threadIdx.x == 0) {
@@ -447,12 +454,12 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dq_kernel(
   if (warp == 0) tmem_alloc_all(tmem_slot);
   // one copy group: Q, dO and the first K and V tiles (K double-buffered:
   // tile j in the K area when j is even, in the spare area when odd)
-  load_tile_async(base + kBOffA, q + head, rs, q0, T);
-  load_tile_async(base + kBOffB, dO + head, rs, q0, T);
-  load_tile_async(base + kBOffC, k + head, rs, 0, T);
-  load_tile_async(base + kBOffD, v + head, rs, 0, T);
+  load_tile_async<kBThreads>(base + kBOffA, q + head, rs, q0, T);
+  load_tile_async<kBThreads>(base + kBOffB, dO + head, rs, q0, T);
+  load_tile_async<kBThreads>(base + kBOffC, k + head, rs, 0, T);
+  load_tile_async<kBThreads>(base + kBOffD, v + head, rs, 0, T);
   cp_async_commit();
-  // delta = sum_d dO * O of this row, and its lse in base 2
+  // delta = sum_d dO * O of this row (both threads of the row), and its lse in base 2
   float delta = 0.f, lse2 = 0.f;
   if (row < T) {
     const bf16_t* orow = o + head + (int64_t)row * rs;
@@ -468,12 +475,12 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dq_kernel(
         delta = fmaf(bf16_hi(aw[i]), bf16_hi(gw[i]), delta);
       }
     }
-    delta_out[((int64_t)b * H + h) * T + row] = delta;
+    if (half == 0) delta_out[((int64_t)b * H + h) * T + row] = delta;
     lse2 = lse[((int64_t)b * H + h) * T + row] * kLog2e;
   }
   cta_sync_tc();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
   const int q_last = min(q0 + kTM, T) - 1;
   const int kv_end = q_last >= n_ctx ? T : q_last + 1;
   constexpr uint32_t kIdS = instr_desc(kTM, kTN, 0, 0);
@@ -486,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dq_kernel(
     cp_async_wait<0>();  // this K and V tile
     cta_sync_tc();
     // the other K buffer was last read by the previous tile's dQ product: fill it now
-    if (more) load_tile_async(base + knext, k + head, rs, k0 + kTN, T);
+    if (more) load_tile_async<kBThreads>(base + knext, k + head, rs, k0 + kTN, T);
     cp_async_commit();
     if (threadIdx.x == 0) {
 #pragma unroll
@@ -504,12 +511,13 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dq_kernel(
     }
     ph ^= 1u;
     tc_fence_after();
-    if (more) load_tile_async(base + kBOffD, v + head, rs, k0 + kTN, T);  // dP has read V
+    if (more) load_tile_async<kBThreads>(base + kBOffD, v + head, rs, k0 + kTN, T);  // dP has read V
     cp_async_commit();
     // every row of the query tile sees every key of the key tile: no per-element mask
     const bool full = k0 + kTN <= T && (q0 >= n_ctx || k0 + kTN - 1 <= q0);
 #pragma unroll
-    for (int cc = 0; cc < kTN / 32; ++cc) {
+    for (int c2 = 0; c2 < kTN / 64; ++c2) {
+      const int cc = half * (kTN / 64) + c2;  // this thread's half of the columns
       float sv[32], dp[32];
       tmem_ld32(tmem + lane_base + kColS + cc * 32, sv);
       tmem_ld32(tmem + lane_base + kColDP + cc * 32, dp);
@@ -525,7 +533,7 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dq_kernel(
         }
         w[i / 2] = pack_bf16x2(p0 * (dp[i] - delta) * scale, p1 * (dp[i + 1] - delta) * scale);
       }
-      st_row32(base + kBOffP, (uint32_t)threadIdx.x, cc, w);
+      st_row32(base + kBOffP, (uint32_t)r_in, cc, w);
     }
     cta_sync_tc();
     if (threadIdx.x == 0) {  // dQ += dS K
@@ -549,18 +557,12 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dq_kernel(
     wait_bar(bar, ph);
   } else {
     tc_fence_after();
-    float acc[kHD];
-#pragma unroll
-    for (int cc = 0; cc < kHD / 32; ++cc) {
-      float t[32];
-      tmem_ld32(tmem + lane_base + kColAcc0 + cc * 32, t);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) acc[cc * 32 + i] = t[i];
-    }
+    float acc[32];  // this thread's half of the row's 64 dQ columns
+    tmem_ld32(tmem + lane_base + kColAcc0 + half * 32, acc);
     if (row < T) {
-      bf16_t* drow = dq + head + (int64_t)row * rs;
+      bf16_t* drow = dq + head + (int64_t)row * rs + half * 32;
 #pragma unroll
-      for (int c = 0; c < kHD / 8; ++c) {
+      for (int c = 0; c < 4; ++c) {
         const float* a = acc + 8 * c;
         *reinterpret_cast<uint4*>(drow + 8 * c) = make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]),
                                                               pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
@@ -574,7 +576,7 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dq_kernel(
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemAll) : "memory");
 }
 
-__global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dkv_kernel(
+__global__ void __launch_bounds__(kBThreads, 1) dflash_attn_bwd_dkv_kernel(
     const bf16_t* __restrict__ q, const bf16_t* __restrict__ k, const bf16_t* __restrict__ v,
     const float* __restrict__ lse, const float* __restrict__ delta, const bf16_t* __restrict__ dO,
     bf16_t* __restrict__ dk, bf16_t* __restrict__ dv, int T, int H, int n_ctx, float scale, int* status) {
@@ -589,7 +591,8 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dkv_kernel(
   const int64_t rs = (int64_t)H * kHD;
   const int64_t head = (int64_t)b * T * rs + (int64_t)h * kHD;
   const int64_t rowv = ((int64_t)b * H + h) * T;
-  const int key = k0 + threadIdx.x;
+  const int r_in = threadIdx.x & (kTN - 1), half = threadIdx.x >> 7;
+  const int key = k0 + r_in;
   const float sl2 = scale * kLog2e;
 
   if (threadIdx.x == 0) {
@@ -604,20 +607,20 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dkv_kernel(
   // Q, dO and the query rows' lse / delta of query tile qt sit in buffer set
   // (qt - qt_first) & 1; the next set is filled while this one is used.
   auto load_query_tile = [&](int qt, int set) {
-    const int qq = qt * kTM, qr = qq + threadIdx.x;
-    load_tile_async(base + (set ? kBOffC2 : kBOffC), q + head, rs, qq, T);
-    load_tile_async(base + (set ? kBOffD2 : kBOffD), dO + head, rs, qq, T);
+    const int qq = qt * kTM, qr = qq + r_in;
+    load_tile_async<kBThreads>(base + (set ? kBOffC2 : kBOffC), q + head, rs, qq, T);
+    load_tile_async<kBThreads>(base + (set ? kBOffD2 : kBOffD), dO + head, rs, qq, T);
+    // thread r_in of half 0 copies lse of query qq + r_in, of half 1 its delta
     const uint32_t rows = base + (set ? kBOffRow2 : kBOffRow);
-    cp_async4(rows + 4u * threadIdx.x, lse + rowv + (qr < T ? qr : 0), qr < T);
-    cp_async4(rows + 4u * (kTM + threadIdx.x), delta + rowv + (qr < T ? qr : 0), qr < T);
+    cp_async4(rows + 4u * (half * kTM + r_in), (half ? delta : lse) + rowv + (qr < T ? qr : 0), qr < T);
   };
-  load_tile_async(base + kBOffA, k + head, rs, k0, T);
-  load_tile_async(base + kBOffB, v + head, rs, k0, T);
+  load_tile_async<kBThreads>(base + kBOffA, k + head, rs, k0, T);
+  load_tile_async<kBThreads>(base + kBOffB, v + head, rs, k0, T);
   if (qt_first < qt_end) load_query_tile(qt_first, 0);
   cp_async_commit();
   cta_sync_tc();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
   constexpr uint32_t kIdS = instr_desc(kTN, kTM, 0, 0);
   constexpr uint32_t kIdKV = instr_desc(kTN, kHD, 0, 1);
   uint32_t ph = 0;
@@ -653,7 +656,8 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dkv_kernel(
     // every query of the tile sees every key of this CTA's tile: no per-element mask
     const bool full = k0 + kTN <= T && q0 + kTM <= T && (q0 >= n_ctx || k0 + kTN - 1 <= q0);
 #pragma unroll
-    for (int cc = 0; cc < kTM / 32; ++cc) {
+    for (int c2 = 0; c2 < kTM / 64; ++c2) {
+      const int cc = half * (kTM / 64) + c2;  // this thread's half of the query columns
       float sv[32], dp[32];
       tmem_ld32(tmem + lane_base + kColS + cc * 32, sv);
       tmem_ld32(tmem + lane_base + kColDP + cc * 32, dp);
@@ -670,8 +674,8 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dkv_kernel(
         wp[i / 2] = pack_bf16x2(p0, p1);
         wd[i / 2] = pack_bf16x2(p0 * (dp[i] - sh_delta[c]) * scale, p1 * (dp[i + 1] - sh_delta[c + 1]) * scale);
       }
-      st_row32(base + kBOffP, (uint32_t)threadIdx.x, cc, wp);
-      st_row32(base + kBOffS, (uint32_t)threadIdx.x, cc, wd);
+      st_row32(base + kBOffP, (uint32_t)r_in, cc, wp);
+      st_row32(base + kBOffS, (uint32_t)r_in, cc, wd);
     }
     cta_sync_tc();
     if (threadIdx.x == 0) {  // dV += P^T dO, dK += dS^T Q
@@ -700,23 +704,20 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_bwd_dkv_kernel(
     wait_bar(bar, ph);
   } else {
     tc_fence_after();
-    // keys no query sees (none here: the qt loop covers every visible pair) still get zeros
-    float av[kHD], ak[kHD];
+    // keys no query sees (none here: the qt loop covers every visible pair) still get zeros;
+    // this thread writes its half of the row's 64 dV and dK columns
+    float av[32], ak[32];
+    tmem_ld32(tmem + lane_base + kColAcc0 + half * 32, av);
+    tmem_ld32(tmem + lane_base + kColAcc1 + half * 32, ak);
+    if (first) {
 #pragma unroll
-    for (int cc = 0; cc < kHD / 32; ++cc) {
-      float t[32];
-      tmem_ld32(tmem + lane_base + kColAcc0 + cc * 32, t);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) av[cc * 32 + i] = first ? 0.f : t[i];
-      tmem_ld32(tmem + lane_base + kColAcc1 + cc * 32, t);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) ak[cc * 32 + i] = first ? 0.f : t[i];
+      for (int i = 0; i < 32; ++i) av[i] = ak[i] = 0.f;
     }
     if (key < T) {
-      bf16_t* vr = dv + head + (int64_t)key * rs;
-      bf16_t* kr = dk + head + (int64_t)key * rs;
+      bf16_t* vr = dv + head + (int64_t)key * rs + half * 32;
+      bf16_t* kr = dk + head + (int64_t)key * rs + half * 32;
 #pragma unroll
-      for (int c = 0; c < kHD / 8; ++c) {
+      for (int c = 0; c < 4; ++c) {
         const float* a = av + 8 * c;
         const float* g = ak + 8 * c;
         *reinterpret_cast<uint4*>(vr + 8 * c) = make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]),
@@ -776,13 +777,13 @@ cudaError_t dflash_attn_bwd_launch(const void* q, const void* k, const void* v, 
     done.fetch_or(bit);
   }
   const dim3 grid((unsigned)(batch * H), (unsigned)((T + kTM - 1) / kTM));
-  dflash_attn_bwd_dq_kernel<<<grid, kThreads, kBSmemBytes, st>>>(
+  dflash_attn_bwd_dq_kernel<<<grid, kBThreads, kBSmemBytes, st>>>(
       static_cast<const bf16_t*>(q), static_cast<const bf16_t*>(k), static_cast<const bf16_t*>(v),
       static_cast<const bf16_t*>(o), lse, static_cast<const bf16_t*>(dO), static_cast<bf16_t*>(dq), delta, T, H,
       n_ctx, scale, status);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  dflash_attn_bwd_dkv_kernel<<<grid, kThreads, kBSmemBytesKV, st>>>(
+  dflash_attn_bwd_dkv_kernel<<<grid, kBThreads, kBSmemBytesKV, st>>>(
       static_cast<const bf16_t*>(q), static_cast<const bf16_t*>(k), static_cast<const bf16_t*>(v), lse, delta,
       static_cast<const bf16_t*>(dO), static_cast<bf16_t*>(dk), static_cast<bf16_t*>(dv), T, H, n_ctx, scale,
       status);
