@@ -14,8 +14,9 @@ Requirements on ``fn``, as for any CUDA-graph capture:
 - no host synchronisation (the library's D-PACE target-range read-back is
   skipped while a stream is capturing; ``check()`` reads the captured
   forward's status word after a replay instead);
-- optimizers built with ``capturable=True``; autocast with
-  ``cache_enabled=False``;
+- optimizers built with ``capturable=True`` (for AdamW also ``fused=True``:
+  the capturable foreach form is dozens of elementwise launches per step);
+  autocast with ``cache_enabled=False``;
 - gradients are set to None before capture (done here), so the captured
   backward writes them fresh on every replay.
 Warm-up calls and the capture run on one side stream, so the library's
