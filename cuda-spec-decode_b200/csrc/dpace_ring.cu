@@ -447,9 +447,10 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
 #define SPECDEC_BWD_BLOCK_STAGES 1
 #endif
 constexpr int kBwdBlockStages = SPECDEC_BWD_BLOCK_STAGES;
-// Stages per forward block of the default shape (0). A smaller block shortens
-// the end of the launch (the last blocks finish closer together) at the cost
-// of more partials per row for the finalize to merge.
+// Stages per forward block of shapes 0 and 6 (the fp32 and bf16 defaults). A
+// smaller block shortens the end of the launch (the last blocks finish closer
+// together) at the cost of more piece closes and more partials per row for
+// the finalize to merge.
 #ifndef SPECDEC_FWD_BLOCK_STAGES
 #define SPECDEC_FWD_BLOCK_STAGES 4
 #endif
@@ -505,7 +506,7 @@ struct Shapes {
   using R3 = RingVariant<T, 4, 8, 4096 * k, 8>;
   using R4 = RingVariant<T, 2, 6, 2048 * k, 8>;
   using R5 = RingVariant<T, 8, 4, 4096 * k, 4>;
-  using R6 = RingVariant<T, 4, 3, 4096 * k, 4>;
+  using R6 = RingVariant<T, 4, 3, 4096 * k, kFwdBlockStages>;
 
   static int block_elems(int shape) {
     switch (shape) {
@@ -514,7 +515,7 @@ struct Shapes {
       case 3: return 4096 * 8 * k;
       case 4: return 2048 * 8 * k;
       case 5: return 4096 * 4 * k;
-      case 6: return 4096 * 4 * k;
+      case 6: return 4096 * kFwdBlockStages * k;
       default: return 4096 * kFwdBlockStages * k;
     }
   }
