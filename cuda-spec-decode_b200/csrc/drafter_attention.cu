@@ -11,31 +11,33 @@
 // needed on either side. lse is fp32 [B, H, T]: the natural-log
 // log-sum-exp of each query row's scaled scores, kept for a backward.
 //
-// One CTA per (b, h, 128-query tile), 4 warps; thread i owns query row i of
-// the tile, which is TMEM lane i. The grid runs the heaviest query tiles
-// (those that see the most keys) first. Per 128-key tile:
+// Forward: one CTA per (b, h, 128-query tile), 4 warps, four CTAs per SM;
+// thread i owns query row i of the tile, which is TMEM lane i. The grid runs
+// the heaviest query tiles (those that see the most keys) first. Per 64-key
+// tile:
 //   1. the K and V tiles are in shared memory in the canonical
 //      128-byte-swizzled layout (rows of 128 bytes, 16-byte chunk c of row r
 //      stored at chunk c ^ (r % 8), 8-row atoms of 1024 bytes), copied by
 //      cp.async ahead of use: the next K tile as soon as this tile's QK^T has
 //      read K, the next V tile as soon as P V has read V, so global-memory
 //      latency overlaps the softmax and the products;
-//   2. thread 0 issues S = Q K^T as four tcgen05.mma (M 128, N 128, K 16,
-//      bf16 in, fp32 accumulate in TMEM columns 0..127) and commits them to
-//      an mbarrier;
-//   3. every thread reads its row of S from TMEM twice (32 columns at a
-//      time): the tile's masked maximum, then p = 2^(s' - m) in bf16, written
-//      to shared memory as the A operand of the next product (same swizzled
-//      layout, two 64-key atoms);
-//   4. thread 0 issues O_tile = P V as eight tcgen05.mma (M 128, N 64, K 16;
-//      V read as an MN-major operand: d contiguous) into TMEM columns
-//      128..191, and commits;
-//   5. every thread reads its row of O_tile and folds it into its register
-//      accumulator with the online-softmax rescaling.
-// Apart from the copies the stages run one after another (the tiles are
-// small: T ~ 528 gives at most five key tiles per CTA). Every mbarrier wait is bounded; a wait that
-// expires sets *status and the CTA stops issuing work, waits (bounded) for
-// what it issued and releases its TMEM.
+//   2. thread 0 issues S = Q K^T as four tcgen05.mma (M 128, N 64, K 16,
+//      bf16 in, fp32 accumulate in TMEM columns 0..63) and commits them to an
+//      mbarrier;
+//   3. every thread reads its row of S from TMEM once (64 registers), takes
+//      the tile maximum and forms p = 2^(s' - m_ref) in bf16 into shared
+//      memory as the A operand of the next product (one 64-key atom row);
+//      m_ref, the row's reference maximum, is raised only when a tile's
+//      maximum exceeds it by more than 2^8, and only then is O rescaled (in
+//      tensor memory: load, scale, store) -- every p stays <= 2^8;
+//   4. thread 0 issues O += P V as four tcgen05.mma (M 128, N 64, K 16; V read
+//      as an MN-major operand: d contiguous) into TMEM columns 64..127, the
+//      output accumulator, and commits.
+// The epilogue reads O from TMEM and divides by the row sum. Apart from the
+// copies the stages run one after another; four CTAs per SM overlap one
+// another's. Every mbarrier wait is bounded; a wait that expires sets
+// *status and the CTA stops issuing work, waits (bounded) for what it issued
+// and releases its TMEM.
 #include <atomic>
 #include <cstdint>
 
@@ -51,17 +53,6 @@ constexpr int kHD = 64;        // head dimension
 constexpr int kTM = 128;       // query rows per CTA (TMEM lanes)
 constexpr int kTN = 128;       // keys per tile
 constexpr int kThreads = 128;  // 4 warps
-constexpr uint32_t kTmemCols = 256;  // S: columns 0..127, O_tile: 128..191
-constexpr uint32_t kColO = 128;
-
-// Shared memory (offsets from a 1024-byte-aligned base).
-constexpr uint32_t kOffQ = 0;             // 128 rows x 128 B
-constexpr uint32_t kOffK = 16384;
-constexpr uint32_t kOffV = 32768;
-constexpr uint32_t kOffP = 49152;         // two atoms of 128 rows x 128 B
-constexpr uint32_t kOffBar = 81920;       // two mbarriers
-constexpr uint32_t kOffTmem = kOffBar + 16;
-constexpr uint32_t kSmemBytes = kOffTmem + 16 + 1024;  // + alignment slack
 
 // Byte offset of 16-byte chunk c of row r in a 128-byte-swizzled tile.
 __device__ __forceinline__ uint32_t sw128(uint32_t r, uint32_t c) { return r * 128u + (((c ^ (r & 7u)) & 7u) << 4); }
@@ -120,6 +111,34 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Two 32-column loads (possibly from different column ranges) and one wait:
+// the load latency is paid once for both.
+__device__ __forceinline__ void tmem_ld32x2(uint32_t ta, uint32_t tb, float (&a)[32], float (&b)[32]) {
+  uint32_t r[32], t[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(ta));
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(t[0]), "=r"(t[1]), "=r"(t[2]), "=r"(t[3]), "=r"(t[4]), "=r"(t[5]), "=r"(t[6]), "=r"(t[7]),
+        "=r"(t[8]), "=r"(t[9]), "=r"(t[10]), "=r"(t[11]), "=r"(t[12]), "=r"(t[13]), "=r"(t[14]), "=r"(t[15]),
+        "=r"(t[16]), "=r"(t[17]), "=r"(t[18]), "=r"(t[19]), "=r"(t[20]), "=r"(t[21]), "=r"(t[22]), "=r"(t[23]),
+        "=r"(t[24]), "=r"(t[25]), "=r"(t[26]), "=r"(t[27]), "=r"(t[28]), "=r"(t[29]), "=r"(t[30]), "=r"(t[31])
+      : "r"(tb));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    a[i] = __uint_as_float(r[i]);
+    b[i] = __uint_as_float(t[i]);
+  }
+}
+
 __device__ __forceinline__ void st_shared_u4(uint32_t addr, uint4 v) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                : "memory");
@@ -142,11 +161,11 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-template <int NT = kThreads>
+template <int NT = kThreads, int ROWS = kTM>
 __device__ __forceinline__ void load_tile_async(uint32_t tile, const bf16_t* base, int64_t row_stride, int t0,
                                                 int T) {
 #pragma unroll
-  for (int j = 0; j < (kTM * 8) / NT; ++j) {
+  for (int j = 0; j < (ROWS * 8) / NT; ++j) {
     const int idx = threadIdx.x + j * NT;
     const int r = idx >> 3, c = idx & 7;
     const bool valid = t0 + r < T;
@@ -158,18 +177,53 @@ __device__ __forceinline__ void load_tile_async(uint32_t tile, const bf16_t* bas
 // Waits for the phase of `bar` with the given parity; false after the limit.
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity) { return mbar_wait(bar, parity); }
 
-__global__ void __launch_bounds__(kThreads, 1) dflash_attn_fwd_kernel(const bf16_t* __restrict__ q,
-                                                                      const bf16_t* __restrict__ k,
-                                                                      const bf16_t* __restrict__ v,
-                                                                      bf16_t* __restrict__ o, float* __restrict__ lse,
-                                                                      int T, int H, int n_ctx, float scale_log2,
-                                                                      int* status) {
+// tcgen05.st of 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])),
+      "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
+      "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])),
+      "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+
+// Forward: 64-key tiles, four CTAs per SM. TMEM columns 0..63 hold S, 64..127
+// the output accumulator O (the tensor core adds each tile's P V into it).
+constexpr int kFN = 64;               // keys per forward tile
+constexpr int kFCtas = 4;             // resident CTAs per SM (registers, TMEM, shared memory)
+constexpr uint32_t kFTmemCols = 128;
+constexpr uint32_t kFColO = 64;
+constexpr uint32_t kFOffQ = 0;        // 128 rows x 128 B
+constexpr uint32_t kFOffK = 16384;    // 64 rows x 128 B
+constexpr uint32_t kFOffV = 24576;    // 64 rows x 128 B
+constexpr uint32_t kFOffP = 32768;    // 128 rows x 128 B (one 64-key atom per row)
+constexpr uint32_t kFOffBar = 49152;  // two mbarriers
+constexpr uint32_t kFOffTmem = kFOffBar + 16;
+constexpr uint32_t kSmemBytes = kFOffTmem + 16 + 1024;  // + alignment slack
+// A row's probabilities are taken against a reference maximum that is
+// raised only when the tile's maximum exceeds it by more than 2^8 (base-2
+// exponent 8): p <= 2^8 then, fine for bf16 P and the fp32 sums, and O in
+// tensor memory is rescaled only on those rare raises, not every tile.
+constexpr float kRescaleLog2 = 8.f;
+
+__global__ void __launch_bounds__(kThreads, kFCtas) dflash_attn_fwd_kernel(const bf16_t* __restrict__ q,
+                                                                           const bf16_t* __restrict__ k,
+                                                                           const bf16_t* __restrict__ v,
+                                                                           bf16_t* __restrict__ o,
+                                                                           float* __restrict__ lse, int T, int H,
+                                                                           int n_ctx, float scale_log2, int* status) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   unsigned char* gbase = smem_raw + (base - smem_u32(smem_raw));
-  uint64_t* bar_s = reinterpret_cast<uint64_t*>(gbase + kOffBar);
+  uint64_t* bar_s = reinterpret_cast<uint64_t*>(gbase + kFOffBar);
   uint64_t* bar_o = bar_s + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kOffTmem);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kFOffTmem);
 
   const int warp = threadIdx.x >> 5;
   // heaviest query tiles first (the last tile sees every key): blocks are
@@ -186,17 +240,17 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_fwd_kernel(const bf16
     mbar_init(bar_o, 1);
     fence_mbar_init();
   }
-  if (warp == 0) {  // TMEM: 256 columns for this CTA
+  if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kTmemCols)
+                 "r"(kFTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   // copies in flight: {Q, K tile 0}, then {V tile 0}
-  load_tile_async(base + kOffQ, qb, rs, q0, T);
-  load_tile_async(base + kOffK, kb, rs, 0, T);
+  load_tile_async<kThreads, kTM>(base + kFOffQ, qb, rs, q0, T);
+  load_tile_async<kThreads, kFN>(base + kFOffK, kb, rs, 0, T);
   cp_async_commit();
-  load_tile_async(base + kOffV, vb, rs, 0, T);
+  load_tile_async<kThreads, kFN>(base + kFOffV, vb, rs, 0, T);
   cp_async_commit();
   tc_fence_before();
   __syncthreads();
@@ -209,18 +263,15 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_fwd_kernel(const bf16
   const int q_last = min(q0 + kTM, T) - 1;
   const int kv_end = q_last >= n_ctx ? T : q_last + 1;
   const int row = q0 + threadIdx.x;  // this thread's query row
-  constexpr uint32_t kIdS = instr_desc(kTM, kTN, 0, 0);
+  constexpr uint32_t kIdS = instr_desc(kTM, kFN, 0, 0);
   constexpr uint32_t kIdO = instr_desc(kTM, kHD, 0, 1);
 
-  float acc[kHD];
-#pragma unroll
-  for (int i = 0; i < kHD; ++i) acc[i] = 0.f;
-  float m_run = -INFINITY, l_run = 0.f;
+  float m_ref = -INFINITY, l_run = 0.f;  // reference maximum (base-2 scaled), row sum against it
   uint32_t ph = 0;
   bool ok = true;
 
-  for (int k0 = 0; k0 < kv_end && ok; k0 += kTN) {
-    const bool more = k0 + kTN < kv_end;
+  for (int k0 = 0; k0 < kv_end && ok; k0 += kFN) {
+    const bool more = k0 + kFN < kv_end;
     cp_async_wait<1>();  // this K tile (and Q) landed; the newest group, this V tile, may be in flight
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
@@ -229,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_fwd_kernel(const bf16
     if (threadIdx.x == 0) {  // S = Q K^T
 #pragma unroll
       for (int kk = 0; kk < kHD / 16; ++kk)
-        umma_bf16(tmem, smem_desc(base + kOffQ + kk * 32, 16, 1024), smem_desc(base + kOffK + kk * 32, 16, 1024),
+        umma_bf16(tmem, smem_desc(base + kFOffQ + kk * 32, 16, 1024), smem_desc(base + kFOffK + kk * 32, 16, 1024),
                   kIdS, kk > 0);
       umma_commit(bar_s);
     }
@@ -239,74 +290,77 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_fwd_kernel(const bf16
     }
     tc_fence_after();
     // the product has read K: the next K tile streams in during the softmax and P V
-    if (more) load_tile_async(base + kOffK, kb, rs, k0 + kTN, T);
+    if (more) load_tile_async<kThreads, kFN>(base + kFOffK, kb, rs, k0 + kFN, T);
     cp_async_commit();
     // every row of this query tile sees every key of this key tile: no
     // per-element mask (a context row sees keys up to itself, a block row all
     // keys; rows past T are never stored)
-    const bool full = k0 + kTN <= T && (q0 >= n_ctx || k0 + kTN - 1 <= q0);
-    // pass 1: the tile's (masked) maximum of this row; the base-2 scale is
-    // positive, so scaling the maximum equals the maximum of scaled scores
-    float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    const bool full = k0 + kFN <= T && (q0 >= n_ctx || k0 + kFN - 1 <= q0);
+    float s[2][32];  // this row's 64 scores, kept for both passes
+    tmem_ld32x2(tmem + lane_base, tmem + lane_base + 32, s[0], s[1]);
+    if (!full) {
 #pragma unroll
-    for (int cc = 0; cc < kTN / 32; ++cc) {
-      float s[32];
-      tmem_ld32(tmem + lane_base + cc * 32, s);
-      if (full) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], s[i]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int j = k0 + cc * 32 + i;
-          if (j < T && (row >= n_ctx || j <= row)) mx[i & 3] = fmaxf(mx[i & 3], s[i]);
-        }
+      for (int i = 0; i < kFN; ++i) {
+        const int j = k0 + i;
+        if (!(j < T && (row >= n_ctx || j <= row))) s[i >> 5][i & 31] = -INFINITY;
       }
     }
-    const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale_log2;
-    const float m_new = fmaxf(m_run, mt);
-    const float alpha = m_run == -INFINITY ? 0.f : exp2_approx(m_run - m_new);
-    const float nm = -m_new;
-    // pass 2: p = 2^(s * scale_log2 - m_new), row sum, P in bf16 to shared memory
-    float ls[4] = {0.f, 0.f, 0.f, 0.f};
+    // the tile's maximum; the base-2 scale is positive, so scaling the
+    // maximum equals the maximum of the scaled scores
+    float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-    for (int cc = 0; cc < kTN / 32; ++cc) {
-      float s[32];
-      tmem_ld32(tmem + lane_base + cc * 32, s);
+    for (int i = 0; i < kFN; ++i) mx[i & 3] = fmaxf(mx[i & 3], s[i >> 5][i & 31]);
+    const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale_log2;
+    // raise the reference maximum only by more than 2^8 (or the first time)
+    const bool raise = mt > m_ref + kRescaleLog2;
+    const float alpha = raise ? (m_ref == -INFINITY ? 0.f : exp2_approx(m_ref - mt)) : 1.f;
+    if (raise) m_ref = mt;
+    // p = 2^(s * scale_log2 - m_ref) (masked scores give exactly 0), row
+    // sum, P in bf16 to shared memory (one 64-key atom row)
+    const float nm = -m_ref;
+    float ls[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint32_t r = (uint32_t)threadIdx.x;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {  // 32 keys at a time: 16 packed words, four 16-byte chunks
       uint32_t pk[16];
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
-        float p0 = exp2_approx(fmaf(s[i], scale_log2, nm));
-        float p1 = exp2_approx(fmaf(s[i + 1], scale_log2, nm));
-        if (!full) {
-          const int j = k0 + cc * 32 + i;
-          p0 = (j < T && (row >= n_ctx || j <= row)) ? p0 : 0.f;
-          p1 = (j + 1 < T && (row >= n_ctx || j + 1 <= row)) ? p1 : 0.f;
-        }
+        const float p0 = exp2_approx(fmaf(s[hh][i], scale_log2, nm));
+        const float p1 = exp2_approx(fmaf(s[hh][i + 1], scale_log2, nm));
         ls[(i >> 1) & 3] += p0 + p1;
         pk[i / 2] = pack_bf16x2(p0, p1);
       }
-      const uint32_t r = (uint32_t)threadIdx.x;
-      const uint32_t atom = base + kOffP + (uint32_t)(cc >> 1) * 16384u;  // keys 0..63 | 64..127
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        const uint32_t chunk = (uint32_t)((cc & 1) * 4 + c4);  // 16-byte chunk within the 64-key atom row
-        st_shared_u4(atom + sw128(r, chunk), make_uint4(pk[4 * c4], pk[4 * c4 + 1], pk[4 * c4 + 2], pk[4 * c4 + 3]));
-      }
+      for (int c4 = 0; c4 < 4; ++c4)
+        st_shared_u4(base + kFOffP + sw128(r, (uint32_t)(hh * 4 + c4)),
+                     make_uint4(pk[4 * c4], pk[4 * c4 + 1], pk[4 * c4 + 2], pk[4 * c4 + 3]));
     }
-    const float lt = (ls[0] + ls[1]) + (ls[2] + ls[3]);
+    l_run = fmaf(l_run, alpha, (ls[0] + ls[1]) + (ls[2] + ls[3]));
+    // O holds earlier tiles' P V against the old reference: rescale it in
+    // tensor memory before this tile's product adds to it (only the warps with
+    // a raised row; the first tile writes O without accumulating)
+    if (k0 > 0 && __any_sync(kFullMask, raise)) {
+      float ot[2][32];
+      tmem_ld32x2(tmem + lane_base + kFColO, tmem + lane_base + kFColO + 32, ot[0], ot[1]);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        ot[0][i] *= alpha;
+        ot[1][i] *= alpha;
+      }
+      tmem_st32(tmem + lane_base + kFColO, ot[0]);
+      tmem_st32(tmem + lane_base + kFColO + 32, ot[1]);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+    }
     cp_async_wait<1>();  // this V tile; the next K tile may be in flight
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (threadIdx.x == 0) {  // O_tile = P V
+    if (threadIdx.x == 0) {  // O += P V (the first tile writes O)
 #pragma unroll
-      for (int kk = 0; kk < kTN / 16; ++kk) {
-        const uint64_t ad = smem_desc(base + kOffP + (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u, 16, 1024);
-        const uint64_t bd = smem_desc(base + kOffV + (uint32_t)kk * 2048u, 16384, 1024);
-        umma_bf16(tmem + kColO, ad, bd, kIdO, kk > 0);
-      }
+      for (int kk = 0; kk < kFN / 16; ++kk)
+        umma_bf16(tmem + kFColO, smem_desc(base + kFOffP + (uint32_t)kk * 32u, 16, 1024),
+                  smem_desc(base + kFOffV + (uint32_t)kk * 2048u, 16384, 1024), kIdO, (k0 > 0 || kk > 0) ? 1u : 0u);
       umma_commit(bar_o);
     }
     if (__syncthreads_or(!wait_bar(bar_o, ph) ? 1 : 0)) {
@@ -314,22 +368,9 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_fwd_kernel(const bf16
       break;
     }
     tc_fence_after();
-    if (more) load_tile_async(base + kOffV, vb, rs, k0 + kTN, T);  // the product has read V
+    if (more) load_tile_async<kThreads, kFN>(base + kFOffV, vb, rs, k0 + kFN, T);  // the product has read V
     cp_async_commit();
-#pragma unroll
-    for (int cc = 0; cc < kHD / 32; ++cc) {
-      float ot[32];
-      tmem_ld32(tmem + lane_base + kColO + cc * 32, ot);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) acc[cc * 32 + i] = fmaf(acc[cc * 32 + i], alpha, ot[i]);
-    }
-    l_run = fmaf(l_run, alpha, lt);
-    m_run = m_new;
     ph ^= 1u;
-    // every thread is done with S, P, K and V before the next tile overwrites them
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
   }
 
   cp_async_wait<0>();  // no copy outlives the CTA
@@ -338,23 +379,27 @@ __global__ void __launch_bounds__(kThreads, 1) dflash_attn_fwd_kernel(const bf16
     // wait (bounded) for the products this CTA may still have in flight
     wait_bar(bar_s, ph);
     wait_bar(bar_o, ph);
-  } else if (row < T) {
-    const float inv = 1.f / l_run;
-    bf16_t* orow = o + ((int64_t)b * T + row) * rs + (int64_t)h * kHD;
+  } else {
+    float ot[2][32];
+    tmem_ld32x2(tmem + lane_base + kFColO, tmem + lane_base + kFColO + 32, ot[0], ot[1]);
+    if (row < T) {
+      const float inv = 1.f / l_run;
+      bf16_t* orow = o + ((int64_t)b * T + row) * rs + (int64_t)h * kHD;
 #pragma unroll
-    for (int c = 0; c < kHD / 8; ++c) {
-      const float* a = acc + 8 * c;
-      *reinterpret_cast<uint4*>(orow + 8 * c) =
-          make_uint4(pack_bf16x2(a[0] * inv, a[1] * inv), pack_bf16x2(a[2] * inv, a[3] * inv),
-                     pack_bf16x2(a[4] * inv, a[5] * inv), pack_bf16x2(a[6] * inv, a[7] * inv));
+      for (int c = 0; c < kHD / 8; ++c) {
+        const float* a = &ot[c >> 2][(c & 3) * 8];
+        *reinterpret_cast<uint4*>(orow + 8 * c) =
+            make_uint4(pack_bf16x2(a[0] * inv, a[1] * inv), pack_bf16x2(a[2] * inv, a[3] * inv),
+                       pack_bf16x2(a[4] * inv, a[5] * inv), pack_bf16x2(a[6] * inv, a[7] * inv));
+      }
+      lse[((int64_t)b * H + h) * T + row] = (m_ref + log2f(l_run)) * kLn2;
     }
-    lse[((int64_t)b * H + h) * T + row] = (m_run + log2f(l_run)) * kLn2;
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kFTmemCols) : "memory");
 }
 
 
@@ -519,8 +564,7 @@ __global__ void __launch_bounds__(kBThreads, 1) dflash_attn_bwd_dq_kernel(
     for (int c2 = 0; c2 < kTN / 64; ++c2) {
       const int cc = half * (kTN / 64) + c2;  // this thread's half of the columns
       float sv[32], dp[32];
-      tmem_ld32(tmem + lane_base + kColS + cc * 32, sv);
-      tmem_ld32(tmem + lane_base + kColDP + cc * 32, dp);
+      tmem_ld32x2(tmem + lane_base + kColS + cc * 32, tmem + lane_base + kColDP + cc * 32, sv, dp);
       uint32_t w[16];
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
@@ -659,8 +703,7 @@ __global__ void __launch_bounds__(kBThreads, 1) dflash_attn_bwd_dkv_kernel(
     for (int c2 = 0; c2 < kTM / 64; ++c2) {
       const int cc = half * (kTM / 64) + c2;  // this thread's half of the query columns
       float sv[32], dp[32];
-      tmem_ld32(tmem + lane_base + kColS + cc * 32, sv);
-      tmem_ld32(tmem + lane_base + kColDP + cc * 32, dp);
+      tmem_ld32x2(tmem + lane_base + kColS + cc * 32, tmem + lane_base + kColDP + cc * 32, sv, dp);
       uint32_t wp[16], wd[16];
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
@@ -707,8 +750,7 @@ __global__ void __launch_bounds__(kBThreads, 1) dflash_attn_bwd_dkv_kernel(
     // keys no query sees (none here: the qt loop covers every visible pair) still get zeros;
     // this thread writes its half of the row's 64 dV and dK columns
     float av[32], ak[32];
-    tmem_ld32(tmem + lane_base + kColAcc0 + half * 32, av);
-    tmem_ld32(tmem + lane_base + kColAcc1 + half * 32, ak);
+    tmem_ld32x2(tmem + lane_base + kColAcc0 + half * 32, tmem + lane_base + kColAcc1 + half * 32, av, ak);
     if (first) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) av[i] = ak[i] = 0.f;
