@@ -51,7 +51,6 @@ namespace {
 
 constexpr int kHD = 64;        // head dimension
 constexpr int kTM = 128;       // query rows per CTA (TMEM lanes)
-constexpr int kTN = 128;       // keys per tile
 constexpr int kThreads = 128;  // 4 warps
 
 // Byte offset of 16-byte chunk c of row r in a 128-byte-swizzled tile.
@@ -407,62 +406,69 @@ __global__ void __launch_bounds__(kThreads, kFCtas) dflash_attn_fwd_kernel(const
 // Backward. Two kernels, no atomics (every accumulation runs in a fixed order
 // inside one CTA, so the gradients are bitwise repeatable):
 //   dq kernel, one CTA per (b, h, 128-query tile), thread = query row:
-//     delta = sum_d dO * O for its row (kept for the dkv kernel); per key tile:
-//     S = Q K^T and dP = dO V^T (tcgen05, TMEM columns 0..127 / 128..255),
-//     p = e^(s * scale - lse), dS = p * (dP - delta) * scale to shared memory
-//     in bf16, dQ += dS K (K as an MN-major operand) in TMEM columns 256..319.
-//   dkv kernel, one CTA per (b, h, 128-key tile), thread = key row: per query
-//     tile: S^T = K Q^T and dP^T = V dO^T, p^T and dS^T in bf16 to shared
-//     memory, dV += P^T dO and dK += dS^T Q (dO and Q as MN-major operands)
-//     in TMEM columns 256..319 / 320..383.
-// Each CTA holds all 512 TMEM columns (one CTA per SM). Tiles arrive by
-// cp.async one step ahead: the dq kernel double-buffers K (its dS^T area is
-// spare) and refills V once dP has read it; the dkv kernel double-buffers the
-// query tile's Q, dO, lse and delta.
+//     delta = sum_d dO * O for its row (kept for the dkv kernel); per 64-key
+//     tile: S = Q K^T and dP = dO V^T (tcgen05, TMEM columns 0..63 /
+//     64..127), p = e^(s * scale - lse), dS = p * (dP - delta) * scale to
+//     shared memory in bf16, dQ += dS K (K as an MN-major operand) in TMEM
+//     columns 128..191.
+//   dkv kernel, one CTA per (b, h, 128-key tile), thread = key row: per
+//     64-query tile: S^T = K Q^T and dP^T = V dO^T, p^T and dS^T in bf16 to
+//     shared memory, dV += P^T dO and dK += dS^T Q (dO and Q as MN-major
+//     operands) in TMEM columns 128..191 / 192..255.
+// 8 warps per CTA, two CTAs per SM (256 TMEM columns each). Warps w and w + 4
+// share TMEM lanes 32 (w % 4) .. 32 (w % 4) + 31 (one row each, thread t and
+// t + 128) and split a tile's 64 columns into halves: with the row's
+// log-sum-exp known, the halves are independent. Tiles arrive by cp.async one
+// step ahead: the dq kernel double-buffers K and refills V once dP has read
+// it; the dkv kernel double-buffers the query tile's Q, dO, lse and delta.
 // ---------------------------------------------------------------------------
 
-constexpr uint32_t kTmemAll = 512;
-// Backward CTAs: 8 warps. Warps w and w + 4 share TMEM lanes 32 (w % 4) ..
-// 32 (w % 4) + 31 (one row each, thread t and t + 128), and split a tile's
-// 128 columns into halves: with the row's log-sum-exp known, the halves are
-// independent.
-constexpr int kBThreads = 256;
-constexpr uint32_t kColS = 0, kColDP = 128, kColAcc0 = 256, kColAcc1 = 320;
+constexpr int kBN = 64;            // keys per dq tile, queries per dkv tile
+constexpr int kBThreads = 256;     // 8 warps
+constexpr int kBCtas = 2;          // resident CTAs per SM
+constexpr uint32_t kBTmemCols = 256;
+constexpr uint32_t kColS = 0, kColDP = 64, kColAcc0 = 128, kColAcc1 = 192;
 
-// Shared memory of the backward kernels (offsets from a 1024-byte-aligned base).
-constexpr uint32_t kBOffA = 0;        // Q (dq kernel) | K (dkv kernel)
-constexpr uint32_t kBOffB = 16384;    // dO            | V
-constexpr uint32_t kBOffC = 32768;    // K             | Q
-constexpr uint32_t kBOffD = 49152;    // V             | dO
-constexpr uint32_t kBOffP = 65536;    // dS            | P^T   (two atoms)
-constexpr uint32_t kBOffS = 98304;    // K (odd tiles)  | dS^T  (two atoms)
-constexpr uint32_t kBOffRow = 131072; // -             | lse, delta of the query tile (2 x 128 floats)
-constexpr uint32_t kBOffBar = 132096;
-constexpr uint32_t kBOffTmem = kBOffBar + 16;
-constexpr uint32_t kBSmemBytes = kBOffTmem + 16 + 1024;
-// dkv kernel only: the second buffer set of the query tile (Q, dO, lse / delta)
-constexpr uint32_t kBOffC2 = 133120;
-constexpr uint32_t kBOffD2 = kBOffC2 + 16384;
-constexpr uint32_t kBOffRow2 = kBOffD2 + 16384;
-constexpr uint32_t kBSmemBytesKV = kBOffRow2 + 1024 + 1024;
+// dq kernel shared memory (offsets from a 1024-byte-aligned base)
+constexpr uint32_t kQOffQ = 0;        // 128 rows x 128 B
+constexpr uint32_t kQOffG = 16384;    // dO, 128 rows
+constexpr uint32_t kQOffK0 = 32768;   // K, even tiles, 64 rows
+constexpr uint32_t kQOffK1 = 40960;   // K, odd tiles
+constexpr uint32_t kQOffV = 49152;    // V, 64 rows
+constexpr uint32_t kQOffS = 57344;    // dS, 128 rows x 64 keys (one atom per row)
+constexpr uint32_t kQOffBar = 73728;
+constexpr uint32_t kBSmemBytes = kQOffBar + 32 + 1024;
+
+// dkv kernel shared memory
+constexpr uint32_t kVOffK = 0;        // 128 rows
+constexpr uint32_t kVOffV = 16384;    // 128 rows
+constexpr uint32_t kVOffQ0 = 32768;   // query tile set 0: Q, 64 rows
+constexpr uint32_t kVOffG0 = 40960;   //                   dO
+constexpr uint32_t kVOffQ1 = 49152;   // query tile set 1
+constexpr uint32_t kVOffG1 = 57344;
+constexpr uint32_t kVOffP = 65536;    // P^T, 128 keys x 64 queries
+constexpr uint32_t kVOffS = 81920;    // dS^T
+constexpr uint32_t kVOffRow0 = 98304; // lse (64 floats) then delta (64 floats), set 0
+constexpr uint32_t kVOffRow1 = 98816; // set 1
+constexpr uint32_t kVOffBar = 99328;
+constexpr uint32_t kBSmemBytesKV = kVOffBar + 32 + 1024;
 
 __device__ __forceinline__ bool visible(int qrow, int key, int T, int n_ctx) {
   return qrow < T && key < T && (qrow >= n_ctx || key <= qrow);
 }
 
-// Writes 32 consecutive bf16 values (16 words) of row r of a two-atom
-// K-major operand at columns [32 cc, 32 cc + 32).
-__device__ __forceinline__ void st_row32(uint32_t tile, uint32_t r, int cc, const uint32_t (&w)[16]) {
-  const uint32_t atom = tile + (uint32_t)(cc >> 1) * 16384u;
+// Writes 32 consecutive bf16 values (16 words) of row r of a one-atom (64
+// columns) K-major operand at columns [32 hh, 32 hh + 32).
+__device__ __forceinline__ void st_row32(uint32_t tile, uint32_t r, int hh, const uint32_t (&w)[16]) {
 #pragma unroll
   for (int c4 = 0; c4 < 4; ++c4)
-    st_shared_u4(atom + sw128(r, (uint32_t)((cc & 1) * 4 + c4)),
+    st_shared_u4(tile + sw128(r, (uint32_t)(hh * 4 + c4)),
                  make_uint4(w[4 * c4], w[4 * c4 + 1], w[4 * c4 + 2], w[4 * c4 + 3]));
 }
 
-__device__ __forceinline__ void tmem_alloc_all(uint32_t* slot) {
+__device__ __forceinline__ void tmem_alloc_bwd(uint32_t* slot) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
-               "r"(kTmemAll)
+               "r"(kBTmemCols)
                : "memory");
   asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
 }
@@ -474,15 +480,15 @@ __device__ __forceinline__ void cta_sync_tc() {
   tc_fence_after();
 }
 
-__global__ void __launch_bounds__(kBThreads, 1) dflash_attn_bwd_dq_kernel(
+__global__ void __launch_bounds__(kBThreads, kBCtas) dflash_attn_bwd_dq_kernel(
     const bf16_t* __restrict__ q, const bf16_t* __restrict__ k, const bf16_t* __restrict__ v,
     const bf16_t* __restrict__ o, const float* __restrict__ lse, const bf16_t* __restrict__ dO,
     bf16_t* __restrict__ dq, float* __restrict__ delta_out, int T, int H, int n_ctx, float scale, int* status) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   unsigned char* gbase = smem_raw + (base - smem_u32(smem_raw));
-  uint64_t* bar = reinterpret_cast<uint64_t*>(gbase + kBOffBar);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kBOffTmem);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(gbase + kQOffBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kQOffBar + 16);
   const int warp = threadIdx.x >> 5;
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
   const int q0 = (gridDim.y - 1 - blockIdx.y) * kTM;  // heaviest query tiles first
@@ -496,13 +502,12 @@ __global__ void __launch_bounds__(kBThreads, 1) dflash_attn_bwd_dq_kernel(
     mbar_init(bar, 1);
     fence_mbar_init();
   }
-  if (warp == 0) tmem_alloc_all(tmem_slot);
-  // one copy group: Q, dO and the first K and V tiles (K double-buffered:
-  // tile j in the K area when j is even, in the spare area when odd)
-  load_tile_async<kBThreads>(base + kBOffA, q + head, rs, q0, T);
-  load_tile_async<kBThreads>(base + kBOffB, dO + head, rs, q0, T);
-  load_tile_async<kBThreads>(base + kBOffC, k + head, rs, 0, T);
-  load_tile_async<kBThreads>(base + kBOffD, v + head, rs, 0, T);
+  if (warp == 0) tmem_alloc_bwd(tmem_slot);
+  // one copy group: Q, dO and the first K and V tiles
+  load_tile_async<kBThreads, kTM>(base + kQOffQ, q + head, rs, q0, T);
+  load_tile_async<kBThreads, kTM>(base + kQOffG, dO + head, rs, q0, T);
+  load_tile_async<kBThreads, kBN>(base + kQOffK0, k + head, rs, 0, T);
+  load_tile_async<kBThreads, kBN>(base + kQOffV, v + head, rs, 0, T);
   cp_async_commit();
   // delta = sum_d dO * O of this row (both threads of the row), and its lse in base 2
   float delta = 0.f, lse2 = 0.f;
@@ -528,25 +533,25 @@ __global__ void __launch_bounds__(kBThreads, 1) dflash_attn_bwd_dq_kernel(
   const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
   const int q_last = min(q0 + kTM, T) - 1;
   const int kv_end = q_last >= n_ctx ? T : q_last + 1;
-  constexpr uint32_t kIdS = instr_desc(kTM, kTN, 0, 0);
+  constexpr uint32_t kIdS = instr_desc(kTM, kBN, 0, 0);
   constexpr uint32_t kIdQ = instr_desc(kTM, kHD, 0, 1);
   uint32_t ph = 0;
   bool ok = true;
-  for (int k0 = 0, it = 0; k0 < kv_end; k0 += kTN, ++it) {
-    const bool more = k0 + kTN < kv_end;
-    const uint32_t kcur = (it & 1) ? kBOffS : kBOffC, knext = (it & 1) ? kBOffC : kBOffS;
+  for (int k0 = 0, it = 0; k0 < kv_end; k0 += kBN, ++it) {
+    const bool more = k0 + kBN < kv_end;
+    const uint32_t kcur = (it & 1) ? kQOffK1 : kQOffK0, knext = (it & 1) ? kQOffK0 : kQOffK1;
     cp_async_wait<0>();  // this K and V tile
     cta_sync_tc();
     // the other K buffer was last read by the previous tile's dQ product: fill it now
-    if (more) load_tile_async<kBThreads>(base + knext, k + head, rs, k0 + kTN, T);
+    if (more) load_tile_async<kBThreads, kBN>(base + knext, k + head, rs, k0 + kBN, T);
     cp_async_commit();
     if (threadIdx.x == 0) {
 #pragma unroll
       for (int kk = 0; kk < kHD / 16; ++kk) {  // S = Q K^T, dP = dO V^T
-        umma_bf16(tmem + kColS, smem_desc(base + kBOffA + kk * 32, 16, 1024),
+        umma_bf16(tmem + kColS, smem_desc(base + kQOffQ + kk * 32, 16, 1024),
                   smem_desc(base + kcur + kk * 32, 16, 1024), kIdS, kk > 0);
-        umma_bf16(tmem + kColDP, smem_desc(base + kBOffB + kk * 32, 16, 1024),
-                  smem_desc(base + kBOffD + kk * 32, 16, 1024), kIdS, kk > 0);
+        umma_bf16(tmem + kColDP, smem_desc(base + kQOffG + kk * 32, 16, 1024),
+                  smem_desc(base + kQOffV + kk * 32, 16, 1024), kIdS, kk > 0);
       }
       umma_commit(bar);
     }
@@ -556,35 +561,32 @@ __global__ void __launch_bounds__(kBThreads, 1) dflash_attn_bwd_dq_kernel(
     }
     ph ^= 1u;
     tc_fence_after();
-    if (more) load_tile_async<kBThreads>(base + kBOffD, v + head, rs, k0 + kTN, T);  // dP has read V
+    if (more) load_tile_async<kBThreads, kBN>(base + kQOffV, v + head, rs, k0 + kBN, T);  // dP has read V
     cp_async_commit();
     // every row of the query tile sees every key of the key tile: no per-element mask
-    const bool full = k0 + kTN <= T && (q0 >= n_ctx || k0 + kTN - 1 <= q0);
-#pragma unroll
-    for (int c2 = 0; c2 < kTN / 64; ++c2) {
-      const int cc = half * (kTN / 64) + c2;  // this thread's half of the columns
-      float sv[32], dp[32];
-      tmem_ld32x2(tmem + lane_base + kColS + cc * 32, tmem + lane_base + kColDP + cc * 32, sv, dp);
+    const bool full = k0 + kBN <= T && (q0 >= n_ctx || k0 + kBN - 1 <= q0);
+    {
+      float sv[32], dp[32];  // this thread's half of the tile's 64 columns
+      tmem_ld32x2(tmem + lane_base + kColS + half * 32, tmem + lane_base + kColDP + half * 32, sv, dp);
       uint32_t w[16];
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
         float p0 = exp2_approx(fmaf(sv[i], sl2, -lse2));
         float p1 = exp2_approx(fmaf(sv[i + 1], sl2, -lse2));
         if (!full) {
-          const int j = k0 + cc * 32 + i;
+          const int j = k0 + half * 32 + i;
           p0 = visible(row, j, T, n_ctx) ? p0 : 0.f;
           p1 = visible(row, j + 1, T, n_ctx) ? p1 : 0.f;
         }
         w[i / 2] = pack_bf16x2(p0 * (dp[i] - delta) * scale, p1 * (dp[i + 1] - delta) * scale);
       }
-      st_row32(base + kBOffP, (uint32_t)r_in, cc, w);
+      st_row32(base + kQOffS, (uint32_t)r_in, half, w);
     }
     cta_sync_tc();
     if (threadIdx.x == 0) {  // dQ += dS K
 #pragma unroll
-      for (int kk = 0; kk < kTN / 16; ++kk)
-        umma_bf16(tmem + kColAcc0,
-                  smem_desc(base + kBOffP + (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u, 16, 1024),
+      for (int kk = 0; kk < kBN / 16; ++kk)
+        umma_bf16(tmem + kColAcc0, smem_desc(base + kQOffS + (uint32_t)kk * 32u, 16, 1024),
                   smem_desc(base + kcur + (uint32_t)kk * 2048u, 16384, 1024), kIdQ, (k0 > 0 || kk > 0) ? 1u : 0u);
       umma_commit(bar);
     }
@@ -617,25 +619,25 @@ __global__ void __launch_bounds__(kBThreads, 1) dflash_attn_bwd_dq_kernel(
   __syncthreads();
   tc_fence_after();
   if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemAll) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kBTmemCols) : "memory");
 }
 
-__global__ void __launch_bounds__(kBThreads, 1) dflash_attn_bwd_dkv_kernel(
+__global__ void __launch_bounds__(kBThreads, kBCtas) dflash_attn_bwd_dkv_kernel(
     const bf16_t* __restrict__ q, const bf16_t* __restrict__ k, const bf16_t* __restrict__ v,
     const float* __restrict__ lse, const float* __restrict__ delta, const bf16_t* __restrict__ dO,
     bf16_t* __restrict__ dk, bf16_t* __restrict__ dv, int T, int H, int n_ctx, float scale, int* status) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   unsigned char* gbase = smem_raw + (base - smem_u32(smem_raw));
-  uint64_t* bar = reinterpret_cast<uint64_t*>(gbase + kBOffBar);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kBOffTmem);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(gbase + kVOffBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kVOffBar + 16);
   const int warp = threadIdx.x >> 5;
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
-  const int k0 = blockIdx.y * kTN;  // the first key tiles are seen by the most query tiles: heaviest first
+  const int k0 = blockIdx.y * kTM;  // the first key tiles are seen by the most query tiles: heaviest first
   const int64_t rs = (int64_t)H * kHD;
   const int64_t head = (int64_t)b * T * rs + (int64_t)h * kHD;
   const int64_t rowv = ((int64_t)b * H + h) * T;
-  const int r_in = threadIdx.x & (kTN - 1), half = threadIdx.x >> 7;
+  const int r_in = threadIdx.x & (kTM - 1), half = threadIdx.x >> 7;
   const int key = k0 + r_in;
   const float sl2 = scale * kLog2e;
 
@@ -643,39 +645,41 @@ __global__ void __launch_bounds__(kBThreads, 1) dflash_attn_bwd_dkv_kernel(
     mbar_init(bar, 1);
     fence_mbar_init();
   }
-  if (warp == 0) tmem_alloc_all(tmem_slot);
-  // query tiles that see a key of this tile: context queries from the
+  if (warp == 0) tmem_alloc_bwd(tmem_slot);
+  // 64-query tiles that see a key of this tile: context queries from the
   // diagonal on, and every tile holding a block slot
-  const int qt_first = (k0 < n_ctx ? k0 : n_ctx) / kTM;
-  const int qt_end = (T + kTM - 1) / kTM;
+  const int qt_first = (k0 < n_ctx ? k0 : n_ctx) / kBN;
+  const int qt_end = (T + kBN - 1) / kBN;
   // Q, dO and the query rows' lse / delta of query tile qt sit in buffer set
   // (qt - qt_first) & 1; the next set is filled while this one is used.
   auto load_query_tile = [&](int qt, int set) {
-    const int qq = qt * kTM, qr = qq + r_in;
-    load_tile_async<kBThreads>(base + (set ? kBOffC2 : kBOffC), q + head, rs, qq, T);
-    load_tile_async<kBThreads>(base + (set ? kBOffD2 : kBOffD), dO + head, rs, qq, T);
-    // thread r_in of half 0 copies lse of query qq + r_in, of half 1 its delta
-    const uint32_t rows = base + (set ? kBOffRow2 : kBOffRow);
-    cp_async4(rows + 4u * (half * kTM + r_in), (half ? delta : lse) + rowv + (qr < T ? qr : 0), qr < T);
+    const int qq = qt * kBN;
+    load_tile_async<kBThreads, kBN>(base + (set ? kVOffQ1 : kVOffQ0), q + head, rs, qq, T);
+    load_tile_async<kBThreads, kBN>(base + (set ? kVOffG1 : kVOffG0), dO + head, rs, qq, T);
+    if (r_in < kBN) {  // half 0 copies lse of query qq + r_in, half 1 its delta
+      const int qr = qq + r_in;
+      const uint32_t rows = base + (set ? kVOffRow1 : kVOffRow0);
+      cp_async4(rows + 4u * (half * kBN + r_in), (half ? delta : lse) + rowv + (qr < T ? qr : 0), qr < T);
+    }
   };
-  load_tile_async<kBThreads>(base + kBOffA, k + head, rs, k0, T);
-  load_tile_async<kBThreads>(base + kBOffB, v + head, rs, k0, T);
+  load_tile_async<kBThreads, kTM>(base + kVOffK, k + head, rs, k0, T);
+  load_tile_async<kBThreads, kTM>(base + kVOffV, v + head, rs, k0, T);
   if (qt_first < qt_end) load_query_tile(qt_first, 0);
   cp_async_commit();
   cta_sync_tc();
   const uint32_t tmem = *tmem_slot;
   const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-  constexpr uint32_t kIdS = instr_desc(kTN, kTM, 0, 0);
-  constexpr uint32_t kIdKV = instr_desc(kTN, kHD, 0, 1);
+  constexpr uint32_t kIdS = instr_desc(kTM, kBN, 0, 0);
+  constexpr uint32_t kIdKV = instr_desc(kTM, kHD, 0, 1);
   uint32_t ph = 0;
   bool ok = true;
   bool first = true;
   for (int qt = qt_first; qt < qt_end; ++qt) {
-    const int q0 = qt * kTM;
+    const int q0 = qt * kBN;
     const int set = (qt - qt_first) & 1;
-    const uint32_t offq = set ? kBOffC2 : kBOffC, offg = set ? kBOffD2 : kBOffD;
-    const float* sh_lse = reinterpret_cast<const float*>(gbase + (set ? kBOffRow2 : kBOffRow));
-    const float* sh_delta = sh_lse + kTM;
+    const uint32_t offq = set ? kVOffQ1 : kVOffQ0, offg = set ? kVOffG1 : kVOffG0;
+    const float* sh_lse = reinterpret_cast<const float*>(gbase + (set ? kVOffRow1 : kVOffRow0));
+    const float* sh_delta = sh_lse + kBN;
     cp_async_wait<0>();  // this query tile's Q, dO, lse and delta
     cta_sync_tc();
     // the other set was last read by the previous tile's dV / dK products
@@ -684,9 +688,9 @@ __global__ void __launch_bounds__(kBThreads, 1) dflash_attn_bwd_dkv_kernel(
     if (threadIdx.x == 0) {
 #pragma unroll
       for (int kk = 0; kk < kHD / 16; ++kk) {  // S^T = K Q^T, dP^T = V dO^T
-        umma_bf16(tmem + kColS, smem_desc(base + kBOffA + kk * 32, 16, 1024),
+        umma_bf16(tmem + kColS, smem_desc(base + kVOffK + kk * 32, 16, 1024),
                   smem_desc(base + offq + kk * 32, 16, 1024), kIdS, kk > 0);
-        umma_bf16(tmem + kColDP, smem_desc(base + kBOffB + kk * 32, 16, 1024),
+        umma_bf16(tmem + kColDP, smem_desc(base + kVOffV + kk * 32, 16, 1024),
                   smem_desc(base + offg + kk * 32, 16, 1024), kIdS, kk > 0);
       }
       umma_commit(bar);
@@ -698,16 +702,14 @@ __global__ void __launch_bounds__(kBThreads, 1) dflash_attn_bwd_dkv_kernel(
     ph ^= 1u;
     tc_fence_after();
     // every query of the tile sees every key of this CTA's tile: no per-element mask
-    const bool full = k0 + kTN <= T && q0 + kTM <= T && (q0 >= n_ctx || k0 + kTN - 1 <= q0);
-#pragma unroll
-    for (int c2 = 0; c2 < kTM / 64; ++c2) {
-      const int cc = half * (kTM / 64) + c2;  // this thread's half of the query columns
-      float sv[32], dp[32];
-      tmem_ld32x2(tmem + lane_base + kColS + cc * 32, tmem + lane_base + kColDP + cc * 32, sv, dp);
+    const bool full = k0 + kTM <= T && q0 + kBN <= T && (q0 >= n_ctx || k0 + kTM - 1 <= q0);
+    {
+      float sv[32], dp[32];  // this thread's half of the tile's 64 query columns
+      tmem_ld32x2(tmem + lane_base + kColS + half * 32, tmem + lane_base + kColDP + half * 32, sv, dp);
       uint32_t wp[16], wd[16];
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
-        const int c = cc * 32 + i;
+        const int c = half * 32 + i;
         float p0 = exp2_approx(fmaf(sv[i], sl2, -sh_lse[c] * kLog2e));
         float p1 = exp2_approx(fmaf(sv[i + 1], sl2, -sh_lse[c + 1] * kLog2e));
         if (!full) {
@@ -717,18 +719,17 @@ __global__ void __launch_bounds__(kBThreads, 1) dflash_attn_bwd_dkv_kernel(
         wp[i / 2] = pack_bf16x2(p0, p1);
         wd[i / 2] = pack_bf16x2(p0 * (dp[i] - sh_delta[c]) * scale, p1 * (dp[i + 1] - sh_delta[c + 1]) * scale);
       }
-      st_row32(base + kBOffP, (uint32_t)r_in, cc, wp);
-      st_row32(base + kBOffS, (uint32_t)r_in, cc, wd);
+      st_row32(base + kVOffP, (uint32_t)r_in, half, wp);
+      st_row32(base + kVOffS, (uint32_t)r_in, half, wd);
     }
     cta_sync_tc();
     if (threadIdx.x == 0) {  // dV += P^T dO, dK += dS^T Q
 #pragma unroll
-      for (int kk = 0; kk < kTM / 16; ++kk) {
+      for (int kk = 0; kk < kBN / 16; ++kk) {
         const uint32_t acc = (!first || kk > 0) ? 1u : 0u;
-        const uint32_t aoff = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
-        umma_bf16(tmem + kColAcc0, smem_desc(base + kBOffP + aoff, 16, 1024),
+        umma_bf16(tmem + kColAcc0, smem_desc(base + kVOffP + (uint32_t)kk * 32u, 16, 1024),
                   smem_desc(base + offg + (uint32_t)kk * 2048u, 16384, 1024), kIdKV, acc);
-        umma_bf16(tmem + kColAcc1, smem_desc(base + kBOffS + aoff, 16, 1024),
+        umma_bf16(tmem + kColAcc1, smem_desc(base + kVOffS + (uint32_t)kk * 32u, 16, 1024),
                   smem_desc(base + offq + (uint32_t)kk * 2048u, 16384, 1024), kIdKV, acc);
       }
       umma_commit(bar);
@@ -773,7 +774,7 @@ __global__ void __launch_bounds__(kBThreads, 1) dflash_attn_bwd_dkv_kernel(
   __syncthreads();
   tc_fence_after();
   if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemAll) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kBTmemCols) : "memory");
 }
 
 }  // namespace
