@@ -672,7 +672,10 @@ def time_drafter_step(args, dev, world, max_over_ranks, barrier):
             # the drafter body stays fp32; its output feature enters the bf16 head in bf16
             m.final_norm.register_forward_hook(lambda _m, _i, out: out.to(torch.bfloat16))
         if world > 1:
-            m = nn.parallel.DistributedDataParallel(m, device_ids=[dev.index])
+            # gradients as views of the all-reduce buckets (no copy in or out), no buffer
+            # broadcast (the drafter has none), and the same graph every step
+            m = nn.parallel.DistributedDataParallel(m, device_ids=[dev.index], broadcast_buffers=False,
+                                                    gradient_as_bucket_view=True, static_graph=True)
         return m
 
     def loss_fused(logits, tok):
