@@ -184,3 +184,47 @@ def test_drafter_with_kernels_matches_plain_torch(cuda):
     for n, g in gt.items():
         rel = float((gk[n].float() - g.float()).norm() / (g.float().norm() + 1e-12))
         assert rel <= 5e-2, (n, rel)
+
+
+@pytest.mark.parametrize("n_ctx", [0, 384])
+def test_attention_forward_rescale_path(cuda, n_ctx):
+    """Scores that grow tile by tile (key j scaled by 1 + j / 16): a row's
+    reference maximum is raised several times and O is rescaled in tensor
+    memory each time; output, lse and the backward still match the fp32
+    reference."""
+    from specdec import _lib, drafter
+
+    B, T, H = 2, 528, 2
+    g = torch.Generator(device="cuda").manual_seed(123)
+    q = torch.randn(B, T, H, 64, device="cuda", generator=g)
+    k = torch.randn(B, T, H, 64, device="cuda", generator=g)
+    k = k * (1.0 + torch.arange(T, device="cuda", dtype=torch.float32) / 16.0).view(1, T, 1, 1)
+    v = torch.randn(B, T, H, 64, device="cuda", generator=g)
+    q, k, v = (t.to(torch.bfloat16) for t in (q, k, v))
+    lib = _lib.load()
+    o = torch.empty_like(q)
+    lse = torch.empty(B, H, T, device="cuda")
+    status = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    rc = lib.specdec_dflash_attention_forward(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                                              lse.data_ptr(), B, T, H, 64, n_ctx, 0.125, status.data_ptr(),
+                                              torch.cuda.current_stream().cuda_stream)
+    assert rc == _lib.OK, _lib.last_error()
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    o_ref, lse_ref = _ref_attention(q, k, v, n_ctx, 0.125)
+    assert float((lse_ref.amax() - lse_ref.amin())) > 20.0  # the scores do span several 2^8 steps
+    err = (o.float() - o_ref).abs()
+    assert bool((err <= 1e-2 + 1e-2 * o_ref.abs()).all()), float(err.max())
+    assert float(((lse - lse_ref).abs() / lse_ref.abs().clamp_min(1.0)).max()) <= 1e-3
+    do = torch.randn(B, T, H, 64, device="cuda", generator=g).to(torch.bfloat16)
+    qs, ks, vs = (t.clone().requires_grad_(True) for t in (q, k, v))
+    drafter.dflash_attention(qs, ks, vs, n_ctx).backward(do)
+    qr, kr, vr = (t.float().clone().requires_grad_(True) for t in (q, k, v))
+    _ref_attention(qr, kr, vr, n_ctx, 0.125)[0].backward(do.float())
+    # keys up to 34x larger make dQ = dS K sum ~500 products of that size with dS rounded to
+    # bf16 (2^-9): the bound is relative to each gradient's own scale
+    for got, want in ((qs.grad, qr.grad), (ks.grad, kr.grad), (vs.grad, vr.grad)):
+        err = (got.float() - want).abs()
+        scale = float(want.abs().max())
+        assert float(err.max()) <= 2e-2 * scale, (float(err.max()), scale)
+        assert float(err.norm() / want.norm()) <= 1e-2
