@@ -10,6 +10,7 @@ There is no fallback: if the library is missing, every entry point raises.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 import threading
@@ -131,6 +132,14 @@ def check(code: int, what: str) -> None:
 
 def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
+
+
+def on_device(device: torch.device):
+    """Context that makes `device` current: a no-op when it already is (the
+    common case; entering torch.cuda.device costs host time on every call)."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
 
 
 def stream_handle(device: torch.device) -> int:

@@ -46,7 +46,7 @@ class _RMSNorm(torch.autograd.Function):
         w = weight.detach().float().contiguous()
         y = torch.empty_like(x2)
         rstd = torch.empty(x2.shape[0], dtype=torch.float32, device=x.device)
-        with torch.cuda.device(x.device):
+        with _lib.on_device(x.device):
             _lib.check(lib.specdec_rmsnorm_forward(x2.data_ptr(), w.data_ptr(), y.data_ptr(), rstd.data_ptr(),
                                                    x2.shape[0], D, float(eps), _DTYPES[x.dtype], _stream(x)),
                        "specdec_rmsnorm_forward")
@@ -62,7 +62,7 @@ class _RMSNorm(torch.autograd.Function):
         dy2 = dy.to(x2.dtype).contiguous().view(-1, D)
         dx = torch.empty_like(x2)
         dw = torch.empty(D, dtype=torch.float32, device=x2.device)
-        with torch.cuda.device(x2.device):
+        with _lib.on_device(x2.device):
             ws_bytes = lib.specdec_rmsnorm_workspace_bytes(x2.shape[0], D, x2.device.index)
             ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x2.device)
             _lib.check(lib.specdec_rmsnorm_backward(x2.data_ptr(), w.data_ptr(), rstd.data_ptr(), dy2.data_ptr(),
@@ -91,7 +91,7 @@ class _DFlashAttention(torch.autograd.Function):
         q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
         o = torch.empty_like(q)
         lse = torch.empty(B, H, T, dtype=torch.float32, device=q.device)
-        with torch.cuda.device(q.device):
+        with _lib.on_device(q.device):
             _lib.check(lib.specdec_dflash_attention_forward(
                 q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), B, T, H, Dh,
                 int(n_ctx), float(scale), None, _stream(q)), "specdec_dflash_attention_forward")
@@ -106,7 +106,7 @@ class _DFlashAttention(torch.autograd.Function):
         B, T, H, Dh = q.shape
         do = do.to(q.dtype).contiguous()
         dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-        with torch.cuda.device(q.device):
+        with _lib.on_device(q.device):
             ws_bytes = lib.specdec_dflash_attention_workspace_bytes(B, T, H)
             ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
             _lib.check(lib.specdec_dflash_attention_backward(
@@ -118,7 +118,7 @@ class _DFlashAttention(torch.autograd.Function):
 
 def attention_supported(q: torch.Tensor) -> bool:
     return (ENABLED and q.is_cuda and q.dtype == torch.bfloat16 and q.dim() == 4 and q.shape[-1] == 64
-            and q.shape[0] * q.shape[2] <= 65535)
+            and q.shape[1] <= 65535 * 128)
 
 
 def dflash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, n_ctx: int,

@@ -249,7 +249,7 @@ def _dflash_backward(logits: torch.Tensor, target_logits: torch.Tensor | None, s
 
 def _on_device(fn):
     def wrapped(logits, *args, **kwargs):
-        with torch.cuda.device(logits.device):
+        with _lib.on_device(logits.device):
             return fn(logits, *args, **kwargs)
     wrapped.__name__ = fn.__name__.lstrip("_")
     wrapped.__doc__ = fn.__doc__
