@@ -665,13 +665,13 @@ def time_drafter_step(args, dev, world, max_over_ranks, barrier):
     mask = torch.ones(Nb, blk, device=dev)
     mask[:, 0] = 0.0
 
-    def build(lm_head):
+    def build(lm_head, ddp):
         m = DFlashSpeculator(d_target=D, d_model=256, target_vocab_size=V, block_size=blk, num_layers=3,
                              num_heads=4, target_lm_head=lm_head).to(dev)
         if lm_head.weight.dtype == torch.bfloat16:
             # the drafter body stays fp32; its output feature enters the bf16 head in bf16
             m.final_norm.register_forward_hook(lambda _m, _i, out: out.to(torch.bfloat16))
-        if world > 1:
+        if ddp and world > 1:
             # gradients as views of the all-reduce buckets (no copy in or out), no buffer
             # broadcast (the drafter has none), and the same graph every step
             m = nn.parallel.DistributedDataParallel(m, device_ids=[dev.index], broadcast_buffers=False,
@@ -685,6 +685,7 @@ def time_drafter_step(args, dev, world, max_over_ranks, barrier):
         return torch_ops_dpace_loss(logits, tok, 0.5, mask)
 
     from specdec import drafter as layer_kernels
+    from specdec.graphs import allreduce_grads
 
     # (name, lm_head, objective, autocast, the drafter's norms/attention on the library's kernels)
     variants = [("fused_loss_fp32_logits", head, loss_fused, False, True, False),
@@ -692,15 +693,15 @@ def time_drafter_step(args, dev, world, max_over_ranks, barrier):
                 ("fused_loss_bf16_logits", head_bf16, loss_fused, False, True, False),
                 ("bf16_autocast_drafter_fused_loss", head_bf16, loss_fused, True, True, False),
                 ("bf16_autocast_drafter_torch_layers_fused_loss", head_bf16, loss_fused, True, False, False)]
-    if world == 1:
-        # the same step captured once as a CUDA graph (specdec.graphs.GraphedStep) and replayed
-        variants.append(("bf16_autocast_drafter_fused_loss_graphed", head_bf16, loss_fused, True, True, True))
+    # the same step captured once as a CUDA graph (specdec.graphs.GraphedStep) and replayed; with
+    # N > 1 the gradient all-reduce (one NCCL call on the flat gradient) is captured with it
+    variants.append(("bf16_autocast_drafter_fused_loss_graphed", head_bf16, loss_fused, True, True, True))
     out = {}
     stream = torch.cuda.current_stream(dev)
     for name, lm_head, lfn, autocast, kernels, graphed in variants:
         layer_kernels.set_enabled(kernels)
-        model = build(lm_head)
-        core = model.module if world > 1 else model
+        model = build(lm_head, ddp=not graphed)
+        core = model.module if (world > 1 and not graphed) else model
         params = [p for p in model.parameters() if p.requires_grad]
         # the graphed step runs the fused AdamW kernel (capturable): the capturable foreach form
         # is ~60 elementwise launches per step, ~0.8 ms at this size
@@ -709,9 +710,11 @@ def time_drafter_step(args, dev, world, max_over_ranks, barrier):
         def step_fn(f_in, t_in):
             opt.zero_grad(set_to_none=True)
             with torch.autocast("cuda", dtype=torch.bfloat16, enabled=autocast, cache_enabled=not graphed):
-                loss = core.compute_loss(f_in, t_in, loss_fn=lfn) if world == 1 else \
+                loss = core.compute_loss(f_in, t_in, loss_fn=lfn) if (world == 1 or graphed) else \
                     lfn(model(f_in), t_in)
             loss.backward()
+            if graphed and world > 1:
+                allreduce_grads(params)
             torch.nn.utils.clip_grad_norm_(params, 1.0)
             opt.step()
             return loss
@@ -745,7 +748,10 @@ def time_drafter_step(args, dev, world, max_over_ranks, barrier):
         out[name] = {"ms_per_step": round(ms, 3), "rows_per_s": round(Nb * blk * world / (ms * 1e-3), 1),
                      "loss": round(float(loss.detach()), 6), "library_layers": kernels,
                      "cuda_graph": graphed}
-        del model, core, opt, params, gstep, step, step_fn
+        # the graph (with its NCCL all-reduce for N > 1) is released here, well before the
+        # process group is destroyed
+        del model, core, opt, params, gstep, step, step_fn, loss
+        torch.cuda.synchronize(dev)
         torch.cuda.empty_cache()
     layer_kernels.set_enabled(True)
     torch.backends.cuda.matmul.allow_tf32 = prev_tf32
@@ -764,10 +770,11 @@ def time_drafter_step(args, dev, world, max_over_ranks, barrier):
                        "gemms": "cuBLAS, TF32 for fp32", "parallelism": f"ddp{world}",
                        "library_layers": "RMSNorm kernels (fp32/bf16) and, for bf16 q/k/v, the tcgen05 "
                                          "attention forward and backward (specdec.drafter)",
-                       "cuda_graph": "the _graphed variant (one GPU) replays the whole step -- forward, "
-                                     "loss, backward, clip, AdamW(fused, capturable) -- as one CUDA graph "
-                                     "(specdec.graphs.GraphedStep); the others launch eagerly with the "
-                                     "default AdamW"},
+                       "cuda_graph": "the _graphed variant replays the whole step -- forward, loss, "
+                                     "backward, the gradient all-reduce (N > 1: one NCCL call on the flat "
+                                     "gradient, specdec.graphs.allreduce_grads), clip, AdamW(fused, "
+                                     "capturable) -- as one CUDA graph (specdec.graphs.GraphedStep); the "
+                                     "others launch eagerly with the default AdamW and, for N > 1, DDP"},
             "variants": out}
 
 

@@ -22,12 +22,35 @@ Requirements on ``fn``, as for any CUDA-graph capture:
 Warm-up calls and the capture run on one side stream, so the library's
 per-stream workspace and status words exist before capture starts. Replays of
 one GraphedStep must not overlap (they share that workspace).
+
+Data parallel over N GPUs: call ``allreduce_grads(params)`` after
+``loss.backward()`` inside ``fn`` (one NCCL all-reduce of the flat gradient,
+captured with the step) on a model that is not wrapped in DDP; every rank
+builds, warms up, captures and replays the same step. Release the
+GraphedStep before ``destroy_process_group``.
 """
 from __future__ import annotations
 
 import torch
+import torch.distributed as dist
 
 from . import _lib
+
+
+def allreduce_grads(params, group=None) -> None:
+    """Averages the parameters' gradients over the ranks of `group` with one
+    all-reduce of a flat buffer (one NCCL call instead of one per tensor).
+    Nothing in it synchronises with the host, so it captures inside a CUDA
+    graph with the rest of the step: every rank replays the same collective.
+    Every rank must pass the same parameters, with gradients."""
+    grads = [p.grad for p in params if p.grad is not None]
+    if not grads:
+        return
+    flat = torch.cat([g.reshape(-1) for g in grads])
+    dist.all_reduce(flat, group=group)
+    flat.div_(dist.get_world_size(group))
+    for g, v in zip(grads, torch._utils._unflatten_dense_tensors(flat, grads)):
+        g.copy_(v)
 
 
 class GraphedStep:

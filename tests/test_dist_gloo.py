@@ -116,3 +116,50 @@ def test_failed_rank_surfaces_as_error_on_peer():
     out = _run("fail")
     assert out[1][1] == "error" and "injected" in out[1][3]
     assert out[0][1] == "error", out[0]  # the peer's reduction errors out instead of hanging
+
+
+def _grad_worker(rank, world, port, q):
+    _setup_paths()
+    import torch.distributed as dist
+
+    from specdec.graphs import allreduce_grads
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+        torch.manual_seed(0)
+        params = [torch.nn.Parameter(torch.randn(3, 5)), torch.nn.Parameter(torch.randn(7)),
+                  torch.nn.Parameter(torch.randn(2, 2, 2))]
+        g = torch.Generator().manual_seed(100 + rank)
+        for p in params:
+            p.grad = torch.randn(p.shape, generator=g)
+        local = [p.grad.clone() for p in params]
+        allreduce_grads(params)
+        q.put((rank, [l.numpy() for l in local], [p.grad.numpy() for p in params]))
+        dist.destroy_process_group()
+    except Exception:
+        q.put((rank, "error", traceback.format_exc()))
+
+
+def test_allreduce_grads_averages_over_ranks():
+    """specdec.graphs.allreduce_grads: every rank ends with the mean of the
+    ranks' gradients, tensor by tensor, in the original shapes."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_grad_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict()
+    for _ in range(2):
+        r, a, b = q.get(timeout=60)
+        assert a != "error", b
+        res[r] = (a, b)
+    for p in procs:
+        p.join(timeout=30)
+    mean = [(x + y) / 2 for x, y in zip(res[0][0], res[1][0])]
+    for r in range(2):
+        for m_, got in zip(mean, res[r][1]):
+            assert got.shape == m_.shape
+            np.testing.assert_allclose(got, m_, rtol=1e-6, atol=1e-7)
