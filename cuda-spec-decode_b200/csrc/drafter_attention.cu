@@ -216,7 +216,8 @@ __global__ void __launch_bounds__(kThreads, kFCtas) dflash_attn_fwd_kernel(const
                                                                            const bf16_t* __restrict__ v,
                                                                            bf16_t* __restrict__ o,
                                                                            float* __restrict__ lse, int T, int H,
-                                                                           int n_ctx, float scale_log2, int* status) {
+                                                                           int n_ctx, float scale_log2, int* status,
+                                                                           int withhold) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   unsigned char* gbase = smem_raw + (base - smem_u32(smem_raw));
@@ -276,7 +277,9 @@ __global__ void __launch_bounds__(kThreads, kFCtas) dflash_attn_fwd_kernel(const
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (threadIdx.x == 0) {  // S = Q K^T
+    // failure-detection test hook: the grid's first CTA issues nothing for its
+    // first tile, so its own wait runs into the limit
+    if (threadIdx.x == 0 && !(withhold && k0 == 0 && blockIdx.x == 0 && blockIdx.y == 0)) {  // S = Q K^T
 #pragma unroll
       for (int kk = 0; kk < kHD / 16; ++kk)
         umma_bf16(tmem, smem_desc(base + kFOffQ + kk * 32, 16, 1024), smem_desc(base + kFOffK + kk * 32, 16, 1024),
@@ -378,6 +381,14 @@ __global__ void __launch_bounds__(kThreads, kFCtas) dflash_attn_fwd_kernel(const
     // wait (bounded) for the products this CTA may still have in flight
     wait_bar(bar_s, ph);
     wait_bar(bar_o, ph);
+    // never a plausible wrong number: this CTA's rows of o and lse are NaN
+    if (row < T) {
+      bf16_t* orow = o + ((int64_t)b * T + row) * rs + (int64_t)h * kHD;
+#pragma unroll
+      for (int c = 0; c < kHD / 8; ++c)
+        *reinterpret_cast<uint4*>(orow + 8 * c) = make_uint4(0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u);
+      lse[((int64_t)b * H + h) * T + row] = __int_as_float(0x7fc00000);
+    }
   } else {
     float ot[2][32];
     tmem_ld32x2(tmem + lane_base + kFColO, tmem + lane_base + kFColO + 32, ot[0], ot[1]);
@@ -483,7 +494,8 @@ __device__ __forceinline__ void cta_sync_tc() {
 __global__ void __launch_bounds__(kBThreads, kBCtas) dflash_attn_bwd_dq_kernel(
     const bf16_t* __restrict__ q, const bf16_t* __restrict__ k, const bf16_t* __restrict__ v,
     const bf16_t* __restrict__ o, const float* __restrict__ lse, const bf16_t* __restrict__ dO,
-    bf16_t* __restrict__ dq, float* __restrict__ delta_out, int T, int H, int n_ctx, float scale, int* status) {
+    bf16_t* __restrict__ dq, float* __restrict__ delta_out, int T, int H, int n_ctx, float scale, int* status,
+    int withhold) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   unsigned char* gbase = smem_raw + (base - smem_u32(smem_raw));
@@ -545,7 +557,8 @@ __global__ void __launch_bounds__(kBThreads, kBCtas) dflash_attn_bwd_dq_kernel(
     // the other K buffer was last read by the previous tile's dQ product: fill it now
     if (more) load_tile_async<kBThreads, kBN>(base + knext, k + head, rs, k0 + kBN, T);
     cp_async_commit();
-    if (threadIdx.x == 0) {
+    // failure-detection test hook: the grid's first CTA issues nothing for its first tile
+    if (threadIdx.x == 0 && !(withhold && k0 == 0 && blockIdx.x == 0 && blockIdx.y == 0)) {
 #pragma unroll
       for (int kk = 0; kk < kHD / 16; ++kk) {  // S = Q K^T, dP = dO V^T
         umma_bf16(tmem + kColS, smem_desc(base + kQOffQ + kk * 32, 16, 1024),
@@ -601,6 +614,11 @@ __global__ void __launch_bounds__(kBThreads, kBCtas) dflash_attn_bwd_dq_kernel(
   if (!ok) {
     if (threadIdx.x == 0 && status) atomicExch(status, kStatusTimeout);
     wait_bar(bar, ph);
+    if (row < T) {  // never a plausible wrong number: this CTA's rows of dq are NaN
+      bf16_t* drow = dq + head + (int64_t)row * rs + half * 32;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(drow + 8 * c) = make_uint4(0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u);
+    }
   } else {
     tc_fence_after();
     float acc[32];  // this thread's half of the row's 64 dQ columns
@@ -625,7 +643,8 @@ __global__ void __launch_bounds__(kBThreads, kBCtas) dflash_attn_bwd_dq_kernel(
 __global__ void __launch_bounds__(kBThreads, kBCtas) dflash_attn_bwd_dkv_kernel(
     const bf16_t* __restrict__ q, const bf16_t* __restrict__ k, const bf16_t* __restrict__ v,
     const float* __restrict__ lse, const float* __restrict__ delta, const bf16_t* __restrict__ dO,
-    bf16_t* __restrict__ dk, bf16_t* __restrict__ dv, int T, int H, int n_ctx, float scale, int* status) {
+    bf16_t* __restrict__ dk, bf16_t* __restrict__ dv, int T, int H, int n_ctx, float scale, int* status,
+    int withhold) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   unsigned char* gbase = smem_raw + (base - smem_u32(smem_raw));
@@ -685,7 +704,8 @@ __global__ void __launch_bounds__(kBThreads, kBCtas) dflash_attn_bwd_dkv_kernel(
     // the other set was last read by the previous tile's dV / dK products
     if (qt + 1 < qt_end) load_query_tile(qt + 1, set ^ 1);
     cp_async_commit();
-    if (threadIdx.x == 0) {
+    // failure-detection test hook: the grid's first CTA issues nothing for its first tile
+    if (threadIdx.x == 0 && !(withhold && first && blockIdx.x == 0 && blockIdx.y == 0)) {
 #pragma unroll
       for (int kk = 0; kk < kHD / 16; ++kk) {  // S^T = K Q^T, dP^T = V dO^T
         umma_bf16(tmem + kColS, smem_desc(base + kVOffK + kk * 32, 16, 1024),
@@ -746,6 +766,15 @@ __global__ void __launch_bounds__(kBThreads, kBCtas) dflash_attn_bwd_dkv_kernel(
   if (!ok) {
     if (threadIdx.x == 0 && status) atomicExch(status, kStatusTimeout);
     wait_bar(bar, ph);
+    if (key < T) {  // never a plausible wrong number: this CTA's rows of dk and dv are NaN
+      bf16_t* vr = dv + head + (int64_t)key * rs + half * 32;
+      bf16_t* kr = dk + head + (int64_t)key * rs + half * 32;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        *reinterpret_cast<uint4*>(vr + 8 * c) = make_uint4(0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u);
+        *reinterpret_cast<uint4*>(kr + 8 * c) = make_uint4(0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u);
+      }
+    }
   } else {
     tc_fence_after();
     // keys no query sees (none here: the qt loop covers every visible pair) still get zeros;
@@ -793,19 +822,19 @@ static cudaError_t ensure_smem_limit_attn(size_t bytes) {
 }
 
 cudaError_t dflash_attn_fwd_launch(const void* q, const void* k, const void* v, void* o, float* lse, int batch, int T,
-                                   int H, int n_ctx, float scale, int* status, cudaStream_t st) {
+                                   int H, int n_ctx, float scale, int* status, int withhold, cudaStream_t st) {
   const cudaError_t e = ensure_smem_limit_attn(kSmemBytes);
   if (e != cudaSuccess) return e;
   const dim3 grid((unsigned)(batch * H), (unsigned)((T + kTM - 1) / kTM));
   dflash_attn_fwd_kernel<<<grid, kThreads, kSmemBytes, st>>>(
       static_cast<const bf16_t*>(q), static_cast<const bf16_t*>(k), static_cast<const bf16_t*>(v),
-      static_cast<bf16_t*>(o), lse, T, H, n_ctx, scale * kLog2e, status);
+      static_cast<bf16_t*>(o), lse, T, H, n_ctx, scale * kLog2e, status, withhold);
   return cudaGetLastError();
 }
 
 cudaError_t dflash_attn_bwd_launch(const void* q, const void* k, const void* v, const void* o, const float* lse,
                                    const void* dO, void* dq, void* dk, void* dv, float* delta, int batch, int T, int H,
-                                   int n_ctx, float scale, int* status, cudaStream_t st) {
+                                   int n_ctx, float scale, int* status, int withhold, cudaStream_t st) {
   static std::atomic<unsigned long long> done{0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -823,13 +852,13 @@ cudaError_t dflash_attn_bwd_launch(const void* q, const void* k, const void* v, 
   dflash_attn_bwd_dq_kernel<<<grid, kBThreads, kBSmemBytes, st>>>(
       static_cast<const bf16_t*>(q), static_cast<const bf16_t*>(k), static_cast<const bf16_t*>(v),
       static_cast<const bf16_t*>(o), lse, static_cast<const bf16_t*>(dO), static_cast<bf16_t*>(dq), delta, T, H,
-      n_ctx, scale, status);
+      n_ctx, scale, status, withhold);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   dflash_attn_bwd_dkv_kernel<<<grid, kBThreads, kBSmemBytesKV, st>>>(
       static_cast<const bf16_t*>(q), static_cast<const bf16_t*>(k), static_cast<const bf16_t*>(v), lse, delta,
       static_cast<const bf16_t*>(dO), static_cast<bf16_t*>(dk), static_cast<bf16_t*>(dv), T, H, n_ctx, scale,
-      status);
+      status, withhold);
   return cudaGetLastError();
 }
 

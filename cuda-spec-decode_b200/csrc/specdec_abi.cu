@@ -893,15 +893,12 @@ int specdec_dflash_attention_forward(const uint16_t* q, const uint16_t* k, const
   if ((T + 127) / 128 > 65535) return fail(SPECDEC_ERR_ARGUMENT, "T must be <= 65535 * 128");
   if (!(scale > 0.f)) return fail(SPECDEC_ERR_VALUE, "scale must be > 0");
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (status) {
-    const cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int32_t), st);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
-  }
   if (batch == 0 || T == 0) return ok();
   if (!q || !k || !v || !o || !lse) return fail(SPECDEC_ERR_ARGUMENT, "null input or output pointer");
   if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(o, 16))
     return fail(SPECDEC_ERR_ARGUMENT, "q, k, v and o must be 16-byte aligned");
-  const cudaError_t e = dflash_attn_fwd_launch(q, k, v, o, lse, batch, T, heads, n_ctx, scale, status, st);
+  const cudaError_t e =
+      dflash_attn_fwd_launch(q, k, v, o, lse, batch, T, heads, n_ctx, scale, status, take_withhold_stage(), st);
   return e == cudaSuccess ? ok() : cuda_fail(e, "attention forward launch");
 }
 
@@ -922,10 +919,6 @@ int specdec_dflash_attention_backward(const uint16_t* q, const uint16_t* k, cons
   if ((T + 127) / 128 > 65535) return fail(SPECDEC_ERR_ARGUMENT, "T must be <= 65535 * 128");
   if (!(scale > 0.f)) return fail(SPECDEC_ERR_VALUE, "scale must be > 0");
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (status) {
-    const cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int32_t), st);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
-  }
   if (batch == 0 || T == 0) return ok();
   if (!q || !k || !v || !o || !lse || !dout || !dq || !dk || !dv || !workspace)
     return fail(SPECDEC_ERR_ARGUMENT, "null input, output or workspace pointer");
@@ -935,7 +928,7 @@ int specdec_dflash_attention_backward(const uint16_t* q, const uint16_t* k, cons
   const size_t need = (size_t)batch * (size_t)heads * (size_t)T * sizeof(float);
   if (workspace_bytes < need) return fail(SPECDEC_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
   const cudaError_t e = dflash_attn_bwd_launch(q, k, v, o, lse, dout, dq, dk, dv, static_cast<float*>(workspace), batch,
-                                               T, heads, n_ctx, scale, status, st);
+                                               T, heads, n_ctx, scale, status, take_withhold_stage(), st);
   return e == cudaSuccess ? ok() : cuda_fail(e, "attention backward launch");
 }
 

@@ -182,11 +182,11 @@ cudaError_t rmsnorm_bwd_launch(int dtype, const void* x, const float* w, const f
 // Attention of the drafter on the tensor cores (drafter_attention.cu):
 // bf16 q/k/v/o [B, T, H, 64], lse fp32 [B, H, T].
 cudaError_t dflash_attn_fwd_launch(const void* q, const void* k, const void* v, void* o, float* lse, int batch, int T,
-                                   int H, int n_ctx, float scale, int* status, cudaStream_t st);
+                                   int H, int n_ctx, float scale, int* status, int withhold, cudaStream_t st);
 // Backward: delta [B, H, T] fp32 is scratch written by the first kernel.
 cudaError_t dflash_attn_bwd_launch(const void* q, const void* k, const void* v, const void* o, const float* lse,
                                    const void* dO, void* dq, void* dk, void* dv, float* delta, int batch, int T, int H,
-                                   int n_ctx, float scale, int* status, cudaStream_t st);
+                                   int n_ctx, float scale, int* status, int withhold, cudaStream_t st);
 
 // Sets the calling thread's specdec_last_error() text.
 void set_last_error(const char* msg);

@@ -196,6 +196,7 @@ def workspace(family: str, device: torch.device) -> Workspace:
 STATUS_DPACE_FWD = 0   # the D-PACE forward (and forward_backward): 0, ERR_TARGET_RANGE or ERR_CUDA
 STATUS_DPACE_BWD = 1   # the last D-PACE backward: 0 or ERR_CUDA
 STATUS_DFLASH_BWD = 2  # the last DFlash backward: 0 or ERR_CUDA
+STATUS_DRAFTER = 3     # the drafter's attention kernels, sticky: 0, or ERR_CUDA once any wait expired
 _status: dict = {}
 
 

@@ -37,6 +37,14 @@ def _stream(t: torch.Tensor) -> int:
     return _lib.stream_handle(t.device)
 
 
+def _status(dev: torch.device) -> int:
+    """The stream's sticky drafter status word: the attention kernels set it
+    when a bounded wait expires (their failed rows are then NaN); the next
+    synchronising check (specdec.ops.check_backward, a validating D-PACE
+    forward, GraphedStep.check) raises RuntimeError and clears it."""
+    return _lib.status_words(dev)[_lib.STATUS_DRAFTER:].data_ptr()
+
+
 class _RMSNorm(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight, eps):
@@ -94,7 +102,7 @@ class _DFlashAttention(torch.autograd.Function):
         with _lib.on_device(q.device):
             _lib.check(lib.specdec_dflash_attention_forward(
                 q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), B, T, H, Dh,
-                int(n_ctx), float(scale), None, _stream(q)), "specdec_dflash_attention_forward")
+                int(n_ctx), float(scale), _status(q.device), _stream(q)), "specdec_dflash_attention_forward")
         ctx.save_for_backward(q, k, v, o, lse)
         ctx.n_ctx, ctx.scale = int(n_ctx), float(scale)
         return o
@@ -111,7 +119,7 @@ class _DFlashAttention(torch.autograd.Function):
             ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
             _lib.check(lib.specdec_dflash_attention_backward(
                 q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), do.data_ptr(),
-                dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, T, H, Dh, ctx.n_ctx, ctx.scale, None,
+                dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, T, H, Dh, ctx.n_ctx, ctx.scale, _status(q.device),
                 ws.data_ptr(), ws_bytes, _stream(q)), "specdec_dflash_attention_backward")
         return dq, dk, dv, None, None
 

@@ -88,10 +88,13 @@ class GraphedStep:
         """Synchronises and raises as the eager calls would have: ValueError
         for a D-PACE target outside [0, V) in the last replay, RuntimeError
         for an expired bounded wait in any captured kernel."""
-        st = self.status[:3].tolist()
+        st = self.status[:4].tolist()
         if st[_lib.STATUS_DPACE_BWD] or st[_lib.STATUS_DFLASH_BWD]:
             self.status[1:3].zero_()
             raise RuntimeError("a backward kernel of the captured step had a bounded wait expire")
+        if st[_lib.STATUS_DRAFTER]:
+            self.status[3:4].zero_()
+            raise RuntimeError("an attention kernel of the captured step had a bounded wait expire")
         if st[_lib.STATUS_DPACE_FWD] == _lib.ERR_TARGET_RANGE:
             raise ValueError("targets out of range")
         if st[_lib.STATUS_DPACE_FWD] == _lib.ERR_CUDA:

@@ -60,6 +60,8 @@ def _aligned(t: torch.Tensor | None) -> torch.Tensor | None:
     return t.clone()
 
 
+_ATTN_TIMEOUT_MSG = ("an earlier drafter attention launch on this stream had a bounded wait expire; the rows "
+                     "of its outputs that the failed part owned hold NaN")
 _BWD_TIMEOUT_MSG = ("an earlier backward launch on this stream had a bounded wait expire; the blocks of "
                     "its gradient that the failed part left unfinished hold NaN")
 
@@ -78,10 +80,13 @@ def _read_status(dev: torch.device, what: str, V: int) -> None:
     backward on the stream (reported here, at the next synchronising call, so
     that the autograd backward itself never synchronises)."""
     words = _lib.status_words(dev)
-    st = words[:3].tolist()
+    st = words[:4].tolist()
     if st[_lib.STATUS_DPACE_BWD] or st[_lib.STATUS_DFLASH_BWD]:
         words[1:3].zero_()
         raise RuntimeError(_BWD_TIMEOUT_MSG)
+    if st[_lib.STATUS_DRAFTER]:
+        words[3:4].zero_()
+        raise RuntimeError(_ATTN_TIMEOUT_MSG)
     if st[_lib.STATUS_DPACE_FWD] == _lib.ERR_TARGET_RANGE:
         raise ValueError(f"targets out of range [0, {V})")
     if st[_lib.STATUS_DPACE_FWD] == _lib.ERR_CUDA:  # counters are in an unknown state
@@ -91,16 +96,20 @@ def _read_status(dev: torch.device, what: str, V: int) -> None:
 
 def check_backward(device: torch.device | int | None = None) -> None:
     """Synchronise with the current stream of `device` and raise RuntimeError
-    if a D-PACE or DFlash backward launched on it since the last check had a
-    bounded wait expire (its gradient then holds NaN blocks). Every D-PACE
-    forward that validates its targets performs this check as well."""
+    if a D-PACE or DFlash backward, or a drafter attention kernel, launched on
+    it since the last check had a bounded wait expire (its outputs then hold
+    NaN where the failed part wrote). Every D-PACE forward that validates its
+    targets performs this check as well."""
     dev = torch.device("cuda", torch.cuda.current_device() if device is None else
                        (device if isinstance(device, int) else device.index))
     words = _lib.status_words(dev)
-    st = words[:3].tolist()
+    st = words[:4].tolist()
     if st[_lib.STATUS_DPACE_BWD] or st[_lib.STATUS_DFLASH_BWD]:
         words[1:3].zero_()
         raise RuntimeError(_BWD_TIMEOUT_MSG)
+    if st[_lib.STATUS_DRAFTER]:
+        words[3:4].zero_()
+        raise RuntimeError(_ATTN_TIMEOUT_MSG)
 
 
 def _dpace_forward(logits: torch.Tensor, targets: torch.Tensor, mask: torch.Tensor | None,

@@ -303,8 +303,10 @@ int specdec_rmsnorm_backward(const void* x, const float* weight, const float* rs
  *               projections' own layout), 16-byte aligned; head_dim = 64
  *   lse         [batch, heads, T] fp32: log-sum-exp of each query row's
  *               scaled scores (natural log), for a backward
- *   status      [1] int32 or NULL: SPECDEC_ERR_CUDA if a bounded wait of
- *               the kernel expired (the outputs are then unspecified)
+ *   status      [1] int32 or NULL: set to SPECDEC_ERR_CUDA if a bounded
+ *               wait of the kernel expired, never cleared by the call (zero
+ *               it first for a per-call report); the rows of o and lse the
+ *               failed part owned are then NaN, never a plausible value
  * P = softmax is rounded to bf16 before the second product, the
  * accumulation is fp32. 0 <= n_ctx <= T <= 65535 * 128.
  */
@@ -323,7 +325,8 @@ size_t specdec_dflash_attention_workspace_bytes(int32_t batch, int32_t T, int32_
  * are recomputed from lse; dS = P * (dP - rowsum(dout * o)) * scale;
  * products in bf16 with fp32 accumulation, every sum in a fixed order (no
  * atomics: bitwise repeatable). workspace: specdec_dflash_attention_
- * workspace_bytes() of device memory, no initialisation required.
+ * workspace_bytes() of device memory, no initialisation required. status
+ * as in the forward (sticky; the failed part's rows of dq / dk / dv NaN).
  */
 int specdec_dflash_attention_backward(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* o,
                                       const float* lse, const uint16_t* dout, uint16_t* dq, uint16_t* dk,
@@ -376,8 +379,11 @@ int specdec_set_block_queue(int32_t dynamic);
  * 2 s. A forward so failed gives a NaN loss and NaN per-row lse/scale/logz
  * (and, for D-PACE, *status = SPECDEC_ERR_CUDA); a backward gives
  * *status = SPECDEC_ERR_CUDA and NaN over the blocks CTA 0 held. The context
- * stays usable and the next launch is normal. 0 cancels. Not for production
- * use. The same reports follow any wait that expires for a real reason.
+ * stays usable and the next launch is normal. Drafter attention launches
+ * (forward, backward) consume armed launches too: the grid's first CTA
+ * issues no product for its first tile, its wait expires, *status is set and
+ * its rows of the outputs are NaN. 0 cancels. Not for production use. The
+ * same reports follow any wait that expires for a real reason.
  */
 int specdec_test_withhold_stage(int32_t launches);
 

@@ -91,7 +91,7 @@ def test_attention_forward_matches_reference(cuda, B, T, H, n_ctx):
     lib = _lib.load()
     o = torch.empty_like(q)
     lse = torch.empty(B, H, T, device="cuda")
-    status = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    status = torch.zeros((1,), dtype=torch.int32, device="cuda")  # sticky: set only on an expired wait
     rc = lib.specdec_dflash_attention_forward(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
                                               lse.data_ptr(), B, T, H, 64, n_ctx, 0.125, status.data_ptr(),
                                               torch.cuda.current_stream().cuda_stream)
@@ -204,7 +204,7 @@ def test_attention_forward_rescale_path(cuda, n_ctx):
     lib = _lib.load()
     o = torch.empty_like(q)
     lse = torch.empty(B, H, T, device="cuda")
-    status = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    status = torch.zeros((1,), dtype=torch.int32, device="cuda")  # sticky: set only on an expired wait
     rc = lib.specdec_dflash_attention_forward(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
                                               lse.data_ptr(), B, T, H, 64, n_ctx, 0.125, status.data_ptr(),
                                               torch.cuda.current_stream().cuda_stream)

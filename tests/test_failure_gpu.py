@@ -244,3 +244,111 @@ def test_dflash_forward_expired_wait_makes_the_whole_gradient_nan(cuda):
     torch.cuda.synchronize()
     assert bool(torch.isnan(loss.detach()))
     assert bool(torch.isnan(xg.grad).all())
+
+
+def _attn_inputs(seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    B, T, H = 2, 528, 2
+    return [torch.randn(B, T, H, 64, device="cuda", generator=g).to(torch.bfloat16) for _ in range(4)]
+
+
+def test_attention_expired_wait_gives_status_and_nan_rows(cuda):
+    """The drafter's attention: with a stage withheld the grid's first CTA
+    (batch 0, head 0, the last query tile -- the block slots, rows 512..527)
+    gives up after its bounded wait; *status is 5 and exactly its rows of o
+    and lse are NaN; every other row equals a normal call's. The backward the
+    same: status 5, the failed CTAs' rows of dq (query rows 512..527) and of
+    dk / dv (keys 0..127) NaN, the rest normal."""
+    from specdec import _lib
+
+    lib = _lib.load()
+    q, k, v, do = _attn_inputs(5)
+    B, T, H, _ = q.shape
+    s = torch.cuda.current_stream().cuda_stream
+
+    def fwd(status):
+        o = torch.empty_like(q)
+        lse = torch.empty(B, H, T, device="cuda")
+        rc = lib.specdec_dflash_attention_forward(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                                                  lse.data_ptr(), B, T, H, 64, 512, 0.125, status.data_ptr(), s)
+        assert rc == _lib.OK, _lib.last_error()
+        return o, lse
+
+    def bwd(o, lse, status):
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        wsb = lib.specdec_dflash_attention_workspace_bytes(B, T, H)
+        ws = torch.empty(wsb, dtype=torch.uint8, device="cuda")
+        rc = lib.specdec_dflash_attention_backward(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                                                   lse.data_ptr(), do.data_ptr(), dq.data_ptr(), dk.data_ptr(),
+                                                   dv.data_ptr(), B, T, H, 64, 512, 0.125, status.data_ptr(),
+                                                   ws.data_ptr(), wsb, s)
+        assert rc == _lib.OK, _lib.last_error()
+        return dq, dk, dv
+
+    good = torch.zeros(1, dtype=torch.int32, device="cuda")
+    o_ref, lse_ref = fwd(good)
+    dq_ref, dk_ref, dv_ref = bwd(o_ref, lse_ref, good)
+    torch.cuda.synchronize()
+    assert int(good.item()) == 0
+    bad = torch.zeros(1, dtype=torch.int32, device="cuda")
+    try:
+        _lib.check(lib.specdec_test_withhold_stage(1), "specdec_test_withhold_stage")
+        o, lse = fwd(bad)
+    finally:
+        lib.specdec_test_withhold_stage(0)
+    torch.cuda.synchronize()
+    assert int(bad.item()) == 5
+    failed = torch.zeros(B, T, H, dtype=torch.bool, device="cuda")
+    failed[0, 512:, 0] = True
+    assert bool(torch.isnan(o.float())[failed].all()) and bool(torch.isnan(lse[0, 0, 512:]).all())
+    assert torch.equal(o[~failed], o_ref[~failed])
+    keep = torch.ones(B, H, T, dtype=torch.bool, device="cuda")
+    keep[0, 0, 512:] = False
+    assert torch.equal(lse[keep], lse_ref[keep])
+    # the backward, from the good forward's outputs
+    bad.zero_()
+    try:
+        _lib.check(lib.specdec_test_withhold_stage(1), "specdec_test_withhold_stage")
+        dq, dk, dv = bwd(o_ref, lse_ref, bad)
+    finally:
+        lib.specdec_test_withhold_stage(0)
+    torch.cuda.synchronize()
+    assert int(bad.item()) == 5
+    fq = torch.zeros(B, T, H, dtype=torch.bool, device="cuda")
+    fq[0, 512:, 0] = True
+    fk = torch.zeros(B, T, H, dtype=torch.bool, device="cuda")
+    fk[0, :128, 0] = True
+    assert bool(torch.isnan(dq.float())[fq].all()) and torch.equal(dq[~fq], dq_ref[~fq])
+    assert bool(torch.isnan(dk.float())[fk].all()) and torch.equal(dk[~fk], dk_ref[~fk])
+    assert bool(torch.isnan(dv.float())[fk].all()) and torch.equal(dv[~fk], dv_ref[~fk])
+    # the next calls are normal
+    again = torch.zeros(1, dtype=torch.int32, device="cuda")
+    o2, lse2 = fwd(again)
+    dq2, dk2, dv2 = bwd(o2, lse2, again)
+    torch.cuda.synchronize()
+    assert int(again.item()) == 0 and torch.equal(o2, o_ref) and torch.equal(dq2, dq_ref)
+
+
+def test_attention_expired_wait_is_raised_by_the_next_check(cuda):
+    """Through the drafter module: the sticky stream status word carries an
+    attention timeout to the next synchronising check (RuntimeError), which
+    clears it."""
+    from specdec import _lib, drafter, ops
+
+    lib = _lib.load()
+    q, k, v, _ = _attn_inputs(6)
+    ops.check_backward()  # clean start
+    try:
+        _lib.check(lib.specdec_test_withhold_stage(1), "specdec_test_withhold_stage")
+        with torch.no_grad():
+            o = drafter.dflash_attention(q, k, v, 512)
+    finally:
+        lib.specdec_test_withhold_stage(0)
+    with pytest.raises(RuntimeError, match="attention"):
+        ops.check_backward()
+    assert bool(torch.isnan(o[0, 512:, 0].float()).all())
+    ops.check_backward()  # cleared
+    with torch.no_grad():
+        o2 = drafter.dflash_attention(q, k, v, 512)
+    ops.check_backward()
+    assert not bool(torch.isnan(o2.float()).any())
