@@ -414,15 +414,16 @@ __global__ void __launch_bounds__(kThreads, kFCtas) dflash_attn_fwd_kernel(const
 
 
 // ---------------------------------------------------------------------------
-// Backward. Two kernels, no atomics (every accumulation runs in a fixed order
-// inside one CTA, so the gradients are bitwise repeatable):
-//   dq kernel, one CTA per (b, h, 128-query tile), thread = query row:
-//     delta = sum_d dO * O for its row (kept for the dkv kernel); per 64-key
-//     tile: S = Q K^T and dP = dO V^T (tcgen05, TMEM columns 0..63 /
+// Backward, no atomics (every accumulation runs in a fixed order inside one
+// CTA, so the gradients are bitwise repeatable). A small kernel first forms
+// delta = sum_d dO * O per query row; then one grid runs both roles, dq and
+// dk/dv tiles interleaved heaviest first, so their long tiles overlap:
+//   dq role, one CTA per (b, h, 128-query tile), thread = query row: per
+//     64-key tile: S = Q K^T and dP = dO V^T (tcgen05, TMEM columns 0..63 /
 //     64..127), p = e^(s * scale - lse), dS = p * (dP - delta) * scale to
 //     shared memory in bf16, dQ += dS K (K as an MN-major operand) in TMEM
 //     columns 128..191.
-//   dkv kernel, one CTA per (b, h, 128-key tile), thread = key row: per
+//   dk/dv role, one CTA per (b, h, 128-key tile), thread = key row: per
 //     64-query tile: S^T = K Q^T and dP^T = V dO^T, p^T and dS^T in bf16 to
 //     shared memory, dV += P^T dO and dK += dS^T Q (dO and Q as MN-major
 //     operands) in TMEM columns 128..191 / 192..255.
@@ -430,8 +431,8 @@ __global__ void __launch_bounds__(kThreads, kFCtas) dflash_attn_fwd_kernel(const
 // share TMEM lanes 32 (w % 4) .. 32 (w % 4) + 31 (one row each, thread t and
 // t + 128) and split a tile's 64 columns into halves: with the row's
 // log-sum-exp known, the halves are independent. Tiles arrive by cp.async one
-// step ahead: the dq kernel double-buffers K and refills V once dP has read
-// it; the dkv kernel double-buffers the query tile's Q, dO, lse and delta.
+// step ahead: the dq role double-buffers K and refills V once dP has read
+// it; the dk/dv role double-buffers the query tile's Q, dO, lse and delta.
 // ---------------------------------------------------------------------------
 
 constexpr int kBN = 64;            // keys per dq tile, queries per dkv tile
@@ -440,7 +441,7 @@ constexpr int kBCtas = 2;          // resident CTAs per SM
 constexpr uint32_t kBTmemCols = 256;
 constexpr uint32_t kColS = 0, kColDP = 64, kColAcc0 = 128, kColAcc1 = 192;
 
-// dq kernel shared memory (offsets from a 1024-byte-aligned base)
+// dq role shared memory (offsets from a 1024-byte-aligned base)
 constexpr uint32_t kQOffQ = 0;        // 128 rows x 128 B
 constexpr uint32_t kQOffG = 16384;    // dO, 128 rows
 constexpr uint32_t kQOffK0 = 32768;   // K, even tiles, 64 rows
@@ -450,7 +451,7 @@ constexpr uint32_t kQOffS = 57344;    // dS, 128 rows x 64 keys (one atom per ro
 constexpr uint32_t kQOffBar = 73728;
 constexpr uint32_t kBSmemBytes = kQOffBar + 32 + 1024;
 
-// dkv kernel shared memory
+// dk/dv role shared memory
 constexpr uint32_t kVOffK = 0;        // 128 rows
 constexpr uint32_t kVOffV = 16384;    // 128 rows
 constexpr uint32_t kVOffQ0 = 32768;   // query tile set 0: Q, 64 rows
@@ -491,11 +492,13 @@ __device__ __forceinline__ void cta_sync_tc() {
   tc_fence_after();
 }
 
-__global__ void __launch_bounds__(kBThreads, kBCtas) dflash_attn_bwd_dq_kernel(
-    const bf16_t* __restrict__ q, const bf16_t* __restrict__ k, const bf16_t* __restrict__ v,
-    const bf16_t* __restrict__ o, const float* __restrict__ lse, const bf16_t* __restrict__ dO,
-    bf16_t* __restrict__ dq, float* __restrict__ delta_out, int T, int H, int n_ctx, float scale, int* status,
-    int withhold) {
+// dq for query tile (n_tiles - 1 - rank): rank 0 is the heaviest (the last
+// query tile sees every key). `fail_first`: the failure-detection test hook.
+__device__ __forceinline__ void attn_bwd_dq(const bf16_t* __restrict__ q, const bf16_t* __restrict__ k,
+                                            const bf16_t* __restrict__ v, const float* __restrict__ lse,
+                                            const float* __restrict__ delta_in, const bf16_t* __restrict__ dO,
+                                            bf16_t* __restrict__ dq, int T, int H, int n_ctx, float scale,
+                                            int* status, int rank, bool fail_first) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   unsigned char* gbase = smem_raw + (base - smem_u32(smem_raw));
@@ -503,7 +506,7 @@ __global__ void __launch_bounds__(kBThreads, kBCtas) dflash_attn_bwd_dq_kernel(
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kQOffBar + 16);
   const int warp = threadIdx.x >> 5;
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
-  const int q0 = (gridDim.y - 1 - blockIdx.y) * kTM;  // heaviest query tiles first
+  const int q0 = ((T + kTM - 1) / kTM - 1 - rank) * kTM;
   const int64_t rs = (int64_t)H * kHD;
   const int64_t head = (int64_t)b * T * rs + (int64_t)h * kHD;
   const int r_in = threadIdx.x & (kTM - 1), half = threadIdx.x >> 7;
@@ -521,23 +524,10 @@ __global__ void __launch_bounds__(kBThreads, kBCtas) dflash_attn_bwd_dq_kernel(
   load_tile_async<kBThreads, kBN>(base + kQOffK0, k + head, rs, 0, T);
   load_tile_async<kBThreads, kBN>(base + kQOffV, v + head, rs, 0, T);
   cp_async_commit();
-  // delta = sum_d dO * O of this row (both threads of the row), and its lse in base 2
+  // this row's delta = sum_d dO * O (the delta kernel) and its lse in base 2
   float delta = 0.f, lse2 = 0.f;
   if (row < T) {
-    const bf16_t* orow = o + head + (int64_t)row * rs;
-    const bf16_t* grow = dO + head + (int64_t)row * rs;
-#pragma unroll
-    for (int c = 0; c < kHD / 8; ++c) {
-      const uint4 a = *reinterpret_cast<const uint4*>(orow + 8 * c);
-      const uint4 g = *reinterpret_cast<const uint4*>(grow + 8 * c);
-      const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, gw[4] = {g.x, g.y, g.z, g.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        delta = fmaf(bf16_lo(aw[i]), bf16_lo(gw[i]), delta);
-        delta = fmaf(bf16_hi(aw[i]), bf16_hi(gw[i]), delta);
-      }
-    }
-    if (half == 0) delta_out[((int64_t)b * H + h) * T + row] = delta;
+    delta = delta_in[((int64_t)b * H + h) * T + row];
     lse2 = lse[((int64_t)b * H + h) * T + row] * kLog2e;
   }
   cta_sync_tc();
@@ -557,8 +547,8 @@ __global__ void __launch_bounds__(kBThreads, kBCtas) dflash_attn_bwd_dq_kernel(
     // the other K buffer was last read by the previous tile's dQ product: fill it now
     if (more) load_tile_async<kBThreads, kBN>(base + knext, k + head, rs, k0 + kBN, T);
     cp_async_commit();
-    // failure-detection test hook: the grid's first CTA issues nothing for its first tile
-    if (threadIdx.x == 0 && !(withhold && k0 == 0 && blockIdx.x == 0 && blockIdx.y == 0)) {
+    // failure-detection test hook: this CTA issues nothing for its first tile
+    if (threadIdx.x == 0 && !(fail_first && k0 == 0)) {
 #pragma unroll
       for (int kk = 0; kk < kHD / 16; ++kk) {  // S = Q K^T, dP = dO V^T
         umma_bf16(tmem + kColS, smem_desc(base + kQOffQ + kk * 32, 16, 1024),
@@ -640,11 +630,12 @@ __global__ void __launch_bounds__(kBThreads, kBCtas) dflash_attn_bwd_dq_kernel(
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kBTmemCols) : "memory");
 }
 
-__global__ void __launch_bounds__(kBThreads, kBCtas) dflash_attn_bwd_dkv_kernel(
-    const bf16_t* __restrict__ q, const bf16_t* __restrict__ k, const bf16_t* __restrict__ v,
-    const float* __restrict__ lse, const float* __restrict__ delta, const bf16_t* __restrict__ dO,
-    bf16_t* __restrict__ dk, bf16_t* __restrict__ dv, int T, int H, int n_ctx, float scale, int* status,
-    int withhold) {
+// dk, dv for key tile kt (kt 0 is the heaviest: every query tile sees it).
+__device__ __forceinline__ void attn_bwd_dkv(const bf16_t* __restrict__ q, const bf16_t* __restrict__ k,
+                                             const bf16_t* __restrict__ v, const float* __restrict__ lse,
+                                             const float* __restrict__ delta, const bf16_t* __restrict__ dO,
+                                             bf16_t* __restrict__ dk, bf16_t* __restrict__ dv, int T, int H,
+                                             int n_ctx, float scale, int* status, int kt, bool fail_first) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   unsigned char* gbase = smem_raw + (base - smem_u32(smem_raw));
@@ -652,7 +643,7 @@ __global__ void __launch_bounds__(kBThreads, kBCtas) dflash_attn_bwd_dkv_kernel(
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kVOffBar + 16);
   const int warp = threadIdx.x >> 5;
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
-  const int k0 = blockIdx.y * kTM;  // the first key tiles are seen by the most query tiles: heaviest first
+  const int k0 = kt * kTM;
   const int64_t rs = (int64_t)H * kHD;
   const int64_t head = (int64_t)b * T * rs + (int64_t)h * kHD;
   const int64_t rowv = ((int64_t)b * H + h) * T;
@@ -704,8 +695,8 @@ __global__ void __launch_bounds__(kBThreads, kBCtas) dflash_attn_bwd_dkv_kernel(
     // the other set was last read by the previous tile's dV / dK products
     if (qt + 1 < qt_end) load_query_tile(qt + 1, set ^ 1);
     cp_async_commit();
-    // failure-detection test hook: the grid's first CTA issues nothing for its first tile
-    if (threadIdx.x == 0 && !(withhold && first && blockIdx.x == 0 && blockIdx.y == 0)) {
+    // failure-detection test hook: this CTA issues nothing for its first tile
+    if (threadIdx.x == 0 && !(fail_first && first)) {
 #pragma unroll
       for (int kk = 0; kk < kHD / 16; ++kk) {  // S^T = K Q^T, dP^T = V dO^T
         umma_bf16(tmem + kColS, smem_desc(base + kVOffK + kk * 32, 16, 1024),
@@ -806,6 +797,49 @@ __global__ void __launch_bounds__(kBThreads, kBCtas) dflash_attn_bwd_dkv_kernel(
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kBTmemCols) : "memory");
 }
 
+// delta[b, h, t] = sum_d dO * O of query row t (fp32, d in order): the
+// rows' term of dS, read by both backward roles. One thread per row.
+__global__ void __launch_bounds__(256) dflash_attn_delta_kernel(const bf16_t* __restrict__ o,
+                                                                const bf16_t* __restrict__ dO,
+                                                                float* __restrict__ delta, int B, int T, int H) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // over [B, T, H], the inputs' row order
+  if (i >= (int64_t)B * T * H) return;
+  const int h = (int)(i % H), t = (int)((i / H) % T), b = (int)(i / ((int64_t)H * T));
+  const bf16_t* orow = o + i * kHD;
+  const bf16_t* grow = dO + i * kHD;
+  float d = 0.f;
+#pragma unroll
+  for (int c = 0; c < kHD / 8; ++c) {
+    const uint4 a = *reinterpret_cast<const uint4*>(orow + 8 * c);
+    const uint4 g = *reinterpret_cast<const uint4*>(grow + 8 * c);
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, gw[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      d = fmaf(bf16_lo(aw[j]), bf16_lo(gw[j]), d);
+      d = fmaf(bf16_hi(aw[j]), bf16_hi(gw[j]), d);
+    }
+  }
+  delta[((int64_t)b * H + h) * T + t] = d;
+}
+
+// Both backward roles in one grid: blockIdx.y even = dq for the query tile of
+// rank y / 2, odd = dk / dv for key tile y / 2. Blocks are dispatched in index
+// order and both roles run their heaviest tiles at rank 0, so the two roles'
+// long tiles start first and their critical paths overlap.
+__global__ void __launch_bounds__(kBThreads, kBCtas) dflash_attn_bwd_kernel(
+    const bf16_t* __restrict__ q, const bf16_t* __restrict__ k, const bf16_t* __restrict__ v,
+    const float* __restrict__ lse, const float* __restrict__ delta, const bf16_t* __restrict__ dO,
+    bf16_t* __restrict__ dq, bf16_t* __restrict__ dk, bf16_t* __restrict__ dv, int T, int H, int n_ctx,
+    float scale, int* status, int withhold) {
+  const int idx = (int)(blockIdx.y >> 1);
+  // failure-detection test hook: both roles' first CTA of (batch 0, head 0)
+  const bool fail_first = withhold && blockIdx.x == 0 && idx == 0;
+  if ((blockIdx.y & 1) == 0)
+    attn_bwd_dq(q, k, v, lse, delta, dO, dq, T, H, n_ctx, scale, status, idx, fail_first);
+  else
+    attn_bwd_dkv(q, k, v, lse, delta, dO, dk, dv, T, H, n_ctx, scale, status, idx, fail_first);
+}
+
 }  // namespace
 
 // Raises the kernel's dynamic shared-memory limit once per device.
@@ -841,24 +875,22 @@ cudaError_t dflash_attn_bwd_launch(const void* q, const void* k, const void* v, 
   if (e != cudaSuccess) return e;
   const unsigned long long bit = 1ull << (dev & 63);
   if (!(done.load() & bit)) {
-    e = cudaFuncSetAttribute(dflash_attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBSmemBytes);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(dflash_attn_bwd_dkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)kBSmemBytesKV);
+    // the grid's CTAs take the larger of the two roles' shared memory
+    e = cudaFuncSetAttribute(dflash_attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(kBSmemBytesKV > kBSmemBytes ? kBSmemBytesKV : kBSmemBytes));
     if (e != cudaSuccess) return e;
     done.fetch_or(bit);
   }
-  const dim3 grid((unsigned)(batch * H), (unsigned)((T + kTM - 1) / kTM));
-  dflash_attn_bwd_dq_kernel<<<grid, kBThreads, kBSmemBytes, st>>>(
-      static_cast<const bf16_t*>(q), static_cast<const bf16_t*>(k), static_cast<const bf16_t*>(v),
-      static_cast<const bf16_t*>(o), lse, static_cast<const bf16_t*>(dO), static_cast<bf16_t*>(dq), delta, T, H,
-      n_ctx, scale, status, withhold);
+  const int64_t rows = (int64_t)batch * T * H;
+  dflash_attn_delta_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, st>>>(
+      static_cast<const bf16_t*>(o), static_cast<const bf16_t*>(dO), delta, batch, T, H);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  dflash_attn_bwd_dkv_kernel<<<grid, kBThreads, kBSmemBytesKV, st>>>(
+  const dim3 grid((unsigned)(batch * H), (unsigned)(2 * ((T + kTM - 1) / kTM)));
+  dflash_attn_bwd_kernel<<<grid, kBThreads, (kBSmemBytesKV > kBSmemBytes ? kBSmemBytesKV : kBSmemBytes), st>>>(
       static_cast<const bf16_t*>(q), static_cast<const bf16_t*>(k), static_cast<const bf16_t*>(v), lse, delta,
-      static_cast<const bf16_t*>(dO), static_cast<bf16_t*>(dk), static_cast<bf16_t*>(dv), T, H, n_ctx, scale,
-      status, withhold);
+      static_cast<const bf16_t*>(dO), static_cast<bf16_t*>(dq), static_cast<bf16_t*>(dk), static_cast<bf16_t*>(dv),
+      T, H, n_ctx, scale, status, withhold);
   return cudaGetLastError();
 }
 
