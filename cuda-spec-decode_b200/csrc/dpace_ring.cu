@@ -55,10 +55,24 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
   q.retired = a.q_retired;
   q.nblocks = (unsigned)((E + BL - 1) / BL);
   q.dynamic = a.q_dynamic;
-  // the producer's first block, dequeued before the prologue so that the
-  // atomic's latency overlaps it
-  const unsigned first = (warp == NC && lane == 0) ? q.first() : 0u;
+  // the producer's first block is its own index; with SPECDEC_EARLY_FIRST_STAGE
+  // the producer lane initialises the ring and posts that block's first stage
+  // before the liveness table is built, so the copy's latency overlaps the
+  // table's loads
+  const unsigned first = q.first();
+  const bool withhold = a.withhold_stage && blockIdx.x == 0;
+#if SPECDEC_EARLY_FIRST_STAGE
+  ring_init(sm, NC, NC * 32);
+  bool posted = false;
+  if (warp == NC && lane == 0) {
+    const T* src0[1] = {X};
+    posted = ring_post_first<1, S, SE, BS>(src0, E, V, q, sm.ring, sm.full, sm.sf0, sm.srow, first, withhold,
+                                           static_cast<RingTrack<S>*>(nullptr));
+  }
+#else
   ring_init(sm, NC);
+  const bool posted = false;
+#endif
   const RowBits rb = build_row_bits(sm.bits, R, NC + 1, [&](int64_t r) {
     return a.mask == nullptr || a.mask[r] > 0.f;
   });
@@ -68,7 +82,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
     if (lane == 0) {
       const T* src[1] = {X};
       if (!ring_produce<1, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow, first,
-                                      a.withhold_stage && blockIdx.x == 0)) {
+                                      withhold, static_cast<RingTrack<S>*>(nullptr), posted)) {
         atomicOr(a.flag, 2);
         if (a.status) a.status[0] = kStatusTimeout;
       }
@@ -292,8 +306,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
   q.retired = a.q_retired;
   q.nblocks = (unsigned)((E + BL - 1) / BL);
   q.dynamic = a.q_dynamic;
-  // the producer's first block, dequeued before the prologue so that the
-  // atomic's latency overlaps it
+  // the producer's first block: its own index (no atomic)
   const unsigned first = (warp == NC && lane == 0) ? q.first() : 0u;
   ring_init(sm, NC);
   // Rows to read: those with a nonzero scale * dloss -- or, when chained

@@ -38,9 +38,11 @@ struct BlockQueue {
   unsigned nblocks;
   int dynamic;  // 0: block = blockIdx.x + k * gridDim.x (static interleave)
 
-  __device__ __forceinline__ unsigned first() const { return dynamic ? atomicAdd(ctr, 1u) : blockIdx.x; }
+  // Every CTA's first block is its own index (no atomic on the way to the
+  // first copy); the dynamic queue hands out the rest, from gridDim.x on.
+  __device__ __forceinline__ unsigned first() const { return blockIdx.x; }
   __device__ __forceinline__ unsigned next(unsigned cur) const {
-    return dynamic ? atomicAdd(ctr, 1u) : cur + gridDim.x;
+    return dynamic ? gridDim.x + atomicAdd(ctr, 1u) : cur + gridDim.x;
   }
   // Called once per CTA, after its last dequeue; true for the last CTA, which
   // has seen every earlier CTA's writes that preceded their retire.
@@ -145,16 +147,53 @@ __device__ __forceinline__ int64_t copied_end(int64_t f0, int64_t f1) {
 // stage: this CTA's consumers then see their bounded wait expire, which is
 // the path under test. `trk` (or null) receives the progress record. The
 // caller retires the CTA from the queue afterwards.
+// 1: the forwards' producers post their first stage before the liveness table
+// is built (ring_post_first); 0: after it, like the backwards.
+#ifndef SPECDEC_EARLY_FIRST_STAGE
+#define SPECDEC_EARLY_FIRST_STAGE 1
+#endif
+
+// The producer's first stage, posted before the CTA's liveness table exists
+// (called by the producer lane right after it initialised the barriers): the
+// first stage of block `first` is copied whatever its rows' liveness -- the
+// consumers skip a dead row's stage by the table, so a dead copy costs only
+// its bytes -- and the copy's latency overlaps the table's loads. Returns
+// false (nothing posted; ring_produce starts from the beginning) when the
+// block is past the end, is a single stage, or the test hook withholds it.
+template <int NIN, int S, int SE, int BS, class T>
+__device__ bool ring_post_first(const T* const* src, int64_t E, int64_t V, const BlockQueue& q, T* ring,
+                                uint64_t* full, int64_t* sf0, int64_t* srow, unsigned first, bool withhold_first,
+                                RingTrack<S>* trk) {
+  constexpr int64_t BL = (int64_t)BS * SE;
+  if (withhold_first || first >= q.nblocks) return false;
+  const int64_t blk_end = min((int64_t)(first + 1) * BL, E);
+  const int64_t f0 = (int64_t)first * BL;
+  const int64_t f1 = min(f0 + SE, blk_end);
+  if (f1 == blk_end) return false;
+  if (trk) trk->sblk[0] = first;
+  sf0[0] = f0;
+  srow[0] = f0 / V;
+  const uint32_t vbytes = (uint32_t)(((f1 - f0) * (int64_t)sizeof(T)) & ~int64_t(15));
+  if (vbytes) {
+    mbar_arrive_expect_tx(full, vbytes * NIN);
+#pragma unroll
+    for (int i = 0; i < NIN; ++i) bulk_g2s(ring + (size_t)i * S * SE, src[i] + f0, vbytes, full);
+  } else {
+    mbar_arrive(full);
+  }
+  return true;
+}
+
 template <int NIN, int S, int SE, int BS, class T>
 __device__ bool ring_produce(const T* const* src, int64_t E, int64_t V, const RowBits& rb,
                              const BlockQueue& q, T* ring, uint64_t* full, uint64_t* empty,
                              int64_t* sf0, int64_t* srow, unsigned first, bool withhold_first = false,
-                             RingTrack<S>* trk = nullptr) {
+                             RingTrack<S>* trk = nullptr, bool first_posted = false) {
   constexpr int64_t BL = (int64_t)BS * SE;
   unsigned b = first, nb = q.nblocks;
   bool have_nb = false, switch_pending = false;
   int64_t blk_end = 0, r_issue = 0;
-  int k = 0;
+  int k = first_posted ? 1 : 0;  // ring_post_first already posted stage 0 of block `first`
   auto enter_block = [&]() {
     if (b < q.nblocks) {
       blk_end = min((int64_t)(b + 1) * BL, E);
@@ -163,7 +202,7 @@ __device__ bool ring_produce(const T* const* src, int64_t E, int64_t V, const Ro
   };
   enter_block();
   bool ok = true;
-  int64_t it = 0;
+  int64_t it = first_posted ? 1 : 0;
   for (;; ++it) {
     const int slot = (int)(it % S);
     if (!mbar_wait(empty + slot, (uint32_t)(((it / S) & 1) ^ 1))) {
@@ -249,8 +288,8 @@ constexpr int ring_min_ctas() {
 }
 
 template <int NIN, int S, int SE, class T>
-__device__ __forceinline__ void ring_init(RingSmem<NIN, S, SE, T>& sm, int consumers) {
-  if (threadIdx.x == 0) {
+__device__ __forceinline__ void ring_init(RingSmem<NIN, S, SE, T>& sm, int consumers, int init_thread = 0) {
+  if ((int)threadIdx.x == init_thread) {
     for (int i = 0; i < S; ++i) {
       mbar_init(sm.full + i, 1);
       mbar_init(sm.empty + i, consumers);
