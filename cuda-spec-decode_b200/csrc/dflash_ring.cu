@@ -80,8 +80,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 2, S, SE, T>
   bool posted = false;
   if (warp == NC && lane == 0) {
     const T* src0[2] = {XL, XT};
-    posted = ring_post_first<2, S, SE, BS>(src0, E, V, q, sm.ring, sm.full, sm.sf0, sm.srow, first, withhold,
-                                           static_cast<RingTrack<S>*>(nullptr));
+    posted = ring_post_first<2, S, SE>(src0, make_block_map(E, BL, SE, -1), V, q, sm.ring, sm.full, sm.sf0,
+                                       sm.srow, first, withhold, static_cast<RingTrack<S>*>(nullptr));
   }
 #else
   ring_init(sm, NC);
@@ -93,8 +93,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 2, S, SE, T>
   if (warp == NC) {  // producer
     if (lane == 0) {
       const T* src[2] = {XL, XT};
-      if (!ring_produce<2, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow, first,
-                                      withhold, static_cast<RingTrack<S>*>(nullptr), posted))
+      if (!ring_produce<2, S, SE>(src, make_block_map(E, BL, SE, -1), V, rb, q, sm.ring, sm.full, sm.empty,
+                                  sm.sf0, sm.srow, first, withhold, static_cast<RingTrack<S>*>(nullptr), posted))
         atomicOr(a.flag, 2);
       q.retire();
     }
@@ -322,8 +322,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, (KIND == kKi
   if (warp == NC) {
     if (lane == 0) {
       const T* src[2] = {XL, XT};
-      if (!ring_produce<NIN, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow, first,
-                                        a.withhold_stage && blockIdx.x == 0, &sm.trk))
+      if (!ring_produce<NIN, S, SE>(src, make_block_map(E, BL, SE, -1), V, rb, q, sm.ring, sm.full, sm.empty,
+                                    sm.sf0, sm.srow, first, a.withhold_stage && blockIdx.x == 0, &sm.trk))
         sm.trk.timeout = 1;
     }
   } else {

@@ -4,10 +4,12 @@
 // kept for inputs whose base address is not 16-byte aligned).
 //
 // Forward = two launches on the stream:
-//   1. dpace_fwd_ring_kernel streams the logits once. Each consumer warp keeps
-//      an online (max, sum of e^(x - max)) for the row it is in and, whenever
-//      a (row, block) piece ends, stores it to
-//      part[((r * pmax + block_in_row) * NC) + warp]. Plain stores only, no
+//   1. dpace_fwd_ring_kernel streams the logits once, in queue blocks of
+//      BS stages and, over the last SPECDEC_FWD_TAIL_BLOCKS blocks' worth of
+//      elements, of one stage (BlockMap). Each consumer warp keeps an online
+//      (max, sum of e^(x - max)) for the row it is in and, whenever a
+//      (row, block) piece ends, stores it to part[(block + r) * NC + warp]
+//      (row r's slots start at index(r V) + r). Plain stores only, no
 //      counters, no global loads in the consumers.
 //   2. dpace_finalize_kernel (chained with programmatic dependent launch): one
 //      CTA per sequence, warp j <-> row j merges the row's partials in slot
@@ -40,7 +42,6 @@ template <class T, int NC, int S, int SE, int BS>
 __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>())) dpace_fwd_ring_kernel(const __grid_constant__ DpaceFwdArgs a) {
   constexpr int kSub = SE / NC;
   constexpr int64_t BL = (int64_t)BS * SE;
-  constexpr int kLogBL = __builtin_ctzll(BL);
   static_assert(kSub % (32 * (16 / sizeof(T))) == 0, "sub-range must be whole 16-byte rounds of a warp");
   static_assert((BL & (BL - 1)) == 0, "block length must be a power of two");
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -48,12 +49,13 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
   const T* X = static_cast<const T*>(a.logits);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t E = a.pt.E, V = a.pt.V, R = E / V;
-  const int pmax = a.pt.pmax;
+  // blocks of BL elements, then one-stage blocks from a.pt.split on
+  const BlockMap bm = make_block_map(E, BL, SE, a.pt.split);
 
   BlockQueue q;
   q.ctr = a.q_ctr;
   q.retired = a.q_retired;
-  q.nblocks = (unsigned)((E + BL - 1) / BL);
+  q.nblocks = bm.nblocks;
   q.dynamic = a.q_dynamic;
   // the producer's first block is its own index; with SPECDEC_EARLY_FIRST_STAGE
   // the producer lane initialises the ring and posts that block's first stage
@@ -66,8 +68,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
   bool posted = false;
   if (warp == NC && lane == 0) {
     const T* src0[1] = {X};
-    posted = ring_post_first<1, S, SE, BS>(src0, E, V, q, sm.ring, sm.full, sm.sf0, sm.srow, first, withhold,
-                                           static_cast<RingTrack<S>*>(nullptr));
+    posted = ring_post_first<1, S, SE>(src0, bm, V, q, sm.ring, sm.full, sm.sf0, sm.srow, first, withhold,
+                                       static_cast<RingTrack<S>*>(nullptr));
   }
 #else
   ring_init(sm, NC);
@@ -81,8 +83,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
   if (warp == NC) {  // producer
     if (lane == 0) {
       const T* src[1] = {X};
-      if (!ring_produce<1, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow, first,
-                                      withhold, static_cast<RingTrack<S>*>(nullptr), posted)) {
+      if (!ring_produce<1, S, SE>(src, bm, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow, first,
+                                  withhold, static_cast<RingTrack<S>*>(nullptr), posted)) {
         atomicOr(a.flag, 2);
         if (a.status) a.status[0] = kStatusTimeout;
       }
@@ -103,8 +105,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
     if (live) {
       warp_lse(m, s);
       if (lane == 0) {
-        const int64_t slot = blk - (r * V) / BL;
-        a.part[(r * pmax + slot) * NC + warp] = make_float2(m, s);
+        a.part[(blk + r) * NC + warp] = make_float2(m, s);  // row r's slot blk - index(r V)
       }
     }
     m = kNegSeed;
@@ -122,8 +123,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
     }
     const int64_t f0 = sm.sf0[slot];
     if (f0 < 0) break;
-    const int64_t b = f0 >> kLogBL;
-    const int64_t blk_end = min((b + 1) * BL, E);
+    const int64_t b = bm.index(f0);
+    const int64_t blk_end = bm.end((unsigned)b);
     const int64_t f1 = min(f0 + SE, blk_end);
     if (b != blk) {  // first stage of a new block
       blk = b;
@@ -185,8 +186,9 @@ __global__ void __launch_bounds__(1024) dpace_finalize_kernel(const __grid_const
   pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int B = a.B;
-  const int64_t n = blockIdx.x, V = a.pt.V, BL = a.pt.chunk;
+  const int64_t n = blockIdx.x, V = a.pt.V;
   const int NC = a.nc;
+  const BlockMap bm = make_block_map(a.pt.E, a.pt.chunk, a.pt.stage, a.pt.split);
   bool timed_out;
   {
     const int64_t r = n * B + warp;
@@ -199,17 +201,22 @@ __global__ void __launch_bounds__(1024) dpace_finalize_kernel(const __grid_const
     // a wait of the streaming grid expired: partials may be missing, so every
     // per-row output is NaN (a backward from them gives a NaN gradient)
     timed_out = (*reinterpret_cast<volatile int*>(a.flag) & 2) != 0;
-    const int k = blocks_in_row(r, V, BL) * NC;
-    const float2* part = a.part + r * a.pt.pmax * NC;
-    float2 pv[2];
-    pv[0] = lane < k ? part[lane] : make_float2(kNegSeed, 0.f);
-    pv[1] = lane + 32 < k ? part[lane + 32] : make_float2(kNegSeed, 0.f);
+    const int k = bm.pieces(r, V) * NC;
+    const float2* part = a.part + (bm.index(r * V) + r) * NC;
+    // up to 8 partials per lane are loaded before the first merge (rows in
+    // the one-stage blocks at the end have up to ceil(V / stage) + 1 slots);
+    // merging an absent one (kNegSeed, 0) leaves (m, s) bit for bit unchanged
+    constexpr int kPre = 8;
+    float2 pv[kPre];
+#pragma unroll
+    for (int i = 0; i < kPre; ++i) pv[i] = lane + 32 * i < k ? part[lane + 32 * i] : make_float2(kNegSeed, 0.f);
     const bool live = mk > 0.f;
     float lse = 0.f, ce = 0.f;
     if (live) {
       float m = pv[0].x, s = pv[0].y;  // slot-major, warp-minor, then a fixed butterfly
-      lse_merge(m, s, pv[1].x, pv[1].y);
-      for (int qd = lane + 64; qd < k; qd += 32) {
+#pragma unroll
+      for (int i = 1; i < kPre; ++i) lse_merge(m, s, pv[i].x, pv[i].y);
+      for (int qd = lane + 32 * kPre; qd < k; qd += 32) {
         const float2 v = part[qd];
         lse_merge(m, s, v.x, v.y);
       }
@@ -323,8 +330,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
   if (warp == NC) {
     if (lane == 0) {
       const T* src[1] = {X};
-      if (!ring_produce<1, S, SE, BS>(src, E, V, rb, q, sm.ring, sm.full, sm.empty, sm.sf0, sm.srow, first,
-                                      a.withhold_stage && blockIdx.x == 0, &sm.trk))
+      if (!ring_produce<1, S, SE>(src, make_block_map(E, BL, SE, -1), V, rb, q, sm.ring, sm.full, sm.empty,
+                                  sm.sf0, sm.srow, first, a.withhold_stage && blockIdx.x == 0, &sm.trk))
         sm.trk.timeout = 1;
     }
   } else {
@@ -468,6 +475,15 @@ constexpr int kBwdBlockStages = SPECDEC_BWD_BLOCK_STAGES;
 #define SPECDEC_FWD_BLOCK_STAGES 4
 #endif
 constexpr int kFwdBlockStages = SPECDEC_FWD_BLOCK_STAGES;
+// The D-PACE forward's last SPECDEC_FWD_TAIL_BLOCKS blocks' worth of elements
+// are queued as one-stage blocks (BlockMap), so the launch's CTAs finish within
+// about a stage of one another; 0: every block is kFwdBlockStages long. A
+// constant, not a multiple of the grid: the block boundaries, and so the
+// results, do not depend on the CTA count.
+#ifndef SPECDEC_FWD_TAIL_BLOCKS
+#define SPECDEC_FWD_TAIL_BLOCKS 256
+#endif
+constexpr int64_t kFwdTailBlocks = SPECDEC_FWD_TAIL_BLOCKS;
 
 template <class T, int NC, int S, int SE, int BS>
 struct RingVariant {
@@ -532,6 +548,13 @@ struct Shapes {
       default: return 4096 * kFwdBlockStages * k;
     }
   }
+  static int stage_elems(int shape) {
+    switch (shape) {
+      case 1: return 8192 * k;
+      case 4: return 2048 * k;
+      default: return 4096 * k;
+    }
+  }
   static int fwd_ctas(int shape, int device, int cap) {
     switch (shape) {
       case 1: return R1::fwd_ctas(device, cap);
@@ -582,6 +605,16 @@ struct Shapes {
 
 int dpace_ring_block_elems(int dtype, int shape) {
   return dtype == kDtypeBF16 ? Shapes<bf16_t>::block_elems(shape) : Shapes<float>::block_elems(shape);
+}
+
+int dpace_ring_stage_elems(int dtype, int shape) {
+  return dtype == kDtypeBF16 ? Shapes<bf16_t>::stage_elems(shape) : Shapes<float>::stage_elems(shape);
+}
+
+int64_t dpace_fwd_split(int64_t E, int64_t BL) {
+  if (kFwdTailBlocks <= 0 || E <= 0) return -1;
+  const int64_t nb = (E + BL - 1) / BL;
+  return (nb > kFwdTailBlocks ? nb - kFwdTailBlocks : 0) * BL;
 }
 
 int dpace_ring_consumers(int shape) {

@@ -160,14 +160,13 @@ __device__ __forceinline__ int64_t copied_end(int64_t f0, int64_t f1) {
 // its bytes -- and the copy's latency overlaps the table's loads. Returns
 // false (nothing posted; ring_produce starts from the beginning) when the
 // block is past the end, is a single stage, or the test hook withholds it.
-template <int NIN, int S, int SE, int BS, class T>
-__device__ bool ring_post_first(const T* const* src, int64_t E, int64_t V, const BlockQueue& q, T* ring,
+template <int NIN, int S, int SE, class T>
+__device__ bool ring_post_first(const T* const* src, const BlockMap& bm, int64_t V, const BlockQueue& q, T* ring,
                                 uint64_t* full, int64_t* sf0, int64_t* srow, unsigned first, bool withhold_first,
                                 RingTrack<S>* trk) {
-  constexpr int64_t BL = (int64_t)BS * SE;
   if (withhold_first || first >= q.nblocks) return false;
-  const int64_t blk_end = min((int64_t)(first + 1) * BL, E);
-  const int64_t f0 = (int64_t)first * BL;
+  const int64_t blk_end = bm.end(first);
+  const int64_t f0 = bm.start(first);
   const int64_t f1 = min(f0 + SE, blk_end);
   if (f1 == blk_end) return false;
   if (trk) trk->sblk[0] = first;
@@ -184,20 +183,20 @@ __device__ bool ring_post_first(const T* const* src, int64_t E, int64_t V, const
   return true;
 }
 
-template <int NIN, int S, int SE, int BS, class T>
-__device__ bool ring_produce(const T* const* src, int64_t E, int64_t V, const RowBits& rb,
+template <int NIN, int S, int SE, class T>
+__device__ bool ring_produce(const T* const* src, const BlockMap& bm, int64_t V, const RowBits& rb,
                              const BlockQueue& q, T* ring, uint64_t* full, uint64_t* empty,
                              int64_t* sf0, int64_t* srow, unsigned first, bool withhold_first = false,
                              RingTrack<S>* trk = nullptr, bool first_posted = false) {
-  constexpr int64_t BL = (int64_t)BS * SE;
   unsigned b = first, nb = q.nblocks;
   bool have_nb = false, switch_pending = false;
-  int64_t blk_end = 0, r_issue = 0;
+  int64_t blk_start = 0, blk_end = 0, r_issue = 0;
   int k = first_posted ? 1 : 0;  // ring_post_first already posted stage 0 of block `first`
   auto enter_block = [&]() {
     if (b < q.nblocks) {
-      blk_end = min((int64_t)(b + 1) * BL, E);
-      r_issue = ((int64_t)b * BL) / V;
+      blk_start = bm.start(b);
+      blk_end = bm.end(b);
+      r_issue = blk_start / V;
     }
   };
   enter_block();
@@ -224,7 +223,7 @@ __device__ bool ring_produce(const T* const* src, int64_t E, int64_t V, const Ro
       ++it;
       break;
     }
-    const int64_t f0 = (int64_t)b * BL + (int64_t)k * SE;
+    const int64_t f0 = blk_start + (int64_t)k * SE;
     const int64_t f1 = min(f0 + SE, blk_end);
     if (f1 == blk_end) {  // the block's last stage: dequeue the next block now
       nb = q.next(b);

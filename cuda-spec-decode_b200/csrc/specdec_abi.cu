@@ -155,7 +155,7 @@ DpaceLayout dpace_layout(int64_t N, int64_t B, const Partition& pt, int nc) {
   DpaceLayout L;
   const size_t R = size_t(N) * size_t(B);
   L.part = 0;
-  L.xtgt = align256(L.part + R * size_t(pt.pmax) * size_t(nc) * sizeof(float2));
+  L.xtgt = align256(L.part + size_t(pt.nslots) * size_t(nc) * sizeof(float2));
   L.seq_loss = align256(L.xtgt + R * sizeof(float));
   L.scratch = align256(L.seq_loss + size_t(N) * sizeof(float));
   L.counters = dpace_counter_bytes(N, B);
@@ -170,6 +170,20 @@ Partition ring_partition(int64_t rows, int64_t V, int64_t block_elems, int ctas)
   p.chunk = block_elems;
   p.grid = ctas;
   p.pmax = int((V - 1) / block_elems + 2);
+  p.nslots = rows * p.pmax;
+  return p;
+}
+
+// D-PACE ring forward: one-stage queue blocks at the end of the launch
+// (BlockMap) and the compact partial table -- row r's slot s at
+// index(r V) + r + s, blocks + rows slots in all.
+Partition dpace_ring_fwd_partition(int64_t rows, int64_t V, int dtype, int shape, int ctas) {
+  Partition p = ring_partition(rows, V, dpace_ring_block_elems(dtype, shape), ctas);
+  p.stage = dpace_ring_stage_elems(dtype, shape);
+  p.split = dpace_fwd_split(p.E, p.chunk);
+  const BlockMap bm = make_block_map(p.E, p.chunk, p.stage, p.split);
+  if (bm.split < p.E) p.pmax = int((V - 1) / p.stage + 2);
+  p.nslots = (int64_t)bm.nblocks + rows;
   return p;
 }
 
@@ -191,14 +205,12 @@ DflashLayout dflash_layout(int64_t N, int64_t B, const Partition& pt, int nc) {
   return L;
 }
 
-// A bf16 block holds twice the elements of the float block of the same shape,
-// so its partition has no more pieces per row: the float workspace sizes
-// bound the bf16 ones.
+// A bf16 block (and stage) holds twice the elements of the float one of the
+// same shape, so its partition has no more pieces per row.
 Partition dpace_fwd_partition(int64_t N, int32_t B, int64_t V, bool tma, int device, int dtype = kDtypeF32) {
   const int units = kernel_units(SPECDEC_KERNEL_DPACE_FWD, 0, tma, device, dtype);
   if (tma || dtype == kDtypeBF16)
-    return ring_partition(N * B, V, dpace_ring_block_elems(dtype, ring_shape(SPECDEC_KERNEL_DPACE_FWD, dtype)),
-                          units);
+    return dpace_ring_fwd_partition(N * B, V, dtype, ring_shape(SPECDEC_KERNEL_DPACE_FWD, dtype), units);
   return make_partition(N * B, V, units, kMinChunk);
 }
 

@@ -244,12 +244,72 @@ struct Partition {
   int64_t chunk = 0;  // elements per CTA, a multiple of 4
   int64_t grid = 0;   // number of CTAs
   int pmax = 0;       // upper bound on the number of CTAs that touch one row
+  // ring kernels: elements per stage, and the start of the one-stage queue
+  // blocks at the end of the launch (-1: none; see BlockMap)
+  int64_t stage = 0;
+  int64_t split = -1;
+  // partial slots per consumer warp in the workspace: rows * pmax, or for
+  // the D-PACE ring forward blocks + rows (row r's slot s at index(r V) + r + s)
+  int64_t nslots = 0;
 
   __host__ __device__ __forceinline__ int64_t first_cta(int64_t r) const { return (r * V) / chunk; }
   __host__ __device__ __forceinline__ int pieces(int64_t r) const {
     return int(((r + 1) * V - 1) / chunk - (r * V) / chunk + 1);
   }
 };
+
+// Queue geometry: blocks of BL = BS * SE elements below `split`, blocks of one
+// stage (SE elements) from `split` to E. The D-PACE forward sets `split` so
+// that its launch ends on short blocks: CTAs then finish within about a stage
+// of one another instead of a whole block. `split` is a multiple of BL fixed
+// by the problem size alone, never by the grid, so the partial slots -- and
+// the results -- do not depend on the CTA count or the queue's schedule.
+// Without short blocks split = ceil(E / BL) * BL. BL and SE are powers of two.
+struct BlockMap {
+  int64_t E = 0, split = 0;
+  int lbl = 0, lse = 0;  // log2 of BL and SE
+  unsigned nmain = 0, nblocks = 0;
+
+  __host__ __device__ __forceinline__ int64_t start(unsigned b) const {
+    return b < nmain ? (int64_t)b << lbl : split + ((int64_t)(b - nmain) << lse);
+  }
+  __host__ __device__ __forceinline__ int64_t end(unsigned b) const {
+    const int64_t e = b < nmain ? (int64_t)(b + 1) << lbl : split + ((int64_t)(b - nmain + 1) << lse);
+    return e < E ? e : E;
+  }
+  // the block containing element e (0 <= e < E)
+  __host__ __device__ __forceinline__ int64_t index(int64_t e) const {
+    return e < split ? e >> lbl : (int64_t)nmain + ((e - split) >> lse);
+  }
+  // blocks overlapping row r (= partial slots of the row)
+  __host__ __device__ __forceinline__ int pieces(int64_t r, int64_t V) const {
+    return (int)(index((r + 1) * V - 1) - index(r * V) + 1);
+  }
+};
+
+__host__ __device__ __forceinline__ int ilog2_pow2(int64_t x) {
+  int l = 0;
+  while ((int64_t(1) << l) < x) ++l;
+  return l;
+}
+
+// split: a multiple of BL (<= E rounded up to BL), or negative for none.
+__host__ __device__ __forceinline__ BlockMap make_block_map(int64_t E, int64_t BL, int64_t SE, int64_t split) {
+  BlockMap m;
+  m.E = E;
+  m.lbl = ilog2_pow2(BL);
+  m.lse = ilog2_pow2(SE);
+  const int64_t nb = (E + BL - 1) / BL;
+  if (split < 0 || split >= E) {
+    m.split = nb * BL;
+    m.nmain = m.nblocks = (unsigned)nb;
+  } else {
+    m.split = split;
+    m.nmain = (unsigned)(split / BL);
+    m.nblocks = m.nmain + (unsigned)((E - split + SE - 1) / SE);
+  }
+  return m;
+}
 
 inline Partition make_partition(int64_t rows, int64_t V, int64_t ctas, int64_t min_chunk) {
   Partition p;
@@ -263,6 +323,7 @@ inline Partition make_partition(int64_t rows, int64_t V, int64_t ctas, int64_t m
   p.chunk = c;
   p.grid = (p.E + c - 1) / c;
   p.pmax = int((V - 1) / c + 2);
+  p.nslots = rows * p.pmax;
   return p;
 }
 

@@ -154,6 +154,10 @@ cudaError_t dpace_bwd_launch(int shape, const DpaceBwdArgs& a, cudaStream_t st);
 // kDtypeF32 or kDtypeBF16; a bf16 shape moves the same bytes per stage as the
 // float shape of the same number (twice the elements).
 int dpace_ring_block_elems(int dtype, int shape);
+int dpace_ring_stage_elems(int dtype, int shape);
+// start of the D-PACE forward's one-stage queue blocks for E elements in
+// blocks of BL (-1: none)
+int64_t dpace_fwd_split(int64_t E, int64_t BL);
 int dpace_ring_consumers(int shape);
 int dpace_fwd_ring_ctas(int dtype, int shape, int device, int cap_per_sm);
 int dpace_bwd_ring_ctas(int dtype, int shape, int device, int cap_per_sm);

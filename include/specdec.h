@@ -165,7 +165,8 @@ int specdec_scale_inplace_bf16(uint16_t* x, int64_t n, const float* factor, void
  * until exit): 64 KiB of counters and 4 MiB - 64 KiB of scratch. A problem
  * fits when specdec_dpace_counter_bytes(N, B) <= 64 KiB (N <= 16376) and
  * specdec_dpace_scratch_bytes(N, B, V, device) <= 4 MiB - 64 KiB -- at
- * V = 128256 about 14000 rows of N*B (292 bytes of scratch per row). Larger problems
+ * V = 128256 about 14000 rows of N*B (about 287 bytes of scratch per row
+ * plus 24 KiB for the forward's short final queue blocks). Larger problems
  * return SPECDEC_ERR_WORKSPACE before any launch; invalid arguments return
  * the same codes as specdec_dpace_forward, checked first. The first call on
  * a device looks up the array's address with that device current; make it
