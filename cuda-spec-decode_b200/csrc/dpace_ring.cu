@@ -524,8 +524,9 @@ struct RingVariant {
 // (128 KB ring, 1 CTA/SM); 2 = 4 x 6 x 4096 x 4 (96 KB ring, 2 CTAs/SM); 3 =
 // 4 x 8 x 4096 x 8 (128 KB ring, 128 KB blocks); 4 = 2 x 6 x 2048 x 8 (48 KB
 // ring, 4 CTAs/SM); 5 = 8 x 4 x 4096 x 4 (64 KB ring, 8 consumer warps); 6 =
-// 4 x 3 x 4096 x 4 (48 KB ring, 4 CTAs/SM). bf16 shapes have the same bytes
-// (twice the elements).
+// 4 x 3 x 4096 x 4 (48 KB ring, 4 CTAs/SM); 7 = 4 x 6 x 2048 x 8 (48 KB ring
+// in 8 KB stages, 4 CTAs/SM). bf16 shapes have the same bytes (twice the
+// elements).
 template <class T>
 struct Shapes {
   static constexpr int k = 4 / sizeof(T);  // elements per float's bytes
@@ -536,6 +537,7 @@ struct Shapes {
   using R4 = RingVariant<T, 2, 6, 2048 * k, 8>;
   using R5 = RingVariant<T, 8, 4, 4096 * k, 4>;
   using R6 = RingVariant<T, 4, 3, 4096 * k, kFwdBlockStages>;
+  using R7 = RingVariant<T, 4, 6, 2048 * k, 8>;
 
   static int block_elems(int shape) {
     switch (shape) {
@@ -545,6 +547,7 @@ struct Shapes {
       case 4: return 2048 * 8 * k;
       case 5: return 4096 * 4 * k;
       case 6: return 4096 * kFwdBlockStages * k;
+      case 7: return 2048 * 8 * k;
       default: return 4096 * kFwdBlockStages * k;
     }
   }
@@ -552,6 +555,7 @@ struct Shapes {
     switch (shape) {
       case 1: return 8192 * k;
       case 4: return 2048 * k;
+      case 7: return 2048 * k;
       default: return 4096 * k;
     }
   }
@@ -563,6 +567,7 @@ struct Shapes {
       case 4: return R4::fwd_ctas(device, cap);
       case 5: return R5::fwd_ctas(device, cap);
       case 6: return R6::fwd_ctas(device, cap);
+      case 7: return R7::fwd_ctas(device, cap);
       default: return R0::fwd_ctas(device, cap);
     }
   }
@@ -574,6 +579,7 @@ struct Shapes {
       case 4: return R4::bwd_ctas(device, cap);
       case 5: return R5::bwd_ctas(device, cap);
       case 6: return R6::bwd_ctas(device, cap);
+      case 7: return R7::bwd_ctas(device, cap);
       default: return R0::bwd_ctas(device, cap);
     }
   }
@@ -585,6 +591,7 @@ struct Shapes {
       case 4: return R4::fwd(a, ctas, st);
       case 5: return R5::fwd(a, ctas, st);
       case 6: return R6::fwd(a, ctas, st);
+      case 7: return R7::fwd(a, ctas, st);
       default: return R0::fwd(a, ctas, st);
     }
   }
@@ -596,6 +603,7 @@ struct Shapes {
       case 4: return R4::bwd(a, ctas, st);
       case 5: return R5::bwd(a, ctas, st);
       case 6: return R6::bwd(a, ctas, st);
+      case 7: return R7::bwd(a, ctas, st);
       default: return R0::bwd(a, ctas, st);
     }
   }

@@ -61,7 +61,7 @@ int current_device() {
 // shape - 10.
 constexpr int kLdgShapeBase = 10;
 // highest ring shape per kernel id (D-PACE fwd/bwd have shape 6, DFlash up to 5)
-constexpr int kMaxRingShape[4] = {6, 6, 5, 5};
+constexpr int kMaxRingShape[4] = {7, 7, 5, 5};
 
 bool has_ring_path(int kernel) { return kernel >= 0 && kernel <= 3; }
 

@@ -351,7 +351,7 @@ int specdec_dflash_attention_backward(const uint16_t* q, const uint16_t* k, cons
 
 /*
  * Selects a kernel variant and caps resident CTAs per SM (0 = occupancy
- * limit) for one kernel, process-wide. Shapes 0..5 (0..6 for the D-PACE
+ * limit) for one kernel, process-wide. Shapes 0..5 (0..7 for the D-PACE
  * kernels) are warp-specialized bulk-copy ring variants (used when the
  * streamed pointers are 16-byte
  * aligned; otherwise the 128-bit-load kernels run with their default shape);

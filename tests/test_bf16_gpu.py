@@ -177,11 +177,14 @@ def test_dflash_mixed_dtypes_widen_the_bf16_side(cuda):
     assert float((xg.grad.cpu() - g_ref).abs().max()) <= 1e-6
 
 
-@pytest.mark.parametrize("shape", [0, 1, 2, 3, 4, 5, 10])
+@pytest.mark.parametrize("shape", [0, 1, 2, 3, 4, 5, 6, 7, 10])
 def test_bf16_every_launch_shape(cuda, shape):
     """Every bf16 ring shape (10 selects the fp32 128-bit-load kernels, for
-    which bf16 uses ring shape 0) gives the oracle's results."""
+    which bf16 uses ring shape 0; 6 and 7 exist for the D-PACE kernels only,
+    the DFlash ones keep their default) gives the oracle's results."""
     from specdec import _lib
+
+    kernels = (0, 1) if shape in (6, 7) else range(4)
 
     rng = np.random.default_rng(9)
     N, B, V = 6, 8, 20011
@@ -190,7 +193,7 @@ def test_bf16_every_launch_shape(cuda, shape):
     t = torch.from_numpy(rng.integers(0, V, (N, B))).cuda()
     m = torch.from_numpy((rng.random((N, B)) < 0.8).astype(np.float32)).cuda()
     try:
-        for k in range(4):
+        for k in kernels:
             _lib.set_launch_shape(k, shape, 0)
         loss, g = _dpace(x16, t, m)
         want, g_ref = odp.dpace_fwd_bwd_torch(x16.float().cpu(), t.cpu(), 0.5, m.cpu())
