@@ -467,7 +467,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, (ring_min_ctas<NC, 1, S, SE, T>
 #define SPECDEC_BWD_BLOCK_STAGES 1
 #endif
 constexpr int kBwdBlockStages = SPECDEC_BWD_BLOCK_STAGES;
-// Stages per forward block of shapes 0 and 6 (the fp32 and bf16 defaults). A
+// Stages per forward block of shapes 0, 6 and 8 (8 is the forward's default). A
 // smaller block shortens the end of the launch (the last blocks finish closer
 // together) at the cost of more piece closes and more partials per row for
 // the finalize to merge.
@@ -525,8 +525,9 @@ struct RingVariant {
 // 4 x 8 x 4096 x 8 (128 KB ring, 128 KB blocks); 4 = 2 x 6 x 2048 x 8 (48 KB
 // ring, 4 CTAs/SM); 5 = 8 x 4 x 4096 x 4 (64 KB ring, 8 consumer warps); 6 =
 // 4 x 3 x 4096 x 4 (48 KB ring, 4 CTAs/SM); 7 = 4 x 6 x 2048 x 8 (48 KB ring
-// in 8 KB stages, 4 CTAs/SM). bf16 shapes have the same bytes (twice the
-// elements).
+// in 8 KB stages, 4 CTAs/SM); 8 = 4 x 2 x 4096 x 4 (32 KB ring, 4 CTAs/SM for
+// fp32, 5 for bf16: the D-PACE forward's default). bf16 shapes have the same
+// bytes (twice the elements).
 template <class T>
 struct Shapes {
   static constexpr int k = 4 / sizeof(T);  // elements per float's bytes
@@ -538,6 +539,7 @@ struct Shapes {
   using R5 = RingVariant<T, 8, 4, 4096 * k, 4>;
   using R6 = RingVariant<T, 4, 3, 4096 * k, kFwdBlockStages>;
   using R7 = RingVariant<T, 4, 6, 2048 * k, 8>;
+  using R8 = RingVariant<T, 4, 2, 4096 * k, kFwdBlockStages>;
 
   static int block_elems(int shape) {
     switch (shape) {
@@ -548,6 +550,7 @@ struct Shapes {
       case 5: return 4096 * 4 * k;
       case 6: return 4096 * kFwdBlockStages * k;
       case 7: return 2048 * 8 * k;
+      case 8: return 4096 * kFwdBlockStages * k;
       default: return 4096 * kFwdBlockStages * k;
     }
   }
@@ -568,6 +571,7 @@ struct Shapes {
       case 5: return R5::fwd_ctas(device, cap);
       case 6: return R6::fwd_ctas(device, cap);
       case 7: return R7::fwd_ctas(device, cap);
+      case 8: return R8::fwd_ctas(device, cap);
       default: return R0::fwd_ctas(device, cap);
     }
   }
@@ -580,6 +584,7 @@ struct Shapes {
       case 5: return R5::bwd_ctas(device, cap);
       case 6: return R6::bwd_ctas(device, cap);
       case 7: return R7::bwd_ctas(device, cap);
+      case 8: return R8::bwd_ctas(device, cap);
       default: return R0::bwd_ctas(device, cap);
     }
   }
@@ -592,6 +597,7 @@ struct Shapes {
       case 5: return R5::fwd(a, ctas, st);
       case 6: return R6::fwd(a, ctas, st);
       case 7: return R7::fwd(a, ctas, st);
+      case 8: return R8::fwd(a, ctas, st);
       default: return R0::fwd(a, ctas, st);
     }
   }
@@ -604,6 +610,7 @@ struct Shapes {
       case 5: return R5::bwd(a, ctas, st);
       case 6: return R6::bwd(a, ctas, st);
       case 7: return R7::bwd(a, ctas, st);
+      case 8: return R8::bwd(a, ctas, st);
       default: return R0::bwd(a, ctas, st);
     }
   }

@@ -60,15 +60,24 @@ int current_device() {
 // default shape); shapes 10..14 force the 128-bit-load kernels, variant
 // shape - 10.
 constexpr int kLdgShapeBase = 10;
-// highest ring shape per kernel id (D-PACE fwd/bwd have shape 6, DFlash up to 5)
-constexpr int kMaxRingShape[4] = {7, 7, 5, 5};
+// highest ring shape per kernel id (D-PACE fwd/bwd up to 8, DFlash up to 5)
+constexpr int kMaxRingShape[4] = {8, 8, 5, 5};
 
 bool has_ring_path(int kernel) { return kernel >= 0 && kernel <= 3; }
+
+// Built-in ring shape: 8 for the D-PACE forward (two 16 KB stages per CTA:
+// 4 CTAs per SM for fp32, 5 for bf16 -- the bf16 forward is bound by its
+// consumers' exponentials and gains the warps; the fp32 forward runs as fast
+// as on shape 0 and leaves the shared memory that lets the chained backward's
+// CTAs move in while it drains), 0 for every other kernel. Graph-timed at
+// [64, 16, 128256]: fp32 fused step 230.3 -> 227.1 us against shape 0, bf16
+// forward 47.3 -> 46.1 us and bf16 fused step 128.0 -> 126.0 us against shape 6.
+int default_ring_shape(int kernel) { return kernel == SPECDEC_KERNEL_DPACE_FWD ? 8 : 0; }
 
 // Variant id inside the chosen kernel family.
 int kernel_shape(int kernel, bool tma) {
   const int raw = g_shape[kernel].load();
-  if (raw < 0) return 0;  // default: fp32 ring shape 0, or the 128-bit-load kernels' shape 0
+  if (raw < 0) return tma ? default_ring_shape(kernel) : 0;  // or the 128-bit-load kernels' shape 0
   if (tma) return raw;
   if (!has_ring_path(kernel)) return raw % kLdgShapeBase;
   return raw >= kLdgShapeBase ? raw - kLdgShapeBase : 0;
@@ -79,13 +88,10 @@ bool use_tma(int kernel, bool ptrs_aligned) {
 }
 
 // bf16 has only the ring kernels: a shape that selects the 128-bit-load
-// kernels falls back to ring shape 0. Default: ring shape 0, except the
-// D-PACE forward, ring shape 6 (16 consumer warps per SM: the bf16 forward is
-// bound by its consumers' exponentials, and measured 5% faster there at
-// [64, 16, 128256]; the fp32 forward is not, and keeps shape 0).
+// kernels falls back to ring shape 0. Default: default_ring_shape.
 int bf16_shape(int kernel) {
   const int raw = g_shape[kernel].load();
-  if (raw < 0) return kernel == SPECDEC_KERNEL_DPACE_FWD ? 6 : 0;
+  if (raw < 0) return default_ring_shape(kernel);
   return raw < kLdgShapeBase ? raw : 0;
 }
 

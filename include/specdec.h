@@ -346,7 +346,7 @@ int specdec_dflash_attention_backward(const uint16_t* q, const uint16_t* k, cons
 #define SPECDEC_KERNEL_DFLASH_BWD 3
 
 /* specdec_set_launch_shape: the built-in choice (ring shape 0 for every
- * kernel and dtype, except ring shape 6 for the bf16 D-PACE forward). */
+ * kernel and dtype, except ring shape 8 for the D-PACE forward). */
 #define SPECDEC_SHAPE_DEFAULT (-1)
 
 /*

@@ -296,9 +296,9 @@ SHAPE_CASES = [c for c in cases.DPACE_CASES if c["name"] in (
     "type_SP_N4_B8_V1024", "seq0masked_N4_B8_V512", "ws2_N4_B16_V128256_sd2_prefix4")]
 
 
-@pytest.mark.parametrize("shape", [0, 1, 2, 3, 4, 5, 6, 7, 10, 11, 12, 13, 14])
+@pytest.mark.parametrize("shape", [0, 1, 2, 3, 4, 5, 6, 7, 8, 10, 11, 12, 13, 14])
 def test_every_launch_shape_matches_golden(cuda, gd, shape):
-    """Shapes 0-7: warp-specialized bulk-copy ring variants; 10-14: 128-bit-load kernels."""
+    """Shapes 0-8: warp-specialized bulk-copy ring variants; 10-14: 128-bit-load kernels."""
     from specdec import _lib
 
     try:
