@@ -134,19 +134,6 @@ __device__ __forceinline__ int64_t copied_end(int64_t f0, int64_t f1) {
   return f0 + ((((f1 - f0) * (int64_t)sizeof(T)) & ~int64_t(15)) / (int64_t)sizeof(T));
 }
 
-// Producer loop, lane 0 of the producer warp. NIN input streams of element
-// type T share the flattened index space (ring k holds stream k's stages at
-// ring + k*S*SE). A stage whose rows are all dead is posted without a copy.
-// `first` is the CTA's first block, dequeued by the caller before its
-// prologue so that the atomic's latency overlaps it. The next block is
-// dequeued only when the current block's last stage is posted, and taken up
-// after the next slot wait: the atomic's latency hides behind that wait, and
-// no CTA holds a whole unstarted block when the queue runs dry (which would
-// leave the others idle at the end). Returns false on a wait timeout.
-// `withhold_first` (failure-detection tests only) never posts the first
-// stage: this CTA's consumers then see their bounded wait expire, which is
-// the path under test. `trk` (or null) receives the progress record. The
-// caller retires the CTA from the queue afterwards.
 // 1: the forwards' producers post their first stage before the liveness table
 // is built (ring_post_first); 0: after it, like the backwards.
 #ifndef SPECDEC_EARLY_FIRST_STAGE
@@ -183,6 +170,19 @@ __device__ bool ring_post_first(const T* const* src, const BlockMap& bm, int64_t
   return true;
 }
 
+// Producer loop, lane 0 of the producer warp. NIN input streams of element
+// type T share the flattened index space (ring k holds stream k's stages at
+// ring + k*S*SE). A stage whose rows are all dead is posted without a copy.
+// `first` is the CTA's first block (its own index; `first_posted`: its first
+// stage was already posted by ring_post_first). The next block is
+// dequeued only when the current block's last stage is posted, and taken up
+// after the next slot wait: the atomic's latency hides behind that wait, and
+// no CTA holds a whole unstarted block when the queue runs dry (which would
+// leave the others idle at the end). Returns false on a wait timeout.
+// `withhold_first` (failure-detection tests only) never posts the first
+// stage: this CTA's consumers then see their bounded wait expire, which is
+// the path under test. `trk` (or null) receives the progress record. The
+// caller retires the CTA from the queue afterwards.
 template <int NIN, int S, int SE, class T>
 __device__ bool ring_produce(const T* const* src, const BlockMap& bm, int64_t V, const RowBits& rb,
                              const BlockQueue& q, T* ring, uint64_t* full, uint64_t* empty,
