@@ -525,8 +525,8 @@ struct DfRing {
 // 1 = 4 x 4 x 4096 x 4 (128 KB ring, 1 CTA/SM); 2 = 4 x 6 x 2048 x 8 (96 KB
 // ring, 2 CTAs/SM); 3 = 2 x 4 x 2048 x 8 (64 KB ring, 3 CTAs/SM);
 // 4 = 8 x 3 x 4096 x 4 (96 KB ring, 2 CTAs/SM); 5 = 8 x 4 x 2048 x 8 (64 KB
-// ring, 8 consumer warps). bf16 shapes have the same bytes (twice the
-// elements).
+// ring, 8 consumer warps); 6 = 4 x 2 x 2048 x 8 (32 KB ring, 4 CTAs/SM). bf16
+// shapes have the same bytes (twice the elements).
 template <class T>
 struct DfShapes {
   static constexpr int k = 4 / sizeof(T);
@@ -536,6 +536,7 @@ struct DfShapes {
   using D3 = DfRing<T, 2, 4, 2048 * k, 8>;
   using D4 = DfRing<T, 8, 3, 4096 * k, 4>;
   using D5 = DfRing<T, 8, 4, 2048 * k, 8>;
+  using D6 = DfRing<T, 4, 2, 2048 * k, 8>;
 
   static int block_elems(int shape) {
     switch (shape) {
@@ -552,6 +553,7 @@ struct DfShapes {
       case 3: return D3::template fwd_ctas<KIND>(device, cap);
       case 4: return D4::template fwd_ctas<KIND>(device, cap);
       case 5: return D5::template fwd_ctas<KIND>(device, cap);
+      case 6: return D6::template fwd_ctas<KIND>(device, cap);
       default: return D0::template fwd_ctas<KIND>(device, cap);
     }
   }
@@ -563,6 +565,7 @@ struct DfShapes {
       case 3: return D3::template bwd_ctas<KIND>(device, cap);
       case 4: return D4::template bwd_ctas<KIND>(device, cap);
       case 5: return D5::template bwd_ctas<KIND>(device, cap);
+      case 6: return D6::template bwd_ctas<KIND>(device, cap);
       default: return D0::template bwd_ctas<KIND>(device, cap);
     }
   }
@@ -574,6 +577,7 @@ struct DfShapes {
       case 3: return D3::template fwd<KIND>(a, ctas, st);
       case 4: return D4::template fwd<KIND>(a, ctas, st);
       case 5: return D5::template fwd<KIND>(a, ctas, st);
+      case 6: return D6::template fwd<KIND>(a, ctas, st);
       default: return D0::template fwd<KIND>(a, ctas, st);
     }
   }
@@ -585,6 +589,7 @@ struct DfShapes {
       case 3: return D3::template bwd<KIND>(a, ctas, st);
       case 4: return D4::template bwd<KIND>(a, ctas, st);
       case 5: return D5::template bwd<KIND>(a, ctas, st);
+      case 6: return D6::template bwd<KIND>(a, ctas, st);
       default: return D0::template bwd<KIND>(a, ctas, st);
     }
   }

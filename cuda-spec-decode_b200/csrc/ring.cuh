@@ -281,8 +281,9 @@ struct RingSmem {
 template <int NC, int NIN, int S, int SE, class T>
 constexpr int ring_min_ctas() {
   constexpr int by_smem = int((227 * 1024) / sizeof(RingSmem<NIN, S, SE, T>));
-  // two-stage bf16 rings of up to 160 threads: 5 CTAs per SM (80 registers)
-  constexpr int by_threads = (NC + 1) * 32 <= 160 ? (sizeof(T) == 2 && S <= 2 ? 5 : 4) : 2;
+  // two-stage one-stream bf16 rings of up to 160 threads: 5 CTAs per SM (80
+  // registers); the two-stream DFlash forward needs more registers and stays at 4
+  constexpr int by_threads = (NC + 1) * 32 <= 160 ? (sizeof(T) == 2 && S <= 2 && NIN == 1 ? 5 : 4) : 2;
   constexpr int m = by_smem < by_threads ? (by_smem < 1 ? 1 : by_smem) : by_threads;
   return (sizeof(T) == 2 || m >= 4) ? m : 1;
 }

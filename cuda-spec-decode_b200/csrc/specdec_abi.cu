@@ -60,8 +60,8 @@ int current_device() {
 // default shape); shapes 10..14 force the 128-bit-load kernels, variant
 // shape - 10.
 constexpr int kLdgShapeBase = 10;
-// highest ring shape per kernel id (D-PACE fwd/bwd up to 8, DFlash up to 5)
-constexpr int kMaxRingShape[4] = {8, 8, 5, 5};
+// highest ring shape per kernel id (D-PACE fwd/bwd up to 8, DFlash up to 6)
+constexpr int kMaxRingShape[4] = {8, 8, 6, 6};
 
 bool has_ring_path(int kernel) { return kernel >= 0 && kernel <= 3; }
 
@@ -88,10 +88,14 @@ bool use_tma(int kernel, bool ptrs_aligned) {
 }
 
 // bf16 has only the ring kernels: a shape that selects the 128-bit-load
-// kernels falls back to ring shape 0. Default: default_ring_shape.
+// kernels falls back to ring shape 0. Default: default_ring_shape, except the
+// DFlash forward, ring shape 6 (two stages, 4 CTAs per SM instead of 3: the
+// bf16 forward is bound by its consumers' exponentials; graph-timed at
+// [64, 16, 128256] 97.5 -> 92.4 us, while the fp32 forward measured 1 us
+// slower there and keeps shape 0).
 int bf16_shape(int kernel) {
   const int raw = g_shape[kernel].load();
-  if (raw < 0) return default_ring_shape(kernel);
+  if (raw < 0) return kernel == SPECDEC_KERNEL_DFLASH_FWD ? 6 : default_ring_shape(kernel);
   return raw < kLdgShapeBase ? raw : 0;
 }
 

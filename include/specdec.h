@@ -346,12 +346,13 @@ int specdec_dflash_attention_backward(const uint16_t* q, const uint16_t* k, cons
 #define SPECDEC_KERNEL_DFLASH_BWD 3
 
 /* specdec_set_launch_shape: the built-in choice (ring shape 0 for every
- * kernel and dtype, except ring shape 8 for the D-PACE forward). */
+ * kernel and dtype, except ring shape 8 for the D-PACE forward and ring
+ * shape 6 for the bf16 DFlash forward). */
 #define SPECDEC_SHAPE_DEFAULT (-1)
 
 /*
  * Selects a kernel variant and caps resident CTAs per SM (0 = occupancy
- * limit) for one kernel, process-wide. Shapes 0..5 (0..7 for the D-PACE
+ * limit) for one kernel, process-wide. Shapes 0..6 (0..8 for the D-PACE
  * kernels) are warp-specialized bulk-copy ring variants (used when the
  * streamed pointers are 16-byte
  * aligned; otherwise the 128-bit-load kernels run with their default shape);

@@ -180,11 +180,11 @@ def test_dflash_mixed_dtypes_widen_the_bf16_side(cuda):
 @pytest.mark.parametrize("shape", [0, 1, 2, 3, 4, 5, 6, 7, 8, 10])
 def test_bf16_every_launch_shape(cuda, shape):
     """Every bf16 ring shape (10 selects the fp32 128-bit-load kernels, for
-    which bf16 uses ring shape 0; 6, 7 and 8 exist for the D-PACE kernels only,
+    which bf16 uses ring shape 0; 7 and 8 exist for the D-PACE kernels only,
     the DFlash ones keep their default) gives the oracle's results."""
     from specdec import _lib
 
-    kernels = (0, 1) if shape in (6, 7, 8) else range(4)
+    kernels = (0, 1) if shape in (7, 8) else range(4)
 
     rng = np.random.default_rng(9)
     N, B, V = 6, 8, 20011

@@ -200,9 +200,9 @@ SHAPE_CASES = [c for c in cases.DFLASH_CASES if c["name"] in (
     "ws3_kl_N4_B16_V128256_sd2_corr", "ws3_ce_N2_B16_V128256_sd2_corr")]
 
 
-@pytest.mark.parametrize("shape", [0, 1, 2, 3, 4, 5, 10, 11, 12, 13, 14])
+@pytest.mark.parametrize("shape", [0, 1, 2, 3, 4, 5, 6, 10, 11, 12, 13, 14])
 def test_every_launch_shape_matches_golden(cuda, gf, shape):
-    """Shapes 0-5: warp-specialized bulk-copy ring variants; 10-14: 128-bit-load kernels."""
+    """Shapes 0-6: warp-specialized bulk-copy ring variants; 10-14: 128-bit-load kernels."""
     from specdec import _lib
 
     try:
