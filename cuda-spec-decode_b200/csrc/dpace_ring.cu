@@ -481,7 +481,7 @@ constexpr int kFwdBlockStages = SPECDEC_FWD_BLOCK_STAGES;
 // constant, not a multiple of the grid: the block boundaries, and so the
 // results, do not depend on the CTA count.
 #ifndef SPECDEC_FWD_TAIL_BLOCKS
-#define SPECDEC_FWD_TAIL_BLOCKS 256
+#define SPECDEC_FWD_TAIL_BLOCKS 512
 #endif
 constexpr int64_t kFwdTailBlocks = SPECDEC_FWD_TAIL_BLOCKS;
 

@@ -65,14 +65,24 @@ constexpr int kMaxRingShape[4] = {8, 8, 6, 6};
 
 bool has_ring_path(int kernel) { return kernel >= 0 && kernel <= 3; }
 
-// Built-in ring shape: 8 for the D-PACE forward (two 16 KB stages per CTA:
-// 4 CTAs per SM for fp32, 5 for bf16 -- the bf16 forward is bound by its
-// consumers' exponentials and gains the warps; the fp32 forward runs as fast
-// as on shape 0 and leaves the shared memory that lets the chained backward's
-// CTAs move in while it drains), 0 for every other kernel. Graph-timed at
-// [64, 16, 128256]: fp32 fused step 230.3 -> 227.1 us against shape 0, bf16
-// forward 47.3 -> 46.1 us and bf16 fused step 128.0 -> 126.0 us against shape 6.
-int default_ring_shape(int kernel) { return kernel == SPECDEC_KERNEL_DPACE_FWD ? 8 : 0; }
+// Built-in ring shapes per element type and kernel (D-PACE fwd, D-PACE bwd,
+// DFlash fwd, DFlash bwd), picked by graph-timed A/B at [64, 16, 128256]:
+//  - D-PACE forward, shape 8 (two 16 KB stages per CTA: 4 CTAs per SM for
+//    fp32, 5 for bf16). The bf16 forward is bound by its consumers'
+//    exponentials and gains the warps (47.3 -> 46.1 us against shape 6); the
+//    fp32 forward runs as fast as on shape 0 and leaves the shared memory that
+//    lets the chained backward's CTAs move in while it drains (fused step
+//    230.3 -> 227.1 us).
+//  - bf16 D-PACE backward, shape 6 (fused step 126.0 -> 125.1 us; fp32 keeps
+//    shape 0: 228.3 vs 229.1 us on shape 6).
+//  - bf16 DFlash forward, shape 6 (two stages per stream, 4 CTAs per SM
+//    instead of 3: 97.5 -> 92.4 us; fp32 151.7 vs 150.5 us keeps shape 0).
+//  - fp32 DFlash backward, shape 6 (221.8 -> 221.0 us; bf16 116.2 vs 115.1 us
+//    keeps shape 0).
+constexpr int kDefaultRingShape[2][4] = {{8, 0, 0, 6}, {8, 6, 6, 0}};  // [fp32, bf16][kernel]
+int default_ring_shape(int kernel, int dtype = kDtypeF32) {
+  return has_ring_path(kernel) ? kDefaultRingShape[dtype == kDtypeBF16 ? 1 : 0][kernel] : 0;
+}
 
 // Variant id inside the chosen kernel family.
 int kernel_shape(int kernel, bool tma) {
@@ -88,14 +98,10 @@ bool use_tma(int kernel, bool ptrs_aligned) {
 }
 
 // bf16 has only the ring kernels: a shape that selects the 128-bit-load
-// kernels falls back to ring shape 0. Default: default_ring_shape, except the
-// DFlash forward, ring shape 6 (two stages, 4 CTAs per SM instead of 3: the
-// bf16 forward is bound by its consumers' exponentials; graph-timed at
-// [64, 16, 128256] 97.5 -> 92.4 us, while the fp32 forward measured 1 us
-// slower there and keeps shape 0).
+// kernels falls back to ring shape 0. Default: default_ring_shape.
 int bf16_shape(int kernel) {
   const int raw = g_shape[kernel].load();
-  if (raw < 0) return kernel == SPECDEC_KERNEL_DFLASH_FWD ? 6 : default_ring_shape(kernel);
+  if (raw < 0) return default_ring_shape(kernel, kDtypeBF16);
   return raw < kLdgShapeBase ? raw : 0;
 }
 

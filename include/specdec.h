@@ -166,7 +166,7 @@ int specdec_scale_inplace_bf16(uint16_t* x, int64_t n, const float* factor, void
  * fits when specdec_dpace_counter_bytes(N, B) <= 64 KiB (N <= 16376) and
  * specdec_dpace_scratch_bytes(N, B, V, device) <= 4 MiB - 64 KiB -- at
  * V = 128256 about 14000 rows of N*B (about 287 bytes of scratch per row
- * plus 24 KiB for the forward's short final queue blocks). Larger problems
+ * plus 48 KiB for the forward's short final queue blocks). Larger problems
  * return SPECDEC_ERR_WORKSPACE before any launch; invalid arguments return
  * the same codes as specdec_dpace_forward, checked first. The first call on
  * a device looks up the array's address with that device current; make it
@@ -345,9 +345,9 @@ int specdec_dflash_attention_backward(const uint16_t* q, const uint16_t* k, cons
 #define SPECDEC_KERNEL_DFLASH_FWD 2
 #define SPECDEC_KERNEL_DFLASH_BWD 3
 
-/* specdec_set_launch_shape: the built-in choice (ring shape 0 for every
- * kernel and dtype, except ring shape 8 for the D-PACE forward and ring
- * shape 6 for the bf16 DFlash forward). */
+/* specdec_set_launch_shape: the built-in choice (ring shape 8 for the
+ * D-PACE forward; ring shape 6 for the bf16 D-PACE backward, the bf16 DFlash
+ * forward and the fp32 DFlash backward; ring shape 0 otherwise). */
 #define SPECDEC_SHAPE_DEFAULT (-1)
 
 /*
